@@ -1,0 +1,145 @@
+/*
+ * dcn_b200.h -- C ABI of libdcn_b200, the B200 (sm_100a) deformable
+ * convolution library (DCNv1 / DCNv2, fp32 NCHW).
+ *
+ * This is the drop-in boundary for the hot path of
+ * ilirium/pytorch_mps_deform_conv2d.  The reference exports its path as
+ * PyTorch operator schemas registered from ObjC++
+ * (src/deform_conv2d_mps/_C/deform_conv2d_mps.mm:892-925); each entry point
+ * below replaces one of those schemas and keeps its argument meaning:
+ *
+ *   dcn_forward       <- deform_conv2d_forward   (.mm:905-909, impl :192-374)
+ *   dcn_backward      <- deform_conv2d_backward  (.mm:910-915, impl :682-890)
+ *   dcn_col2im        <- deformable_col2im       (.mm:895-898, impl :388-504)
+ *   dcn_col2im_coord  <- deformable_col2im_coord (.mm:900-904, impl :516-651)
+ *
+ * Conventions (same as the reference op):
+ *   - all tensors are dense, contiguous fp32 in device memory of the current
+ *     CUDA device: input (N, C, H, W); weight (outC, C/groups, kh, kw);
+ *     offset (N, 2*dg*kh*kw, Ho, Wo) with (dy, dx) interleaved per tap;
+ *     mask (N, dg*kh*kw, Ho, Wo); bias (outC); output (N, outC, Ho, Wo);
+ *   - mask == NULL means DCNv1 (the reference passes an empty mask tensor,
+ *     .mm:247); bias == NULL means no bias (Tensor? bias);
+ *   - Ho = (H + 2*pad_h - dilation_h*(kh-1) - 1) / stride_h + 1, likewise Wo
+ *     (.mm:231-234);
+ *   - inputs are never written; outputs are fully overwritten;
+ *   - work is enqueued on `stream` (a cudaStream_t, NULL = legacy default
+ *     stream) and nothing synchronises the host, like the reference's lazy
+ *     MPS encoding (.mm:372);
+ *   - invalid arguments return DCN_ERR_INVALID_ARGUMENT and leave a message
+ *     with the reference's wording in dcn_last_error() (the reference raises
+ *     RuntimeError from TORCH_CHECK, .mm:202-267 and :693-760);
+ *   - scratch memory is caller-provided (`workspace`, at least the size the
+ *     matching *_workspace_size query returns); the library itself never
+ *     allocates device memory.
+ */
+#ifndef DCN_B200_H_
+#define DCN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define DCN_API __attribute__((visibility("default")))
+#else
+#define DCN_API
+#endif
+
+#define DCN_ABI_VERSION 1
+
+/* status codes */
+#define DCN_OK 0
+#define DCN_ERR_INVALID_ARGUMENT 1
+#define DCN_ERR_WORKSPACE 2
+#define DCN_ERR_CUDA 3
+#define DCN_ERR_UNSUPPORTED 4
+
+/* `flags` of dcn_forward / dcn_backward.  The low byte selects the math:
+ *   DCN_MATH_FP32  fp32 FFMA on the CUDA cores (strict parity mode);
+ *   DCN_MATH_TF32  tcgen05 tensor cores with TF32 operands and fp32
+ *                  accumulation where a tensor-core kernel covers the shape,
+ *                  fp32 FFMA elsewhere.
+ * The second byte can pin a kernel family (test use; 0 = automatic). */
+#define DCN_MATH_FP32 0x0
+#define DCN_MATH_TF32 0x1
+#define DCN_ALGO_SIMT_GEMM 0x100
+#define DCN_ALGO_SIMT_DIRECT 0x200
+
+/* Geometry of one deformable convolution: the shapes of the reference op's
+ * tensors plus its integer arguments. */
+typedef struct dcn_shape {
+  int64_t batch, in_channels, height, width;  /* input (N, C, H, W)          */
+  int64_t out_channels, kernel_h, kernel_w;   /* weight (outC, C/g, kh, kw)  */
+  int64_t stride_h, stride_w;
+  int64_t pad_h, pad_w;
+  int64_t dilation_h, dilation_w;
+  int64_t groups, deformable_groups;
+} dcn_shape;
+
+/* ABI version of the loaded library (DCN_ABI_VERSION). */
+DCN_API int dcn_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+DCN_API const char* dcn_last_error(void);
+
+/* Output spatial size of `shape` (.mm:231-234).  Returns DCN_OK, or
+ * DCN_ERR_INVALID_ARGUMENT when it is non-positive. */
+DCN_API int dcn_output_size(const dcn_shape* shape, int64_t* out_h, int64_t* out_w);
+
+/* Bytes of workspace dcn_forward needs for `shape` and `flags`. */
+DCN_API size_t dcn_forward_workspace_size(const dcn_shape* shape, uint32_t flags);
+
+/* Forward pass; replaces deform_conv2d_forward (.mm:192-374).
+ * output = bias + sum_{c,k} weight * mask * bilinear(input, sample(offset)). */
+DCN_API int dcn_forward(const dcn_shape* shape, const float* input, const float* weight,
+                        const float* offset, const float* mask, const float* bias,
+                        float* output, uint32_t flags, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace dcn_backward needs for `shape` and `flags`. */
+DCN_API size_t dcn_backward_workspace_size(const dcn_shape* shape, uint32_t flags);
+
+/* Backward pass; replaces deform_conv2d_backward (.mm:682-890).  Writes all
+ * five gradients.  grad_mask must be NULL when mask is NULL (the reference
+ * returns an empty tensor there, .mm:766-767); grad_bias may be NULL when no
+ * bias gradient is wanted (the reference returns an empty tensor when the
+ * op had no bias, .mm:885-886). */
+DCN_API int dcn_backward(const dcn_shape* shape, const float* grad_output,
+                         const float* input, const float* weight, const float* offset,
+                         const float* mask, float* grad_input, float* grad_offset,
+                         float* grad_mask, float* grad_weight, float* grad_bias,
+                         uint32_t flags, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Single-image scatter of a column gradient into the input gradient;
+ * replaces deformable_col2im (.mm:388-504).  columns (C*kh*kw, Ho*Wo) with
+ * row c*kh*kw + k; offset (2*dg*kh*kw, Ho, Wo); mask (dg*kh*kw, Ho, Wo) or
+ * NULL; grad_im (C, H, W) is overwritten. */
+DCN_API int dcn_col2im(const float* columns, const float* offset, const float* mask,
+                       float* grad_im, int64_t channels, int64_t height, int64_t width,
+                       int64_t kernel_h, int64_t kernel_w, int64_t stride_h,
+                       int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                       int64_t dilation_h, int64_t dilation_w,
+                       int64_t deformable_groups, void* stream);
+
+/* Single-image offset / mask gradients from a column gradient; replaces
+ * deformable_col2im_coord (.mm:516-651).  input (C, H, W); grad_offset
+ * (2*dg*kh*kw, Ho, Wo) and grad_mask (dg*kh*kw, Ho, Wo, NULL when mask is
+ * NULL) are overwritten. */
+DCN_API int dcn_col2im_coord(const float* columns, const float* input,
+                             const float* offset, const float* mask, float* grad_offset,
+                             float* grad_mask, int64_t channels, int64_t height,
+                             int64_t width, int64_t kernel_h, int64_t kernel_w,
+                             int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                             int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+                             int64_t deformable_groups, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DCN_B200_H_ */

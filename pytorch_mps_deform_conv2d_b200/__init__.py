@@ -1,0 +1,12 @@
+"""B200 (sm_100a) deformable convolution, DCNv1 / DCNv2.
+
+Drop-in for the public API of ilirium/pytorch_mps_deform_conv2d
+(``deform_conv2d``, ``DeformConv2d``), itself the API of torchvision.ops:
+
+    from pytorch_mps_deform_conv2d_b200 import deform_conv2d, DeformConv2d
+"""
+from .ops import deform_conv2d, get_math_mode, set_math_mode
+from .module import DeformConv2d
+
+__all__ = ["deform_conv2d", "DeformConv2d", "set_math_mode", "get_math_mode"]
+__version__ = "0.1.0"

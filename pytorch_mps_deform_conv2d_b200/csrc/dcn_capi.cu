@@ -1,0 +1,369 @@
+// dcn_capi.cu -- extern "C" entry points of libdcn_b200 (declared in
+// include/dcn_b200.h): argument validation with the reference's messages,
+// workspace carving and kernel dispatch.  No entry point allocates device
+// memory or synchronises the host.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "dcn_b200.h"
+#include "dcn_kernels.h"
+#include "dcn_tc.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(DCN_ERR_CUDA, "%s: CUDA error %d (%s)", where, (int)e, cudaGetErrorString(e));
+}
+
+#define DCN_CHECK(cond, ...)                                  \
+  do {                                                        \
+    if (!(cond)) return fail(DCN_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+#define DCN_CUDA(expr, where)                    \
+  do {                                           \
+    cudaError_t e_ = (expr);                     \
+    if (e_ != cudaSuccess) return cuda_fail(e_, where); \
+  } while (0)
+
+bool is_device_ptr(const void* p) {
+  if (p == nullptr) return false;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+int num_sms_current() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Carves aligned sub-buffers out of the caller's workspace.
+struct Carver {
+  char* base;
+  size_t used = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  float* take(size_t nfloats) {
+    float* p = reinterpret_cast<float*>(base + used);
+    used += align_up(nfloats * sizeof(float));
+    return p;
+  }
+};
+
+// Validation shared by forward and backward (.mm:202-267, :693-760).
+int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
+              const char* op) {
+  DCN_CHECK(s != nullptr, "%s: shape must not be NULL", op);
+  DCN_CHECK(s->batch >= 0 && s->in_channels >= 0 && s->height >= 0 && s->width >= 0 &&
+                s->out_channels >= 0,
+            "%s: tensor dimensions must be non-negative", op);
+  DCN_CHECK(s->kernel_h > 0 && s->kernel_w > 0, "kernel dims must be positive");
+  DCN_CHECK(s->groups > 0, "groups must be positive, got %lld", (long long)s->groups);
+  DCN_CHECK(s->stride_h > 0 && s->stride_w > 0, "stride must be positive");
+  DCN_CHECK(s->dilation_h > 0 && s->dilation_w > 0, "dilation must be positive");
+  DCN_CHECK(s->pad_h >= 0 && s->pad_w >= 0, "padding must be non-negative");
+  DCN_CHECK(s->in_channels % s->groups == 0, "channels (%lld) not divisible by groups (%lld)",
+            (long long)s->in_channels, (long long)s->groups);
+  DCN_CHECK(s->out_channels % s->groups == 0,
+            "out_channels (%lld) not divisible by groups (%lld)", (long long)s->out_channels,
+            (long long)s->groups);
+  const int64_t Ho = (s->height + 2 * s->pad_h - s->dilation_h * (s->kernel_h - 1) - 1) / s->stride_h + 1;
+  const int64_t Wo = (s->width + 2 * s->pad_w - s->dilation_w * (s->kernel_w - 1) - 1) / s->stride_w + 1;
+  DCN_CHECK(Ho > 0 && Wo > 0, "calculated output size (%lldx%lld) is non-positive",
+            (long long)Ho, (long long)Wo);
+  DCN_CHECK(s->deformable_groups > 0, "deformable_groups must be positive, got %lld",
+            (long long)s->deformable_groups);
+  DCN_CHECK(s->in_channels % s->deformable_groups == 0,
+            "channels (%lld) not divisible by deformable_groups (%lld)",
+            (long long)s->in_channels, (long long)s->deformable_groups);
+  const int64_t kk = s->kernel_h * s->kernel_w;
+  const int64_t lim = (int64_t)1 << 31;
+  // per-image element counts are indexed in int32 inside the kernels
+  if (s->in_channels * s->height * s->width >= lim || s->out_channels * Ho * Wo >= lim ||
+      2 * s->deformable_groups * kk * Ho * Wo >= lim || s->batch * Ho * Wo >= lim ||
+      s->out_channels * (s->in_channels / s->groups) * kk >= lim || s->height * s->width > 65535LL * 32)
+    return fail(DCN_ERR_UNSUPPORTED, "%s: per-image tensor sizes beyond 2^31 elements are not supported", op);
+  g.N = (int)s->batch; g.C = (int)s->in_channels; g.H = (int)s->height; g.W = (int)s->width;
+  g.outC = (int)s->out_channels; g.kh = (int)s->kernel_h; g.kw = (int)s->kernel_w;
+  g.sh = (int)s->stride_h; g.sw = (int)s->stride_w; g.ph = (int)s->pad_h; g.pw = (int)s->pad_w;
+  g.dh = (int)s->dilation_h; g.dw = (int)s->dilation_w;
+  g.G = (int)s->groups; g.dg = (int)s->deformable_groups;
+  g.Ho = (int)Ho; g.Wo = (int)Wo;
+  g.use_mask = use_mask ? 1 : 0; g.use_bias = use_bias ? 1 : 0;
+  g.Cg = g.C / g.G; g.Og = g.outC / g.G; g.cpg = g.dg ? g.C / g.dg : 0;
+  g.kk = g.kh * g.kw; g.P = g.Ho * g.Wo; g.HW = g.H * g.W;
+  g.NP = (long long)g.N * g.P;
+  return DCN_OK;
+}
+
+int fwd_cpad(const dcn::Geom& g) { return dcn::ceil_div(g.Cg, 8) * 8; }
+
+enum class FwdAlgo { kDirect, kGemm, kTc };
+
+FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
+  if (flags & DCN_ALGO_SIMT_GEMM) return FwdAlgo::kGemm;
+  if (flags & DCN_ALGO_SIMT_DIRECT) return dcn::fwd_direct_supported(g) ? FwdAlgo::kDirect : FwdAlgo::kGemm;
+  if ((flags & 0xff) == DCN_MATH_TF32 && dcn::tc_fwd_supported(g)) return FwdAlgo::kTc;
+  if (dcn::fwd_direct_supported(g)) return FwdAlgo::kDirect;
+  return FwdAlgo::kGemm;
+}
+
+size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
+  size_t b = align_up((size_t)g.N * g.HW * g.C * sizeof(float));  // xt
+  switch (pick_fwd(g, flags)) {
+    case FwdAlgo::kGemm:
+      b += align_up((size_t)g.G * g.kk * fwd_cpad(g) * g.Og * sizeof(float));
+      break;
+    case FwdAlgo::kTc:
+      b += align_up(dcn::tc_fwd_weight_bytes(g));
+      break;
+    case FwdAlgo::kDirect:
+      break;
+  }
+  return b + kAlign;  // slack for aligning the caller's base pointer
+}
+
+size_t bwd_ws(const dcn::Geom& g, uint32_t /*flags*/) {
+  size_t b = align_up((size_t)g.N * g.HW * g.C * sizeof(float));      // xt
+  b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
+  b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));     // packed weight
+  return b + kAlign;
+}
+
+void* align_ptr(void* p) {
+  uintptr_t v = reinterpret_cast<uintptr_t>(p);
+  return reinterpret_cast<void*>((v + kAlign - 1) / kAlign * kAlign);
+}
+
+}  // namespace
+
+extern "C" {
+
+DCN_API int dcn_abi_version(void) { return DCN_ABI_VERSION; }
+
+DCN_API const char* dcn_last_error(void) { return g_last_error.c_str(); }
+
+DCN_API int dcn_output_size(const dcn_shape* s, int64_t* out_h, int64_t* out_w) {
+  dcn::Geom g;
+  const int rc = make_geom(s, false, false, g, "dcn_output_size");
+  if (rc != DCN_OK) return rc;
+  if (out_h) *out_h = g.Ho;
+  if (out_w) *out_w = g.Wo;
+  return DCN_OK;
+}
+
+DCN_API size_t dcn_forward_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_forward_workspace_size") != DCN_OK) return 0;
+  return fwd_ws(g, flags);
+}
+
+DCN_API size_t dcn_backward_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_backward_workspace_size") != DCN_OK) return 0;
+  return bwd_ws(g, flags);
+}
+
+DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* weight,
+                        const float* offset, const float* mask, const float* bias,
+                        float* output, uint32_t flags, void* workspace,
+                        size_t workspace_bytes, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
+  if (rc != DCN_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const long long out_numel = (long long)g.N * g.outC * g.P;
+  if (out_numel == 0) return DCN_OK;  // .mm:273: nothing to dispatch
+  auto dev_or_empty = [](const void* p, long long n) { return n == 0 || is_device_ptr(p); };
+  DCN_CHECK(is_device_ptr(output), "deform_conv2d_forward: output must be a CUDA device buffer");
+  DCN_CHECK(dev_or_empty(input, (long long)g.N * g.C * g.HW) &&
+                dev_or_empty(offset, (long long)g.N * 2 * g.dg * g.kk * g.P) &&
+                dev_or_empty(weight, (long long)g.outC * g.Cg * g.kk),
+            "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
+  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a float32 CUDA tensor");
+  DCN_CHECK(bias == nullptr || is_device_ptr(bias), "bias must be a float32 CUDA tensor");
+  if (g.C == 0) {  // .mm:303-308: output is zeros (+ bias)
+    DCN_CUDA(dcn::launch_fill_bias(output, g.use_bias ? bias : nullptr, g, stream), "fill");
+    return DCN_OK;
+  }
+  const size_t need = fwd_ws(g, flags);
+  if (workspace_bytes < need || workspace == nullptr)
+    return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
+                need, workspace_bytes);
+  Carver ws(align_ptr(workspace));
+  float* xt = ws.take((size_t)g.N * g.HW * g.C);
+  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
+  switch (pick_fwd(g, flags)) {
+    case FwdAlgo::kDirect:
+      DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
+               "fwd_simt_direct");
+      break;
+    case FwdAlgo::kGemm: {
+      const int cpad = fwd_cpad(g);
+      float* wf = ws.take((size_t)g.G * g.kk * cpad * g.Og);
+      DCN_CUDA(dcn::launch_pack_weight_fwd(weight, wf, g, cpad, stream), "pack_weight_fwd");
+      DCN_CUDA(dcn::launch_fwd_simt_gemm(g, xt, wf, cpad, offset, mask, bias, output, stream),
+               "fwd_simt_gemm");
+      break;
+    }
+    case FwdAlgo::kTc: {
+      float* wt = ws.take(dcn::tc_fwd_weight_bytes(g) / sizeof(float));
+      DCN_CUDA(dcn::launch_tc_pack_weight(weight, wt, g, stream), "tc_pack_weight");
+      DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, num_sms_current(), stream),
+               "fwd_tc");
+      break;
+    }
+  }
+  return DCN_OK;
+}
+
+DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const float* input,
+                         const float* weight, const float* offset, const float* mask,
+                         float* grad_input, float* grad_offset, float* grad_mask,
+                         float* grad_weight, float* grad_bias, uint32_t flags,
+                         void* workspace, size_t workspace_bytes, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
+  if (rc != DCN_OK) return rc;
+  DCN_CHECK(mask != nullptr || grad_mask == nullptr,
+            "deform_conv2d_backward: grad_mask must be NULL when mask is NULL");
+  DCN_CHECK(mask == nullptr || grad_mask != nullptr,
+            "deform_conv2d_backward: grad_mask is required when mask is given");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t x_bytes = (size_t)g.N * g.C * g.HW * sizeof(float);
+  const size_t off_bytes = (size_t)g.N * 2 * g.dg * g.kk * g.P * sizeof(float);
+  const size_t msk_bytes = (size_t)g.N * g.dg * g.kk * g.P * sizeof(float);
+  const size_t w_bytes = (size_t)g.outC * g.Cg * g.kk * sizeof(float);
+  auto dev_or_empty = [](const void* p, size_t bytes) { return bytes == 0 || is_device_ptr(p); };
+  DCN_CHECK(dev_or_empty(grad_output, (size_t)g.N * g.outC * g.P) && dev_or_empty(input, x_bytes) &&
+                dev_or_empty(weight, w_bytes) && dev_or_empty(offset, off_bytes),
+            "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
+  DCN_CHECK(dev_or_empty(grad_input, x_bytes) && dev_or_empty(grad_offset, off_bytes) &&
+                dev_or_empty(grad_weight, w_bytes) &&
+                (grad_mask == nullptr || dev_or_empty(grad_mask, msk_bytes)) &&
+                (grad_bias == nullptr || dev_or_empty(grad_bias, (size_t)g.outC)),
+            "deform_conv2d_backward: gradient outputs must be CUDA device buffers");
+  DCN_CHECK(mask == nullptr || dev_or_empty(mask, msk_bytes), "mask must be a float32 CUDA tensor");
+
+  // Zero what the kernels accumulate into (.mm:764-777 zero-initialise too).
+  if (off_bytes) DCN_CUDA(cudaMemsetAsync(grad_offset, 0, off_bytes, stream), "memset");
+  if (grad_mask && msk_bytes) DCN_CUDA(cudaMemsetAsync(grad_mask, 0, msk_bytes, stream), "memset");
+  if (w_bytes) DCN_CUDA(cudaMemsetAsync(grad_weight, 0, w_bytes, stream), "memset");
+  if (grad_bias) {
+    if (g.N * (long long)g.P == 0) {
+      if (g.outC) DCN_CUDA(cudaMemsetAsync(grad_bias, 0, (size_t)g.outC * sizeof(float), stream), "memset");
+    } else {
+      DCN_CUDA(dcn::launch_grad_bias(grad_output, grad_bias, g, stream), "grad_bias");
+    }
+  }
+  const bool skip = g.N == 0 || g.C == 0 || g.outC == 0 || g.P == 0;  // .mm:779-782
+  if (skip) {
+    if (x_bytes) DCN_CUDA(cudaMemsetAsync(grad_input, 0, x_bytes, stream), "memset");
+    return DCN_OK;
+  }
+  const size_t need = bwd_ws(g, flags);
+  if (workspace_bytes < need || workspace == nullptr)
+    return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
+                need, workspace_bytes);
+  Carver ws(align_ptr(workspace));
+  float* xt = ws.take((size_t)g.N * g.HW * g.C);
+  float* gxt = ws.take((size_t)g.N * g.HW * g.C);
+  float* wb = ws.take((size_t)g.G * g.kk * g.Og * g.Cg);
+  DCN_CUDA(cudaMemsetAsync(gxt, 0, x_bytes, stream), "memset");
+  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
+  DCN_CUDA(dcn::launch_pack_weight_bwd(weight, wb, g, stream), "pack_weight_bwd");
+  DCN_CUDA(dcn::launch_bwd_data_simt(g, grad_output, wb, xt, offset, mask, gxt, grad_offset,
+                                     grad_mask, stream),
+           "bwd_data_simt");
+  DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+  DCN_CUDA(dcn::launch_bwd_weight_simt(g, grad_output, xt, offset, mask, grad_weight,
+                                       num_sms_current(), stream),
+           "bwd_weight_simt");
+  return DCN_OK;
+}
+
+static int single_geom(dcn::Geom& g, int64_t C, int64_t H, int64_t W, int64_t kh, int64_t kw,
+                       int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
+                       int64_t dg, bool use_mask, const char* op) {
+  dcn_shape s;
+  s.batch = 1; s.in_channels = C; s.height = H; s.width = W; s.out_channels = C;
+  s.kernel_h = kh; s.kernel_w = kw; s.stride_h = sh; s.stride_w = sw; s.pad_h = ph; s.pad_w = pw;
+  s.dilation_h = dh; s.dilation_w = dw; s.groups = 1; s.deformable_groups = dg;
+  return make_geom(&s, use_mask, false, g, op);
+}
+
+DCN_API int dcn_col2im(const float* columns, const float* offset, const float* mask,
+                       float* grad_im, int64_t C, int64_t H, int64_t W, int64_t kh, int64_t kw,
+                       int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t dh, int64_t dw,
+                       int64_t dg, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = single_geom(g, C, H, W, kh, kw, sh, sw, ph, pw, dh, dw, dg, mask != nullptr,
+                       "deformable_col2im");
+  if (rc != DCN_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t im_bytes = (size_t)C * H * W * sizeof(float);
+  if (im_bytes == 0) return DCN_OK;
+  DCN_CHECK(is_device_ptr(grad_im), "deformable_col2im: grad_im must be a CUDA device buffer");
+  DCN_CUDA(cudaMemsetAsync(grad_im, 0, im_bytes, stream), "memset");
+  if ((long long)C * g.kk * g.P == 0) return DCN_OK;
+  DCN_CHECK(is_device_ptr(columns) && is_device_ptr(offset),
+            "deformable_col2im: columns and offset must be CUDA tensors");
+  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a float32 CUDA tensor");
+  DCN_CUDA(dcn::launch_col2im_single(g, columns, offset, mask, grad_im, stream), "col2im");
+  return DCN_OK;
+}
+
+DCN_API int dcn_col2im_coord(const float* columns, const float* input, const float* offset,
+                             const float* mask, float* grad_offset, float* grad_mask, int64_t C,
+                             int64_t H, int64_t W, int64_t kh, int64_t kw, int64_t sh, int64_t sw,
+                             int64_t ph, int64_t pw, int64_t dh, int64_t dw, int64_t dg,
+                             void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = single_geom(g, C, H, W, kh, kw, sh, sw, ph, pw, dh, dw, dg, mask != nullptr,
+                       "deformable_col2im_coord");
+  if (rc != DCN_OK) return rc;
+  DCN_CHECK(mask != nullptr || grad_mask == nullptr,
+            "deformable_col2im_coord: grad_mask must be NULL when mask is NULL");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const long long total = 2LL * g.dg * g.kk * g.P;
+  if (total == 0) return DCN_OK;
+  DCN_CHECK(is_device_ptr(grad_offset) && (mask == nullptr || is_device_ptr(grad_mask)),
+            "deformable_col2im_coord: gradient outputs must be CUDA device buffers");
+  DCN_CHECK(is_device_ptr(offset) && (C == 0 || (is_device_ptr(columns) && is_device_ptr(input))),
+            "deformable_col2im_coord: columns, input and offset must be CUDA tensors");
+  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a float32 CUDA tensor");
+  DCN_CUDA(dcn::launch_col2im_coord_single(g, columns, input, offset, mask, grad_offset, grad_mask,
+                                           stream),
+           "col2im_coord");
+  return DCN_OK;
+}
+
+}  // extern "C"

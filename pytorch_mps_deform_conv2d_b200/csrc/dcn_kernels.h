@@ -1,0 +1,64 @@
+// dcn_kernels.h -- host-side launchers of the libdcn_b200 kernels.  Every
+// launcher enqueues on `stream` and returns cudaGetLastError() of its launch;
+// none allocates or synchronises.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "dcn_common.cuh"
+
+namespace dcn {
+
+// ---- layout kernels (dcn_layout.cu) --------------------------------------
+// x (N, C, H, W) -> xt (N, H, W, C)
+cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
+                                cudaStream_t stream);
+// gxt (N, H, W, C) -> gx (N, C, H, W)
+cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
+                                cudaStream_t stream);
+// weight (outC, Cg, kk) -> wf[G][kk][cpad][Og] (forward SIMT operand,
+// channels zero-padded to cpad)
+cudaError_t launch_pack_weight_fwd(const float* w, float* wf, const Geom& g,
+                                   int cpad, cudaStream_t stream);
+// weight (outC, Cg, kk) -> wb[G][kk][Og][Cg] (grad-column operand)
+cudaError_t launch_pack_weight_bwd(const float* w, float* wb, const Geom& g,
+                                   cudaStream_t stream);
+// out[n, o, p] = bias[o] (0 when bias is NULL); the C == 0 forward
+cudaError_t launch_fill_bias(float* out, const float* bias, const Geom& g,
+                             cudaStream_t stream);
+// grad_bias[o] = sum_{n,p} grad_out[n, o, p]
+cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
+                             cudaStream_t stream);
+
+// ---- fp32 SIMT kernels (dcn_simt.cu) --------------------------------------
+// Forward, fp32 FFMA.  `xt` is the NHWC copy of the input.
+cudaError_t launch_fwd_simt_gemm(const Geom& g, const float* xt, const float* wf,
+                                 int cpad, const float* off, const float* mask,
+                                 const float* bias, float* out, cudaStream_t stream);
+cudaError_t launch_fwd_simt_direct(const Geom& g, const float* xt, const float* w,
+                                   const float* off, const float* mask,
+                                   const float* bias, float* out, cudaStream_t stream);
+bool fwd_direct_supported(const Geom& g);
+// Backward data path: grad_col = W^T go per tap, fused with the col2im
+// scatter (into gxt, NHWC, pre-zeroed) and the coordinate / mask gradient
+// reduction (into goff / gmask, pre-zeroed).
+cudaError_t launch_bwd_data_simt(const Geom& g, const float* go, const float* wb,
+                                 const float* xt, const float* off, const float* mask,
+                                 float* gxt, float* goff, float* gmask,
+                                 cudaStream_t stream);
+// grad_weight (outC, Cg, kh, kw) += go . col^T, col gathered on the fly;
+// `gw` pre-zeroed.
+cudaError_t launch_bwd_weight_simt(const Geom& g, const float* go, const float* xt,
+                                   const float* off, const float* mask, float* gw,
+                                   int num_sms, cudaStream_t stream);
+
+// ---- single-image building blocks (dcn_debug_ops.cu) ----------------------
+cudaError_t launch_col2im_single(const Geom& g, const float* col, const float* off,
+                                 const float* mask, float* grad_im,
+                                 cudaStream_t stream);
+cudaError_t launch_col2im_coord_single(const Geom& g, const float* col,
+                                       const float* im, const float* off,
+                                       const float* mask, float* grad_off,
+                                       float* grad_mask, cudaStream_t stream);
+
+}  // namespace dcn

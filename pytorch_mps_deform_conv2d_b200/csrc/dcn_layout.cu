@@ -1,0 +1,160 @@
+// dcn_layout.cu -- layout kernels around the deformable-convolution hot path:
+// NCHW <-> NHWC transposes (the gathers and the scatter work on a
+// channel-contiguous copy so one sample's channel vector is one run of
+// 16-byte loads / vector reductions), weight repacking and the bias gradient.
+#include "dcn_kernels.h"
+
+namespace dcn {
+
+namespace {
+
+constexpr int TT = 32;  // transpose tile
+
+// in (N, R, S) -> out (N, S, R); one 32x32 tile per block, 32x8 threads.
+__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ in,
+                                                        float* __restrict__ out,
+                                                        int R, int S) {
+  __shared__ float tile[TT][TT + 1];
+  const int n = blockIdx.z;
+  const int r0 = blockIdx.y * TT, s0 = blockIdx.x * TT;
+  const float* src = in + (long long)n * R * S;
+  float* dst = out + (long long)n * R * S;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int i = 0; i < TT; i += 8) {
+    const int r = r0 + ty + i, s = s0 + tx;
+    if (r < R && s < S) tile[ty + i][tx] = src[(long long)r * S + s];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < TT; i += 8) {
+    const int s = s0 + ty + i, r = r0 + tx;
+    if (r < R && s < S) dst[(long long)s * R + r] = tile[tx][ty + i];
+  }
+}
+
+cudaError_t launch_transpose(const float* in, float* out, int N, int R, int S,
+                             cudaStream_t stream) {
+  if ((long long)N * R * S == 0) return cudaSuccess;
+  dim3 grid(ceil_div(S, TT), ceil_div(R, TT), N);
+  transpose_kernel<<<grid, dim3(TT, 8), 0, stream>>>(in, out, R, S);
+  return cudaGetLastError();
+}
+
+__global__ void pack_weight_fwd_kernel(const float* __restrict__ w,
+                                       float* __restrict__ wf, Geom g, int cpad) {
+  // wf[gi][k][c][o], c < cpad (zero beyond Cg)
+  const long long total = (long long)g.G * g.kk * cpad * g.Og;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(i % g.Og);
+    long long t = i / g.Og;
+    const int c = (int)(t % cpad);
+    t /= cpad;
+    const int k = (int)(t % g.kk);
+    const int gi = (int)(t / g.kk);
+    float v = 0.f;
+    if (c < g.Cg) v = w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k];
+    wf[i] = v;
+  }
+}
+
+__global__ void pack_weight_bwd_kernel(const float* __restrict__ w,
+                                       float* __restrict__ wb, Geom g) {
+  // wb[gi][k][o][c]
+  const long long total = (long long)g.G * g.kk * g.Og * g.Cg;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % g.Cg);
+    long long t = i / g.Cg;
+    const int o = (int)(t % g.Og);
+    t /= g.Og;
+    const int k = (int)(t % g.kk);
+    const int gi = (int)(t / g.kk);
+    wb[i] = w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k];
+  }
+}
+
+// One block per output channel; deterministic tree reduction.
+__global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict__ go,
+                                                        float* __restrict__ gb, Geom g) {
+  const int o = blockIdx.x;
+  float s = 0.f;
+  for (int n = 0; n < g.N; ++n) {
+    const float* row = go + ((long long)n * g.outC + o) * g.P;
+    for (int p = threadIdx.x; p < g.P; p += blockDim.x) s += row[p];
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+    if (threadIdx.x == 0) gb[o] = s;
+  }
+}
+
+__global__ void fill_bias_kernel(float* __restrict__ out, const float* __restrict__ bias,
+                                 Geom g) {
+  const long long total = (long long)g.N * g.outC * g.P;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)((i / g.P) % g.outC);
+    out[i] = bias ? bias[o] : 0.f;
+  }
+}
+
+int grid_for(long long total) {
+  long long b = (total + 255) / 256;
+  if (b > 148LL * 32) b = 148LL * 32;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace
+
+cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
+                                cudaStream_t stream) {
+  return launch_transpose(x, xt, N, C, HW, stream);
+}
+
+cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
+                                cudaStream_t stream) {
+  return launch_transpose(gxt, gx, N, HW, C, stream);
+}
+
+cudaError_t launch_pack_weight_fwd(const float* w, float* wf, const Geom& g, int cpad,
+                                   cudaStream_t stream) {
+  const long long total = (long long)g.G * g.kk * cpad * g.Og;
+  if (total == 0) return cudaSuccess;
+  pack_weight_fwd_kernel<<<grid_for(total), 256, 0, stream>>>(w, wf, g, cpad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_weight_bwd(const float* w, float* wb, const Geom& g,
+                                   cudaStream_t stream) {
+  const long long total = (long long)g.G * g.kk * g.Og * g.Cg;
+  if (total == 0) return cudaSuccess;
+  pack_weight_bwd_kernel<<<grid_for(total), 256, 0, stream>>>(w, wb, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_bias(float* out, const float* bias, const Geom& g,
+                             cudaStream_t stream) {
+  const long long total = (long long)g.N * g.outC * g.P;
+  if (total == 0) return cudaSuccess;
+  fill_bias_kernel<<<grid_for(total), 256, 0, stream>>>(out, bias, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
+                             cudaStream_t stream) {
+  if (g.outC == 0) return cudaSuccess;
+  grad_bias_kernel<<<g.outC, 256, 0, stream>>>(go, gb, g);
+  return cudaGetLastError();
+}
+
+}  // namespace dcn

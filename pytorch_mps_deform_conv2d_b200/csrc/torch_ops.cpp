@@ -1,0 +1,322 @@
+// torch_ops.cpp -- PyTorch operator registration for libdcn_b200.
+//
+// Registers the reference's operator schemas
+// (src/deform_conv2d_mps/_C/deform_conv2d_mps.mm:892-916) under the namespace
+// `deform_conv2d_b200` with a CUDA dispatch implementation.  Each
+// implementation validates with the reference's messages, makes inputs
+// contiguous, allocates outputs and scratch through PyTorch's caching
+// allocator, and calls the C ABI (include/dcn_b200.h) on the current CUDA
+// stream.  Every schema has one extra trailing argument, `int math=-1`: -1
+// follows torch.backends.cuda.matmul.allow_tf32, otherwise it is the
+// DCN_MATH_* / DCN_ALGO_* flag word of the C ABI.
+#include <ATen/ATen.h>
+#include <ATen/Context.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "dcn_b200.h"
+
+namespace {
+
+uint32_t resolve_flags(int64_t math) {
+  if (math >= 0) return static_cast<uint32_t>(math);
+  return at::globalContext().allowTF32CuBLAS() ? DCN_MATH_TF32 : DCN_MATH_FP32;
+}
+
+void check_rc(int rc) {
+  TORCH_CHECK(rc == DCN_OK, dcn_last_error());
+}
+
+void check_cuda_f32(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.device().is_cuda() && t.scalar_type() == at::kFloat, what);
+}
+
+dcn_shape make_shape(const at::Tensor& x, const at::Tensor& w, int64_t stride_h,
+                     int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                     int64_t dilation_w, int64_t groups, int64_t dg) {
+  dcn_shape s;
+  s.batch = x.size(0);
+  s.in_channels = x.size(1);
+  s.height = x.size(2);
+  s.width = x.size(3);
+  s.out_channels = w.size(0);
+  s.kernel_h = w.size(2);
+  s.kernel_w = w.size(3);
+  s.stride_h = stride_h;
+  s.stride_w = stride_w;
+  s.pad_h = pad_h;
+  s.pad_w = pad_w;
+  s.dilation_h = dilation_h;
+  s.dilation_w = dilation_w;
+  s.groups = groups;
+  s.deformable_groups = dg;
+  return s;
+}
+
+// Shape checks of .mm:202-267 (forward) / :693-760 (backward).
+void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& off,
+                  const at::Tensor& msk, bool use_mask, int64_t stride_h, int64_t stride_w,
+                  int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+                  int64_t groups, int64_t dg, int64_t& out_h, int64_t& out_w) {
+  TORCH_CHECK(x.dim() == 4, "input must be 4-D (N, C, H, W), got ", x.dim());
+  TORCH_CHECK(w.dim() == 4, "weight must be 4-D (outC, C/groups, kh, kw), got ", w.dim());
+  TORCH_CHECK(off.dim() == 4, "offset must be 4-D (N, 2*dg*kh*kw, oh, ow), got ", off.dim());
+  TORCH_CHECK(groups > 0, "groups must be positive, got ", groups);
+  TORCH_CHECK(stride_h > 0 && stride_w > 0, "stride must be positive");
+  TORCH_CHECK(dilation_h > 0 && dilation_w > 0, "dilation must be positive");
+  const int64_t N = x.size(0), C = x.size(1), H = x.size(2), W = x.size(3);
+  const int64_t outC = w.size(0), kh = w.size(2), kw = w.size(3);
+  TORCH_CHECK(w.size(1) * groups == C, "weight shape mismatch: expected in-channels ", C,
+              ", got ", w.size(1) * groups);
+  TORCH_CHECK(C % groups == 0, "channels (", C, ") not divisible by groups (", groups, ")");
+  TORCH_CHECK(outC % groups == 0, "out_channels (", outC, ") not divisible by groups (", groups,
+              ")");
+  out_h = (H + 2 * pad_h - dilation_h * (kh - 1) - 1) / stride_h + 1;
+  out_w = (W + 2 * pad_w - dilation_w * (kw - 1) - 1) / stride_w + 1;
+  TORCH_CHECK(out_h > 0 && out_w > 0, "calculated output size (", out_h, "x", out_w,
+              ") is non-positive");
+  TORCH_CHECK(dg > 0, "deformable_groups must be positive, got ", dg);
+  TORCH_CHECK(C % dg == 0, "channels (", C, ") not divisible by deformable_groups (", dg, ")");
+  TORCH_CHECK(off.size(0) == N && off.size(1) == 2 * dg * kh * kw && off.size(2) == out_h &&
+                  off.size(3) == out_w,
+              "offset shape mismatch: expected (", N, ", ", 2 * dg * kh * kw, ", ", out_h, ", ",
+              out_w, "), got ", off.sizes());
+  if (use_mask) {
+    check_cuda_f32(msk, "mask must be a float32 CUDA tensor");
+    TORCH_CHECK(msk.dim() == 4 && msk.size(0) == N && msk.size(1) == dg * kh * kw &&
+                    msk.size(2) == out_h && msk.size(3) == out_w,
+                "mask shape mismatch: expected (", N, ", ", dg * kh * kw, ", ", out_h, ", ",
+                out_w, "), got ", msk.sizes());
+  }
+}
+
+at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weight,
+                                 const at::Tensor& offset, const at::Tensor& mask,
+                                 const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                 int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                 int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                 int64_t deformable_groups, int64_t math) {
+  TORCH_CHECK(input.device().is_cuda() && weight.device().is_cuda() && offset.device().is_cuda(),
+              "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
+  TORCH_CHECK(input.scalar_type() == at::kFloat && weight.scalar_type() == at::kFloat &&
+                  offset.scalar_type() == at::kFloat,
+              "deform_conv2d_forward: only float32 is supported");
+  const bool use_mask = mask.defined() && mask.numel() > 0;
+  int64_t out_h = 0, out_w = 0;
+  check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
+               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
+  at::Tensor b;
+  if (bias.has_value() && bias->defined() && bias->numel() > 0) {
+    check_cuda_f32(*bias, "bias must be a float32 CUDA tensor");
+    TORCH_CHECK(bias->numel() == weight.size(0), "bias must have ", weight.size(0),
+                " elements, got ", bias->numel());
+    b = bias->contiguous();
+  }
+  c10::cuda::CUDAGuard guard(input.device());
+  auto x = input.contiguous();
+  auto w = weight.contiguous();
+  auto off = offset.contiguous();
+  auto msk = use_mask ? mask.contiguous() : at::Tensor();
+  auto out = at::empty({x.size(0), w.size(0), out_h, out_w}, x.options());
+  if (out.numel() == 0) return out;
+  const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                                 groups, deformable_groups);
+  const uint32_t flags = resolve_flags(math);
+  const size_t ws_bytes = dcn_forward_workspace_size(&s, flags);
+  auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  check_rc(dcn_forward(&s, x.data_ptr<float>(), w.data_ptr<float>(), off.data_ptr<float>(),
+                       use_mask ? msk.data_ptr<float>() : nullptr,
+                       b.defined() ? b.data_ptr<float>() : nullptr, out.data_ptr<float>(), flags,
+                       ws.data_ptr(), ws_bytes, stream.stream()));
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_conv2d_backward(
+    const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
+    const at::Tensor& offset, const at::Tensor& mask, const c10::optional<at::Tensor>& bias,
+    int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+    int64_t dilation_w, int64_t groups, int64_t deformable_groups, int64_t math) {
+  TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
+                  weight.device().is_cuda() && offset.device().is_cuda(),
+              "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
+  TORCH_CHECK(grad_output.scalar_type() == at::kFloat && input.scalar_type() == at::kFloat &&
+                  weight.scalar_type() == at::kFloat && offset.scalar_type() == at::kFloat,
+              "deform_conv2d_backward: only float32 is supported");
+  TORCH_CHECK(grad_output.dim() == 4, "grad_output must be 4-D, got ", grad_output.dim());
+  const bool use_mask = mask.defined() && mask.numel() > 0;
+  int64_t out_h = 0, out_w = 0;
+  check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
+               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
+  TORCH_CHECK(grad_output.size(0) == input.size(0) && grad_output.size(1) == weight.size(0) &&
+                  grad_output.size(2) == out_h && grad_output.size(3) == out_w,
+              "grad_output shape mismatch: expected (", input.size(0), ", ", weight.size(0), ", ",
+              out_h, ", ", out_w, "), got ", grad_output.sizes());
+  const bool use_bias = bias.has_value() && bias->defined() && bias->numel() > 0;
+  c10::cuda::CUDAGuard guard(input.device());
+  auto go = grad_output.contiguous();
+  auto x = input.contiguous();
+  auto w = weight.contiguous();
+  auto off = offset.contiguous();
+  auto msk = use_mask ? mask.contiguous() : at::Tensor();
+  auto grad_input = at::empty_like(x);
+  auto grad_offset = at::empty_like(off);
+  auto grad_mask = use_mask ? at::empty_like(msk) : at::empty({0}, x.options());
+  auto grad_weight = at::empty_like(w);
+  auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
+  const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                                 groups, deformable_groups);
+  const uint32_t flags = resolve_flags(math);
+  const size_t ws_bytes = dcn_backward_workspace_size(&s, flags);
+  auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto ptr = [](at::Tensor& t) { return t.numel() ? t.data_ptr<float>() : nullptr; };
+  auto cptr = [](const at::Tensor& t) -> const float* {
+    return t.defined() && t.numel() ? t.data_ptr<float>() : nullptr;
+  };
+  check_rc(dcn_backward(&s, cptr(go), cptr(x), cptr(w), cptr(off), use_mask ? cptr(msk) : nullptr,
+                        ptr(grad_input), ptr(grad_offset), use_mask ? ptr(grad_mask) : nullptr,
+                        ptr(grad_weight), use_bias ? ptr(grad_bias) : nullptr, flags, ws.data_ptr(),
+                        ws_bytes, stream.stream()));
+  return std::make_tuple(grad_input, grad_offset, grad_mask, grad_weight, grad_bias);
+}
+
+at::Tensor deformable_col2im(const at::Tensor& columns, const at::Tensor& offset,
+                             const at::Tensor& mask, int64_t height, int64_t width,
+                             int64_t kernel_h, int64_t kernel_w, int64_t stride_h,
+                             int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                             int64_t dilation_w, int64_t deformable_groups, int64_t math) {
+  (void)math;
+  TORCH_CHECK(columns.device().is_cuda() && offset.device().is_cuda(),
+              "deformable_col2im: columns and offset must be CUDA tensors");
+  TORCH_CHECK(columns.scalar_type() == at::kFloat && offset.scalar_type() == at::kFloat,
+              "deformable_col2im: only float32 is supported");
+  TORCH_CHECK(columns.dim() == 2, "columns must be 2-D (C*kh*kw, oh*ow)");
+  TORCH_CHECK(offset.dim() == 3, "offset must be 3-D (2*dg*kh*kw, oh, ow)");
+  TORCH_CHECK(kernel_h > 0 && kernel_w > 0, "kernel dims must be positive");
+  TORCH_CHECK(stride_h > 0 && stride_w > 0, "stride must be positive");
+  TORCH_CHECK(dilation_h > 0 && dilation_w > 0, "dilation must be positive");
+  const int64_t kk = kernel_h * kernel_w;
+  TORCH_CHECK(columns.size(0) % kk == 0, "columns rows (", columns.size(0),
+              ") not divisible by kh*kw (", kk, ")");
+  const int64_t C = columns.size(0) / kk;
+  const int64_t out_h = (height + 2 * pad_h - dilation_h * (kernel_h - 1) - 1) / stride_h + 1;
+  const int64_t out_w = (width + 2 * pad_w - dilation_w * (kernel_w - 1) - 1) / stride_w + 1;
+  TORCH_CHECK(columns.size(1) == out_h * out_w, "columns cols (", columns.size(1),
+              ") != out_h*out_w (", out_h * out_w, ")");
+  const int64_t dg = deformable_groups;
+  TORCH_CHECK(dg > 0, "deformable_groups must be positive, got ", dg);
+  TORCH_CHECK(C % dg == 0, "channels (", C, ") not divisible by deformable_groups (", dg, ")");
+  TORCH_CHECK(offset.size(0) == 2 * dg * kk && offset.size(1) == out_h && offset.size(2) == out_w,
+              "offset shape mismatch: expected (", 2 * dg * kk, ", ", out_h, ", ", out_w,
+              "), got ", offset.sizes());
+  const bool use_mask = mask.defined() && mask.numel() > 0;
+  if (use_mask) {
+    check_cuda_f32(mask, "mask must be a float32 CUDA tensor");
+    TORCH_CHECK(mask.dim() == 3 && mask.size(0) == dg * kk && mask.size(1) == out_h &&
+                    mask.size(2) == out_w,
+                "mask shape mismatch: expected (", dg * kk, ", ", out_h, ", ", out_w, "), got ",
+                mask.sizes());
+  }
+  c10::cuda::CUDAGuard guard(columns.device());
+  auto col = columns.contiguous();
+  auto off = offset.contiguous();
+  auto msk = use_mask ? mask.contiguous() : at::Tensor();
+  auto grad_im = at::empty({C, height, width}, col.options());
+  if (grad_im.numel() == 0) return grad_im;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  check_rc(dcn_col2im(col.data_ptr<float>(), off.data_ptr<float>(),
+                      use_mask ? msk.data_ptr<float>() : nullptr, grad_im.data_ptr<float>(), C,
+                      height, width, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, dg, stream.stream()));
+  return grad_im;
+}
+
+std::tuple<at::Tensor, at::Tensor> deformable_col2im_coord(
+    const at::Tensor& columns, const at::Tensor& input, const at::Tensor& offset,
+    const at::Tensor& mask, int64_t kernel_h, int64_t kernel_w, int64_t stride_h,
+    int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+    int64_t deformable_groups, int64_t math) {
+  (void)math;
+  TORCH_CHECK(columns.device().is_cuda() && input.device().is_cuda() && offset.device().is_cuda(),
+              "deformable_col2im_coord: columns, input and offset must be CUDA tensors");
+  TORCH_CHECK(columns.scalar_type() == at::kFloat && input.scalar_type() == at::kFloat &&
+                  offset.scalar_type() == at::kFloat,
+              "deformable_col2im_coord: only float32 is supported");
+  TORCH_CHECK(columns.dim() == 2, "columns must be 2-D (C*kh*kw, oh*ow)");
+  TORCH_CHECK(input.dim() == 3, "input must be 3-D (C, H, W)");
+  TORCH_CHECK(offset.dim() == 3, "offset must be 3-D (2*dg*kh*kw, oh, ow)");
+  TORCH_CHECK(kernel_h > 0 && kernel_w > 0, "kernel dims must be positive");
+  TORCH_CHECK(stride_h > 0 && stride_w > 0, "stride must be positive");
+  TORCH_CHECK(dilation_h > 0 && dilation_w > 0, "dilation must be positive");
+  const int64_t C = input.size(0), H = input.size(1), W = input.size(2);
+  const int64_t kk = kernel_h * kernel_w;
+  TORCH_CHECK(columns.size(0) == C * kk, "columns rows (", columns.size(0), ") != C*kh*kw (",
+              C * kk, ")");
+  const int64_t out_h = (H + 2 * pad_h - dilation_h * (kernel_h - 1) - 1) / stride_h + 1;
+  const int64_t out_w = (W + 2 * pad_w - dilation_w * (kernel_w - 1) - 1) / stride_w + 1;
+  TORCH_CHECK(columns.size(1) == out_h * out_w, "columns cols (", columns.size(1),
+              ") != out_h*out_w (", out_h * out_w, ")");
+  const int64_t dg = deformable_groups;
+  TORCH_CHECK(dg > 0, "deformable_groups must be positive, got ", dg);
+  TORCH_CHECK(C % dg == 0, "channels (", C, ") not divisible by deformable_groups (", dg, ")");
+  TORCH_CHECK(offset.size(0) == 2 * dg * kk && offset.size(1) == out_h && offset.size(2) == out_w,
+              "offset shape mismatch: expected (", 2 * dg * kk, ", ", out_h, ", ", out_w,
+              "), got ", offset.sizes());
+  const bool use_mask = mask.defined() && mask.numel() > 0;
+  if (use_mask) {
+    check_cuda_f32(mask, "mask must be a float32 CUDA tensor");
+    TORCH_CHECK(mask.dim() == 3 && mask.size(0) == dg * kk && mask.size(1) == out_h &&
+                    mask.size(2) == out_w,
+                "mask shape mismatch: expected (", dg * kk, ", ", out_h, ", ", out_w, "), got ",
+                mask.sizes());
+  }
+  c10::cuda::CUDAGuard guard(columns.device());
+  auto col = columns.contiguous();
+  auto x = input.contiguous();
+  auto off = offset.contiguous();
+  auto msk = use_mask ? mask.contiguous() : at::Tensor();
+  auto grad_offset = at::empty({2 * dg * kk, out_h, out_w}, off.options());
+  auto grad_mask = use_mask ? at::empty({dg * kk, out_h, out_w}, off.options())
+                            : at::empty({0}, off.options());
+  if (grad_offset.numel() == 0) return std::make_tuple(grad_offset, grad_mask);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  check_rc(dcn_col2im_coord(col.numel() ? col.data_ptr<float>() : nullptr,
+                            x.numel() ? x.data_ptr<float>() : nullptr, off.data_ptr<float>(),
+                            use_mask ? msk.data_ptr<float>() : nullptr,
+                            grad_offset.data_ptr<float>(),
+                            use_mask ? grad_mask.data_ptr<float>() : nullptr, C, H, W, kernel_h,
+                            kernel_w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                            dg, stream.stream()));
+  return std::make_tuple(grad_offset, grad_mask);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(deform_conv2d_b200, m) {
+  m.def(
+      "deformable_col2im(Tensor columns, Tensor offset, Tensor mask, int height, int width, "
+      "int kernel_h, int kernel_w, int stride_h, int stride_w, int pad_h, int pad_w, "
+      "int dilation_h, int dilation_w, int deformable_groups, int math=-1) -> Tensor");
+  m.def(
+      "deformable_col2im_coord(Tensor columns, Tensor input, Tensor offset, Tensor mask, "
+      "int kernel_h, int kernel_w, int stride_h, int stride_w, int pad_h, int pad_w, "
+      "int dilation_h, int dilation_w, int deformable_groups, int math=-1) -> (Tensor, Tensor)");
+  m.def(
+      "deform_conv2d_forward(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
+      "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
+      "int dilation_w, int groups, int deformable_groups, int math=-1) -> Tensor");
+  m.def(
+      "deform_conv2d_backward(Tensor grad_output, Tensor input, Tensor weight, Tensor offset, "
+      "Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, "
+      "int dilation_h, int dilation_w, int groups, int deformable_groups, int math=-1) "
+      "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+}
+
+TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
+  m.impl("deformable_col2im", TORCH_FN(deformable_col2im));
+  m.impl("deformable_col2im_coord", TORCH_FN(deformable_col2im_coord));
+  m.impl("deform_conv2d_forward", TORCH_FN(deform_conv2d_forward));
+  m.impl("deform_conv2d_backward", TORCH_FN(deform_conv2d_backward));
+}

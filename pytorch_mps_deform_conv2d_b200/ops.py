@@ -1,0 +1,147 @@
+"""Functional deformable convolution, API-compatible with torchvision.
+
+Mirrors the reference's functional layer
+(src/deform_conv2d_mps/ops.py:62-169): same signature, same inference of
+``groups`` and ``deformable_groups`` from the tensor shapes, same autograd
+conventions (an empty mask means DCNv1, an empty bias means no bias; absent
+inputs get ``None`` gradients).  CUDA tensors run the sm_100a kernels of
+``libdcn_b200`` through the ``torch.ops.deform_conv2d_b200`` operators.
+There is no fallback to another backend: tensors on any other device raise.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import _native
+
+# Flag words of the C ABI (include/dcn_b200.h).
+MATH_FP32 = 0x0
+MATH_TF32 = 0x1
+ALGO_SIMT_GEMM = 0x100
+ALGO_SIMT_DIRECT = 0x200
+
+_MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32}
+_math_override: Optional[int] = None
+
+
+def set_math_mode(mode: Optional[str]) -> None:
+    """Select the arithmetic of the CUDA kernels.
+
+    ``"fp32"``: fp32 FFMA on the CUDA cores (tolerance of the reference's own
+    tests, 1e-4).  ``"tf32"``: tcgen05 tensor cores with TF32 operands and
+    fp32 accumulation.  ``None`` (default): follow
+    ``torch.backends.cuda.matmul.allow_tf32``, as PyTorch's own convolutions
+    and matmuls do.
+    """
+    global _math_override
+    if mode is None:
+        _math_override = None
+        return
+    if mode not in _MODES:
+        raise ValueError(f"math mode must be one of {sorted(_MODES)} or None, got {mode!r}")
+    _math_override = _MODES[mode]
+
+
+def get_math_mode() -> str:
+    """The math mode the next call will use ("fp32" or "tf32")."""
+    if _math_override is not None:
+        return "tf32" if (_math_override & 0xff) == MATH_TF32 else "fp32"
+    return "tf32" if torch.backends.cuda.matmul.allow_tf32 else "fp32"
+
+
+def _flags(flags: Optional[int]) -> int:
+    if flags is not None:
+        return int(flags)
+    return -1 if _math_override is None else _math_override
+
+
+def _pair(x) -> Tuple[int, int]:
+    if isinstance(x, (tuple, list)):
+        return int(x[0]), int(x[1])
+    return int(x), int(x)
+
+
+class _DeformConv2dFunction(torch.autograd.Function):
+    """Autograd node over the native forward / backward operators.
+
+    Same saved tensors and gradient layout as the reference's
+    ``_DeformConv2dFunction`` (src/deform_conv2d_mps/ops.py:68-115).
+    """
+
+    @staticmethod
+    def forward(ctx, input, weight, offset, mask, bias, stride, padding,
+                dilation, groups, deformable_groups, flags):
+        ops = _native.load_ops()
+        empty = input.new_empty(0)
+        out = ops.deform_conv2d_forward(
+            input, weight, offset, mask if mask is not None else empty, bias,
+            stride[0], stride[1], padding[0], padding[1], dilation[0],
+            dilation[1], groups, deformable_groups, math=flags)
+        ctx.save_for_backward(input, weight, offset,
+                              mask if mask is not None else empty,
+                              bias if bias is not None else empty)
+        ctx.params = (stride, padding, dilation, groups, deformable_groups, flags)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        input, weight, offset, mask, bias = ctx.saved_tensors
+        stride, padding, dilation, groups, deformable_groups, flags = ctx.params
+        has_mask = mask.numel() > 0
+        has_bias = bias.numel() > 0
+        ops = _native.load_ops()
+        grad_input, grad_offset, grad_mask, grad_weight, grad_bias = \
+            ops.deform_conv2d_backward(
+                grad_output.contiguous(), input, weight, offset, mask,
+                bias if has_bias else None, stride[0], stride[1], padding[0],
+                padding[1], dilation[0], dilation[1], groups,
+                deformable_groups, math=flags)
+        return (grad_input, grad_weight, grad_offset,
+                grad_mask if has_mask else None,
+                grad_bias if has_bias else None,
+                None, None, None, None, None, None)
+
+
+def deform_conv2d(
+    input: Tensor,
+    offset: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor] = None,
+    stride=(1, 1),
+    padding=(0, 0),
+    dilation=(1, 1),
+    mask: Optional[Tensor] = None,
+) -> Tensor:
+    """Deformable Conv2d (DCNv2; DCNv1 when ``mask is None``).
+
+    Signature of ``torchvision.ops.deform_conv2d``; ``groups`` and
+    ``deformable_groups`` are inferred from ``weight`` and ``offset`` like the
+    reference does (src/deform_conv2d_mps/ops.py:151-153).
+    """
+    return deform_conv2d_ex(input, offset, weight, bias, stride, padding,
+                            dilation, mask)
+
+
+def deform_conv2d_ex(input, offset, weight, bias=None, stride=(1, 1),
+                     padding=(0, 0), dilation=(1, 1), mask=None,
+                     flags: Optional[int] = None) -> Tensor:
+    """:func:`deform_conv2d` with an explicit C-ABI flag word (``MATH_*`` |
+    ``ALGO_*``); ``flags=None`` uses the current math mode."""
+    stride, padding, dilation = _pair(stride), _pair(padding), _pair(dilation)
+    for name, t in (("input", input), ("offset", offset), ("weight", weight),
+                    ("bias", bias), ("mask", mask)):
+        if t is not None and t.device.type != "cuda":
+            raise NotImplementedError(
+                f"pytorch_mps_deform_conv2d_b200.deform_conv2d runs on CUDA "
+                f"(sm_100a) tensors only; {name} is on {t.device}")
+    kh, kw = weight.shape[-2], weight.shape[-1]
+    if weight.dim() != 4 or weight.shape[1] == 0:
+        raise RuntimeError("weight must be 4-D (outC, C/groups, kh, kw) with C/groups > 0")
+    groups = input.shape[1] // weight.shape[1]
+    deformable_groups = offset.shape[1] // (2 * kh * kw)
+    return _DeformConv2dFunction.apply(
+        input, weight, offset, mask, bias, stride, padding, dilation, groups,
+        deformable_groups, _flags(flags))
