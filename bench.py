@@ -1,0 +1,570 @@
+#!/usr/bin/env python
+"""Benchmark: DCNv2 forward + backward on the detection-neck workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--math tf32|fp32] [--workload neck|train|grouped|dcnv1]
+
+One step is one training pass of the deformable convolution over one batch:
+forward, backward with a fixed upstream gradient, and (N > 1) the NCCL
+all-reduce of grad_weight / grad_bias.  Each rank holds its own full batch
+(weak scaling, data parallel), so `value` -- milliseconds per iteration of
+the 2x256x100x152 workload for the whole job -- is the per-step time (max
+over ranks) divided by the number of batches all ranks processed.
+
+Inputs are synthetic, seeded CPU tensors with the workload's shapes and
+distributions (x randn, weight kaiming_uniform(a=sqrt 5), bias randn, offset
+N(0, 4^2), mask sigmoid(randn), grad_out randn), copied to the device before
+timing.  L2 is flushed (a 256 MiB write) between timed iterations, outside
+the timed events.
+
+The printed JSON line carries the roofline of the dominant kernel (timed live
+with the library's CUDA-event profiler), the CPU baseline (the reference
+package's own CPU route -- torchvision's kernel -- on a bounded sample of the
+same workload) and an end-to-end number through the public module API with
+host<->device copies inside the timed region.
+
+`--impl reference` times the reference's CPU implementation alone (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = ("DCNv2 fwd+bwd ms/iter (2×256×100×152) and % roofline at 1/2/4/8 "
+          "B200 vs host CPU")
+
+WORKLOADS = {
+    "neck": dict(desc="detection-neck DCNv2 fwd+bwd: x 2x256x100x152, weight 256x256x3x3, "
+                      "bias, stride 1, pad 1, dil 1, dg 1, offset N(0,4^2), mask sigmoid(randn)",
+                 N=2, C=256, outC=256, H=100, W=152, k=3, stride=(1, 1), pad=(1, 1),
+                 dil=(1, 1), groups=1, dg=1, offset_std=4.0, mask=True, bias=True),
+    "train": dict(desc="DCNv2 training step: x 8x64x64x64, weight 64x64x3x3, bias, pad 1, "
+                       "offset N(0,2^2), mask sigmoid(randn)",
+                  N=8, C=64, outC=64, H=64, W=64, k=3, stride=(1, 1), pad=(1, 1), dil=(1, 1),
+                  groups=1, dg=1, offset_std=2.0, mask=True, bias=True),
+    "grouped": dict(desc="grouped DCNv2: x 8x64x64x64, weight 64x2x3x3 (groups 32), dg 4, pad 1, "
+                         "offset N(0,2^2), mask sigmoid(randn), bias",
+                    N=8, C=64, outC=64, H=64, W=64, k=3, stride=(1, 1), pad=(1, 1), dil=(1, 1),
+                    groups=32, dg=4, offset_std=2.0, mask=True, bias=True),
+    "dcnv1": dict(desc="DCNv1 sweep: x 64x512x28x28, weight 512x512x3x3, no bias, stride (2,1), "
+                       "pad (2,1), dil (2,1), dg 8, offset N(0,3^2), no mask",
+                  N=64, C=512, outC=512, H=28, W=28, k=3, stride=(2, 1), pad=(2, 1), dil=(2, 1),
+                  groups=1, dg=8, offset_std=3.0, mask=False, bias=False),
+}
+
+FLUSH_BYTES = 256 << 20
+
+
+def out_hw(wl):
+    k = wl["k"]
+    ho = (wl["H"] + 2 * wl["pad"][0] - wl["dil"][0] * (k - 1) - 1) // wl["stride"][0] + 1
+    wo = (wl["W"] + 2 * wl["pad"][1] - wl["dil"][1] * (k - 1) - 1) // wl["stride"][1] + 1
+    return ho, wo
+
+
+def make_inputs(wl, seed=0, n=None, c_in=None):
+    """Seeded CPU tensors in the order x, weight, bias, offset, mask, grad_out.
+    `n` / `c_in` cut a sample: the first n images / first c_in input channels."""
+    import torch
+    torch.manual_seed(seed)
+    N, C, O, H, W, k = wl["N"], wl["C"], wl["outC"], wl["H"], wl["W"], wl["k"]
+    g, dg = wl["groups"], wl["dg"]
+    ho, wo = out_hw(wl)
+    x = torch.randn(N, C, H, W)
+    w = torch.empty(O, C // g, k, k)
+    torch.nn.init.kaiming_uniform_(w, a=math.sqrt(5))
+    b = torch.randn(O) if wl["bias"] else None
+    off = wl["offset_std"] * torch.randn(N, 2 * dg * k * k, ho, wo)
+    m = torch.sigmoid(torch.randn(N, dg * k * k, ho, wo)) if wl["mask"] else None
+    go = torch.randn(N, O, ho, wo)
+    if n is not None:
+        x, off, go = x[:n], off[:n], go[:n]
+        m = m[:n] if m is not None else None
+    if c_in is not None:
+        assert g == 1
+        x, w = x[:, :c_in].contiguous(), w[:, :c_in].contiguous()
+    return x, w, b, off, m, go
+
+
+def algorithmic_work(wl):
+    """FLOPs and compulsory HBM bytes of one fwd+bwd iteration."""
+    N, C, O, k, g, dg = wl["N"], wl["C"], wl["outC"], wl["k"], wl["groups"], wl["dg"]
+    ho, wo = out_hw(wl)
+    P = ho * wo
+    gemm = 2.0 * O * (C // g) * k * k * N * P
+    x = N * C * wl["H"] * wl["W"]
+    off = N * 2 * dg * k * k * P
+    msk = N * dg * k * k * P if wl["mask"] else 0
+    wts = O * (C // g) * k * k
+    bia = O if wl["bias"] else 0
+    out = N * O * P
+    fwd = x + off + msk + wts + bia + out
+    bwd = (out + x + off + msk + wts) + (x + off + msk + wts + bia)
+    return dict(flops=3 * gemm, gemm_flops=gemm, bytes=4.0 * (fwd + bwd), P=P)
+
+
+def kernel_work(name, wl):
+    """(amount, unit, bound) of one launch of a library kernel."""
+    w = algorithmic_work(wl)
+    N, C = wl["N"], wl["C"]
+    if name.startswith(("fwd_", "bwd_data", "bwd_weight")):
+        return w["gemm_flops"], "flop", "tensor"
+    if name in ("nchw_to_nhwc", "nhwc_to_nchw"):
+        return 2.0 * 4 * N * C * wl["H"] * wl["W"], "byte", "hbm"
+    if name == "grad_bias":
+        return 4.0 * N * wl["outC"] * w["P"], "byte", "hbm"
+    return None, None, None
+
+
+# ---------------------------------------------------------------------------
+# peaks
+# ---------------------------------------------------------------------------
+def measured_peaks_file():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "MEASURED_PEAKS.json"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def measure_matmul_tflops(dtype_mode, n=8192, reps=5):
+    """cuBLAS burst throughput, best of `reps` (torch.matmul n^3, 2 n^3 flop)."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    dt = torch.bfloat16 if dtype_mode == "bf16" else torch.float32
+    torch.backends.cuda.matmul.allow_tf32 = dtype_mode == "tf32"
+    try:
+        a = torch.randn(n, n, device="cuda", dtype=dt)
+        b = torch.randn(n, n, device="cuda", dtype=dt)
+        for _ in range(2):
+            torch.matmul(a, b)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU route on a bounded sample
+# ---------------------------------------------------------------------------
+def reference_cpu_op():
+    """The reference package's public deform_conv2d (its CPU route calls
+    torchvision's kernel, src/deform_conv2d_mps/ops.py:165-169); torchvision
+    directly when the package is not installed under baseline/_ref."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if os.path.isdir(os.path.join(ref_dir, "deform_conv2d_mps")):
+        if ref_dir not in sys.path:
+            sys.path.insert(0, ref_dir)
+        from deform_conv2d_mps import deform_conv2d as ref_op
+        return ref_op, "reference package deform_conv2d_mps 0.1.0 (CPU route -> torchvision)"
+    from torchvision.ops import deform_conv2d as tv_op
+    return tv_op, "torchvision.ops.deform_conv2d (the reference's CPU route)"
+
+
+def cpu_sample_plan(wl):
+    """A sample of the workload: one image and a slice of the input channels.
+    Every term of the op's cost is linear in images x input channels, so the
+    per-iteration time is the sample time times `scale`."""
+    n = 1
+    c_in = wl["C"]
+    if wl["groups"] == 1:
+        while c_in > 32 and (wl["N"] // n) * (wl["C"] // c_in) < 16:
+            c_in //= 2
+    scale = (wl["N"] / n) * (wl["C"] / c_in)
+    return n, c_in, scale
+
+
+def cpu_reference_step_fn(wl, threads):
+    import torch
+    torch.set_num_threads(threads)
+    op, label = reference_cpu_op()
+    n, c_in, scale = cpu_sample_plan(wl)
+    x, w, b, off, m, go = make_inputs(wl, n=n, c_in=c_in if c_in != wl["C"] else None)
+    leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, w, b, off, m)]
+
+    def step():
+        for t in leaves:
+            if t is not None:
+                t.grad = None
+        xx, ww, bb, oo, mm = leaves
+        out = op(xx, oo, ww, bias=bb, stride=wl["stride"], padding=wl["pad"],
+                 dilation=wl["dil"], mask=mm)
+        out.backward(go)
+
+    sample = (f"{n} of {wl['N']} images x {c_in} of {wl['C']} input channels of the workload "
+              f"(1/{scale:g} of its work; every cost term is linear in images x input channels), "
+              f"fwd+bwd through {label}; value = sample time x {scale:g}")
+    return step, scale, sample
+
+
+def cpu_baseline(wl, min_seconds=10.0):
+    import torch
+    threads = os.cpu_count() or 1
+    step, scale, sample = cpu_reference_step_fn(wl, threads)
+    step()  # warm-up
+    times = []
+    t_end = time.perf_counter() + min_seconds
+    while len(times) < 2 or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    ms = statistics.mean(times) * 1e3 * scale
+    return {"value": round(ms, 3), "unit": "ms/iter", "cores": torch.get_num_threads(),
+            "kind": "reference", "sample": sample + f"; {len(times)} timed sample steps"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+    import pytorch_mps_deform_conv2d_b200 as dcn
+    from pytorch_mps_deform_conv2d_b200 import _native
+    from pytorch_mps_deform_conv2d_b200.ops import MATH_FP32, MATH_TF32, deform_conv2d_ex
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    flags = MATH_TF32 if args.math == "tf32" else MATH_FP32
+
+    x, w, b, off, m, go = make_inputs(wl, seed=rank)
+    xd, offd, md, god = (t.to(dev) if t is not None else None for t in (x, off, m, go))
+    wd = w.to(dev).requires_grad_(True)
+    bd = b.to(dev).requires_grad_(True) if b is not None else None
+    xd.requires_grad_(True)
+    offd.requires_grad_(True)
+    if md is not None:
+        md.requires_grad_(True)
+    params = [p for p in (wd, bd) if p is not None]
+    leaves = [t for t in (xd, offd, md, wd, bd) if t is not None]
+    flush = torch.empty(FLUSH_BYTES // 4, device=dev)
+    comm_stream = torch.cuda.current_stream(dev)
+
+    def allreduce(grads):
+        if world == 1:
+            return
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        dist.all_reduce(flat)
+        o = 0
+        for g in grads:
+            g.copy_(flat[o:o + g.numel()].view_as(g))
+            o += g.numel()
+
+    def step():
+        for t in leaves:
+            t.grad = None
+        out = deform_conv2d_ex(xd, offd, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
+                               flags=flags)
+        out.backward(god)
+        allreduce([p.grad for p in params])
+
+    for _ in range(args.warmup):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    _native.profiler_read()  # drop anything recorded before
+    clocks = ClockSampler(local)
+    with clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        _native.profiler_enable(True)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        _native.profiler_enable(False)
+        if world > 1:
+            dist.barrier()
+    kstats = _native.profiler_read()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = ms_per_step / world
+
+    # ---- dominant kernel roofline ----
+    kernels = {k: v for k, v in kstats.items() if k != "memset"}
+    launches = sum(v[0] for v in kernels.values())
+    dom = max(kernels, key=lambda k: kernels[k][1])
+    dom_launches, dom_ms = kernels[dom]
+    avg_ms = dom_ms / dom_launches
+    amount, unit, bound = kernel_work(dom, wl)
+    peaks, peaks_src = measured_peaks_file()
+    if args.profile:
+        peak_tf32 = 0.5 * peaks.get("bf16_tflops", 1590.0)
+        peak_fp32 = peak_tf32 / 8.0
+    else:
+        peak_tf32 = measure_matmul_tflops("tf32")
+        peak_fp32 = measure_matmul_tflops("fp32")
+    roof = {"kernel": dom, "bound": bound, "share_of_step": round(dom_ms / total_ms, 3)
+            if world == 1 else None}
+    if bound == "tensor":
+        if dom.endswith("_tc"):
+            peak = peak_tf32
+            src = ("cuBLAS tf32 8192^3 burst measured in this run (MEASURED_PEAKS.json holds bf16 "
+                   f"only: {peaks.get('bf16_tflops')} TFLOP/s)")
+        else:
+            peak = peak_fp32
+            src = "cuBLAS fp32 (FFMA, no TF32) 8192^3 burst measured in this run"
+        achieved = amount / (avg_ms * 1e-3) / 1e12
+        roof.update(achieved=round(achieved, 2), peak=round(peak, 1), unit="TFLOP/s",
+                    frac=round(achieved / peak, 3), peak_source=src,
+                    flop_per_launch=amount)
+    else:
+        peak = peaks.get("hbm_gbs", 6650.0)
+        achieved = amount / (avg_ms * 1e-3) / 1e9
+        roof.update(achieved=round(achieved, 1), peak=peak, unit="GB/s",
+                    frac=round(achieved / peak, 3), peak_source=f"{peaks_src} hbm_gbs",
+                    bytes_per_launch=amount)
+    traffic = load_traffic().get(f"{args.workload}:{args.math}:{dom}")
+    roof["traffic"] = traffic["bytes_per_launch"] if traffic else None
+    work = algorithmic_work(wl)
+    step_roof_ms = work["flops"] / ((peak_tf32 if flags == MATH_TF32 else peak_fp32) * 1e12) * 1e3
+    roof["step_roofline_ms"] = round(max(step_roof_ms, work["bytes"] / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3), 4)
+    roof["step_frac"] = round(roof["step_roofline_ms"] / ms_per_step, 3)
+    roof["peaks_measured_tflops"] = {"tf32": round(peak_tf32, 1), "fp32": round(peak_fp32, 1)}
+
+    # ---- end to end through the public module API, host buffers ----
+    e2e = None if args.profile else run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags,
+                                            allreduce, flush)
+
+    kernel_table = {k: {"launches": v[0], "ms_per_launch": round(v[1] / v[0], 4)}
+                    for k, v in sorted(kernels.items(), key=lambda kv: -kv[1][1])}
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "tf32" if any(k.endswith("_tc") for k in kernels) else "f32",
+        "data": "synthetic",
+        "config": {"workload": wl["desc"], "global_batch": wl["N"] * world,
+                   "per_gpu_batch": wl["N"], "parallelism": f"dp{world}",
+                   "math": args.math, "l2": "flushed between timed iterations (256 MiB write, "
+                                             "outside the timed events)",
+                   "wall_s": round(wall, 3)},
+        "roofline": roof, "e2e": e2e, "gpu_launches": launches,
+        "kernels": kernel_table,
+    }
+    if world == 1 and not (args.no_cpu_baseline or args.profile):
+        line["cpu_baseline"] = cpu_baseline(wl)
+    clk = clocks.summary()
+    line["clocks"] = {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                      "reasons": clk["reasons"]}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
+    """Same step through the public module API with the batch coming from
+    pinned host memory and the parameter gradients read back each step."""
+    import torch
+    import pytorch_mps_deform_conv2d_b200 as dcn
+    mod = dcn.DeformConv2d(wl["C"], wl["outC"], wl["k"], stride=wl["stride"], padding=wl["pad"],
+                           dilation=wl["dil"], groups=wl["groups"], bias=wl["bias"]).to(dev)
+    with torch.no_grad():
+        mod.weight.copy_(w)
+        if b is not None:
+            mod.bias.copy_(b)
+    dcn.set_math_mode("tf32" if flags & 0xff else "fp32")
+    host = [t.pin_memory() if t is not None else None for t in (x, off, m, go)]
+    params = [p for p in mod.parameters()]
+    outs = [torch.empty(p.shape, pin_memory=True) for p in params]
+    h2d = sum(t.numel() * 4 for t in host if t is not None)
+    d2h = sum(p.numel() * 4 for p in params)
+
+    def step():
+        xh, oh, mh, gh = host
+        xd = xh.to(dev, non_blocking=True).requires_grad_(True)
+        od = oh.to(dev, non_blocking=True).requires_grad_(True)
+        md = mh.to(dev, non_blocking=True).requires_grad_(True) if mh is not None else None
+        gd = gh.to(dev, non_blocking=True)
+        for p in params:
+            p.grad = None
+        out = mod(xd, od, md)
+        out.backward(gd)
+        allreduce([p.grad for p in params])
+        for p, o in zip(params, outs):
+            o.copy_(p.grad, non_blocking=True)
+
+    try:
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step()
+            e1.record()
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+    finally:
+        dcn.set_math_mode(None)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([tot], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tot = float(t.item())
+    return {"value": round(tot / args.steps / world, 4), "unit": "ms/iter",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    step, scale, sample = cpu_reference_step_fn(wl, threads)
+    import torch
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    sec = time.perf_counter() - t0
+    value = sec / args.steps * 1e3 * scale
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "ms/iter",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["desc"], "global_batch": wl["N"], "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "ms/iter",
+                         "cores": torch.get_num_threads(), "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "ms/iter", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--math", choices=["tf32", "fp32"], default="tf32")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="device steps only (no CPU baseline, no e2e pass, no cuBLAS peak "
+                         "runs): the command the ncu captures wrap")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

@@ -138,6 +138,22 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
                              int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
                              int64_t deformable_groups, void* stream);
 
+/* Kernel profiler (no reference counterpart: the reference times its ops
+ * with wall clocks around torch.mps.synchronize(), benchmarks/bench.py:39-49).
+ * When enabled, every kernel launch and scratch memset of the entry points
+ * above is bracketed by a CUDA event pair on its stream.  dcn_profiler_read
+ * waits for the recorded events, reports per-name launch counts and summed
+ * device milliseconds (at most max_stats entries; *count gets the number of
+ * names) and clears the records.  Events are created on first use. */
+typedef struct dcn_kernel_stat {
+  char name[48];
+  int64_t launches;
+  double total_ms;
+} dcn_kernel_stat;
+
+DCN_API int dcn_profiler_enable(int enable);
+DCN_API int dcn_profiler_read(dcn_kernel_stat* stats, int max_stats, int* count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,12 @@ class DcnShape(ctypes.Structure):
         "dilation_w", "groups", "deformable_groups")]
 
 
+class KernelStat(ctypes.Structure):
+    """``dcn_kernel_stat`` of include/dcn_b200.h."""
+    _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_int64),
+                ("total_ms", ctypes.c_double)]
+
+
 def load_capi():
     """ctypes handle of libdcn_b200.so with the C ABI prototypes set."""
     global _capi
@@ -79,9 +85,32 @@ def load_capi():
         lib.dcn_col2im.restype = ctypes.c_int
         lib.dcn_col2im_coord.argtypes = [vp] * 6 + [i64] * 12 + [vp]
         lib.dcn_col2im_coord.restype = ctypes.c_int
+        lib.dcn_profiler_enable.argtypes = [ctypes.c_int]
+        lib.dcn_profiler_enable.restype = ctypes.c_int
+        lib.dcn_profiler_read.argtypes = [ctypes.POINTER(KernelStat), ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_int)]
+        lib.dcn_profiler_read.restype = ctypes.c_int
         _capi = lib
         return lib
 
 
 def capi_error() -> str:
     return load_capi().dcn_last_error().decode()
+
+
+def profiler_enable(on: bool = True) -> None:
+    """Bracket every kernel launch of the library with CUDA events."""
+    load_capi().dcn_profiler_enable(1 if on else 0)
+
+
+def profiler_read(max_kernels: int = 64):
+    """Per-kernel ``{name: (launches, total_ms)}`` since the last read
+    (waits for the recorded events)."""
+    lib = load_capi()
+    stats = (KernelStat * max_kernels)()
+    count = ctypes.c_int(0)
+    rc = lib.dcn_profiler_read(stats, max_kernels, ctypes.byref(count))
+    if rc != 0:
+        raise RuntimeError(capi_error())
+    return {stats[i].name.decode(): (int(stats[i].launches), float(stats[i].total_ms))
+            for i in range(min(count.value, max_kernels))}

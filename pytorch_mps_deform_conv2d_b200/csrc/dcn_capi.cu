@@ -7,7 +7,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "dcn_b200.h"
 #include "dcn_kernels.h"
@@ -36,10 +39,58 @@ int cuda_fail(cudaError_t e, const char* where) {
     if (!(cond)) return fail(DCN_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
   } while (0)
 
-#define DCN_CUDA(expr, where)                    \
-  do {                                           \
-    cudaError_t e_ = (expr);                     \
-    if (e_ != cudaSuccess) return cuda_fail(e_, where); \
+// ---- kernel profiler: a CUDA event pair around every launch when enabled --
+// (tracing for the bench and for users; off by default, one branch per
+// launch when off).
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof_recs;
+std::vector<cudaEvent_t> g_prof_pool;
+
+cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+struct ProfScope {
+  const char* name;
+  cudaStream_t stream;
+  cudaEvent_t start = nullptr;
+  ProfScope(const char* n, cudaStream_t s) : name(n), stream(s) {
+    if (!g_prof_on) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    start = prof_event();
+    if (start) cudaEventRecord(start, stream);
+  }
+  void done() {
+    if (!start) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEvent_t stop = prof_event();
+    if (stop) {
+      cudaEventRecord(stop, stream);
+      g_prof_recs.push_back({name, start, stop});
+    } else {
+      g_prof_pool.push_back(start);
+    }
+  }
+};
+
+#define DCN_CUDA(expr, where)                             \
+  do {                                                    \
+    ProfScope ps_(where, stream);                         \
+    cudaError_t e_ = (expr);                              \
+    ps_.done();                                           \
+    if (e_ != cudaSuccess) return cuda_fail(e_, where);   \
   } while (0)
 
 bool is_device_ptr(const void* p) {
@@ -364,6 +415,46 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input, const flo
                                            stream),
            "col2im_coord");
   return DCN_OK;
+}
+
+DCN_API int dcn_profiler_enable(int enable) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_on = enable != 0;
+  return DCN_OK;
+}
+
+DCN_API int dcn_profiler_read(dcn_kernel_stat* stats, int max_stats, int* count) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  std::map<std::string, std::pair<int64_t, double>> agg;
+  std::vector<std::string> order;
+  int rc = DCN_OK;
+  for (auto& r : g_prof_recs) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.stop) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, r.start, r.stop) != cudaSuccess) {
+      cudaGetLastError();
+      rc = fail(DCN_ERR_CUDA, "dcn_profiler_read: event query failed");
+    }
+    if (!agg.count(r.name)) order.push_back(r.name);
+    auto& a = agg[r.name];
+    a.first += 1;
+    a.second += ms;
+    g_prof_pool.push_back(r.start);
+    g_prof_pool.push_back(r.stop);
+  }
+  g_prof_recs.clear();
+  int n = 0;
+  for (auto& name : order) {
+    if (stats && n < max_stats) {
+      std::memset(&stats[n], 0, sizeof(dcn_kernel_stat));
+      std::strncpy(stats[n].name, name.c_str(), sizeof(stats[n].name) - 1);
+      stats[n].launches = agg[name].first;
+      stats[n].total_ms = agg[name].second;
+    }
+    ++n;
+  }
+  if (count) *count = n;
+  return rc;
 }
 
 }  // extern "C"
