@@ -1,0 +1,102 @@
+"""Batch-sharded data parallelism on CPU ranks (gloo, world size 2): sharded
+forward/backward with the oracle plus the all-reduce of grad_weight /
+grad_bias equals the single-process result; a rank that fails before the
+collective makes the others fail on a short timeout instead of hanging."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from pytorch_mps_deform_conv2d_b200.distributed import allreduce_grads, shard_batch, shard_range
+
+
+def test_shard_range_balanced():
+    for n in range(0, 11):
+        for w in range(1, 5):
+            sl = [shard_range(n, r, w) for r in range(w)]
+            assert sl[0].start == 0 and sl[-1].stop == n
+            assert all(a.stop == b.start for a, b in zip(sl, sl[1:]))
+            sizes = [s.stop - s.start for s in sl]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(4, 2, 2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, case, result_q, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the collective")
+        from oracle import oracle
+        x, off, m, go = shard_batch([case["x"], case["off"], case["m"], case["go"]], rank, world)
+        _, _, _, gw, gb = oracle.backward(go.numpy(), x.numpy(), off.numpy(), case["w"].numpy(),
+                                          case["b"].numpy(), 1, 1, 1, m.numpy())
+        w = torch.nn.Parameter(case["w"].clone())
+        b = torch.nn.Parameter(case["b"].clone())
+        w.grad, b.grad = torch.from_numpy(gw), torch.from_numpy(gb)
+        allreduce_grads([w, b])
+        result_q.put((rank, "ok", w.grad.numpy(), b.grad.numpy()))
+    except Exception as e:  # report, then leave the group
+        result_q.put((rank, "error", repr(e), None))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _case():
+    torch.manual_seed(0)
+    N, C, O, H, W = 4, 8, 6, 9, 10
+    return dict(x=torch.randn(N, C, H, W), w=torch.randn(O, C, 3, 3), b=torch.randn(O),
+                off=torch.randn(N, 18, H, W), m=torch.rand(N, 9, H, W), go=torch.randn(N, O, H, W))
+
+
+def _run(world, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    case = _case()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, fail_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return case, sorted(out, key=lambda r: r[0])
+
+
+def test_sharded_grads_equal_full_batch():
+    from oracle import oracle
+    case, out = _run(2)
+    _, _, _, gw, gb = oracle.backward(case["go"].numpy(), case["x"].numpy(), case["off"].numpy(),
+                                      case["w"].numpy(), case["b"].numpy(), 1, 1, 1,
+                                      case["m"].numpy())
+    for rank, status, rgw, rgb in out:
+        assert status == "ok", rgw
+        np.testing.assert_allclose(rgw, gw, rtol=1e-5, atol=1e-4)
+        np.testing.assert_allclose(rgb, gb, rtol=1e-5, atol=1e-4)
+
+
+def test_failed_rank_surfaces_as_error_not_hang():
+    _, out = _run(2, fail_rank=1)
+    assert out[1][1] == "error" and "injected" in out[1][2]
+    assert out[0][1] == "error"  # the survivor's collective fails on the timeout
