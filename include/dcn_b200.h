@@ -138,6 +138,25 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
                              int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
                              int64_t deformable_groups, void* stream);
 
+/* Forward for callers that cannot allocate device memory.  No counterpart in
+ * the reference: it exists for code that may not call cudaMalloc (inside an
+ * allocator's or memory pool's own hooks, host-framework plugins that only
+ * receive input and output buffers, deployments that fix device memory at
+ * start-up).  Same arguments and results as dcn_forward without the workspace:
+ * the scratch comes from a 16 MiB array compiled into the library, which every
+ * GPU that loads the library holds until the process exits.  Shapes whose
+ * dcn_forward_workspace_size exceeds 16 MiB are rejected with
+ * DCN_ERR_WORKSPACE before anything is launched.  The first call on a device
+ * looks up the array's device address there (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls that can overlap on the GPU (different streams, or different host
+ * threads on the same device) race on it and must be serialised by the
+ * caller.  Nothing in the array needs to start at zero: each call overwrites
+ * the part it uses before reading it. */
+DCN_API int dcn_forward_noalloc(const dcn_shape* shape, const float* input,
+                                const float* weight, const float* offset, const float* mask,
+                                const float* bias, float* output, uint32_t flags, void* stream);
+
 /* Kernel profiler (no reference counterpart: the reference times its ops
  * with wall clocks around torch.mps.synchronize(), benchmarks/bench.py:39-49).
  * When enabled, every kernel launch and scratch memset of the entry points

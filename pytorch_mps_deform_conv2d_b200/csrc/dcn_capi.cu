@@ -212,6 +212,11 @@ void* align_ptr(void* p) {
 
 }  // namespace
 
+namespace dcn {
+// Lets other translation units of the library report through dcn_last_error.
+void set_last_error(int code, const char* msg) { fail(code, "%s", msg); }
+}  // namespace dcn
+
 extern "C" {
 
 DCN_API int dcn_abi_version(void) { return DCN_ABI_VERSION; }
