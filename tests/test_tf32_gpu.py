@@ -1,0 +1,68 @@
+"""TF32 tensor-core mode (tcgen05): parity against the CPU oracle within the
+stated TF32 tolerance -- outputs <= 5e-3 relative (norm-wise, and element-wise
+against 5e-3 x max|ref|) -- and checks that the tensor-core kernels are the
+ones that ran."""
+import numpy as np
+import pytest
+import torch
+
+from _util import make_case, rel_norm_err, run_oracle, run_ours
+from pytorch_mps_deform_conv2d_b200 import _native
+from pytorch_mps_deform_conv2d_b200.ops import MATH_TF32
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL = 5e-3
+
+TC_CASES = {
+    "c32-o32": dict(inC=32, outC=32, H=12, W=14, offset_scale=2.0),
+    "c64-o48-v1-nobias": dict(inC=64, outC=48, H=11, W=9, use_mask=False, use_bias=False),
+    "c64-o64-dg2": dict(inC=64, outC=64, dg=2, H=10, W=13, offset_scale=3.0),
+    "c64-o32-g2": dict(inC=64, outC=32, groups=2, H=9, W=9),
+    "c128-o16-asym": dict(inC=128, outC=16, H=8, W=11, kh=1, kw=3, stride=(2, 1),
+                          pad=(0, 2), dil=(2, 1)),
+    "c32-o512-ntiles": dict(N=1, inC=32, outC=512, H=7, W=9),
+    "c64-o256-boundary": dict(N=3, inC=64, outC=256, H=13, W=17, offset_scale=8.0),
+    "c256-o256-neck-like": dict(N=1, inC=256, outC=256, H=20, W=30, offset_scale=4.0,
+                                mask_kind="sigmoid", weight_kind="kaiming"),
+    "c512-o512-dcnv1-like": dict(N=2, inC=512, outC=512, H=10, W=10, stride=(2, 1),
+                                 pad=(2, 1), dil=(2, 1), dg=8, use_mask=False,
+                                 use_bias=False, offset_scale=3.0, weight_kind="kaiming"),
+}
+
+
+@pytest.mark.parametrize("name", sorted(TC_CASES))
+def test_forward_tf32(cuda_device, name):
+    case = make_case(**TC_CASES[name])
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out, _ = run_ours(case, flags=MATH_TF32, backward=False)
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    assert "fwd_tc" in stats, f"tensor-core forward did not run: {sorted(stats)}"
+    ref, _ = run_oracle(case, backward=False)
+    assert rel_norm_err(out, ref) <= OUT_TOL
+    np.testing.assert_allclose(out, ref, rtol=0, atol=OUT_TOL * float(np.abs(ref).max()))
+
+
+def test_tf32_falls_back_to_fp32_kernels_when_shape_not_covered(cuda_device):
+    case = make_case(inC=6, outC=6)  # 6 channels per group: no tensor-core tiling
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out, _ = run_ours(case, flags=MATH_TF32, backward=False)
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    assert "fwd_tc" not in stats
+    ref, _ = run_oracle(case, backward=False)
+    np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-4 * max(1, np.abs(ref).max()))
+
+
+def test_tf32_repeatable(cuda_device):
+    case = make_case(inC=64, outC=64, H=16, W=16, offset_scale=2.0)
+    a, _ = run_ours(case, flags=MATH_TF32, backward=False)
+    b, _ = run_ours(case, flags=MATH_TF32, backward=False)
+    assert np.array_equal(a, b)  # the forward has no atomics: bitwise repeatable
