@@ -1,0 +1,519 @@
+// dcn_bwd_tc.cu -- backward deformable convolution on tcgen05 tensor cores
+// (kind::tf32, fp32 accumulation in tensor memory).
+//
+//  prep          go -> go_t (pixel-major [n][p][o]) and go_r (NCHW), both
+//                rounded to TF32 with round-to-nearest.
+//  bwd_data_tc   per 128-pixel tile and tap k:
+//                  gcol[q, c] = sum_o go[q, o] W[o, c, k]            (.mm:820-821)
+//                on the tensor core, then an epilogue that reads each pixel's
+//                row of gcol out of tensor memory and, in the same pass,
+//                  * scatters gcol * mask * corner weight into the NHWC
+//                    grad-input accumulator (col2im, deform_conv2d.metal:141-204)
+//                    with 16-byte vector reductions;
+//                  * sums the coordinate and mask gradients over the channels
+//                    (col2im_coord, deform_conv2d.metal:225-295) -- a pixel's
+//                    channels are all in its thread, so the sums are local.
+//  bwd_weight_tc gW'[c, o] = sum_q col[q, c] go[q, o] for 128 channels of one
+//                tap, split over pixel ranges (.mm:842-880).  The column tile
+//                is gathered (bilinear sampling, as in the forward) straight
+//                into an MN-major operand (32-byte-atom swizzle); go_r rows arrive by
+//                cp.async.  Partial tiles are reduced into grad_weight.
+#include "dcn_tc.h"
+#include "dcn_tc_common.cuh"
+
+namespace dcn {
+
+__device__ int g_tc_bwd_status;  // set to 1 by a wait that ran out
+
+namespace {
+
+constexpr int THREADS = 256;
+
+int pow2_cols(int n) {
+  int c = 32;
+  while (c < n) c <<= 1;
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// prep: go (N, outC, P) -> go_t (N*P, outC) and go_r (N, outC, P), tf32-rounded
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
+                                                      float* __restrict__ go_t,
+                                                      float* __restrict__ go_r, int outC,
+                                                      int P, int Ppad) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int o0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const float* src = go + (long long)n * outC * P;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int o = o0 + ty + i, p = p0 + tx;
+    if (o < outC && p < Ppad) {
+      const float v = p < P ? tc::to_tf32(src[(long long)o * P + p]) : 0.f;
+      tile[ty + i][tx] = v;
+      go_r[((long long)n * outC + o) * Ppad + p] = v;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int p = p0 + ty + i, o = o0 + tx;
+    if (o < outC && p < P) go_t[((long long)n * P + p) * outC + o] = tile[tx][ty + i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bwd_data_tc
+// ---------------------------------------------------------------------------
+constexpr int D_BM = 128;
+
+size_t data_smem_bytes(int bn) { return 2 * 16384 + 2 * (size_t)bn * 128 + 64 + 1024; }
+
+__global__ void __launch_bounds__(THREADS, 2)
+bwd_data_tc_kernel(Geom g, const float* __restrict__ go_t, const float* __restrict__ wb,
+                   int bn, int tcols, const float* __restrict__ xt,
+                   const float* __restrict__ off, const float* __restrict__ mask,
+                   float* __restrict__ gxt, float* __restrict__ goff,
+                   float* __restrict__ gmask) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_u32 = tc::smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  const uint32_t sA0 = tc::smem_u32(smem);
+  const uint32_t sB0 = sA0 + 2 * 16384;
+  const uint32_t b_stage = (uint32_t)bn * 128;
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 2 * 16384 + 2 * b_stage);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long q0 = (long long)blockIdx.x * D_BM;
+  const int c0 = blockIdx.y * bn;  // channel tile within the group
+  const int gi = blockIdx.z;
+  const int ochunks = g.Og >> 5;
+
+  if (tid == 0) {
+    tc::mbar_init(&mma_bar[0], 1);
+    tc::mbar_init(&mma_bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, (uint32_t)tcols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = tc::idesc_tf32(D_BM, bn);
+
+  // epilogue identity: pixel row r, channel half
+  const int lq = warp & 3, half = warp >> 2;
+  const int r = lq * 32 + lane;
+  const long long q = q0 + r;
+  const bool valid = q < g.NP;
+  const int n = valid ? (int)(q / g.P) : 0;
+  const int p = valid ? (int)(q - (long long)n * g.P) : 0;
+  const int oy = p / g.Wo, ox = p - oy * g.Wo;
+  const float* xt_n = xt + (long long)n * g.HW * g.C;
+  float* gxt_n = gxt + (long long)n * g.HW * g.C;
+
+  int s_global = 0;  // K steps issued so far (stage / parity bookkeeping)
+  for (int k = 0; k < g.kk; ++k) {
+    // ---- mainloop: gcol_k = go_t[tile] . W_k^T over Og in 32-wide steps ----
+    const float* bsrc = wb + ((size_t)(gi * g.kk + k) * g.Cg + c0) * g.Og;
+    for (int s = 0; s < ochunks; ++s, ++s_global) {
+      const int st = s_global & 1;
+      if (s_global >= 2) tc::mbar_wait(&mma_bar[st], ((s_global - 2) >> 1) & 1, &g_tc_bwd_status);
+      const uint32_t sA = sA0 + st * 16384, sB = sB0 + st * b_stage;
+      // A: 128 pixel rows x 32 out channels
+      for (int i = tid; i < D_BM * 8; i += THREADS) {
+        const int row = i >> 3, j = i & 7;
+        const long long qq = q0 + row;
+        const uint32_t dst = sA + tc::sw128_offset(row, j);
+        if (qq < g.NP)
+          tc::cp_async16(dst, go_t + qq * g.outC + (long long)gi * g.Og + s * 32 + j * 4);
+        else
+          tc::st_shared_v4(dst, 0.f, 0.f, 0.f, 0.f);
+      }
+      // B: bn channel rows x 32 out channels
+      for (int i = tid; i < bn * 8; i += THREADS) {
+        const int row = i >> 3, j = i & 7;
+        tc::cp_async16(sB + tc::sw128_offset(row, j), bsrc + (size_t)row * g.Og + s * 32 + j * 4);
+      }
+      tc::cp_async_wait_all();
+      tc::fence_proxy_async();
+      __syncthreads();
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          tc::umma_tf32(tmem, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
+                        (s | j) != 0 ? 1u : 0u);
+        tc::umma_commit(&mma_bar[st]);
+      }
+    }
+    const int last = s_global - 1;
+    tc::mbar_wait(&mma_bar[last & 1], (last >> 1) & 1, &g_tc_bwd_status);
+    tc::tc_fence_after();
+
+    // ---- epilogue: col2im scatter + coordinate / mask sums ----
+    const int ki = k / g.kw, kj = k - ki * g.kw;
+    const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
+    int cur_dgi = -1;
+    Sample sp = make_sample(-2.f, -2.f, 1, 1);
+    float msk = 0.f, s_h = 0.f, s_w = 0.f, s_m = 0.f;
+    for (int cb = cbeg; cb < cend; cb += 16) {
+      float gc[16];
+      {
+        float t0[8], t1[8];
+        const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb;
+        tc::tmem_ld8(ta, t0);
+        tc::tmem_ld8(ta + 8, t1);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gc[j] = t0[j];
+          gc[8 + j] = t1[j];
+        }
+      }
+      if (!valid) continue;
+      const int gch = gi * g.Cg + c0 + cb;  // 16 channels gch .. gch+15, one dg group
+      const int dgi = gch / g.cpg;
+      if (dgi != cur_dgi) {
+        if (cur_dgi >= 0 && sp.valid) {
+          const long long oi = off_h_index(g, n, cur_dgi, k, p);
+          red_add_f32(goff + oi, s_h);
+          red_add_f32(goff + oi + g.P, s_w);
+          if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+        }
+        s_h = s_w = s_m = 0.f;
+        cur_dgi = dgi;
+        const long long oi = off_h_index(g, n, dgi, k, p);
+        float h, w;
+        sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+        msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+        sp = make_sample(h, w, g.H, g.W);
+      }
+      if (!sp.valid) continue;
+      // corner values of the 16 channels
+      float4 v[4][4];
+      const float* base = xt_n + gch;
+      const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4)
+          v[c][h4] = (sp.live >> c) & 1u ? ldg4(base + (long long)ci[c] * g.C + 4 * h4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int h4 = 0; h4 < 4; ++h4) {
+        const float a[4] = {v[0][h4].x, v[0][h4].y, v[0][h4].z, v[0][h4].w};
+        const float b[4] = {v[1][h4].x, v[1][h4].y, v[1][h4].z, v[1][h4].w};
+        const float c[4] = {v[2][h4].x, v[2][h4].y, v[2][h4].z, v[2][h4].w};
+        const float d[4] = {v[3][h4].x, v[3][h4].y, v[3][h4].z, v[3][h4].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gcv = gc[4 * h4 + j];
+          s_h += msk * coord_dh(sp, a[j], b[j], c[j], d[j]) * gcv;
+          s_w += msk * coord_dw(sp, a[j], b[j], c[j], d[j]) * gcv;
+          s_m += gcv * bilerp(sp, a[j], b[j], c[j], d[j]);
+        }
+      }
+      float* gbase = gxt_n + gch;
+      const float wts[4] = {sp.w1 * msk, sp.w2 * msk, sp.w3 * msk, sp.w4 * msk};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (!((sp.live >> c) & 1u)) continue;
+        float* dst = gbase + (long long)ci[c] * g.C;
+        const float wc = wts[c];
+#pragma unroll
+        for (int h4 = 0; h4 < 4; ++h4)
+          red_add_v4(dst + 4 * h4, wc * gc[4 * h4], wc * gc[4 * h4 + 1], wc * gc[4 * h4 + 2],
+                     wc * gc[4 * h4 + 3]);
+      }
+    }
+    if (valid && cur_dgi >= 0 && sp.valid) {
+      const long long oi = off_h_index(g, n, cur_dgi, k, p);
+      red_add_f32(goff + oi, s_h);
+      red_add_f32(goff + oi + g.P, s_w);
+      if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+    }
+    tc::tc_fence_before();  // our tensor-memory reads precede the next tap's MMAs
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, (uint32_t)tcols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// bwd_weight_tc
+// ---------------------------------------------------------------------------
+constexpr int W_BM = 128;  // channels of one tap per CTA
+// MN-major A (channels contiguous).  For 32-bit operands the tensor core
+// takes MN-major tiles only in the "128-byte swizzle, 32-byte atom" layout:
+// an atom is 4 K rows (pixels) x 128 B (32 channels), and within it the
+// 32-byte chunk c of row r sits at chunk position c ^ r.  Atoms: K groups of
+// 4 pixels at W_SBO = 512 B, channel blocks of 32 at W_LBO = 4096 B
+// (16 KB per 128-channel x 32-pixel stage).
+constexpr int W_LBO = 4096, W_SBO = 512;
+
+size_t weight_smem_bytes(int bn) { return 2 * 16384 + 2 * (size_t)bn * 128 + 64 + 1024; }
+
+// Instruction descriptor with A MN-major (bit 15), B K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) {
+  return tc::idesc_tf32(M, N) | (1u << 15);
+}
+__device__ __forceinline__ uint64_t sdesc_sw128b32_mn(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(W_LBO >> 4) << 16) |
+         ((uint64_t)(W_SBO >> 4) << 32) | (1ull << 46) | (1ull << 61);
+}
+// Byte offset of channel quad `quad` (channels 4*quad .. 4*quad+3 of a
+// 32-channel block) of pixel `pix` (0..31 of the stage) in one channel block.
+__device__ __forceinline__ uint32_t mn32_offset(int pix, int quad) {
+  const int kr = pix & 3;
+  return (uint32_t)((pix >> 2) * W_SBO + kr * 128 + ((((quad >> 1) ^ kr) & 3) << 5) +
+                    ((quad & 1) << 4));
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+bwd_weight_tc_kernel(Geom g, const float* __restrict__ go_r, int bn, int tcols,
+                     const float* __restrict__ xt, const float* __restrict__ off,
+                     const float* __restrict__ mask, float* __restrict__ gw, int splits,
+                     int chunks_per_split) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_u32 = tc::smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  const uint32_t sA0 = tc::smem_u32(smem);
+  const uint32_t sB0 = sA0 + 2 * 16384;
+  const uint32_t b_stage = (uint32_t)bn * 128;
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 2 * 16384 + 2 * b_stage);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mtiles = g.Cg / W_BM;
+  const int k = blockIdx.x / mtiles;                  // tap
+  const int cm0 = (blockIdx.x - k * mtiles) * W_BM;   // channel tile within the group
+  const int o0 = blockIdx.y * bn;
+  const int gi = blockIdx.z / splits;
+  const int split = blockIdx.z - gi * splits;
+  const int pchunks = (g.P + 31) >> 5;
+  const int total_chunks = g.N * pchunks;
+  const int t_begin = split * chunks_per_split;
+  const int t_end = min(total_chunks, t_begin + chunks_per_split);
+  if (t_begin >= t_end) return;  // uniform for the CTA; nothing allocated yet
+
+  if (tid == 0) {
+    tc::mbar_init(&mma_bar[0], 1);
+    tc::mbar_init(&mma_bar[1], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, (uint32_t)tcols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
+
+  // gather role: channel block mb (32 channels), pixels ph*16 + i*4 + sub
+  const int mb = warp & 3, ph = warp >> 2;
+  const int quad = lane & 7, sub = lane >> 3;
+  const int gch = gi * g.Cg + cm0 + mb * 32 + quad * 4;
+  const int dgi = (gi * g.Cg + cm0 + mb * 32) / g.cpg;
+  const int ki = k / g.kw, kj = k - ki * g.kw;
+
+  for (int t = t_begin; t < t_end; ++t) {
+    const int s = t - t_begin;
+    const int st = s & 1;
+    const int n = t / pchunks;
+    const int p0 = (t - n * pchunks) << 5;
+    if (s >= 2) tc::mbar_wait(&mma_bar[st], ((s - 2) >> 1) & 1, &g_tc_bwd_status);
+    const uint32_t sA = sA0 + st * 16384, sB = sB0 + st * b_stage;
+
+    // B: bn out-channel rows x 32 pixels of image n (zero beyond P)
+    const int Ppad = (g.P + 3) & ~3;
+    const float* bsrc = go_r + ((long long)n * g.outC + (long long)gi * g.Og + o0) * Ppad + p0;
+    for (int i = tid; i < bn * 8; i += THREADS) {
+      const int row = i >> 3, j = i & 7;
+      const uint32_t dst = sB + tc::sw128_offset(row, j);
+      if (p0 + j * 4 < Ppad)
+        tc::cp_async16(dst, bsrc + (long long)row * Ppad + j * 4);
+      else
+        tc::st_shared_v4(dst, 0.f, 0.f, 0.f, 0.f);
+    }
+
+    // A: column values for 32 pixels x 128 channels, MN-major
+    const float* xt_n = xt + (long long)n * g.HW * g.C;
+    float4 v[4][4];
+    float cw[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pix = ph * 16 + i * 4 + sub;
+      const int pp = p0 + pix;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) cw[i][c] = 0.f;
+      int cidx[4] = {-1, -1, -1, -1};
+      if (pp < g.P) {
+        const int oy = pp / g.Wo, ox = pp - oy * g.Wo;
+        const long long oi = off_h_index(g, n, dgi, k, pp);
+        float h, w;
+        sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+        const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, pp)) : 1.f;
+        const Sample sp = make_sample(h, w, g.H, g.W);
+        if (sp.valid) {
+          if (sp.live & 1u) { cidx[0] = sp.i1; cw[i][0] = sp.w1 * m; }
+          if (sp.live & 2u) { cidx[1] = sp.i2; cw[i][1] = sp.w2 * m; }
+          if (sp.live & 4u) { cidx[2] = sp.i3; cw[i][2] = sp.w3 * m; }
+          if (sp.live & 8u) { cidx[3] = sp.i4; cw[i][3] = sp.w4 * m; }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        v[i][c] = cidx[c] >= 0 ? ldg4(xt_n + (long long)cidx[c] * g.C + gch)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pix = ph * 16 + i * 4 + sub;
+      const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
+      const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
+      const uint32_t addr = sA + mb * W_LBO + mn32_offset(pix, quad);
+      tc::st_shared_v4(addr, tc::to_tf32(a * A.x + b * B.x + c * C.x + d * D.x),
+                       tc::to_tf32(a * A.y + b * B.y + c * C.y + d * D.y),
+                       tc::to_tf32(a * A.z + b * B.z + c * C.z + d * D.z),
+                       tc::to_tf32(a * A.w + b * B.w + c * C.w + d * D.w));
+    }
+    tc::cp_async_wait_all();
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        tc::umma_tf32(tmem, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32), idesc,
+                      (s | j) != 0 ? 1u : 0u);
+      tc::umma_commit(&mma_bar[st]);
+    }
+  }
+  const int last = t_end - t_begin - 1;
+  tc::mbar_wait(&mma_bar[last & 1], (last >> 1) & 1, &g_tc_bwd_status);
+  tc::tc_fence_after();
+  {
+    // lanes = channels, columns = out channels
+    const int lq = warp & 3, half = warp >> 2;
+    const int c = cm0 + lq * 32 + lane;
+    const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
+    float* dst = gw + ((long long)(gi * g.Og + o0) * g.Cg + c) * g.kk + k;
+    const long long ostride = (long long)g.Cg * g.kk;
+    for (int cb = cbeg; cb < cend; cb += 8) {
+      float vv[8];
+      tc::tmem_ld8(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb, vv);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, (uint32_t)tcols);
+  }
+}
+
+// wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels)
+__global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __restrict__ wb,
+                                          Geom g) {
+  const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(i % g.Og);
+    long long t = i / g.Og;
+    const int c = (int)(t % g.Cg);
+    t /= g.Cg;
+    const int k = (int)(t % g.kk);
+    const int gi = (int)(t / g.kk);
+    wb[i] = tc::to_tf32(w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k]);
+  }
+}
+
+int data_bn(const Geom& g) { return g.Cg <= 256 ? g.Cg : 256; }
+int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
+
+}  // namespace
+
+bool tc_bwd_supported(const Geom& g) {
+  return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
+         (g.Og <= 256 || g.Og % 256 == 0) && (g.Cg <= 256 || g.Cg % 256 == 0) &&
+         g.Cg % W_BM == 0 && g.NP > 0 && (long long)g.N * g.HW < (1LL << 31);
+}
+
+size_t tc_bwd_scratch_bytes(const Geom& g) {
+  // go_t + go_r (rows padded to a multiple of 4 pixels) + packed weight
+  return (size_t)g.N * g.outC * (g.P + ((g.P + 3) & ~3)) * sizeof(float) +
+         (size_t)g.outC * g.Cg * g.kk * sizeof(float);
+}
+
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
+                              cudaStream_t stream) {
+  if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
+  const int Ppad = (g.P + 3) & ~3;
+  dim3 grid((Ppad + 31) / 32, (g.outC + 31) / 32, g.N);
+  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_r, g.outC, g.P, Ppad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
+                                      cudaStream_t stream) {
+  const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  tc_pack_weight_bwd_kernel<<<(int)blocks, 256, 0, stream>>>(w, wbt, g);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
+                               const float* xt, const float* off, const float* mask,
+                               float* gxt, float* goff, float* gmask, cudaStream_t stream) {
+  const int bn = data_bn(g);
+  const size_t smem = data_smem_bytes(bn);
+  cudaError_t e = cudaFuncSetAttribute(bwd_data_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((g.NP + D_BM - 1) / D_BM), g.Cg / bn, g.G);
+  bwd_data_tc_kernel<<<grid, THREADS, smem, stream>>>(g, go_t, wbt, bn, pow2_cols(bn), xt, off,
+                                                       mask, gxt, goff, gmask);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
+                                 const float* off, const float* mask, float* gw, int num_sms,
+                                 cudaStream_t stream) {
+  const int bn = weight_bn(g);
+  const size_t smem = weight_smem_bytes(bn);
+  cudaError_t e = cudaFuncSetAttribute(bwd_weight_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int base = g.kk * (g.Cg / W_BM) * (g.Og / bn) * g.G;
+  const int pchunks = (g.P + 31) / 32;
+  const int total_chunks = g.N * pchunks;
+  int splits = (2 * num_sms + base - 1) / base;
+  const int max_splits = (total_chunks + 7) / 8;  // >= 8 K steps per CTA
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  if ((long long)splits * g.G > 65535) splits = 65535 / g.G;
+  const int per = (total_chunks + splits - 1) / splits;
+  dim3 grid(g.kk * (g.Cg / W_BM), g.Og / bn, g.G * splits);
+  bwd_weight_tc_kernel<<<grid, THREADS, smem, stream>>>(g, go_r, bn, pow2_cols(bn), xt, off, mask,
+                                                         gw, splits, per);
+  return cudaGetLastError();
+}
+
+}  // namespace dcn

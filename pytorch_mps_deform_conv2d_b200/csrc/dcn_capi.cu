@@ -198,10 +198,21 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
   return b + kAlign;  // slack for aligning the caller's base pointer
 }
 
-size_t bwd_ws(const dcn::Geom& g, uint32_t /*flags*/) {
+bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
+  return (flags & 0xff) == DCN_MATH_TF32 && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
+         dcn::tc_bwd_supported(g);
+}
+
+size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
   size_t b = align_up((size_t)g.N * g.HW * g.C * sizeof(float));      // xt
   b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
-  b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));     // packed weight
+  if (use_tc_bwd(g, flags)) {
+    b += align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
+    b += align_up((size_t)g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));  // go_r
+    b += align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));       // packed weight
+  } else {
+    b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
+  }
   return b + kAlign;
 }
 
@@ -350,9 +361,24 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   Carver ws(align_ptr(workspace));
   float* xt = ws.take((size_t)g.N * g.HW * g.C);
   float* gxt = ws.take((size_t)g.N * g.HW * g.C);
-  float* wb = ws.take((size_t)g.G * g.kk * g.Og * g.Cg);
   DCN_CUDA(cudaMemsetAsync(gxt, 0, x_bytes, stream), "memset");
   DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
+  if (use_tc_bwd(g, flags)) {
+    float* go_t = ws.take((size_t)g.N * g.outC * g.P);
+    float* go_r = ws.take((size_t)g.N * g.outC * ((g.P + 3) & ~3));
+    float* wbt = ws.take((size_t)g.outC * g.Cg * g.kk);
+    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_r, stream), "tc_prep_go");
+    DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, stream), "tc_pack_weight_bwd");
+    DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, wbt, xt, offset, mask, gxt, grad_offset, grad_mask,
+                                     stream),
+             "bwd_data_tc");
+    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, offset, mask, grad_weight, num_sms_current(),
+                                       stream),
+             "bwd_weight_tc");
+    return DCN_OK;
+  }
+  float* wb = ws.take((size_t)g.G * g.kk * g.Og * g.Cg);
   DCN_CUDA(dcn::launch_pack_weight_bwd(weight, wb, g, stream), "pack_weight_bwd");
   DCN_CUDA(dcn::launch_bwd_data_simt(g, grad_output, wb, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, stream),

@@ -21,4 +21,25 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
                           const float* off, const float* mask, const float* bias,
                           float* out, int num_sms, cudaStream_t stream);
 
+// Whether the tensor-core backward covers this geometry.
+bool tc_bwd_supported(const Geom& g);
+// Scratch of the tensor-core backward beyond the NHWC input / grad-input
+// copies: go_t and go_r (tf32-rounded grad_out, pixel-major and NCHW) and the
+// packed weight.
+size_t tc_bwd_scratch_bytes(const Geom& g);
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
+                              cudaStream_t stream);
+cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
+                                      cudaStream_t stream);
+// grad_col = W^T go on the tensor core per (pixel tile, tap), fused with the
+// col2im scatter into gxt (NHWC, pre-zeroed) and the coordinate / mask
+// reductions into goff / gmask (pre-zeroed).
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
+                               const float* xt, const float* off, const float* mask,
+                               float* gxt, float* goff, float* gmask, cudaStream_t stream);
+// grad_weight (pre-zeroed) += col^T go on the tensor core, split over pixels.
+cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
+                                 const float* off, const float* mask, float* gw, int num_sms,
+                                 cudaStream_t stream);
+
 }  // namespace dcn

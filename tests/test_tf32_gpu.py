@@ -66,3 +66,56 @@ def test_tf32_repeatable(cuda_device):
     a, _ = run_ours(case, flags=MATH_TF32, backward=False)
     b, _ = run_ours(case, flags=MATH_TF32, backward=False)
     assert np.array_equal(a, b)  # the forward has no atomics: bitwise repeatable
+
+
+GRAD_TOL = 1e-3  # norm-wise relative error of every gradient in TF32 mode
+
+TC_BWD_CASES = {
+    "c128-o64": dict(inC=128, outC=64, H=12, W=10, offset_scale=2.0),
+    "c128-o32-dg4-v1": dict(inC=128, outC=32, H=8, W=12, dg=4, use_mask=False,
+                            use_bias=False, offset_scale=3.0),
+    "c256-o64-g2": dict(inC=256, outC=64, groups=2, H=10, W=8),
+    "c256-o256-neck-like": dict(N=2, inC=256, outC=256, H=16, W=20, offset_scale=4.0,
+                                mask_kind="sigmoid", weight_kind="kaiming"),
+    "c512-o512-dcnv1-like": dict(N=2, inC=512, outC=512, H=10, W=8, stride=(2, 1),
+                                 pad=(2, 1), dil=(2, 1), dg=8, use_mask=False,
+                                 use_bias=False, offset_scale=3.0, weight_kind="kaiming"),
+    "c128-o128-asym-boundary-p70": dict(inC=128, outC=128, H=9, W=14, kh=3, kw=1,
+                                    stride=(2, 1), pad=(1, 0), offset_scale=8.0),
+}
+
+
+def _grad_errors(case):
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out, grads = run_ours(case, flags=MATH_TF32)
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    ref, rgrads = run_oracle(case)
+    errs = {k: rel_norm_err(grads[k], v) for k, v in rgrads.items()}
+    elem = {k: float(np.abs(grads[k] - v).max() / max(1e-30, np.abs(v).max()))
+            for k, v in rgrads.items()}
+    return stats, rel_norm_err(out, ref), errs, elem
+
+
+@pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
+def test_backward_tf32(cuda_device, name):
+    stats, out_err, errs, elem = _grad_errors(make_case(upstream="randn", **TC_BWD_CASES[name]))
+    assert "bwd_data_tc" in stats and "bwd_weight_tc" in stats, sorted(stats)
+    assert out_err <= OUT_TOL
+    for k, e in errs.items():
+        assert e <= GRAD_TOL, f"grad_{k}: norm-wise rel err {e:.2e} (all: {errs}, elem: {elem})"
+        assert elem[k] <= 10 * GRAD_TOL, f"grad_{k}: max elem err {elem[k]:.2e} of max|ref|"
+
+
+def test_backward_tf32_uncovered_shape_uses_fp32_kernels(cuda_device):
+    # 64 input channels per group: below the 128-channel tile of the
+    # tensor-core weight gradient, so the fp32 backward kernels run and meet
+    # the fp32 tolerances.
+    case = make_case(inC=64, outC=64, H=9, W=9, upstream="randn")
+    stats, out_err, errs, elem = _grad_errors(case)
+    assert "bwd_data_tc" not in stats and "bwd_data_simt" in stats
+    for k, e in errs.items():
+        assert e <= 1e-4, f"grad_{k}: {e:.2e}"
