@@ -71,6 +71,158 @@ constexpr int D_BM = 128;
 
 size_t data_smem_bytes(int bn) { return 2 * 16384 + 2 * (size_t)bn * 128 + 64 + 1024; }
 
+// Sampling plan of one pixel for one (tap, deformable group), kept in shared
+// memory so that the 8 lanes working on the pixel can read it.
+struct PixPlan {
+  int cidx[4];     // n*H*W + y*W + x of each live corner, -1 when dropped
+  float w[4];      // bilinear weights (0 for dropped corners)
+  float lh, lw;    // fractional position
+  float msk;       // modulation scalar
+  int oi;          // offset-gradient index of (n, dgi, k, p); -1: pixel or sample void
+  int mi;          // mask-gradient index
+  int pad_;
+};
+static_assert(sizeof(PixPlan) == 56, "PixPlan is 14 words");
+
+constexpr int EPI_TSTRIDE = 33;  // transpose buffer row stride (floats)
+constexpr int EPI_WARP_BYTES = 32 * EPI_TSTRIDE * 4 + 32 * (int)sizeof(PixPlan);  // 6016
+
+__device__ __forceinline__ void epilogue_tap(const Geom& g, int k, uint32_t tmem, int c0, int gi,
+                                             long long q0, int warp, int lane,
+                                             unsigned char* smem, const float* __restrict__ xt,
+                                             const float* __restrict__ off,
+                                             const float* __restrict__ mask,
+                                             float* __restrict__ gxt, float* __restrict__ goff,
+                                             float* __restrict__ gmask, int bn) {
+  const int lq = warp & 3, half = warp >> 2;
+  float* T = reinterpret_cast<float*>(smem + warp * EPI_WARP_BYTES);
+  PixPlan* plan = reinterpret_cast<PixPlan*>(smem + warp * EPI_WARP_BYTES + 32 * EPI_TSTRIDE * 4);
+  const int ki = k / g.kw, kj = k - ki * g.kw;
+  // this lane's own pixel (row of the accumulator)
+  const long long myq = q0 + lq * 32 + lane;
+  const bool myvalid = myq < g.NP;
+  const int myn = myvalid ? (int)(myq / g.P) : 0;
+  const int myp = myvalid ? (int)(myq - (long long)myn * g.P) : 0;
+  const int myoy = myp / g.Wo, myox = myp - myoy * g.Wo;
+  // cooperative role: channel quad, pixel sub-index
+  const int quad = lane & 7, sub = lane >> 3;
+  int plan_dgi = -1;
+  const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
+  for (int cb = cbeg; cb < cend; cb += 32) {
+    float vals[32];
+    {
+      const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float t[8];
+        tc::tmem_ld8(ta + 8 * j, t);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vals[8 * j + e] = t[e];
+      }
+      tc::tmem_ld_wait();
+    }
+    const int gch0 = gi * g.Cg + c0 + cb;  // 32 channels, one deformable group
+    const int dgi = gch0 / g.cpg;
+    __syncwarp();
+    if (dgi != plan_dgi) {
+      plan_dgi = dgi;
+      PixPlan pl;
+      pl.oi = -1;
+      pl.mi = 0;
+      pl.pad_ = 0;
+      pl.lh = pl.lw = 0.f;
+      pl.msk = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        pl.cidx[c] = -1;
+        pl.w[c] = 0.f;
+      }
+      if (myvalid) {
+        const long long oi = off_h_index(g, myn, dgi, k, myp);
+        float h, w;
+        sample_pos(g, myoy, myox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+        const Sample sp = make_sample(h, w, g.H, g.W);
+        if (sp.valid) {
+          const int nb = myn * g.HW;
+          const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
+          const float wv[4] = {sp.w1, sp.w2, sp.w3, sp.w4};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            pl.cidx[c] = ((sp.live >> c) & 1u) ? nb + ci[c] : -1;
+            pl.w[c] = wv[c];
+          }
+          pl.lh = sp.lh;
+          pl.lw = sp.lw;
+          pl.msk = g.use_mask ? __ldg(mask + mask_index(g, myn, dgi, k, myp)) : 1.f;
+          pl.oi = (int)oi;
+          pl.mi = (int)mask_index(g, myn, dgi, k, myp);
+        }
+      }
+      plan[lane] = pl;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) T[lane * EPI_TSTRIDE + j] = vals[j];
+    __syncwarp();
+    // 8 lanes per pixel, 4 pixels per round, 8 rounds
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int px = i * 4 + sub;
+      const PixPlan& pl = plan[px];
+      float s_h = 0.f, s_w = 0.f, s_m = 0.f;
+      if (pl.oi >= 0) {
+        const float gc0 = T[px * EPI_TSTRIDE + quad * 4 + 0];
+        const float gc1 = T[px * EPI_TSTRIDE + quad * 4 + 1];
+        const float gc2 = T[px * EPI_TSTRIDE + quad * 4 + 2];
+        const float gc3 = T[px * EPI_TSTRIDE + quad * 4 + 3];
+        const float* xq = xt + gch0 + quad * 4;
+        float4 v[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          v[c] = pl.cidx[c] >= 0 ? ldg4(xq + (size_t)pl.cidx[c] * g.C)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        Sample sp;
+        sp.w1 = pl.w[0]; sp.w2 = pl.w[1]; sp.w3 = pl.w[2]; sp.w4 = pl.w[3];
+        sp.lh = pl.lh; sp.lw = pl.lw;
+        const float m = pl.msk;
+        const float gcs[4] = {gc0, gc1, gc2, gc3};
+        const float a[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
+        const float b[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
+        const float c[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
+        const float d[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
+          s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
+          s_m += gcs[e] * bilerp(sp, a[e], b[e], c[e], d[e]);
+        }
+        float* gq = gxt + gch0 + quad * 4;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          if (pl.cidx[cc] < 0) continue;
+          const float wc = pl.w[cc] * m;
+          red_add_v4(gq + (size_t)pl.cidx[cc] * g.C, wc * gc0, wc * gc1, wc * gc2, wc * gc3);
+        }
+      }
+      // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
+      s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);
+      s_w += __shfl_xor_sync(0xffffffffu, s_w, 1);
+      s_m += __shfl_xor_sync(0xffffffffu, s_m, 1);
+      s_h += __shfl_xor_sync(0xffffffffu, s_h, 2);
+      s_w += __shfl_xor_sync(0xffffffffu, s_w, 2);
+      s_m += __shfl_xor_sync(0xffffffffu, s_m, 2);
+      s_h += __shfl_xor_sync(0xffffffffu, s_h, 4);
+      s_w += __shfl_xor_sync(0xffffffffu, s_w, 4);
+      s_m += __shfl_xor_sync(0xffffffffu, s_m, 4);
+      if (quad == 0 && pl.oi >= 0) {
+        red_add_f32(goff + pl.oi, s_h);
+        red_add_f32(goff + pl.oi + g.P, s_w);
+        if (g.use_mask) red_add_f32(gmask + pl.mi, s_m);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 __global__ void __launch_bounds__(THREADS, 2)
 bwd_data_tc_kernel(Geom g, const float* __restrict__ go_t, const float* __restrict__ wb,
                    int bn, int tcols, const float* __restrict__ xt,
@@ -106,17 +258,6 @@ bwd_data_tc_kernel(Geom g, const float* __restrict__ go_t, const float* __restri
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t idesc = tc::idesc_tf32(D_BM, bn);
-
-  // epilogue identity: pixel row r, channel half
-  const int lq = warp & 3, half = warp >> 2;
-  const int r = lq * 32 + lane;
-  const long long q = q0 + r;
-  const bool valid = q < g.NP;
-  const int n = valid ? (int)(q / g.P) : 0;
-  const int p = valid ? (int)(q - (long long)n * g.P) : 0;
-  const int oy = p / g.Wo, ox = p - oy * g.Wo;
-  const float* xt_n = xt + (long long)n * g.HW * g.C;
-  float* gxt_n = gxt + (long long)n * g.HW * g.C;
 
   int s_global = 0;  // K steps issued so far (stage / parity bookkeeping)
   for (int k = 0; k < g.kk; ++k) {
@@ -158,87 +299,12 @@ bwd_data_tc_kernel(Geom g, const float* __restrict__ go_t, const float* __restri
     tc::tc_fence_after();
 
     // ---- epilogue: col2im scatter + coordinate / mask sums ----
-    const int ki = k / g.kw, kj = k - ki * g.kw;
-    const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
-    int cur_dgi = -1;
-    Sample sp = make_sample(-2.f, -2.f, 1, 1);
-    float msk = 0.f, s_h = 0.f, s_w = 0.f, s_m = 0.f;
-    for (int cb = cbeg; cb < cend; cb += 16) {
-      float gc[16];
-      {
-        float t0[8], t1[8];
-        const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb;
-        tc::tmem_ld8(ta, t0);
-        tc::tmem_ld8(ta + 8, t1);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          gc[j] = t0[j];
-          gc[8 + j] = t1[j];
-        }
-      }
-      if (!valid) continue;
-      const int gch = gi * g.Cg + c0 + cb;  // 16 channels gch .. gch+15, one dg group
-      const int dgi = gch / g.cpg;
-      if (dgi != cur_dgi) {
-        if (cur_dgi >= 0 && sp.valid) {
-          const long long oi = off_h_index(g, n, cur_dgi, k, p);
-          red_add_f32(goff + oi, s_h);
-          red_add_f32(goff + oi + g.P, s_w);
-          if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
-        }
-        s_h = s_w = s_m = 0.f;
-        cur_dgi = dgi;
-        const long long oi = off_h_index(g, n, dgi, k, p);
-        float h, w;
-        sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-        msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
-        sp = make_sample(h, w, g.H, g.W);
-      }
-      if (!sp.valid) continue;
-      // corner values of the 16 channels
-      float4 v[4][4];
-      const float* base = xt_n + gch;
-      const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int h4 = 0; h4 < 4; ++h4)
-          v[c][h4] = (sp.live >> c) & 1u ? ldg4(base + (long long)ci[c] * g.C + 4 * h4)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int h4 = 0; h4 < 4; ++h4) {
-        const float a[4] = {v[0][h4].x, v[0][h4].y, v[0][h4].z, v[0][h4].w};
-        const float b[4] = {v[1][h4].x, v[1][h4].y, v[1][h4].z, v[1][h4].w};
-        const float c[4] = {v[2][h4].x, v[2][h4].y, v[2][h4].z, v[2][h4].w};
-        const float d[4] = {v[3][h4].x, v[3][h4].y, v[3][h4].z, v[3][h4].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float gcv = gc[4 * h4 + j];
-          s_h += msk * coord_dh(sp, a[j], b[j], c[j], d[j]) * gcv;
-          s_w += msk * coord_dw(sp, a[j], b[j], c[j], d[j]) * gcv;
-          s_m += gcv * bilerp(sp, a[j], b[j], c[j], d[j]);
-        }
-      }
-      float* gbase = gxt_n + gch;
-      const float wts[4] = {sp.w1 * msk, sp.w2 * msk, sp.w3 * msk, sp.w4 * msk};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (!((sp.live >> c) & 1u)) continue;
-        float* dst = gbase + (long long)ci[c] * g.C;
-        const float wc = wts[c];
-#pragma unroll
-        for (int h4 = 0; h4 < 4; ++h4)
-          red_add_v4(dst + 4 * h4, wc * gc[4 * h4], wc * gc[4 * h4 + 1], wc * gc[4 * h4 + 2],
-                     wc * gc[4 * h4 + 3]);
-      }
-    }
-    if (valid && cur_dgi >= 0 && sp.valid) {
-      const long long oi = off_h_index(g, n, cur_dgi, k, p);
-      red_add_f32(goff + oi, s_h);
-      red_add_f32(goff + oi + g.P, s_w);
-      if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
-    }
+    // Tensor memory hands each thread its own pixel's row.  Each warp moves
+    // 32 pixels x 32 channels at a time through shared memory (the stage
+    // buffers are free now) so that 8 lanes cover one pixel's 32 channels:
+    // corner loads and vector reductions are then full 128-byte lines.
+    epilogue_tap(g, k, tmem, c0, gi, q0, warp, lane, smem, xt, off, mask, gxt, goff, gmask, bn);
+    __syncthreads();  // the next tap's stage writes reuse the epilogue's shared memory
     tc::tc_fence_before();  // our tensor-memory reads precede the next tap's MMAs
   }
   tc::tc_fence_before();
@@ -443,15 +509,16 @@ __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __
   }
 }
 
-int data_bn(const Geom& g) { return g.Cg <= 256 ? g.Cg : 256; }
+int data_bn(const Geom& g) { return g.Cg <= 128 ? g.Cg : 128; }
 int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
 
 }  // namespace
 
 bool tc_bwd_supported(const Geom& g) {
   return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
-         (g.Og <= 256 || g.Og % 256 == 0) && (g.Cg <= 256 || g.Cg % 256 == 0) &&
-         g.Cg % W_BM == 0 && g.NP > 0 && (long long)g.N * g.HW < (1LL << 31);
+         (g.Og <= 256 || g.Og % 256 == 0) && g.Cg % W_BM == 0 && g.NP > 0 &&
+         (long long)g.N * g.HW < (1LL << 31) &&
+         (long long)g.N * 2 * g.dg * g.kk * g.P < (1LL << 31);
 }
 
 size_t tc_bwd_scratch_bytes(const Geom& g) {

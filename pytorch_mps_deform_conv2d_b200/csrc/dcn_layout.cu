@@ -75,14 +75,21 @@ __global__ void pack_weight_bwd_kernel(const float* __restrict__ w,
   }
 }
 
-// One block per output channel; deterministic tree reduction.
+// grad_bias: block (o, split) sums a contiguous range of the (n, p) pixels
+// of channel o and adds it into the zeroed grad_bias.
+constexpr int GB_CHUNK = 8192;
+
 __global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict__ go,
                                                         float* __restrict__ gb, Geom g) {
   const int o = blockIdx.x;
+  const long long total = (long long)g.N * g.P;
+  const long long beg = (long long)blockIdx.y * GB_CHUNK;
+  const long long end = beg + GB_CHUNK < total ? beg + GB_CHUNK : total;
   float s = 0.f;
-  for (int n = 0; n < g.N; ++n) {
-    const float* row = go + ((long long)n * g.outC + o) * g.P;
-    for (int p = threadIdx.x; p < g.P; p += blockDim.x) s += row[p];
+  for (long long i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const int n = (int)(i / g.P);
+    const int p = (int)(i - (long long)n * g.P);
+    s += go[((long long)n * g.outC + o) * g.P + p];
   }
   __shared__ float red[32];
 #pragma unroll
@@ -93,7 +100,7 @@ __global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict_
     s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
-    if (threadIdx.x == 0) gb[o] = s;
+    if (threadIdx.x == 0) atomicAdd(gb + o, s);
   }
 }
 
@@ -153,7 +160,13 @@ cudaError_t launch_fill_bias(float* out, const float* bias, const Geom& g,
 cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
                              cudaStream_t stream) {
   if (g.outC == 0) return cudaSuccess;
-  grad_bias_kernel<<<g.outC, 256, 0, stream>>>(go, gb, g);
+  cudaError_t e = cudaMemsetAsync(gb, 0, (size_t)g.outC * sizeof(float), stream);
+  if (e != cudaSuccess) return e;
+  const long long total = (long long)g.N * g.P;
+  if (total == 0) return cudaSuccess;
+  const long long splits = (total + GB_CHUNK - 1) / GB_CHUNK;
+  if (splits > 65535) return cudaErrorInvalidValue;
+  grad_bias_kernel<<<dim3(g.outC, (unsigned)splits), 256, 0, stream>>>(go, gb, g);
   return cudaGetLastError();
 }
 
