@@ -20,6 +20,7 @@
 //                cp.async.  Partial tiles are reduced into grad_weight.
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
+#include "dcn_tma.h"
 
 namespace dcn {
 
@@ -327,7 +328,6 @@ constexpr int W_BM = 128;  // channels of one tap per CTA
 // (16 KB per 128-channel x 32-pixel stage).
 constexpr int W_LBO = 4096, W_SBO = 512;
 
-size_t weight_smem_bytes(int bn) { return 2 * 16384 + 2 * (size_t)bn * 128 + 64 + 1024; }
 
 // Instruction descriptor with A MN-major (bit 15), B K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) {
@@ -345,39 +345,79 @@ __device__ __forceinline__ uint32_t mn32_offset(int pix, int quad) {
                     ((quad & 1) << 4));
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
-bwd_weight_tc_kernel(Geom g, const float* __restrict__ go_r, int bn, int tcols,
+// Persistent, warp-specialised weight-gradient kernel.  A tile is (tap k,
+// 128 input channels, bn out channels, group, pixel range); its K loop runs
+// over 32-pixel chunks of the range.
+//   warps 0-3   epilogue: accumulator -> fp32 reductions into grad_weight
+//   warp  4     MMA issue: 4 UMMAs 128(channels) x bn x 8(pixels) per K step
+//   warp  5     TMA producer of go_r rows (bn out channels x 32 pixels)
+//   warps 6-21  16 gather warps: 32 channels x 8 pixels each; the column
+//               values are written MN-major (channels contiguous).
+// Stage ring and accumulator double buffering as in the forward kernel.
+constexpr int W2_STAGES = 4;
+constexpr int W2_GATHER_WARPS = 16;
+constexpr int W2_MMA_WARP = 4, W2_TMA_WARP = 5, W2_GATHER_WARP0 = 6;
+constexpr int W2_THREADS = (W2_GATHER_WARP0 + W2_GATHER_WARPS) * 32;  // 704
+constexpr int W2_A_STAGE = 16384;
+
+size_t weight_smem_bytes(int bn) {
+  return (size_t)W2_STAGES * W2_A_STAGE + (size_t)W2_STAGES * bn * 128 + 128 + 1024;
+}
+
+struct WTile {
+  int k, cm0, o0, gi, t_begin, t_end;
+};
+__device__ __forceinline__ WTile wtile_of(const Geom& g, int t, int mtiles, int ntn, int splits,
+                                          int per, int total_chunks, int bn) {
+  WTile T;
+  const int sp = t % splits;
+  int r = t / splits;
+  const int nt = r % ntn;
+  r /= ntn;
+  const int mt = r % mtiles;
+  r /= mtiles;
+  T.k = r % g.kk;
+  T.gi = r / g.kk;
+  T.cm0 = mt * W_BM;
+  T.o0 = nt * bn;
+  T.t_begin = sp * per;
+  T.t_end = min(total_chunks, T.t_begin + per);
+  return T;
+}
+
+__global__ void __launch_bounds__(W2_THREADS, 1)
+bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
                      const float* __restrict__ xt, const float* __restrict__ off,
-                     const float* __restrict__ mask, float* __restrict__ gw, int splits,
-                     int chunks_per_split) {
+                     const float* __restrict__ mask, float* __restrict__ gw, int mtiles, int ntn,
+                     int splits, int per, int ntiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
   const uint32_t sA0 = tc::smem_u32(smem);
-  const uint32_t sB0 = sA0 + 2 * 16384;
   const uint32_t b_stage = (uint32_t)bn * 128;
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 2 * 16384 + 2 * b_stage);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 2);
+  const uint32_t sB0 = sA0 + W2_STAGES * W2_A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + W2_STAGES * W2_A_STAGE + W2_STAGES * b_stage);
+  uint64_t* empty = full + W2_STAGES;
+  uint64_t* acc_full = empty + W2_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int mtiles = g.Cg / W_BM;
-  const int k = blockIdx.x / mtiles;                  // tap
-  const int cm0 = (blockIdx.x - k * mtiles) * W_BM;   // channel tile within the group
-  const int o0 = blockIdx.y * bn;
-  const int gi = blockIdx.z / splits;
-  const int split = blockIdx.z - gi * splits;
   const int pchunks = (g.P + 31) >> 5;
   const int total_chunks = g.N * pchunks;
-  const int t_begin = split * chunks_per_split;
-  const int t_end = min(total_chunks, t_begin + chunks_per_split);
-  if (t_begin >= t_end) return;  // uniform for the CTA; nothing allocated yet
 
   if (tid == 0) {
-    tc::mbar_init(&mma_bar[0], 1);
-    tc::mbar_init(&mma_bar[1], 1);
+    for (int s = 0; s < W2_STAGES; ++s) {
+      tc::mbar_init(&full[s], W2_GATHER_WARPS + 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&acc_full[a], 1);
+      tc::mbar_init(&acc_empty[a], 4);
+    }
     tc::fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == W2_MMA_WARP) {
     tc::tmem_alloc(tmem_slot, (uint32_t)tcols);
     tc::tmem_relinquish();
   }
@@ -385,109 +425,158 @@ bwd_weight_tc_kernel(Geom g, const float* __restrict__ go_r, int bn, int tcols,
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
 
-  // gather role: channel block mb (32 channels), pixels ph*16 + i*4 + sub
-  const int mb = warp & 3, ph = warp >> 2;
-  const int quad = lane & 7, sub = lane >> 3;
-  const int gch = gi * g.Cg + cm0 + mb * 32 + quad * 4;
-  const int dgi = (gi * g.Cg + cm0 + mb * 32) / g.cpg;
-  const int ki = k / g.kw, kj = k - ki * g.kw;
-
-  for (int t = t_begin; t < t_end; ++t) {
-    const int s = t - t_begin;
-    const int st = s & 1;
-    const int n = t / pchunks;
-    const int p0 = (t - n * pchunks) << 5;
-    if (s >= 2) tc::mbar_wait(&mma_bar[st], ((s - 2) >> 1) & 1, &g_tc_bwd_status);
-    const uint32_t sA = sA0 + st * 16384, sB = sB0 + st * b_stage;
-
-    // B: bn out-channel rows x 32 pixels of image n (zero beyond P)
-    const int Ppad = (g.P + 3) & ~3;
-    const float* bsrc = go_r + ((long long)n * g.outC + (long long)gi * g.Og + o0) * Ppad + p0;
-    for (int i = tid; i < bn * 8; i += THREADS) {
-      const int row = i >> 3, j = i & 7;
-      const uint32_t dst = sB + tc::sw128_offset(row, j);
-      if (p0 + j * 4 < Ppad)
-        tc::cp_async16(dst, bsrc + (long long)row * Ppad + j * 4);
-      else
-        tc::st_shared_v4(dst, 0.f, 0.f, 0.f, 0.f);
-    }
-
-    // A: column values for 32 pixels x 128 channels, MN-major
-    const float* xt_n = xt + (long long)n * g.HW * g.C;
-    float4 v[4][4];
-    float cw[4][4];
+  if (warp >= W2_GATHER_WARP0) {
+    // ------------------------------ gather ------------------------------
+    const int gwp = warp - W2_GATHER_WARP0;
+    const int mb = gwp & 3, pg = gwp >> 2;
+    const int quad = lane & 7, sub = lane >> 3;
+    const int zoff = g.N * g.HW * g.C;
+    int gs = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+      if (T.t_begin >= T.t_end) continue;
+      const int gch = T.gi * g.Cg + T.cm0 + mb * 32 + quad * 4;
+      const int dgi = (T.gi * g.Cg + T.cm0 + mb * 32) / g.cpg;
+      const int ki = T.k / g.kw, kj = T.k - ki * g.kw;
+      const float* xq = xt + gch;
+      uint32_t soff[2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int pix = ph * 16 + i * 4 + sub;
-      const int pp = p0 + pix;
+      for (int i = 0; i < 2; ++i) soff[i] = mb * W_LBO + mn32_offset(pg * 8 + i * 4 + sub, quad);
+      int n = T.t_begin / pchunks;
+      int p0 = (T.t_begin - n * pchunks) << 5;
+      for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
+        const int st = gs & (W2_STAGES - 1);
+        const int u = gs / W2_STAGES;
+        int coff[2][4];
+        float cw[2][4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) cw[i][c] = 0.f;
-      int cidx[4] = {-1, -1, -1, -1};
-      if (pp < g.P) {
-        const int oy = pp / g.Wo, ox = pp - oy * g.Wo;
-        const long long oi = off_h_index(g, n, dgi, k, pp);
-        float h, w;
-        sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-        const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, pp)) : 1.f;
-        const Sample sp = make_sample(h, w, g.H, g.W);
-        if (sp.valid) {
-          if (sp.live & 1u) { cidx[0] = sp.i1; cw[i][0] = sp.w1 * m; }
-          if (sp.live & 2u) { cidx[1] = sp.i2; cw[i][1] = sp.w2 * m; }
-          if (sp.live & 4u) { cidx[2] = sp.i3; cw[i][2] = sp.w3 * m; }
-          if (sp.live & 8u) { cidx[3] = sp.i4; cw[i][3] = sp.w4 * m; }
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            coff[i][c] = zoff;
+            cw[i][c] = 0.f;
+          }
+          const int pp = p0 + pg * 8 + i * 4 + sub;
+          if (pp >= g.P) continue;
+          const int oy = pp / g.Wo, ox = pp - oy * g.Wo;
+          const long long oi = off_h_index(g, n, dgi, T.k, pp);
+          float h, w;
+          sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+          const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, T.k, pp)) : 1.f;
+          const Sample sp = make_sample(h, w, g.H, g.W);
+          if (!sp.valid) continue;
+          const int xn = n * g.HW;
+          if (sp.live & 1u) { coff[i][0] = (xn + sp.i1) * g.C; cw[i][0] = sp.w1 * m; }
+          if (sp.live & 2u) { coff[i][1] = (xn + sp.i2) * g.C; cw[i][1] = sp.w2 * m; }
+          if (sp.live & 4u) { coff[i][2] = (xn + sp.i3) * g.C; cw[i][2] = sp.w3 * m; }
+          if (sp.live & 8u) { coff[i][3] = (xn + sp.i4) * g.C; cw[i][3] = sp.w4 * m; }
+        }
+        float4 v[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            v[i][c] = ldg4(xq + (unsigned)coff[i][c]);  // dropped corners: zero row
+        if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+        const uint32_t sA = sA0 + st * W2_A_STAGE;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
+          const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
+          tc::st_shared_v4(sA + soff[i], tc::to_tf32(a * A.x + b * B.x + c * C.x + d * D.x),
+                           tc::to_tf32(a * A.y + b * B.y + c * C.y + d * D.y),
+                           tc::to_tf32(a * A.z + b * B.z + c * C.z + d * D.z),
+                           tc::to_tf32(a * A.w + b * B.w + c * C.w + d * D.w));
+        }
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&full[st]);
+        p0 += 32;
+        if (p0 >= g.P) {
+          p0 = 0;
+          ++n;
         }
       }
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        v[i][c] = cidx[c] >= 0 ? ldg4(xt_n + (long long)cidx[c] * g.C + gch)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int pix = ph * 16 + i * 4 + sub;
-      const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
-      const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
-      const uint32_t addr = sA + mb * W_LBO + mn32_offset(pix, quad);
-      tc::st_shared_v4(addr, tc::to_tf32(a * A.x + b * B.x + c * C.x + d * D.x),
-                       tc::to_tf32(a * A.y + b * B.y + c * C.y + d * D.y),
-                       tc::to_tf32(a * A.z + b * B.z + c * C.z + d * D.z),
-                       tc::to_tf32(a * A.w + b * B.w + c * C.w + d * D.w));
+  } else if (warp == W2_TMA_WARP) {
+    // ------------------------------ go_r rows (TMA) ------------------------------
+    if (lane == 0) {
+      int gs = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+        for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
+          const int st = gs & (W2_STAGES - 1);
+          const int u = gs / W2_STAGES;
+          const int n = tt / pchunks;
+          const int p0 = (tt - n * pchunks) << 5;
+          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+          tc::mbar_arrive_expect_tx(&full[st], b_stage);
+          tc::tma_load_2d(sB0 + st * b_stage, &gomap, p0, n * g.outC + T.gi * g.Og + T.o0,
+                          &full[st]);
+        }
+      }
     }
-    tc::cp_async_wait_all();
-    tc::fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
+    __syncwarp();
+  } else if (warp == W2_MMA_WARP) {
+    // ------------------------------ MMA ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
+      int gs = 0, it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+        if (T.t_begin >= T.t_end) continue;
+        const int acc = it & 1;
+        if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_bwd_status);
+        tc::tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * bn);
+        for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
+          const int st = gs & (W2_STAGES - 1);
+          const int s = tt - T.t_begin;
+          tc::mbar_wait(&full[st], (gs / W2_STAGES) & 1, &g_tc_bwd_status);
+          tc::tc_fence_after();
+          const uint32_t sA = sA0 + st * W2_A_STAGE, sB = sB0 + st * b_stage;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
+                          idesc, (s | j) != 0 ? 1u : 0u);
+          tc::umma_commit(&empty[st]);
+        }
+        tc::umma_commit(&acc_full[acc]);
+        ++it;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+      if (T.t_begin >= T.t_end) continue;
+      const int acc = it & 1;
+      tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
       tc::tc_fence_after();
+      const int c = T.cm0 + warp * 32 + lane;  // channel within the group
+      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + T.k;
+      const long long ostride = (long long)g.Cg * g.kk;
+      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
+      for (int cb = 0; cb < bn; cb += 8) {
+        float vv[8];
+        tc::tmem_ld8(ta + (uint32_t)cb, vv);
+        tc::tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        tc::umma_tf32(tmem, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32), idesc,
-                      (s | j) != 0 ? 1u : 0u);
-      tc::umma_commit(&mma_bar[st]);
+        for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+      ++it;
     }
   }
-  const int last = t_end - t_begin - 1;
-  tc::mbar_wait(&mma_bar[last & 1], (last >> 1) & 1, &g_tc_bwd_status);
-  tc::tc_fence_after();
-  {
-    // lanes = channels, columns = out channels
-    const int lq = warp & 3, half = warp >> 2;
-    const int c = cm0 + lq * 32 + lane;
-    const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
-    float* dst = gw + ((long long)(gi * g.Og + o0) * g.Cg + c) * g.kk + k;
-    const long long ostride = (long long)g.Cg * g.kk;
-    for (int cb = cbeg; cb < cend; cb += 8) {
-      float vv[8];
-      tc::tmem_ld8(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb, vv);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
-    }
-  }
+
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == W2_MMA_WARP) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, (uint32_t)tcols);
   }
@@ -564,22 +653,31 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
                                  const float* off, const float* mask, float* gw, int num_sms,
                                  cudaStream_t stream) {
   const int bn = weight_bn(g);
-  const size_t smem = weight_smem_bytes(bn);
-  cudaError_t e = cudaFuncSetAttribute(bwd_weight_tc_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int Ppad = (g.P + 3) & ~3;
+  CUtensorMap gomap;
+  cudaError_t e = make_tmap_2d_f32(&gomap, go_r, (uint64_t)Ppad, (uint64_t)g.N * g.outC,
+                                   (uint64_t)Ppad, (uint32_t)bn);
   if (e != cudaSuccess) return e;
-  const int base = g.kk * (g.Cg / W_BM) * (g.Og / bn) * g.G;
+  const size_t smem = weight_smem_bytes(bn);
+  e = cudaFuncSetAttribute(bwd_weight_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+  if (e != cudaSuccess) return e;
+  const int mtiles = g.Cg / W_BM;
+  const int ntn = g.Og / bn;
+  const long long base = (long long)g.kk * mtiles * ntn * g.G;
   const int pchunks = (g.P + 31) / 32;
   const int total_chunks = g.N * pchunks;
-  int splits = (2 * num_sms + base - 1) / base;
-  const int max_splits = (total_chunks + 7) / 8;  // >= 8 K steps per CTA
+  long long splits = (2LL * num_sms + base - 1) / base;
+  const long long max_splits = (total_chunks + 7) / 8;  // >= 8 K steps per tile
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
-  if ((long long)splits * g.G > 65535) splits = 65535 / g.G;
-  const int per = (total_chunks + splits - 1) / splits;
-  dim3 grid(g.kk * (g.Cg / W_BM), g.Og / bn, g.G * splits);
-  bwd_weight_tc_kernel<<<grid, THREADS, smem, stream>>>(g, go_r, bn, pow2_cols(bn), xt, off, mask,
-                                                         gw, splits, per);
+  const int per = (int)((total_chunks + splits - 1) / splits);
+  const long long ntiles = base * splits;
+  if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
+  bwd_weight_tc_kernel<<<grid, W2_THREADS, smem, stream>>>(g, gomap, bn, pow2_cols(2 * bn), xt,
+                                                          off, mask, gw, mtiles, ntn,
+                                                          (int)splits, per, (int)ntiles);
   return cudaGetLastError();
 }
 

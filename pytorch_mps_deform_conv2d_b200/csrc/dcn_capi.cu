@@ -183,8 +183,12 @@ FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
   return FwdAlgo::kGemm;
 }
 
+// NHWC copy of the input plus one zero pixel row (C floats) at its end, the
+// target of the tensor-core gathers' dropped corners.
+size_t xt_floats(const dcn::Geom& g) { return (size_t)g.N * g.HW * g.C + g.C; }
+
 size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
-  size_t b = align_up((size_t)g.N * g.HW * g.C * sizeof(float));  // xt
+  size_t b = align_up(xt_floats(g) * sizeof(float));  // xt + zero row
   switch (pick_fwd(g, flags)) {
     case FwdAlgo::kGemm:
       b += align_up((size_t)g.G * g.kk * fwd_cpad(g) * g.Og * sizeof(float));
@@ -204,7 +208,7 @@ bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
 }
 
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
-  size_t b = align_up((size_t)g.N * g.HW * g.C * sizeof(float));      // xt
+  size_t b = align_up(xt_floats(g) * sizeof(float));                   // xt + zero row
   b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
   if (use_tc_bwd(g, flags)) {
     b += align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
@@ -283,8 +287,10 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
-  float* xt = ws.take((size_t)g.N * g.HW * g.C);
+  float* xt = ws.take(xt_floats(g));
   DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
+  DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
+           "memset");
   switch (pick_fwd(g, flags)) {
     case FwdAlgo::kDirect:
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
@@ -359,10 +365,12 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
-  float* xt = ws.take((size_t)g.N * g.HW * g.C);
+  float* xt = ws.take(xt_floats(g));
   float* gxt = ws.take((size_t)g.N * g.HW * g.C);
   DCN_CUDA(cudaMemsetAsync(gxt, 0, x_bytes, stream), "memset");
   DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
+  DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
+           "memset");
   if (use_tc_bwd(g, flags)) {
     float* go_t = ws.take((size_t)g.N * g.outC * g.P);
     float* go_r = ws.take((size_t)g.N * g.outC * ((g.P + 3) & ~3));

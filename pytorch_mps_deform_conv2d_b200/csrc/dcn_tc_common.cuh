@@ -44,15 +44,26 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// One hardware-suspended wait attempt: the thread sleeps until the phase
+// completes or a system time limit passes (no issue slots spent polling).
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Waits until the phase with the given parity has completed.  Gives up after
 // ~`limit_cycles` SM clocks (then returns false and raises *err).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
                                           long long limit_cycles = 4000000000LL) {
-  if (mbar_test(bar, parity)) return true;
+  if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
-  int spins = 0;
-  while (!mbar_test(bar, parity)) {
-    if (++spins > 64) __nanosleep(64);
+  while (!mbar_try(bar, parity)) {
     if (clock64() - t0 > limit_cycles) {
       flag_timeout(err, 1);
       return false;
@@ -153,6 +164,35 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, fl
 }
 __device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+}  // namespace tc
+}  // namespace dcn
+
+// ---- TMA (bulk tensor copies) and plain mbarrier arrivals ----
+#include <cuda.h>
+
+namespace dcn {
+namespace tc {
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// 2-D tiled TMA load (no multicast): box at (x = inner element index, y = row)
+// into `dst` (1024-byte aligned for the 128-byte swizzle), completion counted
+// in bytes on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 }  // namespace tc

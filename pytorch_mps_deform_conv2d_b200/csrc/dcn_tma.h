@@ -1,0 +1,19 @@
+// dcn_tma.h -- host-side construction of TMA tensor maps (driver entry point
+// resolved through the runtime, so the library does not link libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+namespace dcn {
+
+// 2-D fp32 tensor map over `rows` rows of `inner` contiguous elements with a
+// row pitch of `pitch_elems`; boxes of 32 elements (128 B) x `box_rows` rows,
+// 128-byte swizzle, out-of-range elements read as zero.  `base` and the pitch
+// in bytes must be multiples of 16.
+cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
+                             uint64_t pitch_elems, uint32_t box_rows);
+
+}  // namespace dcn
