@@ -69,13 +69,18 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
 // bwd_data_tc
 // ---------------------------------------------------------------------------
 constexpr int D_BM = 128;
-
-size_t data_smem_bytes(int bn) { return 2 * 16384 + 2 * (size_t)bn * 128 + 64 + 1024; }
+constexpr int D_BN = 128;          // channels of one tap per tile
+constexpr int D_STAGES = 3;
+constexpr int D_EPI_WARPS = 16;    // 4 per tensor-memory lane quarter, 32 channels each
+constexpr int D_TMA_WARP = 0, D_MMA_WARP = 1, D_EPI_WARP0 = 2;
+constexpr int D_THREADS = (D_EPI_WARP0 + D_EPI_WARPS) * 32;  // 576
+constexpr int D_STAGE = D_BM * 128 + D_BN * 128;             // A + B = 32 KB
 
 // Sampling plan of one pixel for one (tap, deformable group), kept in shared
 // memory so that the 8 lanes working on the pixel can read it.
 struct PixPlan {
-  int cidx[4];     // n*H*W + y*W + x of each live corner, -1 when dropped
+  int cidx[4];     // element offset (n*H*W + y*W + x) * C of each corner; the
+                   // zero row for dropped corners
   float w[4];      // bilinear weights (0 for dropped corners)
   float lh, lw;    // fractional position
   float msk;       // modulation scalar
@@ -88,231 +93,277 @@ static_assert(sizeof(PixPlan) == 56, "PixPlan is 14 words");
 constexpr int EPI_TSTRIDE = 33;  // transpose buffer row stride (floats)
 constexpr int EPI_WARP_BYTES = 32 * EPI_TSTRIDE * 4 + 32 * (int)sizeof(PixPlan);  // 6016
 
-__device__ __forceinline__ void epilogue_tap(const Geom& g, int k, uint32_t tmem, int c0, int gi,
-                                             long long q0, int warp, int lane,
-                                             unsigned char* smem, const float* __restrict__ xt,
-                                             const float* __restrict__ off,
-                                             const float* __restrict__ mask,
-                                             float* __restrict__ gxt, float* __restrict__ goff,
-                                             float* __restrict__ gmask, int bn) {
-  const int lq = warp & 3, half = warp >> 2;
-  float* T = reinterpret_cast<float*>(smem + warp * EPI_WARP_BYTES);
-  PixPlan* plan = reinterpret_cast<PixPlan*>(smem + warp * EPI_WARP_BYTES + 32 * EPI_TSTRIDE * 4);
-  const int ki = k / g.kw, kj = k - ki * g.kw;
-  // this lane's own pixel (row of the accumulator)
-  const long long myq = q0 + lq * 32 + lane;
-  const bool myvalid = myq < g.NP;
-  const int myn = myvalid ? (int)(myq / g.P) : 0;
-  const int myp = myvalid ? (int)(myq - (long long)myn * g.P) : 0;
-  const int myoy = myp / g.Wo, myox = myp - myoy * g.Wo;
-  // cooperative role: channel quad, pixel sub-index
-  const int quad = lane & 7, sub = lane >> 3;
-  int plan_dgi = -1;
-  const int cbeg = half * (bn >> 1), cend = cbeg + (bn >> 1);
-  for (int cb = cbeg; cb < cend; cb += 32) {
-    float vals[32];
-    {
-      const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)cb;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float t[8];
-        tc::tmem_ld8(ta + 8 * j, t);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) vals[8 * j + e] = t[e];
-      }
-      tc::tmem_ld_wait();
-    }
-    const int gch0 = gi * g.Cg + c0 + cb;  // 32 channels, one deformable group
-    const int dgi = gch0 / g.cpg;
-    __syncwarp();
-    if (dgi != plan_dgi) {
-      plan_dgi = dgi;
-      PixPlan pl;
-      pl.oi = -1;
-      pl.mi = 0;
-      pl.pad_ = 0;
-      pl.lh = pl.lw = 0.f;
-      pl.msk = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        pl.cidx[c] = -1;
-        pl.w[c] = 0.f;
-      }
-      if (myvalid) {
-        const long long oi = off_h_index(g, myn, dgi, k, myp);
-        float h, w;
-        sample_pos(g, myoy, myox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-        const Sample sp = make_sample(h, w, g.H, g.W);
-        if (sp.valid) {
-          const int nb = myn * g.HW;
-          const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
-          const float wv[4] = {sp.w1, sp.w2, sp.w3, sp.w4};
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            pl.cidx[c] = ((sp.live >> c) & 1u) ? nb + ci[c] : -1;
-            pl.w[c] = wv[c];
-          }
-          pl.lh = sp.lh;
-          pl.lw = sp.lw;
-          pl.msk = g.use_mask ? __ldg(mask + mask_index(g, myn, dgi, k, myp)) : 1.f;
-          pl.oi = (int)oi;
-          pl.mi = (int)mask_index(g, myn, dgi, k, myp);
-        }
-      }
-      plan[lane] = pl;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) T[lane * EPI_TSTRIDE + j] = vals[j];
-    __syncwarp();
-    // 8 lanes per pixel, 4 pixels per round, 8 rounds
-#pragma unroll 2
-    for (int i = 0; i < 8; ++i) {
-      const int px = i * 4 + sub;
-      const PixPlan& pl = plan[px];
-      float s_h = 0.f, s_w = 0.f, s_m = 0.f;
-      if (pl.oi >= 0) {
-        const float gc0 = T[px * EPI_TSTRIDE + quad * 4 + 0];
-        const float gc1 = T[px * EPI_TSTRIDE + quad * 4 + 1];
-        const float gc2 = T[px * EPI_TSTRIDE + quad * 4 + 2];
-        const float gc3 = T[px * EPI_TSTRIDE + quad * 4 + 3];
-        const float* xq = xt + gch0 + quad * 4;
-        float4 v[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          v[c] = pl.cidx[c] >= 0 ? ldg4(xq + (size_t)pl.cidx[c] * g.C)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        Sample sp;
-        sp.w1 = pl.w[0]; sp.w2 = pl.w[1]; sp.w3 = pl.w[2]; sp.w4 = pl.w[3];
-        sp.lh = pl.lh; sp.lw = pl.lw;
-        const float m = pl.msk;
-        const float gcs[4] = {gc0, gc1, gc2, gc3};
-        const float a[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
-        const float b[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
-        const float c[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
-        const float d[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
-          s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
-          s_m += gcs[e] * bilerp(sp, a[e], b[e], c[e], d[e]);
-        }
-        float* gq = gxt + gch0 + quad * 4;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          if (pl.cidx[cc] < 0) continue;
-          const float wc = pl.w[cc] * m;
-          red_add_v4(gq + (size_t)pl.cidx[cc] * g.C, wc * gc0, wc * gc1, wc * gc2, wc * gc3);
-        }
-      }
-      // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
-      s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);
-      s_w += __shfl_xor_sync(0xffffffffu, s_w, 1);
-      s_m += __shfl_xor_sync(0xffffffffu, s_m, 1);
-      s_h += __shfl_xor_sync(0xffffffffu, s_h, 2);
-      s_w += __shfl_xor_sync(0xffffffffu, s_w, 2);
-      s_m += __shfl_xor_sync(0xffffffffu, s_m, 2);
-      s_h += __shfl_xor_sync(0xffffffffu, s_h, 4);
-      s_w += __shfl_xor_sync(0xffffffffu, s_w, 4);
-      s_m += __shfl_xor_sync(0xffffffffu, s_m, 4);
-      if (quad == 0 && pl.oi >= 0) {
-        red_add_f32(goff + pl.oi, s_h);
-        red_add_f32(goff + pl.oi + g.P, s_w);
-        if (g.use_mask) red_add_f32(gmask + pl.mi, s_m);
-      }
-    }
-  }
-  __syncwarp();
+size_t data_smem_bytes() {
+  return (size_t)D_STAGES * D_STAGE + (size_t)D_EPI_WARPS * EPI_WARP_BYTES + 128 + 1024;
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
-bwd_data_tc_kernel(Geom g, const float* __restrict__ go_t, const float* __restrict__ wb,
-                   int bn, int tcols, const float* __restrict__ xt,
-                   const float* __restrict__ off, const float* __restrict__ mask,
-                   float* __restrict__ gxt, float* __restrict__ goff,
-                   float* __restrict__ gmask) {
+struct DTile {
+  long long q0;
+  int c0, gi;
+};
+__device__ __forceinline__ DTile dtile_of(int t, int mtiles, int ctiles) {
+  DTile T;
+  const int mt = t % mtiles;
+  const int r = t / mtiles;
+  T.q0 = (long long)mt * D_BM;
+  T.c0 = (r % ctiles) * D_BN;
+  T.gi = r / ctiles;
+  return T;
+}
+
+// One epilogue warp, one tap: 32 pixel rows x 32 channels of the grad-column
+// accumulator.  Tensor memory gives each lane its own pixel's row; the rows go
+// through a shared-memory transpose so that 8 lanes cover one pixel's 32
+// channels, making every corner load and vector reduction a full 128-byte
+// line.  Scatters into the NHWC grad-input accumulator (col2im) and reduces
+// the coordinate / mask gradients of each pixel over its channels.
+__device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float (&vals)[32],
+                                               int gch0, long long row_q, int lane,
+                                               unsigned char* scratch,
+                                               const float* __restrict__ xt,
+                                               const float* __restrict__ off,
+                                               const float* __restrict__ mask,
+                                               float* __restrict__ gxt, float* __restrict__ goff,
+                                               float* __restrict__ gmask, int& plan_key) {
+  float* T = reinterpret_cast<float*>(scratch);
+  PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + 32 * EPI_TSTRIDE * 4);
+  const int quad = lane & 7, sub = lane >> 3;
+  const int zoff = g.N * g.HW * g.C;
+  const int dgi = gch0 / g.cpg;
+  const int key = k * 65536 + dgi;
+  __syncwarp();
+  if (key != plan_key) {
+    plan_key = key;
+    PixPlan pl;
+    pl.oi = -1;
+    pl.mi = 0;
+    pl.pad_ = 0;
+    pl.lh = pl.lw = 0.f;
+    pl.msk = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      pl.cidx[c] = zoff;
+      pl.w[c] = 0.f;
+    }
+    if (row_q < g.NP) {
+      const int n = (int)(row_q / g.P);
+      const int p = (int)(row_q - (long long)n * g.P);
+      const int oy = p / g.Wo, ox = p - oy * g.Wo;
+      const int ki = k / g.kw, kj = k - ki * g.kw;
+      const long long oi = off_h_index(g, n, dgi, k, p);
+      float h, w;
+      sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+      const Sample sp = make_sample(h, w, g.H, g.W);
+      if (sp.valid) {
+        const int nb = n * g.HW;
+        const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
+        const float wv[4] = {sp.w1, sp.w2, sp.w3, sp.w4};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          pl.cidx[c] = ((sp.live >> c) & 1u) ? (nb + ci[c]) * g.C : zoff;
+          pl.w[c] = wv[c];
+        }
+        pl.lh = sp.lh;
+        pl.lw = sp.lw;
+        pl.msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+        pl.oi = (int)oi;
+        pl.mi = (int)mask_index(g, n, dgi, k, p);
+      }
+    }
+    plan[lane] = pl;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) T[lane * EPI_TSTRIDE + j] = vals[j];
+  __syncwarp();
+  const float* xq = xt + gch0 + quad * 4;
+  float* gq = gxt + gch0 + quad * 4;
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int px = i * 4 + sub;
+    const PixPlan& pl = plan[px];
+    float s_h = 0.f, s_w = 0.f, s_m = 0.f;
+    if (pl.oi >= 0) {
+      const float gc0 = T[px * EPI_TSTRIDE + quad * 4 + 0];
+      const float gc1 = T[px * EPI_TSTRIDE + quad * 4 + 1];
+      const float gc2 = T[px * EPI_TSTRIDE + quad * 4 + 2];
+      const float gc3 = T[px * EPI_TSTRIDE + quad * 4 + 3];
+      float4 v[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[c] = ldg4(xq + (unsigned)pl.cidx[c]);  // dropped: zero row
+      Sample sp;
+      sp.w1 = pl.w[0]; sp.w2 = pl.w[1]; sp.w3 = pl.w[2]; sp.w4 = pl.w[3];
+      sp.lh = pl.lh; sp.lw = pl.lw;
+      const float m = pl.msk;
+      const float gcs[4] = {gc0, gc1, gc2, gc3};
+      const float a[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
+      const float b[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
+      const float c[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
+      const float d[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
+        s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
+        s_m += gcs[e] * bilerp(sp, a[e], b[e], c[e], d[e]);
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        if (pl.cidx[cc] == zoff) continue;
+        const float wc = pl.w[cc] * m;
+        red_add_v4(gq + (unsigned)pl.cidx[cc], wc * gc0, wc * gc1, wc * gc2, wc * gc3);
+      }
+    }
+    // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
+    s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);
+    s_w += __shfl_xor_sync(0xffffffffu, s_w, 1);
+    s_m += __shfl_xor_sync(0xffffffffu, s_m, 1);
+    s_h += __shfl_xor_sync(0xffffffffu, s_h, 2);
+    s_w += __shfl_xor_sync(0xffffffffu, s_w, 2);
+    s_m += __shfl_xor_sync(0xffffffffu, s_m, 2);
+    s_h += __shfl_xor_sync(0xffffffffu, s_h, 4);
+    s_w += __shfl_xor_sync(0xffffffffu, s_w, 4);
+    s_m += __shfl_xor_sync(0xffffffffu, s_m, 4);
+    if (quad == 0 && pl.oi >= 0) {
+      red_add_f32(goff + pl.oi, s_h);
+      red_add_f32(goff + pl.oi + g.P, s_w);
+      if (g.use_mask) red_add_f32(gmask + pl.mi, s_m);
+    }
+  }
+}
+
+// Persistent, warp-specialised grad-column kernel.  Tile = 128 pixels x 128
+// channels of one group; per tap a K = Og GEMM into one of two tensor-memory
+// accumulators (taps alternate), consumed by 16 epilogue warps while the next
+// tap accumulates.
+//   warp 0      TMA producer: go_t rows (128 pixels x 32 out channels) and
+//               packed weight rows (128 channels x 32 out channels) per K step
+//   warp 1      MMA issue: 4 UMMAs 128 x 128 x 8 per K step
+//   warps 2-17  epilogue (epilogue_chunk)
+__global__ void __launch_bounds__(D_THREADS, 1)
+bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap bmap, int mtiles, int ctiles, int ntiles,
+                   const float* __restrict__ xt, const float* __restrict__ off,
+                   const float* __restrict__ mask, float* __restrict__ gxt,
+                   float* __restrict__ goff, float* __restrict__ gmask) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
-  const uint32_t sA0 = tc::smem_u32(smem);
-  const uint32_t sB0 = sA0 + 2 * 16384;
-  const uint32_t b_stage = (uint32_t)bn * 128;
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 2 * 16384 + 2 * b_stage);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_bar + 2);
+  const uint32_t s0 = tc::smem_u32(smem);
+  unsigned char* epi = smem + D_STAGES * D_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi + D_EPI_WARPS * EPI_WARP_BYTES);
+  uint64_t* empty = full + D_STAGES;
+  uint64_t* acc_full = empty + D_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const long long q0 = (long long)blockIdx.x * D_BM;
-  const int c0 = blockIdx.y * bn;  // channel tile within the group
-  const int gi = blockIdx.z;
   const int ochunks = g.Og >> 5;
 
   if (tid == 0) {
-    tc::mbar_init(&mma_bar[0], 1);
-    tc::mbar_init(&mma_bar[1], 1);
+    for (int s = 0; s < D_STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&acc_full[a], 1);
+      tc::mbar_init(&acc_empty[a], D_EPI_WARPS);
+    }
     tc::fence_mbar_init();
   }
-  if (warp == 0) {
-    tc::tmem_alloc(tmem_slot, (uint32_t)tcols);
+  if (warp == D_MMA_WARP) {
+    tc::tmem_alloc(tmem_slot, 2 * D_BN);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t idesc = tc::idesc_tf32(D_BM, bn);
 
-  int s_global = 0;  // K steps issued so far (stage / parity bookkeeping)
-  for (int k = 0; k < g.kk; ++k) {
-    // ---- mainloop: gcol_k = go_t[tile] . W_k^T over Og in 32-wide steps ----
-    const float* bsrc = wb + ((size_t)(gi * g.kk + k) * g.Cg + c0) * g.Og;
-    for (int s = 0; s < ochunks; ++s, ++s_global) {
-      const int st = s_global & 1;
-      if (s_global >= 2) tc::mbar_wait(&mma_bar[st], ((s_global - 2) >> 1) & 1, &g_tc_bwd_status);
-      const uint32_t sA = sA0 + st * 16384, sB = sB0 + st * b_stage;
-      // A: 128 pixel rows x 32 out channels
-      for (int i = tid; i < D_BM * 8; i += THREADS) {
-        const int row = i >> 3, j = i & 7;
-        const long long qq = q0 + row;
-        const uint32_t dst = sA + tc::sw128_offset(row, j);
-        if (qq < g.NP)
-          tc::cp_async16(dst, go_t + qq * g.outC + (long long)gi * g.Og + s * 32 + j * 4);
-        else
-          tc::st_shared_v4(dst, 0.f, 0.f, 0.f, 0.f);
-      }
-      // B: bn channel rows x 32 out channels
-      for (int i = tid; i < bn * 8; i += THREADS) {
-        const int row = i >> 3, j = i & 7;
-        tc::cp_async16(sB + tc::sw128_offset(row, j), bsrc + (size_t)row * g.Og + s * 32 + j * 4);
-      }
-      tc::cp_async_wait_all();
-      tc::fence_proxy_async();
-      __syncthreads();
-      if (tid == 0) {
-        tc::tc_fence_after();
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          tc::umma_tf32(tmem, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
-                        (s | j) != 0 ? 1u : 0u);
-        tc::umma_commit(&mma_bar[st]);
+  if (warp == D_TMA_WARP) {
+    if (lane == 0) {
+      int gs = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const DTile T = dtile_of(t, mtiles, ctiles);
+        for (int k = 0; k < g.kk; ++k) {
+          const int brow = (T.gi * g.kk + k) * g.Cg + T.c0;
+          for (int s = 0; s < ochunks; ++s, ++gs) {
+            const int st = gs % D_STAGES;
+            const int u = gs / D_STAGES;
+            if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+            tc::mbar_arrive_expect_tx(&full[st], D_STAGE);
+            const uint32_t sA = s0 + st * D_STAGE;
+            tc::tma_load_2d(sA, &amap, T.gi * g.Og + s * 32, (int)T.q0, &full[st]);
+            tc::tma_load_2d(sA + D_BM * 128, &bmap, s * 32, brow, &full[st]);
+          }
+        }
       }
     }
-    const int last = s_global - 1;
-    tc::mbar_wait(&mma_bar[last & 1], (last >> 1) & 1, &g_tc_bwd_status);
-    tc::tc_fence_after();
-
-    // ---- epilogue: col2im scatter + coordinate / mask sums ----
-    // Tensor memory hands each thread its own pixel's row.  Each warp moves
-    // 32 pixels x 32 channels at a time through shared memory (the stage
-    // buffers are free now) so that 8 lanes cover one pixel's 32 channels:
-    // corner loads and vector reductions are then full 128-byte lines.
-    epilogue_tap(g, k, tmem, c0, gi, q0, warp, lane, smem, xt, off, mask, gxt, goff, gmask, bn);
-    __syncthreads();  // the next tap's stage writes reuse the epilogue's shared memory
-    tc::tc_fence_before();  // our tensor-memory reads precede the next tap's MMAs
+    __syncwarp();
+  } else if (warp == D_MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_tf32(D_BM, D_BN);
+      int gs = 0, gt = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        for (int k = 0; k < g.kk; ++k, ++gt) {
+          const int acc = gt & 1;
+          if (gt >= 2) tc::mbar_wait(&acc_empty[acc], ((gt >> 1) - 1) & 1, &g_tc_bwd_status);
+          tc::tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(acc * D_BN);
+          for (int s = 0; s < ochunks; ++s, ++gs) {
+            const int st = gs % D_STAGES;
+            tc::mbar_wait(&full[st], (gs / D_STAGES) & 1, &g_tc_bwd_status);
+            tc::tc_fence_after();
+            const uint32_t sA = s0 + st * D_STAGE, sB = sA + D_BM * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
+                            (s | j) != 0 ? 1u : 0u);
+            tc::umma_commit(&empty[st]);
+          }
+          tc::umma_commit(&acc_full[acc]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    const int e = warp - D_EPI_WARP0;
+    const int lq = warp & 3;      // tensor-memory lane quarter this warp may read
+    const int chunk = e >> 2;     // 32-channel chunk of the tile
+    unsigned char* scratch = epi + e * EPI_WARP_BYTES;
+    int gt = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const DTile T = dtile_of(t, mtiles, ctiles);
+      const long long row_q = T.q0 + lq * 32 + lane;
+      int plan_key = -1;
+      for (int k = 0; k < g.kk; ++k, ++gt) {
+        const int acc = gt & 1;
+        tc::mbar_wait(&acc_full[acc], (gt >> 1) & 1, &g_tc_bwd_status);
+        tc::tc_fence_after();
+        float vals[32];
+        {
+          const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(acc * D_BN + chunk * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float tv[8];
+            tc::tmem_ld8(ta + 8 * j, tv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) vals[8 * j + q] = tv[q];
+          }
+          tc::tmem_ld_wait();
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for tap + 2
+        epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, lane, scratch, xt, off,
+                       mask, gxt, goff, gmask, plan_key);
+      }
+    }
   }
+
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == D_MMA_WARP) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, (uint32_t)tcols);
+    tc::tmem_dealloc(tmem, 2 * D_BN);
   }
 }
 
@@ -443,11 +494,36 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       uint32_t soff[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) soff[i] = mb * W_LBO + mn32_offset(pg * 8 + i * 4 + sub, quad);
+      // The offsets / mask of the next K step are loaded one step ahead, so
+      // each step waits for one L2 round trip (its corners), not two.
       int n = T.t_begin / pchunks;
       int p0 = (T.t_begin - n * pchunks) << 5;
+      float nh[2], nw[2], nm[2];  // raw offset pair and mask of the next step's pixels
+      auto fetch = [&](int fn, int fp0) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int pp = fp0 + pg * 8 + i * 4 + sub;
+          nh[i] = nw[i] = 0.f;
+          nm[i] = 1.f;
+          if (pp < g.P && fn < g.N) {
+            const long long oi = off_h_index(g, fn, dgi, T.k, pp);
+            nh[i] = __ldg(off + oi);
+            nw[i] = __ldg(off + oi + g.P);
+            if (g.use_mask) nm[i] = __ldg(mask + mask_index(g, fn, dgi, T.k, pp));
+          }
+        }
+      };
+      fetch(n, p0);
       for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
         const int st = gs & (W2_STAGES - 1);
         const int u = gs / W2_STAGES;
+        const float ch[2] = {nh[0], nh[1]}, cwo[2] = {nw[0], nw[1]}, cm[2] = {nm[0], nm[1]};
+        const int cn = n, cp0 = p0;
+        p0 += 32;
+        if (p0 >= g.P) {
+          p0 = 0;
+          ++n;
+        }
         int coff[2][4];
         float cw[2][4];
 #pragma unroll
@@ -457,16 +533,15 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
             coff[i][c] = zoff;
             cw[i][c] = 0.f;
           }
-          const int pp = p0 + pg * 8 + i * 4 + sub;
+          const int pp = cp0 + pg * 8 + i * 4 + sub;
           if (pp >= g.P) continue;
           const int oy = pp / g.Wo, ox = pp - oy * g.Wo;
-          const long long oi = off_h_index(g, n, dgi, T.k, pp);
           float h, w;
-          sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-          const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, T.k, pp)) : 1.f;
+          sample_pos(g, oy, ox, ki, kj, ch[i], cwo[i], h, w);
+          const float m = cm[i];
           const Sample sp = make_sample(h, w, g.H, g.W);
           if (!sp.valid) continue;
-          const int xn = n * g.HW;
+          const int xn = cn * g.HW;
           if (sp.live & 1u) { coff[i][0] = (xn + sp.i1) * g.C; cw[i][0] = sp.w1 * m; }
           if (sp.live & 2u) { coff[i][1] = (xn + sp.i2) * g.C; cw[i][1] = sp.w2 * m; }
           if (sp.live & 4u) { coff[i][2] = (xn + sp.i3) * g.C; cw[i][2] = sp.w3 * m; }
@@ -478,6 +553,7 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             v[i][c] = ldg4(xq + (unsigned)coff[i][c]);  // dropped corners: zero row
+        if (tt + 1 < T.t_end) fetch(n, p0);
         if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
         const uint32_t sA = sA0 + st * W2_A_STAGE;
 #pragma unroll
@@ -492,11 +568,6 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
         tc::fence_proxy_async();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&full[st]);
-        p0 += 32;
-        if (p0 >= g.P) {
-          p0 = 0;
-          ++n;
-        }
       }
     }
   } else if (warp == W2_TMA_WARP) {
@@ -598,7 +669,6 @@ __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __
   }
 }
 
-int data_bn(const Geom& g) { return g.Cg <= 128 ? g.Cg : 128; }
 int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
 
 }  // namespace
@@ -638,14 +708,28 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
                                const float* xt, const float* off, const float* mask,
                                float* gxt, float* goff, float* gmask, cudaStream_t stream) {
-  const int bn = data_bn(g);
-  const size_t smem = data_smem_bytes(bn);
-  cudaError_t e = cudaFuncSetAttribute(bwd_data_tc_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  CUtensorMap amap, bmap;
+  cudaError_t e = make_tmap_2d_f32(&amap, go_t, (uint64_t)g.outC, (uint64_t)g.NP,
+                                   (uint64_t)g.outC, (uint32_t)D_BM);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((g.NP + D_BM - 1) / D_BM), g.Cg / bn, g.G);
-  bwd_data_tc_kernel<<<grid, THREADS, smem, stream>>>(g, go_t, wbt, bn, pow2_cols(bn), xt, off,
-                                                       mask, gxt, goff, gmask);
+  e = make_tmap_2d_f32(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg, (uint64_t)g.Og,
+                       (uint32_t)D_BN);
+  if (e != cudaSuccess) return e;
+  const size_t smem = data_smem_bytes();
+  e = cudaFuncSetAttribute(bwd_data_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int mtiles = (int)((g.NP + D_BM - 1) / D_BM);
+  const int ctiles = g.Cg / D_BN;
+  const long long ntiles = (long long)mtiles * ctiles * g.G;
+  if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(ntiles < sms ? ntiles : sms);
+  bwd_data_tc_kernel<<<grid, D_THREADS, smem, stream>>>(g, amap, bmap, mtiles, ctiles,
+                                                         (int)ntiles, xt, off, mask, gxt, goff,
+                                                         gmask);
   return cudaGetLastError();
 }
 
