@@ -39,9 +39,12 @@ int pow2_cols(int n) {
 // ---------------------------------------------------------------------------
 // prep: go (N, outC, P) -> go_t (N*P, outC) and go_r (N, outC, P), tf32-rounded
 // ---------------------------------------------------------------------------
+// Also accumulates grad_bias (pre-zeroed; NULL when not wanted) from the
+// unrounded values: each block adds its 32 x 32 tile's per-channel sums.
 __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
                                                       float* __restrict__ go_t,
-                                                      float* __restrict__ go_r, int outC,
+                                                      float* __restrict__ go_r,
+                                                      float* __restrict__ gb, int outC,
                                                       int P, int Ppad) {
   __shared__ float tile[32][33];
   const int n = blockIdx.z;
@@ -51,10 +54,18 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
     const int o = o0 + ty + i, p = p0 + tx;
+    float raw = 0.f;
     if (o < outC && p < Ppad) {
-      const float v = p < P ? tc::to_tf32(src[(long long)o * P + p]) : 0.f;
+      raw = p < P ? src[(long long)o * P + p] : 0.f;
+      const float v = tc::to_tf32(raw);
       tile[ty + i][tx] = v;
       go_r[((long long)n * outC + o) * Ppad + p] = v;
+    }
+    if (gb) {
+      float sum = raw;
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+      if (tx == 0 && o < outC) atomicAdd(gb + o, sum);
     }
   }
   __syncthreads();
@@ -687,11 +698,11 @@ size_t tc_bwd_scratch_bytes(const Geom& g) {
 }
 
 cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
-                              cudaStream_t stream) {
+                              float* gb, cudaStream_t stream) {
   if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
   const int Ppad = (g.P + 3) & ~3;
   dim3 grid((Ppad + 31) / 32, (g.outC + 31) / 32, g.N);
-  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_r, g.outC, g.P, Ppad);
+  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_r, gb, g.outC, g.P, Ppad);
   return cudaGetLastError();
 }
 

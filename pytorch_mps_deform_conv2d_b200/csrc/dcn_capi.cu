@@ -348,6 +348,7 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   if (off_bytes) DCN_CUDA(cudaMemsetAsync(grad_offset, 0, off_bytes, stream), "memset");
   if (grad_mask && msk_bytes) DCN_CUDA(cudaMemsetAsync(grad_mask, 0, msk_bytes, stream), "memset");
   if (w_bytes) DCN_CUDA(cudaMemsetAsync(grad_weight, 0, w_bytes, stream), "memset");
+  const bool tc_bwd = use_tc_bwd(g, flags);
   if (grad_bias) {
     if (g.N * (long long)g.P == 0) {
       if (g.outC) DCN_CUDA(cudaMemsetAsync(grad_bias, 0, (size_t)g.outC * sizeof(float), stream), "memset");
@@ -371,11 +372,11 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
   DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
            "memset");
-  if (use_tc_bwd(g, flags)) {
+  if (tc_bwd) {
     float* go_t = ws.take((size_t)g.N * g.outC * g.P);
     float* go_r = ws.take((size_t)g.N * g.outC * ((g.P + 3) & ~3));
     float* wbt = ws.take((size_t)g.outC * g.Cg * g.kk);
-    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_r, stream), "tc_prep_go");
+    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_r, nullptr, stream), "tc_prep_go");
     DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, stream), "tc_pack_weight_bwd");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, wbt, xt, offset, mask, gxt, grad_offset, grad_mask,
                                      stream),
@@ -384,6 +385,13 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, offset, mask, grad_weight, num_sms_current(),
                                        stream),
              "bwd_weight_tc");
+    return DCN_OK;
+  }
+  if (dcn::bwd_small_supported(g) && !(flags & DCN_ALGO_SIMT_GEMM)) {
+    DCN_CUDA(dcn::launch_bwd_small(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
+                                   grad_mask, grad_weight, stream),
+             "bwd_small");
+    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
     return DCN_OK;
   }
   float* wb = ws.take((size_t)g.G * g.kk * g.Og * g.Cg);

@@ -52,6 +52,14 @@ cudaError_t launch_bwd_weight_simt(const Geom& g, const float* go, const float* 
                                    const float* off, const float* mask, float* gw,
                                    int num_sms, cudaStream_t stream);
 
+// Whole backward for small groups (out channels per group <= 8, in channels
+// per group <= 16): grad-input scatter into gxt (NHWC), coordinate / mask
+// gradients and grad_weight, all pre-zeroed accumulators.
+bool bwd_small_supported(const Geom& g);
+cudaError_t launch_bwd_small(const Geom& g, const float* go, const float* w, const float* xt,
+                             const float* off, const float* mask, float* gxt, float* goff,
+                             float* gmask, float* gw, cudaStream_t stream);
+
 // ---- single-image building blocks (dcn_debug_ops.cu) ----------------------
 cudaError_t launch_col2im_single(const Geom& g, const float* col, const float* off,
                                  const float* mask, float* grad_im,

@@ -33,11 +33,54 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
   }
 }
 
+// Same transpose with 64 x 64 tiles and 16-byte loads and stores; needs R and
+// S multiples of 4 and 16-byte aligned buffers.
+__global__ void __launch_bounds__(256) transpose4_kernel(const float* __restrict__ in,
+                                                         float* __restrict__ out, int R, int S) {
+  __shared__ float tile[64][65];
+  const int n = blockIdx.z;
+  const int r0 = blockIdx.y * 64, s0 = blockIdx.x * 64;
+  const float* src = in + (long long)n * R * S;
+  float* dst = out + (long long)n * R * S;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + ty + 16 * i, s = s0 + tx * 4;
+    if (r < R && s < S) {
+      const float4 v = *reinterpret_cast<const float4*>(src + (long long)r * S + s);
+      tile[ty + 16 * i][tx * 4 + 0] = v.x;
+      tile[ty + 16 * i][tx * 4 + 1] = v.y;
+      tile[ty + 16 * i][tx * 4 + 2] = v.z;
+      tile[ty + 16 * i][tx * 4 + 3] = v.w;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int s = s0 + ty + 16 * i, r = r0 + tx * 4;
+    if (s < S && r < R) {
+      float4 v;
+      v.x = tile[tx * 4 + 0][ty + 16 * i];
+      v.y = tile[tx * 4 + 1][ty + 16 * i];
+      v.z = tile[tx * 4 + 2][ty + 16 * i];
+      v.w = tile[tx * 4 + 3][ty + 16 * i];
+      *reinterpret_cast<float4*>(dst + (long long)s * R + r) = v;
+    }
+  }
+}
+
 cudaError_t launch_transpose(const float* in, float* out, int N, int R, int S,
                              cudaStream_t stream) {
   if ((long long)N * R * S == 0) return cudaSuccess;
-  dim3 grid(ceil_div(S, TT), ceil_div(R, TT), N);
-  transpose_kernel<<<grid, dim3(TT, 8), 0, stream>>>(in, out, R, S);
+  const bool vec = R % 4 == 0 && S % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && ceil_div(R, 64) <= 65535;
+  if (vec) {
+    dim3 grid(ceil_div(S, 64), ceil_div(R, 64), N);
+    transpose4_kernel<<<grid, 256, 0, stream>>>(in, out, R, S);
+  } else {
+    dim3 grid(ceil_div(S, TT), ceil_div(R, TT), N);
+    transpose_kernel<<<grid, dim3(TT, 8), 0, stream>>>(in, out, R, S);
+  }
   return cudaGetLastError();
 }
 
@@ -75,21 +118,22 @@ __global__ void pack_weight_bwd_kernel(const float* __restrict__ w,
   }
 }
 
-// grad_bias: block (o, split) sums a contiguous range of the (n, p) pixels
-// of channel o and adds it into the zeroed grad_bias.
-constexpr int GB_CHUNK = 8192;
-
+// grad_bias: block (o, n) sums grad_out[n, o, :] (16-byte loads when the
+// row allows it) and adds it into the zeroed grad_bias.
+template <bool VEC>
 __global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict__ go,
                                                         float* __restrict__ gb, Geom g) {
-  const int o = blockIdx.x;
-  const long long total = (long long)g.N * g.P;
-  const long long beg = (long long)blockIdx.y * GB_CHUNK;
-  const long long end = beg + GB_CHUNK < total ? beg + GB_CHUNK : total;
+  const int o = blockIdx.x, n = blockIdx.y;
+  const float* row = go + ((long long)n * g.outC + o) * g.P;
   float s = 0.f;
-  for (long long i = beg + threadIdx.x; i < end; i += blockDim.x) {
-    const int n = (int)(i / g.P);
-    const int p = (int)(i - (long long)n * g.P);
-    s += go[((long long)n * g.outC + o) * g.P + p];
+  if (VEC) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    for (int i = threadIdx.x; i < (g.P >> 2); i += blockDim.x) {
+      const float4 v = __ldg(r4 + i);
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < g.P; i += blockDim.x) s += __ldg(row + i);
   }
   __shared__ float red[32];
 #pragma unroll
@@ -162,12 +206,14 @@ cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
   if (g.outC == 0) return cudaSuccess;
   cudaError_t e = cudaMemsetAsync(gb, 0, (size_t)g.outC * sizeof(float), stream);
   if (e != cudaSuccess) return e;
-  const long long total = (long long)g.N * g.P;
-  if (total == 0) return cudaSuccess;
-  const long long splits = (total + GB_CHUNK - 1) / GB_CHUNK;
-  if (splits > 65535) return cudaErrorInvalidValue;
-  grad_bias_kernel<<<dim3(g.outC, (unsigned)splits), 256, 0, stream>>>(go, gb, g);
+  if ((long long)g.N * g.P == 0) return cudaSuccess;
+  if (g.N > 65535) return cudaErrorInvalidValue;
+  const bool vec = (g.P % 4 == 0) && ((reinterpret_cast<uintptr_t>(go) & 15u) == 0);
+  dim3 grid(g.outC, g.N);
+  if (vec)
+    grad_bias_kernel<true><<<grid, 256, 0, stream>>>(go, gb, g);
+  else
+    grad_bias_kernel<false><<<grid, 256, 0, stream>>>(go, gb, g);
   return cudaGetLastError();
 }
-
 }  // namespace dcn

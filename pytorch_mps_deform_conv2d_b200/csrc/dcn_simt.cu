@@ -639,6 +639,106 @@ bwd_weight_simt_kernel(Geom g, const float* __restrict__ go, const float* __rest
   }
 }
 
+// ===========================================================================
+// Backward for small groups (<= 8 out channels and <= 16 in channels per
+// group, e.g. groups=32 with 2 channels each).  One thread per (pixel, group)
+// does the whole backward of its pixel for that group: the grad-column values
+// (a tiny K = Og dot product), the col2im scatter, the coordinate / mask sums
+// of its channels (atomics, since other groups share the deformable group),
+// and its contribution to grad_weight, first summed over the block's pixels
+// in shared memory.  Block = 128 pixels of one group.
+// ===========================================================================
+constexpr int SMALL_THREADS = 128;
+constexpr int SMALL_MAX_OG = 8, SMALL_MAX_CG = 16;
+
+template <int OG>
+__global__ void __launch_bounds__(SMALL_THREADS)
+bwd_small_kernel(Geom g, const float* __restrict__ go, const float* __restrict__ w,
+                 const float* __restrict__ xt, const float* __restrict__ off,
+                 const float* __restrict__ mask, float* __restrict__ gxt,
+                 float* __restrict__ goff, float* __restrict__ gmask, float* __restrict__ gw) {
+  extern __shared__ float sm[];  // [Og][Cg][kk] weights, then the same size of grad_weight sums
+  const int gi = blockIdx.y;
+  const int wcount = g.Og * g.Cg * g.kk;
+  float* ws = sm;
+  float* gws = sm + wcount;
+  for (int i = threadIdx.x; i < wcount; i += SMALL_THREADS) {
+    ws[i] = w[(long long)gi * wcount + i];
+    gws[i] = 0.f;
+  }
+  __syncthreads();
+  const long long q = (long long)blockIdx.x * SMALL_THREADS + threadIdx.x;
+  if (q < g.NP) {
+    const int n = (int)(q / g.P);
+    const int p = (int)(q - (long long)n * g.P);
+    const int oy = p / g.Wo, ox = p - oy * g.Wo;
+    float gov[OG];
+#pragma unroll
+    for (int o = 0; o < OG; ++o)
+      gov[o] = o < g.Og ? __ldg(go + ((long long)n * g.outC + gi * g.Og + o) * g.P + p) : 0.f;
+    const float* xt_n = xt + (long long)n * g.HW * g.C;
+    float* gxt_n = gxt + (long long)n * g.HW * g.C;
+    for (int k = 0; k < g.kk; ++k) {
+      const int ki = k / g.kw, kj = k - ki * g.kw;
+      int cur_dgi = -1;
+      Sample sp = make_sample(-2.f, -2.f, 1, 1);
+      float msk = 0.f, s_h = 0.f, s_w = 0.f, s_m = 0.f;
+      for (int c = 0; c < g.Cg; ++c) {
+        const int gch = gi * g.Cg + c;
+        const int dgi = gch / g.cpg;
+        if (dgi != cur_dgi) {
+          if (cur_dgi >= 0 && sp.valid) {
+            const long long oi = off_h_index(g, n, cur_dgi, k, p);
+            red_add_f32(goff + oi, s_h);
+            red_add_f32(goff + oi + g.P, s_w);
+            if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+          }
+          s_h = s_w = s_m = 0.f;
+          cur_dgi = dgi;
+          const long long oi = off_h_index(g, n, dgi, k, p);
+          float h, wv;
+          sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, wv);
+          msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+          sp = make_sample(h, wv, g.H, g.W);
+        }
+        if (!sp.valid) continue;
+        float gc = 0.f;
+#pragma unroll
+        for (int o = 0; o < OG; ++o)
+          if (o < g.Og) gc = fmaf(gov[o], ws[(o * g.Cg + c) * g.kk + k], gc);
+        const float* base = xt_n + gch;
+        const float a = (sp.live & 1u) ? __ldg(base + (long long)sp.i1 * g.C) : 0.f;
+        const float b = (sp.live & 2u) ? __ldg(base + (long long)sp.i2 * g.C) : 0.f;
+        const float cc = (sp.live & 4u) ? __ldg(base + (long long)sp.i3 * g.C) : 0.f;
+        const float d = (sp.live & 8u) ? __ldg(base + (long long)sp.i4 * g.C) : 0.f;
+        const float val = bilerp(sp, a, b, cc, d);
+        s_h += msk * coord_dh(sp, a, b, cc, d) * gc;
+        s_w += msk * coord_dw(sp, a, b, cc, d) * gc;
+        s_m += gc * val;
+        const float top = gc * msk;
+        float* gb = gxt_n + gch;
+        if (sp.live & 1u) red_add_f32(gb + (long long)sp.i1 * g.C, sp.w1 * top);
+        if (sp.live & 2u) red_add_f32(gb + (long long)sp.i2 * g.C, sp.w2 * top);
+        if (sp.live & 4u) red_add_f32(gb + (long long)sp.i3 * g.C, sp.w3 * top);
+        if (sp.live & 8u) red_add_f32(gb + (long long)sp.i4 * g.C, sp.w4 * top);
+        const float colv = val * msk;
+#pragma unroll
+        for (int o = 0; o < OG; ++o)
+          if (o < g.Og) atomicAdd(&gws[(o * g.Cg + c) * g.kk + k], gov[o] * colv);
+      }
+      if (cur_dgi >= 0 && sp.valid) {
+        const long long oi = off_h_index(g, n, cur_dgi, k, p);
+        red_add_f32(goff + oi, s_h);
+        red_add_f32(goff + oi + g.P, s_w);
+        if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < wcount; i += SMALL_THREADS)
+    red_add_f32(gw + (long long)gi * wcount + i, gws[i]);
+}
+
 bool vec4_ok(const Geom& g) { return g.C % 4 == 0 && g.Cg % 4 == 0 && g.cpg % 4 == 0; }
 bool vec8_ok(const Geom& g) { return g.C % 4 == 0 && g.Cg % 8 == 0 && g.cpg % 8 == 0; }
 
@@ -688,6 +788,27 @@ cudaError_t launch_bwd_data_simt(const Geom& g, const float* go, const float* wb
     bwd_data_simt_kernel<true><<<grid, 256, 0, stream>>>(g, go, wb, xt, off, mask, gxt, goff, gmask);
   else
     bwd_data_simt_kernel<false><<<grid, 256, 0, stream>>>(g, go, wb, xt, off, mask, gxt, goff, gmask);
+  return cudaGetLastError();
+}
+
+bool bwd_small_supported(const Geom& g) {
+  return g.Og <= SMALL_MAX_OG && g.Cg <= SMALL_MAX_CG &&
+         (size_t)2 * g.Og * g.Cg * g.kk * sizeof(float) <= 48 * 1024;
+}
+
+cudaError_t launch_bwd_small(const Geom& g, const float* go, const float* w, const float* xt,
+                             const float* off, const float* mask, float* gxt, float* goff,
+                             float* gmask, float* gw, cudaStream_t stream) {
+  if (g.NP == 0 || g.Cg == 0 || g.Og == 0) return cudaSuccess;
+  if (!bwd_small_supported(g)) return cudaErrorInvalidValue;
+  dim3 grid((unsigned)((g.NP + SMALL_THREADS - 1) / SMALL_THREADS), g.G);
+  const size_t smem = (size_t)2 * g.Og * g.Cg * g.kk * sizeof(float);
+  if (g.Og <= 2)
+    bwd_small_kernel<2><<<grid, SMALL_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
+  else if (g.Og <= 4)
+    bwd_small_kernel<4><<<grid, SMALL_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
+  else
+    bwd_small_kernel<8><<<grid, SMALL_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
   return cudaGetLastError();
 }
 

@@ -27,8 +27,10 @@ bool tc_bwd_supported(const Geom& g);
 // copies: go_t and go_r (tf32-rounded grad_out, pixel-major and NCHW) and the
 // packed weight.
 size_t tc_bwd_scratch_bytes(const Geom& g);
+// go -> go_t / go_r (tf32-rounded); also sums grad_bias into `gb` (zeroed by
+// the caller) when it is not NULL.
 cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
-                              cudaStream_t stream);
+                              float* gb, cudaStream_t stream);
 cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
                                       cudaStream_t stream);
 // grad_col = W^T go on the tensor core per (pixel tile, tap), fused with the
