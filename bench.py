@@ -329,15 +329,11 @@ def run_ours(args, wl):
     flush = torch.empty(FLUSH_BYTES // 4, device=dev)
     comm_stream = torch.cuda.current_stream(dev)
 
-    def allreduce(grads):
-        if world == 1:
-            return
-        flat = torch.cat([g.reshape(-1) for g in grads])
-        dist.all_reduce(flat)
-        o = 0
-        for g in grads:
-            g.copy_(flat[o:o + g.numel()].view_as(g))
-            o += g.numel()
+    from pytorch_mps_deform_conv2d_b200.distributed import allreduce_grads
+
+    def allreduce(params_):
+        if world > 1:
+            allreduce_grads(params_)
 
     def step():
         for t in leaves:
@@ -345,7 +341,7 @@ def run_ours(args, wl):
         out = deform_conv2d_ex(xd, offd, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
                                flags=flags)
         out.backward(god)
-        allreduce([p.grad for p in params])
+        allreduce(params)
 
     for _ in range(args.warmup):
         step()
@@ -484,7 +480,7 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
             p.grad = None
         out = mod(xd, od, md)
         out.backward(gd)
-        allreduce([p.grad for p in params])
+        allreduce(params)
         for p, o in zip(params, outs):
             o.copy_(p.grad, non_blocking=True)
 

@@ -108,17 +108,23 @@ size_t data_smem_bytes() {
   return (size_t)D_STAGES * D_STAGE + (size_t)D_EPI_WARPS * EPI_WARP_BYTES + 128 + 1024;
 }
 
+// A tile is (128 pixels, 128 channels, group, range of taps); the taps are
+// independent in this kernel, so splitting them evens out the CTAs' loads.
 struct DTile {
   long long q0;
-  int c0, gi;
+  int c0, gi, k0, k1;
 };
-__device__ __forceinline__ DTile dtile_of(int t, int mtiles, int ctiles) {
+__device__ __forceinline__ DTile dtile_of(int t, int mtiles, int ctiles, int ksplits, int kk) {
   DTile T;
-  const int mt = t % mtiles;
-  const int r = t / mtiles;
+  const int ks = t % ksplits;
+  int r = t / ksplits;
+  const int mt = r % mtiles;
+  r /= mtiles;
   T.q0 = (long long)mt * D_BM;
   T.c0 = (r % ctiles) * D_BN;
   T.gi = r / ctiles;
+  T.k0 = ks * kk / ksplits;
+  T.k1 = (ks + 1) * kk / ksplits;
   return T;
 }
 
@@ -251,7 +257,8 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
 //   warps 2-17  epilogue (epilogue_chunk)
 __global__ void __launch_bounds__(D_THREADS, 1)
 bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
-                   const __grid_constant__ CUtensorMap bmap, int mtiles, int ctiles, int ntiles,
+                   const __grid_constant__ CUtensorMap bmap, int mtiles, int ctiles, int ksplits,
+                   int ntiles,
                    const float* __restrict__ xt, const float* __restrict__ off,
                    const float* __restrict__ mask, float* __restrict__ gxt,
                    float* __restrict__ goff, float* __restrict__ gmask) {
@@ -293,8 +300,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     if (lane == 0) {
       int gs = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const DTile T = dtile_of(t, mtiles, ctiles);
-        for (int k = 0; k < g.kk; ++k) {
+        const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
+        for (int k = T.k0; k < T.k1; ++k) {
           const int brow = (T.gi * g.kk + k) * g.Cg + T.c0;
           for (int s = 0; s < ochunks; ++s, ++gs) {
             const int st = gs % D_STAGES;
@@ -314,7 +321,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
       const uint32_t idesc = tc::idesc_tf32(D_BM, D_BN);
       int gs = 0, gt = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        for (int k = 0; k < g.kk; ++k, ++gt) {
+        const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
+        for (int k = T.k0; k < T.k1; ++k, ++gt) {
           const int acc = gt & 1;
           if (gt >= 2) tc::mbar_wait(&acc_empty[acc], ((gt >> 1) - 1) & 1, &g_tc_bwd_status);
           tc::tc_fence_after();
@@ -342,10 +350,10 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     unsigned char* scratch = epi + e * EPI_WARP_BYTES;
     int gt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const DTile T = dtile_of(t, mtiles, ctiles);
+      const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
       const long long row_q = T.q0 + lq * 32 + lane;
       int plan_key = -1;
-      for (int k = 0; k < g.kk; ++k, ++gt) {
+      for (int k = T.k0; k < T.k1; ++k, ++gt) {
         const int acc = gt & 1;
         tc::mbar_wait(&acc_full[acc], (gt >> 1) & 1, &g_tc_bwd_status);
         tc::tc_fence_after();
@@ -375,6 +383,46 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   if (warp == D_MMA_WARP) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 2 * D_BN);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// sampling plans: one 32-byte record per (n, deformable group, tap, pixel):
+// the element offsets ((n*H*W + y*W + x) * C) of the four corners -- the zero
+// row for dropped corners -- and their bilinear weights times the mask.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) plan_kernel(Geom g, const float* __restrict__ off,
+                                                   const float* __restrict__ mask,
+                                                   int4* __restrict__ plans) {
+  const long long total = (long long)g.N * g.dg * g.kk * g.P;
+  const int zoff = g.N * g.HW * g.C;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(i % g.P);
+    long long r = i / g.P;
+    const int k = (int)(r % g.kk);
+    r /= g.kk;
+    const int dgi = (int)(r % g.dg);
+    const int n = (int)(r / g.dg);
+    const int oy = p / g.Wo, ox = p - oy * g.Wo;
+    const int ki = k / g.kw, kj = k - ki * g.kw;
+    const long long oi = off_h_index(g, n, dgi, k, p);
+    float h, w;
+    sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+    const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+    const Sample sp = make_sample(h, w, g.H, g.W);
+    int4 o = make_int4(zoff, zoff, zoff, zoff);
+    float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sp.valid) {
+      const int nb = n * g.HW;
+      if (sp.live & 1u) { o.x = (nb + sp.i1) * g.C; wv.x = sp.w1 * m; }
+      if (sp.live & 2u) { o.y = (nb + sp.i2) * g.C; wv.y = sp.w2 * m; }
+      if (sp.live & 4u) { o.z = (nb + sp.i3) * g.C; wv.z = sp.w3 * m; }
+      if (sp.live & 8u) { o.w = (nb + sp.i4) * g.C; wv.w = sp.w4 * m; }
+    }
+    plans[2 * i] = o;
+    plans[2 * i + 1] = make_int4(__float_as_int(wv.x), __float_as_int(wv.y),
+                                 __float_as_int(wv.z), __float_as_int(wv.w));
   }
 }
 
@@ -449,9 +497,9 @@ __device__ __forceinline__ WTile wtile_of(const Geom& g, int t, int mtiles, int 
 
 __global__ void __launch_bounds__(W2_THREADS, 1)
 bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
-                     const float* __restrict__ xt, const float* __restrict__ off,
-                     const float* __restrict__ mask, float* __restrict__ gw, int mtiles, int ntn,
-                     int splits, int per, int ntiles) {
+                     const float* __restrict__ xt, const int4* __restrict__ plans,
+                     float* __restrict__ gw, int mtiles, int ntn, int splits, int per,
+                     int ntiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
@@ -500,27 +548,28 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       if (T.t_begin >= T.t_end) continue;
       const int gch = T.gi * g.Cg + T.cm0 + mb * 32 + quad * 4;
       const int dgi = (T.gi * g.Cg + T.cm0 + mb * 32) / g.cpg;
-      const int ki = T.k / g.kw, kj = T.k - ki * g.kw;
       const float* xq = xt + gch;
       uint32_t soff[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) soff[i] = mb * W_LBO + mn32_offset(pg * 8 + i * 4 + sub, quad);
-      // The offsets / mask of the next K step are loaded one step ahead, so
-      // each step waits for one L2 round trip (its corners), not two.
+      // The sampling plans of the next K step are loaded one step ahead, so
+      // each step waits for one L2 round trip (its corners).
+      const int4* plan_k = plans + 2 * ((long long)dgi * g.kk + T.k) * g.P;  // + n*dg*kk*P
+      const long long plan_n_stride = 2LL * g.dg * g.kk * g.P;
       int n = T.t_begin / pchunks;
       int p0 = (T.t_begin - n * pchunks) << 5;
-      float nh[2], nw[2], nm[2];  // raw offset pair and mask of the next step's pixels
+      int4 npo[2], npw[2];
       auto fetch = [&](int fn, int fp0) {
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const int pp = fp0 + pg * 8 + i * 4 + sub;
-          nh[i] = nw[i] = 0.f;
-          nm[i] = 1.f;
           if (pp < g.P && fn < g.N) {
-            const long long oi = off_h_index(g, fn, dgi, T.k, pp);
-            nh[i] = __ldg(off + oi);
-            nw[i] = __ldg(off + oi + g.P);
-            if (g.use_mask) nm[i] = __ldg(mask + mask_index(g, fn, dgi, T.k, pp));
+            const int4* rec = plan_k + fn * plan_n_stride + 2 * pp;
+            npo[i] = __ldg(rec);
+            npw[i] = __ldg(rec + 1);
+          } else {
+            npo[i] = make_int4(zoff, zoff, zoff, zoff);
+            npw[i] = make_int4(0, 0, 0, 0);
           }
         }
       };
@@ -528,35 +577,16 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
         const int st = gs & (W2_STAGES - 1);
         const int u = gs / W2_STAGES;
-        const float ch[2] = {nh[0], nh[1]}, cwo[2] = {nw[0], nw[1]}, cm[2] = {nm[0], nm[1]};
-        const int cn = n, cp0 = p0;
+        const int coff[2][4] = {{npo[0].x, npo[0].y, npo[0].z, npo[0].w},
+                                {npo[1].x, npo[1].y, npo[1].z, npo[1].w}};
+        const float cw[2][4] = {{__int_as_float(npw[0].x), __int_as_float(npw[0].y),
+                                 __int_as_float(npw[0].z), __int_as_float(npw[0].w)},
+                                {__int_as_float(npw[1].x), __int_as_float(npw[1].y),
+                                 __int_as_float(npw[1].z), __int_as_float(npw[1].w)}};
         p0 += 32;
         if (p0 >= g.P) {
           p0 = 0;
           ++n;
-        }
-        int coff[2][4];
-        float cw[2][4];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            coff[i][c] = zoff;
-            cw[i][c] = 0.f;
-          }
-          const int pp = cp0 + pg * 8 + i * 4 + sub;
-          if (pp >= g.P) continue;
-          const int oy = pp / g.Wo, ox = pp - oy * g.Wo;
-          float h, w;
-          sample_pos(g, oy, ox, ki, kj, ch[i], cwo[i], h, w);
-          const float m = cm[i];
-          const Sample sp = make_sample(h, w, g.H, g.W);
-          if (!sp.valid) continue;
-          const int xn = cn * g.HW;
-          if (sp.live & 1u) { coff[i][0] = (xn + sp.i1) * g.C; cw[i][0] = sp.w1 * m; }
-          if (sp.live & 2u) { coff[i][1] = (xn + sp.i2) * g.C; cw[i][1] = sp.w2 * m; }
-          if (sp.live & 4u) { coff[i][2] = (xn + sp.i3) * g.C; cw[i][2] = sp.w3 * m; }
-          if (sp.live & 8u) { coff[i][3] = (xn + sp.i4) * g.C; cw[i][3] = sp.w4 * m; }
         }
         float4 v[2][4];
 #pragma unroll
@@ -687,7 +717,7 @@ int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
 bool tc_bwd_supported(const Geom& g) {
   return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
          (g.Og <= 256 || g.Og % 256 == 0) && g.Cg % W_BM == 0 && g.NP > 0 &&
-         (long long)g.N * g.HW < (1LL << 31) &&
+         (long long)g.N * g.HW * g.C + g.C < (1LL << 31) &&
          (long long)g.N * 2 * g.dg * g.kk * g.P < (1LL << 31);
 }
 
@@ -735,17 +765,39 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wb
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int mtiles = (int)((g.NP + D_BM - 1) / D_BM);
   const int ctiles = g.Cg / D_BN;
-  const long long ntiles = (long long)mtiles * ctiles * g.G;
+  const long long base = (long long)mtiles * ctiles * g.G;
+  // split the taps so the busiest CTA carries the fewest taps
+  int ksplits = 1;
+  long long best = -1;
+  for (int ks = 1; ks <= g.kk; ++ks) {
+    const long long rounds = (base * ks + sms - 1) / sms;
+    const long long cost = rounds * ((g.kk + ks - 1) / ks);
+    if (best < 0 || cost < best) {
+      best = cost;
+      ksplits = ks;
+    }
+  }
+  const long long ntiles = base * ksplits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < sms ? ntiles : sms);
-  bwd_data_tc_kernel<<<grid, D_THREADS, smem, stream>>>(g, amap, bmap, mtiles, ctiles,
+  bwd_data_tc_kernel<<<grid, D_THREADS, smem, stream>>>(g, amap, bmap, mtiles, ctiles, ksplits,
                                                          (int)ntiles, xt, off, mask, gxt, goff,
                                                          gmask);
   return cudaGetLastError();
 }
 
+cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, void* plans,
+                            cudaStream_t stream) {
+  const long long total = (long long)g.N * g.dg * g.kk * g.P;
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  plan_kernel<<<(int)blocks, 256, 0, stream>>>(g, off, mask, static_cast<int4*>(plans));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const float* off, const float* mask, float* gw, int num_sms,
+                                 const void* plans, float* gw, int num_sms,
                                  cudaStream_t stream) {
   const int bn = weight_bn(g);
   const int Ppad = (g.P + 3) & ~3;
@@ -762,17 +814,25 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   const long long base = (long long)g.kk * mtiles * ntn * g.G;
   const int pchunks = (g.P + 31) / 32;
   const int total_chunks = g.N * pchunks;
-  long long splits = (2LL * num_sms + base - 1) / base;
-  const long long max_splits = (total_chunks + 7) / 8;  // >= 8 K steps per tile
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
+  // pixel-range splits: pick the count that minimises the busiest CTA's K
+  // steps (rounds of tiles x chunks per tile), with >= 8 K steps per tile
+  const long long max_splits = (total_chunks + 7) / 8 > 0 ? (total_chunks + 7) / 8 : 1;
+  long long splits = 1, best = -1;
+  for (long long sp = 1; sp <= max_splits && sp * base <= 64LL * num_sms; ++sp) {
+    const long long rounds = (base * sp + num_sms - 1) / num_sms;
+    const long long cost = rounds * ((total_chunks + sp - 1) / sp);
+    if (best < 0 || cost < best) {
+      best = cost;
+      splits = sp;
+    }
+  }
   const int per = (int)((total_chunks + splits - 1) / splits);
   const long long ntiles = base * splits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  bwd_weight_tc_kernel<<<grid, W2_THREADS, smem, stream>>>(g, gomap, bn, pow2_cols(2 * bn), xt,
-                                                          off, mask, gw, mtiles, ntn,
-                                                          (int)splits, per, (int)ntiles);
+  bwd_weight_tc_kernel<<<grid, W2_THREADS, smem, stream>>>(
+      g, gomap, bn, pow2_cols(2 * bn), xt, static_cast<const int4*>(plans), gw, mtiles, ntn,
+      (int)splits, per, (int)ntiles);
   return cudaGetLastError();
 }
 

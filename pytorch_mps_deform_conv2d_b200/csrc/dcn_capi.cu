@@ -214,6 +214,7 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     b += align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
     b += align_up((size_t)g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));  // go_r
     b += align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));       // packed weight
+    b += align_up(dcn::tc_plan_bytes(g));                              // sampling plans
   } else {
     b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
   }
@@ -376,14 +377,15 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     float* go_t = ws.take((size_t)g.N * g.outC * g.P);
     float* go_r = ws.take((size_t)g.N * g.outC * ((g.P + 3) & ~3));
     float* wbt = ws.take((size_t)g.outC * g.Cg * g.kk);
+    void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
     DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_r, nullptr, stream), "tc_prep_go");
     DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, stream), "tc_pack_weight_bwd");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, wbt, xt, offset, mask, gxt, grad_offset, grad_mask,
                                      stream),
              "bwd_data_tc");
     DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
-    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, offset, mask, grad_weight, num_sms_current(),
-                                       stream),
+    DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
+    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, num_sms_current(), stream),
              "bwd_weight_tc");
     return DCN_OK;
   }

@@ -39,9 +39,14 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
                                const float* xt, const float* off, const float* mask,
                                float* gxt, float* goff, float* gmask, cudaStream_t stream);
+// Sampling plans of every (n, deformable group, tap, pixel): 32 bytes each
+// (corner element offsets into the NHWC copy, weights times mask).
+inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }
+cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, void* plans,
+                            cudaStream_t stream);
 // grad_weight (pre-zeroed) += col^T go on the tensor core, split over pixels.
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const float* off, const float* mask, float* gw, int num_sms,
+                                 const void* plans, float* gw, int num_sms,
                                  cudaStream_t stream);
 
 }  // namespace dcn
