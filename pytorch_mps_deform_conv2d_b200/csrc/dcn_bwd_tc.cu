@@ -89,20 +89,20 @@ constexpr int D_STAGE = D_BM * 128 + D_BN * 128;             // A + B = 32 KB
 
 // Sampling plan of one pixel for one (tap, deformable group), kept in shared
 // memory so that the 8 lanes working on the pixel can read it.
-struct PixPlan {
-  int cidx[4];     // element offset (n*H*W + y*W + x) * C of each corner; the
+// Four 16-byte words, read with vector loads.
+struct __align__(16) PixPlan {
+  int4 cidx;       // element offset (n*H*W + y*W + x) * C of each corner; the
                    // zero row for dropped corners
-  float w[4];      // bilinear weights (0 for dropped corners)
-  float lh, lw;    // fractional position
-  float msk;       // modulation scalar
-  int oi;          // offset-gradient index of (n, dgi, k, p); -1: pixel or sample void
-  int mi;          // mask-gradient index
-  int pad_;
+  float4 w;        // bilinear weights (0 for dropped corners)
+  float4 geo;      // lh, lw (fractional position), msk (modulation), unused
+  int4 idx;        // offset-gradient index of (n, dgi, k, p) (-1: pixel or
+                   // sample void), mask-gradient index, unused x2
 };
-static_assert(sizeof(PixPlan) == 56, "PixPlan is 14 words");
+static_assert(sizeof(PixPlan) == 64, "PixPlan is 4 x 16 bytes");
 
 constexpr int EPI_TSTRIDE = 33;  // transpose buffer row stride (floats)
-constexpr int EPI_WARP_BYTES = 32 * EPI_TSTRIDE * 4 + 32 * (int)sizeof(PixPlan);  // 6016
+constexpr int EPI_T_BYTES = 32 * EPI_TSTRIDE * 4 + 128;  // 4352: keeps the plans 16-byte aligned
+constexpr int EPI_WARP_BYTES = EPI_T_BYTES + 32 * (int)sizeof(PixPlan);  // 6400
 
 size_t data_smem_bytes() {
   return (size_t)D_STAGES * D_STAGE + (size_t)D_EPI_WARPS * EPI_WARP_BYTES + 128 + 1024;
@@ -143,7 +143,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
                                                float* __restrict__ gxt, float* __restrict__ goff,
                                                float* __restrict__ gmask, int& plan_key) {
   float* T = reinterpret_cast<float*>(scratch);
-  PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + 32 * EPI_TSTRIDE * 4);
+  PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + EPI_T_BYTES);
   const int quad = lane & 7, sub = lane >> 3;
   const int zoff = g.N * g.HW * g.C;
   const int dgi = gch0 / g.cpg;
@@ -151,17 +151,10 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
   __syncwarp();
   if (key != plan_key) {
     plan_key = key;
-    PixPlan pl;
-    pl.oi = -1;
-    pl.mi = 0;
-    pl.pad_ = 0;
-    pl.lh = pl.lw = 0.f;
-    pl.msk = 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      pl.cidx[c] = zoff;
-      pl.w[c] = 0.f;
-    }
+    int4 cidx = make_int4(zoff, zoff, zoff, zoff);
+    float4 wv4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 geo = make_float4(0.f, 0.f, 0.f, 0.f);
+    int4 idx = make_int4(-1, 0, 0, 0);
     if (row_q < g.NP) {
       const int n = (int)(row_q / g.P);
       const int p = (int)(row_q - (long long)n * g.P);
@@ -173,20 +166,23 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
       const Sample sp = make_sample(h, w, g.H, g.W);
       if (sp.valid) {
         const int nb = n * g.HW;
-        const int ci[4] = {sp.i1, sp.i2, sp.i3, sp.i4};
-        const float wv[4] = {sp.w1, sp.w2, sp.w3, sp.w4};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          pl.cidx[c] = ((sp.live >> c) & 1u) ? (nb + ci[c]) * g.C : zoff;
-          pl.w[c] = wv[c];
-        }
-        pl.lh = sp.lh;
-        pl.lw = sp.lw;
-        pl.msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
-        pl.oi = (int)oi;
-        pl.mi = (int)mask_index(g, n, dgi, k, p);
+        cidx.x = (sp.live & 1u) ? (nb + sp.i1) * g.C : zoff;
+        cidx.y = (sp.live & 2u) ? (nb + sp.i2) * g.C : zoff;
+        cidx.z = (sp.live & 4u) ? (nb + sp.i3) * g.C : zoff;
+        cidx.w = (sp.live & 8u) ? (nb + sp.i4) * g.C : zoff;
+        wv4 = make_float4(sp.w1, sp.w2, sp.w3, sp.w4);
+        geo.x = sp.lh;
+        geo.y = sp.lw;
+        geo.z = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+        idx.x = (int)oi;
+        idx.y = (int)mask_index(g, n, dgi, k, p);
       }
     }
+    PixPlan pl;
+    pl.cidx = cidx;
+    pl.w = wv4;
+    pl.geo = geo;
+    pl.idx = idx;
     plan[lane] = pl;
   }
 #pragma unroll
@@ -197,36 +193,42 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
 #pragma unroll 2
   for (int i = 0; i < 8; ++i) {
     const int px = i * 4 + sub;
-    const PixPlan& pl = plan[px];
+    const int4 pc = plan[px].cidx;
+    const int4 pidx = plan[px].idx;
     float s_h = 0.f, s_w = 0.f, s_m = 0.f;
-    if (pl.oi >= 0) {
+    if (pidx.x >= 0) {
+      const float4 pw = plan[px].w;
+      const float4 geo = plan[px].geo;
       const float gc0 = T[px * EPI_TSTRIDE + quad * 4 + 0];
       const float gc1 = T[px * EPI_TSTRIDE + quad * 4 + 1];
       const float gc2 = T[px * EPI_TSTRIDE + quad * 4 + 2];
       const float gc3 = T[px * EPI_TSTRIDE + quad * 4 + 3];
-      float4 v[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) v[c] = ldg4(xq + (unsigned)pl.cidx[c]);  // dropped: zero row
+      const float4 v0 = ldg4(xq + (unsigned)pc.x);  // dropped corners: zero row
+      const float4 v1 = ldg4(xq + (unsigned)pc.y);
+      const float4 v2 = ldg4(xq + (unsigned)pc.z);
+      const float4 v3 = ldg4(xq + (unsigned)pc.w);
       Sample sp;
-      sp.w1 = pl.w[0]; sp.w2 = pl.w[1]; sp.w3 = pl.w[2]; sp.w4 = pl.w[3];
-      sp.lh = pl.lh; sp.lw = pl.lw;
-      const float m = pl.msk;
+      sp.w1 = pw.x; sp.w2 = pw.y; sp.w3 = pw.z; sp.w4 = pw.w;
+      sp.lh = geo.x; sp.lw = geo.y;
+      const float m = geo.z;
       const float gcs[4] = {gc0, gc1, gc2, gc3};
-      const float a[4] = {v[0].x, v[0].y, v[0].z, v[0].w};
-      const float b[4] = {v[1].x, v[1].y, v[1].z, v[1].w};
-      const float c[4] = {v[2].x, v[2].y, v[2].z, v[2].w};
-      const float d[4] = {v[3].x, v[3].y, v[3].z, v[3].w};
+      const float a[4] = {v0.x, v0.y, v0.z, v0.w};
+      const float b[4] = {v1.x, v1.y, v1.z, v1.w};
+      const float c[4] = {v2.x, v2.y, v2.z, v2.w};
+      const float d[4] = {v3.x, v3.y, v3.z, v3.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
         s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
         s_m += gcs[e] * bilerp(sp, a[e], b[e], c[e], d[e]);
       }
+      const int cis[4] = {pc.x, pc.y, pc.z, pc.w};
+      const float wss[4] = {pw.x, pw.y, pw.z, pw.w};
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
-        if (pl.cidx[cc] == zoff) continue;
-        const float wc = pl.w[cc] * m;
-        red_add_v4(gq + (unsigned)pl.cidx[cc], wc * gc0, wc * gc1, wc * gc2, wc * gc3);
+        if (cis[cc] == zoff) continue;
+        const float wc = wss[cc] * m;
+        red_add_v4(gq + (unsigned)cis[cc], wc * gc0, wc * gc1, wc * gc2, wc * gc3);
       }
     }
     // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
@@ -239,10 +241,10 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
     s_h += __shfl_xor_sync(0xffffffffu, s_h, 4);
     s_w += __shfl_xor_sync(0xffffffffu, s_w, 4);
     s_m += __shfl_xor_sync(0xffffffffu, s_m, 4);
-    if (quad == 0 && pl.oi >= 0) {
-      red_add_f32(goff + pl.oi, s_h);
-      red_add_f32(goff + pl.oi + g.P, s_w);
-      if (g.use_mask) red_add_f32(gmask + pl.mi, s_m);
+    if (quad == 0 && pidx.x >= 0) {
+      red_add_f32(goff + pidx.x, s_h);
+      red_add_f32(goff + pidx.x + g.P, s_w);
+      if (g.use_mask) red_add_f32(gmask + pidx.y, s_m);
     }
   }
 }
