@@ -62,10 +62,14 @@ extern "C" {
  *   DCN_MATH_FP32  fp32 FFMA on the CUDA cores (strict parity mode);
  *   DCN_MATH_TF32  tcgen05 tensor cores with TF32 operands and fp32
  *                  accumulation where a tensor-core kernel covers the shape,
- *                  fp32 FFMA elsewhere.
+ *                  fp32 FFMA elsewhere;
+ *   DCN_MATH_3XTF32  the same tensor-core kernels with every operand split
+ *                  into high and low TF32 parts (hi*hi + hi*lo + lo*hi):
+ *                  close to fp32 accuracy at tensor-core speed.
  * The second byte can pin a kernel family (test use; 0 = automatic). */
 #define DCN_MATH_FP32 0x0
 #define DCN_MATH_TF32 0x1
+#define DCN_MATH_3XTF32 0x2
 #define DCN_ALGO_SIMT_GEMM 0x100
 #define DCN_ALGO_SIMT_DIRECT 0x200
 

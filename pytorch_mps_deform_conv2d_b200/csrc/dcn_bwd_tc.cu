@@ -41,11 +41,15 @@ int pow2_cols(int n) {
 // ---------------------------------------------------------------------------
 // Also accumulates grad_bias (pre-zeroed; NULL when not wanted) from the
 // unrounded values: each block adds its 32 x 32 tile's per-channel sums.
+// With `go_t_lo` (3xTF32), the low TF32 parts go to go_t_lo and to the rows
+// N*outC .. 2*N*outC-1 of go_r.
 __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
                                                       float* __restrict__ go_t,
+                                                      float* __restrict__ go_t_lo,
                                                       float* __restrict__ go_r,
-                                                      float* __restrict__ gb, int outC,
+                                                      float* __restrict__ gb, int N, int outC,
                                                       int P, int Ppad) {
+  __shared__ float tile_lo[32][33];
   __shared__ float tile[32][33];
   const int n = blockIdx.z;
   const int o0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
@@ -60,6 +64,11 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
       const float v = tc::to_tf32(raw);
       tile[ty + i][tx] = v;
       go_r[((long long)n * outC + o) * Ppad + p] = v;
+      if (go_t_lo) {
+        const float lo = tc::to_tf32(raw - v);
+        tile_lo[ty + i][tx] = lo;
+        go_r[((long long)(N + n) * outC + o) * Ppad + p] = lo;
+      }
     }
     if (gb) {
       float sum = raw;
@@ -72,7 +81,10 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
     const int p = p0 + ty + i, o = o0 + tx;
-    if (o < outC && p < P) go_t[((long long)n * P + p) * outC + o] = tile[tx][ty + i];
+    if (o < outC && p < P) {
+      go_t[((long long)n * P + p) * outC + o] = tile[tx][ty + i];
+      if (go_t_lo) go_t_lo[((long long)n * P + p) * outC + o] = tile_lo[tx][ty + i];
+    }
   }
 }
 
@@ -81,11 +93,17 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
 // ---------------------------------------------------------------------------
 constexpr int D_BM = 128;
 constexpr int D_BN = 128;          // channels of one tap per tile
-constexpr int D_STAGES = 3;
-constexpr int D_EPI_WARPS = 16;    // 4 per tensor-memory lane quarter, 32 channels each
 constexpr int D_TMA_WARP = 0, D_MMA_WARP = 1, D_EPI_WARP0 = 2;
-constexpr int D_THREADS = (D_EPI_WARP0 + D_EPI_WARPS) * 32;  // 576
 constexpr int D_STAGE = D_BM * 128 + D_BN * 128;             // A + B = 32 KB
+// TF32: 3 stages, 16 epilogue warps (4 per tensor-memory lane quarter, 32
+// channels each).  3xTF32: the stages carry high and low parts (64 KB), 2
+// stages, 8 epilogue warps of 64 channels, to fit shared memory.
+template <bool SPLIT> struct DCfg {
+  static constexpr int STAGES = SPLIT ? 2 : 3;
+  static constexpr int PARTS = SPLIT ? 2 : 1;
+  static constexpr int EPI_WARPS = SPLIT ? 8 : 16;
+  static constexpr int THREADS = (D_EPI_WARP0 + EPI_WARPS) * 32;
+};
 
 // Sampling plan of one pixel for one (tap, deformable group), kept in shared
 // memory so that the 8 lanes working on the pixel can read it.
@@ -104,8 +122,11 @@ constexpr int EPI_TSTRIDE = 33;  // transpose buffer row stride (floats)
 constexpr int EPI_T_BYTES = 32 * EPI_TSTRIDE * 4 + 128;  // 4352: keeps the plans 16-byte aligned
 constexpr int EPI_WARP_BYTES = EPI_T_BYTES + 32 * (int)sizeof(PixPlan);  // 6400
 
-size_t data_smem_bytes() {
-  return (size_t)D_STAGES * D_STAGE + (size_t)D_EPI_WARPS * EPI_WARP_BYTES + 128 + 1024;
+size_t data_smem_bytes(bool split) {
+  const int stages = split ? DCfg<true>::STAGES : DCfg<false>::STAGES;
+  const int parts = split ? 2 : 1;
+  const int epi = split ? DCfg<true>::EPI_WARPS : DCfg<false>::EPI_WARPS;
+  return (size_t)stages * parts * D_STAGE + (size_t)epi * EPI_WARP_BYTES + 128 + 1024;
 }
 
 // A tile is (128 pixels, 128 channels, group, range of taps); the taps are
@@ -257,8 +278,10 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
 //               packed weight rows (128 channels x 32 out channels) per K step
 //   warp 1      MMA issue: 4 UMMAs 128 x 128 x 8 per K step
 //   warps 2-17  epilogue (epilogue_chunk)
-__global__ void __launch_bounds__(D_THREADS, 1)
+template <bool SPLIT>
+__global__ void __launch_bounds__(DCfg<SPLIT>::THREADS, 1)
 bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
+                   const __grid_constant__ CUtensorMap amap_lo,
                    const __grid_constant__ CUtensorMap bmap, int mtiles, int ctiles, int ksplits,
                    int ntiles,
                    const float* __restrict__ xt, const float* __restrict__ off,
@@ -267,8 +290,12 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  constexpr int D_STAGES = DCfg<SPLIT>::STAGES;
+  constexpr int PARTS = DCfg<SPLIT>::PARTS;
+  constexpr int D_EPI_WARPS = DCfg<SPLIT>::EPI_WARPS;
+  constexpr int SSTAGE = PARTS * D_STAGE;  // [A_hi B_hi] ([A_lo B_lo])
   const uint32_t s0 = tc::smem_u32(smem);
-  unsigned char* epi = smem + D_STAGES * D_STAGE;
+  unsigned char* epi = smem + D_STAGES * SSTAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(epi + D_EPI_WARPS * EPI_WARP_BYTES);
   uint64_t* empty = full + D_STAGES;
   uint64_t* acc_full = empty + D_STAGES;
@@ -309,10 +336,15 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             const int st = gs % D_STAGES;
             const int u = gs / D_STAGES;
             if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
-            tc::mbar_arrive_expect_tx(&full[st], D_STAGE);
-            const uint32_t sA = s0 + st * D_STAGE;
+            tc::mbar_arrive_expect_tx(&full[st], SSTAGE);
+            const uint32_t sA = s0 + st * SSTAGE;
             tc::tma_load_2d(sA, &amap, T.gi * g.Og + s * 32, (int)T.q0, &full[st]);
             tc::tma_load_2d(sA + D_BM * 128, &bmap, s * 32, brow, &full[st]);
+            if constexpr (SPLIT) {  // low parts
+              tc::tma_load_2d(sA + D_STAGE, &amap_lo, T.gi * g.Og + s * 32, (int)T.q0, &full[st]);
+              tc::tma_load_2d(sA + D_STAGE + D_BM * 128, &bmap, s * 32, g.G * g.kk * g.Cg + brow,
+                              &full[st]);
+            }
           }
         }
       }
@@ -333,11 +365,21 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             const int st = gs % D_STAGES;
             tc::mbar_wait(&full[st], (gs / D_STAGES) & 1, &g_tc_bwd_status);
             tc::tc_fence_after();
-            const uint32_t sA = s0 + st * D_STAGE, sB = sA + D_BM * 128;
+            const uint32_t sA = s0 + st * SSTAGE, sB = sA + D_BM * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
-                            (s | j) != 0 ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) {
+              if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
+                tc::umma_tf32(d, tc::sdesc_sw128(sA + D_STAGE + j * 32),
+                              tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32),
+                              tc::sdesc_sw128(sB + D_STAGE + j * 32), idesc, 1u);
+                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32),
+                              idesc, 1u);
+              } else {
+                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32),
+                              idesc, (s | j) != 0 ? 1u : 0u);
+              }
+            }
             tc::umma_commit(&empty[st]);
           }
           tc::umma_commit(&acc_full[acc]);
@@ -348,7 +390,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   } else {
     const int e = warp - D_EPI_WARP0;
     const int lq = warp & 3;      // tensor-memory lane quarter this warp may read
-    const int chunk = e >> 2;     // 32-channel chunk of the tile
+    constexpr int CPW = 16 / D_EPI_WARPS;  // 32-channel chunks per warp
     unsigned char* scratch = epi + e * EPI_WARP_BYTES;
     int gt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -359,23 +401,30 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
         const int acc = gt & 1;
         tc::mbar_wait(&acc_full[acc], (gt >> 1) & 1, &g_tc_bwd_status);
         tc::tc_fence_after();
-        float vals[32];
-        {
-          const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(acc * D_BN + chunk * 32);
+#pragma unroll 1
+        for (int cc = 0; cc < CPW; ++cc) {
+          const int chunk = (e >> 2) * CPW + cc;  // 32-channel chunk of the tile
+          float vals[32];
+          {
+            const uint32_t ta =
+                tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(acc * D_BN + chunk * 32);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float tv[8];
-            tc::tmem_ld8(ta + 8 * j, tv);
+            for (int j = 0; j < 4; ++j) {
+              float tv[8];
+              tc::tmem_ld8(ta + 8 * j, tv);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) vals[8 * j + q] = tv[q];
+              for (int q = 0; q < 8; ++q) vals[8 * j + q] = tv[q];
+            }
+            tc::tmem_ld_wait();
           }
-          tc::tmem_ld_wait();
+          if (cc == CPW - 1) {
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for tap + 2
+          }
+          epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, lane, scratch, xt,
+                         off, mask, gxt, goff, gmask, plan_key);
         }
-        tc::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for tap + 2
-        epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, lane, scratch, xt, off,
-                       mask, gxt, goff, gmask, plan_key);
       }
     }
   }
@@ -466,14 +515,15 @@ __device__ __forceinline__ uint32_t mn32_offset(int pix, int quad) {
 //   warps 6-21  16 gather warps: 32 channels x 8 pixels each; the column
 //               values are written MN-major (channels contiguous).
 // Stage ring and accumulator double buffering as in the forward kernel.
-constexpr int W2_STAGES = 4;
 constexpr int W2_GATHER_WARPS = 16;
 constexpr int W2_MMA_WARP = 4, W2_TMA_WARP = 5, W2_GATHER_WARP0 = 6;
 constexpr int W2_THREADS = (W2_GATHER_WARP0 + W2_GATHER_WARPS) * 32;  // 704
 constexpr int W2_A_STAGE = 16384;
 
-size_t weight_smem_bytes(int bn) {
-  return (size_t)W2_STAGES * W2_A_STAGE + (size_t)W2_STAGES * bn * 128 + 128 + 1024;
+// 3xTF32 carries high and low parts: 2 stages of twice the size.
+size_t weight_smem_bytes(int bn, bool split) {
+  const int stages = split ? 2 : 4, parts = split ? 2 : 1;
+  return (size_t)stages * parts * (W2_A_STAGE + (size_t)bn * 128) + 128 + 1024;
 }
 
 struct WTile {
@@ -497,6 +547,7 @@ __device__ __forceinline__ WTile wtile_of(const Geom& g, int t, int mtiles, int 
   return T;
 }
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(W2_THREADS, 1)
 bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
                      const float* __restrict__ xt, const int4* __restrict__ plans,
@@ -505,10 +556,13 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  constexpr int W2_STAGES = SPLIT ? 2 : 4;
+  constexpr int PARTS = SPLIT ? 2 : 1;
   const uint32_t sA0 = tc::smem_u32(smem);
   const uint32_t b_stage = (uint32_t)bn * 128;
-  const uint32_t sB0 = sA0 + W2_STAGES * W2_A_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + W2_STAGES * W2_A_STAGE + W2_STAGES * b_stage);
+  const uint32_t sB0 = sA0 + W2_STAGES * PARTS * W2_A_STAGE;
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + W2_STAGES * PARTS * (W2_A_STAGE + b_stage));
   uint64_t* empty = full + W2_STAGES;
   uint64_t* acc_full = empty + W2_STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -577,7 +631,7 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       };
       fetch(n, p0);
       for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
-        const int st = gs & (W2_STAGES - 1);
+        const int st = gs % W2_STAGES;
         const int u = gs / W2_STAGES;
         const int coff[2][4] = {{npo[0].x, npo[0].y, npo[0].z, npo[0].w},
                                 {npo[1].x, npo[1].y, npo[1].z, npo[1].w}};
@@ -598,15 +652,21 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
             v[i][c] = ldg4(xq + (unsigned)coff[i][c]);  // dropped corners: zero row
         if (tt + 1 < T.t_end) fetch(n, p0);
         if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
-        const uint32_t sA = sA0 + st * W2_A_STAGE;
+        const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
           const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
-          tc::st_shared_v4(sA + soff[i], tc::to_tf32(a * A.x + b * B.x + c * C.x + d * D.x),
-                           tc::to_tf32(a * A.y + b * B.y + c * C.y + d * D.y),
-                           tc::to_tf32(a * A.z + b * B.z + c * C.z + d * D.z),
-                           tc::to_tf32(a * A.w + b * B.w + c * C.w + d * D.w));
+          const float e0 = a * A.x + b * B.x + c * C.x + d * D.x;
+          const float e1 = a * A.y + b * B.y + c * C.y + d * D.y;
+          const float e2 = a * A.z + b * B.z + c * C.z + d * D.z;
+          const float e3 = a * A.w + b * B.w + c * C.w + d * D.w;
+          const float h0 = tc::to_tf32(e0), h1 = tc::to_tf32(e1), h2 = tc::to_tf32(e2),
+                      h3 = tc::to_tf32(e3);
+          tc::st_shared_v4(sA + soff[i], h0, h1, h2, h3);
+          if constexpr (SPLIT)
+            tc::st_shared_v4(sA + W2_A_STAGE + soff[i], tc::to_tf32(e0 - h0), tc::to_tf32(e1 - h1),
+                             tc::to_tf32(e2 - h2), tc::to_tf32(e3 - h3));
         }
         tc::fence_proxy_async();
         __syncwarp();
@@ -620,14 +680,17 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
-          const int st = gs & (W2_STAGES - 1);
+          const int st = gs % W2_STAGES;
           const int u = gs / W2_STAGES;
           const int n = tt / pchunks;
           const int p0 = (tt - n * pchunks) << 5;
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
-          tc::mbar_arrive_expect_tx(&full[st], b_stage);
-          tc::tma_load_2d(sB0 + st * b_stage, &gomap, p0, n * g.outC + T.gi * g.Og + T.o0,
-                          &full[st]);
+          tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
+          const int row = n * g.outC + T.gi * g.Og + T.o0;
+          const uint32_t sB = sB0 + st * PARTS * b_stage;
+          tc::tma_load_2d(sB, &gomap, p0, row, &full[st]);
+          if constexpr (SPLIT)  // low parts: rows N*outC .. of go_r
+            tc::tma_load_2d(sB + b_stage, &gomap, p0, g.N * g.outC + row, &full[st]);
         }
       }
     }
@@ -645,15 +708,25 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
         tc::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * bn);
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
-          const int st = gs & (W2_STAGES - 1);
+          const int st = gs % W2_STAGES;
           const int s = tt - T.t_begin;
           tc::mbar_wait(&full[st], (gs / W2_STAGES) & 1, &g_tc_bwd_status);
           tc::tc_fence_after();
-          const uint32_t sA = sA0 + st * W2_A_STAGE, sB = sB0 + st * b_stage;
+          const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
-                          idesc, (s | j) != 0 ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + W2_A_STAGE + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + b_stage + j * 32), idesc, 1u);
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, 1u);
+            } else {
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+            }
+          }
           tc::umma_commit(&empty[st]);
         }
         tc::umma_commit(&acc_full[acc]);
@@ -696,9 +769,10 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
   }
 }
 
-// wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels)
+// wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels);
+// with `split`, the low parts follow in rows G*kk*Cg ..
 __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __restrict__ wb,
-                                          Geom g) {
+                                          Geom g, int split) {
   const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -708,7 +782,10 @@ __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __
     t /= g.Cg;
     const int k = (int)(t % g.kk);
     const int gi = (int)(t / g.kk);
-    wb[i] = tc::to_tf32(w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k]);
+    const float v = w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k];
+    const float hi = tc::to_tf32(v);
+    wb[i] = hi;
+    if (split) wb[total + i] = tc::to_tf32(v - hi);
   }
 }
 
@@ -729,38 +806,45 @@ size_t tc_bwd_scratch_bytes(const Geom& g) {
          (size_t)g.outC * g.Cg * g.kk * sizeof(float);
 }
 
-cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
-                              float* gb, cudaStream_t stream) {
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
+                              float* go_r, float* gb, cudaStream_t stream) {
   if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
   const int Ppad = (g.P + 3) & ~3;
   dim3 grid((Ppad + 31) / 32, (g.outC + 31) / 32, g.N);
-  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_r, gb, g.outC, g.P, Ppad);
+  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_t_lo, go_r, gb, g.N, g.outC, g.P,
+                                                   Ppad);
   return cudaGetLastError();
 }
 
-cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
+cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g, bool split,
                                       cudaStream_t stream) {
   const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
   if (total == 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  tc_pack_weight_bwd_kernel<<<(int)blocks, 256, 0, stream>>>(w, wbt, g);
+  tc_pack_weight_bwd_kernel<<<(int)blocks, 256, 0, stream>>>(w, wbt, g, split ? 1 : 0);
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
-                               const float* xt, const float* off, const float* mask,
-                               float* gxt, float* goff, float* gmask, cudaStream_t stream) {
-  CUtensorMap amap, bmap;
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
+                               const float* wbt, const float* xt, const float* off,
+                               const float* mask, float* gxt, float* goff, float* gmask,
+                               cudaStream_t stream) {
+  const bool split = go_t_lo != nullptr;
+  CUtensorMap amap, amap_lo, bmap;
   cudaError_t e = make_tmap_2d_f32(&amap, go_t, (uint64_t)g.outC, (uint64_t)g.NP,
                                    (uint64_t)g.outC, (uint32_t)D_BM);
   if (e != cudaSuccess) return e;
-  e = make_tmap_2d_f32(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg, (uint64_t)g.Og,
-                       (uint32_t)D_BN);
+  e = make_tmap_2d_f32(&amap_lo, split ? go_t_lo : go_t, (uint64_t)g.outC, (uint64_t)g.NP,
+                       (uint64_t)g.outC, (uint32_t)D_BM);
   if (e != cudaSuccess) return e;
-  const size_t smem = data_smem_bytes();
-  e = cudaFuncSetAttribute(bwd_data_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
+  e = make_tmap_2d_f32(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg * (split ? 2 : 1),
+                       (uint64_t)g.Og, (uint32_t)D_BN);
+  if (e != cudaSuccess) return e;
+  const size_t smem = data_smem_bytes(split);
+  auto kern = split ? bwd_data_tc_kernel<true> : bwd_data_tc_kernel<false>;
+  const int threads = split ? DCfg<true>::THREADS : DCfg<false>::THREADS;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -782,9 +866,8 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wb
   const long long ntiles = base * ksplits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < sms ? ntiles : sms);
-  bwd_data_tc_kernel<<<grid, D_THREADS, smem, stream>>>(g, amap, bmap, mtiles, ctiles, ksplits,
-                                                         (int)ntiles, xt, off, mask, gxt, goff,
-                                                         gmask);
+  kern<<<grid, threads, smem, stream>>>(g, amap, amap_lo, bmap, mtiles, ctiles, ksplits,
+                                         (int)ntiles, xt, off, mask, gxt, goff, gmask);
   return cudaGetLastError();
 }
 
@@ -799,17 +882,18 @@ cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, 
 }
 
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const void* plans, float* gw, int num_sms,
+                                 const void* plans, float* gw, bool split, int num_sms,
                                  cudaStream_t stream) {
   const int bn = weight_bn(g);
   const int Ppad = (g.P + 3) & ~3;
   CUtensorMap gomap;
-  cudaError_t e = make_tmap_2d_f32(&gomap, go_r, (uint64_t)Ppad, (uint64_t)g.N * g.outC,
-                                   (uint64_t)Ppad, (uint32_t)bn);
+  cudaError_t e = make_tmap_2d_f32(&gomap, go_r, (uint64_t)Ppad,
+                                   (uint64_t)g.N * g.outC * (split ? 2 : 1), (uint64_t)Ppad,
+                                   (uint32_t)bn);
   if (e != cudaSuccess) return e;
-  const size_t smem = weight_smem_bytes(bn);
-  e = cudaFuncSetAttribute(bwd_weight_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
+  const size_t smem = weight_smem_bytes(bn, split);
+  auto kern = split ? bwd_weight_tc_kernel<true> : bwd_weight_tc_kernel<false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int mtiles = g.Cg / W_BM;
   const int ntn = g.Og / bn;
@@ -832,9 +916,9 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   const long long ntiles = base * splits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  bwd_weight_tc_kernel<<<grid, W2_THREADS, smem, stream>>>(
-      g, gomap, bn, pow2_cols(2 * bn), xt, static_cast<const int4*>(plans), gw, mtiles, ntn,
-      (int)splits, per, (int)ntiles);
+  kern<<<grid, W2_THREADS, smem, stream>>>(g, gomap, bn, pow2_cols(2 * bn), xt,
+                                            static_cast<const int4*>(plans), gw, mtiles, ntn,
+                                            (int)splits, per, (int)ntiles);
   return cudaGetLastError();
 }
 

@@ -175,10 +175,17 @@ int fwd_cpad(const dcn::Geom& g) { return dcn::ceil_div(g.Cg, 8) * 8; }
 
 enum class FwdAlgo { kDirect, kGemm, kTc };
 
+// TF32 and 3xTF32 run the tensor-core kernels; 3xTF32 splits every operand.
+bool tc_math(uint32_t flags) {
+  const uint32_t m = flags & 0xff;
+  return m == DCN_MATH_TF32 || m == DCN_MATH_3XTF32;
+}
+bool split_math(uint32_t flags) { return (flags & 0xff) == DCN_MATH_3XTF32; }
+
 FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
   if (flags & DCN_ALGO_SIMT_GEMM) return FwdAlgo::kGemm;
   if (flags & DCN_ALGO_SIMT_DIRECT) return dcn::fwd_direct_supported(g) ? FwdAlgo::kDirect : FwdAlgo::kGemm;
-  if ((flags & 0xff) == DCN_MATH_TF32 && dcn::tc_fwd_supported(g)) return FwdAlgo::kTc;
+  if (tc_math(flags) && dcn::tc_fwd_supported(g)) return FwdAlgo::kTc;
   if (dcn::fwd_direct_supported(g)) return FwdAlgo::kDirect;
   return FwdAlgo::kGemm;
 }
@@ -194,7 +201,7 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
       b += align_up((size_t)g.G * g.kk * fwd_cpad(g) * g.Og * sizeof(float));
       break;
     case FwdAlgo::kTc:
-      b += align_up(dcn::tc_fwd_weight_bytes(g));
+      b += align_up(dcn::tc_fwd_weight_bytes(g, split_math(flags)));
       break;
     case FwdAlgo::kDirect:
       break;
@@ -203,7 +210,7 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
 }
 
 bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
-  return (flags & 0xff) == DCN_MATH_TF32 && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
+  return tc_math(flags) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
          dcn::tc_bwd_supported(g);
 }
 
@@ -211,9 +218,10 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
   size_t b = align_up(xt_floats(g) * sizeof(float));                   // xt + zero row
   b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
   if (use_tc_bwd(g, flags)) {
-    b += align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
-    b += align_up((size_t)g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));  // go_r
-    b += align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));       // packed weight
+    const size_t parts = split_math(flags) ? 2 : 1;                   // high (+ low) TF32 parts
+    b += parts * align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
+    b += align_up(parts * g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));   // go_r
+    b += align_up(parts * g.outC * g.Cg * g.kk * sizeof(float));               // packed weight
     b += align_up(dcn::tc_plan_bytes(g));                              // sampling plans
   } else {
     b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
@@ -306,9 +314,11 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
       break;
     }
     case FwdAlgo::kTc: {
-      float* wt = ws.take(dcn::tc_fwd_weight_bytes(g) / sizeof(float));
-      DCN_CUDA(dcn::launch_tc_pack_weight(weight, wt, g, stream), "tc_pack_weight");
-      DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, num_sms_current(), stream),
+      const bool split = split_math(flags);
+      float* wt = ws.take(dcn::tc_fwd_weight_bytes(g, split) / sizeof(float));
+      DCN_CUDA(dcn::launch_tc_pack_weight(weight, wt, g, split, stream), "tc_pack_weight");
+      DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, num_sms_current(),
+                                  stream),
                "fwd_tc");
       break;
     }
@@ -374,18 +384,23 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
            "memset");
   if (tc_bwd) {
+    const bool split = split_math(flags);
+    const size_t parts = split ? 2 : 1;
     float* go_t = ws.take((size_t)g.N * g.outC * g.P);
-    float* go_r = ws.take((size_t)g.N * g.outC * ((g.P + 3) & ~3));
-    float* wbt = ws.take((size_t)g.outC * g.Cg * g.kk);
+    float* go_t_lo = split ? ws.take((size_t)g.N * g.outC * g.P) : nullptr;
+    float* go_r = ws.take(parts * g.N * g.outC * ((g.P + 3) & ~3));
+    float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
-    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_r, nullptr, stream), "tc_prep_go");
-    DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, stream), "tc_pack_weight_bwd");
-    DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, wbt, xt, offset, mask, gxt, grad_offset, grad_mask,
-                                     stream),
+    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r, nullptr, stream),
+             "tc_prep_go");
+    DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, stream), "tc_pack_weight_bwd");
+    DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,
+                                     grad_mask, stream),
              "bwd_data_tc");
     DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
     DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
-    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, num_sms_current(), stream),
+    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split, num_sms_current(),
+                                       stream),
              "bwd_weight_tc");
     return DCN_OK;
   }

@@ -24,6 +24,11 @@
 // columns in tensor memory (acc_full / acc_empty barriers) let the epilogue of
 // tile i run while tile i+1 is being accumulated.  Every wait is bounded.
 //
+// 3xTF32 (SPLIT): each operand is carried as a high TF32 part and a low TF32
+// part (x - hi); every K step issues lo.hi + hi.lo + hi.hi, which recovers
+// fp32-level products at three times the tensor work (2 stages of twice the
+// size instead of 4).
+//
 // The packed weight is rounded to TF32 with round-to-nearest; the gathered
 // column values are staged as fp32 and the tensor core uses their TF32 part
 // (the low 13 mantissa bits are ignored), a relative error below 2^-10 per
@@ -41,7 +46,6 @@ __device__ int g_tc_fwd_status;  // set to 1 by a wait that ran out
 namespace {
 
 constexpr int BM = 128;
-constexpr int STAGES = 4;
 constexpr int GATHER_WARPS = 16;
 constexpr int ROUNDS = 2;  // rows per lane: 16 warps x 2 rounds x 4 sub-rows = 128
 constexpr int EPI_WARPS = 4;
@@ -55,8 +59,13 @@ int tmem_cols_for(int bn) {
   while (c < 2 * bn) c <<= 1;
   return c;
 }
-size_t smem_bytes(int bn) {
-  return (size_t)STAGES * A_STAGE + (size_t)STAGES * bn * 128 + 128 + 1024;
+// 3xTF32 keeps a high and a low TF32 part of each operand: twice the stage
+// bytes, so half the stages.
+template <bool SPLIT>
+__host__ __device__ constexpr int stages_of() { return SPLIT ? 2 : 4; }
+size_t smem_bytes(int bn, bool split) {
+  const int parts = split ? 2 : 1, stages = split ? 2 : 4;
+  return (size_t)stages * parts * (A_STAGE + (size_t)bn * 128) + 128 + 1024;
 }
 
 struct Tile {
@@ -73,6 +82,7 @@ __device__ __forceinline__ Tile tile_of(int t, int mtiles, int ntiles_n, int bn)
   return T;
 }
 
+template <bool SPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
 fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __restrict__ xt,
               int bn, int tcols, int mtiles, int ntiles_n, int ntiles,
@@ -81,10 +91,12 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  constexpr int STAGES = stages_of<SPLIT>();
+  constexpr int PARTS = SPLIT ? 2 : 1;  // hi (+ lo) TF32 parts per operand
   const uint32_t sA0 = tc::smem_u32(smem);
   const uint32_t b_stage = (uint32_t)bn * 128;
-  const uint32_t sB0 = sA0 + STAGES * A_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * A_STAGE + STAGES * b_stage);
+  const uint32_t sB0 = sA0 + STAGES * PARTS * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * PARTS * (A_STAGE + b_stage));
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -149,7 +161,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
       int dgi = gbase / g.cpg, cpos = gbase - dgi * g.cpg;
       bool replan = true;
       for (int s = 0; s < steps; ++s, ++gs) {
-        const int st = gs & (STAGES - 1);
+        const int st = gs % STAGES;
         const int u = gs / STAGES;
         if (replan) {
           replan = false;
@@ -183,16 +195,25 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
           for (int c = 0; c < 4; ++c)
             v[i][c] = ldg4(xq + (unsigned)(coff[i][c] + gch0));
         if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
-        const uint32_t sA = sA0 + st * A_STAGE;
+        const uint32_t sA = sA0 + st * PARTS * A_STAGE;
 #pragma unroll
         for (int i = 0; i < ROUNDS; ++i) {
           const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
           const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
-          // stored as fp32; the tensor core reads the TF32 part of each value
-          tc::st_shared_v4(sA + soff[i], a * A.x + b * B.x + c * C.x + d * D.x,
-                           a * A.y + b * B.y + c * C.y + d * D.y,
-                           a * A.z + b * B.z + c * C.z + d * D.z,
-                           a * A.w + b * B.w + c * C.w + d * D.w);
+          const float e0 = a * A.x + b * B.x + c * C.x + d * D.x;
+          const float e1 = a * A.y + b * B.y + c * C.y + d * D.y;
+          const float e2 = a * A.z + b * B.z + c * C.z + d * D.z;
+          const float e3 = a * A.w + b * B.w + c * C.w + d * D.w;
+          if constexpr (SPLIT) {
+            const float h0 = tc::to_tf32(e0), h1 = tc::to_tf32(e1), h2 = tc::to_tf32(e2),
+                        h3 = tc::to_tf32(e3);
+            tc::st_shared_v4(sA + soff[i], h0, h1, h2, h3);
+            tc::st_shared_v4(sA + A_STAGE + soff[i], tc::to_tf32(e0 - h0), tc::to_tf32(e1 - h1),
+                             tc::to_tf32(e2 - h2), tc::to_tf32(e3 - h3));
+          } else {
+            // stored as fp32; the tensor core reads the TF32 part of each value
+            tc::st_shared_v4(sA + soff[i], e0, e1, e2, e3);
+          }
         }
         tc::fence_proxy_async();
         __syncwarp();
@@ -229,8 +250,11 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
           const int st = gs % STAGES;
           const int u = gs / STAGES;
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
-          tc::mbar_arrive_expect_tx(&full[st], b_stage);
-          tc::tma_load_2d(sB0 + st * b_stage, &wmap, s * 32, row, &full[st]);
+          tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
+          const uint32_t sB = sB0 + st * PARTS * b_stage;
+          tc::tma_load_2d(sB, &wmap, s * 32, row, &full[st]);
+          if constexpr (SPLIT)  // low parts: rows outC .. 2*outC - 1 of the packed weight
+            tc::tma_load_2d(sB + b_stage, &wmap, s * 32, g.outC + row, &full[st]);
         }
       }
     }
@@ -249,11 +273,21 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
           const int st = gs % STAGES;
           tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_fwd_status);
           tc::tc_fence_after();
-          const uint32_t sA = sA0 + st * A_STAGE, sB = sB0 + st * b_stage;
+          const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
-                          (s | j) != 0 ? 1u : 0u);
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
+              tc::umma_tf32(d, tc::sdesc_sw128(sA + A_STAGE + j * 32),
+                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+              tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32),
+                            tc::sdesc_sw128(sB + b_stage + j * 32), idesc, 1u);
+              tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
+                            1u);
+            } else {
+              tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
+                            (s | j) != 0 ? 1u : 0u);
+            }
+          }
           tc::umma_commit(&empty[st]);
         }
         tc::umma_commit(&acc_full[acc]);
@@ -300,9 +334,10 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
   }
 }
 
-// Packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = tf32(W[g*Og+o][c][k]).
+// Packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = tf32(W[g*Og+o][c][k]);
+// with `split`, rows outC .. 2*outC-1 hold the low parts tf32(W - hi).
 __global__ void tc_pack_weight_kernel(const float* __restrict__ w, float* __restrict__ wt,
-                                      Geom g) {
+                                      Geom g, int split) {
   const int Kpad = g.kk * g.Cg;
   const long long total = (long long)g.outC * Kpad;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -310,7 +345,10 @@ __global__ void tc_pack_weight_kernel(const float* __restrict__ w, float* __rest
     const int kc = (int)(i % Kpad);
     const long long oc = i / Kpad;
     const int k = kc / g.Cg, c = kc - k * g.Cg;
-    wt[i] = tc::to_tf32(w[(oc * g.Cg + c) * g.kk + k]);
+    const float v = w[(oc * g.Cg + c) * g.kk + k];
+    const float hi = tc::to_tf32(v);
+    wt[i] = hi;
+    if (split) wt[total + i] = tc::to_tf32(v - hi);
   }
 }
 
@@ -322,39 +360,42 @@ bool tc_fwd_supported(const Geom& g) {
          (long long)g.N * g.HW * g.C + g.C < (1LL << 31) && (long long)g.kk * g.Cg < (1LL << 30);
 }
 
-size_t tc_fwd_weight_bytes(const Geom& g) {
-  return (size_t)g.outC * g.kk * g.Cg * sizeof(float);
+size_t tc_fwd_weight_bytes(const Geom& g, bool split) {
+  return (size_t)(split ? 2 : 1) * g.outC * g.kk * g.Cg * sizeof(float);
 }
 
-cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, cudaStream_t stream) {
+cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
+                                  cudaStream_t stream) {
   const long long total = (long long)g.outC * g.kk * g.Cg;
   if (total == 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  tc_pack_weight_kernel<<<(int)blocks, 256, 0, stream>>>(w, wt, g);
+  tc_pack_weight_kernel<<<(int)blocks, 256, 0, stream>>>(w, wt, g, split ? 1 : 0);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt, const float* off,
-                          const float* mask, const float* bias, float* out, int num_sms,
-                          cudaStream_t stream) {
+                          const float* mask, const float* bias, float* out, bool split,
+                          int num_sms, cudaStream_t stream) {
   if (!tc_fwd_supported(g)) return cudaErrorInvalidValue;
   const int bn = tc_bn(g);
   const int Kpad = g.kk * g.Cg;
   CUtensorMap wmap;
-  cudaError_t e = make_tmap_2d_f32(&wmap, wt, (uint64_t)Kpad, (uint64_t)g.outC, (uint64_t)Kpad,
+  cudaError_t e = make_tmap_2d_f32(&wmap, wt, (uint64_t)Kpad,
+                                   (uint64_t)g.outC * (split ? 2 : 1), (uint64_t)Kpad,
                                    (uint32_t)bn);
   if (e != cudaSuccess) return e;
-  const size_t smem = smem_bytes(bn);
-  e = cudaFuncSetAttribute(fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = smem_bytes(bn, split);
+  auto kern = split ? fwd_tc_kernel<true> : fwd_tc_kernel<false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int mtiles = (int)((g.NP + BM - 1) / BM);
   const int ntiles_n = g.Og / bn;
   const long long ntiles = (long long)mtiles * ntiles_n * g.G;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  fwd_tc_kernel<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, tmem_cols_for(bn), mtiles,
-                                                  ntiles_n, (int)ntiles, off, mask, bias, out);
+  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, tmem_cols_for(bn), mtiles, ntiles_n,
+                                         (int)ntiles, off, mask, bias, out);
   return cudaGetLastError();
 }
 

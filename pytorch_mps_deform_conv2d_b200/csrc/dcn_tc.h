@@ -10,16 +10,18 @@ namespace dcn {
 
 // Whether the tensor-core forward covers this geometry.
 bool tc_fwd_supported(const Geom& g);
-// Bytes of the packed weight operand of the tensor-core forward.
-size_t tc_fwd_weight_bytes(const Geom& g);
+// Bytes of the packed weight operand of the tensor-core forward (`split`:
+// high and low TF32 parts, for 3xTF32).
+size_t tc_fwd_weight_bytes(const Geom& g, bool split);
 // weight (outC, Cg, kh, kw) -> packed tensor-core B operand.
-cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g,
+cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
                                   cudaStream_t stream);
 // Forward on tcgen05: implicit GEMM whose A tiles are gathered (bilinear
 // deformable sampling) by producer warps straight into swizzled shared memory.
+// `split`: 3xTF32 (fp32-level accuracy).
 cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
                           const float* off, const float* mask, const float* bias,
-                          float* out, int num_sms, cudaStream_t stream);
+                          float* out, bool split, int num_sms, cudaStream_t stream);
 
 // Whether the tensor-core backward covers this geometry.
 bool tc_bwd_supported(const Geom& g);
@@ -28,17 +30,20 @@ bool tc_bwd_supported(const Geom& g);
 // packed weight.
 size_t tc_bwd_scratch_bytes(const Geom& g);
 // go -> go_t / go_r (tf32-rounded); also sums grad_bias into `gb` (zeroed by
-// the caller) when it is not NULL.
-cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_r,
-                              float* gb, cudaStream_t stream);
-cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
+// the caller) when it is not NULL.  With `go_t_lo` (3xTF32) the low TF32
+// parts go to go_t_lo and to a second copy of go_r's rows after the first.
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
+                              float* go_r, float* gb, cudaStream_t stream);
+cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g, bool split,
                                       cudaStream_t stream);
 // grad_col = W^T go on the tensor core per (pixel tile, tap), fused with the
 // col2im scatter into gxt (NHWC, pre-zeroed) and the coordinate / mask
 // reductions into goff / gmask (pre-zeroed).
-cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* wbt,
-                               const float* xt, const float* off, const float* mask,
-                               float* gxt, float* goff, float* gmask, cudaStream_t stream);
+// `go_t_lo` non-NULL selects 3xTF32 (wbt then holds high and low parts).
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
+                               const float* wbt, const float* xt, const float* off,
+                               const float* mask, float* gxt, float* goff, float* gmask,
+                               cudaStream_t stream);
 // Sampling plans of every (n, deformable group, tap, pixel): 32 bytes each
 // (corner element offsets into the NHWC copy, weights times mask).
 inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }
@@ -46,7 +51,7 @@ cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, 
                             cudaStream_t stream);
 // grad_weight (pre-zeroed) += col^T go on the tensor core, split over pixels.
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const void* plans, float* gw, int num_sms,
+                                 const void* plans, float* gw, bool split, int num_sms,
                                  cudaStream_t stream);
 
 }  // namespace dcn

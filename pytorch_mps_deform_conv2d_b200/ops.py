@@ -20,10 +20,12 @@ from . import _native
 # Flag words of the C ABI (include/dcn_b200.h).
 MATH_FP32 = 0x0
 MATH_TF32 = 0x1
+MATH_3XTF32 = 0x2
 ALGO_SIMT_GEMM = 0x100
 ALGO_SIMT_DIRECT = 0x200
 
-_MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32}
+_MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32, "3xtf32": MATH_3XTF32}
+_NAMES = {v: k for k, v in _MODES.items()}
 _math_override: Optional[int] = None
 
 
@@ -32,7 +34,9 @@ def set_math_mode(mode: Optional[str]) -> None:
 
     ``"fp32"``: fp32 FFMA on the CUDA cores (tolerance of the reference's own
     tests, 1e-4).  ``"tf32"``: tcgen05 tensor cores with TF32 operands and
-    fp32 accumulation.  ``None`` (default): follow
+    fp32 accumulation.  ``"3xtf32"``: the same tensor-core kernels with each
+    operand split into high and low TF32 parts (three products per
+    multiply-add), close to fp32 accuracy.  ``None`` (default): follow
     ``torch.backends.cuda.matmul.allow_tf32``, as PyTorch's own convolutions
     and matmuls do.
     """
@@ -46,9 +50,9 @@ def set_math_mode(mode: Optional[str]) -> None:
 
 
 def get_math_mode() -> str:
-    """The math mode the next call will use ("fp32" or "tf32")."""
+    """The math mode the next call will use ("fp32", "tf32" or "3xtf32")."""
     if _math_override is not None:
-        return "tf32" if (_math_override & 0xff) == MATH_TF32 else "fp32"
+        return _NAMES.get(_math_override & 0xff, "fp32")
     return "tf32" if torch.backends.cuda.matmul.allow_tf32 else "fp32"
 
 

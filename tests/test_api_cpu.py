@@ -36,6 +36,8 @@ def test_math_mode_switch():
     assert dcn.get_math_mode() == "fp32"
     dcn.set_math_mode("tf32")
     assert dcn.get_math_mode() == "tf32"
+    dcn.set_math_mode("3xtf32")
+    assert dcn.get_math_mode() == "3xtf32"
     dcn.set_math_mode(None)
     with pytest.raises(ValueError):
         dcn.set_math_mode("bf16")
