@@ -66,12 +66,18 @@ extern "C" {
  *   DCN_MATH_3XTF32  the same tensor-core kernels with every operand split
  *                  into high and low TF32 parts (hi*hi + hi*lo + lo*hi):
  *                  close to fp32 accuracy at tensor-core speed.
- * The second byte can pin a kernel family (test use; 0 = automatic). */
+ * The second byte can pin a kernel family (0 = automatic):
+ *   DCN_ALGO_SIMT_GEMM / DCN_ALGO_SIMT_DIRECT  fp32 CUDA-core kernels (tests);
+ *   DCN_ALGO_TC_GATHER_WEIGHT  tensor-core backward without the column buffer:
+ *                  the weight gradient re-gathers its columns, so the backward
+ *                  workspace drops kernel_h*kernel_w*N*Ho*Wo*C floats (x2 in
+ *                  3xTF32) at some speed. */
 #define DCN_MATH_FP32 0x0
 #define DCN_MATH_TF32 0x1
 #define DCN_MATH_3XTF32 0x2
 #define DCN_ALGO_SIMT_GEMM 0x100
 #define DCN_ALGO_SIMT_DIRECT 0x200
+#define DCN_ALGO_TC_GATHER_WEIGHT 0x400
 
 /* Geometry of one deformable convolution: the shapes of the reference op's
  * tensors plus its integer arguments. */

@@ -154,15 +154,19 @@ __device__ __forceinline__ DTile dtile_of(int t, int mtiles, int ctiles, int ksp
 // through a shared-memory transpose so that 8 lanes cover one pixel's 32
 // channels, making every corner load and vector reduction a full 128-byte
 // line.  Scatters into the NHWC grad-input accumulator (col2im) and reduces
-// the coordinate / mask gradients of each pixel over its channels.
+// the coordinate / mask gradients of each pixel over its channels.  With a
+// column buffer (`col` non-NULL) it also stores the sampled column values
+// col[k][q][c] = mask * bilinear(x) -- TF32-rounded; with `col_lo` non-zero
+// the low TF32 parts go `col_lo` floats further -- for the weight gradient.
 __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float (&vals)[32],
-                                               int gch0, long long row_q, int lane,
-                                               unsigned char* scratch,
+                                               int gch0, long long row_q, long long qbase,
+                                               int lane, unsigned char* scratch,
                                                const float* __restrict__ xt,
                                                const float* __restrict__ off,
                                                const float* __restrict__ mask,
                                                float* __restrict__ gxt, float* __restrict__ goff,
-                                               float* __restrict__ gmask, int& plan_key) {
+                                               float* __restrict__ gmask, float* __restrict__ col,
+                                               long long col_lo, int& plan_key) {
   float* T = reinterpret_cast<float*>(scratch);
   PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + EPI_T_BYTES);
   const int quad = lane & 7, sub = lane >> 3;
@@ -217,6 +221,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
     const int4 pc = plan[px].cidx;
     const int4 pidx = plan[px].idx;
     float s_h = 0.f, s_w = 0.f, s_m = 0.f;
+    float cv[4] = {0.f, 0.f, 0.f, 0.f};  // column values (mask * bilinear)
     if (pidx.x >= 0) {
       const float4 pw = plan[px].w;
       const float4 geo = plan[px].geo;
@@ -241,7 +246,9 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
       for (int e = 0; e < 4; ++e) {
         s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
         s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
-        s_m += gcs[e] * bilerp(sp, a[e], b[e], c[e], d[e]);
+        const float bv = bilerp(sp, a[e], b[e], c[e], d[e]);
+        s_m += gcs[e] * bv;
+        cv[e] = m * bv;
       }
       const int cis[4] = {pc.x, pc.y, pc.z, pc.w};
       const float wss[4] = {pw.x, pw.y, pw.z, pw.w};
@@ -251,6 +258,16 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
         const float wc = wss[cc] * m;
         red_add_v4(gq + (unsigned)cis[cc], wc * gc0, wc * gc1, wc * gc2, wc * gc3);
       }
+    }
+    if (col != nullptr && qbase + px < g.NP) {  // every (k, q, c) is written, voids as 0
+      float* dst = col + ((long long)k * g.NP + qbase + px) * g.C + gch0 + quad * 4;
+      const float h0 = tc::to_tf32(cv[0]), h1 = tc::to_tf32(cv[1]), h2 = tc::to_tf32(cv[2]),
+                  h3 = tc::to_tf32(cv[3]);
+      *reinterpret_cast<float4*>(dst) = make_float4(h0, h1, h2, h3);
+      if (col_lo != 0)
+        *reinterpret_cast<float4*>(dst + col_lo) =
+            make_float4(tc::to_tf32(cv[0] - h0), tc::to_tf32(cv[1] - h1),
+                        tc::to_tf32(cv[2] - h2), tc::to_tf32(cv[3] - h3));
     }
     // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
     s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);
@@ -286,7 +303,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
                    int ntiles,
                    const float* __restrict__ xt, const float* __restrict__ off,
                    const float* __restrict__ mask, float* __restrict__ gxt,
-                   float* __restrict__ goff, float* __restrict__ gmask) {
+                   float* __restrict__ goff, float* __restrict__ gmask,
+                   float* __restrict__ col) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
@@ -395,7 +413,9 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     int gt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
-      const long long row_q = T.q0 + lq * 32 + lane;
+      const long long qbase = T.q0 + lq * 32;
+      const long long row_q = qbase + lane;
+      const long long col_lo = SPLIT ? (long long)g.kk * g.NP * g.C : 0;
       int plan_key = -1;
       for (int k = T.k0; k < T.k1; ++k, ++gt) {
         const int acc = gt & 1;
@@ -422,8 +442,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for tap + 2
           }
-          epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, lane, scratch, xt,
-                         off, mask, gxt, goff, gmask, plan_key);
+          epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, qbase, lane,
+                         scratch, xt, off, mask, gxt, goff, gmask, col, col_lo, plan_key);
         }
       }
     }
@@ -769,6 +789,171 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// bwd_weight_col: the weight gradient from the column buffer written by the
+// grad-column epilogue (col[k][q][C], TF32-rounded; low parts kk*NP rows
+// further in 3xTF32):  gW'[c, o] += sum_q col[k][q][c] go[q, o]  (.mm:842-880)
+// as a dense tcgen05 GEMM with both operands brought in by TMA.  Tiles as in
+// bwd_weight_tc: (tap k, 128 channels, bn out channels, group, pixel range).
+//   warps 0-3  epilogue: accumulator -> fp32 reductions into grad_weight
+//   warp  4    MMA issue
+//   warp  5    TMA producer: per 32-pixel K step, four 32-channel blocks of
+//              col (MN-major operand, 128-byte swizzle with 32-byte atoms)
+//              and bn go_r rows
+// Rows of a K step past an image's last pixel read the next pixels' columns;
+// their go_r columns are zero (padding / out of range), so they add nothing.
+// ---------------------------------------------------------------------------
+constexpr int WC_THREADS = 192;
+constexpr int WC_MMA_WARP = 4, WC_TMA_WARP = 5;
+
+template <bool SPLIT>
+__global__ void __launch_bounds__(WC_THREADS, 1)
+bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
+                      const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
+                      float* __restrict__ gw, int mtiles, int ntn, int splits, int per,
+                      int ntiles) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_u32 = tc::smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  constexpr int STAGES = SPLIT ? 2 : 4;
+  constexpr int PARTS = SPLIT ? 2 : 1;
+  const uint32_t sA0 = tc::smem_u32(smem);
+  const uint32_t b_stage = (uint32_t)bn * 128;
+  const uint32_t sB0 = sA0 + STAGES * PARTS * W2_A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * PARTS * (W2_A_STAGE + b_stage));
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pchunks = (g.P + 31) >> 5;
+  const int total_chunks = g.N * pchunks;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&acc_full[a], 1);
+      tc::mbar_init(&acc_empty[a], 4);
+    }
+    tc::fence_mbar_init();
+  }
+  if (warp == WC_MMA_WARP) {
+    tc::tmem_alloc(tmem_slot, (uint32_t)tcols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == WC_TMA_WARP) {
+    if (lane == 0) {
+      const int lo_rows = g.kk * (int)g.NP;  // row offset of the low parts
+      int gs = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+        const int x0 = T.gi * g.Cg + T.cm0;
+        for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
+          const int st = gs % STAGES;
+          const int u = gs / STAGES;
+          const int n = tt / pchunks;
+          const int p0 = (tt - n * pchunks) << 5;
+          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+          tc::mbar_arrive_expect_tx(&full[st], PARTS * (W2_A_STAGE + b_stage));
+          const int y = T.k * (int)g.NP + n * g.P + p0;
+          const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE;
+#pragma unroll
+          for (int mb = 0; mb < 4; ++mb) {
+            tc::tma_load_2d(sA + mb * W_LBO, &colmap, x0 + mb * 32, y, &full[st]);
+            if constexpr (SPLIT)
+              tc::tma_load_2d(sA + W2_A_STAGE + mb * W_LBO, &colmap, x0 + mb * 32, lo_rows + y,
+                              &full[st]);
+          }
+          const int row = n * g.outC + T.gi * g.Og + T.o0;
+          const uint32_t sB = sB0 + st * PARTS * b_stage;
+          tc::tma_load_2d(sB, &gomap, p0, row, &full[st]);
+          if constexpr (SPLIT)
+            tc::tma_load_2d(sB + b_stage, &gomap, p0, g.N * g.outC + row, &full[st]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == WC_MMA_WARP) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
+      int gs = 0, it = 0;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+        if (T.t_begin >= T.t_end) continue;
+        const int acc = it & 1;
+        if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_bwd_status);
+        tc::tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * bn);
+        for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
+          const int st = gs % STAGES;
+          const int s = tt - T.t_begin;
+          tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_bwd_status);
+          tc::tc_fence_after();
+          const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE, sB = sB0 + st * PARTS * b_stage;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + W2_A_STAGE + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + b_stage + j * 32), idesc, 1u);
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, 1u);
+            } else {
+              tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+            }
+          }
+          tc::umma_commit(&empty[st]);
+        }
+        tc::umma_commit(&acc_full[acc]);
+        ++it;
+      }
+    }
+    __syncwarp();
+  } else {
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+      if (T.t_begin >= T.t_end) continue;
+      const int acc = it & 1;
+      tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
+      tc::tc_fence_after();
+      const int c = T.cm0 + warp * 32 + lane;  // channel within the group
+      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + T.k;
+      const long long ostride = (long long)g.Cg * g.kk;
+      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
+      for (int cb = 0; cb < bn; cb += 8) {
+        float vv[8];
+        tc::tmem_ld8(ta + (uint32_t)cb, vv);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+      ++it;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == WC_MMA_WARP) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, (uint32_t)tcols);
+  }
+}
+
 // wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels);
 // with `split`, the low parts follow in rows G*kk*Cg ..
 __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __restrict__ wb,
@@ -790,6 +975,37 @@ __global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __
 }
 
 int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
+
+// Tiles of the weight-gradient kernels and their pixel-range splits: the
+// split count minimises the busiest CTA's time, modelled as rounds of tiles x
+// (K steps per tile + `tile_cost`, a tile's fixed cost in K steps: pipeline
+// fill and the grad_weight reductions), with >= 8 K steps per tile.
+struct WSplit {
+  int mtiles, ntn, splits, per;
+  long long ntiles;
+};
+WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
+  WSplit w;
+  w.mtiles = g.Cg / W_BM;
+  w.ntn = g.Og / bn;
+  const long long base = (long long)g.kk * w.mtiles * w.ntn * g.G;
+  const int pchunks = (g.P + 31) / 32;
+  const int total_chunks = g.N * pchunks;
+  const long long max_splits = (total_chunks + 7) / 8 > 0 ? (total_chunks + 7) / 8 : 1;
+  long long splits = 1, best = -1;
+  for (long long sp = 1; sp <= max_splits && sp * base <= 64LL * num_sms; ++sp) {
+    const long long rounds = (base * sp + num_sms - 1) / num_sms;
+    const long long cost = rounds * ((total_chunks + sp - 1) / sp + tile_cost);
+    if (best < 0 || cost < best) {
+      best = cost;
+      splits = sp;
+    }
+  }
+  w.splits = (int)splits;
+  w.per = (int)((total_chunks + splits - 1) / splits);
+  w.ntiles = base * splits;
+  return w;
+}
 
 }  // namespace
 
@@ -829,7 +1045,7 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
                                const float* wbt, const float* xt, const float* off,
                                const float* mask, float* gxt, float* goff, float* gmask,
-                               cudaStream_t stream) {
+                               float* col, cudaStream_t stream) {
   const bool split = go_t_lo != nullptr;
   CUtensorMap amap, amap_lo, bmap;
   cudaError_t e = make_tmap_2d_f32(&amap, go_t, (uint64_t)g.outC, (uint64_t)g.NP,
@@ -867,7 +1083,7 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < sms ? ntiles : sms);
   kern<<<grid, threads, smem, stream>>>(g, amap, amap_lo, bmap, mtiles, ctiles, ksplits,
-                                         (int)ntiles, xt, off, mask, gxt, goff, gmask);
+                                         (int)ntiles, xt, off, mask, gxt, goff, gmask, col);
   return cudaGetLastError();
 }
 
@@ -895,30 +1111,46 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   auto kern = split ? bwd_weight_tc_kernel<true> : bwd_weight_tc_kernel<false>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int mtiles = g.Cg / W_BM;
-  const int ntn = g.Og / bn;
-  const long long base = (long long)g.kk * mtiles * ntn * g.G;
-  const int pchunks = (g.P + 31) / 32;
-  const int total_chunks = g.N * pchunks;
-  // pixel-range splits: pick the count that minimises the busiest CTA's K
-  // steps (rounds of tiles x chunks per tile), with >= 8 K steps per tile
-  const long long max_splits = (total_chunks + 7) / 8 > 0 ? (total_chunks + 7) / 8 : 1;
-  long long splits = 1, best = -1;
-  for (long long sp = 1; sp <= max_splits && sp * base <= 64LL * num_sms; ++sp) {
-    const long long rounds = (base * sp + num_sms - 1) / num_sms;
-    const long long cost = rounds * ((total_chunks + sp - 1) / sp);
-    if (best < 0 || cost < best) {
-      best = cost;
-      splits = sp;
-    }
-  }
-  const int per = (int)((total_chunks + splits - 1) / splits);
-  const long long ntiles = base * splits;
-  if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
-  const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
+  // a gathered K step costs far more than the tile's fixed work
+  const WSplit w = weight_split(g, bn, num_sms, 0);
+  if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(w.ntiles < num_sms ? w.ntiles : num_sms);
   kern<<<grid, W2_THREADS, smem, stream>>>(g, gomap, bn, pow2_cols(2 * bn), xt,
-                                            static_cast<const int4*>(plans), gw, mtiles, ntn,
-                                            (int)splits, per, (int)ntiles);
+                                            static_cast<const int4*>(plans), gw, w.mtiles, w.ntn,
+                                            w.splits, w.per, (int)w.ntiles);
+  return cudaGetLastError();
+}
+
+bool tc_wcol_supported(const Geom& g, bool split) {
+  return tc_bwd_supported(g) && (long long)g.kk * g.NP * (split ? 2 : 1) < (1LL << 31);
+}
+
+size_t tc_col_bytes(const Geom& g, bool split) {
+  return (size_t)(split ? 2 : 1) * g.kk * g.NP * g.C * sizeof(float);
+}
+
+cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* go_r, float* gw,
+                                  bool split, int num_sms, cudaStream_t stream) {
+  if (!tc_wcol_supported(g, split)) return cudaErrorInvalidValue;
+  const int bn = weight_bn(g);
+  const int Ppad = (g.P + 3) & ~3;
+  CUtensorMap colmap, gomap;
+  cudaError_t e = make_tmap_2d_f32(&colmap, col, (uint64_t)g.C,
+                                   (uint64_t)g.kk * g.NP * (split ? 2 : 1), (uint64_t)g.C, 32u,
+                                   /*atom32=*/true);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_2d_f32(&gomap, go_r, (uint64_t)Ppad, (uint64_t)g.N * g.outC * (split ? 2 : 1),
+                       (uint64_t)Ppad, (uint32_t)bn);
+  if (e != cudaSuccess) return e;
+  const size_t smem = weight_smem_bytes(bn, split);
+  auto kern = split ? bwd_weight_col_kernel<true> : bwd_weight_col_kernel<false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const WSplit w = weight_split(g, bn, num_sms, 16);
+  if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(w.ntiles < num_sms ? w.ntiles : num_sms);
+  kern<<<grid, WC_THREADS, smem, stream>>>(g, colmap, gomap, bn, pow2_cols(2 * bn), gw, w.mtiles,
+                                            w.ntn, w.splits, w.per, (int)w.ntiles);
   return cudaGetLastError();
 }
 

@@ -214,6 +214,12 @@ bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
          dcn::tc_bwd_supported(g);
 }
 
+// Tensor-core backward with the column buffer (weight gradient as a dense
+// GEMM over the columns the grad-column kernel writes).
+bool use_col_path(const dcn::Geom& g, uint32_t flags) {
+  return !(flags & DCN_ALGO_TC_GATHER_WEIGHT) && dcn::tc_wcol_supported(g, split_math(flags));
+}
+
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
   size_t b = align_up(xt_floats(g) * sizeof(float));                   // xt + zero row
   b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
@@ -222,7 +228,10 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     b += parts * align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
     b += align_up(parts * g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));   // go_r
     b += align_up(parts * g.outC * g.Cg * g.kk * sizeof(float));               // packed weight
-    b += align_up(dcn::tc_plan_bytes(g));                              // sampling plans
+    if (use_col_path(g, flags))
+      b += align_up(dcn::tc_col_bytes(g, split_math(flags)));                  // column buffer
+    else
+      b += align_up(dcn::tc_plan_bytes(g));                                    // sampling plans
   } else {
     b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
   }
@@ -390,18 +399,26 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     float* go_t_lo = split ? ws.take((size_t)g.N * g.outC * g.P) : nullptr;
     float* go_r = ws.take(parts * g.N * g.outC * ((g.P + 3) & ~3));
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
-    void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
+    const bool colp = use_col_path(g, flags);
+    float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
     DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r, nullptr, stream),
              "tc_prep_go");
     DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, stream), "tc_pack_weight_bwd");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,
-                                     grad_mask, stream),
+                                     grad_mask, col, stream),
              "bwd_data_tc");
     DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
-    DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
-    DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split, num_sms_current(),
-                                       stream),
-             "bwd_weight_tc");
+    if (colp) {
+      DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, grad_weight, split, num_sms_current(),
+                                          stream),
+               "bwd_weight_col");
+    } else {
+      void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
+      DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
+      DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split,
+                                         num_sms_current(), stream),
+               "bwd_weight_tc");
+    }
     return DCN_OK;
   }
   if (dcn::bwd_small_supported(g) && !(flags & DCN_ALGO_SIMT_GEMM)) {

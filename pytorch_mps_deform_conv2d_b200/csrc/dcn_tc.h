@@ -40,10 +40,17 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 // col2im scatter into gxt (NHWC, pre-zeroed) and the coordinate / mask
 // reductions into goff / gmask (pre-zeroed).
 // `go_t_lo` non-NULL selects 3xTF32 (wbt then holds high and low parts).
+// `col` non-NULL: also writes the column buffer (tc_col_bytes) that
+// launch_bwd_weight_col reads.
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
                                const float* wbt, const float* xt, const float* off,
                                const float* mask, float* gxt, float* goff, float* gmask,
-                               cudaStream_t stream);
+                               float* col, cudaStream_t stream);
+// Weight gradient as a dense TMA-fed GEMM over the column buffer.
+bool tc_wcol_supported(const Geom& g, bool split);
+size_t tc_col_bytes(const Geom& g, bool split);
+cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* go_r, float* gw,
+                                  bool split, int num_sms, cudaStream_t stream);
 // Sampling plans of every (n, deformable group, tap, pixel): 32 bytes each
 // (corner element offsets into the NHWC copy, weights times mask).
 inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }

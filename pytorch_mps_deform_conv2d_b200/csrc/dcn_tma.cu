@@ -21,7 +21,7 @@ void resolve_encode() {
 }  // namespace
 
 cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
-                             uint64_t pitch_elems, uint32_t box_rows) {
+                             uint64_t pitch_elems, uint32_t box_rows, bool atom32) {
   std::call_once(g_encode_once, resolve_encode);
   if (g_encode_status != cudaSuccess) return g_encode_status;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (pitch_elems * 4) % 16 != 0 ||
@@ -33,7 +33,9 @@ cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base),
                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                     : CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }

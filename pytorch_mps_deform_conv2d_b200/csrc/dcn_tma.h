@@ -12,8 +12,10 @@ namespace dcn {
 // 2-D fp32 tensor map over `rows` rows of `inner` contiguous elements with a
 // row pitch of `pitch_elems`; boxes of 32 elements (128 B) x `box_rows` rows,
 // 128-byte swizzle, out-of-range elements read as zero.  `base` and the pitch
-// in bytes must be multiples of 16.
+// in bytes must be multiples of 16.  `atom32` selects the 128-byte swizzle
+// with 32-byte atoms (32-byte chunk c of row r lands at chunk c ^ (r % 4)),
+// the layout of an MN-major TF32 tensor-core operand.
 cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
-                             uint64_t pitch_elems, uint32_t box_rows);
+                             uint64_t pitch_elems, uint32_t box_rows, bool atom32 = false);
 
 }  // namespace dcn

@@ -23,6 +23,7 @@ MATH_TF32 = 0x1
 MATH_3XTF32 = 0x2
 ALGO_SIMT_GEMM = 0x100
 ALGO_SIMT_DIRECT = 0x200
+ALGO_TC_GATHER_WEIGHT = 0x400
 
 _MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32, "3xtf32": MATH_3XTF32}
 _NAMES = {v: k for k, v in _MODES.items()}

@@ -9,18 +9,18 @@ import pytest
 from _util import assert_close, make_case, run_oracle, run_ours
 from pytorch_mps_deform_conv2d_b200 import _native
 from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32
-from test_tf32_gpu import TC_BWD_CASES, TC_CASES
+from test_tf32_gpu import TC_BWD_CASES, TC_CASES, WEIGHT_PATHS
 
 pytestmark = pytest.mark.gpu
 
 TOL = {"x": 2e-3, "off": 1e-4, "m": 1e-4, "w": 1e-4, "b": 1e-4}
 
 
-def _run_profiled(case, backward):
+def _run_profiled(case, backward, algo=0):
     _native.profiler_read()
     _native.profiler_enable(True)
     try:
-        out, grads = run_ours(case, flags=MATH_3XTF32, backward=backward)
+        out, grads = run_ours(case, flags=MATH_3XTF32 | algo, backward=backward)
     finally:
         _native.profiler_enable(False)
     return out, grads, _native.profiler_read()
@@ -36,11 +36,13 @@ def test_forward_3xtf32(cuda_device, name):
     assert_close(out, ref, rtol=1e-4, atol=1e-4 * scale, name="out")
 
 
+@pytest.mark.parametrize("path", sorted(WEIGHT_PATHS))
 @pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
-def test_backward_3xtf32(cuda_device, name):
+def test_backward_3xtf32(cuda_device, name, path):
+    algo, kernel = WEIGHT_PATHS[path]
     case = make_case(upstream="randn", **TC_BWD_CASES[name])
-    out, grads, stats = _run_profiled(case, backward=True)
-    assert "bwd_data_tc" in stats and "bwd_weight_tc" in stats, sorted(stats)
+    out, grads, stats = _run_profiled(case, backward=True, algo=algo)
+    assert "bwd_data_tc" in stats and kernel in stats, sorted(stats)
     ref, rgrads = run_oracle(case)
     scale = max(1.0, float(np.abs(ref).max()))
     assert_close(out, ref, rtol=1e-4, atol=1e-4 * scale, name="out")

@@ -8,7 +8,7 @@ import torch
 
 from _util import make_case, rel_norm_err, run_oracle, run_ours
 from pytorch_mps_deform_conv2d_b200 import _native
-from pytorch_mps_deform_conv2d_b200.ops import MATH_TF32
+from pytorch_mps_deform_conv2d_b200.ops import ALGO_TC_GATHER_WEIGHT, MATH_TF32
 
 pytestmark = pytest.mark.gpu
 
@@ -85,11 +85,17 @@ TC_BWD_CASES = {
 }
 
 
-def _grad_errors(case):
+# The two tensor-core weight-gradient kernels: the dense GEMM over the column
+# buffer written by the grad-column kernel (default), and the one that
+# gathers its own columns (no column buffer).
+WEIGHT_PATHS = {"col": (0, "bwd_weight_col"), "gather": (ALGO_TC_GATHER_WEIGHT, "bwd_weight_tc")}
+
+
+def _grad_errors(case, flags=MATH_TF32):
     _native.profiler_read()
     _native.profiler_enable(True)
     try:
-        out, grads = run_ours(case, flags=MATH_TF32)
+        out, grads = run_ours(case, flags=flags)
     finally:
         _native.profiler_enable(False)
     stats = _native.profiler_read()
@@ -100,10 +106,13 @@ def _grad_errors(case):
     return stats, rel_norm_err(out, ref), errs, elem
 
 
+@pytest.mark.parametrize("path", sorted(WEIGHT_PATHS))
 @pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
-def test_backward_tf32(cuda_device, name):
-    stats, out_err, errs, elem = _grad_errors(make_case(upstream="randn", **TC_BWD_CASES[name]))
-    assert "bwd_data_tc" in stats and "bwd_weight_tc" in stats, sorted(stats)
+def test_backward_tf32(cuda_device, name, path):
+    algo, kernel = WEIGHT_PATHS[path]
+    stats, out_err, errs, elem = _grad_errors(make_case(upstream="randn", **TC_BWD_CASES[name]),
+                                              flags=MATH_TF32 | algo)
+    assert "bwd_data_tc" in stats and kernel in stats, sorted(stats)
     assert out_err <= OUT_TOL
     for k, e in errs.items():
         assert e <= GRAD_TOL, f"grad_{k}: norm-wise rel err {e:.2e} (all: {errs}, elem: {elem})"
