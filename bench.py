@@ -2,7 +2,7 @@
 """Benchmark: DCNv2 forward + backward on the detection-neck workload.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--math tf32|fp32] [--workload neck|train|grouped|dcnv1]
+                    [--math tf32|fp32|3xtf32] [--workload neck|train|grouped|dcnv1]
 
 One step is one training pass of the deformable convolution over one batch:
 forward, backward with a fixed upstream gradient, and (N > 1) the NCCL
@@ -111,6 +111,10 @@ def algorithmic_work(wl):
     fwd = x + off + msk + wts + bia + out
     bwd = (out + x + off + msk + wts) + (x + off + msk + wts + bia)
     return dict(flops=3 * gemm, gemm_flops=gemm, bytes=4.0 * (fwd + bwd), P=P)
+
+
+# tcgen05 kernels (TF32 operands; 3xTF32 issues three products per multiply-add)
+TC_KERNELS = ("fwd_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col")
 
 
 def kernel_work(name, wl):
@@ -304,7 +308,7 @@ def run_ours(args, wl):
     import torch.distributed as dist
     import pytorch_mps_deform_conv2d_b200 as dcn
     from pytorch_mps_deform_conv2d_b200 import _native
-    from pytorch_mps_deform_conv2d_b200.ops import MATH_FP32, MATH_TF32, deform_conv2d_ex
+    from pytorch_mps_deform_conv2d_b200.ops import _MODES, deform_conv2d_ex
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -314,7 +318,7 @@ def run_ours(args, wl):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    flags = MATH_TF32 if args.math == "tf32" else MATH_FP32
+    flags = _MODES[args.math]
 
     x, w, b, off, m, go = make_inputs(wl, seed=rank)
     xd, offd, md, god = (t.to(dev) if t is not None else None for t in (x, off, m, go))
@@ -395,7 +399,7 @@ def run_ours(args, wl):
     roof = {"kernel": dom, "bound": bound, "share_of_step": round(dom_ms / total_ms, 3)
             if world == 1 else None}
     if bound == "tensor":
-        if dom.endswith("_tc"):
+        if dom in TC_KERNELS:
             peak = peak_tf32
             src = ("cuBLAS tf32 8192^3 burst measured in this run (MEASURED_PEAKS.json holds bf16 "
                    f"only: {peaks.get('bf16_tflops')} TFLOP/s)")
@@ -415,7 +419,7 @@ def run_ours(args, wl):
     traffic = load_traffic().get(f"{args.workload}:{args.math}:{dom}")
     roof["traffic"] = traffic["bytes_per_launch"] if traffic else None
     work = algorithmic_work(wl)
-    step_roof_ms = work["flops"] / ((peak_tf32 if flags == MATH_TF32 else peak_fp32) * 1e12) * 1e3
+    step_roof_ms = work["flops"] / ((peak_tf32 if args.math != "fp32" else peak_fp32) * 1e12) * 1e3
     roof["step_roofline_ms"] = round(max(step_roof_ms, work["bytes"] / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3), 4)
     roof["step_frac"] = round(roof["step_roofline_ms"] / ms_per_step, 3)
     roof["peaks_measured_tflops"] = {"tf32": round(peak_tf32, 1), "fp32": round(peak_fp32, 1)}
@@ -430,7 +434,7 @@ def run_ours(args, wl):
         "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-        "dtype": "tf32" if any(k.endswith("_tc") for k in kernels) else "f32",
+        "dtype": args.math if any(k in TC_KERNELS for k in kernels) else "f32",
         "data": "synthetic",
         "config": {"workload": wl["desc"], "global_batch": wl["N"] * world,
                    "per_gpu_batch": wl["N"], "parallelism": f"dp{world}",
@@ -463,7 +467,7 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
         mod.weight.copy_(w)
         if b is not None:
             mod.bias.copy_(b)
-    dcn.set_math_mode("tf32" if flags & 0xff else "fp32")
+    dcn.set_math_mode(args.math)
     host = [t.pin_memory() if t is not None else None for t in (x, off, m, go)]
     params = [p for p in mod.parameters()]
     outs = [torch.empty(p.shape, pin_memory=True) for p in params]
@@ -546,7 +550,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--math", choices=["tf32", "fp32"], default="tf32")
+    ap.add_argument("--math", choices=["tf32", "fp32", "3xtf32"], default="tf32")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",

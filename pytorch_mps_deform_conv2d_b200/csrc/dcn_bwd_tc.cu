@@ -39,15 +39,13 @@ int pow2_cols(int n) {
 // ---------------------------------------------------------------------------
 // prep: go (N, outC, P) -> go_t (N*P, outC) and go_r (N, outC, P), tf32-rounded
 // ---------------------------------------------------------------------------
-// Also accumulates grad_bias (pre-zeroed; NULL when not wanted) from the
-// unrounded values: each block adds its 32 x 32 tile's per-channel sums.
 // With `go_t_lo` (3xTF32), the low TF32 parts go to go_t_lo and to the rows
-// N*outC .. 2*N*outC-1 of go_r.
+// N*outC .. 2*N*outC-1 of go_r.  Scalar version for any P (rows padded to
+// Ppad with zeros).
 __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
                                                       float* __restrict__ go_t,
                                                       float* __restrict__ go_t_lo,
-                                                      float* __restrict__ go_r,
-                                                      float* __restrict__ gb, int N, int outC,
+                                                      float* __restrict__ go_r, int N, int outC,
                                                       int P, int Ppad) {
   __shared__ float tile_lo[32][33];
   __shared__ float tile[32][33];
@@ -58,9 +56,8 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
 #pragma unroll
   for (int i = 0; i < 32; i += 8) {
     const int o = o0 + ty + i, p = p0 + tx;
-    float raw = 0.f;
     if (o < outC && p < Ppad) {
-      raw = p < P ? src[(long long)o * P + p] : 0.f;
+      const float raw = p < P ? src[(long long)o * P + p] : 0.f;
       const float v = tc::to_tf32(raw);
       tile[ty + i][tx] = v;
       go_r[((long long)n * outC + o) * Ppad + p] = v;
@@ -70,12 +67,6 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
         go_r[((long long)(N + n) * outC + o) * Ppad + p] = lo;
       }
     }
-    if (gb) {
-      float sum = raw;
-#pragma unroll
-      for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
-      if (tx == 0 && o < outC) atomicAdd(gb + o, sum);
-    }
   }
   __syncthreads();
 #pragma unroll
@@ -84,6 +75,75 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
     if (o < outC && p < P) {
       go_t[((long long)n * P + p) * outC + o] = tile[tx][ty + i];
       if (go_t_lo) go_t_lo[((long long)n * P + p) * outC + o] = tile_lo[tx][ty + i];
+    }
+  }
+}
+
+// Vector version (P % 4 == 0, so Ppad == P; outC % 4 == 0; 16-byte aligned
+// buffers): a block walks PG_SPAN pixels of 64 out channels of one image in
+// 64 x 64 tiles with 16-byte loads and stores, and also sums grad_bias
+// (pre-zeroed) -- one atomic per out channel per block.
+constexpr int PG_SPAN = 256;
+__global__ void __launch_bounds__(256) prep_go4_kernel(const float* __restrict__ go,
+                                                       float* __restrict__ go_t,
+                                                       float* __restrict__ go_t_lo,
+                                                       float* __restrict__ go_r,
+                                                       float* __restrict__ gb, int N, int outC,
+                                                       int P) {
+  __shared__ float tile[64][65];
+  __shared__ float tile_lo[64][65];
+  const int n = blockIdx.z, o0 = blockIdx.y * 64, pbeg = blockIdx.x * PG_SPAN;
+  const int pend = min(P, pbeg + PG_SPAN);
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float bsum[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int p0 = pbeg; p0 < pend; p0 += 64) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int o = o0 + ty + 16 * i, p = p0 + 4 * tx;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (o < outC && p < P) {
+        const long long at = ((long long)n * outC + o) * P + p;
+        v = __ldg(reinterpret_cast<const float4*>(go + at));
+        const float4 h = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z),
+                                     tc::to_tf32(v.w));
+        *reinterpret_cast<float4*>(go_r + at) = h;
+        float* row = tile[ty + 16 * i] + 4 * tx;
+        row[0] = h.x; row[1] = h.y; row[2] = h.z; row[3] = h.w;
+        if (go_t_lo) {
+          const float4 l = make_float4(tc::to_tf32(v.x - h.x), tc::to_tf32(v.y - h.y),
+                                       tc::to_tf32(v.z - h.z), tc::to_tf32(v.w - h.w));
+          *reinterpret_cast<float4*>(go_r + (long long)N * outC * P + at) = l;
+          float* rl = tile_lo[ty + 16 * i] + 4 * tx;
+          rl[0] = l.x; rl[1] = l.y; rl[2] = l.z; rl[3] = l.w;
+        }
+      }
+      bsum[i] += (v.x + v.y) + (v.z + v.w);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int p = p0 + ty + 16 * i, o = o0 + 4 * tx;
+      if (p < P && o < outC) {
+        const long long at = ((long long)n * P + p) * outC + o;
+        *reinterpret_cast<float4*>(go_t + at) =
+            make_float4(tile[4 * tx][ty + 16 * i], tile[4 * tx + 1][ty + 16 * i],
+                        tile[4 * tx + 2][ty + 16 * i], tile[4 * tx + 3][ty + 16 * i]);
+        if (go_t_lo)
+          *reinterpret_cast<float4*>(go_t_lo + at) =
+              make_float4(tile_lo[4 * tx][ty + 16 * i], tile_lo[4 * tx + 1][ty + 16 * i],
+                          tile_lo[4 * tx + 2][ty + 16 * i], tile_lo[4 * tx + 3][ty + 16 * i]);
+      }
+    }
+    __syncthreads();
+  }
+  if (gb) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float v = bsum[i];
+#pragma unroll
+      for (int d = 8; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);  // 16-lane row
+      const int o = o0 + ty + 16 * i;
+      if (tx == 0 && o < outC) atomicAdd(gb + o, v);
     }
   }
 }
@@ -955,22 +1015,35 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
 }
 
 // wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels);
-// with `split`, the low parts follow in rows G*kk*Cg ..
-__global__ void tc_pack_weight_bwd_kernel(const float* __restrict__ w, float* __restrict__ wb,
-                                          Geom g, int split) {
-  const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int o = (int)(i % g.Og);
-    long long t = i / g.Og;
-    const int c = (int)(t % g.Cg);
-    t /= g.Cg;
-    const int k = (int)(t % g.kk);
-    const int gi = (int)(t / g.kk);
-    const float v = w[((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k];
-    const float hi = tc::to_tf32(v);
-    wb[i] = hi;
-    if (split) wb[total + i] = tc::to_tf32(v - hi);
+// with `split`, the low parts follow in rows G*kk*Cg ..  Per group a 32 x 32
+// tile transpose of W viewed as [o][c*kk + k]: coalesced on both sides.
+__global__ void __launch_bounds__(256) tc_pack_weight_bwd_kernel(const float* __restrict__ w,
+                                                                 float* __restrict__ wb, Geom g,
+                                                                 int split) {
+  __shared__ float tile[32][33];
+  const int gi = blockIdx.z;
+  const int CK = g.Cg * g.kk;
+  const int o0 = blockIdx.y * 32, ck0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const float* src = w + (long long)gi * g.Og * CK;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int o = o0 + ty + i, ck = ck0 + tx;
+    if (o < g.Og && ck < CK) tile[ty + i][tx] = __ldg(src + (long long)o * CK + ck);
+  }
+  __syncthreads();
+  const long long lo = (long long)g.G * g.kk * g.Cg * g.Og;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int ck = ck0 + ty + i, o = o0 + tx;
+    if (o < g.Og && ck < CK) {
+      const int c = ck / g.kk, k = ck - c * g.kk;
+      const long long idx = ((long long)(gi * g.kk + k) * g.Cg + c) * g.Og + o;
+      const float v = tile[tx][ty + i];
+      const float hi = tc::to_tf32(v);
+      wb[idx] = hi;
+      if (split) wb[lo + idx] = tc::to_tf32(v - hi);
+    }
   }
 }
 
@@ -1022,12 +1095,25 @@ size_t tc_bwd_scratch_bytes(const Geom& g) {
          (size_t)g.outC * g.Cg * g.kk * sizeof(float);
 }
 
+bool tc_prep_sums_bias(const Geom& g, const float* go) {
+  return g.P % 4 == 0 && g.outC % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
+         (g.outC + 63) / 64 <= 65535 && g.N <= 65535;
+}
+
 cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
                               float* go_r, float* gb, cudaStream_t stream) {
   if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
+  if (tc_prep_sums_bias(g, go) && (reinterpret_cast<uintptr_t>(go_t) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0 &&
+      (reinterpret_cast<uintptr_t>(go_t_lo) & 15u) == 0) {
+    dim3 grid((g.P + PG_SPAN - 1) / PG_SPAN, (g.outC + 63) / 64, g.N);
+    prep_go4_kernel<<<grid, 256, 0, stream>>>(go, go_t, go_t_lo, go_r, gb, g.N, g.outC, g.P);
+    return cudaGetLastError();
+  }
+  if (gb != nullptr) return cudaErrorInvalidValue;  // the scalar kernel leaves grad_bias alone
   const int Ppad = (g.P + 3) & ~3;
   dim3 grid((Ppad + 31) / 32, (g.outC + 31) / 32, g.N);
-  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_t_lo, go_r, gb, g.N, g.outC, g.P,
+  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_t_lo, go_r, g.N, g.outC, g.P,
                                                    Ppad);
   return cudaGetLastError();
 }
@@ -1036,9 +1122,9 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
                                       cudaStream_t stream) {
   const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
   if (total == 0) return cudaSuccess;
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  tc_pack_weight_bwd_kernel<<<(int)blocks, 256, 0, stream>>>(w, wbt, g, split ? 1 : 0);
+  if ((g.Og + 31) / 32 > 65535 || g.G > 65535) return cudaErrorInvalidValue;
+  dim3 grid((g.Cg * g.kk + 31) / 32, (g.Og + 31) / 32, g.G);
+  tc_pack_weight_bwd_kernel<<<grid, 256, 0, stream>>>(w, wbt, g, split ? 1 : 0);
   return cudaGetLastError();
 }
 

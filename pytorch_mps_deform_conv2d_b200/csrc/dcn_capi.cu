@@ -306,9 +306,8 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
-  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
-  DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
-           "memset");
+  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, nullptr, stream),
+           "nchw_to_nhwc");
   switch (pick_fwd(g, flags)) {
     case FwdAlgo::kDirect:
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
@@ -364,19 +363,22 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
             "deform_conv2d_backward: gradient outputs must be CUDA device buffers");
   DCN_CHECK(mask == nullptr || dev_or_empty(mask, msk_bytes), "mask must be a float32 CUDA tensor");
 
-  // Zero what the kernels accumulate into (.mm:764-777 zero-initialise too).
-  if (off_bytes) DCN_CUDA(cudaMemsetAsync(grad_offset, 0, off_bytes, stream), "memset");
-  if (grad_mask && msk_bytes) DCN_CUDA(cudaMemsetAsync(grad_mask, 0, msk_bytes, stream), "memset");
-  if (w_bytes) DCN_CUDA(cudaMemsetAsync(grad_weight, 0, w_bytes, stream), "memset");
   const bool tc_bwd = use_tc_bwd(g, flags);
-  if (grad_bias) {
-    if (g.N * (long long)g.P == 0) {
-      if (g.outC) DCN_CUDA(cudaMemsetAsync(grad_bias, 0, (size_t)g.outC * sizeof(float), stream), "memset");
-    } else {
-      DCN_CUDA(dcn::launch_grad_bias(grad_output, grad_bias, g, stream), "grad_bias");
-    }
-  }
   const bool skip = g.N == 0 || g.C == 0 || g.outC == 0 || g.P == 0;  // .mm:779-782
+  // the tensor-core prep kernel sums grad_bias while it reads grad_output
+  const bool bias_in_prep =
+      grad_bias != nullptr && tc_bwd && !skip && dcn::tc_prep_sums_bias(g, grad_output);
+  const bool no_pixels = (long long)g.N * g.P == 0;
+  // Zero what the kernels accumulate into (.mm:764-777 zero-initialise too),
+  // in one launch.
+  dcn::ZeroList z{};
+  z.add(grad_offset, (long long)(off_bytes / sizeof(float)));
+  z.add(grad_mask, (long long)(msk_bytes / sizeof(float)));
+  z.add(grad_weight, (long long)(w_bytes / sizeof(float)));
+  if (bias_in_prep || no_pixels) z.add(grad_bias, g.outC);
+  DCN_CUDA(dcn::launch_zero(z, stream), "zero");
+  if (grad_bias != nullptr && !bias_in_prep && !no_pixels)
+    DCN_CUDA(dcn::launch_grad_bias(grad_output, grad_bias, g, stream), "grad_bias");
   if (skip) {
     if (x_bytes) DCN_CUDA(cudaMemsetAsync(grad_input, 0, x_bytes, stream), "memset");
     return DCN_OK;
@@ -388,10 +390,9 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
   float* gxt = ws.take((size_t)g.N * g.HW * g.C);
-  DCN_CUDA(cudaMemsetAsync(gxt, 0, x_bytes, stream), "memset");
-  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, stream), "nchw_to_nhwc");
-  DCN_CUDA(cudaMemsetAsync(xt + (size_t)g.N * g.HW * g.C, 0, (size_t)g.C * sizeof(float), stream),
-           "memset");
+  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
+  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
+           "nchw_to_nhwc");
   if (tc_bwd) {
     const bool split = split_math(flags);
     const size_t parts = split ? 2 : 1;
@@ -401,7 +402,8 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     const bool colp = use_col_path(g, flags);
     float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
-    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r, nullptr, stream),
+    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r,
+                                    bias_in_prep ? grad_bias : nullptr, stream),
              "tc_prep_go");
     DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, stream), "tc_pack_weight_bwd");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,

@@ -335,20 +335,23 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
 }
 
 // Packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = tf32(W[g*Og+o][c][k]);
-// with `split`, rows outC .. 2*outC-1 hold the low parts tf32(W - hi).
-__global__ void tc_pack_weight_kernel(const float* __restrict__ w, float* __restrict__ wt,
-                                      Geom g, int split) {
+// with `split`, rows outC .. 2*outC-1 hold the low parts tf32(W - hi).  One
+// block per out channel: the (Cg x kk) row is read through L1 and written
+// tap-major with coalesced stores.
+__global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __restrict__ w,
+                                                             float* __restrict__ wt, Geom g,
+                                                             int split) {
   const int Kpad = g.kk * g.Cg;
-  const long long total = (long long)g.outC * Kpad;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int kc = (int)(i % Kpad);
-    const long long oc = i / Kpad;
-    const int k = kc / g.Cg, c = kc - k * g.Cg;
-    const float v = w[(oc * g.Cg + c) * g.kk + k];
+  const long long oc = blockIdx.x;
+  const float* src = w + oc * Kpad;
+  float* dst = wt + oc * Kpad;
+  const long long lo = (long long)g.outC * Kpad;
+  for (int j = threadIdx.x; j < Kpad; j += blockDim.x) {
+    const int k = j / g.Cg, c = j - k * g.Cg;
+    const float v = __ldg(src + c * g.kk + k);
     const float hi = tc::to_tf32(v);
-    wt[i] = hi;
-    if (split) wt[total + i] = tc::to_tf32(v - hi);
+    dst[j] = hi;
+    if (split) dst[lo + j] = tc::to_tf32(v - hi);
   }
 }
 
@@ -366,11 +369,8 @@ size_t tc_fwd_weight_bytes(const Geom& g, bool split) {
 
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
                                   cudaStream_t stream) {
-  const long long total = (long long)g.outC * g.kk * g.Cg;
-  if (total == 0) return cudaSuccess;
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  tc_pack_weight_kernel<<<(int)blocks, 256, 0, stream>>>(w, wt, g, split ? 1 : 0);
+  if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
+  tc_pack_weight_kernel<<<g.outC, 256, 0, stream>>>(w, wt, g, split ? 1 : 0);
   return cudaGetLastError();
 }
 

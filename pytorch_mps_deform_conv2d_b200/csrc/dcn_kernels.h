@@ -10,9 +10,11 @@
 namespace dcn {
 
 // ---- layout kernels (dcn_layout.cu) --------------------------------------
-// x (N, C, H, W) -> xt (N, H, W, C)
+// x (N, C, H, W) -> xt (N, H, W, C).  `zero_row`: also zeroes the C floats
+// after xt (the zero pixel row the gathers read for dropped corners);
+// `zero_like` (NULL or an (N, H, W, C) buffer) is zeroed in the same pass.
 cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
-                                cudaStream_t stream);
+                                bool zero_row, float* zero_like, cudaStream_t stream);
 // gxt (N, H, W, C) -> gx (N, C, H, W)
 cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
                                 cudaStream_t stream);
@@ -26,9 +28,23 @@ cudaError_t launch_pack_weight_bwd(const float* w, float* wb, const Geom& g,
 // out[n, o, p] = bias[o] (0 when bias is NULL); the C == 0 forward
 cudaError_t launch_fill_bias(float* out, const float* bias, const Geom& g,
                              cudaStream_t stream);
-// grad_bias[o] = sum_{n,p} grad_out[n, o, p]
+// grad_bias[o] = sum_{n,p} grad_out[n, o, p] (written, not accumulated)
 cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
                              cudaStream_t stream);
+// Zeroes up to four fp32 buffers with one launch.
+struct ZeroList {
+  float* ptr[4];
+  long long n[4];
+  int count;
+  void add(float* p, long long count_) {
+    if (p != nullptr && count_ > 0) {
+      ptr[count] = p;
+      n[count] = count_;
+      ++count;
+    }
+  }
+};
+cudaError_t launch_zero(const ZeroList& z, cudaStream_t stream);
 
 // ---- fp32 SIMT kernels (dcn_simt.cu) --------------------------------------
 // Forward, fp32 FFMA.  `xt` is the NHWC copy of the input.

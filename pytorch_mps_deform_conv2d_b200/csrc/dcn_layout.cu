@@ -10,11 +10,28 @@ namespace {
 
 constexpr int TT = 32;  // transpose tile
 
+// Extras of a transpose launch: `zout` (same shape as the output, or NULL)
+// is zeroed tile by tile alongside; `tail` (NULL or `tail_n` floats) is
+// zeroed by the first block.
+struct TransposeExtras {
+  float* zout;
+  float* tail;
+  int tail_n;
+};
+
+__device__ __forceinline__ void zero_tail(const TransposeExtras& ex) {
+  if (ex.tail != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+    const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+    for (int i = tid; i < ex.tail_n; i += blockDim.x * blockDim.y) ex.tail[i] = 0.f;
+  }
+}
+
 // in (N, R, S) -> out (N, S, R); one 32x32 tile per block, 32x8 threads.
 __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ in,
                                                         float* __restrict__ out,
-                                                        int R, int S) {
+                                                        int R, int S, TransposeExtras ex) {
   __shared__ float tile[TT][TT + 1];
+  zero_tail(ex);
   const int n = blockIdx.z;
   const int r0 = blockIdx.y * TT, s0 = blockIdx.x * TT;
   const float* src = in + (long long)n * R * S;
@@ -29,15 +46,20 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
 #pragma unroll
   for (int i = 0; i < TT; i += 8) {
     const int s = s0 + ty + i, r = r0 + tx;
-    if (r < R && s < S) dst[(long long)s * R + r] = tile[tx][ty + i];
+    if (r < R && s < S) {
+      dst[(long long)s * R + r] = tile[tx][ty + i];
+      if (ex.zout) ex.zout[(long long)n * R * S + (long long)s * R + r] = 0.f;
+    }
   }
 }
 
 // Same transpose with 64 x 64 tiles and 16-byte loads and stores; needs R and
 // S multiples of 4 and 16-byte aligned buffers.
 __global__ void __launch_bounds__(256) transpose4_kernel(const float* __restrict__ in,
-                                                         float* __restrict__ out, int R, int S) {
+                                                         float* __restrict__ out, int R, int S,
+                                                         TransposeExtras ex) {
   __shared__ float tile[64][65];
+  zero_tail(ex);
   const int n = blockIdx.z;
   const int r0 = blockIdx.y * 64, s0 = blockIdx.x * 64;
   const float* src = in + (long long)n * R * S;
@@ -65,21 +87,29 @@ __global__ void __launch_bounds__(256) transpose4_kernel(const float* __restrict
       v.z = tile[tx * 4 + 2][ty + 16 * i];
       v.w = tile[tx * 4 + 3][ty + 16 * i];
       *reinterpret_cast<float4*>(dst + (long long)s * R + r) = v;
+      if (ex.zout)
+        *reinterpret_cast<float4*>(ex.zout + (long long)n * R * S + (long long)s * R + r) =
+            make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
 }
 
 cudaError_t launch_transpose(const float* in, float* out, int N, int R, int S,
-                             cudaStream_t stream) {
-  if ((long long)N * R * S == 0) return cudaSuccess;
+                             const TransposeExtras& ex, cudaStream_t stream) {
+  if ((long long)N * R * S == 0) {
+    if (ex.tail != nullptr && ex.tail_n > 0)
+      return cudaMemsetAsync(ex.tail, 0, (size_t)ex.tail_n * sizeof(float), stream);
+    return cudaSuccess;
+  }
   const bool vec = R % 4 == 0 && S % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 15u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && ceil_div(R, 64) <= 65535;
+                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(ex.zout) & 15u) == 0 && ceil_div(R, 64) <= 65535;
   if (vec) {
     dim3 grid(ceil_div(S, 64), ceil_div(R, 64), N);
-    transpose4_kernel<<<grid, 256, 0, stream>>>(in, out, R, S);
+    transpose4_kernel<<<grid, 256, 0, stream>>>(in, out, R, S, ex);
   } else {
     dim3 grid(ceil_div(S, TT), ceil_div(R, TT), N);
-    transpose_kernel<<<grid, dim3(TT, 8), 0, stream>>>(in, out, R, S);
+    transpose_kernel<<<grid, dim3(TT, 8), 0, stream>>>(in, out, R, S, ex);
   }
   return cudaGetLastError();
 }
@@ -118,22 +148,24 @@ __global__ void pack_weight_bwd_kernel(const float* __restrict__ w,
   }
 }
 
-// grad_bias: block (o, n) sums grad_out[n, o, :] (16-byte loads when the
-// row allows it) and adds it into the zeroed grad_bias.
+// grad_bias: block o sums grad_out[:, o, :] (16-byte loads when the rows
+// allow it) and writes grad_bias[o]; no atomics, no pre-zeroing.
 template <bool VEC>
 __global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict__ go,
                                                         float* __restrict__ gb, Geom g) {
-  const int o = blockIdx.x, n = blockIdx.y;
-  const float* row = go + ((long long)n * g.outC + o) * g.P;
+  const int o = blockIdx.x;
   float s = 0.f;
-  if (VEC) {
-    const float4* r4 = reinterpret_cast<const float4*>(row);
-    for (int i = threadIdx.x; i < (g.P >> 2); i += blockDim.x) {
-      const float4 v = __ldg(r4 + i);
-      s += (v.x + v.y) + (v.z + v.w);
+  for (int n = 0; n < g.N; ++n) {
+    const float* row = go + ((long long)n * g.outC + o) * g.P;
+    if (VEC) {
+      const float4* r4 = reinterpret_cast<const float4*>(row);
+      for (int i = threadIdx.x; i < (g.P >> 2); i += blockDim.x) {
+        const float4 v = __ldg(r4 + i);
+        s += (v.x + v.y) + (v.z + v.w);
+      }
+    } else {
+      for (int i = threadIdx.x; i < g.P; i += blockDim.x) s += __ldg(row + i);
     }
-  } else {
-    for (int i = threadIdx.x; i < g.P; i += blockDim.x) s += __ldg(row + i);
   }
   __shared__ float red[32];
 #pragma unroll
@@ -144,7 +176,21 @@ __global__ void __launch_bounds__(256) grad_bias_kernel(const float* __restrict_
     s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
-    if (threadIdx.x == 0) atomicAdd(gb + o, s);
+    if (threadIdx.x == 0) gb[o] = s;
+  }
+}
+
+// Zeroes up to four buffers in one launch (16-byte stores where aligned).
+__global__ void __launch_bounds__(256) zero_kernel(ZeroList z) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  for (int b = 0; b < z.count; ++b) {
+    float* p = z.ptr[b];
+    const long long n = z.n[b];
+    const long long n4 = (reinterpret_cast<uintptr_t>(p) & 15u) == 0 ? n >> 2 : 0;
+    float4* p4 = reinterpret_cast<float4*>(p);
+    for (long long i = t0; i < n4; i += stride) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long i = (n4 << 2) + t0; i < n; i += stride) p[i] = 0.f;
   }
 }
 
@@ -168,13 +214,25 @@ int grid_for(long long total) {
 }  // namespace
 
 cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
-                                cudaStream_t stream) {
-  return launch_transpose(x, xt, N, C, HW, stream);
+                                bool zero_row, float* zero_like, cudaStream_t stream) {
+  TransposeExtras ex{zero_like, zero_row ? xt + (long long)N * HW * C : nullptr, C};
+  return launch_transpose(x, xt, N, C, HW, ex, stream);
 }
 
 cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
                                 cudaStream_t stream) {
-  return launch_transpose(gxt, gx, N, HW, C, stream);
+  return launch_transpose(gxt, gx, N, HW, C, TransposeExtras{nullptr, nullptr, 0}, stream);
+}
+
+cudaError_t launch_zero(const ZeroList& z, cudaStream_t stream) {
+  long long most = 0;
+  for (int b = 0; b < z.count; ++b) most = z.n[b] > most ? z.n[b] : most;
+  if (most == 0) return cudaSuccess;
+  long long blocks = (most / 4 + 255) / 256;
+  if (blocks > 148LL * 8) blocks = 148LL * 8;
+  if (blocks < 1) blocks = 1;
+  zero_kernel<<<(int)blocks, 256, 0, stream>>>(z);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pack_weight_fwd(const float* w, float* wf, const Geom& g, int cpad,
@@ -204,12 +262,10 @@ cudaError_t launch_fill_bias(float* out, const float* bias, const Geom& g,
 cudaError_t launch_grad_bias(const float* go, float* gb, const Geom& g,
                              cudaStream_t stream) {
   if (g.outC == 0) return cudaSuccess;
-  cudaError_t e = cudaMemsetAsync(gb, 0, (size_t)g.outC * sizeof(float), stream);
-  if (e != cudaSuccess) return e;
-  if ((long long)g.N * g.P == 0) return cudaSuccess;
-  if (g.N > 65535) return cudaErrorInvalidValue;
+  if ((long long)g.N * g.P == 0)
+    return cudaMemsetAsync(gb, 0, (size_t)g.outC * sizeof(float), stream);
   const bool vec = (g.P % 4 == 0) && ((reinterpret_cast<uintptr_t>(go) & 15u) == 0);
-  dim3 grid(g.outC, g.N);
+  dim3 grid(g.outC);
   if (vec)
     grad_bias_kernel<true><<<grid, 256, 0, stream>>>(go, gb, g);
   else

@@ -29,9 +29,11 @@ bool tc_bwd_supported(const Geom& g);
 // copies: go_t and go_r (tf32-rounded grad_out, pixel-major and NCHW) and the
 // packed weight.
 size_t tc_bwd_scratch_bytes(const Geom& g);
-// go -> go_t / go_r (tf32-rounded); also sums grad_bias into `gb` (zeroed by
-// the caller) when it is not NULL.  With `go_t_lo` (3xTF32) the low TF32
+// go -> go_t / go_r (tf32-rounded).  With `go_t_lo` (3xTF32) the low TF32
 // parts go to go_t_lo and to a second copy of go_r's rows after the first.
+// When tc_prep_sums_bias(g, go), `gb` (NULL or grad_bias, zeroed by the
+// caller) also receives the bias gradient; otherwise `gb` must be NULL.
+bool tc_prep_sums_bias(const Geom& g, const float* go);
 cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
                               float* go_r, float* gb, cudaStream_t stream);
 cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g, bool split,
