@@ -40,6 +40,8 @@ def load_ops():
             if not os.path.exists(TORCH_LIB_PATH):
                 raise _missing(TORCH_LIB_PATH)
             torch.ops.load_library(TORCH_LIB_PATH)
+            from . import _registrations
+            _registrations.register()
             _ops_loaded = True
     return torch.ops.deform_conv2d_b200
 

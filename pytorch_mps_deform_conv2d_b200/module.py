@@ -13,6 +13,7 @@ from typing import Optional
 import torch
 from torch import Tensor, nn
 
+from . import _native
 from .ops import _pair, deform_conv2d
 
 
@@ -39,6 +40,12 @@ class DeformConv2d(nn.Module):
         else:
             self.register_parameter("bias", None)
         self.reset_parameters()
+        # Load the operator library now, outside any torch.compile trace; a
+        # missing library raises at the first forward instead.
+        try:
+            _native.load_ops()
+        except _native.NativeLibraryError:
+            pass
 
     def reset_parameters(self) -> None:
         # kaiming_uniform_(a=sqrt(5)) and a uniform bias in +-1/sqrt(fan_in),

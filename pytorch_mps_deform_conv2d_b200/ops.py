@@ -63,6 +63,15 @@ def _flags(flags: Optional[int]) -> int:
     return -1 if _math_override is None else _math_override
 
 
+def _ops():
+    """``torch.ops.deform_conv2d_b200``; loads the library on first use.  The
+    loaded case reads one flag and takes no lock, so torch.compile traces
+    through it without a graph break."""
+    if _native._ops_loaded:
+        return torch.ops.deform_conv2d_b200
+    return _native.load_ops()
+
+
 def _pair(x) -> Tuple[int, int]:
     if isinstance(x, (tuple, list)):
         return int(x[0]), int(x[1])
@@ -79,7 +88,7 @@ class _DeformConv2dFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, input, weight, offset, mask, bias, stride, padding,
                 dilation, groups, deformable_groups, flags):
-        ops = _native.load_ops()
+        ops = _ops()
         empty = input.new_empty(0)
         out = ops.deform_conv2d_forward(
             input, weight, offset, mask if mask is not None else empty, bias,
@@ -97,7 +106,7 @@ class _DeformConv2dFunction(torch.autograd.Function):
         stride, padding, dilation, groups, deformable_groups, flags = ctx.params
         has_mask = mask.numel() > 0
         has_bias = bias.numel() > 0
-        ops = _native.load_ops()
+        ops = _ops()
         grad_input, grad_offset, grad_mask, grad_weight, grad_bias = \
             ops.deform_conv2d_backward(
                 grad_output.contiguous(), input, weight, offset, mask,
