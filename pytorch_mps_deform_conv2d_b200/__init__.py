@@ -4,9 +4,14 @@ Drop-in for the public API of ilirium/pytorch_mps_deform_conv2d
 (``deform_conv2d``, ``DeformConv2d``), itself the API of torchvision.ops:
 
     from pytorch_mps_deform_conv2d_b200 import deform_conv2d, DeformConv2d
+
+or, for code that calls torchvision directly, ``patch_torchvision()`` routes
+``torchvision.ops.deform_conv2d`` / ``DeformConv2d`` on CUDA tensors here.
 """
 from .ops import deform_conv2d, get_math_mode, set_math_mode
 from .module import DeformConv2d
+from .torchvision_patch import patch_torchvision, unpatch_torchvision
 
-__all__ = ["deform_conv2d", "DeformConv2d", "set_math_mode", "get_math_mode"]
+__all__ = ["deform_conv2d", "DeformConv2d", "set_math_mode", "get_math_mode",
+           "patch_torchvision", "unpatch_torchvision"]
 __version__ = "0.1.0"
