@@ -189,23 +189,25 @@ size_t data_smem_bytes(bool split) {
   return (size_t)stages * parts * D_STAGE + (size_t)epi * EPI_WARP_BYTES + 128 + 1024;
 }
 
-// A tile is (128 pixels, 128 channels, group, range of taps); the taps are
-// independent in this kernel, so splitting them evens out the CTAs' loads.
+// The packed weight of a group is kk*Cg rows ordered (tap, channel); a
+// "slot" is 128 consecutive rows of it: 128 channels of one tap when
+// Cg % 128 == 0, or 128 / Cg whole taps when Cg is 32 or 64 (the last slot
+// of a group may reach past its last tap; those columns are not used).  A
+// tile is (128 pixels, group, range of slots); slots are independent here,
+// so splitting them evens out the CTAs' loads.
 struct DTile {
   long long q0;
-  int c0, gi, k0, k1;
+  int gi, s0, s1;
 };
-__device__ __forceinline__ DTile dtile_of(int t, int mtiles, int ctiles, int ksplits, int kk) {
+__device__ __forceinline__ DTile dtile_of(int t, int mtiles, int nslots, int ksplits) {
   DTile T;
   const int ks = t % ksplits;
-  int r = t / ksplits;
+  const int r = t / ksplits;
   const int mt = r % mtiles;
-  r /= mtiles;
   T.q0 = (long long)mt * D_BM;
-  T.c0 = (r % ctiles) * D_BN;
-  T.gi = r / ctiles;
-  T.k0 = ks * kk / ksplits;
-  T.k1 = (ks + 1) * kk / ksplits;
+  T.gi = r / mtiles;
+  T.s0 = ks * nslots / ksplits;
+  T.s1 = (ks + 1) * nslots / ksplits;
   return T;
 }
 
@@ -359,7 +361,7 @@ template <bool SPLIT>
 __global__ void __launch_bounds__(DCfg<SPLIT>::THREADS, 1)
 bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
                    const __grid_constant__ CUtensorMap amap_lo,
-                   const __grid_constant__ CUtensorMap bmap, int mtiles, int ctiles, int ksplits,
+                   const __grid_constant__ CUtensorMap bmap, int mtiles, int nslots, int ksplits,
                    int ntiles,
                    const float* __restrict__ xt, const float* __restrict__ off,
                    const float* __restrict__ mask, float* __restrict__ gxt,
@@ -407,9 +409,9 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     if (lane == 0) {
       int gs = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
-        for (int k = T.k0; k < T.k1; ++k) {
-          const int brow = (T.gi * g.kk + k) * g.Cg + T.c0;
+        const DTile T = dtile_of(t, mtiles, nslots, ksplits);
+        for (int sl = T.s0; sl < T.s1; ++sl) {
+          const int brow = T.gi * g.kk * g.Cg + sl * D_BN;
           for (int s = 0; s < ochunks; ++s, ++gs) {
             const int st = gs % D_STAGES;
             const int u = gs / D_STAGES;
@@ -433,8 +435,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
       const uint32_t idesc = tc::idesc_tf32(D_BM, D_BN);
       int gs = 0, gt = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
-        for (int k = T.k0; k < T.k1; ++k, ++gt) {
+        const DTile T = dtile_of(t, mtiles, nslots, ksplits);
+        for (int sl = T.s0; sl < T.s1; ++sl, ++gt) {
           const int acc = gt & 1;
           if (gt >= 2) tc::mbar_wait(&acc_empty[acc], ((gt >> 1) - 1) & 1, &g_tc_bwd_status);
           tc::tc_fence_after();
@@ -472,12 +474,12 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     unsigned char* scratch = epi + e * EPI_WARP_BYTES;
     int gt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const DTile T = dtile_of(t, mtiles, ctiles, ksplits, g.kk);
+      const DTile T = dtile_of(t, mtiles, nslots, ksplits);
       const long long qbase = T.q0 + lq * 32;
       const long long row_q = qbase + lane;
       const long long col_lo = SPLIT ? (long long)g.kk * g.NP * g.C : 0;
       int plan_key = -1;
-      for (int k = T.k0; k < T.k1; ++k, ++gt) {
+      for (int sl = T.s0; sl < T.s1; ++sl, ++gt) {
         const int acc = gt & 1;
         tc::mbar_wait(&acc_full[acc], (gt >> 1) & 1, &g_tc_bwd_status);
         tc::tc_fence_after();
@@ -500,10 +502,13 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
           if (cc == CPW - 1) {
             tc::tc_fence_before();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for tap + 2
+            if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // accumulator free for slot + 2
           }
-          epilogue_chunk(g, k, vals, T.gi * g.Cg + T.c0 + chunk * 32, row_q, qbase, lane,
-                         scratch, xt, off, mask, gxt, goff, gmask, col, col_lo, plan_key);
+          const int row = sl * D_BN + chunk * 32;  // (tap, channel) row within the group
+          const int k = row / g.Cg;
+          if (k < g.kk)
+            epilogue_chunk(g, k, vals, T.gi * g.Cg + (row - k * g.Cg), row_q, qbase, lane,
+                           scratch, xt, off, mask, gxt, goff, gmask, col, col_lo, plan_key);
         }
       }
     }
@@ -862,15 +867,35 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
 //              and bn go_r rows
 // Rows of a K step past an image's last pixel read the next pixels' columns;
 // their go_r columns are zero (padding / out of range), so they add nothing.
+// The M side is a 128-row slot of the group's (tap, channel) rows, as in
+// bwd_data_tc: 128 channels of one tap, or 128 / Cg taps of 32 or 64
+// channels; rows past the last tap are computed and dropped.
 // ---------------------------------------------------------------------------
 constexpr int WC_THREADS = 192;
 constexpr int WC_MMA_WARP = 4, WC_TMA_WARP = 5;
+
+struct WCTile {
+  int slot, o0, gi, t_begin, t_end;
+};
+__device__ __forceinline__ WCTile wctile_of(int t, int nslots, int ntn, int splits, int per,
+                                            int total_chunks, int bn) {
+  WCTile T;
+  const int sp = t % splits;
+  int r = t / splits;
+  T.o0 = (r % ntn) * bn;
+  r /= ntn;
+  T.slot = r % nslots;
+  T.gi = r / nslots;
+  T.t_begin = sp * per;
+  T.t_end = min(total_chunks, T.t_begin + per);
+  return T;
+}
 
 template <bool SPLIT>
 __global__ void __launch_bounds__(WC_THREADS, 1)
 bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
                       const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
-                      float* __restrict__ gw, int mtiles, int ntn, int splits, int per,
+                      float* __restrict__ gw, int nslots, int ntn, int splits, int per,
                       int ntiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
@@ -915,8 +940,15 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
       const int lo_rows = g.kk * (int)g.NP;  // row offset of the low parts
       int gs = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
-        const int x0 = T.gi * g.Cg + T.cm0;
+        const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
+        // the four 32-row blocks of the slot: (tap, channel) of each
+        int bk[4], bx[4];
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) {
+          const int row = T.slot * 128 + mb * 32;
+          bk[mb] = row / g.Cg;
+          bx[mb] = T.gi * g.Cg + (row - bk[mb] * g.Cg);
+        }
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
           const int st = gs % STAGES;
           const int u = gs / STAGES;
@@ -924,13 +956,15 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
           const int p0 = (tt - n * pchunks) << 5;
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
           tc::mbar_arrive_expect_tx(&full[st], PARTS * (W2_A_STAGE + b_stage));
-          const int y = T.k * (int)g.NP + n * g.P + p0;
           const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE;
 #pragma unroll
           for (int mb = 0; mb < 4; ++mb) {
-            tc::tma_load_2d(sA + mb * W_LBO, &colmap, x0 + mb * 32, y, &full[st]);
+            // a block past the last tap reads rows beyond the plane (zero fill, or
+            // the low plane in 3xTF32); its accumulator rows are dropped
+            const int y = bk[mb] * (int)g.NP + n * g.P + p0;
+            tc::tma_load_2d(sA + mb * W_LBO, &colmap, bx[mb], y, &full[st]);
             if constexpr (SPLIT)
-              tc::tma_load_2d(sA + W2_A_STAGE + mb * W_LBO, &colmap, x0 + mb * 32, lo_rows + y,
+              tc::tma_load_2d(sA + W2_A_STAGE + mb * W_LBO, &colmap, bx[mb], lo_rows + y,
                               &full[st]);
           }
           const int row = n * g.outC + T.gi * g.Og + T.o0;
@@ -947,7 +981,7 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
       const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
       int gs = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+        const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
         if (T.t_begin >= T.t_end) continue;
         const int acc = it & 1;
         if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_bwd_status);
@@ -983,21 +1017,25 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
   } else {
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
+      const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
       if (T.t_begin >= T.t_end) continue;
       const int acc = it & 1;
       tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
       tc::tc_fence_after();
-      const int c = T.cm0 + warp * 32 + lane;  // channel within the group
-      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + T.k;
+      const int row = T.slot * 128 + warp * 32 + lane;  // (tap, channel) row of the group
+      const int k = row / g.Cg, c = row - k * g.Cg;
+      const bool live = k < g.kk;
+      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + k;
       const long long ostride = (long long)g.Cg * g.kk;
       const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
       for (int cb = 0; cb < bn; cb += 8) {
         float vv[8];
         tc::tmem_ld8(ta + (uint32_t)cb, vv);
         tc::tmem_ld_wait();
+        if (live) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
+          for (int j = 0; j < 8; ++j) red_add_f32(dst + (long long)(cb + j) * ostride, vv[j]);
+        }
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -1048,6 +1086,9 @@ __global__ void __launch_bounds__(256) tc_pack_weight_bwd_kernel(const float* __
 }
 
 int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
+// 128-row slots of a group's (tap, channel) rows (= kk * Cg / 128 when
+// Cg % 128 == 0)
+int weight_slots(const Geom& g) { return (g.kk * g.Cg + 127) / 128; }
 
 // Tiles of the weight-gradient kernels and their pixel-range splits: the
 // split count minimises the busiest CTA's time, modelled as rounds of tiles x
@@ -1059,9 +1100,9 @@ struct WSplit {
 };
 WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
   WSplit w;
-  w.mtiles = g.Cg / W_BM;
+  w.mtiles = g.Cg / W_BM;  // 128-channel tiles per tap (gather kernel)
   w.ntn = g.Og / bn;
-  const long long base = (long long)g.kk * w.mtiles * w.ntn * g.G;
+  const long long base = (long long)weight_slots(g) * w.ntn * g.G;
   const int pchunks = (g.P + 31) / 32;
   const int total_chunks = g.N * pchunks;
   const long long max_splits = (total_chunks + 7) / 8 > 0 ? (total_chunks + 7) / 8 : 1;
@@ -1083,17 +1124,14 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
 }  // namespace
 
 bool tc_bwd_supported(const Geom& g) {
+  // channels per group: a multiple of 128, or 32 / 64 (slots of several taps)
   return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
-         (g.Og <= 256 || g.Og % 256 == 0) && g.Cg % W_BM == 0 && g.NP > 0 &&
-         (long long)g.N * g.HW * g.C + g.C < (1LL << 31) &&
+         (g.Og <= 256 || g.Og % 256 == 0) && (g.Cg % W_BM == 0 || W_BM % g.Cg == 0) &&
+         g.NP > 0 && (long long)g.N * g.HW * g.C + g.C < (1LL << 31) &&
          (long long)g.N * 2 * g.dg * g.kk * g.P < (1LL << 31);
 }
 
-size_t tc_bwd_scratch_bytes(const Geom& g) {
-  // go_t + go_r (rows padded to a multiple of 4 pixels) + packed weight
-  return (size_t)g.N * g.outC * (g.P + ((g.P + 3) & ~3)) * sizeof(float) +
-         (size_t)g.outC * g.Cg * g.kk * sizeof(float);
-}
+bool tc_wgather_supported(const Geom& g) { return tc_bwd_supported(g) && g.Cg % W_BM == 0; }
 
 bool tc_prep_sums_bias(const Geom& g, const float* go) {
   return g.P % 4 == 0 && g.outC % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
@@ -1152,14 +1190,14 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int mtiles = (int)((g.NP + D_BM - 1) / D_BM);
-  const int ctiles = g.Cg / D_BN;
-  const long long base = (long long)mtiles * ctiles * g.G;
-  // split the taps so the busiest CTA carries the fewest taps
+  const int nslots = (g.kk * g.Cg + D_BN - 1) / D_BN;
+  const long long base = (long long)mtiles * g.G;
+  // split the slots so the busiest CTA carries the fewest
   int ksplits = 1;
   long long best = -1;
-  for (int ks = 1; ks <= g.kk; ++ks) {
+  for (int ks = 1; ks <= nslots; ++ks) {
     const long long rounds = (base * ks + sms - 1) / sms;
-    const long long cost = rounds * ((g.kk + ks - 1) / ks);
+    const long long cost = rounds * ((nslots + ks - 1) / ks);
     if (best < 0 || cost < best) {
       best = cost;
       ksplits = ks;
@@ -1168,7 +1206,7 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go
   const long long ntiles = base * ksplits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < sms ? ntiles : sms);
-  kern<<<grid, threads, smem, stream>>>(g, amap, amap_lo, bmap, mtiles, ctiles, ksplits,
+  kern<<<grid, threads, smem, stream>>>(g, amap, amap_lo, bmap, mtiles, nslots, ksplits,
                                          (int)ntiles, xt, off, mask, gxt, goff, gmask, col);
   return cudaGetLastError();
 }
@@ -1186,6 +1224,7 @@ cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, 
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
                                  const void* plans, float* gw, bool split, int num_sms,
                                  cudaStream_t stream) {
+  if (!tc_wgather_supported(g)) return cudaErrorInvalidValue;
   const int bn = weight_bn(g);
   const int Ppad = (g.P + 3) & ~3;
   CUtensorMap gomap;
@@ -1235,8 +1274,9 @@ cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* 
   const WSplit w = weight_split(g, bn, num_sms, 16);
   if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(w.ntiles < num_sms ? w.ntiles : num_sms);
-  kern<<<grid, WC_THREADS, smem, stream>>>(g, colmap, gomap, bn, pow2_cols(2 * bn), gw, w.mtiles,
-                                            w.ntn, w.splits, w.per, (int)w.ntiles);
+  kern<<<grid, WC_THREADS, smem, stream>>>(g, colmap, gomap, bn, pow2_cols(2 * bn), gw,
+                                            weight_slots(g), w.ntn, w.splits, w.per,
+                                            (int)w.ntiles);
   return cudaGetLastError();
 }
 

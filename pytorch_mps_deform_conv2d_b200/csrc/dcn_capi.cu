@@ -209,15 +209,17 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
   return b + kAlign;  // slack for aligning the caller's base pointer
 }
 
-bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
-  return tc_math(flags) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
-         dcn::tc_bwd_supported(g);
+// Tensor-core backward with the column buffer (weight gradient as a dense
+// GEMM over the columns the grad-column kernel writes); DCN_ALGO_TC_GATHER_WEIGHT
+// asks for the gather-based weight gradient where that kernel covers the shape.
+bool use_col_path(const dcn::Geom& g, uint32_t flags) {
+  return dcn::tc_wcol_supported(g, split_math(flags)) &&
+         (!(flags & DCN_ALGO_TC_GATHER_WEIGHT) || !dcn::tc_wgather_supported(g));
 }
 
-// Tensor-core backward with the column buffer (weight gradient as a dense
-// GEMM over the columns the grad-column kernel writes).
-bool use_col_path(const dcn::Geom& g, uint32_t flags) {
-  return !(flags & DCN_ALGO_TC_GATHER_WEIGHT) && dcn::tc_wcol_supported(g, split_math(flags));
+bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
+  return tc_math(flags) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
+         dcn::tc_bwd_supported(g) && (use_col_path(g, flags) || dcn::tc_wgather_supported(g));
 }
 
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {

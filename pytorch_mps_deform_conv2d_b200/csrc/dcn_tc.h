@@ -23,12 +23,11 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
                           const float* off, const float* mask, const float* bias,
                           float* out, bool split, int num_sms, cudaStream_t stream);
 
-// Whether the tensor-core backward covers this geometry.
+// Whether the tensor-core backward covers this geometry (grad-column kernel
+// and the column-buffer weight gradient), and whether the gather-based
+// weight-gradient kernel does too (128-channel multiples only).
 bool tc_bwd_supported(const Geom& g);
-// Scratch of the tensor-core backward beyond the NHWC input / grad-input
-// copies: go_t and go_r (tf32-rounded grad_out, pixel-major and NCHW) and the
-// packed weight.
-size_t tc_bwd_scratch_bytes(const Geom& g);
+bool tc_wgather_supported(const Geom& g);
 // go -> go_t / go_r (tf32-rounded).  With `go_t_lo` (3xTF32) the low TF32
 // parts go to go_t_lo and to a second copy of go_r's rows after the first.
 // When tc_prep_sums_bias(g, go), `gb` (NULL or grad_bias, zeroed by the

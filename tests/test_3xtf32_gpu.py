@@ -9,7 +9,7 @@ import pytest
 from _util import assert_close, make_case, run_oracle, run_ours
 from pytorch_mps_deform_conv2d_b200 import _native
 from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32
-from test_tf32_gpu import TC_BWD_CASES, TC_CASES, WEIGHT_PATHS
+from test_tf32_gpu import TC_BWD_CASES, TC_CASES, _weight_kernel
 
 pytestmark = pytest.mark.gpu
 
@@ -36,10 +36,10 @@ def test_forward_3xtf32(cuda_device, name):
     assert_close(out, ref, rtol=1e-4, atol=1e-4 * scale, name="out")
 
 
-@pytest.mark.parametrize("path", sorted(WEIGHT_PATHS))
+@pytest.mark.parametrize("path", ["col", "gather"])
 @pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
 def test_backward_3xtf32(cuda_device, name, path):
-    algo, kernel = WEIGHT_PATHS[path]
+    algo, kernel = _weight_kernel(TC_BWD_CASES[name], path)
     case = make_case(upstream="randn", **TC_BWD_CASES[name])
     out, grads, stats = _run_profiled(case, backward=True, algo=algo)
     assert "bwd_data_tc" in stats and kernel in stats, sorted(stats)

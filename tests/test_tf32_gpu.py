@@ -82,7 +82,22 @@ TC_BWD_CASES = {
                                  use_bias=False, offset_scale=3.0, weight_kind="kaiming"),
     "c128-o128-asym-boundary-p70": dict(inC=128, outC=128, H=9, W=14, kh=3, kw=1,
                                     stride=(2, 1), pad=(1, 0), offset_scale=8.0),
+    # 64 / 32 channels per group: 128-row slots of 2 / 4 taps, the last one partial
+    "c64-o64-training-like": dict(N=2, inC=64, outC=64, H=12, W=10, offset_scale=2.0,
+                                  mask_kind="sigmoid", weight_kind="kaiming"),
+    "c128-o64-g2-cg64": dict(inC=128, outC=64, groups=2, H=9, W=11, offset_scale=2.0),
+    "c64-o64-g2-dg2-cg32": dict(inC=64, outC=64, groups=2, dg=2, H=10, W=9, offset_scale=3.0),
+    "c32-o32-k1x3-v1": dict(inC=32, outC=32, kh=1, kw=3, H=8, W=13, pad=(0, 1),
+                            use_mask=False, use_bias=False, offset_scale=2.0),
 }
+
+
+def _weight_kernel(case, path):
+    """Kernel name the weight path runs; the gather kernel covers only
+    128-channel multiples per group, other shapes keep the column buffer."""
+    algo, kernel = WEIGHT_PATHS[path]
+    cg = case["inC"] // case.get("groups", 1)
+    return algo, (kernel if cg % 128 == 0 else "bwd_weight_col")
 
 
 # The two tensor-core weight-gradient kernels: the dense GEMM over the column
@@ -109,7 +124,7 @@ def _grad_errors(case, flags=MATH_TF32):
 @pytest.mark.parametrize("path", sorted(WEIGHT_PATHS))
 @pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
 def test_backward_tf32(cuda_device, name, path):
-    algo, kernel = WEIGHT_PATHS[path]
+    algo, kernel = _weight_kernel(TC_BWD_CASES[name], path)
     stats, out_err, errs, elem = _grad_errors(make_case(upstream="randn", **TC_BWD_CASES[name]),
                                               flags=MATH_TF32 | algo)
     assert "bwd_data_tc" in stats and kernel in stats, sorted(stats)
@@ -120,10 +135,10 @@ def test_backward_tf32(cuda_device, name, path):
 
 
 def test_backward_tf32_uncovered_shape_uses_fp32_kernels(cuda_device):
-    # 64 input channels per group: below the 128-channel tile of the
-    # tensor-core weight gradient, so the fp32 backward kernels run and meet
-    # the fp32 tolerances.
-    case = make_case(inC=64, outC=64, H=9, W=9, upstream="randn")
+    # 96 input channels per group: neither a multiple of 128 nor a divisor of
+    # the 128-row slot, so the fp32 backward kernels run and meet the fp32
+    # tolerances.
+    case = make_case(inC=96, outC=64, H=9, W=9, upstream="randn")
     stats, out_err, errs, elem = _grad_errors(case)
     assert "bwd_data_tc" not in stats and "bwd_data_simt" in stats
     for k, e in errs.items():
