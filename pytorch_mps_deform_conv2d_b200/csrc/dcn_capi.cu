@@ -173,7 +173,7 @@ int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
 
 int fwd_cpad(const dcn::Geom& g) { return dcn::ceil_div(g.Cg, 8) * 8; }
 
-enum class FwdAlgo { kDirect, kGemm, kTc };
+enum class FwdAlgo { kDirect, kGemm, kTc, kDgroup };
 
 // TF32 and 3xTF32 run the tensor-core kernels; 3xTF32 splits every operand.
 bool tc_math(uint32_t flags) {
@@ -186,6 +186,7 @@ FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
   if (flags & DCN_ALGO_SIMT_GEMM) return FwdAlgo::kGemm;
   if (flags & DCN_ALGO_SIMT_DIRECT) return dcn::fwd_direct_supported(g) ? FwdAlgo::kDirect : FwdAlgo::kGemm;
   if (tc_math(flags) && dcn::tc_fwd_supported(g)) return FwdAlgo::kTc;
+  if (dcn::dgroup_supported(g)) return FwdAlgo::kDgroup;
   if (dcn::fwd_direct_supported(g)) return FwdAlgo::kDirect;
   return FwdAlgo::kGemm;
 }
@@ -204,6 +205,7 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
       b += align_up(dcn::tc_fwd_weight_bytes(g, split_math(flags)));
       break;
     case FwdAlgo::kDirect:
+    case FwdAlgo::kDgroup:
       break;
   }
   return b + kAlign;  // slack for aligning the caller's base pointer
@@ -315,6 +317,10 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
                "fwd_simt_direct");
       break;
+    case FwdAlgo::kDgroup:
+      DCN_CUDA(dcn::launch_fwd_dgroup(g, xt, weight, offset, mask, bias, output, stream),
+               "fwd_dgroup");
+      break;
     case FwdAlgo::kGemm: {
       const int cpad = fwd_cpad(g);
       float* wf = ws.take((size_t)g.G * g.kk * cpad * g.Og);
@@ -423,6 +429,13 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
                                          num_sms_current(), stream),
                "bwd_weight_tc");
     }
+    return DCN_OK;
+  }
+  if (dcn::dgroup_supported(g) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT))) {
+    DCN_CUDA(dcn::launch_bwd_dgroup(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
+                                    grad_mask, grad_weight, stream),
+             "bwd_dgroup");
+    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
     return DCN_OK;
   }
   if (dcn::bwd_small_supported(g) && !(flags & DCN_ALGO_SIMT_GEMM)) {

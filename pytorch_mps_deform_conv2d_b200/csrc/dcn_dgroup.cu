@@ -1,0 +1,276 @@
+// dcn_dgroup.cu -- forward and backward for small convolution groups that
+// tile a deformable group: the channels of one deformable group (cpg of them,
+// 4..16) hold GPD whole convolution groups of CG channels and OG out channels
+// each -- e.g. groups=32 with 2 channels each and 4 deformable groups: a
+// deformable group is 16 channels = 8 convolution groups.
+//
+// One thread per (output pixel, deformable group).  Per tap it computes the
+// sampling plan once (deform_conv2d.metal:100-118) and reads the four corner
+// runs of the deformable group's channels with 16-byte loads from the NHWC
+// input (dropped corners read the zero pixel row after it), so every sector
+// fetched is used, instead of each convolution group re-reading the sector
+// for its few channels.
+//  * forward: the OPD = GPD*OG outputs of the pixel, weights in shared memory;
+//  * backward: grad columns (K = OG dot products), col2im as 16-byte vector
+//    reductions into the NHWC grad-input accumulator, the coordinate and mask
+//    gradients of the pixel (its thread owns them: plain stores), and its
+//    grad_weight products reduced over the warp with a transpose-reduce (31
+//    shuffles for 32 values) and over the block in shared memory.
+#include "dcn_kernels.h"
+
+namespace dcn {
+
+namespace {
+
+constexpr int DG_THREADS = 128;
+
+__device__ __forceinline__ float f4at(const float4& v, int e) {
+  return e == 0 ? v.x : (e == 1 ? v.y : (e == 2 ? v.z : v.w));
+}
+
+// Plan of one (pixel, tap, deformable group): element offsets of the four
+// corner pixel rows (the zero row for dropped corners), weights, mask.
+struct CornerPlan {
+  int c[4];
+  Sample s;
+  float m;
+};
+
+__device__ __forceinline__ CornerPlan corner_plan(const Geom& g, const float* __restrict__ off,
+                                                  const float* __restrict__ mask, int n, int p,
+                                                  int oy, int ox, int k, int dgi) {
+  CornerPlan cp;
+  const int ki = k / g.kw, kj = k - ki * g.kw;
+  const long long oi = off_h_index(g, n, dgi, k, p);
+  float h, w;
+  sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+  cp.m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+  cp.s = make_sample(h, w, g.H, g.W);
+  const int zoff = g.N * g.HW * g.C;
+  const int xn = n * g.HW;
+  cp.c[0] = (cp.s.live & 1u) ? (xn + cp.s.i1) * g.C : zoff;
+  cp.c[1] = (cp.s.live & 2u) ? (xn + cp.s.i2) * g.C : zoff;
+  cp.c[2] = (cp.s.live & 4u) ? (xn + cp.s.i3) * g.C : zoff;
+  cp.c[3] = (cp.s.live & 8u) ? (xn + cp.s.i4) * g.C : zoff;
+  return cp;
+}
+
+template <int CG, int OG, int GPD>
+__global__ void __launch_bounds__(DG_THREADS)
+fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict__ w,
+                  const float* __restrict__ off, const float* __restrict__ mask,
+                  const float* __restrict__ bias, float* __restrict__ out) {
+  constexpr int CPG = CG * GPD, OPD = OG * GPD, NQ = CPG / 4;
+  extern __shared__ float ws[];  // [OPD][CG][kk]: out channels dgi*OPD .. of the group
+  const int dgi = blockIdx.y;
+  const int wcount = OPD * CG * g.kk;
+  for (int i = threadIdx.x; i < wcount; i += DG_THREADS) ws[i] = w[(long long)dgi * wcount + i];
+  __syncthreads();
+  const long long q = (long long)blockIdx.x * DG_THREADS + threadIdx.x;
+  if (q >= g.NP) return;
+  const int n = (int)(q / g.P);
+  const int p = (int)(q - (long long)n * g.P);
+  const int oy = p / g.Wo, ox = p - oy * g.Wo;
+  const float* xq = xt + dgi * CPG;
+  float acc[OPD];
+#pragma unroll
+  for (int i = 0; i < OPD; ++i) acc[i] = 0.f;
+  for (int k = 0; k < g.kk; ++k) {
+    const CornerPlan cp = corner_plan(g, off, mask, n, p, oy, ox, k, dgi);
+    if (!cp.s.valid) continue;
+    const float w1 = cp.s.w1 * cp.m, w2 = cp.s.w2 * cp.m, w3 = cp.s.w3 * cp.m,
+                w4 = cp.s.w4 * cp.m;
+#pragma unroll
+    for (int qd = 0; qd < NQ; ++qd) {
+      const float4 a = ldg4(xq + (unsigned)cp.c[0] + 4 * qd);
+      const float4 b = ldg4(xq + (unsigned)cp.c[1] + 4 * qd);
+      const float4 c = ldg4(xq + (unsigned)cp.c[2] + 4 * qd);
+      const float4 d = ldg4(xq + (unsigned)cp.c[3] + 4 * qd);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = w1 * f4at(a, e) + w2 * f4at(b, e) + w3 * f4at(c, e) + w4 * f4at(d, e);
+        const int cl = 4 * qd + e;  // channel within the deformable group
+        const int j = cl / CG, cc = cl - (cl / CG) * CG;
+#pragma unroll
+        for (int o = 0; o < OG; ++o)
+          acc[j * OG + o] = fmaf(ws[((j * OG + o) * CG + cc) * g.kk + k], v, acc[j * OG + o]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < OPD; ++i) {
+    const int oc = dgi * OPD + i;
+    out[((long long)n * g.outC + oc) * g.P + p] = acc[i] + (g.use_bias ? __ldg(bias + oc) : 0.f);
+  }
+}
+
+// Sum of v[0..31] over the warp's lanes, transposed: lane L returns the total
+// of v[L] (16 + 8 + 4 + 2 + 1 shuffles).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    const bool upper = (lane & d) != 0;
+#pragma unroll
+    for (int i = 0; i < d; ++i) {
+      const float send = upper ? v[i] : v[i + d];
+      const float keep = upper ? v[i + d] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+    }
+  }
+  return v[0];
+}
+
+template <int CG, int OG, int GPD>
+__global__ void __launch_bounds__(DG_THREADS)
+bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict__ w,
+                  const float* __restrict__ xt, const float* __restrict__ off,
+                  const float* __restrict__ mask, float* __restrict__ gxt,
+                  float* __restrict__ goff, float* __restrict__ gmask, float* __restrict__ gw) {
+  constexpr int CPG = CG * GPD, OPD = OG * GPD, NQ = CPG / 4, NV = OPD * CG;
+  static_assert(NV <= 32, "one grad_weight value per lane");
+  extern __shared__ float sm[];  // weights [OPD][CG][kk], then grad_weight sums, same layout
+  const int dgi = blockIdx.y;
+  const int wcount = OPD * CG * g.kk;
+  float* ws = sm;
+  float* gws = sm + wcount;
+  for (int i = threadIdx.x; i < wcount; i += DG_THREADS) {
+    ws[i] = w[(long long)dgi * wcount + i];
+    gws[i] = 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long q = (long long)blockIdx.x * DG_THREADS + threadIdx.x;
+  const bool valid = q < g.NP;  // no early exit: the warp reduces together
+  const int n = valid ? (int)(q / g.P) : 0;
+  const int p = valid ? (int)(q - (long long)n * g.P) : 0;
+  const int oy = p / g.Wo, ox = p - oy * g.Wo;
+  float gov[OPD];
+#pragma unroll
+  for (int i = 0; i < OPD; ++i)
+    gov[i] = valid ? __ldg(go + ((long long)n * g.outC + dgi * OPD + i) * g.P + p) : 0.f;
+  const float* xq = xt + dgi * CPG;
+  float* gq = gxt + dgi * CPG;
+  const int zoff = g.N * g.HW * g.C;
+  for (int k = 0; k < g.kk; ++k) {
+    float gwp[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) gwp[i] = 0.f;
+    if (valid) {
+      const CornerPlan cp = corner_plan(g, off, mask, n, p, oy, ox, k, dgi);
+      float s_h = 0.f, s_w = 0.f, s_m = 0.f;
+      if (cp.s.valid) {
+        const float m = cp.m;
+#pragma unroll
+        for (int qd = 0; qd < NQ; ++qd) {
+          const float4 a = ldg4(xq + (unsigned)cp.c[0] + 4 * qd);
+          const float4 b = ldg4(xq + (unsigned)cp.c[1] + 4 * qd);
+          const float4 c = ldg4(xq + (unsigned)cp.c[2] + 4 * qd);
+          const float4 d = ldg4(xq + (unsigned)cp.c[3] + 4 * qd);
+          float top[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int cl = 4 * qd + e;
+            const int j = cl / CG, cc = cl - (cl / CG) * CG;
+            float gc = 0.f;  // grad column (.mm:820-821)
+#pragma unroll
+            for (int o = 0; o < OG; ++o)
+              gc = fmaf(gov[j * OG + o], ws[((j * OG + o) * CG + cc) * g.kk + k], gc);
+            const float A = f4at(a, e), B = f4at(b, e), Cv = f4at(c, e), D = f4at(d, e);
+            s_h += m * coord_dh(cp.s, A, B, Cv, D) * gc;
+            s_w += m * coord_dw(cp.s, A, B, Cv, D) * gc;
+            const float val = bilerp(cp.s, A, B, Cv, D);
+            s_m += gc * val;
+            top[e] = gc * m;
+            const float colv = val * m;
+#pragma unroll
+            for (int o = 0; o < OG; ++o) gwp[(j * OG + o) * CG + cc] = gov[j * OG + o] * colv;
+          }
+          // col2im (deform_conv2d.metal:141-204): dropped corners are skipped
+          const float ws4[4] = {cp.s.w1, cp.s.w2, cp.s.w3, cp.s.w4};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (cp.c[i] == zoff) continue;
+            const float wi = ws4[i];
+            red_add_v4(gq + (unsigned)cp.c[i] + 4 * qd, wi * top[0], wi * top[1], wi * top[2],
+                       wi * top[3]);
+          }
+        }
+      }
+      // this thread owns the pixel's (deformable group, tap) gradients
+      // (col2im_coord, deform_conv2d.metal:225-295)
+      const long long oi = off_h_index(g, n, dgi, k, p);
+      goff[oi] = s_h;
+      goff[oi + g.P] = s_w;
+      if (g.use_mask) gmask[mask_index(g, n, dgi, k, p)] = s_m;
+    }
+    const float tot = warp_transpose_sum32(gwp, lane);
+    if (lane < NV) atomicAdd(&gws[lane * g.kk + k], tot);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < wcount; i += DG_THREADS)
+    red_add_f32(gw + (long long)dgi * wcount + i, gws[i]);
+}
+
+using FwdFn = void (*)(Geom, const float*, const float*, const float*, const float*,
+                       const float*, float*);
+using BwdFn = void (*)(Geom, const float*, const float*, const float*, const float*,
+                       const float*, float*, float*, float*, float*);
+
+struct DgroupEntry {
+  int cg, og, gpd;
+  FwdFn fwd;
+  BwdFn bwd;
+};
+
+#define DG_ENTRY(CG, OG, GPD) \
+  { CG, OG, GPD, fwd_dgroup_kernel<CG, OG, GPD>, bwd_dgroup_kernel<CG, OG, GPD> }
+
+// (channels, out channels) per convolution group x groups per deformable
+// group: 4, 8 or 16 channels per deformable group, <= 32 grad_weight values
+// per pixel.
+const DgroupEntry kDgroup[] = {
+    DG_ENTRY(1, 1, 4), DG_ENTRY(1, 1, 8), DG_ENTRY(1, 1, 16), DG_ENTRY(2, 2, 2),
+    DG_ENTRY(2, 2, 4), DG_ENTRY(2, 2, 8), DG_ENTRY(4, 4, 1),  DG_ENTRY(4, 4, 2),
+    DG_ENTRY(1, 2, 4), DG_ENTRY(1, 2, 8), DG_ENTRY(2, 4, 2),  DG_ENTRY(2, 4, 4),
+};
+
+const DgroupEntry* find_dgroup(const Geom& g) {
+  if (g.cpg % g.Cg != 0 || g.C % 4 != 0) return nullptr;
+  const int gpd = g.cpg / g.Cg;
+  for (const DgroupEntry& e : kDgroup)
+    if (e.cg == g.Cg && e.og == g.Og && e.gpd == gpd) return &e;
+  return nullptr;
+}
+
+}  // namespace
+
+bool dgroup_supported(const Geom& g) {
+  return find_dgroup(g) != nullptr && g.NP > 0 &&
+         (long long)g.N * g.HW * g.C + g.C < (1LL << 31) && g.dg <= 65535;
+}
+
+cudaError_t launch_fwd_dgroup(const Geom& g, const float* xt, const float* w, const float* off,
+                              const float* mask, const float* bias, float* out,
+                              cudaStream_t stream) {
+  if (!dgroup_supported(g)) return cudaErrorInvalidValue;
+  const DgroupEntry* e = find_dgroup(g);
+  dim3 grid((unsigned)((g.NP + DG_THREADS - 1) / DG_THREADS), g.dg);
+  const size_t smem = (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  e->fwd<<<grid, DG_THREADS, smem, stream>>>(g, xt, w, off, mask, bias, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_dgroup(const Geom& g, const float* go, const float* w, const float* xt,
+                              const float* off, const float* mask, float* gxt, float* goff,
+                              float* gmask, float* gw, cudaStream_t stream) {
+  if (!dgroup_supported(g)) return cudaErrorInvalidValue;
+  const DgroupEntry* e = find_dgroup(g);
+  dim3 grid((unsigned)((g.NP + DG_THREADS - 1) / DG_THREADS), g.dg);
+  const size_t smem = 2 * (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  e->bwd<<<grid, DG_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
+  return cudaGetLastError();
+}
+
+}  // namespace dcn

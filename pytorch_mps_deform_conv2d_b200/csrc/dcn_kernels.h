@@ -76,6 +76,19 @@ cudaError_t launch_bwd_small(const Geom& g, const float* go, const float* w, con
                              const float* off, const float* mask, float* gxt, float* goff,
                              float* gmask, float* gw, cudaStream_t stream);
 
+// Small convolution groups tiling a deformable group (dcn_dgroup.cu): one
+// thread per (pixel, deformable group), 16-byte corner loads.  Covered:
+// (Cg, Og) in {(1,1), (2,2), (4,4), (1,2), (2,4)} with 4, 8 or 16 channels
+// per deformable group.  Forward writes `out`; backward accumulates into gxt
+// (NHWC) and gw (pre-zeroed) and writes goff / gmask.
+bool dgroup_supported(const Geom& g);
+cudaError_t launch_fwd_dgroup(const Geom& g, const float* xt, const float* w, const float* off,
+                              const float* mask, const float* bias, float* out,
+                              cudaStream_t stream);
+cudaError_t launch_bwd_dgroup(const Geom& g, const float* go, const float* w, const float* xt,
+                              const float* off, const float* mask, float* gxt, float* goff,
+                              float* gmask, float* gw, cudaStream_t stream);
+
 // ---- single-image building blocks (dcn_debug_ops.cu) ----------------------
 cudaError_t launch_col2im_single(const Geom& g, const float* col, const float* off,
                                  const float* mask, float* grad_im,
