@@ -78,6 +78,13 @@ extern "C" {
 #define DCN_ALGO_SIMT_GEMM 0x100
 #define DCN_ALGO_SIMT_DIRECT 0x200
 #define DCN_ALGO_TC_GATHER_WEIGHT 0x400
+/* Third byte: operand conventions.
+ *   DCN_MASK_LOGITS  `mask` holds logits: the kernels use sigmoid(mask) and
+ *                    dcn_backward's grad_mask is the gradient with respect to
+ *                    the logits -- the DCNv2 block's mask sigmoid fused into
+ *                    the op (no reference counterpart: the reference takes
+ *                    the mask after the sigmoid). */
+#define DCN_MASK_LOGITS 0x10000
 
 /* Geometry of one deformable convolution: the shapes of the reference op's
  * tensors plus its integer arguments. */

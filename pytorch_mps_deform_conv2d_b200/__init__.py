@@ -9,9 +9,9 @@ or, for code that calls torchvision directly, ``patch_torchvision()`` routes
 ``torchvision.ops.deform_conv2d`` / ``DeformConv2d`` on CUDA tensors here.
 """
 from .ops import deform_conv2d, get_math_mode, set_math_mode
-from .module import DeformConv2d
+from .module import DeformConv2d, DeformConv2dPack
 from .torchvision_patch import patch_torchvision, unpatch_torchvision
 
-__all__ = ["deform_conv2d", "DeformConv2d", "set_math_mode", "get_math_mode",
+__all__ = ["deform_conv2d", "DeformConv2d", "DeformConv2dPack", "set_math_mode", "get_math_mode",
            "patch_torchvision", "unpatch_torchvision"]
 __version__ = "0.1.0"

@@ -260,7 +260,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
         wv4 = make_float4(sp.w1, sp.w2, sp.w3, sp.w4);
         geo.x = sp.lh;
         geo.y = sp.lw;
-        geo.z = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+        geo.z = mask_of(g, mask, mask_index(g, n, dgi, k, p));
         idx.x = (int)oi;
         idx.y = (int)mask_index(g, n, dgi, k, p);
       }
@@ -344,7 +344,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
     if (quad == 0 && pidx.x >= 0) {
       red_add_f32(goff + pidx.x, s_h);
       red_add_f32(goff + pidx.x + g.P, s_w);
-      if (g.use_mask) red_add_f32(gmask + pidx.y, s_m);
+      if (g.use_mask) red_add_f32(gmask + pidx.y, s_m * mask_grad_scale(g, plan[px].geo.z));
     }
   }
 }
@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(256) plan_kernel(Geom g, const float* __restri
     const long long oi = off_h_index(g, n, dgi, k, p);
     float h, w;
     sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-    const float m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+    const float m = mask_of(g, mask, mask_index(g, n, dgi, k, p));
     const Sample sp = make_sample(h, w, g.H, g.W);
     int4 o = make_int4(zoff, zoff, zoff, zoff);
     float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);

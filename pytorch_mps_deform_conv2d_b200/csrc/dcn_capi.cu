@@ -165,6 +165,7 @@ int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
   g.G = (int)s->groups; g.dg = (int)s->deformable_groups;
   g.Ho = (int)Ho; g.Wo = (int)Wo;
   g.use_mask = use_mask ? 1 : 0; g.use_bias = use_bias ? 1 : 0;
+  g.mask_logits = 0;
   g.Cg = g.C / g.G; g.Og = g.outC / g.G; g.cpg = g.dg ? g.C / g.dg : 0;
   g.kk = g.kh * g.kw; g.P = g.Ho * g.Wo; g.HW = g.H * g.W;
   g.NP = (long long)g.N * g.P;
@@ -289,6 +290,7 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
   if (rc != DCN_OK) return rc;
+  g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;  // .mm:273: nothing to dispatch
@@ -351,6 +353,7 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
   if (rc != DCN_OK) return rc;
+  g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   DCN_CHECK(mask != nullptr || grad_mask == nullptr,
             "deform_conv2d_backward: grad_mask must be NULL when mask is NULL");
   DCN_CHECK(mask == nullptr || grad_mask != nullptr,

@@ -22,6 +22,7 @@ struct Geom {
   int G, dg;           // groups, deformable groups
   int Ho, Wo;
   int use_mask, use_bias;
+  int mask_logits;     // the mask tensor holds logits: mask = sigmoid(stored)
   // derived
   int Cg, Og;          // channels per group (in / out)
   int cpg;             // channels per deformable group
@@ -93,6 +94,20 @@ __device__ __forceinline__ long long off_h_index(const Geom& g, int n, int dgi, 
 }
 __device__ __forceinline__ long long mask_index(const Geom& g, int n, int dgi, int k, int p) {
   return ((long long)n * g.dg * g.kk + (dgi * g.kk + k)) * g.P + p;
+}
+
+// Mask value of one (image, deformable group, tap, pixel): the stored value,
+// or sigmoid(stored) when the mask tensor holds logits (a DCNv2 block feeding
+// the raw output of its mask convolution); 1 without a mask (DCNv1).
+__device__ __forceinline__ float mask_of(const Geom& g, const float* __restrict__ mask,
+                                         long long i) {
+  if (!g.use_mask) return 1.f;
+  const float v = __ldg(mask + i);
+  return g.mask_logits ? 1.f / (1.f + expf(-v)) : v;
+}
+// d(mask) / d(stored value): 1, or sigmoid'(x) = m (1 - m) for logits.
+__device__ __forceinline__ float mask_grad_scale(const Geom& g, float m) {
+  return g.mask_logits ? m * (1.f - m) : 1.f;
 }
 
 // Vector reduction into global memory (sm_90+): four consecutive fp32

@@ -44,7 +44,7 @@ __device__ __forceinline__ CornerPlan corner_plan(const Geom& g, const float* __
   const long long oi = off_h_index(g, n, dgi, k, p);
   float h, w;
   sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
-  cp.m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+  cp.m = mask_of(g, mask, mask_index(g, n, dgi, k, p));
   cp.s = make_sample(h, w, g.H, g.W);
   const int zoff = g.N * g.HW * g.C;
   const int xn = n * g.HW;
@@ -158,6 +158,7 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
     if (valid) {
       const CornerPlan cp = corner_plan(g, off, mask, n, p, oy, ox, k, dgi);
       float s_h = 0.f, s_w = 0.f, s_m = 0.f;
+      const float mscale = mask_grad_scale(g, cp.m);
       if (cp.s.valid) {
         const float m = cp.m;
 #pragma unroll
@@ -201,7 +202,7 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
       const long long oi = off_h_index(g, n, dgi, k, p);
       goff[oi] = s_h;
       goff[oi + g.P] = s_w;
-      if (g.use_mask) gmask[mask_index(g, n, dgi, k, p)] = s_m;
+      if (g.use_mask) gmask[mask_index(g, n, dgi, k, p)] = s_m * mscale;
     }
     const float tot = warp_transpose_sum32(gwp, lane);
     if (lane < NV) atomicAdd(&gws[lane * g.kk + k], tot);

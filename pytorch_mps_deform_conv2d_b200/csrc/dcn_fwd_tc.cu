@@ -176,7 +176,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
             const long long oi = off_h_index(g, rn[i], dgi, k, rp[i]);
             const float h = (float)(roy[i] * g.sh - g.ph + ki * g.dh) + __ldg(off + oi);
             const float w = (float)(rox[i] * g.sw - g.pw + kj * g.dw) + __ldg(off + oi + g.P);
-            const float m = g.use_mask ? __ldg(mask + mask_index(g, rn[i], dgi, k, rp[i])) : 1.f;
+            const float m = mask_of(g, mask, mask_index(g, rn[i], dgi, k, rp[i]));
             const Sample sp = make_sample(h, w, g.H, g.W);
             if (!sp.valid) continue;
             const int xn = rn[i] * g.HW;

@@ -30,7 +30,7 @@ __device__ __forceinline__ Sample load_sample(const Geom& g, const float* __rest
   const float offh = __ldg(off + oi), offw = __ldg(off + oi + g.P);
   float h, w;
   sample_pos(g, oy, ox, ki, kj, offh, offw, h, w);
-  m = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+  m = mask_of(g, mask, mask_index(g, n, dgi, k, p));
   return make_sample(h, w, g.H, g.W);
 }
 
@@ -413,6 +413,7 @@ bwd_data_simt_kernel(Geom g, const float* __restrict__ go, const float* __restri
             s_m += gc * bilerp(smp, a, b, c, d);
             top[j] = gc * msk;
           }
+          s_m *= mask_grad_scale(g, msk);  // per pixel: scales every lane's partial alike
           float* gbase = gxt_n + gch;
           if (smp.live & 1u)
             red_add_v4(gbase + (long long)smp.i1 * g.C, smp.w1 * top[0], smp.w1 * top[1],
@@ -470,7 +471,9 @@ bwd_data_simt_kernel(Geom g, const float* __restrict__ go, const float* __restri
           const long long oi = off_h_index(g, n, dgi, k, p);
           red_add_f32(goff + oi, msk * coord_dh(smp, a, b, cc, d) * gc);
           red_add_f32(goff + oi + g.P, msk * coord_dw(smp, a, b, cc, d) * gc);
-          if (g.use_mask) red_add_f32(gmask + mask_index(g, n, dgi, k, p), gc * bilerp(smp, a, b, cc, d));
+          if (g.use_mask)
+            red_add_f32(gmask + mask_index(g, n, dgi, k, p),
+                        gc * bilerp(smp, a, b, cc, d) * mask_grad_scale(g, msk));
           const float top = gc * msk;
           float* gbase = gxt_n + gch;
           if (smp.live & 1u) red_add_f32(gbase + (long long)smp.i1 * g.C, smp.w1 * top);
@@ -691,14 +694,15 @@ bwd_small_kernel(Geom g, const float* __restrict__ go, const float* __restrict__
             const long long oi = off_h_index(g, n, cur_dgi, k, p);
             red_add_f32(goff + oi, s_h);
             red_add_f32(goff + oi + g.P, s_w);
-            if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+            if (g.use_mask)
+              red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m * mask_grad_scale(g, msk));
           }
           s_h = s_w = s_m = 0.f;
           cur_dgi = dgi;
           const long long oi = off_h_index(g, n, dgi, k, p);
           float h, wv;
           sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, wv);
-          msk = g.use_mask ? __ldg(mask + mask_index(g, n, dgi, k, p)) : 1.f;
+          msk = mask_of(g, mask, mask_index(g, n, dgi, k, p));
           sp = make_sample(h, wv, g.H, g.W);
         }
         if (!sp.valid) continue;
@@ -730,7 +734,8 @@ bwd_small_kernel(Geom g, const float* __restrict__ go, const float* __restrict__
         const long long oi = off_h_index(g, n, cur_dgi, k, p);
         red_add_f32(goff + oi, s_h);
         red_add_f32(goff + oi + g.P, s_w);
-        if (g.use_mask) red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m);
+        if (g.use_mask)
+          red_add_f32(gmask + mask_index(g, n, cur_dgi, k, p), s_m * mask_grad_scale(g, msk));
       }
     }
   }

@@ -14,7 +14,7 @@ import torch
 from torch import Tensor, nn
 
 from . import _native
-from .ops import _pair, deform_conv2d
+from .ops import _pair, deform_conv2d, deform_conv2d_ex
 
 
 class DeformConv2d(nn.Module):
@@ -66,3 +66,44 @@ class DeformConv2d(nn.Module):
                 f"kernel_size={self.kernel_size}, stride={self.stride}, "
                 f"padding={self.padding}, dilation={self.dilation}, "
                 f"groups={self.groups}, bias={self.bias is not None}")
+
+
+class DeformConv2dPack(DeformConv2d):
+    """A DCNv2 block: a regular convolution predicts the offsets and the
+    modulation mask from the input, and the deformable convolution consumes
+    them -- the caller pattern of the reference's tests and examples
+    (tests/test_training.py:32-47, example/example01_deform_conv2d_cpu_mps.py:80-84).
+
+    ``conv_offset`` (same kernel, stride, padding, dilation) outputs
+    ``3 * deformable_groups * kh * kw`` channels: the first
+    ``2 * deformable_groups * kh * kw`` are the offsets (the op's layout), the
+    rest the mask logits.  The mask's sigmoid is applied inside the CUDA
+    kernels (``mask_logits=True``) rather than as a separate pass, and the
+    backward returns the logits' gradient directly.  ``modulated=False``
+    gives the DCNv1 block (offsets only).  ``conv_offset`` starts at zero:
+    a regular convolution at initialisation (mask 0.5 for DCNv2).
+    """
+
+    def __init__(self, in_channels: int, out_channels: int, kernel_size, stride=1, padding=0,
+                 dilation=1, groups: int = 1, deformable_groups: int = 1, bias: bool = True,
+                 modulated: bool = True):
+        super().__init__(in_channels, out_channels, kernel_size, stride=stride, padding=padding,
+                         dilation=dilation, groups=groups, bias=bias)
+        self.deformable_groups = deformable_groups
+        self.modulated = modulated
+        kh, kw = self.kernel_size
+        per_tap = 3 if modulated else 2
+        self.conv_offset = nn.Conv2d(in_channels, per_tap * deformable_groups * kh * kw,
+                                     self.kernel_size, stride=self.stride, padding=self.padding,
+                                     dilation=self.dilation, bias=True)
+        nn.init.zeros_(self.conv_offset.weight)
+        nn.init.zeros_(self.conv_offset.bias)
+
+    def forward(self, input: Tensor) -> Tensor:  # type: ignore[override]
+        kh, kw = self.kernel_size
+        n_off = 2 * self.deformable_groups * kh * kw
+        om = self.conv_offset(input)
+        offset = om[:, :n_off]
+        mask = om[:, n_off:] if self.modulated else None
+        return deform_conv2d_ex(input, offset, self.weight, self.bias, self.stride,
+                                self.padding, self.dilation, mask, mask_logits=self.modulated)

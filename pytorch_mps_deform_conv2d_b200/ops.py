@@ -24,6 +24,7 @@ MATH_3XTF32 = 0x2
 ALGO_SIMT_GEMM = 0x100
 ALGO_SIMT_DIRECT = 0x200
 ALGO_TC_GATHER_WEIGHT = 0x400
+MASK_LOGITS = 0x10000
 
 _MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32, "3xtf32": MATH_3XTF32}
 _NAMES = {v: k for k, v in _MODES.items()}
@@ -139,11 +140,23 @@ def deform_conv2d(
                             dilation, mask)
 
 
+def _resolved_math() -> int:
+    if _math_override is not None:
+        return _math_override
+    return MATH_TF32 if torch.backends.cuda.matmul.allow_tf32 else MATH_FP32
+
+
 def deform_conv2d_ex(input, offset, weight, bias=None, stride=(1, 1),
                      padding=(0, 0), dilation=(1, 1), mask=None,
-                     flags: Optional[int] = None) -> Tensor:
+                     flags: Optional[int] = None, mask_logits: bool = False) -> Tensor:
     """:func:`deform_conv2d` with an explicit C-ABI flag word (``MATH_*`` |
-    ``ALGO_*``); ``flags=None`` uses the current math mode."""
+    ``ALGO_*``); ``flags=None`` uses the current math mode.
+
+    ``mask_logits=True``: ``mask`` holds logits and the kernels apply the
+    sigmoid themselves (forward) and return the gradient with respect to the
+    logits -- the DCNv2 block's ``sigmoid(mask)`` fused into the op."""
+    if mask_logits and mask is not None:
+        flags = (_resolved_math() if flags is None or int(flags) < 0 else int(flags)) | MASK_LOGITS
     stride, padding, dilation = _pair(stride), _pair(padding), _pair(dilation)
     for name, t in (("input", input), ("offset", offset), ("weight", weight),
                     ("bias", bias), ("mask", mask)):
