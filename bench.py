@@ -114,7 +114,8 @@ def algorithmic_work(wl):
 
 
 # tcgen05 kernels (TF32 operands; 3xTF32 issues three products per multiply-add)
-TC_KERNELS = ("fwd_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col")
+TC_KERNELS = ("fwd_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col", "fwd_tc_bf16")
+BF16_KERNELS = ("fwd_tc_bf16",)  # kind::f16 with bf16 operands
 
 
 def kernel_work(name, wl):
@@ -321,6 +322,9 @@ def run_ours(args, wl):
     flags = _MODES[args.math]
 
     x, w, b, off, m, go = make_inputs(wl, seed=rank)
+    if args.dtype == "bf16":  # bf16 I/O: every tensor (and gradient) bf16
+        x, w, b, off, m, go = (None if t is None else t.to(torch.bfloat16)
+                               for t in (x, w, b, off, m, go))
     xd, offd, md, god = (t.to(dev) if t is not None else None for t in (x, off, m, go))
     wd = w.to(dev).requires_grad_(True)
     bd = b.to(dev).requires_grad_(True) if b is not None else None
@@ -404,7 +408,10 @@ def run_ours(args, wl):
     roof = {"kernel": dom, "bound": bound, "share_of_step": round(dom_ms / total_ms, 3)
             if world == 1 else None}
     if bound == "tensor":
-        if dom in TC_KERNELS:
+        if dom in BF16_KERNELS:
+            peak = float(peaks.get("bf16_tflops", 1590.0))
+            src = f"{peaks_src} bf16_tflops (cuBLAS bf16 burst)"
+        elif dom in TC_KERNELS:
             peak = peak_tf32
             src = ("cuBLAS tf32 8192^3 burst measured in this run (MEASURED_PEAKS.json holds bf16 "
                    f"only: {peaks.get('bf16_tflops')} TFLOP/s)")
@@ -439,7 +446,8 @@ def run_ours(args, wl):
         "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
-        "dtype": args.math if any(k in TC_KERNELS for k in kernels) else "f32",
+        "dtype": (("bf16 I/O, " if args.dtype == "bf16" else "") +
+                  (args.math if any(k in TC_KERNELS for k in kernels) else "f32")),
         "data": "synthetic",
         "config": {"workload": wl["desc"], "global_batch": wl["N"] * world,
                    "per_gpu_batch": wl["N"], "parallelism": f"dp{world}",
@@ -475,6 +483,8 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
     import pytorch_mps_deform_conv2d_b200 as dcn
     mod = dcn.DeformConv2d(wl["C"], wl["outC"], wl["k"], stride=wl["stride"], padding=wl["pad"],
                            dilation=wl["dil"], groups=wl["groups"], bias=wl["bias"]).to(dev)
+    if args.dtype == "bf16":
+        mod = mod.to(torch.bfloat16)
     with torch.no_grad():
         mod.weight.copy_(w)
         if b is not None:
@@ -482,12 +492,13 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
     dcn.set_math_mode(args.math)
     host = [t.pin_memory() if t is not None else None for t in (x, off, m, go)]
     params = [p for p in mod.parameters()]
-    outs = [torch.empty(p.shape, pin_memory=True) for p in params]
-    h2d = sum(t.numel() * 4 for t in host if t is not None)
-    d2h = sum(p.numel() * 4 for p in params)
+    outs = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
+    h2d = sum(t.numel() * t.element_size() for t in host if t is not None)
+    d2h = sum(p.numel() * p.element_size() for p in params)
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
-    slots = [[torch.empty(t.shape, device=dev) if t is not None else None for t in host]
+    slots = [[torch.empty(t.shape, dtype=t.dtype, device=dev) if t is not None else None
+              for t in host]
              for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
@@ -597,6 +608,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--math", choices=["tf32", "fp32", "3xtf32"], default="tf32")
+    ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32",
+                    help="tensor dtype of the step (the reference and the headline: fp32)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",

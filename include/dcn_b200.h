@@ -110,6 +110,29 @@ DCN_API int dcn_output_size(const dcn_shape* shape, int64_t* out_h, int64_t* out
 /* Bytes of workspace dcn_forward needs for `shape` and `flags`. */
 DCN_API size_t dcn_forward_workspace_size(const dcn_shape* shape, uint32_t flags);
 
+/* bf16 forward (no reference counterpart: the reference is fp32 only,
+ * .mm:206-209).  Every tensor argument is bf16 (16-bit words, the layouts of
+ * dcn_forward) and so is the output.  When channels per group and per
+ * deformable group are multiples of 64, tcgen05 tensor cores run with bf16
+ * operands and fp32 accumulation (bf16 gathers: half the bytes of fp32);
+ * other shapes are upcast to fp32 inside the workspace and run on
+ * dcn_forward's kernels under `flags`, the result rounded back to bf16. */
+DCN_API size_t dcn_forward_bf16_workspace_size(const dcn_shape* shape, uint32_t flags);
+DCN_API int dcn_forward_bf16(const dcn_shape* shape, const void* input, const void* weight,
+                             const void* offset, const void* mask, const void* bias,
+                             void* output, uint32_t flags, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* bf16 backward (no reference counterpart): every tensor argument and
+ * gradient bf16; the gradients are computed by dcn_backward's kernels under
+ * `flags` from fp32 copies made inside the workspace and rounded to bf16. */
+DCN_API size_t dcn_backward_bf16_workspace_size(const dcn_shape* shape, uint32_t flags);
+DCN_API int dcn_backward_bf16(const dcn_shape* shape, const void* grad_output, const void* input,
+                              const void* weight, const void* offset, const void* mask,
+                              void* grad_input, void* grad_offset, void* grad_mask,
+                              void* grad_weight, void* grad_bias, uint32_t flags,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Forward pass; replaces deform_conv2d_forward (.mm:192-374).
  * output = bias + sum_{c,k} weight * mask * bilinear(input, sample(offset)). */
 DCN_API int dcn_forward(const dcn_shape* shape, const float* input, const float* weight,

@@ -344,6 +344,98 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
   return DCN_OK;
 }
 
+}  // extern "C"
+
+namespace {
+bool use_bf16_tc(const dcn::Geom& g, uint32_t flags) {
+  return g.C > 0 && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
+         dcn::tc_fwd_bf16_supported(g);
+}
+// fp32 copies of the operands for the upcast route: x, weight, offset, mask,
+// bias, output (mask and bias counted whether present or not: an upper bound).
+size_t bf16_upcast_bytes(const dcn::Geom& g) {
+  return align_up((size_t)g.N * g.C * g.HW * 4) + align_up((size_t)g.outC * g.Cg * g.kk * 4) +
+         align_up((size_t)g.N * 2 * g.dg * g.kk * g.P * 4) +
+         align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + align_up((size_t)g.outC * 4) +
+         align_up((size_t)g.N * g.outC * g.P * 4);
+}
+size_t fwd_bf16_ws(const dcn::Geom& g, uint32_t flags) {
+  if (use_bf16_tc(g, flags))
+    return align_up(((size_t)g.N * g.HW * g.C + g.C) * 2) +
+           align_up(dcn::tc_fwd_weight_bf16_bytes(g)) + kAlign;
+  return bf16_upcast_bytes(g) + kAlign + fwd_ws(g, flags);
+}
+}  // namespace
+
+extern "C" {
+
+DCN_API size_t dcn_forward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_forward_bf16_workspace_size") != DCN_OK) return 0;
+  return fwd_bf16_ws(g, flags);
+}
+
+DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* weight,
+                             const void* offset, const void* mask, const void* bias,
+                             void* output, uint32_t flags, void* workspace,
+                             size_t workspace_bytes, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
+  if (rc != DCN_OK) return rc;
+  g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const long long out_numel = (long long)g.N * g.outC * g.P;
+  if (out_numel == 0) return DCN_OK;
+  auto dev_or_empty = [](const void* p, long long n) { return n == 0 || is_device_ptr(p); };
+  DCN_CHECK(is_device_ptr(output), "deform_conv2d_forward: output must be a CUDA device buffer");
+  DCN_CHECK(dev_or_empty(input, (long long)g.N * g.C * g.HW) &&
+                dev_or_empty(offset, (long long)g.N * 2 * g.dg * g.kk * g.P) &&
+                dev_or_empty(weight, (long long)g.outC * g.Cg * g.kk),
+            "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
+  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a bfloat16 CUDA tensor");
+  DCN_CHECK(bias == nullptr || is_device_ptr(bias), "bias must be a bfloat16 CUDA tensor");
+  const size_t need = fwd_bf16_ws(g, flags);
+  if (workspace_bytes < need || workspace == nullptr)
+    return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
+                need, workspace_bytes);
+  char* base = static_cast<char*>(align_ptr(workspace));
+  if (use_bf16_tc(g, flags)) {
+    void* xt = base;
+    void* wt = base + align_up(((size_t)g.N * g.HW * g.C + g.C) * 2);
+    DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, stream),
+             "nchw_to_nhwc");
+    DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, stream), "tc_pack_weight");
+    DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, num_sms_current(),
+                                     stream),
+             "fwd_tc_bf16");
+    return DCN_OK;
+  }
+  // upcast route: fp32 copies, the fp32 forward, the result rounded to bf16
+  Carver ws(base);
+  const long long nx = (long long)g.N * g.C * g.HW, nw = (long long)g.outC * g.Cg * g.kk;
+  const long long noff = (long long)g.N * 2 * g.dg * g.kk * g.P;
+  const long long nm = (long long)g.N * g.dg * g.kk * g.P;
+  float* x32 = ws.take(nx);
+  float* w32 = ws.take(nw);
+  float* off32 = ws.take(noff);
+  float* m32 = ws.take(nm);
+  float* b32 = ws.take(g.outC);
+  float* out32 = ws.take(out_numel);
+  DCN_CUDA(dcn::launch_bf16_to_f32(input, x32, nx, stream), "bf16_to_f32");
+  DCN_CUDA(dcn::launch_bf16_to_f32(weight, w32, nw, stream), "bf16_to_f32");
+  DCN_CUDA(dcn::launch_bf16_to_f32(offset, off32, noff, stream), "bf16_to_f32");
+  if (mask) DCN_CUDA(dcn::launch_bf16_to_f32(mask, m32, nm, stream), "bf16_to_f32");
+  if (bias) DCN_CUDA(dcn::launch_bf16_to_f32(bias, b32, g.outC, stream), "bf16_to_f32");
+  const size_t used = bf16_upcast_bytes(g);
+  rc = dcn_forward(s, x32, w32, off32, mask ? m32 : nullptr, bias ? b32 : nullptr, out32, flags,
+                   base + used, workspace_bytes - (size_t)(base - static_cast<char*>(workspace)) - used,
+                   stream_);
+  if (rc != DCN_OK) return rc;
+  DCN_CUDA(dcn::launch_f32_to_bf16(out32, output, out_numel, stream), "f32_to_bf16");
+  return DCN_OK;
+}
+
 DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const float* input,
                          const float* weight, const float* offset, const float* mask,
                          float* grad_input, float* grad_offset, float* grad_mask,
@@ -457,6 +549,70 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   DCN_CUDA(dcn::launch_bwd_weight_simt(g, grad_output, xt, offset, mask, grad_weight,
                                        num_sms_current(), stream),
            "bwd_weight_simt");
+  return DCN_OK;
+}
+
+// fp32 copies for dcn_backward_bf16: grad_output, input, weight, offset,
+// mask, and the five gradients (input, offset, mask, weight, bias).
+static size_t bwd_bf16_copy_bytes(const dcn::Geom& g) {
+  const size_t x = align_up((size_t)g.N * g.C * g.HW * 4), w = align_up((size_t)g.outC * g.Cg * g.kk * 4);
+  const size_t off = align_up((size_t)g.N * 2 * g.dg * g.kk * g.P * 4);
+  const size_t m = align_up((size_t)g.N * g.dg * g.kk * g.P * 4);
+  const size_t go = align_up((size_t)g.N * g.outC * g.P * 4), b = align_up((size_t)g.outC * 4);
+  return go + 2 * (x + w + off + m) + b;
+}
+
+DCN_API size_t dcn_backward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_backward_bf16_workspace_size") != DCN_OK) return 0;
+  return bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+}
+
+DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const void* input,
+                              const void* weight, const void* offset, const void* mask,
+                              void* grad_input, void* grad_offset, void* grad_mask,
+                              void* grad_weight, void* grad_bias, uint32_t flags,
+                              void* workspace, size_t workspace_bytes, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
+  if (rc != DCN_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t need = bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+  if (workspace_bytes < need || workspace == nullptr)
+    return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
+                need, workspace_bytes);
+  char* base = static_cast<char*>(align_ptr(workspace));
+  Carver ws(base);
+  const long long nx = (long long)g.N * g.C * g.HW, nw = (long long)g.outC * g.Cg * g.kk;
+  const long long noff = (long long)g.N * 2 * g.dg * g.kk * g.P;
+  const long long nm = (long long)g.N * g.dg * g.kk * g.P, ngo = (long long)g.N * g.outC * g.P;
+  float* go32 = ws.take(ngo);
+  float* x32 = ws.take(nx);
+  float* w32 = ws.take(nw);
+  float* off32 = ws.take(noff);
+  float* m32 = ws.take(nm);
+  float* gx32 = ws.take(nx);
+  float* gw32 = ws.take(nw);
+  float* goff32 = ws.take(noff);
+  float* gm32 = ws.take(nm);
+  float* gb32 = ws.take(g.outC);
+  DCN_CUDA(dcn::launch_bf16_to_f32(grad_output, go32, ngo, stream), "bf16_to_f32");
+  DCN_CUDA(dcn::launch_bf16_to_f32(input, x32, nx, stream), "bf16_to_f32");
+  DCN_CUDA(dcn::launch_bf16_to_f32(weight, w32, nw, stream), "bf16_to_f32");
+  DCN_CUDA(dcn::launch_bf16_to_f32(offset, off32, noff, stream), "bf16_to_f32");
+  if (mask) DCN_CUDA(dcn::launch_bf16_to_f32(mask, m32, nm, stream), "bf16_to_f32");
+  const size_t used = bwd_bf16_copy_bytes(g);
+  rc = dcn_backward(s, go32, x32, w32, off32, mask ? m32 : nullptr, gx32, goff32,
+                    mask ? gm32 : nullptr, gw32, grad_bias ? gb32 : nullptr, flags, base + used,
+                    workspace_bytes - (size_t)(base - static_cast<char*>(workspace)) - used,
+                    stream_);
+  if (rc != DCN_OK) return rc;
+  DCN_CUDA(dcn::launch_f32_to_bf16(gx32, grad_input, nx, stream), "f32_to_bf16");
+  DCN_CUDA(dcn::launch_f32_to_bf16(goff32, grad_offset, noff, stream), "f32_to_bf16");
+  if (mask) DCN_CUDA(dcn::launch_f32_to_bf16(gm32, grad_mask, nm, stream), "f32_to_bf16");
+  DCN_CUDA(dcn::launch_f32_to_bf16(gw32, grad_weight, nw, stream), "f32_to_bf16");
+  if (grad_bias) DCN_CUDA(dcn::launch_f32_to_bf16(gb32, grad_bias, g.outC, stream), "f32_to_bf16");
   return DCN_OK;
 }
 

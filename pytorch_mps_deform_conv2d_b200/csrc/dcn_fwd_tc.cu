@@ -35,6 +35,8 @@
 // value -- well inside the output tolerance of TF32 mode.  The backward kernels
 // round their gathered operands to nearest, as the gradients have the tighter
 // tolerance.
+#include <cuda_bf16.h>
+
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
 #include "dcn_tma.h"
@@ -59,10 +61,22 @@ int tmem_cols_for(int bn) {
   while (c < 2 * bn) c <<= 1;
   return c;
 }
-// 3xTF32 keeps a high and a low TF32 part of each operand: twice the stage
-// bytes, so half the stages.
-template <bool SPLIT>
-__host__ __device__ constexpr int stages_of() { return SPLIT ? 2 : 4; }
+// Operand modes of the kernel:
+//   TF32   fp32 tensors, TF32 operands (A staged as fp32, read as TF32);
+//   SPLIT  3xTF32: high and low TF32 parts of each operand, three UMMAs per
+//          K substep, twice the stage bytes so half the stages;
+//   BF16   bf16 tensors (NHWC copy, packed weight, offsets, mask, bias and
+//          output all bf16), kind::f16 UMMAs with bf16 operands; a K step is
+//          64 channels (still 128 B per row) and each gather lane blends 8.
+enum : int { kTF32 = 0, kSplit = 1, kBF16 = 2 };
+template <int MODE>
+struct FwdCfg {
+  static constexpr bool SPLIT = MODE == kSplit;
+  static constexpr bool BF16 = MODE == kBF16;
+  static constexpr int STAGES = SPLIT ? 2 : 4;
+  static constexpr int PARTS = SPLIT ? 2 : 1;
+  static constexpr int KCH = BF16 ? 64 : 32;  // channels of one tap per K step
+};
 size_t smem_bytes(int bn, bool split) {
   const int parts = split ? 2 : 1, stages = split ? 2 : 4;
   return (size_t)stages * parts * (A_STAGE + (size_t)bn * 128) + 128 + 1024;
@@ -82,17 +96,37 @@ __device__ __forceinline__ Tile tile_of(int t, int mtiles, int ntiles_n, int bn)
   return T;
 }
 
-template <bool SPLIT>
+// Scalar loads of the small operands (offsets, mask, bias) as fp32.
+template <bool BF16>
+__device__ __forceinline__ float ld_io(const void* p, long long i) {
+  if constexpr (BF16) {
+    const unsigned short v = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
+    return __uint_as_float((uint32_t)v << 16);
+  } else {
+    return __ldg(reinterpret_cast<const float*>(p) + i);
+  }
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// 704 threads: 22 warps, up to 6 on one SM sub-partition of 16K registers,
+// so at most 80 registers a thread (a few bytes spill).
+template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
-fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __restrict__ xt,
+fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __restrict__ xt_,
               int bn, int tcols, int mtiles, int ntiles_n, int ntiles,
-              const float* __restrict__ off, const float* __restrict__ mask,
-              const float* __restrict__ bias, float* __restrict__ out) {
+              const void* __restrict__ off, const void* __restrict__ mask,
+              const void* __restrict__ bias, void* __restrict__ out) {
+  using Cfg = FwdCfg<MODE>;
+  constexpr bool SPLIT = Cfg::SPLIT, BF16 = Cfg::BF16;
+  constexpr int STAGES = Cfg::STAGES, PARTS = Cfg::PARTS, KCH = Cfg::KCH;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
-  constexpr int STAGES = stages_of<SPLIT>();
-  constexpr int PARTS = SPLIT ? 2 : 1;  // hi (+ lo) TF32 parts per operand
   const uint32_t sA0 = tc::smem_u32(smem);
   const uint32_t b_stage = (uint32_t)bn * 128;
   const uint32_t sB0 = sA0 + STAGES * PARTS * A_STAGE;
@@ -103,7 +137,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nchunk = g.Cg >> 5;
+  const int nchunk = g.Cg / KCH;
   const int steps = g.kk * nchunk;
 
   if (tid == 0) {
@@ -129,11 +163,13 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
   if (warp >= GATHER_WARP0) {
     // ------------------------------ gather ------------------------------
     // Dropped corners read the zero pixel row that follows the NHWC copy, so
-    // the corner loads are unconditional.
+    // the corner loads are unconditional.  A lane covers a 16-byte chunk of a
+    // pixel row: 4 fp32 or 8 bf16 channels.
     const int gw = warp - GATHER_WARP0;
     const int quad = lane & 7, sub = lane >> 3;
     const int zoff = g.N * g.HW * g.C;  // element offset of the zero row
-    const float* xq = xt + quad * 4;
+    const float* xq = static_cast<const float*>(xt_) + quad * 4;
+    const unsigned short* xq16 = static_cast<const unsigned short*>(xt_) + quad * 8;
     int gs = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const Tile T = tile_of(t, mtiles, ntiles_n, bn);
@@ -174,9 +210,13 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
             }
             if (!rvalid[i]) continue;
             const long long oi = off_h_index(g, rn[i], dgi, k, rp[i]);
-            const float h = (float)(roy[i] * g.sh - g.ph + ki * g.dh) + __ldg(off + oi);
-            const float w = (float)(rox[i] * g.sw - g.pw + kj * g.dw) + __ldg(off + oi + g.P);
-            const float m = mask_of(g, mask, mask_index(g, rn[i], dgi, k, rp[i]));
+            const float h = (float)(roy[i] * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
+            const float w = (float)(rox[i] * g.sw - g.pw + kj * g.dw) + ld_io<BF16>(off, oi + g.P);
+            float m = 1.f;
+            if (g.use_mask) {
+              const float raw = ld_io<BF16>(mask, mask_index(g, rn[i], dgi, k, rp[i]));
+              m = g.mask_logits ? 1.f / (1.f + expf(-raw)) : raw;
+            }
             const Sample sp = make_sample(h, w, g.H, g.W);
             if (!sp.valid) continue;
             const int xn = rn[i] * g.HW;
@@ -188,39 +228,68 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
         }
         // issue the loads before waiting for the stage to be free
         const int gch0 = gbase + c0;
-        float4 v[ROUNDS][4];
-#pragma unroll
-        for (int i = 0; i < ROUNDS; ++i)
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            v[i][c] = ldg4(xq + (unsigned)(coff[i][c] + gch0));
-        if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
         const uint32_t sA = sA0 + st * PARTS * A_STAGE;
+        if constexpr (BF16) {
+          uint4 v[ROUNDS][4];
 #pragma unroll
-        for (int i = 0; i < ROUNDS; ++i) {
-          const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
-          const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
-          const float e0 = a * A.x + b * B.x + c * C.x + d * D.x;
-          const float e1 = a * A.y + b * B.y + c * C.y + d * D.y;
-          const float e2 = a * A.z + b * B.z + c * C.z + d * D.z;
-          const float e3 = a * A.w + b * B.w + c * C.w + d * D.w;
-          if constexpr (SPLIT) {
-            const float h0 = tc::to_tf32(e0), h1 = tc::to_tf32(e1), h2 = tc::to_tf32(e2),
-                        h3 = tc::to_tf32(e3);
-            tc::st_shared_v4(sA + soff[i], h0, h1, h2, h3);
-            tc::st_shared_v4(sA + A_STAGE + soff[i], tc::to_tf32(e0 - h0), tc::to_tf32(e1 - h1),
-                             tc::to_tf32(e2 - h2), tc::to_tf32(e3 - h3));
-          } else {
-            // stored as fp32; the tensor core reads the TF32 part of each value
-            tc::st_shared_v4(sA + soff[i], e0, e1, e2, e3);
+          for (int i = 0; i < ROUNDS; ++i)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              v[i][c] = __ldg(reinterpret_cast<const uint4*>(xq16 + (unsigned)(coff[i][c] + gch0)));
+          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
+#pragma unroll
+          for (int i = 0; i < ROUNDS; ++i) {
+            const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
+            const uint32_t A[4] = {v[i][0].x, v[i][0].y, v[i][0].z, v[i][0].w};
+            const uint32_t B[4] = {v[i][1].x, v[i][1].y, v[i][1].z, v[i][1].w};
+            const uint32_t C[4] = {v[i][2].x, v[i][2].y, v[i][2].z, v[i][2].w};
+            const uint32_t D[4] = {v[i][3].x, v[i][3].y, v[i][3].z, v[i][3].w};
+            uint32_t r[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float lo = a * bf_lo(A[j]) + b * bf_lo(B[j]) + c * bf_lo(C[j]) + d * bf_lo(D[j]);
+              const float hi = a * bf_hi(A[j]) + b * bf_hi(B[j]) + c * bf_hi(C[j]) + d * bf_hi(D[j]);
+              r[j] = pack_bf16x2(lo, hi);
+            }
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sA + soff[i]), "r"(r[0]),
+                         "r"(r[1]), "r"(r[2]), "r"(r[3])
+                         : "memory");
+          }
+        } else {
+          float4 v[ROUNDS][4];
+#pragma unroll
+          for (int i = 0; i < ROUNDS; ++i)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              v[i][c] = ldg4(xq + (unsigned)(coff[i][c] + gch0));
+          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
+#pragma unroll
+          for (int i = 0; i < ROUNDS; ++i) {
+            const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
+            const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
+            const float e0 = a * A.x + b * B.x + c * C.x + d * D.x;
+            const float e1 = a * A.y + b * B.y + c * C.y + d * D.y;
+            const float e2 = a * A.z + b * B.z + c * C.z + d * D.z;
+            const float e3 = a * A.w + b * B.w + c * C.w + d * D.w;
+            if constexpr (SPLIT) {
+              const float h0 = tc::to_tf32(e0), h1 = tc::to_tf32(e1), h2 = tc::to_tf32(e2),
+                          h3 = tc::to_tf32(e3);
+              tc::st_shared_v4(sA + soff[i], h0, h1, h2, h3);
+              tc::st_shared_v4(sA + A_STAGE + soff[i], tc::to_tf32(e0 - h0),
+                               tc::to_tf32(e1 - h1), tc::to_tf32(e2 - h2),
+                               tc::to_tf32(e3 - h3));
+            } else {
+              // stored as fp32; the tensor core reads the TF32 part of each value
+              tc::st_shared_v4(sA + soff[i], e0, e1, e2, e3);
+            }
           }
         }
         tc::fence_proxy_async();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&full[st]);
         // advance (tap, chunk, deformable group)
-        c0 += 32;
-        cpos += 32;
+        c0 += KCH;
+        cpos += KCH;
         if (cpos == g.cpg) {
           cpos = 0;
           ++dgi;
@@ -252,9 +321,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
           tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
           const uint32_t sB = sB0 + st * PARTS * b_stage;
-          tc::tma_load_2d(sB, &wmap, s * 32, row, &full[st]);
+          tc::tma_load_2d(sB, &wmap, s * KCH, row, &full[st]);
           if constexpr (SPLIT)  // low parts: rows outC .. 2*outC - 1 of the packed weight
-            tc::tma_load_2d(sB + b_stage, &wmap, s * 32, g.outC + row, &full[st]);
+            tc::tma_load_2d(sB + b_stage, &wmap, s * KCH, g.outC + row, &full[st]);
         }
       }
     }
@@ -262,7 +331,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
   } else if (warp == MMA_WARP) {
     // ------------------------------ MMA ------------------------------
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_tf32(BM, bn);
+      const uint32_t idesc = BF16 ? tc::idesc_bf16(BM, bn) : tc::idesc_tf32(BM, bn);
       int gs = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int acc = it & 1;
@@ -275,8 +344,11 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
           tc::tc_fence_after();
           const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
+          for (int j = 0; j < 4; ++j) {  // 32 bytes of K per UMMA: 8 tf32 or 16 bf16
+            if constexpr (BF16) {
+              tc::umma_bf16(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
+                            (s | j) != 0 ? 1u : 0u);
+            } else if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
               tc::umma_tf32(d, tc::sdesc_sw128(sA + A_STAGE + j * 32),
                             tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
               tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32),
@@ -307,8 +379,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
       const bool valid = q < g.NP;
       const int n = valid ? (int)(q / g.P) : 0;
       const int p = valid ? (int)(q - (long long)n * g.P) : 0;
-      float* orow = out + ((long long)n * g.outC + (long long)T.gi * g.Og + T.o0) * g.P + p;
-      const float* brow = bias + T.gi * g.Og + T.o0;
+      const long long obase = ((long long)n * g.outC + (long long)T.gi * g.Og + T.o0) * g.P + p;
+      const int bbase = T.gi * g.Og + T.o0;
       const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
       for (int cb = 0; cb < bn; cb += 8) {
         float vv[8];
@@ -316,8 +388,15 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const float* __r
         tc::tmem_ld_wait();
         if (valid) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            orow[(long long)(cb + j) * g.P] = vv[j] + (g.use_bias ? __ldg(brow + cb + j) : 0.f);
+          for (int j = 0; j < 8; ++j) {
+            const float y = vv[j] + (g.use_bias ? ld_io<BF16>(bias, bbase + cb + j) : 0.f);
+            const long long at = obase + (long long)(cb + j) * g.P;
+            if constexpr (BF16)
+              static_cast<unsigned short*>(out)[at] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(y));
+            else
+              static_cast<float*>(out)[at] = y;
+          }
         }
       }
       tc::tc_fence_before();
@@ -355,6 +434,40 @@ __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __rest
   }
 }
 
+// bf16 packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = W[g*Og+o][c][k]
+// (both bf16, no rounding).
+__global__ void __launch_bounds__(256) tc_pack_weight_bf16_kernel(
+    const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g) {
+  const int Kpad = g.kk * g.Cg;
+  const long long oc = blockIdx.x;
+  const unsigned short* src = w + oc * Kpad;
+  unsigned short* dst = wt + oc * Kpad;
+  for (int j = threadIdx.x; j < Kpad; j += blockDim.x) {
+    const int k = j / g.Cg, c = j - k * g.Cg;
+    dst[j] = __ldg(src + c * g.kk + k);
+  }
+}
+
+cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUtensorMap& wmap,
+                            const void* off, const void* mask, const void* bias, void* out,
+                            int num_sms, cudaStream_t stream) {
+  const int bn = tc_bn(g);
+  const size_t smem = smem_bytes(bn, mode == kSplit);
+  auto kern = mode == kSplit ? fwd_tc_kernel<kSplit>
+                             : (mode == kBF16 ? fwd_tc_kernel<kBF16> : fwd_tc_kernel<kTF32>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  const int mtiles = (int)((g.NP + BM - 1) / BM);
+  const int ntiles_n = g.Og / bn;
+  const long long ntiles = (long long)mtiles * ntiles_n * g.G;
+  if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
+  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, tmem_cols_for(bn), mtiles, ntiles_n,
+                                         (int)ntiles, off, mask, bias, out);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool tc_fwd_supported(const Geom& g) {
@@ -378,25 +491,42 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt, const
                           const float* mask, const float* bias, float* out, bool split,
                           int num_sms, cudaStream_t stream) {
   if (!tc_fwd_supported(g)) return cudaErrorInvalidValue;
-  const int bn = tc_bn(g);
   const int Kpad = g.kk * g.Cg;
   CUtensorMap wmap;
   cudaError_t e = make_tmap_2d_f32(&wmap, wt, (uint64_t)Kpad,
                                    (uint64_t)g.outC * (split ? 2 : 1), (uint64_t)Kpad,
-                                   (uint32_t)bn);
+                                   (uint32_t)tc_bn(g));
   if (e != cudaSuccess) return e;
-  const size_t smem = smem_bytes(bn, split);
-  auto kern = split ? fwd_tc_kernel<true> : fwd_tc_kernel<false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  const int mtiles = (int)((g.NP + BM - 1) / BM);
-  const int ntiles_n = g.Og / bn;
-  const long long ntiles = (long long)mtiles * ntiles_n * g.G;
-  if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
-  const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, tmem_cols_for(bn), mtiles, ntiles_n,
-                                         (int)ntiles, off, mask, bias, out);
+  return launch_fwd_mode(split ? kSplit : kTF32, g, xt, wmap, off, mask, bias, out, num_sms,
+                         stream);
+}
+
+bool tc_fwd_bf16_supported(const Geom& g) {
+  return g.Cg % 64 == 0 && g.cpg % 64 == 0 && g.C % 8 == 0 && g.Og % 16 == 0 &&
+         (g.Og <= 256 || g.Og % 256 == 0) && g.NP > 0 &&
+         (long long)g.N * g.HW * g.C + g.C < (1LL << 31) && (long long)g.kk * g.Cg < (1LL << 30);
+}
+
+size_t tc_fwd_weight_bf16_bytes(const Geom& g) { return (size_t)g.outC * g.kk * g.Cg * 2; }
+
+cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
+                                       cudaStream_t stream) {
+  if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
+  tc_pack_weight_bf16_kernel<<<g.outC, 256, 0, stream>>>(
+      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wt), g);
   return cudaGetLastError();
+}
+
+cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
+                               const void* mask, const void* bias, void* out, int num_sms,
+                               cudaStream_t stream) {
+  if (!tc_fwd_bf16_supported(g)) return cudaErrorInvalidValue;
+  const int Kpad = g.kk * g.Cg;
+  CUtensorMap wmap;
+  cudaError_t e = make_tmap_2d_bf16(&wmap, wt, (uint64_t)Kpad, (uint64_t)g.outC,
+                                    (uint64_t)Kpad, (uint32_t)tc_bn(g));
+  if (e != cudaSuccess) return e;
+  return launch_fwd_mode(kBF16, g, xt, wmap, off, mask, bias, out, num_sms, stream);
 }
 
 }  // namespace dcn

@@ -2,6 +2,8 @@
 // NCHW <-> NHWC transposes (the gathers and the scatter work on a
 // channel-contiguous copy so one sample's channel vector is one run of
 // 16-byte loads / vector reductions), weight repacking and the bias gradient.
+#include <cuda_bf16.h>
+
 #include "dcn_kernels.h"
 
 namespace dcn {
@@ -212,6 +214,77 @@ int grid_for(long long total) {
 }
 
 }  // namespace
+
+namespace {
+// bf16 (as 16-bit words) in (N, R, S) -> out (N, S, R), 32 x 32 tiles; the
+// first block also zeroes `tail_n` words at `tail`.
+__global__ void __launch_bounds__(256) transpose16_kernel(const unsigned short* __restrict__ in,
+                                                          unsigned short* __restrict__ out, int R,
+                                                          int S, unsigned short* tail,
+                                                          int tail_n) {
+  __shared__ unsigned short tile[32][34];
+  if (tail != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    for (int i = threadIdx.y * 32 + threadIdx.x; i < tail_n; i += 256) tail[i] = 0;
+  const int n = blockIdx.z;
+  const int r0 = blockIdx.y * 32, s0 = blockIdx.x * 32;
+  const unsigned short* src = in + (long long)n * R * S;
+  unsigned short* dst = out + (long long)n * R * S;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int r = r0 + ty + i, s = s0 + tx;
+    if (r < R && s < S) tile[ty + i][tx] = src[(long long)r * S + s];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int s = s0 + ty + i, r = r0 + tx;
+    if (r < R && s < S) dst[(long long)s * R + r] = tile[tx][ty + i];
+  }
+}
+
+__global__ void bf16_to_f32_kernel(const unsigned short* __restrict__ in, float* __restrict__ out,
+                                   long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    out[i] = __uint_as_float((uint32_t)in[i] << 16);
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, unsigned short* __restrict__ out,
+                                   long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(in[i]));
+}
+}  // namespace
+
+cudaError_t launch_nchw_to_nhwc_bf16(const void* x, void* xt, int N, int C, int HW, bool zero_row,
+                                     cudaStream_t stream) {
+  unsigned short* out = static_cast<unsigned short*>(xt);
+  unsigned short* tail = zero_row ? out + (long long)N * HW * C : nullptr;
+  if ((long long)N * C * HW == 0) {
+    if (tail != nullptr && C > 0) return cudaMemsetAsync(tail, 0, (size_t)C * 2, stream);
+    return cudaSuccess;
+  }
+  if (ceil_div(C, 32) > 65535 || N > 65535) return cudaErrorInvalidValue;
+  dim3 grid(ceil_div(HW, 32), ceil_div(C, 32), N);
+  transpose16_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const unsigned short*>(x), out,
+                                                       C, HW, tail, C);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bf16_to_f32(const void* in, float* out, long long n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  bf16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(static_cast<const unsigned short*>(in), out,
+                                                      n);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_bf16(const float* in, void* out, long long n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  f32_to_bf16_kernel<<<grid_for(n), 256, 0, stream>>>(in, static_cast<unsigned short*>(out), n);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
                                 bool zero_row, float* zero_like, cudaStream_t stream) {

@@ -83,7 +83,12 @@ void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& of
               "offset shape mismatch: expected (", N, ", ", 2 * dg * kh * kw, ", ", out_h, ", ",
               out_w, "), got ", off.sizes());
   if (use_mask) {
-    check_cuda_f32(msk, "mask must be a float32 CUDA tensor");
+    if (x.scalar_type() == at::kBFloat16) {
+      TORCH_CHECK(msk.device().is_cuda() && msk.scalar_type() == at::kBFloat16,
+                  "mask must be a bfloat16 CUDA tensor");
+    } else {
+      check_cuda_f32(msk, "mask must be a float32 CUDA tensor");
+    }
     TORCH_CHECK(msk.dim() == 4 && msk.size(0) == N && msk.size(1) == dg * kh * kw &&
                     msk.size(2) == out_h && msk.size(3) == out_w,
                 "mask shape mismatch: expected (", N, ", ", dg * kh * kw, ", ", out_h, ", ",
@@ -99,16 +104,30 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
                                  int64_t deformable_groups, int64_t math) {
   TORCH_CHECK(input.device().is_cuda() && weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
-  TORCH_CHECK(input.scalar_type() == at::kFloat && weight.scalar_type() == at::kFloat &&
-                  offset.scalar_type() == at::kFloat,
-              "deform_conv2d_forward: only float32 is supported");
+  // float32 (the reference's only dtype, .mm:206-209) or, as an addition,
+  // bfloat16 for every tensor
+  const bool bf16 = input.scalar_type() == at::kBFloat16;
+  if (bf16) {
+    TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && offset.scalar_type() == at::kBFloat16,
+                "deform_conv2d_forward: input, weight and offset must all be float32 or all "
+                "bfloat16");
+  } else {
+    TORCH_CHECK(input.scalar_type() == at::kFloat && weight.scalar_type() == at::kFloat &&
+                    offset.scalar_type() == at::kFloat,
+                "deform_conv2d_forward: only float32 is supported");
+  }
   const bool use_mask = mask.defined() && mask.numel() > 0;
   int64_t out_h = 0, out_w = 0;
   check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
                dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
   at::Tensor b;
   if (bias.has_value() && bias->defined() && bias->numel() > 0) {
-    check_cuda_f32(*bias, "bias must be a float32 CUDA tensor");
+    if (bf16) {
+      TORCH_CHECK(bias->device().is_cuda() && bias->scalar_type() == at::kBFloat16,
+                  "bias must be a bfloat16 CUDA tensor");
+    } else {
+      check_cuda_f32(*bias, "bias must be a float32 CUDA tensor");
+    }
     TORCH_CHECK(bias->numel() == weight.size(0), "bias must have ", weight.size(0),
                 " elements, got ", bias->numel());
     b = bias->contiguous();
@@ -123,9 +142,18 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
   const uint32_t flags = resolve_flags(math);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (bf16) {
+    const size_t ws16 = dcn_forward_bf16_workspace_size(&s, flags);
+    auto ws = at::empty({(int64_t)std::max<size_t>(ws16, 1)}, x.options().dtype(at::kByte));
+    check_rc(dcn_forward_bf16(&s, x.data_ptr(), w.data_ptr(), off.data_ptr(),
+                              use_mask ? msk.data_ptr() : nullptr,
+                              b.defined() ? b.data_ptr() : nullptr, out.data_ptr(), flags,
+                              ws.data_ptr(), ws16, stream.stream()));
+    return out;
+  }
   const size_t ws_bytes = dcn_forward_workspace_size(&s, flags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
-  auto stream = at::cuda::getCurrentCUDAStream();
   check_rc(dcn_forward(&s, x.data_ptr<float>(), w.data_ptr<float>(), off.data_ptr<float>(),
                        use_mask ? msk.data_ptr<float>() : nullptr,
                        b.defined() ? b.data_ptr<float>() : nullptr, out.data_ptr<float>(), flags,
@@ -141,6 +169,23 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
   TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
                   weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
+  if (input.scalar_type() == at::kBFloat16) {
+    // bfloat16 tensors: the gradients are computed by the float32 backward
+    // from upcast copies and returned in bfloat16
+    TORCH_CHECK(grad_output.scalar_type() == at::kBFloat16 &&
+                    weight.scalar_type() == at::kBFloat16 && offset.scalar_type() == at::kBFloat16,
+                "deform_conv2d_backward: grad_output, input, weight and offset must all be "
+                "float32 or all bfloat16");
+    auto up = [](const at::Tensor& t) { return t.defined() ? t.to(at::kFloat) : t; };
+    c10::optional<at::Tensor> b32;
+    if (bias.has_value() && bias->defined()) b32 = bias->to(at::kFloat);
+    auto r = deform_conv2d_backward(up(grad_output), up(input), up(weight), up(offset), up(mask),
+                                    b32, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                                    dilation_w, groups, deformable_groups, math);
+    auto down = [](const at::Tensor& t) { return t.to(at::kBFloat16); };
+    return std::make_tuple(down(std::get<0>(r)), down(std::get<1>(r)), down(std::get<2>(r)),
+                           down(std::get<3>(r)), down(std::get<4>(r)));
+  }
   TORCH_CHECK(grad_output.scalar_type() == at::kFloat && input.scalar_type() == at::kFloat &&
                   weight.scalar_type() == at::kFloat && offset.scalar_type() == at::kFloat,
               "deform_conv2d_backward: only float32 is supported");
