@@ -49,7 +49,6 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int GATHER_WARPS = 16;
-constexpr int ROUNDS = 2;  // rows per lane: 16 warps x 2 rounds x 4 sub-rows = 128
 constexpr int EPI_WARPS = 4;
 constexpr int MMA_WARP = 4, TMA_WARP = 5, GATHER_WARP0 = 6;
 constexpr int THREADS = (GATHER_WARP0 + GATHER_WARPS) * 32;  // 704
@@ -105,6 +104,19 @@ __device__ __forceinline__ float ld_io(const void* p, long long i) {
   } else {
     return __ldg(reinterpret_cast<const float*>(p) + i);
   }
+}
+// 256-bit global load (sm_100): 32 bytes at a 32-byte aligned address.
+__device__ __forceinline__ void ldg_v8(const void* p, uint32_t (&r)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
 }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -163,34 +175,27 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   if (warp >= GATHER_WARP0) {
     // ------------------------------ gather ------------------------------
     // Dropped corners read the zero pixel row that follows the NHWC copy, so
-    // the corner loads are unconditional.  A lane covers a 16-byte chunk of a
-    // pixel row: 4 fp32 or 8 bf16 channels.
+    // the corner loads are unconditional.  A warp owns 8 pixel rows of the
+    // tile; 4 lanes share a row, each loading a 32-byte run of it per corner
+    // (one 256-bit load: 8 fp32 or 16 bf16 channels) and storing two 16-byte
+    // chunks of the swizzled row.
     const int gw = warp - GATHER_WARP0;
-    const int quad = lane & 7, sub = lane >> 3;
+    const int q4 = lane & 3, sub = lane >> 2;
     const int zoff = g.N * g.HW * g.C;  // element offset of the zero row
-    const float* xq = static_cast<const float*>(xt_) + quad * 4;
-    const unsigned short* xq16 = static_cast<const unsigned short*>(xt_) + quad * 8;
+    const char* xq = static_cast<const char*>(xt_) + q4 * 32;
+    constexpr int ESZ = BF16 ? 2 : 4;  // element bytes
     int gs = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const Tile T = tile_of(t, mtiles, ntiles_n, bn);
-      int rn[ROUNDS], rp[ROUNDS], roy[ROUNDS], rox[ROUNDS];
-      bool rvalid[ROUNDS];
-#pragma unroll
-      for (int i = 0; i < ROUNDS; ++i) {
-        const long long q = T.q0 + gw * 8 + i * 4 + sub;
-        rvalid[i] = q < g.NP;
-        const int n = rvalid[i] ? (int)(q / g.P) : 0;
-        const int p = rvalid[i] ? (int)(q - (long long)n * g.P) : 0;
-        rn[i] = n;
-        rp[i] = p;
-        roy[i] = p / g.Wo;
-        rox[i] = p - roy[i] * g.Wo;
-      }
-      uint32_t soff[ROUNDS];
-#pragma unroll
-      for (int i = 0; i < ROUNDS; ++i) soff[i] = tc::sw128_offset(gw * 8 + i * 4 + sub, quad);
-      int coff[ROUNDS][4];  // element offsets of the corners' channel vectors
-      float cw[ROUNDS][4];
+      const int row = gw * 8 + sub;
+      const long long q = T.q0 + row;
+      const bool rvalid = q < g.NP;
+      const int rn = rvalid ? (int)(q / g.P) : 0;
+      const int rp = rvalid ? (int)(q - (long long)rn * g.P) : 0;
+      const int roy = rp / g.Wo, rox = rp - roy * g.Wo;
+      const uint32_t soff0 = tc::sw128_offset(row, 2 * q4), soff1 = tc::sw128_offset(row, 2 * q4 + 1);
+      int coff[4];  // element offsets of the corners' channel vectors
+      float cw[4];
       // incremental (tap, channel chunk, deformable group) counters
       int k = 0, ki = 0, kj = 0, c0 = 0;
       const int gbase = T.gi * g.Cg;
@@ -202,86 +207,71 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         if (replan) {
           replan = false;
 #pragma unroll
-          for (int i = 0; i < ROUNDS; ++i) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              coff[i][c] = zoff;
-              cw[i][c] = 0.f;
-            }
-            if (!rvalid[i]) continue;
-            const long long oi = off_h_index(g, rn[i], dgi, k, rp[i]);
-            const float h = (float)(roy[i] * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
-            const float w = (float)(rox[i] * g.sw - g.pw + kj * g.dw) + ld_io<BF16>(off, oi + g.P);
+          for (int c = 0; c < 4; ++c) {
+            coff[c] = zoff;
+            cw[c] = 0.f;
+          }
+          if (rvalid) {
+            const long long oi = off_h_index(g, rn, dgi, k, rp);
+            const float h = (float)(roy * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
+            const float w = (float)(rox * g.sw - g.pw + kj * g.dw) + ld_io<BF16>(off, oi + g.P);
             float m = 1.f;
             if (g.use_mask) {
-              const float raw = ld_io<BF16>(mask, mask_index(g, rn[i], dgi, k, rp[i]));
+              const float raw = ld_io<BF16>(mask, mask_index(g, rn, dgi, k, rp));
               m = g.mask_logits ? 1.f / (1.f + expf(-raw)) : raw;
             }
             const Sample sp = make_sample(h, w, g.H, g.W);
-            if (!sp.valid) continue;
-            const int xn = rn[i] * g.HW;
-            if (sp.live & 1u) { coff[i][0] = (xn + sp.i1) * g.C; cw[i][0] = sp.w1 * m; }
-            if (sp.live & 2u) { coff[i][1] = (xn + sp.i2) * g.C; cw[i][1] = sp.w2 * m; }
-            if (sp.live & 4u) { coff[i][2] = (xn + sp.i3) * g.C; cw[i][2] = sp.w3 * m; }
-            if (sp.live & 8u) { coff[i][3] = (xn + sp.i4) * g.C; cw[i][3] = sp.w4 * m; }
+            if (sp.valid) {
+              const int xn = rn * g.HW;
+              if (sp.live & 1u) { coff[0] = (xn + sp.i1) * g.C; cw[0] = sp.w1 * m; }
+              if (sp.live & 2u) { coff[1] = (xn + sp.i2) * g.C; cw[1] = sp.w2 * m; }
+              if (sp.live & 4u) { coff[2] = (xn + sp.i3) * g.C; cw[2] = sp.w3 * m; }
+              if (sp.live & 8u) { coff[3] = (xn + sp.i4) * g.C; cw[3] = sp.w4 * m; }
+            }
           }
         }
         // issue the loads before waiting for the stage to be free
         const int gch0 = gbase + c0;
         const uint32_t sA = sA0 + st * PARTS * A_STAGE;
+        uint32_t v[4][8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          ldg_v8(xq + (size_t)(unsigned)(coff[c] + gch0) * ESZ, v[c]);
+        if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
+        const float a = cw[0], b = cw[1], c = cw[2], d = cw[3];
         if constexpr (BF16) {
-          uint4 v[ROUNDS][4];
+          uint32_t r[8];
 #pragma unroll
-          for (int i = 0; i < ROUNDS; ++i)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              v[i][c] = __ldg(reinterpret_cast<const uint4*>(xq16 + (unsigned)(coff[i][c] + gch0)));
-          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
-#pragma unroll
-          for (int i = 0; i < ROUNDS; ++i) {
-            const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
-            const uint32_t A[4] = {v[i][0].x, v[i][0].y, v[i][0].z, v[i][0].w};
-            const uint32_t B[4] = {v[i][1].x, v[i][1].y, v[i][1].z, v[i][1].w};
-            const uint32_t C[4] = {v[i][2].x, v[i][2].y, v[i][2].z, v[i][2].w};
-            const uint32_t D[4] = {v[i][3].x, v[i][3].y, v[i][3].z, v[i][3].w};
-            uint32_t r[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float lo = a * bf_lo(A[j]) + b * bf_lo(B[j]) + c * bf_lo(C[j]) + d * bf_lo(D[j]);
-              const float hi = a * bf_hi(A[j]) + b * bf_hi(B[j]) + c * bf_hi(C[j]) + d * bf_hi(D[j]);
-              r[j] = pack_bf16x2(lo, hi);
-            }
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sA + soff[i]), "r"(r[0]),
-                         "r"(r[1]), "r"(r[2]), "r"(r[3])
-                         : "memory");
+          for (int j = 0; j < 8; ++j) {
+            const float lo = a * bf_lo(v[0][j]) + b * bf_lo(v[1][j]) + c * bf_lo(v[2][j]) +
+                             d * bf_lo(v[3][j]);
+            const float hi = a * bf_hi(v[0][j]) + b * bf_hi(v[1][j]) + c * bf_hi(v[2][j]) +
+                             d * bf_hi(v[3][j]);
+            r[j] = pack_bf16x2(lo, hi);
           }
+          st_shared_u4(sA + soff0, r[0], r[1], r[2], r[3]);
+          st_shared_u4(sA + soff1, r[4], r[5], r[6], r[7]);
         } else {
-          float4 v[ROUNDS][4];
+          float e[8];
 #pragma unroll
-          for (int i = 0; i < ROUNDS; ++i)
+          for (int j = 0; j < 8; ++j)
+            e[j] = a * __uint_as_float(v[0][j]) + b * __uint_as_float(v[1][j]) +
+                   c * __uint_as_float(v[2][j]) + d * __uint_as_float(v[3][j]);
+          if constexpr (SPLIT) {
+            float h[8], l[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              v[i][c] = ldg4(xq + (unsigned)(coff[i][c] + gch0));
-          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
-#pragma unroll
-          for (int i = 0; i < ROUNDS; ++i) {
-            const float a = cw[i][0], b = cw[i][1], c = cw[i][2], d = cw[i][3];
-            const float4 A = v[i][0], B = v[i][1], C = v[i][2], D = v[i][3];
-            const float e0 = a * A.x + b * B.x + c * C.x + d * D.x;
-            const float e1 = a * A.y + b * B.y + c * C.y + d * D.y;
-            const float e2 = a * A.z + b * B.z + c * C.z + d * D.z;
-            const float e3 = a * A.w + b * B.w + c * C.w + d * D.w;
-            if constexpr (SPLIT) {
-              const float h0 = tc::to_tf32(e0), h1 = tc::to_tf32(e1), h2 = tc::to_tf32(e2),
-                          h3 = tc::to_tf32(e3);
-              tc::st_shared_v4(sA + soff[i], h0, h1, h2, h3);
-              tc::st_shared_v4(sA + A_STAGE + soff[i], tc::to_tf32(e0 - h0),
-                               tc::to_tf32(e1 - h1), tc::to_tf32(e2 - h2),
-                               tc::to_tf32(e3 - h3));
-            } else {
-              // stored as fp32; the tensor core reads the TF32 part of each value
-              tc::st_shared_v4(sA + soff[i], e0, e1, e2, e3);
+            for (int j = 0; j < 8; ++j) {
+              h[j] = tc::to_tf32(e[j]);
+              l[j] = tc::to_tf32(e[j] - h[j]);
             }
+            tc::st_shared_v4(sA + soff0, h[0], h[1], h[2], h[3]);
+            tc::st_shared_v4(sA + soff1, h[4], h[5], h[6], h[7]);
+            tc::st_shared_v4(sA + A_STAGE + soff0, l[0], l[1], l[2], l[3]);
+            tc::st_shared_v4(sA + A_STAGE + soff1, l[4], l[5], l[6], l[7]);
+          } else {
+            // stored as fp32; the tensor core reads the TF32 part of each value
+            tc::st_shared_v4(sA + soff0, e[0], e[1], e[2], e[3]);
+            tc::st_shared_v4(sA + soff1, e[4], e[5], e[6], e[7]);
           }
         }
         tc::fence_proxy_async();
