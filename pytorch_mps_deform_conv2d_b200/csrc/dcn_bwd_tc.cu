@@ -211,6 +211,13 @@ __device__ __forceinline__ DTile dtile_of(int t, int mtiles, int nslots, int ksp
   return T;
 }
 
+// Streaming (evict-first) 16-byte global store.
+__device__ __forceinline__ void st_cs_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
 // One epilogue warp, one tap: 32 pixel rows x 32 channels of the grad-column
 // accumulator.  Tensor memory gives each lane its own pixel's row; the rows go
 // through a shared-memory transpose so that 8 lanes cover one pixel's 32
@@ -325,11 +332,12 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
       float* dst = col + ((long long)k * g.NP + qbase + px) * g.C + gch0 + quad * 4;
       const float h0 = tc::to_tf32(cv[0]), h1 = tc::to_tf32(cv[1]), h2 = tc::to_tf32(cv[2]),
                   h3 = tc::to_tf32(cv[3]);
-      *reinterpret_cast<float4*>(dst) = make_float4(h0, h1, h2, h3);
+      // evict-first: the 280 MB of columns must not push the input and the
+      // grad-input accumulator (re-read and reduced here) out of L2
+      st_cs_v4(dst, h0, h1, h2, h3);
       if (col_lo != 0)
-        *reinterpret_cast<float4*>(dst + col_lo) =
-            make_float4(tc::to_tf32(cv[0] - h0), tc::to_tf32(cv[1] - h1),
-                        tc::to_tf32(cv[2] - h2), tc::to_tf32(cv[3] - h3));
+        st_cs_v4(dst + col_lo, tc::to_tf32(cv[0] - h0), tc::to_tf32(cv[1] - h1),
+                 tc::to_tf32(cv[2] - h2), tc::to_tf32(cv[3] - h3));
     }
     // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
     s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);

@@ -93,6 +93,76 @@ struct ProfScope {
     if (e_ != cudaSuccess) return cuda_fail(e_, where);   \
   } while (0)
 
+#define DCN_CUDA_ON(strm, expr, where)                    \
+  do {                                                    \
+    ProfScope ps_(where, strm);                           \
+    cudaError_t e_ = (expr);                              \
+    ps_.done();                                           \
+    if (e_ != cudaSuccess) return cuda_fail(e_, where);   \
+  } while (0)
+
+// Stream-ordering calls (no kernel, not profiled).
+#define DCN_ORDER(expr, where)                            \
+  do {                                                    \
+    cudaError_t e_ = (expr);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, where);   \
+  } while (0)
+
+// ---- side streams for independent helper kernels ----
+// Per device, two non-blocking streams and their events, created on first
+// use.  A call forks them from the caller's stream with an event and joins
+// them back before the work that needs their results, so the ordering holds
+// under CUDA graph capture too (make the first call before capturing: it
+// creates the streams).  The mutex keeps one call's fork/join sequence from
+// interleaving with another host thread's on the shared events.
+struct SideStreams {
+  cudaStream_t s[2] = {nullptr, nullptr};
+  cudaEvent_t fork = nullptr, join[2] = {nullptr, nullptr};
+};
+std::mutex g_side_mu;
+std::map<int, SideStreams> g_side;
+
+SideStreams* side_streams_locked() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  auto it = g_side.find(dev);
+  if (it != g_side.end()) return &it->second;
+  SideStreams ss;
+  bool ok = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; i < 2 && ok; ++i)
+    ok = cudaStreamCreateWithFlags(&ss.s[i], cudaStreamNonBlocking) == cudaSuccess &&
+         cudaEventCreateWithFlags(&ss.join[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    return nullptr;  // everything stays on the caller's stream
+  }
+  return &(g_side[dev] = ss);
+}
+
+class Fork {
+ public:
+  explicit Fork(cudaStream_t main) : lk_(g_side_mu), ss_(side_streams_locked()), main_(main) {}
+  cudaStream_t side(int i) const { return ss_ ? ss_->s[i] : main_; }
+  // side streams start after everything enqueued on the caller's stream so far
+  cudaError_t fork() {
+    if (!ss_) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(ss_->fork, main_);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(ss_->s[i], ss_->fork, 0);
+    return e;
+  }
+  // the caller's stream continues after side stream i's work so far
+  cudaError_t join(int i) {
+    if (!ss_) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(ss_->join[i], ss_->s[i]);
+    return e == cudaSuccess ? cudaStreamWaitEvent(main_, ss_->join[i], 0) : e;
+  }
+
+ private:
+  std::unique_lock<std::mutex> lk_;
+  SideStreams* ss_;
+  cudaStream_t main_;
+};
+
 bool is_device_ptr(const void* p) {
   if (p == nullptr) return false;
   cudaPointerAttributes attr;
@@ -312,9 +382,27 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
+  const FwdAlgo algo = pick_fwd(g, flags);
+  if (algo == FwdAlgo::kTc) {
+    // the weight pack (side stream) runs beside the input transpose
+    const bool split = split_math(flags);
+    float* wt = ws.take(dcn::tc_fwd_weight_bytes(g, split) / sizeof(float));
+    Fork fk(stream);
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
+                "tc_pack_weight");
+    DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, nullptr,
+                                      stream),
+             "nchw_to_nhwc");
+    DCN_ORDER(fk.join(0), "join");
+    DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, num_sms_current(),
+                                stream),
+             "fwd_tc");
+    return DCN_OK;
+  }
   DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, nullptr, stream),
            "nchw_to_nhwc");
-  switch (pick_fwd(g, flags)) {
+  switch (algo) {
     case FwdAlgo::kDirect:
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
                "fwd_simt_direct");
@@ -331,15 +419,8 @@ DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* wei
                "fwd_simt_gemm");
       break;
     }
-    case FwdAlgo::kTc: {
-      const bool split = split_math(flags);
-      float* wt = ws.take(dcn::tc_fwd_weight_bytes(g, split) / sizeof(float));
-      DCN_CUDA(dcn::launch_tc_pack_weight(weight, wt, g, split, stream), "tc_pack_weight");
-      DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, num_sms_current(),
-                                  stream),
-               "fwd_tc");
-      break;
-    }
+    case FwdAlgo::kTc:
+      break;  // handled above
   }
   return DCN_OK;
 }
@@ -493,9 +574,6 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
   float* gxt = ws.take((size_t)g.N * g.HW * g.C);
-  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
-  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
-           "nchw_to_nhwc");
   if (tc_bwd) {
     const bool split = split_math(flags);
     const size_t parts = split ? 2 : 1;
@@ -505,27 +583,46 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     const bool colp = use_col_path(g, flags);
     float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
-    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r,
-                                    bias_in_prep ? grad_bias : nullptr, stream),
-             "tc_prep_go");
-    DCN_CUDA(dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, stream), "tc_pack_weight_bwd");
+    // grad_out prep (side 0, after the zeroing of grad_bias above) and the
+    // weight pack (side 1) run beside the input transpose
+    Fork fk(stream);
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0),
+                dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r,
+                                       bias_in_prep ? grad_bias : nullptr, fk.side(0)),
+                "tc_prep_go");
+    DCN_CUDA_ON(fk.side(1), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(1)),
+                "tc_pack_weight_bwd");
+    // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
+    DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
+             "nchw_to_nhwc");
+    DCN_ORDER(fk.join(0), "join");
+    DCN_ORDER(fk.join(1), "join");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, col, stream),
              "bwd_data_tc");
-    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+    // grad_input back to NCHW (side 0) beside the weight gradient
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
+                "nhwc_to_nchw");
     if (colp) {
       DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, grad_weight, split, num_sms_current(),
                                           stream),
                "bwd_weight_col");
+      DCN_ORDER(fk.join(0), "join");
     } else {
       void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
       DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
       DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split,
                                          num_sms_current(), stream),
                "bwd_weight_tc");
+      DCN_ORDER(fk.join(0), "join");
     }
     return DCN_OK;
   }
+  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
+  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
+           "nchw_to_nhwc");
   if (dcn::dgroup_supported(g) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT))) {
     DCN_CUDA(dcn::launch_bwd_dgroup(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
                                     grad_mask, grad_weight, stream),
