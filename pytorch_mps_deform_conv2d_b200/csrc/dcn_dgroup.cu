@@ -24,8 +24,23 @@ namespace {
 
 constexpr int DG_THREADS = 128;
 
-__device__ __forceinline__ float f4at(const float4& v, int e) {
-  return e == 0 ? v.x : (e == 1 ? v.y : (e == 2 ? v.z : v.w));
+// One run of VW consecutive channels of a corner pixel row: a 256-bit load
+// for 8 channels (32-byte aligned: 8 | channels per deformable group), a
+// 128-bit load for 4.
+template <int VW>
+__device__ __forceinline__ void ld_run(const float* p, float (&r)[VW]) {
+  if constexpr (VW == 8) {
+    asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]),
+                   "=f"(r[6]), "=f"(r[7])
+                 : "l"(p));
+  } else {
+    const float4 v = ldg4(p);
+    r[0] = v.x;
+    r[1] = v.y;
+    r[2] = v.z;
+    r[3] = v.w;
+  }
 }
 
 // Plan of one (pixel, tap, deformable group): element offsets of the four
@@ -60,7 +75,8 @@ __global__ void __launch_bounds__(DG_THREADS)
 fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict__ w,
                   const float* __restrict__ off, const float* __restrict__ mask,
                   const float* __restrict__ bias, float* __restrict__ out) {
-  constexpr int CPG = CG * GPD, OPD = OG * GPD, NQ = CPG / 4;
+  constexpr int CPG = CG * GPD, OPD = OG * GPD;
+  constexpr int VW = CPG % 8 == 0 ? 8 : 4, NR = CPG / VW;  // channels per load, loads per corner
   extern __shared__ float ws[];  // [OPD][CG][kk]: out channels dgi*OPD .. of the group
   const int dgi = blockIdx.y;
   const int wcount = OPD * CG * g.kk;
@@ -81,15 +97,16 @@ fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict_
     const float w1 = cp.s.w1 * cp.m, w2 = cp.s.w2 * cp.m, w3 = cp.s.w3 * cp.m,
                 w4 = cp.s.w4 * cp.m;
 #pragma unroll
-    for (int qd = 0; qd < NQ; ++qd) {
-      const float4 a = ldg4(xq + (unsigned)cp.c[0] + 4 * qd);
-      const float4 b = ldg4(xq + (unsigned)cp.c[1] + 4 * qd);
-      const float4 c = ldg4(xq + (unsigned)cp.c[2] + 4 * qd);
-      const float4 d = ldg4(xq + (unsigned)cp.c[3] + 4 * qd);
+    for (int qd = 0; qd < NR; ++qd) {
+      float a[VW], b[VW], c[VW], d[VW];
+      ld_run<VW>(xq + (unsigned)cp.c[0] + VW * qd, a);
+      ld_run<VW>(xq + (unsigned)cp.c[1] + VW * qd, b);
+      ld_run<VW>(xq + (unsigned)cp.c[2] + VW * qd, c);
+      ld_run<VW>(xq + (unsigned)cp.c[3] + VW * qd, d);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float v = w1 * f4at(a, e) + w2 * f4at(b, e) + w3 * f4at(c, e) + w4 * f4at(d, e);
-        const int cl = 4 * qd + e;  // channel within the deformable group
+      for (int e = 0; e < VW; ++e) {
+        const float v = w1 * a[e] + w2 * b[e] + w3 * c[e] + w4 * d[e];
+        const int cl = VW * qd + e;  // channel within the deformable group
         const int j = cl / CG, cc = cl - (cl / CG) * CG;
 #pragma unroll
         for (int o = 0; o < OG; ++o)
@@ -126,7 +143,8 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
                   const float* __restrict__ xt, const float* __restrict__ off,
                   const float* __restrict__ mask, float* __restrict__ gxt,
                   float* __restrict__ goff, float* __restrict__ gmask, float* __restrict__ gw) {
-  constexpr int CPG = CG * GPD, OPD = OG * GPD, NQ = CPG / 4, NV = OPD * CG;
+  constexpr int CPG = CG * GPD, OPD = OG * GPD, NV = OPD * CG;
+  constexpr int VW = CPG % 8 == 0 ? 8 : 4, NR = CPG / VW;  // channels per load, loads per corner
   static_assert(NV <= 32, "one grad_weight value per lane");
   extern __shared__ float sm[];  // weights [OPD][CG][kk], then grad_weight sums, same layout
   const int dgi = blockIdx.y;
@@ -162,21 +180,22 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
       if (cp.s.valid) {
         const float m = cp.m;
 #pragma unroll
-        for (int qd = 0; qd < NQ; ++qd) {
-          const float4 a = ldg4(xq + (unsigned)cp.c[0] + 4 * qd);
-          const float4 b = ldg4(xq + (unsigned)cp.c[1] + 4 * qd);
-          const float4 c = ldg4(xq + (unsigned)cp.c[2] + 4 * qd);
-          const float4 d = ldg4(xq + (unsigned)cp.c[3] + 4 * qd);
-          float top[4];
+        for (int qd = 0; qd < NR; ++qd) {
+          float a[VW], b[VW], c[VW], d[VW];
+          ld_run<VW>(xq + (unsigned)cp.c[0] + VW * qd, a);
+          ld_run<VW>(xq + (unsigned)cp.c[1] + VW * qd, b);
+          ld_run<VW>(xq + (unsigned)cp.c[2] + VW * qd, c);
+          ld_run<VW>(xq + (unsigned)cp.c[3] + VW * qd, d);
+          float top[VW];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int cl = 4 * qd + e;
+          for (int e = 0; e < VW; ++e) {
+            const int cl = VW * qd + e;
             const int j = cl / CG, cc = cl - (cl / CG) * CG;
             float gc = 0.f;  // grad column (.mm:820-821)
 #pragma unroll
             for (int o = 0; o < OG; ++o)
               gc = fmaf(gov[j * OG + o], ws[((j * OG + o) * CG + cc) * g.kk + k], gc);
-            const float A = f4at(a, e), B = f4at(b, e), Cv = f4at(c, e), D = f4at(d, e);
+            const float A = a[e], B = b[e], Cv = c[e], D = d[e];
             s_h += m * coord_dh(cp.s, A, B, Cv, D) * gc;
             s_w += m * coord_dw(cp.s, A, B, Cv, D) * gc;
             const float val = bilerp(cp.s, A, B, Cv, D);
@@ -192,8 +211,10 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
           for (int i = 0; i < 4; ++i) {
             if (cp.c[i] == zoff) continue;
             const float wi = ws4[i];
-            red_add_v4(gq + (unsigned)cp.c[i] + 4 * qd, wi * top[0], wi * top[1], wi * top[2],
-                       wi * top[3]);
+#pragma unroll
+            for (int h = 0; h < VW; h += 4)
+              red_add_v4(gq + (unsigned)cp.c[i] + VW * qd + h, wi * top[h], wi * top[h + 1],
+                         wi * top[h + 2], wi * top[h + 3]);
           }
         }
       }
