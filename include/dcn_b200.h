@@ -110,6 +110,30 @@ DCN_API int dcn_output_size(const dcn_shape* shape, int64_t* out_h, int64_t* out
 /* Bytes of workspace dcn_forward needs for `shape` and `flags`. */
 DCN_API size_t dcn_forward_workspace_size(const dcn_shape* shape, uint32_t flags);
 
+/* Row windows (no reference counterpart): output rows [row_begin,
+ * row_begin + rows) of every image, for splitting one image's output rows
+ * across devices.  `shape` describes the whole problem; offset, mask,
+ * output (forward) and grad_output, grad_offset, grad_mask (backward) hold
+ * only the window's rows, laid out as (N, channels, rows, out_w); input and
+ * grad_input stay whole.  grad_input, grad_weight and grad_bias then hold
+ * this window's contributions: summing them over a partition of the rows
+ * gives the full gradients.  Otherwise as dcn_forward / dcn_backward. */
+DCN_API size_t dcn_forward_rows_workspace_size(const dcn_shape* shape, int64_t rows,
+                                               uint32_t flags);
+DCN_API int dcn_forward_rows(const dcn_shape* shape, int64_t row_begin, int64_t rows,
+                             const float* input, const float* weight, const float* offset,
+                             const float* mask, const float* bias, float* output,
+                             uint32_t flags, void* workspace, size_t workspace_bytes,
+                             void* stream);
+DCN_API size_t dcn_backward_rows_workspace_size(const dcn_shape* shape, int64_t rows,
+                                                uint32_t flags);
+DCN_API int dcn_backward_rows(const dcn_shape* shape, int64_t row_begin, int64_t rows,
+                              const float* grad_output, const float* input, const float* weight,
+                              const float* offset, const float* mask, float* grad_input,
+                              float* grad_offset, float* grad_mask, float* grad_weight,
+                              float* grad_bias, uint32_t flags, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* bf16 forward (no reference counterpart: the reference is fp32 only,
  * .mm:206-209).  Every tensor argument is bf16 (16-bit words, the layouts of
  * dcn_forward) and so is the output.  When channels per group and per

@@ -6,8 +6,9 @@
   the allocation rules of the CUDA implementations (csrc/torch_ops.cpp): an
   empty mask (DCNv1) gives an empty grad_mask, an absent or empty bias an
   empty grad_bias.
-* An autograd formula for ``deform_conv2d_forward``, so the operator itself is
-  differentiable when called directly (the public ``deform_conv2d`` goes
+* Autograd formulas for ``deform_conv2d_forward`` and
+  ``deform_conv2d_forward_rows``, so the operators are differentiable when
+  called directly (the public ``deform_conv2d`` goes
   through ``ops._DeformConv2dFunction``, which mirrors the reference's
   ``_DeformConv2dFunction``, src/deform_conv2d_mps/ops.py:68-115).
 
@@ -39,6 +40,19 @@ def _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, str
     grad_bias = input.new_empty((weight.shape[0],)) if use_bias else input.new_empty((0,))
     return (input.new_empty(input.shape), offset.new_empty(offset.shape), grad_mask,
             weight.new_empty(weight.shape), grad_bias)
+
+
+def _forward_rows_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                       dilation_h, dilation_w, groups, deformable_groups, row_begin, math=-1):
+    wo = _out_size(input.shape[3], weight.shape[3], stride_w, pad_w, dilation_w)
+    return input.new_empty((input.shape[0], weight.shape[0], offset.shape[2], wo))
+
+
+def _backward_rows_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w,
+                        pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups,
+                        row_begin, math=-1):
+    return _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w,
+                          pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups, math)
 
 
 def _col2im_fake(columns, offset, mask, height, width, kernel_h, kernel_w, stride_h, stride_w,
@@ -76,6 +90,16 @@ def _forward_backward(ctx, grad_output):
              grad_bias if ctx.has_bias else None) + (None,) * len(ctx.ints))
 
 
+def _forward_rows_backward(ctx, grad_output):
+    input, weight, offset, mask, bias = ctx.saved_tensors
+    grads = getattr(torch.ops, NS).deform_conv2d_backward_rows(
+        grad_output.contiguous(), input, weight, offset, mask, bias, *ctx.ints)
+    grad_input, grad_offset, grad_mask, grad_weight, grad_bias = grads
+    return ((grad_input, grad_weight, grad_offset,
+             grad_mask if ctx.has_mask else None,
+             grad_bias if ctx.has_bias else None) + (None,) * len(ctx.ints))
+
+
 def register() -> None:
     """Attach the fake kernels and the autograd formula (once, after the
     operator library has been loaded)."""
@@ -85,4 +109,8 @@ def register() -> None:
     torch.library.register_fake(q + "deformable_col2im")(_col2im_fake)
     torch.library.register_fake(q + "deformable_col2im_coord")(_col2im_coord_fake)
     torch.library.register_autograd(q + "deform_conv2d_forward", _forward_backward,
+                                    setup_context=_setup_context)
+    torch.library.register_fake(q + "deform_conv2d_forward_rows")(_forward_rows_fake)
+    torch.library.register_fake(q + "deform_conv2d_backward_rows")(_backward_rows_fake)
+    torch.library.register_autograd(q + "deform_conv2d_forward_rows", _forward_rows_backward,
                                     setup_context=_setup_context)

@@ -236,6 +236,7 @@ int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
   g.Ho = (int)Ho; g.Wo = (int)Wo;
   g.use_mask = use_mask ? 1 : 0; g.use_bias = use_bias ? 1 : 0;
   g.mask_logits = 0;
+  g.oy0 = 0;
   g.Cg = g.C / g.G; g.Og = g.outC / g.G; g.cpg = g.dg ? g.C / g.dg : 0;
   g.kk = g.kh * g.kw; g.P = g.Ho * g.Wo; g.HW = g.H * g.W;
   g.NP = (long long)g.N * g.P;
@@ -340,25 +341,62 @@ DCN_API int dcn_output_size(const dcn_shape* s, int64_t* out_h, int64_t* out_w) 
   return DCN_OK;
 }
 
-DCN_API size_t dcn_forward_workspace_size(const dcn_shape* s, uint32_t flags) {
+// Restricts a geometry to output rows [row0, row0 + rows) of every image:
+// offset / mask / output / grad_output then hold those rows only; the input
+// and grad_input stay whole.  rows < 0: the full output.
+static int apply_rows(dcn::Geom& g, int64_t row0, int64_t rows, const char* op) {
+  if (rows < 0) return DCN_OK;
+  if (row0 < 0 || rows == 0 || row0 + rows > g.Ho)
+    return fail(DCN_ERR_INVALID_ARGUMENT,
+                "%s: output rows [%lld, %lld) outside the %d output rows", op, (long long)row0,
+                (long long)(row0 + rows), g.Ho);
+  g.oy0 = (int)row0;
+  g.Ho = (int)rows;
+  g.P = g.Ho * g.Wo;
+  g.NP = (long long)g.N * g.P;
+  return DCN_OK;
+}
+
+static size_t fwd_ws_rows(const dcn_shape* s, int64_t rows, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_forward_workspace_size") != DCN_OK) return 0;
+  if (apply_rows(g, 0, rows, "dcn_forward_workspace_size") != DCN_OK) return 0;
   return fwd_ws(g, flags);
 }
 
-DCN_API size_t dcn_backward_workspace_size(const dcn_shape* s, uint32_t flags) {
+static size_t bwd_ws_rows(const dcn_shape* s, int64_t rows, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_backward_workspace_size") != DCN_OK) return 0;
+  if (apply_rows(g, 0, rows, "dcn_backward_workspace_size") != DCN_OK) return 0;
   return bwd_ws(g, flags);
 }
 
-DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* weight,
-                        const float* offset, const float* mask, const float* bias,
-                        float* output, uint32_t flags, void* workspace,
+DCN_API size_t dcn_forward_workspace_size(const dcn_shape* s, uint32_t flags) {
+  return fwd_ws_rows(s, -1, flags);
+}
+
+DCN_API size_t dcn_backward_workspace_size(const dcn_shape* s, uint32_t flags) {
+  return bwd_ws_rows(s, -1, flags);
+}
+
+DCN_API size_t dcn_forward_rows_workspace_size(const dcn_shape* s, int64_t rows, uint32_t flags) {
+  return rows > 0 ? fwd_ws_rows(s, rows, flags) : 0;
+}
+
+DCN_API size_t dcn_backward_rows_workspace_size(const dcn_shape* s, int64_t rows,
+                                                uint32_t flags) {
+  return rows > 0 ? bwd_ws_rows(s, rows, flags) : 0;
+}
+
+static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const float* input,
+                        const float* weight, const float* offset, const float* mask,
+                        const float* bias, float* output, uint32_t flags, void* workspace,
                         size_t workspace_bytes, void* stream_) {
   g_last_error.clear();
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
+  if (rc != DCN_OK) return rc;
+  rc = apply_rows(g, row0, rows, "deform_conv2d_forward");
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
@@ -517,14 +555,17 @@ DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* 
   return DCN_OK;
 }
 
-DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const float* input,
-                         const float* weight, const float* offset, const float* mask,
-                         float* grad_input, float* grad_offset, float* grad_mask,
-                         float* grad_weight, float* grad_bias, uint32_t flags,
-                         void* workspace, size_t workspace_bytes, void* stream_) {
+static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
+                         const float* grad_output, const float* input, const float* weight,
+                         const float* offset, const float* mask, float* grad_input,
+                         float* grad_offset, float* grad_mask, float* grad_weight,
+                         float* grad_bias, uint32_t flags, void* workspace,
+                         size_t workspace_bytes, void* stream_) {
   g_last_error.clear();
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
+  if (rc != DCN_OK) return rc;
+  rc = apply_rows(g, row0, rows, "deform_conv2d_backward");
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   DCN_CHECK(mask != nullptr || grad_mask == nullptr,
@@ -647,6 +688,47 @@ DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const flo
                                        num_sms_current(), stream),
            "bwd_weight_simt");
   return DCN_OK;
+}
+
+DCN_API int dcn_forward(const dcn_shape* s, const float* input, const float* weight,
+                        const float* offset, const float* mask, const float* bias,
+                        float* output, uint32_t flags, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return forward_core(s, 0, -1, input, weight, offset, mask, bias, output, flags, workspace,
+                      workspace_bytes, stream);
+}
+
+DCN_API int dcn_forward_rows(const dcn_shape* s, int64_t row_begin, int64_t rows,
+                             const float* input, const float* weight, const float* offset,
+                             const float* mask, const float* bias, float* output, uint32_t flags,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "deform_conv2d_forward: rows must be positive");
+  return forward_core(s, row_begin, rows, input, weight, offset, mask, bias, output, flags,
+                      workspace, workspace_bytes, stream);
+}
+
+DCN_API int dcn_backward(const dcn_shape* s, const float* grad_output, const float* input,
+                         const float* weight, const float* offset, const float* mask,
+                         float* grad_input, float* grad_offset, float* grad_mask,
+                         float* grad_weight, float* grad_bias, uint32_t flags,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  return backward_core(s, 0, -1, grad_output, input, weight, offset, mask, grad_input,
+                       grad_offset, grad_mask, grad_weight, grad_bias, flags, workspace,
+                       workspace_bytes, stream);
+}
+
+DCN_API int dcn_backward_rows(const dcn_shape* s, int64_t row_begin, int64_t rows,
+                              const float* grad_output, const float* input, const float* weight,
+                              const float* offset, const float* mask, float* grad_input,
+                              float* grad_offset, float* grad_mask, float* grad_weight,
+                              float* grad_bias, uint32_t flags, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (rows <= 0)
+    return fail(DCN_ERR_INVALID_ARGUMENT, "deform_conv2d_backward: rows must be positive");
+  return backward_core(s, row_begin, rows, grad_output, input, weight, offset, mask, grad_input,
+                       grad_offset, grad_mask, grad_weight, grad_bias, flags, workspace,
+                       workspace_bytes, stream);
 }
 
 // fp32 copies for dcn_backward_bf16: grad_output, input, weight, offset,

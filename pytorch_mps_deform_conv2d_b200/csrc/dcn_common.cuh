@@ -23,6 +23,7 @@ struct Geom {
   int Ho, Wo;
   int use_mask, use_bias;
   int mask_logits;     // the mask tensor holds logits: mask = sigmoid(stored)
+  int oy0;             // full-output row of local output row 0 (row windows)
   // derived
   int Cg, Og;          // channels per group (in / out)
   int cpg;             // channels per deformable group
@@ -82,7 +83,7 @@ __device__ __forceinline__ Sample make_sample(float h, float w, int H, int W) {
 __device__ __forceinline__ void sample_pos(const Geom& g, int oy, int ox,
                                            int ki, int kj, float off_h,
                                            float off_w, float& h, float& w) {
-  h = (float)(oy * g.sh - g.ph + ki * g.dh) + off_h;
+  h = (float)((oy + g.oy0) * g.sh - g.ph + ki * g.dh) + off_h;
   w = (float)(ox * g.sw - g.pw + kj * g.dw) + off_w;
 }
 

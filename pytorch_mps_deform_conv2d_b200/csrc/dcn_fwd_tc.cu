@@ -213,7 +213,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           }
           if (rvalid) {
             const long long oi = off_h_index(g, rn, dgi, k, rp);
-            const float h = (float)(roy * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
+            const float h = (float)((roy + g.oy0) * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
             const float w = (float)(rox * g.sw - g.pw + kj * g.dw) + ld_io<BF16>(off, oi + g.P);
             float m = 1.f;
             if (g.use_mask) {

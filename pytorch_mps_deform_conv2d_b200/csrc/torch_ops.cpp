@@ -58,7 +58,8 @@ dcn_shape make_shape(const at::Tensor& x, const at::Tensor& w, int64_t stride_h,
 void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& off,
                   const at::Tensor& msk, bool use_mask, int64_t stride_h, int64_t stride_w,
                   int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
-                  int64_t groups, int64_t dg, int64_t& out_h, int64_t& out_w) {
+                  int64_t groups, int64_t dg, int64_t& out_h, int64_t& out_w,
+                  int64_t row_begin = -1) {
   TORCH_CHECK(x.dim() == 4, "input must be 4-D (N, C, H, W), got ", x.dim());
   TORCH_CHECK(w.dim() == 4, "weight must be 4-D (outC, C/groups, kh, kw), got ", w.dim());
   TORCH_CHECK(off.dim() == 4, "offset must be 4-D (N, 2*dg*kh*kw, oh, ow), got ", off.dim());
@@ -76,6 +77,12 @@ void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& of
   out_w = (W + 2 * pad_w - dilation_w * (kw - 1) - 1) / stride_w + 1;
   TORCH_CHECK(out_h > 0 && out_w > 0, "calculated output size (", out_h, "x", out_w,
               ") is non-positive");
+  if (row_begin >= 0) {  // row window: offset / mask hold output rows [row_begin, +rows)
+    const int64_t rows = off.size(2);
+    TORCH_CHECK(rows > 0 && row_begin + rows <= out_h, "output rows [", row_begin, ", ",
+                row_begin + rows, ") outside the ", out_h, " output rows");
+    out_h = rows;
+  }
   TORCH_CHECK(dg > 0, "deformable_groups must be positive, got ", dg);
   TORCH_CHECK(C % dg == 0, "channels (", C, ") not divisible by deformable_groups (", dg, ")");
   TORCH_CHECK(off.size(0) == N && off.size(1) == 2 * dg * kh * kw && off.size(2) == out_h &&
@@ -96,12 +103,12 @@ void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& of
   }
 }
 
-at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weight,
-                                 const at::Tensor& offset, const at::Tensor& mask,
-                                 const c10::optional<at::Tensor>& bias, int64_t stride_h,
-                                 int64_t stride_w, int64_t pad_h, int64_t pad_w,
-                                 int64_t dilation_h, int64_t dilation_w, int64_t groups,
-                                 int64_t deformable_groups, int64_t math) {
+at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
+                        const at::Tensor& offset, const at::Tensor& mask,
+                        const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                        int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                        int64_t dilation_w, int64_t groups, int64_t deformable_groups,
+                        int64_t row_begin, int64_t math) {
   TORCH_CHECK(input.device().is_cuda() && weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
   // float32 (the reference's only dtype, .mm:206-209) or, as an addition,
@@ -119,7 +126,8 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
   const bool use_mask = mask.defined() && mask.numel() > 0;
   int64_t out_h = 0, out_w = 0;
   check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
-               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
+               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w, row_begin);
+  TORCH_CHECK(row_begin < 0 || !bf16, "deform_conv2d_forward_rows: float32 tensors only");
   at::Tensor b;
   if (bias.has_value() && bias->defined() && bias->numel() > 0) {
     if (bf16) {
@@ -152,20 +160,53 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
                               ws.data_ptr(), ws16, stream.stream()));
     return out;
   }
+  const float* mp = use_mask ? msk.data_ptr<float>() : nullptr;
+  const float* bp = b.defined() ? b.data_ptr<float>() : nullptr;
+  if (row_begin >= 0) {
+    const size_t wsr = dcn_forward_rows_workspace_size(&s, out_h, flags);
+    auto ws = at::empty({(int64_t)std::max<size_t>(wsr, 1)}, x.options().dtype(at::kByte));
+    check_rc(dcn_forward_rows(&s, row_begin, out_h, x.data_ptr<float>(), w.data_ptr<float>(),
+                              off.data_ptr<float>(), mp, bp, out.data_ptr<float>(), flags,
+                              ws.data_ptr(), wsr, stream.stream()));
+    return out;
+  }
   const size_t ws_bytes = dcn_forward_workspace_size(&s, flags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
-  check_rc(dcn_forward(&s, x.data_ptr<float>(), w.data_ptr<float>(), off.data_ptr<float>(),
-                       use_mask ? msk.data_ptr<float>() : nullptr,
-                       b.defined() ? b.data_ptr<float>() : nullptr, out.data_ptr<float>(), flags,
-                       ws.data_ptr(), ws_bytes, stream.stream()));
+  check_rc(dcn_forward(&s, x.data_ptr<float>(), w.data_ptr<float>(), off.data_ptr<float>(), mp,
+                       bp, out.data_ptr<float>(), flags, ws.data_ptr(), ws_bytes,
+                       stream.stream()));
   return out;
 }
 
-std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_conv2d_backward(
-    const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
-    const at::Tensor& offset, const at::Tensor& mask, const c10::optional<at::Tensor>& bias,
-    int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
-    int64_t dilation_w, int64_t groups, int64_t deformable_groups, int64_t math) {
+at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weight,
+                                 const at::Tensor& offset, const at::Tensor& mask,
+                                 const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                 int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                 int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                 int64_t deformable_groups, int64_t math) {
+  return forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, groups, deformable_groups, -1, math);
+}
+
+at::Tensor deform_conv2d_forward_rows(const at::Tensor& input, const at::Tensor& weight,
+                                      const at::Tensor& offset, const at::Tensor& mask,
+                                      const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                      int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                      int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                      int64_t deformable_groups, int64_t row_begin,
+                                      int64_t math) {
+  TORCH_CHECK(row_begin >= 0, "deform_conv2d_forward_rows: row_begin must be >= 0");
+  return forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, groups, deformable_groups, row_begin, math);
+}
+
+using Grads = std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor>;
+
+Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
+                    const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
+                    const c10::optional<at::Tensor>& bias, int64_t stride_h, int64_t stride_w,
+                    int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+                    int64_t groups, int64_t deformable_groups, int64_t row_begin, int64_t math) {
   TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
                   weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
@@ -179,9 +220,10 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
     auto up = [](const at::Tensor& t) { return t.defined() ? t.to(at::kFloat) : t; };
     c10::optional<at::Tensor> b32;
     if (bias.has_value() && bias->defined()) b32 = bias->to(at::kFloat);
-    auto r = deform_conv2d_backward(up(grad_output), up(input), up(weight), up(offset), up(mask),
-                                    b32, stride_h, stride_w, pad_h, pad_w, dilation_h,
-                                    dilation_w, groups, deformable_groups, math);
+    TORCH_CHECK(row_begin < 0, "deform_conv2d_backward_rows: float32 tensors only");
+    auto r = backward_impl(up(grad_output), up(input), up(weight), up(offset), up(mask), b32,
+                           stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w, groups,
+                           deformable_groups, -1, math);
     auto down = [](const at::Tensor& t) { return t.to(at::kBFloat16); };
     return std::make_tuple(down(std::get<0>(r)), down(std::get<1>(r)), down(std::get<2>(r)),
                            down(std::get<3>(r)), down(std::get<4>(r)));
@@ -193,7 +235,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
   const bool use_mask = mask.defined() && mask.numel() > 0;
   int64_t out_h = 0, out_w = 0;
   check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
-               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
+               dilation_h, dilation_w, groups, deformable_groups, out_h, out_w, row_begin);
   TORCH_CHECK(grad_output.size(0) == input.size(0) && grad_output.size(1) == weight.size(0) &&
                   grad_output.size(2) == out_h && grad_output.size(3) == out_w,
               "grad_output shape mismatch: expected (", input.size(0), ", ", weight.size(0), ", ",
@@ -213,18 +255,48 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor> deform_co
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
   const uint32_t flags = resolve_flags(math);
-  const size_t ws_bytes = dcn_backward_workspace_size(&s, flags);
+  const size_t ws_bytes = row_begin >= 0 ? dcn_backward_rows_workspace_size(&s, out_h, flags)
+                                         : dcn_backward_workspace_size(&s, flags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
   auto stream = at::cuda::getCurrentCUDAStream();
   auto ptr = [](at::Tensor& t) { return t.numel() ? t.data_ptr<float>() : nullptr; };
   auto cptr = [](const at::Tensor& t) -> const float* {
     return t.defined() && t.numel() ? t.data_ptr<float>() : nullptr;
   };
-  check_rc(dcn_backward(&s, cptr(go), cptr(x), cptr(w), cptr(off), use_mask ? cptr(msk) : nullptr,
-                        ptr(grad_input), ptr(grad_offset), use_mask ? ptr(grad_mask) : nullptr,
-                        ptr(grad_weight), use_bias ? ptr(grad_bias) : nullptr, flags, ws.data_ptr(),
-                        ws_bytes, stream.stream()));
+  float* gm = use_mask ? ptr(grad_mask) : nullptr;
+  float* gb = use_bias ? ptr(grad_bias) : nullptr;
+  const float* mp = use_mask ? cptr(msk) : nullptr;
+  if (row_begin >= 0)
+    check_rc(dcn_backward_rows(&s, row_begin, out_h, cptr(go), cptr(x), cptr(w), cptr(off), mp,
+                               ptr(grad_input), ptr(grad_offset), gm, ptr(grad_weight), gb, flags,
+                               ws.data_ptr(), ws_bytes, stream.stream()));
+  else
+    check_rc(dcn_backward(&s, cptr(go), cptr(x), cptr(w), cptr(off), mp, ptr(grad_input),
+                          ptr(grad_offset), gm, ptr(grad_weight), gb, flags, ws.data_ptr(),
+                          ws_bytes, stream.stream()));
   return std::make_tuple(grad_input, grad_offset, grad_mask, grad_weight, grad_bias);
+}
+
+Grads deform_conv2d_backward(const at::Tensor& grad_output, const at::Tensor& input,
+                             const at::Tensor& weight, const at::Tensor& offset,
+                             const at::Tensor& mask, const c10::optional<at::Tensor>& bias,
+                             int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                             int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                             int64_t deformable_groups, int64_t math) {
+  return backward_impl(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
+                       pad_w, dilation_h, dilation_w, groups, deformable_groups, -1, math);
+}
+
+Grads deform_conv2d_backward_rows(const at::Tensor& grad_output, const at::Tensor& input,
+                                  const at::Tensor& weight, const at::Tensor& offset,
+                                  const at::Tensor& mask, const c10::optional<at::Tensor>& bias,
+                                  int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                                  int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+                                  int64_t groups, int64_t deformable_groups, int64_t row_begin,
+                                  int64_t math) {
+  TORCH_CHECK(row_begin >= 0, "deform_conv2d_backward_rows: row_begin must be >= 0");
+  return backward_impl(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
+                       pad_w, dilation_h, dilation_w, groups, deformable_groups, row_begin, math);
 }
 
 at::Tensor deformable_col2im(const at::Tensor& columns, const at::Tensor& offset,
@@ -357,6 +429,17 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
       "Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, "
       "int dilation_h, int dilation_w, int groups, int deformable_groups, int math=-1) "
       "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  // Row windows (no reference counterpart): offset / mask / output /
+  // grad_output hold output rows [row_begin, row_begin + offset.size(2)).
+  m.def(
+      "deform_conv2d_forward_rows(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
+      "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
+      "int dilation_w, int groups, int deformable_groups, int row_begin, int math=-1) -> Tensor");
+  m.def(
+      "deform_conv2d_backward_rows(Tensor grad_output, Tensor input, Tensor weight, "
+      "Tensor offset, Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, "
+      "int pad_w, int dilation_h, int dilation_w, int groups, int deformable_groups, "
+      "int row_begin, int math=-1) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
@@ -364,4 +447,6 @@ TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
   m.impl("deformable_col2im_coord", TORCH_FN(deformable_col2im_coord));
   m.impl("deform_conv2d_forward", TORCH_FN(deform_conv2d_forward));
   m.impl("deform_conv2d_backward", TORCH_FN(deform_conv2d_backward));
+  m.impl("deform_conv2d_forward_rows", TORCH_FN(deform_conv2d_forward_rows));
+  m.impl("deform_conv2d_backward_rows", TORCH_FN(deform_conv2d_backward_rows));
 }

@@ -60,3 +60,71 @@ def allreduce_grads(params: Iterable[torch.nn.Parameter], group=None,
         else:
             p.grad.copy_(g)
         off += n
+
+
+# ---------------------------------------------------------------------------
+# Row slabs: more ranks than images
+# ---------------------------------------------------------------------------
+# With more ranks than images, each image's output rows are split into slabs
+# over the ranks that share it.  The input is replicated on those ranks (the
+# offsets are unbounded, so there is no fixed halo); each rank computes its
+# slab's rows and the gradients of its slab: grad_offset / grad_mask of its
+# rows (owned, no exchange) and its contributions to grad_input (summed over
+# the image's ranks) and to grad_weight / grad_bias (summed over all ranks).
+
+def image_slab(rank: int, world_size: int, n_images: int):
+    """(first image, image count, slab, slabs per image) of `rank`: batch
+    sharding when world_size <= n_images (slabs per image 1), else
+    world_size / n_images slabs of each image (world_size must then be a
+    multiple of n_images)."""
+    if world_size <= n_images:
+        sl = shard_range(n_images, rank, world_size)
+        return sl.start, sl.stop - sl.start, 0, 1
+    if world_size % n_images:
+        raise ValueError(f"{world_size} ranks cannot split {n_images} images evenly")
+    slabs = world_size // n_images
+    return rank // slabs, 1, rank % slabs, slabs
+
+
+def slab_rows(out_h: int, slab: int, slabs: int) -> slice:
+    """Output rows of slab `slab` of `slabs` balanced slabs."""
+    return shard_range(out_h, slab, slabs)
+
+
+def image_groups(world_size: int, n_images: int):
+    """One process group per image shared by several ranks (created on
+    every rank, in the same order); [] when no image is shared."""
+    _, _, _, slabs = image_slab(0, world_size, n_images)
+    if slabs == 1:
+        return []
+    return [dist.new_group(list(range(i * slabs, (i + 1) * slabs))) for i in range(n_images)]
+
+
+class _SumGradOver(torch.autograd.Function):
+    """Identity forward; the gradient is summed over `group` (an all-reduce)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, grad):
+        grad = grad.contiguous()
+        if ctx.group is not None:
+            dist.all_reduce(grad, group=ctx.group)
+        return grad, None
+
+
+def deform_conv2d_row_sharded(input, offset_rows, weight, bias=None, stride=(1, 1),
+                              padding=(0, 0), dilation=(1, 1), mask_rows=None,
+                              row_begin: int = 0, group=None, flags=None):
+    """This rank's output rows ``[row_begin, row_begin + offset_rows.shape[2])``
+    of the deformable convolution of a replicated ``input``; in the backward
+    the input's gradient is summed over ``group`` (the ranks holding the other
+    rows of the same images).  grad_weight / grad_bias stay per rank: sum them
+    with :func:`allreduce_grads` as in batch data parallelism."""
+    from .ops import deform_conv2d_rows
+    x = _SumGradOver.apply(input, group) if group is not None else input
+    return deform_conv2d_rows(x, offset_rows, weight, bias, stride, padding, dilation, mask_rows,
+                              row_begin=row_begin, flags=flags)

@@ -172,3 +172,31 @@ def deform_conv2d_ex(input, offset, weight, bias=None, stride=(1, 1),
     return _DeformConv2dFunction.apply(
         input, weight, offset, mask, bias, stride, padding, dilation, groups,
         deformable_groups, _flags(flags))
+
+
+def deform_conv2d_rows(input, offset, weight, bias=None, stride=(1, 1), padding=(0, 0),
+                       dilation=(1, 1), mask=None, row_begin: int = 0,
+                       flags: Optional[int] = None) -> Tensor:
+    """Output rows ``[row_begin, row_begin + offset.shape[2])`` of
+    :func:`deform_conv2d` (a row window; no reference counterpart).
+
+    ``input`` is the whole input; ``offset`` / ``mask`` hold the window's
+    rows only, and so does the result.  Differentiable: the input's, the
+    weight's and the bias' gradients are this window's contributions, so
+    summing them over a partition of the rows gives the full gradients (see
+    :func:`pytorch_mps_deform_conv2d_b200.distributed.deform_conv2d_row_sharded`).
+    """
+    stride, padding, dilation = _pair(stride), _pair(padding), _pair(dilation)
+    for name, t in (("input", input), ("offset", offset), ("weight", weight),
+                    ("bias", bias), ("mask", mask)):
+        if t is not None and t.device.type != "cuda":
+            raise NotImplementedError(
+                f"pytorch_mps_deform_conv2d_b200.deform_conv2d_rows runs on CUDA tensors "
+                f"only; {name} is on {t.device}")
+    kh, kw = weight.shape[-2], weight.shape[-1]
+    groups = input.shape[1] // weight.shape[1]
+    deformable_groups = offset.shape[1] // (2 * kh * kw)
+    m = mask if mask is not None else input.new_empty(0)
+    return _ops().deform_conv2d_forward_rows(
+        input, weight, offset, m, bias, stride[0], stride[1], padding[0], padding[1],
+        dilation[0], dilation[1], groups, deformable_groups, int(row_begin), _flags(flags))
