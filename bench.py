@@ -321,7 +321,21 @@ def run_ours(args, wl):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     flags = _MODES[args.math]
 
-    x, w, b, off, m, go = make_inputs(wl, seed=rank)
+    strong = args.scaling == "strong"
+    x, w, b, off, m, go = make_inputs(wl, seed=0 if strong else rank)
+    row0, slabs, group = 0, 1, None
+    if strong:
+        # the one batch split over the ranks: images first, then row slabs
+        from pytorch_mps_deform_conv2d_b200.distributed import (image_groups, image_slab,
+                                                                 slab_rows)
+        first, count, slab, slabs = image_slab(rank, world, wl["N"])
+        groups = image_groups(world, wl["N"]) if world > 1 else []
+        group = groups[first] if slabs > 1 else None
+        rows = slab_rows(go.shape[2], slab, slabs)
+        row0 = rows.start
+        cut = lambda t: None if t is None else t[first:first + count, :, rows].contiguous()
+        x = x[first:first + count].contiguous()
+        off, m, go = cut(off), cut(m), cut(go)
     if args.dtype == "bf16":  # bf16 I/O: every tensor (and gradient) bf16
         x, w, b, off, m, go = (None if t is None else t.to(torch.bfloat16)
                                for t in (x, w, b, off, m, go))
@@ -343,11 +357,18 @@ def run_ours(args, wl):
         if world > 1:
             allreduce_grads(params_)
 
+    from pytorch_mps_deform_conv2d_b200.distributed import deform_conv2d_row_sharded
+
     def step():
         for t in leaves:
             t.grad = None
-        out = deform_conv2d_ex(xd, offd, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
-                               flags=flags)
+        if slabs > 1:  # this rank's output rows; grad_input summed over the image's ranks
+            out = deform_conv2d_row_sharded(xd, offd, wd, bd, wl["stride"], wl["pad"],
+                                            wl["dil"], md, row_begin=row0, group=group,
+                                            flags=flags)
+        else:
+            out = deform_conv2d_ex(xd, offd, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
+                                   flags=flags)
         out.backward(god)
         allreduce(params)
 
@@ -384,7 +405,7 @@ def run_ours(args, wl):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    value = ms_per_step / world
+    value = ms_per_step if strong else ms_per_step / world
 
     # ---- dominant kernel roofline ----
     kernels = {k: v for k, v in kstats.items() if k != "memset"}
@@ -398,6 +419,8 @@ def run_ours(args, wl):
     amount, unit, bound = kernel_work(dom, wl)
     if amount is None:
         amount, unit, bound = 0.0, "byte", "hbm"
+    if strong:  # this rank's part of the batch: its images x its share of their rows
+        amount *= xd.shape[0] / wl["N"] * god.shape[2] / out_hw(wl)[0]
     peaks, peaks_src = measured_peaks_file()
     if args.profile:
         peak_tf32 = 0.5 * peaks.get("bf16_tflops", 1590.0)
@@ -437,7 +460,7 @@ def run_ours(args, wl):
     roof["peaks_measured_tflops"] = {"tf32": round(peak_tf32, 1), "fp32": round(peak_fp32, 1)}
 
     # ---- end to end through the public module API, host buffers ----
-    e2e = None if args.profile else run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags,
+    e2e = None if (args.profile or strong) else run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags,
                                             allreduce, flush)
 
     kernel_table = {k: {"launches": v[0], "ms_per_launch": round(v[1] / v[0], 4)}
@@ -445,12 +468,15 @@ def run_ours(args, wl):
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": False, "scaling": args.scaling, "vs_baseline": None,
         "dtype": (("bf16 I/O, " if args.dtype == "bf16" else "") +
                   (args.math if any(k in TC_KERNELS for k in kernels) else "f32")),
         "data": "synthetic",
-        "config": {"workload": wl["desc"], "global_batch": wl["N"] * world,
-                   "per_gpu_batch": wl["N"], "parallelism": f"dp{world}",
+        "config": {"workload": wl["desc"],
+                   "global_batch": wl["N"] if strong else wl["N"] * world,
+                   "per_gpu_batch": xd.shape[0],
+                   "parallelism": (f"dp{world // slabs}x{slabs} row slabs" if strong
+                                   else f"dp{world}"),
                    "math": args.math, "l2": "flushed between timed iterations (256 MiB write, "
                                              "outside the timed events)",
                    "wall_s": round(wall, 3)},
@@ -608,6 +634,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--math", choices=["tf32", "fp32", "3xtf32"], default="tf32")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="weak: every rank a whole batch; strong: the one batch split over the "
+                         "ranks (images, then row slabs of each image)")
     ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32",
                     help="tensor dtype of the step (the reference and the headline: fp32)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
