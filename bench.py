@@ -483,6 +483,8 @@ def run_ours(args, wl):
         "roofline": roof, "e2e": e2e, "gpu_launches": launches,
         "kernels": kernel_table,
     }
+    if world == 1 and not args.profile:
+        line["cuda_graph"] = graph_step_ms(step, leaves, flush, args.steps)
     if world == 1 and not (args.no_cpu_baseline or args.profile):
         line["cpu_baseline"] = cpu_baseline(wl)
     clk = clocks.summary()
@@ -493,6 +495,38 @@ def run_ours(args, wl):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def graph_step_ms(step, leaves, flush, steps):
+    """The same step captured once in a CUDA graph and replayed (launch gaps
+    removed): CUDA events around each replay, L2 flushed before each,
+    inputs resident.  An extra figure beside the eager `value`."""
+    import torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    for t in leaves:
+        t.grad = None
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        e1.synchronize()
+        total += e0.elapsed_time(e1)
+    del graph
+    return {"ms_per_step": round(total / steps, 4), "mode": "whole fwd+bwd step replayed"}
 
 
 def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
