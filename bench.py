@@ -124,7 +124,7 @@ def kernel_work(name, wl):
     N, C = wl["N"], wl["C"]
     if name.startswith(("fwd_", "bwd_data", "bwd_weight")):
         return w["gemm_flops"], "flop", "tensor"
-    if name in ("nchw_to_nhwc", "nhwc_to_nchw"):
+    if name in ("nchw_to_nhwc", "nhwc_to_nchw", "copy_nhwc"):
         return 2.0 * 4 * N * C * wl["H"] * wl["W"], "byte", "hbm"
     if name == "grad_bias":
         return 4.0 * N * wl["outC"] * w["P"], "byte", "hbm"
@@ -339,6 +339,8 @@ def run_ours(args, wl):
     if args.dtype == "bf16":  # bf16 I/O: every tensor (and gradient) bf16
         x, w, b, off, m, go = (None if t is None else t.to(torch.bfloat16)
                                for t in (x, w, b, off, m, go))
+    if args.layout == "nhwc":  # channels-last input (and grad_input), same values
+        x = x.contiguous(memory_format=torch.channels_last)
     xd, offd, md, god = (t.to(dev) if t is not None else None for t in (x, off, m, go))
     wd = w.to(dev).requires_grad_(True)
     bd = b.to(dev).requires_grad_(True) if b is not None else None
@@ -477,7 +479,7 @@ def run_ours(args, wl):
                    "per_gpu_batch": xd.shape[0],
                    "parallelism": (f"dp{world // slabs}x{slabs} row slabs" if strong
                                    else f"dp{world}"),
-                   "math": args.math, "l2": "flushed between timed iterations (256 MiB write, "
+                   "math": args.math, "input_layout": args.layout, "l2": "flushed between timed iterations (256 MiB write, "
                                              "outside the timed events)",
                    "wall_s": round(wall, 3)},
         "roofline": roof, "e2e": e2e, "gpu_launches": launches,
@@ -557,8 +559,7 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
     d2h = sum(p.numel() * p.element_size() for p in params)
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
-    slots = [[torch.empty(t.shape, dtype=t.dtype, device=dev) if t is not None else None
-              for t in host]
+    slots = [[torch.empty_like(t, device=dev) if t is not None else None for t in host]
              for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
@@ -674,6 +675,8 @@ def main():
     ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32",
                     help="tensor dtype of the step (the reference and the headline: fp32)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
+    ap.add_argument("--layout", choices=["nchw", "nhwc"], default="nchw",
+                    help="memory format of the input (nhwc: torch.channels_last)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="device steps only (no CPU baseline, no e2e pass, no cuBLAS peak "

@@ -85,6 +85,15 @@ extern "C" {
  *                    the op (no reference counterpart: the reference takes
  *                    the mask after the sigmoid). */
 #define DCN_MASK_LOGITS 0x10000
+/*   DCN_INPUT_NHWC   `input` and `grad_input` are channels-last buffers
+ *                    (N, H, W, C) instead of (N, C, H, W); every other
+ *                    operand keeps its layout.  The kernels gather from an
+ *                    NHWC copy of the input in any case, so this replaces the
+ *                    two transposes (input in, grad_input out) with a plain
+ *                    copy and none: the layout of torch's channels_last
+ *                    tensors (no reference counterpart: the reference makes
+ *                    every operand contiguous NCHW). */
+#define DCN_INPUT_NHWC 0x20000
 
 /* Geometry of one deformable convolution: the shapes of the reference op's
  * tensors plus its integer arguments. */

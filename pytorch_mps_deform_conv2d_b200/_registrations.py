@@ -33,12 +33,23 @@ def _forward_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, 
     return input.new_empty((input.shape[0], weight.shape[0], ho, wo))
 
 
+def _input_format(input):
+    """Layout of grad_input: channels-last for a dense channels-last input
+    (the CUDA operators keep it), contiguous NCHW otherwise."""
+    if (input.dim() == 4 and not input.is_contiguous()
+            and input.is_contiguous(memory_format=torch.channels_last)):
+        return torch.channels_last
+    return torch.contiguous_format
+
+
 def _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
                    pad_w, dilation_h, dilation_w, groups, deformable_groups, math=-1):
     grad_mask = mask.new_empty(mask.shape) if mask.numel() > 0 else input.new_empty((0,))
     use_bias = bias is not None and bias.numel() > 0
     grad_bias = input.new_empty((weight.shape[0],)) if use_bias else input.new_empty((0,))
-    return (input.new_empty(input.shape), offset.new_empty(offset.shape), grad_mask,
+    grad_input = torch.empty(input.shape, dtype=input.dtype, device=input.device,
+                             memory_format=_input_format(input))
+    return (grad_input, offset.new_empty(offset.shape), grad_mask,
             weight.new_empty(weight.shape), grad_bias)
 
 

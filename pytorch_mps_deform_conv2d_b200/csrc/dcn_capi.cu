@@ -298,7 +298,8 @@ bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
 
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
   size_t b = align_up(xt_floats(g) * sizeof(float));                   // xt + zero row
-  b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));             // grad x (NHWC)
+  if (!(flags & DCN_INPUT_NHWC))
+    b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));           // grad x (NHWC)
   if (use_tc_bwd(g, flags)) {
     const size_t parts = split_math(flags) ? 2 : 1;                   // high (+ low) TF32 parts
     b += parts * align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
@@ -421,6 +422,12 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
   const FwdAlgo algo = pick_fwd(g, flags);
+  // xt (+ its zero row): a transpose of NCHW input, a copy of NHWC input
+  const bool nhwc = flags & DCN_INPUT_NHWC;
+  auto stage_input = [&]() {
+    return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, nullptr, stream)
+                : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, nullptr, stream);
+  };
   if (algo == FwdAlgo::kTc) {
     // the weight pack (side stream) runs beside the input transpose
     const bool split = split_math(flags);
@@ -429,17 +436,14 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
                 "tc_pack_weight");
-    DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, nullptr,
-                                      stream),
-             "nchw_to_nhwc");
+    DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
     DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, num_sms_current(),
                                 stream),
              "fwd_tc");
     return DCN_OK;
   }
-  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, nullptr, stream),
-           "nchw_to_nhwc");
+  DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
   switch (algo) {
     case FwdAlgo::kDirect:
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
@@ -522,8 +526,16 @@ DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* 
   if (use_bf16_tc(g, flags)) {
     void* xt = base;
     void* wt = base + align_up(((size_t)g.N * g.HW * g.C + g.C) * 2);
-    DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, stream),
-             "nchw_to_nhwc");
+    if (flags & DCN_INPUT_NHWC) {  // channels-last: a copy plus the zero row
+      const size_t xb = (size_t)g.N * g.HW * g.C * 2;
+      if (xb) DCN_CUDA(cudaMemcpyAsync(xt, input, xb, cudaMemcpyDeviceToDevice, stream), "copy");
+      DCN_CUDA(cudaMemsetAsync(static_cast<char*>(xt) + xb, 0, (size_t)g.C * 2, stream),
+               "memset");
+    } else {
+      DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
+                                             stream),
+               "nchw_to_nhwc");
+    }
     DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, stream), "tc_pack_weight");
     DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, num_sms_current(),
                                      stream),
@@ -614,7 +626,15 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
   float* xt = ws.take(xt_floats(g));
-  float* gxt = ws.take((size_t)g.N * g.HW * g.C);
+  // the kernels accumulate grad_input in NHWC: into the caller's buffer when
+  // it is channels-last, else into a workspace copy transposed at the end
+  const bool nhwc = flags & DCN_INPUT_NHWC;
+  float* gxt = nhwc ? grad_input : ws.take((size_t)g.N * g.HW * g.C);
+  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
+  auto stage_input = [&]() {
+    return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream)
+                : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream);
+  };
   if (tc_bwd) {
     const bool split = split_math(flags);
     const size_t parts = split ? 2 : 1;
@@ -634,14 +654,26 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
                 "tc_prep_go");
     DCN_CUDA_ON(fk.side(1), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(1)),
                 "tc_pack_weight_bwd");
-    // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
-    DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
-             "nchw_to_nhwc");
+    DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, col, stream),
              "bwd_data_tc");
+    if (nhwc) {  // grad_input is complete: nothing to transpose
+      if (colp) {
+        DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, grad_weight, split, num_sms_current(),
+                                            stream),
+                 "bwd_weight_col");
+      } else {
+        void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
+        DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
+        DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split,
+                                           num_sms_current(), stream),
+                 "bwd_weight_tc");
+      }
+      return DCN_OK;
+    }
     // grad_input back to NCHW (side 0) beside the weight gradient
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
@@ -661,21 +693,21 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     }
     return DCN_OK;
   }
-  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
-  DCN_CUDA(dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, /*zero_row=*/true, gxt, stream),
-           "nchw_to_nhwc");
+  DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
   if (dcn::dgroup_supported(g) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT))) {
     DCN_CUDA(dcn::launch_bwd_dgroup(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
                                     grad_mask, grad_weight, stream),
              "bwd_dgroup");
-    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+    if (!nhwc)
+      DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
     return DCN_OK;
   }
   if (dcn::bwd_small_supported(g) && !(flags & DCN_ALGO_SIMT_GEMM)) {
     DCN_CUDA(dcn::launch_bwd_small(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
                                    grad_mask, grad_weight, stream),
              "bwd_small");
-    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+    if (!nhwc)
+      DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
     return DCN_OK;
   }
   float* wb = ws.take((size_t)g.G * g.kk * g.Og * g.Cg);
@@ -683,7 +715,8 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   DCN_CUDA(dcn::launch_bwd_data_simt(g, grad_output, wb, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, stream),
            "bwd_data_simt");
-  DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+  if (!nhwc)
+    DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
   DCN_CUDA(dcn::launch_bwd_weight_simt(g, grad_output, xt, offset, mask, grad_weight,
                                        num_sms_current(), stream),
            "bwd_weight_simt");

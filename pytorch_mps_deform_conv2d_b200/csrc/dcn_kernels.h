@@ -21,6 +21,10 @@ cudaError_t launch_nchw_to_nhwc_bf16(const void* x, void* xt, int N, int C, int 
 // Element-wise bf16 <-> fp32 copies (round to nearest even on the way down).
 cudaError_t launch_bf16_to_f32(const void* in, float* out, long long n, cudaStream_t stream);
 cudaError_t launch_f32_to_bf16(const float* in, void* out, long long n, cudaStream_t stream);
+// Channels-last x (N, H, W, C) copied to xt (+ zero row, + zeroed
+// `zero_like` of the same size when not NULL).
+cudaError_t launch_copy_nhwc(const float* x, float* xt, int N, int C, int HW, bool zero_row,
+                             float* zero_like, cudaStream_t stream);
 // gxt (N, H, W, C) -> gx (N, C, H, W)
 cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
                                 cudaStream_t stream);

@@ -292,6 +292,49 @@ cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
   return launch_transpose(x, xt, N, C, HW, ex, stream);
 }
 
+namespace {
+// Channels-last input: a straight copy into the workspace copy (16-byte
+// accesses when aligned), the C floats after it zeroed, and `zero_like` (the
+// grad-input accumulator, or NULL) zeroed in the same pass.
+__global__ void __launch_bounds__(256) copy_nhwc_kernel(const float* __restrict__ x,
+                                                        float* __restrict__ xt, long long n,
+                                                        int C, int zero_row,
+                                                        float* __restrict__ zero_like, int vec) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (vec) {
+    const float4* s4 = reinterpret_cast<const float4*>(x);
+    float4* d4 = reinterpret_cast<float4*>(xt);
+    float4* z4 = reinterpret_cast<float4*>(zero_like);
+    for (long long i = t0; i < n / 4; i += stride) {
+      d4[i] = __ldg(s4 + i);
+      if (zero_like) z4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+    for (long long i = t0; i < n; i += stride) {
+      xt[i] = __ldg(x + i);
+      if (zero_like) zero_like[i] = 0.f;
+    }
+  }
+  if (zero_row && blockIdx.x == 0)
+    for (int c = threadIdx.x; c < C; c += blockDim.x) xt[n + c] = 0.f;
+}
+}  // namespace
+
+cudaError_t launch_copy_nhwc(const float* x, float* xt, int N, int C, int HW, bool zero_row,
+                             float* zero_like, cudaStream_t stream) {
+  const long long n = (long long)N * HW * C;
+  if (n == 0 && !(zero_row && C > 0)) return cudaSuccess;
+  const int vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(xt) & 15u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(zero_like) & 15u) == 0;
+  long long blocks = ((vec ? n / 4 : n) + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks < 1) blocks = 1;
+  copy_nhwc_kernel<<<(int)blocks, 256, 0, stream>>>(x, xt, n, C, zero_row ? 1 : 0, zero_like, vec);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_nhwc_to_nchw(const float* gxt, float* gx, int N, int C, int HW,
                                 cudaStream_t stream) {
   return launch_transpose(gxt, gx, N, HW, C, TransposeExtras{nullptr, nullptr, 0}, stream);

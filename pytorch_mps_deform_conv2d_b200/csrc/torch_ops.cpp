@@ -103,6 +103,14 @@ void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& of
   }
 }
 
+// A dense channels-last input (torch's NHWC strides, e.g. from
+// .to(memory_format=torch.channels_last)) goes to the library as it lies,
+// with DCN_INPUT_NHWC; anything else is made contiguous NCHW.
+bool channels_last(const at::Tensor& t) {
+  return t.dim() == 4 && !t.is_contiguous() &&
+         t.is_contiguous(at::MemoryFormat::ChannelsLast);
+}
+
 at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                         const at::Tensor& offset, const at::Tensor& mask,
                         const c10::optional<at::Tensor>& bias, int64_t stride_h,
@@ -141,7 +149,8 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
     b = bias->contiguous();
   }
   c10::cuda::CUDAGuard guard(input.device());
-  auto x = input.contiguous();
+  const bool nhwc = channels_last(input);
+  auto x = nhwc ? input : input.contiguous();
   auto w = weight.contiguous();
   auto off = offset.contiguous();
   auto msk = use_mask ? mask.contiguous() : at::Tensor();
@@ -149,7 +158,7 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   if (out.numel() == 0) return out;
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
-  const uint32_t flags = resolve_flags(math);
+  const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (bf16) {
     const size_t ws16 = dcn_forward_bf16_workspace_size(&s, flags);
@@ -243,7 +252,8 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   const bool use_bias = bias.has_value() && bias->defined() && bias->numel() > 0;
   c10::cuda::CUDAGuard guard(input.device());
   auto go = grad_output.contiguous();
-  auto x = input.contiguous();
+  const bool nhwc = channels_last(input);
+  auto x = nhwc ? input : input.contiguous();  // grad_input below takes x's layout
   auto w = weight.contiguous();
   auto off = offset.contiguous();
   auto msk = use_mask ? mask.contiguous() : at::Tensor();
@@ -254,7 +264,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
-  const uint32_t flags = resolve_flags(math);
+  const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
   const size_t ws_bytes = row_begin >= 0 ? dcn_backward_rows_workspace_size(&s, out_h, flags)
                                          : dcn_backward_workspace_size(&s, flags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));

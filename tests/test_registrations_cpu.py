@@ -84,3 +84,16 @@ def test_operator_autograd_formula_on_meta_tensors(ops, use_mask, use_bias):
     assert (m.grad.shape == m.shape) if use_mask else (m.grad is None)
     if use_bias:
         assert b.grad.shape == b.shape
+
+
+def test_backward_fake_keeps_channels_last_input_layout(ops):
+    # the CUDA operator accumulates grad_input in the layout of a dense
+    # channels-last input; any other input gets a contiguous grad_input
+    x = meta(2, 4, 10, 12).to(memory_format=torch.channels_last)
+    w, off, go = meta(6, 4, 3, 3), meta(2, 18, 10, 12), meta(2, 6, 10, 12)
+    gi = ops.deform_conv2d_backward(go, x, w, off, meta(0), None, 1, 1, 1, 1, 1, 1, 1, 1)[0]
+    assert gi.is_contiguous(memory_format=torch.channels_last) and not gi.is_contiguous()
+    strided = meta(2, 4, 10, 24)[:, :, :, ::2]
+    gi = ops.deform_conv2d_backward(go, strided, w, off, meta(0), None, 1, 1, 1, 1, 1, 1, 1,
+                                    1)[0]
+    assert gi.is_contiguous()
