@@ -178,9 +178,9 @@ struct __align__(16) PixPlan {
 };
 static_assert(sizeof(PixPlan) == 64, "PixPlan is 4 x 16 bytes");
 
-constexpr int EPI_TSTRIDE = 33;  // transpose buffer row stride (floats)
-constexpr int EPI_T_BYTES = 32 * EPI_TSTRIDE * 4 + 128;  // 4352: keeps the plans 16-byte aligned
-constexpr int EPI_WARP_BYTES = EPI_T_BYTES + 32 * (int)sizeof(PixPlan);  // 6400
+constexpr int EPI_TSTRIDE = 36;  // transpose buffer row stride (floats): 16-byte rows
+constexpr int EPI_T_BYTES = 32 * EPI_TSTRIDE * 4;  // 4608: keeps the plans 16-byte aligned
+constexpr int EPI_WARP_BYTES = EPI_T_BYTES + 32 * (int)sizeof(PixPlan);  // 6656
 
 size_t data_smem_bytes(bool split) {
   const int stages = split ? DCfg<true>::STAGES : DCfg<false>::STAGES;
@@ -211,22 +211,64 @@ __device__ __forceinline__ DTile dtile_of(int t, int mtiles, int nslots, int ksp
   return T;
 }
 
-// Streaming (evict-first) 16-byte global store.
-__device__ __forceinline__ void st_cs_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
+// Streaming (evict-first) 32-byte global store (sm_100: 256-bit vectors).
+__device__ __forceinline__ void st_cs_v8(float* p, const float (&v)[8]) {
+  asm volatile("st.global.cs.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p),
+               "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]),
+               "f"(v[7])
+               : "memory");
+}
+// 32-byte read-only global load (sm_100), 32-byte aligned.  Not volatile: the
+// input copy is not written while the kernel runs, so the loads may be
+// scheduled freely.
+__device__ __forceinline__ void ldg_f8(const float* p, float (&r)[8]) {
+  asm("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]),
+        "=f"(r[7])
+      : "l"(p));
+}
+
+// Predicated vector / scalar reductions: no branch around the instruction.
+__device__ __forceinline__ void red_add_v4_if(bool p, float* addr, float a, float b, float c,
+                                              float d) {
+  asm volatile(
+      "{\n.reg .pred q;\nsetp.ne.b32 q, %5, 0;\n"
+      "@q red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n}\n" ::"l"(addr),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"((int)p)
+      : "memory");
+}
+__device__ __forceinline__ void red_add_f32_if(bool p, float* addr, float a) {
+  asm volatile("{\n.reg .pred q;\nsetp.ne.b32 q, %2, 0;\n@q red.global.add.f32 [%0], %1;\n}\n" ::"l"(
+                   addr),
+               "f"(a), "r"((int)p)
                : "memory");
 }
 
 // One epilogue warp, one tap: 32 pixel rows x 32 channels of the grad-column
 // accumulator.  Tensor memory gives each lane its own pixel's row; the rows go
-// through a shared-memory transpose so that 8 lanes cover one pixel's 32
-// channels, making every corner load and vector reduction a full 128-byte
-// line.  Scatters into the NHWC grad-input accumulator (col2im) and reduces
-// the coordinate / mask gradients of each pixel over its channels.  With a
-// column buffer (`col` non-NULL) it also stores the sampled column values
-// col[k][q][c] = mask * bilinear(x) -- TF32-rounded; with `col_lo` non-zero
-// the low TF32 parts go `col_lo` floats further -- for the weight gradient.
+// through a shared-memory transpose (rows 36 floats apart: every access
+// below is free of bank conflicts within a quarter warp).  The gather runs 4
+// lanes to a pixel, 8 channels each, so that every corner load is one 32-byte
+// vector and a warp instruction covers 8 pixels; the scatter into the NHWC
+// grad-input accumulator (col2im) runs 8 lanes to a pixel, 4 channels each,
+// so that every quarter warp's 16-byte vector reductions fill one 128-byte
+// line (the L1 handles reductions one line per quarter warp at best).  Each
+// lane keeps its gather pixel's sampling plan in registers, and the pixel
+// pair a quarter warp reduces is the pair of lanes L and L ^ 4, so the
+// scatter takes the plans by shuffle.  The coordinate / mask gradients of each
+// pixel are reduced over its channels.  With a column buffer (`col` non-NULL)
+// it also stores the sampled column values col[k][q][c] = mask * bilinear(x)
+// -- TF32-rounded; with `col_lo` non-zero the low TF32 parts go `col_lo`
+// floats further -- for the weight gradient.
+//
+// The coordinate and mask gradients need, per pixel, only the four sums
+// D_i = sum_c gcol[c] * v_i[c] over the channels of the corner values v_i:
+//   d/dh = m ((1 - lw) (D3 - D1) + lw (D4 - D2))
+//   d/dw = m ((1 - lh) (D2 - D1) + lh (D4 - D3))
+//   d/dm = w1 D1 + w2 D2 + w3 D3 + w4 D4
+// (bilinear.metalh:73-99 per channel, summed over the channels by
+// deform_conv2d.metal:225-295), so a lane accumulates four products per
+// channel and the pixel's lanes combine the sums once.
 __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float (&vals)[32],
                                                int gch0, long long row_q, long long qbase,
                                                int lane, unsigned char* scratch,
@@ -238,7 +280,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
                                                long long col_lo, int& plan_key) {
   float* T = reinterpret_cast<float*>(scratch);
   PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + EPI_T_BYTES);
-  const int quad = lane & 7, sub = lane >> 3;
+  const int quad = lane & 3, sub = lane >> 2;
   const int zoff = g.N * g.HW * g.C;
   const int dgi = gch0 / g.cpg;
   const int key = k * 65536 + dgi;
@@ -279,80 +321,112 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
     pl.idx = idx;
     plan[lane] = pl;
   }
+  {  // this lane's pixel row, 16 bytes at a time
+    float4* trow = reinterpret_cast<float4*>(T + lane * EPI_TSTRIDE);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) T[lane * EPI_TSTRIDE + j] = vals[j];
+    for (int j = 0; j < 8; ++j)
+      trow[j] = make_float4(vals[4 * j], vals[4 * j + 1], vals[4 * j + 2], vals[4 * j + 3]);
+  }
   __syncwarp();
-  const float* xq = xt + gch0 + quad * 4;
-  float* gq = gxt + gch0 + quad * 4;
+  const float* xq = xt + gch0 + quad * 8;  // corner loads: channels 8 quad .. 8 quad + 7
 #pragma unroll 2
-  for (int i = 0; i < 8; ++i) {
-    const int px = i * 4 + sub;
-    const int4 pc = plan[px].cidx;
-    const int4 pidx = plan[px].idx;
-    float s_h = 0.f, s_w = 0.f, s_m = 0.f;
-    float cv[4] = {0.f, 0.f, 0.f, 0.f};  // column values (mask * bilinear)
-    if (pidx.x >= 0) {
-      const float4 pw = plan[px].w;
-      const float4 geo = plan[px].geo;
-      const float gc0 = T[px * EPI_TSTRIDE + quad * 4 + 0];
-      const float gc1 = T[px * EPI_TSTRIDE + quad * 4 + 1];
-      const float gc2 = T[px * EPI_TSTRIDE + quad * 4 + 2];
-      const float gc3 = T[px * EPI_TSTRIDE + quad * 4 + 3];
-      const float4 v0 = ldg4(xq + (unsigned)pc.x);  // dropped corners: zero row
-      const float4 v1 = ldg4(xq + (unsigned)pc.y);
-      const float4 v2 = ldg4(xq + (unsigned)pc.z);
-      const float4 v3 = ldg4(xq + (unsigned)pc.w);
-      Sample sp;
-      sp.w1 = pw.x; sp.w2 = pw.y; sp.w3 = pw.z; sp.w4 = pw.w;
-      sp.lh = geo.x; sp.lw = geo.y;
-      const float m = geo.z;
-      const float gcs[4] = {gc0, gc1, gc2, gc3};
-      const float a[4] = {v0.x, v0.y, v0.z, v0.w};
-      const float b[4] = {v1.x, v1.y, v1.z, v1.w};
-      const float c[4] = {v2.x, v2.y, v2.z, v2.w};
-      const float d[4] = {v3.x, v3.y, v3.z, v3.w};
+  for (int i = 0; i < 4; ++i) {
+    const int px = i * 8 + sub;
+    const PixPlan pl = plan[px];
+    const bool live = pl.idx.x >= 0;
+    const float m = pl.geo.z;
+    // corner weights times the mask (0 for void samples)
+    const float mw[4] = {m * pl.w.x, m * pl.w.y, m * pl.w.z, m * pl.w.w};
+    float d1 = 0.f, d2 = 0.f, d3 = 0.f, d4 = 0.f;
+    float cv[8];  // column values (mask * bilinear)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        s_h += m * coord_dh(sp, a[e], b[e], c[e], d[e]) * gcs[e];
-        s_w += m * coord_dw(sp, a[e], b[e], c[e], d[e]) * gcs[e];
-        const float bv = bilerp(sp, a[e], b[e], c[e], d[e]);
-        s_m += gcs[e] * bv;
-        cv[e] = m * bv;
-      }
-      const int cis[4] = {pc.x, pc.y, pc.z, pc.w};
-      const float wss[4] = {pw.x, pw.y, pw.z, pw.w};
+    for (int e = 0; e < 8; ++e) cv[e] = 0.f;
+    if (live) {
+      const float* trow = T + px * EPI_TSTRIDE;
+      const float4 ga = *reinterpret_cast<const float4*>(trow + quad * 8);
+      const float4 gb = *reinterpret_cast<const float4*>(trow + quad * 8 + 4);
+      const float gc[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      float a[8], b[8], c[8], d[8];
+      ldg_f8(xq + (unsigned)pl.cidx.x, a);  // dropped corners: zero row
+      ldg_f8(xq + (unsigned)pl.cidx.y, b);
+      ldg_f8(xq + (unsigned)pl.cidx.z, c);
+      ldg_f8(xq + (unsigned)pl.cidx.w, d);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        if (cis[cc] == zoff) continue;
-        const float wc = wss[cc] * m;
-        red_add_v4(gq + (unsigned)cis[cc], wc * gc0, wc * gc1, wc * gc2, wc * gc3);
+      for (int e = 0; e < 8; ++e) {
+        d1 = fmaf(gc[e], a[e], d1);
+        d2 = fmaf(gc[e], b[e], d2);
+        d3 = fmaf(gc[e], c[e], d3);
+        d4 = fmaf(gc[e], d[e], d4);
+        cv[e] = mw[0] * a[e] + mw[1] * b[e] + mw[2] * c[e] + mw[3] * d[e];
       }
     }
     if (col != nullptr && qbase + px < g.NP) {  // every (k, q, c) is written, voids as 0
-      float* dst = col + ((long long)k * g.NP + qbase + px) * g.C + gch0 + quad * 4;
-      const float h0 = tc::to_tf32(cv[0]), h1 = tc::to_tf32(cv[1]), h2 = tc::to_tf32(cv[2]),
-                  h3 = tc::to_tf32(cv[3]);
+      float* dst = col + ((long long)k * g.NP + qbase + px) * g.C + gch0 + quad * 8;
+      float hi[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hi[e] = tc::to_tf32(cv[e]);
       // evict-first: the 280 MB of columns must not push the input and the
       // grad-input accumulator (re-read and reduced here) out of L2
-      st_cs_v4(dst, h0, h1, h2, h3);
-      if (col_lo != 0)
-        st_cs_v4(dst + col_lo, tc::to_tf32(cv[0] - h0), tc::to_tf32(cv[1] - h1),
-                 tc::to_tf32(cv[2] - h2), tc::to_tf32(cv[3] - h3));
+      st_cs_v8(dst, hi);
+      if (col_lo != 0) {
+        float lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lo[e] = tc::to_tf32(cv[e] - hi[e]);
+        st_cs_v8(dst + col_lo, lo);
+      }
     }
-    // sum over the pixel's 8 quad lanes; lane quad 0 reduces into memory
-    s_h += __shfl_xor_sync(0xffffffffu, s_h, 1);
-    s_w += __shfl_xor_sync(0xffffffffu, s_w, 1);
-    s_m += __shfl_xor_sync(0xffffffffu, s_m, 1);
-    s_h += __shfl_xor_sync(0xffffffffu, s_h, 2);
-    s_w += __shfl_xor_sync(0xffffffffu, s_w, 2);
-    s_m += __shfl_xor_sync(0xffffffffu, s_m, 2);
-    s_h += __shfl_xor_sync(0xffffffffu, s_h, 4);
-    s_w += __shfl_xor_sync(0xffffffffu, s_w, 4);
-    s_m += __shfl_xor_sync(0xffffffffu, s_m, 4);
-    if (quad == 0 && pidx.x >= 0) {
-      red_add_f32(goff + pidx.x, s_h);
-      red_add_f32(goff + pidx.x + g.P, s_w);
-      if (g.use_mask) red_add_f32(gmask + pidx.y, s_m * mask_grad_scale(g, plan[px].geo.z));
+    // the four sums over the pixel's 4 lanes; lanes 0, 1, 2 of the pixel
+    // reduce d/dh, d/dw, d/dm into memory
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+    d2 += __shfl_xor_sync(0xffffffffu, d2, 1);
+    d3 += __shfl_xor_sync(0xffffffffu, d3, 1);
+    d4 += __shfl_xor_sync(0xffffffffu, d4, 1);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+    d2 += __shfl_xor_sync(0xffffffffu, d2, 2);
+    d3 += __shfl_xor_sync(0xffffffffu, d3, 2);
+    d4 += __shfl_xor_sync(0xffffffffu, d4, 2);
+    {  // lane quad 0: d/dh, 1: d/dw, 2: d/dm (mask), 3: nothing
+      const float dh = m * ((1.f - pl.geo.y) * (d3 - d1) + pl.geo.y * (d4 - d2));
+      const float dw = m * ((1.f - pl.geo.x) * (d2 - d1) + pl.geo.x * (d4 - d3));
+      const float dm = (pl.w.x * d1 + pl.w.y * d2 + pl.w.z * d3 + pl.w.w * d4) *
+                       mask_grad_scale(g, m);
+      const float v = quad == 0 ? dh : (quad == 1 ? dw : dm);
+      // void samples carry idx.x = -1: the address is not formed for them
+      float* dst = quad == 2 ? gmask + (live ? pl.idx.y : 0)
+                             : goff + (live ? pl.idx.x : 0) + (quad == 1 ? g.P : 0);
+      red_add_f32_if(live && quad < (g.use_mask ? 3 : 2), dst, v);
+    }
+    // col2im: 8 lanes per pixel, 4 channels each, so that each quarter warp's
+    // 16-byte reductions fill one pixel's 128-byte line.  Lanes L and L ^ 4
+    // hold the plans of the pixel pair (i * 8 + 2 (sub / 2), + 1) that lanes
+    // L & ~7 .. L | 7 reduce.
+    const int oc[4] = {__shfl_xor_sync(0xffffffffu, pl.cidx.x, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.y, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.z, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.w, 4)};
+    const float omw[4] = {__shfl_xor_sync(0xffffffffu, mw[0], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[1], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[2], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[3], 4)};
+    const bool olive = __shfl_xor_sync(0xffffffffu, (int)live, 4) != 0;
+    const int j = lane & 7;
+    float* gq = gxt + gch0 + j * 4;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const bool own = h == (sub & 1);
+      const bool hl = own ? live : olive;
+      const int rp = i * 8 + (sub & ~1) + h;
+      const float4 g4 = *reinterpret_cast<const float4*>(T + rp * EPI_TSTRIDE + j * 4);
+      const int cis[4] = {own ? pl.cidx.x : oc[0], own ? pl.cidx.y : oc[1],
+                          own ? pl.cidx.z : oc[2], own ? pl.cidx.w : oc[3]};
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        // dropped corners (the zero row) and void samples are not reduced
+        const bool on = hl && cis[cc] != zoff;
+        const float wc = own ? mw[cc] : omw[cc];
+        red_add_v4_if(on, gq + (unsigned)(on ? cis[cc] : 0), wc * g4.x, wc * g4.y, wc * g4.z,
+                      wc * g4.w);
+      }
     }
   }
 }

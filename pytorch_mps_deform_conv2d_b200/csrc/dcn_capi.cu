@@ -629,6 +629,9 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   // the kernels accumulate grad_input in NHWC: into the caller's buffer when
   // it is channels-last, else into a workspace copy transposed at the end
   const bool nhwc = flags & DCN_INPUT_NHWC;
+  // the accumulation uses 16-byte vector reductions
+  DCN_CHECK(!nhwc || (reinterpret_cast<uintptr_t>(grad_input) & 15u) == 0,
+            "deform_conv2d_backward: grad_input must be 16-byte aligned with DCN_INPUT_NHWC");
   float* gxt = nhwc ? grad_input : ws.take((size_t)g.N * g.HW * g.C);
   // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
   auto stage_input = [&]() {
