@@ -1,9 +1,10 @@
 // dcn_bwd_tc.cu -- backward deformable convolution on tcgen05 tensor cores
 // (kind::tf32, fp32 accumulation in tensor memory).
 //
-//  prep          go -> go_t (pixel-major [n][p][o]) and go_r (NCHW), both
-//                rounded to TF32 with round-to-nearest.
-//  bwd_data_tc   per 128-pixel tile and tap k:
+//  prep          go -> go_r (NCHW, rows padded to a multiple of 4 pixels),
+//                rounded to TF32 with round-to-nearest (+ the low TF32 parts
+//                in 3xTF32), grad_bias summed on the way.
+//  bwd_data_tc   per 128-pixel tile of one image and tap k:
 //                  gcol[q, c] = sum_o go[q, o] W[o, c, k]            (.mm:820-821)
 //                on the tensor core, then an epilogue that reads each pixel's
 //                row of gcol out of tensor memory and, in the same pass,
@@ -37,115 +38,76 @@ int pow2_cols(int n) {
 }
 
 // ---------------------------------------------------------------------------
-// prep: go (N, outC, P) -> go_t (N*P, outC) and go_r (N, outC, P), tf32-rounded
+// prep: go (N, outC, P) -> go_r (N*outC rows of Ppad), TF32-rounded
 // ---------------------------------------------------------------------------
-// With `go_t_lo` (3xTF32), the low TF32 parts go to go_t_lo and to the rows
-// N*outC .. 2*N*outC-1 of go_r.  Scalar version for any P (rows padded to
-// Ppad with zeros).
+// With `split` (3xTF32) the low TF32 parts fill rows N*outC .. 2*N*outC-1.
+// Pixels P .. Ppad-1 of a row are zero.  A block covers PG_SPAN pixels of one
+// (image, out channel) row -- 16-byte accesses when P % 4 == 0 -- and, with
+// `gb` (pre-zeroed grad_bias), adds its row's sum with one atomic.
+constexpr int PG_SPAN = 2048;
 __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
-                                                      float* __restrict__ go_t,
-                                                      float* __restrict__ go_t_lo,
-                                                      float* __restrict__ go_r, int N, int outC,
-                                                      int P, int Ppad) {
-  __shared__ float tile_lo[32][33];
-  __shared__ float tile[32][33];
-  const int n = blockIdx.z;
-  const int o0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  const float* src = go + (long long)n * outC * P;
-#pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int o = o0 + ty + i, p = p0 + tx;
-    if (o < outC && p < Ppad) {
-      const float raw = p < P ? src[(long long)o * P + p] : 0.f;
-      const float v = tc::to_tf32(raw);
-      tile[ty + i][tx] = v;
-      go_r[((long long)n * outC + o) * Ppad + p] = v;
-      if (go_t_lo) {
-        const float lo = tc::to_tf32(raw - v);
-        tile_lo[ty + i][tx] = lo;
-        go_r[((long long)(N + n) * outC + o) * Ppad + p] = lo;
-      }
+                                                      float* __restrict__ go_r,
+                                                      float* __restrict__ gb, int N, int outC,
+                                                      int P, int Ppad, int pspans, int split,
+                                                      int vec) {
+  __shared__ float part[8];
+  const long long row = blockIdx.x / pspans;  // n * outC + o
+  const int pbeg = (int)(blockIdx.x - row * pspans) * PG_SPAN;
+  const int pend = min(Ppad, pbeg + PG_SPAN);
+  const float* src = go + row * P;
+  float* hi = go_r + row * Ppad;
+  float* lo = go_r + ((long long)N * outC + row) * Ppad;
+  float sum = 0.f;
+  if (vec) {  // P % 4 == 0: Ppad == P, 16-byte aligned rows
+    for (int p = pbeg + 4 * threadIdx.x; p < pend; p += 4 * blockDim.x) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + p));
+      const float4 h = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z),
+                                   tc::to_tf32(v.w));
+      *reinterpret_cast<float4*>(hi + p) = h;
+      if (split)
+        *reinterpret_cast<float4*>(lo + p) =
+            make_float4(tc::to_tf32(v.x - h.x), tc::to_tf32(v.y - h.y), tc::to_tf32(v.z - h.z),
+                        tc::to_tf32(v.w - h.w));
+      sum += (v.x + v.y) + (v.z + v.w);
+    }
+  } else {
+    for (int p = pbeg + threadIdx.x; p < pend; p += blockDim.x) {
+      const float v = p < P ? __ldg(src + p) : 0.f;
+      const float h = tc::to_tf32(v);
+      hi[p] = h;
+      if (split) lo[p] = tc::to_tf32(v - h);
+      sum += v;
     }
   }
-  __syncthreads();
+  if (gb == nullptr) return;
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int p = p0 + ty + i, o = o0 + tx;
-    if (o < outC && p < P) {
-      go_t[((long long)n * P + p) * outC + o] = tile[tx][ty + i];
-      if (go_t_lo) go_t_lo[((long long)n * P + p) * outC + o] = tile_lo[tx][ty + i];
-    }
+  for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(gb + row % outC, t);
   }
 }
 
-// Vector version (P % 4 == 0, so Ppad == P; outC % 4 == 0; 16-byte aligned
-// buffers): a block walks PG_SPAN pixels of 64 out channels of one image in
-// 64 x 64 tiles with 16-byte loads and stores, and also sums grad_bias
-// (pre-zeroed) -- one atomic per out channel per block.
-constexpr int PG_SPAN = 256;
-__global__ void __launch_bounds__(256) prep_go4_kernel(const float* __restrict__ go,
-                                                       float* __restrict__ go_t,
-                                                       float* __restrict__ go_t_lo,
-                                                       float* __restrict__ go_r,
-                                                       float* __restrict__ gb, int N, int outC,
-                                                       int P) {
-  __shared__ float tile[64][65];
-  __shared__ float tile_lo[64][65];
-  const int n = blockIdx.z, o0 = blockIdx.y * 64, pbeg = blockIdx.x * PG_SPAN;
-  const int pend = min(P, pbeg + PG_SPAN);
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  float bsum[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int p0 = pbeg; p0 < pend; p0 += 64) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int o = o0 + ty + 16 * i, p = p0 + 4 * tx;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (o < outC && p < P) {
-        const long long at = ((long long)n * outC + o) * P + p;
-        v = __ldg(reinterpret_cast<const float4*>(go + at));
-        const float4 h = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z),
-                                     tc::to_tf32(v.w));
-        *reinterpret_cast<float4*>(go_r + at) = h;
-        float* row = tile[ty + 16 * i] + 4 * tx;
-        row[0] = h.x; row[1] = h.y; row[2] = h.z; row[3] = h.w;
-        if (go_t_lo) {
-          const float4 l = make_float4(tc::to_tf32(v.x - h.x), tc::to_tf32(v.y - h.y),
-                                       tc::to_tf32(v.z - h.z), tc::to_tf32(v.w - h.w));
-          *reinterpret_cast<float4*>(go_r + (long long)N * outC * P + at) = l;
-          float* rl = tile_lo[ty + 16 * i] + 4 * tx;
-          rl[0] = l.x; rl[1] = l.y; rl[2] = l.z; rl[3] = l.w;
-        }
-      }
-      bsum[i] += (v.x + v.y) + (v.z + v.w);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int p = p0 + ty + 16 * i, o = o0 + 4 * tx;
-      if (p < P && o < outC) {
-        const long long at = ((long long)n * P + p) * outC + o;
-        *reinterpret_cast<float4*>(go_t + at) =
-            make_float4(tile[4 * tx][ty + 16 * i], tile[4 * tx + 1][ty + 16 * i],
-                        tile[4 * tx + 2][ty + 16 * i], tile[4 * tx + 3][ty + 16 * i]);
-        if (go_t_lo)
-          *reinterpret_cast<float4*>(go_t_lo + at) =
-              make_float4(tile_lo[4 * tx][ty + 16 * i], tile_lo[4 * tx + 1][ty + 16 * i],
-                          tile_lo[4 * tx + 2][ty + 16 * i], tile_lo[4 * tx + 3][ty + 16 * i]);
-      }
-    }
-    __syncthreads();
-  }
-  if (gb) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float v = bsum[i];
-#pragma unroll
-      for (int d = 8; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);  // 16-lane row
-      const int o = o0 + ty + 16 * i;
-      if (tx == 0 && o < outC) atomicAdd(gb + o, v);
-    }
-  }
+// MN-major A operands (M contiguous: the channels of the weight gradient's
+// columns, the pixels of the grad-column kernel's grad_out).  For 32-bit
+// operands the tensor core takes MN-major tiles only in the "128-byte
+// swizzle, 32-byte atom" layout: an atom is 4 K rows x 128 B (32 M elements),
+// and within it the 32-byte chunk c of row r sits at chunk position c ^ r --
+// exactly what TMA writes for a box of 32 elements x K rows with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.  Atoms: K groups of 4 rows at
+// W_SBO = 512 B, M blocks of 32 at W_LBO = 4096 B (16 KB per 128 x 32 stage).
+constexpr int W_LBO = 4096, W_SBO = 512;
+
+// Instruction descriptor with A MN-major (bit 15), B K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) {
+  return tc::idesc_tf32(M, N) | (1u << 15);
+}
+__device__ __forceinline__ uint64_t sdesc_sw128b32_mn(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(W_LBO >> 4) << 16) |
+         ((uint64_t)(W_SBO >> 4) << 32) | (1ull << 46) | (1ull << 61);
 }
 
 // ---------------------------------------------------------------------------
@@ -194,17 +156,19 @@ size_t data_smem_bytes(bool split) {
 // Cg % 128 == 0, or 128 / Cg whole taps when Cg is 32 or 64 (the last slot
 // of a group may reach past its last tap; those columns are not used).  A
 // tile is (128 pixels, group, range of slots); slots are independent here,
-// so splitting them evens out the CTAs' loads.
+// so splitting them evens out the CTAs' loads.  The pixel side counts
+// 32-pixel blocks of one image each (`bpi` per image, the last one partial):
+// a tile is 4 consecutive blocks, one per tensor-memory lane quarter, and
+// each block's grad_out rows come from its own image.
 struct DTile {
-  long long q0;
+  int b0;  // first 32-pixel block
   int gi, s0, s1;
 };
 __device__ __forceinline__ DTile dtile_of(int t, int mtiles, int nslots, int ksplits) {
   DTile T;
   const int ks = t % ksplits;
   const int r = t / ksplits;
-  const int mt = r % mtiles;
-  T.q0 = (long long)mt * D_BM;
+  T.b0 = (r % mtiles) * 4;
   T.gi = r / mtiles;
   T.s0 = ks * nslots / ksplits;
   T.s1 = (ks + 1) * nslots / ksplits;
@@ -277,7 +241,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
                                                const float* __restrict__ mask,
                                                float* __restrict__ gxt, float* __restrict__ goff,
                                                float* __restrict__ gmask, float* __restrict__ col,
-                                               long long col_lo, int& plan_key) {
+                                               long long col_lo, long long qend, int& plan_key) {
   float* T = reinterpret_cast<float*>(scratch);
   PixPlan* plan = reinterpret_cast<PixPlan*>(scratch + EPI_T_BYTES);
   const int quad = lane & 3, sub = lane >> 2;
@@ -291,7 +255,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
     float4 wv4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 geo = make_float4(0.f, 0.f, 0.f, 0.f);
     int4 idx = make_int4(-1, 0, 0, 0);
-    if (row_q < g.NP) {
+    if (row_q < qend) {
       const int n = (int)(row_q / g.P);
       const int p = (int)(row_q - (long long)n * g.P);
       const int oy = p / g.Wo, ox = p - oy * g.Wo;
@@ -360,7 +324,7 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
         cv[e] = mw[0] * a[e] + mw[1] * b[e] + mw[2] * c[e] + mw[3] * d[e];
       }
     }
-    if (col != nullptr && qbase + px < g.NP) {  // every (k, q, c) is written, voids as 0
+    if (col != nullptr && qbase + px < qend) {  // every (k, q, c) is written, voids as 0
       float* dst = col + ((long long)k * g.NP + qbase + px) * g.C + gch0 + quad * 8;
       float hi[8];
 #pragma unroll
@@ -435,16 +399,17 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
 // channels of one group; per tap a K = Og GEMM into one of two tensor-memory
 // accumulators (taps alternate), consumed by 16 epilogue warps while the next
 // tap accumulates.
-//   warp 0      TMA producer: go_t rows (128 pixels x 32 out channels) and
-//               packed weight rows (128 channels x 32 out channels) per K step
+//   warp 0      TMA producer per K step: go_r rows of the tile's image (32
+//               out channels x 128 pixels, an MN-major operand in four
+//               32-pixel boxes) and packed weight rows (128 channels x 32 out
+//               channels)
 //   warp 1      MMA issue: 4 UMMAs 128 x 128 x 8 per K step
 //   warps 2-17  epilogue (epilogue_chunk)
 template <bool SPLIT>
 __global__ void __launch_bounds__(DCfg<SPLIT>::THREADS, 1)
 bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
-                   const __grid_constant__ CUtensorMap amap_lo,
-                   const __grid_constant__ CUtensorMap bmap, int mtiles, int nslots, int ksplits,
-                   int ntiles,
+                   const __grid_constant__ CUtensorMap bmap, int bpi, int nblocks, int mtiles,
+                   int nslots, int ksplits, int ntiles,
                    const float* __restrict__ xt, const float* __restrict__ off,
                    const float* __restrict__ mask, float* __restrict__ gxt,
                    float* __restrict__ goff, float* __restrict__ gmask,
@@ -492,6 +457,16 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
       int gs = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const DTile T = dtile_of(t, mtiles, nslots, ksplits);
+        // per block: go_r row of out channel 0 of its image, first pixel; a
+        // block past the last image loads past the row end (zero fill)
+        int arow[4], ax[4];
+#pragma unroll
+        for (int mb = 0; mb < 4; ++mb) {
+          const int b = T.b0 + mb;
+          const int n = b < nblocks ? b / bpi : 0;
+          arow[mb] = n * g.outC + T.gi * g.Og;
+          ax[mb] = b < nblocks ? (b - n * bpi) * 32 : bpi * 32;
+        }
         for (int sl = T.s0; sl < T.s1; ++sl) {
           const int brow = T.gi * g.kk * g.Cg + sl * D_BN;
           for (int s = 0; s < ochunks; ++s, ++gs) {
@@ -500,10 +475,16 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
             tc::mbar_arrive_expect_tx(&full[st], SSTAGE);
             const uint32_t sA = s0 + st * SSTAGE;
-            tc::tma_load_2d(sA, &amap, T.gi * g.Og + s * 32, (int)T.q0, &full[st]);
+            // pixels past the image's last one are outside the map: zero fill
+#pragma unroll
+            for (int mb = 0; mb < 4; ++mb)
+              tc::tma_load_2d(sA + mb * W_LBO, &amap, ax[mb], arow[mb] + s * 32, &full[st]);
             tc::tma_load_2d(sA + D_BM * 128, &bmap, s * 32, brow, &full[st]);
-            if constexpr (SPLIT) {  // low parts
-              tc::tma_load_2d(sA + D_STAGE, &amap_lo, T.gi * g.Og + s * 32, (int)T.q0, &full[st]);
+            if constexpr (SPLIT) {  // low parts: rows N*outC further
+#pragma unroll
+              for (int mb = 0; mb < 4; ++mb)
+                tc::tma_load_2d(sA + D_STAGE + mb * W_LBO, &amap, ax[mb],
+                                g.N * g.outC + arow[mb] + s * 32, &full[st]);
               tc::tma_load_2d(sA + D_STAGE + D_BM * 128, &bmap, s * 32, g.G * g.kk * g.Cg + brow,
                               &full[st]);
             }
@@ -514,7 +495,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     __syncwarp();
   } else if (warp == D_MMA_WARP) {
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_tf32(D_BM, D_BN);
+      const uint32_t idesc = idesc_tf32_amn(D_BM, D_BN);
       int gs = 0, gt = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const DTile T = dtile_of(t, mtiles, nslots, ksplits);
@@ -530,16 +511,17 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             const uint32_t sA = s0 + st * SSTAGE, sB = sA + D_BM * 128;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
+              // A: MN-major, K rows j * 8 .. j * 8 + 7 of the stage
               if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
-                tc::umma_tf32(d, tc::sdesc_sw128(sA + D_STAGE + j * 32),
+                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + D_STAGE + j * 2 * W_SBO),
                               tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
-                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32),
+                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
                               tc::sdesc_sw128(sB + D_STAGE + j * 32), idesc, 1u);
-                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32),
-                              idesc, 1u);
+                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                              tc::sdesc_sw128(sB + j * 32), idesc, 1u);
               } else {
-                tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32),
-                              idesc, (s | j) != 0 ? 1u : 0u);
+                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                              tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
               }
             }
             tc::umma_commit(&empty[st]);
@@ -557,7 +539,13 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     int gt = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const DTile T = dtile_of(t, mtiles, nslots, ksplits);
-      const long long qbase = T.q0 + lq * 32;
+      // this lane quarter's block: pixels qbase .. qbase + 31 of the flat
+      // (image, pixel) index, valid below qend (0 for a block past the end)
+      const int blk = T.b0 + lq;
+      const int bn_ = blk < nblocks ? blk / bpi : 0;
+      const long long qbase =
+          blk < nblocks ? (long long)bn_ * g.P + (long long)(blk - bn_ * bpi) * 32 : 0;
+      const long long qend = blk < nblocks ? (long long)bn_ * g.P + g.P : 0;
       const long long row_q = qbase + lane;
       const long long col_lo = SPLIT ? (long long)g.kk * g.NP * g.C : 0;
       int plan_key = -1;
@@ -590,7 +578,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
           const int k = row / g.Cg;
           if (k < g.kk)
             epilogue_chunk(g, k, vals, T.gi * g.Cg + (row - k * g.Cg), row_q, qbase, lane,
-                           scratch, xt, off, mask, gxt, goff, gmask, col, col_lo, plan_key);
+                           scratch, xt, off, mask, gxt, goff, gmask, col, col_lo, qend,
+                           plan_key);
         }
       }
     }
@@ -648,23 +637,6 @@ __global__ void __launch_bounds__(256) plan_kernel(Geom g, const float* __restri
 // bwd_weight_tc
 // ---------------------------------------------------------------------------
 constexpr int W_BM = 128;  // channels of one tap per CTA
-// MN-major A (channels contiguous).  For 32-bit operands the tensor core
-// takes MN-major tiles only in the "128-byte swizzle, 32-byte atom" layout:
-// an atom is 4 K rows (pixels) x 128 B (32 channels), and within it the
-// 32-byte chunk c of row r sits at chunk position c ^ r.  Atoms: K groups of
-// 4 pixels at W_SBO = 512 B, channel blocks of 32 at W_LBO = 4096 B
-// (16 KB per 128-channel x 32-pixel stage).
-constexpr int W_LBO = 4096, W_SBO = 512;
-
-
-// Instruction descriptor with A MN-major (bit 15), B K-major.
-__host__ __device__ constexpr uint32_t idesc_tf32_amn(int M, int N) {
-  return tc::idesc_tf32(M, N) | (1u << 15);
-}
-__device__ __forceinline__ uint64_t sdesc_sw128b32_mn(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(W_LBO >> 4) << 16) |
-         ((uint64_t)(W_SBO >> 4) << 32) | (1ull << 46) | (1ull << 61);
-}
 // Byte offset of channel quad `quad` (channels 4*quad .. 4*quad+3 of a
 // 32-channel block) of pixel `pix` (0..31 of the stage) in one channel block.
 __device__ __forceinline__ uint32_t mn32_offset(int pix, int quad) {
@@ -1215,26 +1187,17 @@ bool tc_bwd_supported(const Geom& g) {
 
 bool tc_wgather_supported(const Geom& g) { return tc_bwd_supported(g) && g.Cg % W_BM == 0; }
 
-bool tc_prep_sums_bias(const Geom& g, const float* go) {
-  return g.P % 4 == 0 && g.outC % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
-         (g.outC + 63) / 64 <= 65535 && g.N <= 65535;
-}
-
-cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
-                              float* go_r, float* gb, cudaStream_t stream) {
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_r, float* gb,
+                              bool split, cudaStream_t stream) {
   if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
-  if (tc_prep_sums_bias(g, go) && (reinterpret_cast<uintptr_t>(go_t) & 15u) == 0 &&
-      (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0 &&
-      (reinterpret_cast<uintptr_t>(go_t_lo) & 15u) == 0) {
-    dim3 grid((g.P + PG_SPAN - 1) / PG_SPAN, (g.outC + 63) / 64, g.N);
-    prep_go4_kernel<<<grid, 256, 0, stream>>>(go, go_t, go_t_lo, go_r, gb, g.N, g.outC, g.P);
-    return cudaGetLastError();
-  }
-  if (gb != nullptr) return cudaErrorInvalidValue;  // the scalar kernel leaves grad_bias alone
   const int Ppad = (g.P + 3) & ~3;
-  dim3 grid((Ppad + 31) / 32, (g.outC + 31) / 32, g.N);
-  prep_go_kernel<<<grid, dim3(32, 8), 0, stream>>>(go, go_t, go_t_lo, go_r, g.N, g.outC, g.P,
-                                                   Ppad);
+  const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
+  const long long blocks = (long long)g.N * g.outC * pspans;
+  if (blocks > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  const int vec = g.P % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0;
+  prep_go_kernel<<<(unsigned)blocks, 256, 0, stream>>>(go, go_r, gb, g.N, g.outC, g.P, Ppad,
+                                                       pspans, split ? 1 : 0, vec);
   return cudaGetLastError();
 }
 
@@ -1248,17 +1211,16 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
-                               const float* wbt, const float* xt, const float* off,
-                               const float* mask, float* gxt, float* goff, float* gmask,
-                               float* col, cudaStream_t stream) {
-  const bool split = go_t_lo != nullptr;
-  CUtensorMap amap, amap_lo, bmap;
-  cudaError_t e = make_tmap_2d_f32(&amap, go_t, (uint64_t)g.outC, (uint64_t)g.NP,
-                                   (uint64_t)g.outC, (uint32_t)D_BM);
-  if (e != cudaSuccess) return e;
-  e = make_tmap_2d_f32(&amap_lo, split ? go_t_lo : go_t, (uint64_t)g.outC, (uint64_t)g.NP,
-                       (uint64_t)g.outC, (uint32_t)D_BM);
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, const float* wbt,
+                               const float* xt, const float* off, const float* mask, float* gxt,
+                               float* goff, float* gmask, float* col, cudaStream_t stream) {
+  const int Ppad = (g.P + 3) & ~3;
+  CUtensorMap amap, bmap;
+  // go_r viewed as N*outC (x2 in 3xTF32) rows of P pixels, Ppad apart: boxes
+  // of 32 pixels x 32 rows, MN-major swizzle
+  cudaError_t e = make_tmap_2d_f32(&amap, go_r, (uint64_t)g.P,
+                                   (uint64_t)g.N * g.outC * (split ? 2 : 1), (uint64_t)Ppad, 32u,
+                                   /*atom32=*/true);
   if (e != cudaSuccess) return e;
   e = make_tmap_2d_f32(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg * (split ? 2 : 1),
                        (uint64_t)g.Og, (uint32_t)D_BN);
@@ -1271,7 +1233,10 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int mtiles = (int)((g.NP + D_BM - 1) / D_BM);
+  const int bpi = (g.P + 31) / 32;  // 32-pixel blocks per image
+  if ((long long)g.N * bpi > (1LL << 30)) return cudaErrorInvalidValue;
+  const int nblocks = g.N * bpi;
+  const int mtiles = (nblocks + 3) / 4;
   const int nslots = (g.kk * g.Cg + D_BN - 1) / D_BN;
   const long long base = (long long)mtiles * g.G;
   // split the slots so the busiest CTA carries the fewest
@@ -1288,8 +1253,9 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go
   const long long ntiles = base * ksplits;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < sms ? ntiles : sms);
-  kern<<<grid, threads, smem, stream>>>(g, amap, amap_lo, bmap, mtiles, nslots, ksplits,
-                                         (int)ntiles, xt, off, mask, gxt, goff, gmask, col);
+  kern<<<grid, threads, smem, stream>>>(g, amap, bmap, bpi, nblocks, mtiles, nslots, ksplits,
+                                         (int)ntiles,
+                                         xt, off, mask, gxt, goff, gmask, col);
   return cudaGetLastError();
 }
 

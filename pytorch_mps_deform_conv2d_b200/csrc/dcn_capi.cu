@@ -302,7 +302,6 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));           // grad x (NHWC)
   if (use_tc_bwd(g, flags)) {
     const size_t parts = split_math(flags) ? 2 : 1;                   // high (+ low) TF32 parts
-    b += parts * align_up((size_t)g.N * g.outC * g.P * sizeof(float));         // go_t
     b += align_up(parts * g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));   // go_r
     b += align_up(parts * g.outC * g.Cg * g.kk * sizeof(float));               // packed weight
     if (use_col_path(g, flags))
@@ -603,17 +602,17 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   const bool tc_bwd = use_tc_bwd(g, flags);
   const bool skip = g.N == 0 || g.C == 0 || g.outC == 0 || g.P == 0;  // .mm:779-782
   // the tensor-core prep kernel sums grad_bias while it reads grad_output
-  const bool bias_in_prep =
-      grad_bias != nullptr && tc_bwd && !skip && dcn::tc_prep_sums_bias(g, grad_output);
+  const bool bias_in_prep = grad_bias != nullptr && tc_bwd && !skip;
   const bool no_pixels = (long long)g.N * g.P == 0;
   // Zero what the kernels accumulate into (.mm:764-777 zero-initialise too),
-  // in one launch.
+  // in one launch; the tensor-core path zeroes on its side streams instead.
   dcn::ZeroList z{};
   z.add(grad_offset, (long long)(off_bytes / sizeof(float)));
   z.add(grad_mask, (long long)(msk_bytes / sizeof(float)));
   z.add(grad_weight, (long long)(w_bytes / sizeof(float)));
-  if (bias_in_prep || no_pixels) z.add(grad_bias, g.outC);
-  DCN_CUDA(dcn::launch_zero(z, stream), "zero");
+  if (no_pixels) z.add(grad_bias, g.outC);
+  const bool zero_on_side = tc_bwd && !skip;
+  if (!zero_on_side) DCN_CUDA(dcn::launch_zero(z, stream), "zero");
   if (grad_bias != nullptr && !bias_in_prep && !no_pixels)
     DCN_CUDA(dcn::launch_grad_bias(grad_output, grad_bias, g, stream), "grad_bias");
   if (skip) {
@@ -641,26 +640,31 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   if (tc_bwd) {
     const bool split = split_math(flags);
     const size_t parts = split ? 2 : 1;
-    float* go_t = ws.take((size_t)g.N * g.outC * g.P);
-    float* go_t_lo = split ? ws.take((size_t)g.N * g.outC * g.P) : nullptr;
     float* go_r = ws.take(parts * g.N * g.outC * ((g.P + 3) & ~3));
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     const bool colp = use_col_path(g, flags);
     float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
-    // grad_out prep (side 0, after the zeroing of grad_bias above) and the
-    // weight pack (side 1) run beside the input transpose
+    // grad_out prep (side 0, after zeroing grad_bias, which it sums into) and
+    // the weight pack + the zeroing of the other accumulators (side 1) run
+    // beside the input transpose
     Fork fk(stream);
     DCN_ORDER(fk.fork(), "fork");
+    if (bias_in_prep) {
+      dcn::ZeroList zb{};
+      zb.add(grad_bias, g.outC);
+      DCN_CUDA_ON(fk.side(0), dcn::launch_zero(zb, fk.side(0)), "zero");
+    }
     DCN_CUDA_ON(fk.side(0),
-                dcn::launch_tc_prep_go(g, grad_output, go_t, go_t_lo, go_r,
-                                       bias_in_prep ? grad_bias : nullptr, fk.side(0)),
+                dcn::launch_tc_prep_go(g, grad_output, go_r, bias_in_prep ? grad_bias : nullptr,
+                                       split, fk.side(0)),
                 "tc_prep_go");
     DCN_CUDA_ON(fk.side(1), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(1)),
                 "tc_pack_weight_bwd");
+    DCN_CUDA_ON(fk.side(1), dcn::launch_zero(z, fk.side(1)), "zero");
     DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
-    DCN_CUDA(dcn::launch_bwd_data_tc(g, go_t, go_t_lo, wbt, xt, offset, mask, gxt, grad_offset,
+    DCN_CUDA(dcn::launch_bwd_data_tc(g, go_r, split, wbt, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, col, stream),
              "bwd_data_tc");
     if (nhwc) {  // grad_input is complete: nothing to transpose

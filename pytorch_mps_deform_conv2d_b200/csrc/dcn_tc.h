@@ -40,25 +40,22 @@ cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, co
 // weight-gradient kernel does too (128-channel multiples only).
 bool tc_bwd_supported(const Geom& g);
 bool tc_wgather_supported(const Geom& g);
-// go -> go_t / go_r (tf32-rounded).  With `go_t_lo` (3xTF32) the low TF32
-// parts go to go_t_lo and to a second copy of go_r's rows after the first.
-// When tc_prep_sums_bias(g, go), `gb` (NULL or grad_bias, zeroed by the
-// caller) also receives the bias gradient; otherwise `gb` must be NULL.
-bool tc_prep_sums_bias(const Geom& g, const float* go);
-cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_t, float* go_t_lo,
-                              float* go_r, float* gb, cudaStream_t stream);
+// go -> go_r (NCHW, rows padded to Ppad = P rounded up to 4, tf32-rounded);
+// with `split` (3xTF32) the low TF32 parts follow in rows N*outC ...  `gb`
+// (NULL or grad_bias, zeroed by the caller) also receives the bias gradient.
+cudaError_t launch_tc_prep_go(const Geom& g, const float* go, float* go_r, float* gb,
+                              bool split, cudaStream_t stream);
 cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g, bool split,
                                       cudaStream_t stream);
 // grad_col = W^T go on the tensor core per (pixel tile, tap), fused with the
 // col2im scatter into gxt (NHWC, pre-zeroed) and the coordinate / mask
-// reductions into goff / gmask (pre-zeroed).
-// `go_t_lo` non-NULL selects 3xTF32 (wbt then holds high and low parts).
-// `col` non-NULL: also writes the column buffer (tc_col_bytes) that
+// reductions into goff / gmask (pre-zeroed).  `go_r` as written by
+// launch_tc_prep_go; `split` selects 3xTF32 (wbt then holds high and low
+// parts).  `col` non-NULL: also writes the column buffer (tc_col_bytes) that
 // launch_bwd_weight_col reads.
-cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_t, const float* go_t_lo,
-                               const float* wbt, const float* xt, const float* off,
-                               const float* mask, float* gxt, float* goff, float* gmask,
-                               float* col, cudaStream_t stream);
+cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, const float* wbt,
+                               const float* xt, const float* off, const float* mask, float* gxt,
+                               float* goff, float* gmask, float* col, cudaStream_t stream);
 // Weight gradient as a dense TMA-fed GEMM over the column buffer.
 bool tc_wcol_supported(const Geom& g, bool split);
 size_t tc_col_bytes(const Geom& g, bool split);
