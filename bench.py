@@ -114,8 +114,10 @@ def algorithmic_work(wl):
 
 
 # tcgen05 kernels (TF32 operands; 3xTF32 issues three products per multiply-add)
-TC_KERNELS = ("fwd_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col", "fwd_tc_bf16")
-BF16_KERNELS = ("fwd_tc_bf16",)  # kind::f16 with bf16 operands
+TC_KERNELS = ("fwd_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col", "fwd_tc_bf16",
+              "fwd_tc_f16")
+BF16_KERNELS = ("fwd_tc_bf16", "fwd_tc_f16")  # kind::f16 with 16-bit operands
+HALF = {"bf16": "bfloat16", "fp16": "float16"}
 
 
 def kernel_work(name, wl):
@@ -336,8 +338,9 @@ def run_ours(args, wl):
         cut = lambda t: None if t is None else t[first:first + count, :, rows].contiguous()
         x = x[first:first + count].contiguous()
         off, m, go = cut(off), cut(m), cut(go)
-    if args.dtype == "bf16":  # bf16 I/O: every tensor (and gradient) bf16
-        x, w, b, off, m, go = (None if t is None else t.to(torch.bfloat16)
+    if args.dtype in HALF:  # 16-bit I/O: every tensor (and gradient) bf16 / fp16
+        hdt = getattr(torch, HALF[args.dtype])
+        x, w, b, off, m, go = (None if t is None else t.to(hdt)
                                for t in (x, w, b, off, m, go))
     if args.layout == "nhwc":  # channels-last input (and grad_input), same values
         x = x.contiguous(memory_format=torch.channels_last)
@@ -480,7 +483,7 @@ def run_ours(args, wl):
         "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": False, "scaling": args.scaling, "vs_baseline": None,
-        "dtype": (("bf16 I/O, " if args.dtype == "bf16" else "") +
+        "dtype": ((f"{args.dtype} I/O, " if args.dtype in HALF else "") +
                   (args.math if any(k in TC_KERNELS for k in kernels) else "f32")),
         "data": "synthetic",
         "config": {"workload": wl["desc"],
@@ -558,8 +561,8 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
     import pytorch_mps_deform_conv2d_b200 as dcn
     mod = dcn.DeformConv2d(wl["C"], wl["outC"], wl["k"], stride=wl["stride"], padding=wl["pad"],
                            dilation=wl["dil"], groups=wl["groups"], bias=wl["bias"]).to(dev)
-    if args.dtype == "bf16":
-        mod = mod.to(torch.bfloat16)
+    if args.dtype in HALF:
+        mod = mod.to(getattr(torch, HALF[args.dtype]))
     with torch.no_grad():
         mod.weight.copy_(w)
         if b is not None:
@@ -685,7 +688,7 @@ def main():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="weak: every rank a whole batch; strong: the one batch split over the "
                          "ranks (images, then row slabs of each image)")
-    ap.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32",
+    ap.add_argument("--dtype", choices=["fp32", "bf16", "fp16"], default="fp32",
                     help="tensor dtype of the step (the reference and the headline: fp32)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="neck")
     ap.add_argument("--layout", choices=["nchw", "nhwc"], default="nchw",

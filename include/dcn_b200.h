@@ -166,6 +166,21 @@ DCN_API int dcn_backward_bf16(const dcn_shape* shape, const void* grad_output, c
                               void* grad_weight, void* grad_bias, uint32_t flags,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* fp16 forward and backward (no reference counterpart): as the bf16 entry
+ * points with every tensor argument and gradient fp16; the tensor-core
+ * forward runs kind::f16 UMMAs with fp16 operands. */
+DCN_API size_t dcn_forward_f16_workspace_size(const dcn_shape* shape, uint32_t flags);
+DCN_API int dcn_forward_f16(const dcn_shape* shape, const void* input, const void* weight,
+                            const void* offset, const void* mask, const void* bias, void* output,
+                            uint32_t flags, void* workspace, size_t workspace_bytes,
+                            void* stream);
+DCN_API size_t dcn_backward_f16_workspace_size(const dcn_shape* shape, uint32_t flags);
+DCN_API int dcn_backward_f16(const dcn_shape* shape, const void* grad_output, const void* input,
+                             const void* weight, const void* offset, const void* mask,
+                             void* grad_input, void* grad_offset, void* grad_mask,
+                             void* grad_weight, void* grad_bias, uint32_t flags, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Forward pass; replaces deform_conv2d_forward (.mm:192-374).
  * output = bias + sum_{c,k} weight * mask * bilinear(input, sample(offset)). */
 DCN_API int dcn_forward(const dcn_shape* shape, const float* input, const float* weight,

@@ -91,6 +91,14 @@ def load_capi():
         lib.dcn_backward_bf16_workspace_size.restype = sz
         lib.dcn_backward_bf16.argtypes = [shp] + [vp] * 10 + [u32, vp, sz, vp]
         lib.dcn_backward_bf16.restype = ctypes.c_int
+        lib.dcn_forward_f16_workspace_size.argtypes = [shp, u32]
+        lib.dcn_forward_f16_workspace_size.restype = sz
+        lib.dcn_forward_f16.argtypes = [shp] + [vp] * 6 + [u32, vp, sz, vp]
+        lib.dcn_forward_f16.restype = ctypes.c_int
+        lib.dcn_backward_f16_workspace_size.argtypes = [shp, u32]
+        lib.dcn_backward_f16_workspace_size.restype = sz
+        lib.dcn_backward_f16.argtypes = [shp] + [vp] * 10 + [u32, vp, sz, vp]
+        lib.dcn_backward_f16.restype = ctypes.c_int
         lib.dcn_col2im.argtypes = [vp] * 4 + [i64] * 12 + [vp]
         lib.dcn_col2im.restype = ctypes.c_int
         lib.dcn_col2im_coord.argtypes = [vp] * 6 + [i64] * 12 + [vp]

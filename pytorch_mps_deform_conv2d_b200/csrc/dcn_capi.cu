@@ -489,18 +489,12 @@ size_t fwd_bf16_ws(const dcn::Geom& g, uint32_t flags) {
 }
 }  // namespace
 
-extern "C" {
-
-DCN_API size_t dcn_forward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
-  dcn::Geom g;
-  if (make_geom(s, true, true, g, "dcn_forward_bf16_workspace_size") != DCN_OK) return 0;
-  return fwd_bf16_ws(g, flags);
-}
-
-DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* weight,
-                             const void* offset, const void* mask, const void* bias,
-                             void* output, uint32_t flags, void* workspace,
-                             size_t workspace_bytes, void* stream_) {
+// The 16-bit forward, bf16 or fp16 (`f16`): the tensor-core kernel with
+// 16-bit operands where it covers the shape, else the fp32 path on upcast
+// copies with the output rounded back.
+static int forward_h16(bool f16, const dcn_shape* s, const void* input, const void* weight,
+                       const void* offset, const void* mask, const void* bias, void* output,
+                       uint32_t flags, void* workspace, size_t workspace_bytes, void* stream_) {
   g_last_error.clear();
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
@@ -509,14 +503,15 @@ DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;
+  const char* tname = f16 ? "float16" : "bfloat16";
   auto dev_or_empty = [](const void* p, long long n) { return n == 0 || is_device_ptr(p); };
   DCN_CHECK(is_device_ptr(output), "deform_conv2d_forward: output must be a CUDA device buffer");
   DCN_CHECK(dev_or_empty(input, (long long)g.N * g.C * g.HW) &&
                 dev_or_empty(offset, (long long)g.N * 2 * g.dg * g.kk * g.P) &&
                 dev_or_empty(weight, (long long)g.outC * g.Cg * g.kk),
             "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
-  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a bfloat16 CUDA tensor");
-  DCN_CHECK(bias == nullptr || is_device_ptr(bias), "bias must be a bfloat16 CUDA tensor");
+  DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a %s CUDA tensor", tname);
+  DCN_CHECK(bias == nullptr || is_device_ptr(bias), "bias must be a %s CUDA tensor", tname);
   const size_t need = fwd_bf16_ws(g, flags);
   if (workspace_bytes < need || workspace == nullptr)
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
@@ -536,12 +531,12 @@ DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* 
                "nchw_to_nhwc");
     }
     DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, stream), "tc_pack_weight");
-    DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, num_sms_current(),
-                                     stream),
-             "fwd_tc_bf16");
+    DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, f16,
+                                     num_sms_current(), stream),
+             f16 ? "fwd_tc_f16" : "fwd_tc_bf16");
     return DCN_OK;
   }
-  // upcast route: fp32 copies, the fp32 forward, the result rounded to bf16
+  // upcast route: fp32 copies, the fp32 forward, the result rounded back
   Carver ws(base);
   const long long nx = (long long)g.N * g.C * g.HW, nw = (long long)g.outC * g.Cg * g.kk;
   const long long noff = (long long)g.N * 2 * g.dg * g.kk * g.P;
@@ -552,18 +547,50 @@ DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* 
   float* m32 = ws.take(nm);
   float* b32 = ws.take(g.outC);
   float* out32 = ws.take(out_numel);
-  DCN_CUDA(dcn::launch_bf16_to_f32(input, x32, nx, stream), "bf16_to_f32");
-  DCN_CUDA(dcn::launch_bf16_to_f32(weight, w32, nw, stream), "bf16_to_f32");
-  DCN_CUDA(dcn::launch_bf16_to_f32(offset, off32, noff, stream), "bf16_to_f32");
-  if (mask) DCN_CUDA(dcn::launch_bf16_to_f32(mask, m32, nm, stream), "bf16_to_f32");
-  if (bias) DCN_CUDA(dcn::launch_bf16_to_f32(bias, b32, g.outC, stream), "bf16_to_f32");
+  const char* up = f16 ? "f16_to_f32" : "bf16_to_f32";
+  DCN_CUDA(dcn::launch_h16_to_f32(input, x32, nx, f16, stream), up);
+  DCN_CUDA(dcn::launch_h16_to_f32(weight, w32, nw, f16, stream), up);
+  DCN_CUDA(dcn::launch_h16_to_f32(offset, off32, noff, f16, stream), up);
+  if (mask) DCN_CUDA(dcn::launch_h16_to_f32(mask, m32, nm, f16, stream), up);
+  if (bias) DCN_CUDA(dcn::launch_h16_to_f32(bias, b32, g.outC, f16, stream), up);
   const size_t used = bf16_upcast_bytes(g);
   rc = dcn_forward(s, x32, w32, off32, mask ? m32 : nullptr, bias ? b32 : nullptr, out32, flags,
                    base + used, workspace_bytes - (size_t)(base - static_cast<char*>(workspace)) - used,
                    stream_);
   if (rc != DCN_OK) return rc;
-  DCN_CUDA(dcn::launch_f32_to_bf16(out32, output, out_numel, stream), "f32_to_bf16");
+  DCN_CUDA(dcn::launch_f32_to_h16(out32, output, out_numel, f16, stream),
+           f16 ? "f32_to_f16" : "f32_to_bf16");
   return DCN_OK;
+}
+
+extern "C" {
+
+DCN_API size_t dcn_forward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_forward_bf16_workspace_size") != DCN_OK) return 0;
+  return fwd_bf16_ws(g, flags);
+}
+
+DCN_API int dcn_forward_bf16(const dcn_shape* s, const void* input, const void* weight,
+                             const void* offset, const void* mask, const void* bias,
+                             void* output, uint32_t flags, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return forward_h16(false, s, input, weight, offset, mask, bias, output, flags, workspace,
+                     workspace_bytes, stream);
+}
+
+DCN_API size_t dcn_forward_f16_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_forward_f16_workspace_size") != DCN_OK) return 0;
+  return fwd_bf16_ws(g, flags);
+}
+
+DCN_API int dcn_forward_f16(const dcn_shape* s, const void* input, const void* weight,
+                            const void* offset, const void* mask, const void* bias, void* output,
+                            uint32_t flags, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  return forward_h16(true, s, input, weight, offset, mask, bias, output, flags, workspace,
+                     workspace_bytes, stream);
 }
 
 static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
@@ -771,7 +798,7 @@ DCN_API int dcn_backward_rows(const dcn_shape* s, int64_t row_begin, int64_t row
                        workspace_bytes, stream);
 }
 
-// fp32 copies for dcn_backward_bf16: grad_output, input, weight, offset,
+// fp32 copies for the 16-bit backward: grad_output, input, weight, offset,
 // mask, and the five gradients (input, offset, mask, weight, bias).
 static size_t bwd_bf16_copy_bytes(const dcn::Geom& g) {
   const size_t x = align_up((size_t)g.N * g.C * g.HW * 4), w = align_up((size_t)g.outC * g.Cg * g.kk * 4);
@@ -787,11 +814,13 @@ DCN_API size_t dcn_backward_bf16_workspace_size(const dcn_shape* s, uint32_t fla
   return bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
 }
 
-DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const void* input,
-                              const void* weight, const void* offset, const void* mask,
-                              void* grad_input, void* grad_offset, void* grad_mask,
-                              void* grad_weight, void* grad_bias, uint32_t flags,
-                              void* workspace, size_t workspace_bytes, void* stream_) {
+// The 16-bit backward (bf16, or fp16 with `f16`): the fp32 backward on upcast
+// copies, the gradients rounded back.
+static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, const void* input,
+                        const void* weight, const void* offset, const void* mask,
+                        void* grad_input, void* grad_offset, void* grad_mask, void* grad_weight,
+                        void* grad_bias, uint32_t flags, void* workspace,
+                        size_t workspace_bytes, void* stream_) {
   g_last_error.clear();
   dcn::Geom g;
   int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
@@ -816,23 +845,51 @@ DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const
   float* goff32 = ws.take(noff);
   float* gm32 = ws.take(nm);
   float* gb32 = ws.take(g.outC);
-  DCN_CUDA(dcn::launch_bf16_to_f32(grad_output, go32, ngo, stream), "bf16_to_f32");
-  DCN_CUDA(dcn::launch_bf16_to_f32(input, x32, nx, stream), "bf16_to_f32");
-  DCN_CUDA(dcn::launch_bf16_to_f32(weight, w32, nw, stream), "bf16_to_f32");
-  DCN_CUDA(dcn::launch_bf16_to_f32(offset, off32, noff, stream), "bf16_to_f32");
-  if (mask) DCN_CUDA(dcn::launch_bf16_to_f32(mask, m32, nm, stream), "bf16_to_f32");
+  const char* up = f16 ? "f16_to_f32" : "bf16_to_f32";
+  const char* down = f16 ? "f32_to_f16" : "f32_to_bf16";
+  DCN_CUDA(dcn::launch_h16_to_f32(grad_output, go32, ngo, f16, stream), up);
+  DCN_CUDA(dcn::launch_h16_to_f32(input, x32, nx, f16, stream), up);
+  DCN_CUDA(dcn::launch_h16_to_f32(weight, w32, nw, f16, stream), up);
+  DCN_CUDA(dcn::launch_h16_to_f32(offset, off32, noff, f16, stream), up);
+  if (mask) DCN_CUDA(dcn::launch_h16_to_f32(mask, m32, nm, f16, stream), up);
   const size_t used = bwd_bf16_copy_bytes(g);
   rc = dcn_backward(s, go32, x32, w32, off32, mask ? m32 : nullptr, gx32, goff32,
                     mask ? gm32 : nullptr, gw32, grad_bias ? gb32 : nullptr, flags, base + used,
                     workspace_bytes - (size_t)(base - static_cast<char*>(workspace)) - used,
                     stream_);
   if (rc != DCN_OK) return rc;
-  DCN_CUDA(dcn::launch_f32_to_bf16(gx32, grad_input, nx, stream), "f32_to_bf16");
-  DCN_CUDA(dcn::launch_f32_to_bf16(goff32, grad_offset, noff, stream), "f32_to_bf16");
-  if (mask) DCN_CUDA(dcn::launch_f32_to_bf16(gm32, grad_mask, nm, stream), "f32_to_bf16");
-  DCN_CUDA(dcn::launch_f32_to_bf16(gw32, grad_weight, nw, stream), "f32_to_bf16");
-  if (grad_bias) DCN_CUDA(dcn::launch_f32_to_bf16(gb32, grad_bias, g.outC, stream), "f32_to_bf16");
+  DCN_CUDA(dcn::launch_f32_to_h16(gx32, grad_input, nx, f16, stream), down);
+  DCN_CUDA(dcn::launch_f32_to_h16(goff32, grad_offset, noff, f16, stream), down);
+  if (mask) DCN_CUDA(dcn::launch_f32_to_h16(gm32, grad_mask, nm, f16, stream), down);
+  DCN_CUDA(dcn::launch_f32_to_h16(gw32, grad_weight, nw, f16, stream), down);
+  if (grad_bias) DCN_CUDA(dcn::launch_f32_to_h16(gb32, grad_bias, g.outC, f16, stream), down);
   return DCN_OK;
+}
+
+DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const void* input,
+                              const void* weight, const void* offset, const void* mask,
+                              void* grad_input, void* grad_offset, void* grad_mask,
+                              void* grad_weight, void* grad_bias, uint32_t flags,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  return backward_h16(false, s, grad_output, input, weight, offset, mask, grad_input, grad_offset,
+                      grad_mask, grad_weight, grad_bias, flags, workspace, workspace_bytes,
+                      stream);
+}
+
+DCN_API size_t dcn_backward_f16_workspace_size(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_backward_f16_workspace_size") != DCN_OK) return 0;
+  return bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+}
+
+DCN_API int dcn_backward_f16(const dcn_shape* s, const void* grad_output, const void* input,
+                             const void* weight, const void* offset, const void* mask,
+                             void* grad_input, void* grad_offset, void* grad_mask,
+                             void* grad_weight, void* grad_bias, uint32_t flags, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return backward_h16(true, s, grad_output, input, weight, offset, mask, grad_input, grad_offset,
+                      grad_mask, grad_weight, grad_bias, flags, workspace, workspace_bytes,
+                      stream);
 }
 
 static int single_geom(dcn::Geom& g, int64_t C, int64_t H, int64_t W, int64_t kh, int64_t kw,

@@ -36,6 +36,7 @@
 // round their gathered operands to nearest, as the gradients have the tighter
 // tolerance.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
@@ -66,15 +67,19 @@ int tmem_cols_for(int bn) {
 //          K substep, twice the stage bytes so half the stages;
 //   BF16   bf16 tensors (NHWC copy, packed weight, offsets, mask, bias and
 //          output all bf16), kind::f16 UMMAs with bf16 operands; a K step is
-//          64 channels (still 128 B per row) and each gather lane blends 8.
-enum : int { kTF32 = 0, kSplit = 1, kBF16 = 2 };
+//          64 channels (still 128 B per row) and each gather lane blends 16;
+//   F16    the same with fp16 tensors and fp16 operands.
+enum : int { kTF32 = 0, kSplit = 1, kBF16 = 2, kF16 = 3 };
+// Storage formats of the small operands and of the output.
+enum : int { kFmtF32 = 0, kFmtBF16 = 1, kFmtF16 = 2 };
 template <int MODE>
 struct FwdCfg {
   static constexpr bool SPLIT = MODE == kSplit;
-  static constexpr bool BF16 = MODE == kBF16;
+  static constexpr bool H16 = MODE == kBF16 || MODE == kF16;  // 16-bit storage
+  static constexpr int FMT = MODE == kBF16 ? kFmtBF16 : (MODE == kF16 ? kFmtF16 : kFmtF32);
   static constexpr int STAGES = SPLIT ? 2 : 4;
   static constexpr int PARTS = SPLIT ? 2 : 1;
-  static constexpr int KCH = BF16 ? 64 : 32;  // channels of one tap per K step
+  static constexpr int KCH = H16 ? 64 : 32;  // channels of one tap per K step
 };
 size_t smem_bytes(int bn, bool split) {
   const int parts = split ? 2 : 1, stages = split ? 2 : 4;
@@ -96,11 +101,13 @@ __device__ __forceinline__ Tile tile_of(int t, int mtiles, int ntiles_n, int bn)
 }
 
 // Scalar loads of the small operands (offsets, mask, bias) as fp32.
-template <bool BF16>
+template <int FMT>
 __device__ __forceinline__ float ld_io(const void* p, long long i) {
-  if constexpr (BF16) {
+  if constexpr (FMT == kFmtBF16) {
     const unsigned short v = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
     return __uint_as_float((uint32_t)v << 16);
+  } else if constexpr (FMT == kFmtF16) {
+    return __half2float(__ldg(reinterpret_cast<const __half*>(p) + i));
   } else {
     return __ldg(reinterpret_cast<const float*>(p) + i);
   }
@@ -118,11 +125,31 @@ __device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t
                "r"(d)
                : "memory");
 }
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
+// The two 16-bit values of a 32-bit word (low half first) as fp32, and back.
+template <int FMT>
+__device__ __forceinline__ float h16_lo(uint32_t w) {
+  if constexpr (FMT == kFmtF16) return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+  else return __uint_as_float(w << 16);
+}
+template <int FMT>
+__device__ __forceinline__ float h16_hi(uint32_t w) {
+  if constexpr (FMT == kFmtF16) return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+  else return __uint_as_float(w & 0xffff0000u);
+}
+template <int FMT>
+__device__ __forceinline__ uint32_t pack_h16x2(float lo, float hi) {
+  if constexpr (FMT == kFmtF16) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+template <int FMT>
+__device__ __forceinline__ unsigned short to_h16(float y) {
+  if constexpr (FMT == kFmtF16) return __half_as_ushort(__float2half_rn(y));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(y));
 }
 
 // 704 threads: 22 warps, up to 6 on one SM sub-partition of 16K registers,
@@ -134,7 +161,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
               const void* __restrict__ off, const void* __restrict__ mask,
               const void* __restrict__ bias, void* __restrict__ out) {
   using Cfg = FwdCfg<MODE>;
-  constexpr bool SPLIT = Cfg::SPLIT, BF16 = Cfg::BF16;
+  constexpr bool SPLIT = Cfg::SPLIT, H16 = Cfg::H16;
+  constexpr int FMT = Cfg::FMT;
   constexpr int STAGES = Cfg::STAGES, PARTS = Cfg::PARTS, KCH = Cfg::KCH;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
@@ -183,7 +211,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     const int q4 = lane & 3, sub = lane >> 2;
     const int zoff = g.N * g.HW * g.C;  // element offset of the zero row
     const char* xq = static_cast<const char*>(xt_) + q4 * 32;
-    constexpr int ESZ = BF16 ? 2 : 4;  // element bytes
+    constexpr int ESZ = H16 ? 2 : 4;  // element bytes
     int gs = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const Tile T = tile_of(t, mtiles, ntiles_n, bn);
@@ -213,11 +241,11 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           }
           if (rvalid) {
             const long long oi = off_h_index(g, rn, dgi, k, rp);
-            const float h = (float)((roy + g.oy0) * g.sh - g.ph + ki * g.dh) + ld_io<BF16>(off, oi);
-            const float w = (float)(rox * g.sw - g.pw + kj * g.dw) + ld_io<BF16>(off, oi + g.P);
+            const float h = (float)((roy + g.oy0) * g.sh - g.ph + ki * g.dh) + ld_io<FMT>(off, oi);
+            const float w = (float)(rox * g.sw - g.pw + kj * g.dw) + ld_io<FMT>(off, oi + g.P);
             float m = 1.f;
             if (g.use_mask) {
-              const float raw = ld_io<BF16>(mask, mask_index(g, rn, dgi, k, rp));
+              const float raw = ld_io<FMT>(mask, mask_index(g, rn, dgi, k, rp));
               m = g.mask_logits ? 1.f / (1.f + expf(-raw)) : raw;
             }
             const Sample sp = make_sample(h, w, g.H, g.W);
@@ -239,15 +267,15 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           ldg_v8(xq + (size_t)(unsigned)(coff[c] + gch0) * ESZ, v[c]);
         if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
         const float a = cw[0], b = cw[1], c = cw[2], d = cw[3];
-        if constexpr (BF16) {
+        if constexpr (H16) {
           uint32_t r[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float lo = a * bf_lo(v[0][j]) + b * bf_lo(v[1][j]) + c * bf_lo(v[2][j]) +
-                             d * bf_lo(v[3][j]);
-            const float hi = a * bf_hi(v[0][j]) + b * bf_hi(v[1][j]) + c * bf_hi(v[2][j]) +
-                             d * bf_hi(v[3][j]);
-            r[j] = pack_bf16x2(lo, hi);
+            const float lo = a * h16_lo<FMT>(v[0][j]) + b * h16_lo<FMT>(v[1][j]) +
+                             c * h16_lo<FMT>(v[2][j]) + d * h16_lo<FMT>(v[3][j]);
+            const float hi = a * h16_hi<FMT>(v[0][j]) + b * h16_hi<FMT>(v[1][j]) +
+                             c * h16_hi<FMT>(v[2][j]) + d * h16_hi<FMT>(v[3][j]);
+            r[j] = pack_h16x2<FMT>(lo, hi);
           }
           st_shared_u4(sA + soff0, r[0], r[1], r[2], r[3]);
           st_shared_u4(sA + soff1, r[4], r[5], r[6], r[7]);
@@ -321,7 +349,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   } else if (warp == MMA_WARP) {
     // ------------------------------ MMA ------------------------------
     if (lane == 0) {
-      const uint32_t idesc = BF16 ? tc::idesc_bf16(BM, bn) : tc::idesc_tf32(BM, bn);
+      const uint32_t idesc = FMT == kFmtF16    ? tc::idesc_f16(BM, bn)
+                             : FMT == kFmtBF16 ? tc::idesc_bf16(BM, bn)
+                                               : tc::idesc_tf32(BM, bn);
       int gs = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
         const int acc = it & 1;
@@ -335,7 +365,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {  // 32 bytes of K per UMMA: 8 tf32 or 16 bf16
-            if constexpr (BF16) {
+            if constexpr (H16) {
               tc::umma_bf16(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
                             (s | j) != 0 ? 1u : 0u);
             } else if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
@@ -379,11 +409,10 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         if (valid) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float y = vv[j] + (g.use_bias ? ld_io<BF16>(bias, bbase + cb + j) : 0.f);
+            const float y = vv[j] + (g.use_bias ? ld_io<FMT>(bias, bbase + cb + j) : 0.f);
             const long long at = obase + (long long)(cb + j) * g.P;
-            if constexpr (BF16)
-              static_cast<unsigned short*>(out)[at] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(y));
+            if constexpr (H16)
+              static_cast<unsigned short*>(out)[at] = to_h16<FMT>(y);
             else
               static_cast<float*>(out)[at] = y;
           }
@@ -424,8 +453,8 @@ __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __rest
   }
 }
 
-// bf16 packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = W[g*Og+o][c][k]
-// (both bf16, no rounding).
+// 16-bit packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = W[g*Og+o][c][k]
+// (bf16 or fp16 words moved as they are, no rounding).
 __global__ void __launch_bounds__(256) tc_pack_weight_bf16_kernel(
     const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g) {
   const int Kpad = g.kk * g.Cg;
@@ -444,7 +473,9 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
   const int bn = tc_bn(g);
   const size_t smem = smem_bytes(bn, mode == kSplit);
   auto kern = mode == kSplit ? fwd_tc_kernel<kSplit>
-                             : (mode == kBF16 ? fwd_tc_kernel<kBF16> : fwd_tc_kernel<kTF32>);
+               : mode == kBF16 ? fwd_tc_kernel<kBF16>
+               : mode == kF16  ? fwd_tc_kernel<kF16>
+                               : fwd_tc_kernel<kTF32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
@@ -508,15 +539,15 @@ cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
 }
 
 cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
-                               const void* mask, const void* bias, void* out, int num_sms,
-                               cudaStream_t stream) {
+                               const void* mask, const void* bias, void* out, bool f16,
+                               int num_sms, cudaStream_t stream) {
   if (!tc_fwd_bf16_supported(g)) return cudaErrorInvalidValue;
   const int Kpad = g.kk * g.Cg;
   CUtensorMap wmap;
   cudaError_t e = make_tmap_2d_bf16(&wmap, wt, (uint64_t)Kpad, (uint64_t)g.outC,
-                                    (uint64_t)Kpad, (uint32_t)tc_bn(g));
+                                    (uint64_t)Kpad, (uint32_t)tc_bn(g), f16);
   if (e != cudaSuccess) return e;
-  return launch_fwd_mode(kBF16, g, xt, wmap, off, mask, bias, out, num_sms, stream);
+  return launch_fwd_mode(f16 ? kF16 : kBF16, g, xt, wmap, off, mask, bias, out, num_sms, stream);
 }
 
 }  // namespace dcn

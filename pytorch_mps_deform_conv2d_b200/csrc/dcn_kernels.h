@@ -15,12 +15,15 @@ namespace dcn {
 // `zero_like` (NULL or an (N, H, W, C) buffer) is zeroed in the same pass.
 cudaError_t launch_nchw_to_nhwc(const float* x, float* xt, int N, int C, int HW,
                                 bool zero_row, float* zero_like, cudaStream_t stream);
-// bf16 x (N, C, H, W) -> bf16 xt (N, H, W, C) (+ zero row when `zero_row`).
+// 16-bit x (N, C, H, W) -> xt (N, H, W, C) (+ zero row when `zero_row`).
 cudaError_t launch_nchw_to_nhwc_bf16(const void* x, void* xt, int N, int C, int HW, bool zero_row,
                                      cudaStream_t stream);
-// Element-wise bf16 <-> fp32 copies (round to nearest even on the way down).
-cudaError_t launch_bf16_to_f32(const void* in, float* out, long long n, cudaStream_t stream);
-cudaError_t launch_f32_to_bf16(const float* in, void* out, long long n, cudaStream_t stream);
+// Element-wise 16-bit (bf16, or fp16 with `f16`) <-> fp32 copies (round to
+// nearest even on the way down).
+cudaError_t launch_h16_to_f32(const void* in, float* out, long long n, bool f16,
+                              cudaStream_t stream);
+cudaError_t launch_f32_to_h16(const float* in, void* out, long long n, bool f16,
+                              cudaStream_t stream);
 // Channels-last x (N, H, W, C) copied to xt (+ zero row, + zeroed
 // `zero_like` of the same size when not NULL).
 cudaError_t launch_copy_nhwc(const float* x, float* xt, int N, int C, int HW, bool zero_row,

@@ -3,6 +3,7 @@
 // channel-contiguous copy so one sample's channel vector is one run of
 // 16-byte loads / vector reductions), weight repacking and the bias gradient.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "dcn_kernels.h"
 
@@ -243,18 +244,21 @@ __global__ void __launch_bounds__(256) transpose16_kernel(const unsigned short* 
   }
 }
 
-__global__ void bf16_to_f32_kernel(const unsigned short* __restrict__ in, float* __restrict__ out,
-                                   long long n) {
+// 16-bit (bf16, or fp16 with `f16`) <-> fp32, element-wise; fp32 -> 16-bit
+// rounds to nearest even.
+__global__ void h16_to_f32_kernel(const unsigned short* __restrict__ in, float* __restrict__ out,
+                                  long long n, int f16) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
-    out[i] = __uint_as_float((uint32_t)in[i] << 16);
+    out[i] = f16 ? __half2float(__ushort_as_half(in[i])) : __uint_as_float((uint32_t)in[i] << 16);
 }
 
-__global__ void f32_to_bf16_kernel(const float* __restrict__ in, unsigned short* __restrict__ out,
-                                   long long n) {
+__global__ void f32_to_h16_kernel(const float* __restrict__ in, unsigned short* __restrict__ out,
+                                  long long n, int f16) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
-    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(in[i]));
+    out[i] = f16 ? __half_as_ushort(__float2half_rn(in[i]))
+                 : __bfloat16_as_ushort(__float2bfloat16_rn(in[i]));
 }
 }  // namespace
 
@@ -273,16 +277,19 @@ cudaError_t launch_nchw_to_nhwc_bf16(const void* x, void* xt, int N, int C, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_bf16_to_f32(const void* in, float* out, long long n, cudaStream_t stream) {
+cudaError_t launch_h16_to_f32(const void* in, float* out, long long n, bool f16,
+                              cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
-  bf16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(static_cast<const unsigned short*>(in), out,
-                                                      n);
+  h16_to_f32_kernel<<<grid_for(n), 256, 0, stream>>>(static_cast<const unsigned short*>(in), out,
+                                                     n, f16 ? 1 : 0);
   return cudaGetLastError();
 }
 
-cudaError_t launch_f32_to_bf16(const float* in, void* out, long long n, cudaStream_t stream) {
+cudaError_t launch_f32_to_h16(const float* in, void* out, long long n, bool f16,
+                              cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
-  f32_to_bf16_kernel<<<grid_for(n), 256, 0, stream>>>(in, static_cast<unsigned short*>(out), n);
+  f32_to_h16_kernel<<<grid_for(n), 256, 0, stream>>>(in, static_cast<unsigned short*>(out), n,
+                                                     f16 ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -23,17 +23,18 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
                           const float* off, const float* mask, const float* bias,
                           float* out, bool split, int num_sms, cudaStream_t stream);
 
-// bf16 forward (all tensors bf16, kind::f16 UMMAs, fp32 accumulation): 64
-// channels of a tap per K step, so channels per group and per deformable
-// group must be multiples of 64.  `xt` is the bf16 NHWC copy with its zero
-// row, `wt` the packed bf16 weight (tc_fwd_weight_bf16_bytes).
+// 16-bit forward (all tensors bf16, or all fp16 with `f16`; kind::f16 UMMAs,
+// fp32 accumulation): 64 channels of a tap per K step, so channels per group
+// and per deformable group must be multiples of 64.  `xt` is the 16-bit NHWC
+// copy with its zero row, `wt` the packed 16-bit weight
+// (tc_fwd_weight_bf16_bytes).
 bool tc_fwd_bf16_supported(const Geom& g);
 size_t tc_fwd_weight_bf16_bytes(const Geom& g);
 cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
                                        cudaStream_t stream);
 cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
-                               const void* mask, const void* bias, void* out, int num_sms,
-                               cudaStream_t stream);
+                               const void* mask, const void* bias, void* out, bool f16,
+                               int num_sms, cudaStream_t stream);
 
 // Whether the tensor-core backward covers this geometry (grad-column kernel
 // and the column-buffer weight gradient), and whether the gather-based

@@ -41,7 +41,7 @@ cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner
 }
 
 cudaError_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
-                              uint64_t pitch_elems, uint32_t box_rows) {
+                              uint64_t pitch_elems, uint32_t box_rows, bool f16) {
   std::call_once(g_encode_once, resolve_encode);
   if (g_encode_status != cudaSuccess) return g_encode_status;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (pitch_elems * 2) % 16 != 0 ||
@@ -51,7 +51,9 @@ cudaError_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner
   const cuuint64_t strides[1] = {pitch_elems * 2};
   const cuuint32_t box[2] = {64, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+  const CUresult r = g_encode(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                              2, const_cast<void*>(base),
                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

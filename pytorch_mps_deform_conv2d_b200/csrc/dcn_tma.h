@@ -17,8 +17,9 @@ namespace dcn {
 // the layout of an MN-major TF32 tensor-core operand.
 cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner, uint64_t rows,
                              uint64_t pitch_elems, uint32_t box_rows, bool atom32 = false);
-// The same for bf16 elements: boxes of 64 elements (128 B) x `box_rows` rows.
+// The same for 16-bit elements (bf16, or fp16 with `f16`): boxes of 64
+// elements (128 B) x `box_rows` rows.
 cudaError_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
-                              uint64_t pitch_elems, uint32_t box_rows);
+                              uint64_t pitch_elems, uint32_t box_rows, bool f16 = false);
 
 }  // namespace dcn

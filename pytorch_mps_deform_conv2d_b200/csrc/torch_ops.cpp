@@ -90,9 +90,10 @@ void check_shapes(const at::Tensor& x, const at::Tensor& w, const at::Tensor& of
               "offset shape mismatch: expected (", N, ", ", 2 * dg * kh * kw, ", ", out_h, ", ",
               out_w, "), got ", off.sizes());
   if (use_mask) {
-    if (x.scalar_type() == at::kBFloat16) {
-      TORCH_CHECK(msk.device().is_cuda() && msk.scalar_type() == at::kBFloat16,
-                  "mask must be a bfloat16 CUDA tensor");
+    if (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf) {
+      TORCH_CHECK(msk.device().is_cuda() && msk.scalar_type() == x.scalar_type(),
+                  "mask must be a ", x.scalar_type() == at::kHalf ? "float16" : "bfloat16",
+                  " CUDA tensor");
     } else {
       check_cuda_f32(msk, "mask must be a float32 CUDA tensor");
     }
@@ -121,11 +122,14 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
               "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
   // float32 (the reference's only dtype, .mm:206-209) or, as an addition,
   // bfloat16 for every tensor
-  const bool bf16 = input.scalar_type() == at::kBFloat16;
-  if (bf16) {
-    TORCH_CHECK(weight.scalar_type() == at::kBFloat16 && offset.scalar_type() == at::kBFloat16,
-                "deform_conv2d_forward: input, weight and offset must all be float32 or all "
-                "bfloat16");
+  // (as another addition) float16 for every tensor
+  const auto dt = input.scalar_type();
+  const bool h16 = dt == at::kBFloat16 || dt == at::kHalf;  // 16-bit tensors
+  const bool f16 = dt == at::kHalf;
+  if (h16) {
+    TORCH_CHECK(weight.scalar_type() == dt && offset.scalar_type() == dt,
+                "deform_conv2d_forward: input, weight and offset must all be float32, all "
+                "bfloat16 or all float16");
   } else {
     TORCH_CHECK(input.scalar_type() == at::kFloat && weight.scalar_type() == at::kFloat &&
                     offset.scalar_type() == at::kFloat,
@@ -135,12 +139,12 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   int64_t out_h = 0, out_w = 0;
   check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
                dilation_h, dilation_w, groups, deformable_groups, out_h, out_w, row_begin);
-  TORCH_CHECK(row_begin < 0 || !bf16, "deform_conv2d_forward_rows: float32 tensors only");
+  TORCH_CHECK(row_begin < 0 || !h16, "deform_conv2d_forward_rows: float32 tensors only");
   at::Tensor b;
   if (bias.has_value() && bias->defined() && bias->numel() > 0) {
-    if (bf16) {
-      TORCH_CHECK(bias->device().is_cuda() && bias->scalar_type() == at::kBFloat16,
-                  "bias must be a bfloat16 CUDA tensor");
+    if (h16) {
+      TORCH_CHECK(bias->device().is_cuda() && bias->scalar_type() == dt, "bias must be a ",
+                  f16 ? "float16" : "bfloat16", " CUDA tensor");
     } else {
       check_cuda_f32(*bias, "bias must be a float32 CUDA tensor");
     }
@@ -160,13 +164,14 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                                  groups, deformable_groups);
   const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (bf16) {
-    const size_t ws16 = dcn_forward_bf16_workspace_size(&s, flags);
+  if (h16) {
+    const size_t ws16 = f16 ? dcn_forward_f16_workspace_size(&s, flags)
+                            : dcn_forward_bf16_workspace_size(&s, flags);
     auto ws = at::empty({(int64_t)std::max<size_t>(ws16, 1)}, x.options().dtype(at::kByte));
-    check_rc(dcn_forward_bf16(&s, x.data_ptr(), w.data_ptr(), off.data_ptr(),
-                              use_mask ? msk.data_ptr() : nullptr,
-                              b.defined() ? b.data_ptr() : nullptr, out.data_ptr(), flags,
-                              ws.data_ptr(), ws16, stream.stream()));
+    auto fwd16 = f16 ? dcn_forward_f16 : dcn_forward_bf16;
+    check_rc(fwd16(&s, x.data_ptr(), w.data_ptr(), off.data_ptr(),
+                   use_mask ? msk.data_ptr() : nullptr, b.defined() ? b.data_ptr() : nullptr,
+                   out.data_ptr(), flags, ws.data_ptr(), ws16, stream.stream()));
     return out;
   }
   const float* mp = use_mask ? msk.data_ptr<float>() : nullptr;
@@ -219,13 +224,14 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
                   weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
-  if (input.scalar_type() == at::kBFloat16) {
-    // bfloat16 tensors: the gradients are computed by the float32 backward
-    // from upcast copies and returned in bfloat16
-    TORCH_CHECK(grad_output.scalar_type() == at::kBFloat16 &&
-                    weight.scalar_type() == at::kBFloat16 && offset.scalar_type() == at::kBFloat16,
+  const auto dt = input.scalar_type();
+  if (dt == at::kBFloat16 || dt == at::kHalf) {
+    // 16-bit tensors: the gradients are computed by the float32 backward
+    // from upcast copies and returned in the input's dtype
+    TORCH_CHECK(grad_output.scalar_type() == dt && weight.scalar_type() == dt &&
+                    offset.scalar_type() == dt,
                 "deform_conv2d_backward: grad_output, input, weight and offset must all be "
-                "float32 or all bfloat16");
+                "float32, all bfloat16 or all float16");
     auto up = [](const at::Tensor& t) { return t.defined() ? t.to(at::kFloat) : t; };
     c10::optional<at::Tensor> b32;
     if (bias.has_value() && bias->defined()) b32 = bias->to(at::kFloat);
@@ -233,7 +239,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
     auto r = backward_impl(up(grad_output), up(input), up(weight), up(offset), up(mask), b32,
                            stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w, groups,
                            deformable_groups, -1, math);
-    auto down = [](const at::Tensor& t) { return t.to(at::kBFloat16); };
+    auto down = [dt](const at::Tensor& t) { return t.to(dt); };
     return std::make_tuple(down(std::get<0>(r)), down(std::get<1>(r)), down(std::get<2>(r)),
                            down(std::get<3>(r)), down(std::get<4>(r)));
   }

@@ -95,15 +95,15 @@ def test_channels_last_row_window(cuda_device):
         _same(g_cl[k], g[k], f"grad_{k}")
 
 
-@pytest.mark.parametrize("inC", [64, 24])  # bf16 tensor-core forward / upcast forward
-def test_channels_last_bf16(cuda_device, inC):
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("inC", [64, 24])  # 16-bit tensor-core forward / upcast forward
+def test_channels_last_half(cuda_device, inC, dt):
     case = make_case(inC=inC, outC=64, H=9, W=10, offset_scale=2.0, upstream="randn")
-    bf = {k: (v.to(torch.bfloat16) if isinstance(v, torch.Tensor) else v)
-          for k, v in case.items()}
+    bf = {k: (v.to(dt) if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
     out_cl, g_cl = _run(bf, MATH_TF32, CL)
     out, g = _run(bf, MATH_TF32, torch.contiguous_format)
-    assert out_cl.dtype == torch.bfloat16
-    assert g_cl["x"].dtype == torch.bfloat16 and g_cl["x"].is_contiguous(memory_format=CL)
+    assert out_cl.dtype == dt
+    assert g_cl["x"].dtype == dt and g_cl["x"].is_contiguous(memory_format=CL)
     torch.testing.assert_close(out_cl.float(), out.float(), rtol=0, atol=0)
     for k in g:
         s = max(1.0, float(g[k].float().abs().max()))

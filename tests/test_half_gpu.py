@@ -1,10 +1,11 @@
-"""bf16 I/O: every tensor bf16.  Forward on tcgen05 with bf16 operands when
-channels per group and per deformable group are multiples of 64, else the
-fp32 kernels on upcast copies; backward through the fp32 kernels on upcast
-copies, gradients returned in bf16.  Parity against the oracle run on the
-same bf16-rounded inputs: norm-wise relative error <= 1e-2 for outputs and
-gradients (bf16 keeps 8 mantissa bits: one rounding of the column values and
-one of the result are ~2e-3 each)."""
+"""16-bit I/O: every tensor bf16, or every tensor fp16.  Forward on tcgen05
+with 16-bit operands of the same type when channels per group and per
+deformable group are multiples of 64, else the fp32 kernels on upcast copies;
+backward through the fp32 kernels on upcast copies, gradients returned in the
+input's dtype.  Parity against the oracle run on the same rounded inputs:
+norm-wise relative error <= 1e-2 for outputs and gradients (bf16 keeps 8
+mantissa bits, fp16 11: one rounding of the column values and one of the
+result are ~2e-3 each in bf16)."""
 import numpy as np
 import pytest
 import torch
@@ -31,9 +32,12 @@ CASES = {  # name -> (case, bf16 tensor-core forward expected)
 }
 
 
-def _bf16_case(spec):
+DTYPES = {"bf16": (torch.bfloat16, "bf16"), "fp16": (torch.float16, "f16")}
+
+
+def _bf16_case(spec, dt=torch.bfloat16):
     case = make_case(upstream="randn", **spec)
-    r = lambda t: None if t is None else t.to(torch.bfloat16)
+    r = lambda t: None if t is None else t.to(dt)
     c16 = {k: r(case[k]) for k in ("x", "w", "b", "off", "m", "go")}
     # the oracle sees exactly the bf16 values, upcast
     c32 = dict(case, **{k: (None if v is None else v.float()) for k, v in c16.items()})
@@ -53,10 +57,12 @@ def _run(case, c16, backward):
     return out, grads
 
 
+@pytest.mark.parametrize("dtype", sorted(DTYPES))
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_bf16_forward(cuda_device, name):
+def test_half_forward(cuda_device, name, dtype):
+    dt, tag = DTYPES[dtype]
     spec, tc = CASES[name]
-    case, c16, c32 = _bf16_case(spec)
+    case, c16, c32 = _bf16_case(spec, dt)
     _native.profiler_read()
     _native.profiler_enable(True)
     try:
@@ -64,20 +70,22 @@ def test_bf16_forward(cuda_device, name):
     finally:
         _native.profiler_enable(False)
     stats = _native.profiler_read()
-    assert out.dtype == torch.bfloat16
-    assert ("fwd_tc_bf16" in stats) == tc, sorted(stats)
+    assert out.dtype == dt
+    assert (f"fwd_tc_{tag}" in stats) == tc, sorted(stats)
     if not tc:
-        assert "bf16_to_f32" in stats and "f32_to_bf16" in stats, sorted(stats)
+        assert f"{tag}_to_f32" in stats and f"f32_to_{tag}" in stats, sorted(stats)
     ref, _ = run_oracle(c32, backward=False)
     got = out.float().cpu().numpy()
     assert rel_norm_err(got, ref) <= TOL
     np.testing.assert_allclose(got, ref, rtol=0, atol=2 * TOL * float(np.abs(ref).max()))
 
 
+@pytest.mark.parametrize("dtype", sorted(DTYPES))
 @pytest.mark.parametrize("name", ["c64-o64", "c128-o64-g2-v1-nobias", "c6-o6-g3-upcast"])
-def test_bf16_backward(cuda_device, name):
+def test_half_backward(cuda_device, name, dtype):
+    dt, _ = DTYPES[dtype]
     spec, _ = CASES[name]
-    case, c16, c32 = _bf16_case(spec)
+    case, c16, c32 = _bf16_case(spec, dt)
     dcn.set_math_mode("fp32")
     try:
         out, grads = _run(case, c16, backward=True)
@@ -87,33 +95,38 @@ def test_bf16_backward(cuda_device, name):
     assert rel_norm_err(out.detach().float().cpu().numpy(), ref) <= TOL
     assert set(grads) == set(rgrads)
     for k, want in rgrads.items():
-        assert grads[k].dtype == torch.bfloat16, k
+        assert grads[k].dtype == dt, k
         err = rel_norm_err(grads[k].float().cpu().numpy(), want)
         assert err <= TOL, f"grad_{k}: {err:.2e}"
 
 
-def test_bf16_pack_module(cuda_device):
+@pytest.mark.parametrize("dtype", sorted(DTYPES))
+def test_half_pack_module(cuda_device, dtype):
+    dt, _ = DTYPES[dtype]
     torch.manual_seed(0)
     mod = dcn.DeformConv2dPack(64, 64, 3, padding=1).cuda()
     with torch.no_grad():
         mod.conv_offset.weight.normal_(0, 0.02)
     x = torch.randn(2, 64, 10, 12, device="cuda")
     ref = mod(x)
-    mod16 = mod.to(torch.bfloat16)
-    x16 = x.to(torch.bfloat16).requires_grad_()
+    mod16 = mod.to(dt)
+    x16 = x.to(dt).requires_grad_()
     out = mod16(x16)
-    assert out.dtype == torch.bfloat16
+    assert out.dtype == dt
     assert rel_norm_err(out.float().detach().cpu().numpy(), ref.detach().cpu().numpy()) <= 3 * TOL
     out.float().square().sum().backward()
-    assert x16.grad.dtype == torch.bfloat16 and torch.isfinite(x16.grad.float()).all()
-    assert mod16.weight.grad.dtype == torch.bfloat16
+    assert x16.grad.dtype == dt and torch.isfinite(x16.grad.float()).all()
+    assert mod16.weight.grad.dtype == dt
 
 
-def test_capi_bf16_backward_matches_operator(cuda_device):
-    """dcn_backward_bf16 through ctypes gives the operator's bf16 gradients."""
+@pytest.mark.parametrize("dtype", sorted(DTYPES))
+def test_capi_half_backward_matches_operator(cuda_device, dtype):
+    """dcn_backward_bf16 / dcn_backward_f16 through ctypes give the operator's
+    16-bit gradients."""
     from pytorch_mps_deform_conv2d_b200.ops import MATH_FP32
+    dt, tag = DTYPES[dtype]
     spec, _ = CASES["c64-o64"]
-    case, c16, _ = _bf16_case(spec)
+    case, c16, _ = _bf16_case(spec, dt)
     ops = _native.load_ops()
     d = {k: (None if v is None else v.cuda().contiguous()) for k, v in c16.items()}
     want = ops.deform_conv2d_backward(d["go"], d["x"], d["w"], d["off"], d["m"], d["b"],
@@ -121,16 +134,16 @@ def test_capi_bf16_backward_matches_operator(cuda_device):
     lib = _native.load_capi()
     N, C, H, W = d["x"].shape
     s = _native.DcnShape(N, C, H, W, d["w"].shape[0], 3, 3, 1, 1, 1, 1, 1, 1, 1, 1)
-    nbytes = lib.dcn_backward_bf16_workspace_size(s, MATH_FP32)
+    nbytes = getattr(lib, f"dcn_backward_{tag}_workspace_size")(s, MATH_FP32)
     assert nbytes > 0
     ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     outs = [torch.empty_like(t) for t in (d["x"], d["off"], d["m"], d["w"], d["b"])]
     ptr = lambda t: t.data_ptr()
-    rc = lib.dcn_backward_bf16(s, ptr(d["go"]), ptr(d["x"]), ptr(d["w"]), ptr(d["off"]),
+    rc = getattr(lib, f"dcn_backward_{tag}")(s, ptr(d["go"]), ptr(d["x"]), ptr(d["w"]), ptr(d["off"]),
                                ptr(d["m"]), *[ptr(t) for t in outs], MATH_FP32, ptr(ws), nbytes,
                                torch.cuda.current_stream().cuda_stream)
     assert rc == 0, lib.dcn_last_error()
     torch.cuda.synchronize()
     for got, ref in zip(outs, want):
-        assert got.dtype == torch.bfloat16
+        assert got.dtype == dt
         torch.testing.assert_close(got.float(), ref.float(), rtol=1e-2, atol=1e-2)
