@@ -19,6 +19,7 @@
 //                is gathered (bilinear sampling, as in the forward) straight
 //                into an MN-major operand (32-byte-atom swizzle); go_r rows arrive by
 //                cp.async.  Partial tiles are reduced into grad_weight.
+#include "dcn_launch.h"
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
 #include "dcn_tma.h"
@@ -1228,11 +1229,9 @@ cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, con
   const size_t smem = data_smem_bytes(split);
   auto kern = split ? bwd_data_tc_kernel<true> : bwd_data_tc_kernel<false>;
   const int threads = split ? DCfg<true>::THREADS : DCfg<false>::THREADS;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
   const int bpi = (g.P + 31) / 32;  // 32-pixel blocks per image
   if ((long long)g.N * bpi > (1LL << 30)) return cudaErrorInvalidValue;
   const int nblocks = g.N * bpi;
@@ -1282,7 +1281,7 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   if (e != cudaSuccess) return e;
   const size_t smem = weight_smem_bytes(bn, split);
   auto kern = split ? bwd_weight_tc_kernel<true> : bwd_weight_tc_kernel<false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem);
   if (e != cudaSuccess) return e;
   // a gathered K step costs far more than the tile's fixed work
   const WSplit w = weight_split(g, bn, num_sms, 0);
@@ -1317,7 +1316,7 @@ cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* 
   if (e != cudaSuccess) return e;
   const size_t smem = weight_smem_bytes(bn, split);
   auto kern = split ? bwd_weight_col_kernel<true> : bwd_weight_col_kernel<false>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem);
   if (e != cudaSuccess) return e;
   const WSplit w = weight_split(g, bn, num_sms, 16);
   if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;

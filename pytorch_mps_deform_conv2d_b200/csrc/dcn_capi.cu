@@ -12,6 +12,7 @@
 #include <string>
 #include <vector>
 
+#include "dcn_launch.h"
 #include "dcn_b200.h"
 #include "dcn_kernels.h"
 #include "dcn_tc.h"
@@ -173,12 +174,7 @@ bool is_device_ptr(const void* p) {
   return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
 }
 
-int num_sms_current() {
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms > 0 ? sms : 148;
-}
+int num_sms_current() { return dcn::device_sm_count(); }
 
 constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }

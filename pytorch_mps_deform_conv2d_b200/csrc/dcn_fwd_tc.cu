@@ -38,6 +38,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "dcn_launch.h"
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
 #include "dcn_tma.h"
@@ -476,8 +477,7 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
                : mode == kBF16 ? fwd_tc_kernel<kBF16>
                : mode == kF16  ? fwd_tc_kernel<kF16>
                                : fwd_tc_kernel<kTF32>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem);
   if (e != cudaSuccess) return e;
   const int mtiles = (int)((g.NP + BM - 1) / BM);
   const int ntiles_n = g.Og / bn;
