@@ -1179,9 +1179,10 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
 }  // namespace
 
 bool tc_bwd_supported(const Geom& g) {
-  // channels per group: a multiple of 128, or 32 / 64 (slots of several taps)
+  // channels per group: any multiple of 32 (a 128-row slot of the group's
+  // (tap, channel) rows is four 32-channel chunks, each inside one tap)
   return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
-         (g.Og <= 256 || g.Og % 256 == 0) && (g.Cg % W_BM == 0 || W_BM % g.Cg == 0) &&
+         (g.Og <= 256 || g.Og % 256 == 0) &&
          g.NP > 0 && (long long)g.N * g.HW * g.C + g.C < (1LL << 31) &&
          (long long)g.N * 2 * g.dg * g.kk * g.P < (1LL << 31);
 }

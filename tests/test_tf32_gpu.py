@@ -89,6 +89,13 @@ TC_BWD_CASES = {
     "c64-o64-g2-dg2-cg32": dict(inC=64, outC=64, groups=2, dg=2, H=10, W=9, offset_scale=3.0),
     "c32-o32-k1x3-v1": dict(inC=32, outC=32, kh=1, kw=3, H=8, W=13, pad=(0, 1),
                             use_mask=False, use_bias=False, offset_scale=2.0),
+    # channels per group a multiple of 32 but neither of nor a divisor of 128:
+    # slots straddle taps
+    "c96-o64-cg96": dict(inC=96, outC=64, H=9, W=11, offset_scale=2.0),
+    "c192-o128-g2-dg3-cg96": dict(inC=192, outC=128, groups=2, dg=3, H=8, W=10,
+                                 offset_scale=2.0),
+    "c160-o32-cg160-v1": dict(inC=160, outC=32, H=9, W=9, use_mask=False, use_bias=False,
+                              offset_scale=3.0),
 }
 
 
@@ -135,10 +142,9 @@ def test_backward_tf32(cuda_device, name, path):
 
 
 def test_backward_tf32_uncovered_shape_uses_fp32_kernels(cuda_device):
-    # 96 input channels per group: neither a multiple of 128 nor a divisor of
-    # the 128-row slot, so the fp32 backward kernels run and meet the fp32
-    # tolerances.
-    case = make_case(inC=96, outC=64, H=9, W=9, upstream="randn")
+    # 48 input channels per group: not a multiple of 32, so the fp32 backward
+    # kernels run and meet the fp32 tolerances.
+    case = make_case(inC=48, outC=64, H=9, W=9, upstream="randn")
     stats, out_err, errs, elem = _grad_errors(case)
     assert "bwd_data_tc" not in stats and "bwd_data_simt" in stats
     for k, e in errs.items():
