@@ -396,14 +396,13 @@ __device__ __forceinline__ void epilogue_chunk(const Geom& g, int k, const float
   }
 }
 
-// Persistent, warp-specialised grad-column kernel.  Tile = 128 pixels x 128
-// channels of one group; per tap a K = Og GEMM into one of two tensor-memory
-// accumulators (taps alternate), consumed by 16 epilogue warps while the next
-// tap accumulates.
-//   warp 0      TMA producer per K step: go_r rows of the tile's image (32
-//               out channels x 128 pixels, an MN-major operand in four
-//               32-pixel boxes) and packed weight rows (128 channels x 32 out
-//               channels)
+// Persistent, warp-specialised grad-column kernel.  Tile = four 32-pixel
+// blocks (128 pixels) x one 128-row slot of a group's (tap, channel) rows;
+// per slot a K = Og GEMM into one of two tensor-memory accumulators (slots
+// alternate), consumed by 16 epilogue warps while the next slot accumulates.
+//   warp 0      TMA producer per K step: for each pixel block, 32 out channels
+//               x 32 pixels of its image's go_r rows (an MN-major operand),
+//               and packed weight rows (128 channels x 32 out channels)
 //   warp 1      MMA issue: 4 UMMAs 128 x 128 x 8 per K step
 //   warps 2-17  epilogue (epilogue_chunk)
 template <bool SPLIT>
@@ -431,7 +430,9 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ochunks = g.Og >> 5;
+  // 32-out-channel K steps; a partial last one reads zero weights past Og
+  // (the weight map ends there), so the grad_out rows it also loads add nothing
+  const int ochunks = (g.Og + 31) >> 5;
 
   if (tid == 0) {
     for (int s = 0; s < D_STAGES; ++s) {
@@ -1181,7 +1182,7 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
 bool tc_bwd_supported(const Geom& g) {
   // channels per group: any multiple of 32 (a 128-row slot of the group's
   // (tap, channel) rows is four 32-channel chunks, each inside one tap)
-  return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 32 == 0 &&
+  return g.Cg % 32 == 0 && g.cpg % 32 == 0 && g.C % 4 == 0 && g.Og % 16 == 0 &&
          (g.Og <= 256 || g.Og % 256 == 0) &&
          g.NP > 0 && (long long)g.N * g.HW * g.C + g.C < (1LL << 31) &&
          (long long)g.N * 2 * g.dg * g.kk * g.P < (1LL << 31);

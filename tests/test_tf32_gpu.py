@@ -96,6 +96,10 @@ TC_BWD_CASES = {
                                  offset_scale=2.0),
     "c160-o32-cg160-v1": dict(inC=160, outC=32, H=9, W=9, use_mask=False, use_bias=False,
                               offset_scale=3.0),
+    # out channels per group a multiple of 16 but not of 32: a partial last K step
+    "c64-o48-og48": dict(inC=64, outC=48, H=9, W=10, offset_scale=2.0),
+    "c128-o96-g2-og48-cg64": dict(inC=128, outC=96, groups=2, H=8, W=9, offset_scale=2.0),
+    "c128-o16-og16": dict(inC=128, outC=16, H=10, W=9, offset_scale=2.0),
 }
 
 
