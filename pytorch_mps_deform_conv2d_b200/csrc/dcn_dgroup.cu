@@ -4,18 +4,20 @@
 // each -- e.g. groups=32 with 2 channels each and 4 deformable groups: a
 // deformable group is 16 channels = 8 convolution groups.
 //
-// One thread per (output pixel, deformable group).  Per tap it computes the
-// sampling plan once (deform_conv2d.metal:100-118) and reads the four corner
-// runs of the deformable group's channels with 16-byte loads from the NHWC
-// input (dropped corners read the zero pixel row after it), so every sector
-// fetched is used, instead of each convolution group re-reading the sector
-// for its few channels.
+// L lanes per (output pixel, deformable group), each with CPG / L channels
+// (whole convolution groups, 4 or 8 channels): per tap a lane computes the
+// sampling plan (deform_conv2d.metal:100-118) and reads its part of the four
+// corner runs of the deformable group's channels with one 16- or 32-byte load
+// each from the NHWC input (dropped corners read the zero pixel row after
+// it).  The L lanes of a pixel read adjacent runs, so a warp instruction
+// covers 32 / L corner runs whole, and every sector fetched is used instead
+// of each convolution group re-reading the sector for its few channels.
 //  * forward: the OPD = GPD*OG outputs of the pixel, weights in shared memory;
 //  * backward: grad columns (K = OG dot products), col2im as 16-byte vector
 //    reductions into the NHWC grad-input accumulator, the coordinate and mask
-//    gradients of the pixel (its thread owns them: plain stores), and its
-//    grad_weight products reduced over the warp with a transpose-reduce (31
-//    shuffles for 32 values) and over the block in shared memory.
+//    gradients of the pixel (summed over its L lanes, stored by the first:
+//    plain stores), and its grad_weight products reduced over the warp's
+//    pixels with a transpose-reduce and over the block in shared memory.
 #include "dcn_kernels.h"
 
 namespace dcn {
@@ -70,27 +72,30 @@ __device__ __forceinline__ CornerPlan corner_plan(const Geom& g, const float* __
   return cp;
 }
 
-template <int CG, int OG, int GPD>
+template <int CG, int OG, int GPD, int L>
 __global__ void __launch_bounds__(DG_THREADS)
 fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict__ w,
                   const float* __restrict__ off, const float* __restrict__ mask,
                   const float* __restrict__ bias, float* __restrict__ out) {
   constexpr int CPG = CG * GPD, OPD = OG * GPD;
-  constexpr int VW = CPG % 8 == 0 ? 8 : 4, NR = CPG / VW;  // channels per load, loads per corner
+  constexpr int CPL = CPG / L, GPL = GPD / L, OPL = GPL * OG;  // per lane
+  constexpr int VW = CPL % 8 == 0 ? 8 : 4, NR = CPL / VW;  // channels per load, loads per corner
+  static_assert(GPD % L == 0 && CPL % 4 == 0 && 32 % L == 0, "whole groups, 16-byte runs");
   extern __shared__ float ws[];  // [OPD][CG][kk]: out channels dgi*OPD .. of the group
   const int dgi = blockIdx.y;
   const int wcount = OPD * CG * g.kk;
   for (int i = threadIdx.x; i < wcount; i += DG_THREADS) ws[i] = w[(long long)dgi * wcount + i];
   __syncthreads();
-  const long long q = (long long)blockIdx.x * DG_THREADS + threadIdx.x;
+  const int l = threadIdx.x % L;  // this lane's part of the deformable group
+  const long long q = ((long long)blockIdx.x * DG_THREADS + threadIdx.x) / L;
   if (q >= g.NP) return;
   const int n = (int)(q / g.P);
   const int p = (int)(q - (long long)n * g.P);
   const int oy = p / g.Wo, ox = p - oy * g.Wo;
-  const float* xq = xt + dgi * CPG;
-  float acc[OPD];
+  const float* xq = xt + dgi * CPG + l * CPL;
+  float acc[OPL];
 #pragma unroll
-  for (int i = 0; i < OPD; ++i) acc[i] = 0.f;
+  for (int i = 0; i < OPL; ++i) acc[i] = 0.f;
   for (int k = 0; k < g.kk; ++k) {
     const CornerPlan cp = corner_plan(g, off, mask, n, p, oy, ox, k, dgi);
     if (!cp.s.valid) continue;
@@ -106,46 +111,53 @@ fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict_
 #pragma unroll
       for (int e = 0; e < VW; ++e) {
         const float v = w1 * a[e] + w2 * b[e] + w3 * c[e] + w4 * d[e];
-        const int cl = VW * qd + e;  // channel within the deformable group
+        const int cl = VW * qd + e;  // channel within this lane's part
         const int j = cl / CG, cc = cl - (cl / CG) * CG;
+        const int gj = l * GPL + j;  // convolution group within the deformable group
 #pragma unroll
         for (int o = 0; o < OG; ++o)
-          acc[j * OG + o] = fmaf(ws[((j * OG + o) * CG + cc) * g.kk + k], v, acc[j * OG + o]);
+          acc[j * OG + o] = fmaf(ws[((gj * OG + o) * CG + cc) * g.kk + k], v, acc[j * OG + o]);
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < OPD; ++i) {
-    const int oc = dgi * OPD + i;
+  for (int i = 0; i < OPL; ++i) {
+    const int oc = dgi * OPD + l * OPL + i;
     out[((long long)n * g.outC + oc) * g.P + p] = acc[i] + (g.use_bias ? __ldg(bias + oc) : 0.f);
   }
 }
 
-// Sum of v[0..31] over the warp's lanes, transposed: lane L returns the total
-// of v[L] (16 + 8 + 4 + 2 + 1 shuffles).
-__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32], int lane) {
+// Sum over the warp's pixels (lanes L apart) of v[0..32/L-1], transposed: the
+// lane of pixel slot j (lane / L == j) returns the total of v[j].
+template <int L>
+__device__ __forceinline__ float pixel_transpose_sum(float (&v)[32 / L], int lane) {
+  constexpr int PL = 32 / L;
+  int d = 16;
 #pragma unroll
-  for (int d = 16; d >= 1; d >>= 1) {
+  for (int h = PL / 2; h >= 1; h >>= 1, d >>= 1) {
     const bool upper = (lane & d) != 0;
 #pragma unroll
-    for (int i = 0; i < d; ++i) {
-      const float send = upper ? v[i] : v[i + d];
-      const float keep = upper ? v[i + d] : v[i];
+    for (int i = 0; i < h; ++i) {
+      const float send = upper ? v[i] : v[i + h];
+      const float keep = upper ? v[i + h] : v[i];
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, d);
     }
   }
   return v[0];
 }
 
-template <int CG, int OG, int GPD>
+template <int CG, int OG, int GPD, int L>
 __global__ void __launch_bounds__(DG_THREADS)
 bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict__ w,
                   const float* __restrict__ xt, const float* __restrict__ off,
                   const float* __restrict__ mask, float* __restrict__ gxt,
                   float* __restrict__ goff, float* __restrict__ gmask, float* __restrict__ gw) {
   constexpr int CPG = CG * GPD, OPD = OG * GPD, NV = OPD * CG;
-  constexpr int VW = CPG % 8 == 0 ? 8 : 4, NR = CPG / VW;  // channels per load, loads per corner
-  static_assert(NV <= 32, "one grad_weight value per lane");
+  constexpr int CPL = CPG / L, GPL = GPD / L, OPL = GPL * OG, NVL = NV / L;  // per lane
+  constexpr int PL = 32 / L;  // pixels of a warp
+  constexpr int VW = CPL % 8 == 0 ? 8 : 4, NR = CPL / VW;  // channels per load, loads per corner
+  static_assert(GPD % L == 0 && CPL % 4 == 0 && 32 % L == 0, "whole groups, 16-byte runs");
+  static_assert(NVL <= PL, "one grad_weight value per pixel slot of the warp");
   extern __shared__ float sm[];  // weights [OPD][CG][kk], then grad_weight sums, same layout
   const int dgi = blockIdx.y;
   const int wcount = OPD * CG * g.kk;
@@ -157,26 +169,28 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const long long q = (long long)blockIdx.x * DG_THREADS + threadIdx.x;
+  const int l = lane % L;  // this lane's part of the deformable group
+  const long long q = ((long long)blockIdx.x * DG_THREADS + threadIdx.x) / L;
   const bool valid = q < g.NP;  // no early exit: the warp reduces together
   const int n = valid ? (int)(q / g.P) : 0;
   const int p = valid ? (int)(q - (long long)n * g.P) : 0;
   const int oy = p / g.Wo, ox = p - oy * g.Wo;
-  float gov[OPD];
+  float gov[OPL];
 #pragma unroll
-  for (int i = 0; i < OPD; ++i)
-    gov[i] = valid ? __ldg(go + ((long long)n * g.outC + dgi * OPD + i) * g.P + p) : 0.f;
-  const float* xq = xt + dgi * CPG;
-  float* gq = gxt + dgi * CPG;
+  for (int i = 0; i < OPL; ++i)
+    gov[i] = valid ? __ldg(go + ((long long)n * g.outC + dgi * OPD + l * OPL + i) * g.P + p)
+                   : 0.f;
+  const float* xq = xt + dgi * CPG + l * CPL;
+  float* gq = gxt + dgi * CPG + l * CPL;
   const int zoff = g.N * g.HW * g.C;
   for (int k = 0; k < g.kk; ++k) {
-    float gwp[32];
+    float gwp[PL];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) gwp[i] = 0.f;
+    for (int i = 0; i < PL; ++i) gwp[i] = 0.f;
+    float s_h = 0.f, s_w = 0.f, s_m = 0.f, mscale = 1.f;
     if (valid) {
       const CornerPlan cp = corner_plan(g, off, mask, n, p, oy, ox, k, dgi);
-      float s_h = 0.f, s_w = 0.f, s_m = 0.f;
-      const float mscale = mask_grad_scale(g, cp.m);
+      mscale = mask_grad_scale(g, cp.m);
       if (cp.s.valid) {
         const float m = cp.m;
 #pragma unroll
@@ -189,12 +203,13 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
           float top[VW];
 #pragma unroll
           for (int e = 0; e < VW; ++e) {
-            const int cl = VW * qd + e;
+            const int cl = VW * qd + e;  // channel within this lane's part
             const int j = cl / CG, cc = cl - (cl / CG) * CG;
+            const int gj = l * GPL + j;
             float gc = 0.f;  // grad column (.mm:820-821)
 #pragma unroll
             for (int o = 0; o < OG; ++o)
-              gc = fmaf(gov[j * OG + o], ws[((j * OG + o) * CG + cc) * g.kk + k], gc);
+              gc = fmaf(gov[j * OG + o], ws[((gj * OG + o) * CG + cc) * g.kk + k], gc);
             const float A = a[e], B = b[e], Cv = c[e], D = d[e];
             s_h += m * coord_dh(cp.s, A, B, Cv, D) * gc;
             s_w += m * coord_dw(cp.s, A, B, Cv, D) * gc;
@@ -218,15 +233,24 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
           }
         }
       }
-      // this thread owns the pixel's (deformable group, tap) gradients
-      // (col2im_coord, deform_conv2d.metal:225-295)
+    }
+    // the pixel's (deformable group, tap) gradients, summed over its L lanes
+    // and stored by the first (col2im_coord, deform_conv2d.metal:225-295)
+#pragma unroll
+    for (int d = 1; d < L; d <<= 1) {
+      s_h += __shfl_xor_sync(0xffffffffu, s_h, d);
+      s_w += __shfl_xor_sync(0xffffffffu, s_w, d);
+      s_m += __shfl_xor_sync(0xffffffffu, s_m, d);
+    }
+    if (valid && l == 0) {
       const long long oi = off_h_index(g, n, dgi, k, p);
       goff[oi] = s_h;
       goff[oi + g.P] = s_w;
       if (g.use_mask) gmask[mask_index(g, n, dgi, k, p)] = s_m * mscale;
     }
-    const float tot = warp_transpose_sum32(gwp, lane);
-    if (lane < NV) atomicAdd(&gws[lane * g.kk + k], tot);
+    const float tot = pixel_transpose_sum<L>(gwp, lane);
+    const int jv = lane / L;  // the value this lane now holds
+    if (jv < NVL) atomicAdd(&gws[(l * NVL + jv) * g.kk + k], tot);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < wcount; i += DG_THREADS)
@@ -239,21 +263,21 @@ using BwdFn = void (*)(Geom, const float*, const float*, const float*, const flo
                        const float*, float*, float*, float*, float*);
 
 struct DgroupEntry {
-  int cg, og, gpd;
+  int cg, og, gpd, lanes;
   FwdFn fwd;
   BwdFn bwd;
 };
 
-#define DG_ENTRY(CG, OG, GPD) \
-  { CG, OG, GPD, fwd_dgroup_kernel<CG, OG, GPD>, bwd_dgroup_kernel<CG, OG, GPD> }
+#define DG_ENTRY(CG, OG, GPD, L) \
+  { CG, OG, GPD, L, fwd_dgroup_kernel<CG, OG, GPD, L>, bwd_dgroup_kernel<CG, OG, GPD, L> }
 
 // (channels, out channels) per convolution group x groups per deformable
 // group: 4, 8 or 16 channels per deformable group, <= 32 grad_weight values
-// per pixel.
+// per pixel; lanes per (pixel, deformable group): 4 channels each.
 const DgroupEntry kDgroup[] = {
-    DG_ENTRY(1, 1, 4), DG_ENTRY(1, 1, 8), DG_ENTRY(1, 1, 16), DG_ENTRY(2, 2, 2),
-    DG_ENTRY(2, 2, 4), DG_ENTRY(2, 2, 8), DG_ENTRY(4, 4, 1),  DG_ENTRY(4, 4, 2),
-    DG_ENTRY(1, 2, 4), DG_ENTRY(1, 2, 8), DG_ENTRY(2, 4, 2),  DG_ENTRY(2, 4, 4),
+    DG_ENTRY(1, 1, 4, 1), DG_ENTRY(1, 1, 8, 2), DG_ENTRY(1, 1, 16, 4), DG_ENTRY(2, 2, 2, 1),
+    DG_ENTRY(2, 2, 4, 2), DG_ENTRY(2, 2, 8, 4), DG_ENTRY(4, 4, 1, 1),  DG_ENTRY(4, 4, 2, 2),
+    DG_ENTRY(1, 2, 4, 1), DG_ENTRY(1, 2, 8, 2), DG_ENTRY(2, 4, 2, 1),  DG_ENTRY(2, 4, 4, 2),
 };
 
 const DgroupEntry* find_dgroup(const Geom& g) {
@@ -276,7 +300,7 @@ cudaError_t launch_fwd_dgroup(const Geom& g, const float* xt, const float* w, co
                               cudaStream_t stream) {
   if (!dgroup_supported(g)) return cudaErrorInvalidValue;
   const DgroupEntry* e = find_dgroup(g);
-  dim3 grid((unsigned)((g.NP + DG_THREADS - 1) / DG_THREADS), g.dg);
+  dim3 grid((unsigned)((g.NP * e->lanes + DG_THREADS - 1) / DG_THREADS), g.dg);
   const size_t smem = (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   e->fwd<<<grid, DG_THREADS, smem, stream>>>(g, xt, w, off, mask, bias, out);
@@ -288,7 +312,7 @@ cudaError_t launch_bwd_dgroup(const Geom& g, const float* go, const float* w, co
                               float* gmask, float* gw, cudaStream_t stream) {
   if (!dgroup_supported(g)) return cudaErrorInvalidValue;
   const DgroupEntry* e = find_dgroup(g);
-  dim3 grid((unsigned)((g.NP + DG_THREADS - 1) / DG_THREADS), g.dg);
+  dim3 grid((unsigned)((g.NP * e->lanes + DG_THREADS - 1) / DG_THREADS), g.dg);
   const size_t smem = 2 * (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   e->bwd<<<grid, DG_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
