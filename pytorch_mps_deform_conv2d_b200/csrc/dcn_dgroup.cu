@@ -263,21 +263,27 @@ using BwdFn = void (*)(Geom, const float*, const float*, const float*, const flo
                        const float*, float*, float*, float*, float*);
 
 struct DgroupEntry {
-  int cg, og, gpd, lanes;
+  int cg, og, gpd, lanes_fwd, lanes_bwd;
   FwdFn fwd;
   BwdFn bwd;
 };
 
-#define DG_ENTRY(CG, OG, GPD, L) \
-  { CG, OG, GPD, L, fwd_dgroup_kernel<CG, OG, GPD, L>, bwd_dgroup_kernel<CG, OG, GPD, L> }
+#define DG_ENTRY(CG, OG, GPD, LF, LB)                                           \
+  {                                                                             \
+    CG, OG, GPD, LF, LB, fwd_dgroup_kernel<CG, OG, GPD, LF>,                    \
+        bwd_dgroup_kernel<CG, OG, GPD, LB>                                      \
+  }
 
 // (channels, out channels) per convolution group x groups per deformable
 // group: 4, 8 or 16 channels per deformable group, <= 32 grad_weight values
-// per pixel; lanes per (pixel, deformable group): 4 channels each.
+// per pixel; lanes per (pixel, deformable group): 8 channels each in the
+// forward (32-byte loads), 4 in the backward (measured faster on the grouped
+// workload: 0.054 / 0.102 ms against 0.060 / 0.140 ms the other way round).
 const DgroupEntry kDgroup[] = {
-    DG_ENTRY(1, 1, 4, 1), DG_ENTRY(1, 1, 8, 2), DG_ENTRY(1, 1, 16, 4), DG_ENTRY(2, 2, 2, 1),
-    DG_ENTRY(2, 2, 4, 2), DG_ENTRY(2, 2, 8, 4), DG_ENTRY(4, 4, 1, 1),  DG_ENTRY(4, 4, 2, 2),
-    DG_ENTRY(1, 2, 4, 1), DG_ENTRY(1, 2, 8, 2), DG_ENTRY(2, 4, 2, 1),  DG_ENTRY(2, 4, 4, 2),
+    DG_ENTRY(1, 1, 4, 1, 1),  DG_ENTRY(1, 1, 8, 1, 2), DG_ENTRY(1, 1, 16, 2, 4),
+    DG_ENTRY(2, 2, 2, 1, 1),  DG_ENTRY(2, 2, 4, 1, 2), DG_ENTRY(2, 2, 8, 2, 4),
+    DG_ENTRY(4, 4, 1, 1, 1),  DG_ENTRY(4, 4, 2, 1, 2), DG_ENTRY(1, 2, 4, 1, 1),
+    DG_ENTRY(1, 2, 8, 1, 2),  DG_ENTRY(2, 4, 2, 1, 1), DG_ENTRY(2, 4, 4, 1, 2),
 };
 
 const DgroupEntry* find_dgroup(const Geom& g) {
@@ -300,7 +306,7 @@ cudaError_t launch_fwd_dgroup(const Geom& g, const float* xt, const float* w, co
                               cudaStream_t stream) {
   if (!dgroup_supported(g)) return cudaErrorInvalidValue;
   const DgroupEntry* e = find_dgroup(g);
-  dim3 grid((unsigned)((g.NP * e->lanes + DG_THREADS - 1) / DG_THREADS), g.dg);
+  dim3 grid((unsigned)((g.NP * e->lanes_fwd + DG_THREADS - 1) / DG_THREADS), g.dg);
   const size_t smem = (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   e->fwd<<<grid, DG_THREADS, smem, stream>>>(g, xt, w, off, mask, bias, out);
@@ -312,7 +318,7 @@ cudaError_t launch_bwd_dgroup(const Geom& g, const float* go, const float* w, co
                               float* gmask, float* gw, cudaStream_t stream) {
   if (!dgroup_supported(g)) return cudaErrorInvalidValue;
   const DgroupEntry* e = find_dgroup(g);
-  dim3 grid((unsigned)((g.NP * e->lanes + DG_THREADS - 1) / DG_THREADS), g.dg);
+  dim3 grid((unsigned)((g.NP * e->lanes_bwd + DG_THREADS - 1) / DG_THREADS), g.dg);
   const size_t smem = 2 * (size_t)g.Og * (g.cpg / g.Cg) * g.Cg * g.kk * sizeof(float);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
   e->bwd<<<grid, DG_THREADS, smem, stream>>>(g, go, w, xt, off, mask, gxt, goff, gmask, gw);
