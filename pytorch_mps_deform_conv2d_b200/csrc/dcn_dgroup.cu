@@ -81,10 +81,17 @@ fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict_
   constexpr int CPL = CPG / L, GPL = GPD / L, OPL = GPL * OG;  // per lane
   constexpr int VW = CPL % 8 == 0 ? 8 : 4, NR = CPL / VW;  // channels per load, loads per corner
   static_assert(GPD % L == 0 && CPL % 4 == 0 && 32 % L == 0, "whole groups, 16-byte runs");
-  extern __shared__ float ws[];  // [OPD][CG][kk]: out channels dgi*OPD .. of the group
+  constexpr int NV = OPD * CG, NVL = NV / L;  // weights per tap: of the group, of a lane
+  static_assert(NVL % 4 == 0, "16-byte weight loads");
+  // the deformable group's weights (out channels dgi*OPD ..), tap-major
+  // [kk][OPD][CG], so that a lane's weights of one tap are NVL consecutive floats
+  extern __shared__ float ws[];
   const int dgi = blockIdx.y;
   const int wcount = OPD * CG * g.kk;
-  for (int i = threadIdx.x; i < wcount; i += DG_THREADS) ws[i] = w[(long long)dgi * wcount + i];
+  for (int i = threadIdx.x; i < wcount; i += DG_THREADS) {
+    const int v = i / g.kk;
+    ws[(i - v * g.kk) * NV + v] = w[(long long)dgi * wcount + i];
+  }
   __syncthreads();
   const int l = threadIdx.x % L;  // this lane's part of the deformable group
   const long long q = ((long long)blockIdx.x * DG_THREADS + threadIdx.x) / L;
@@ -101,6 +108,15 @@ fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict_
     if (!cp.s.valid) continue;
     const float w1 = cp.s.w1 * cp.m, w2 = cp.s.w2 * cp.m, w3 = cp.s.w3 * cp.m,
                 w4 = cp.s.w4 * cp.m;
+    float wk[NVL];  // this lane's weights of tap k: [group][out][channel]
+#pragma unroll
+    for (int i = 0; i < NVL; i += 4) {
+      const float4 t4 = *reinterpret_cast<const float4*>(ws + k * NV + l * NVL + i);
+      wk[i] = t4.x;
+      wk[i + 1] = t4.y;
+      wk[i + 2] = t4.z;
+      wk[i + 3] = t4.w;
+    }
 #pragma unroll
     for (int qd = 0; qd < NR; ++qd) {
       float a[VW], b[VW], c[VW], d[VW];
@@ -113,10 +129,9 @@ fwd_dgroup_kernel(Geom g, const float* __restrict__ xt, const float* __restrict_
         const float v = w1 * a[e] + w2 * b[e] + w3 * c[e] + w4 * d[e];
         const int cl = VW * qd + e;  // channel within this lane's part
         const int j = cl / CG, cc = cl - (cl / CG) * CG;
-        const int gj = l * GPL + j;  // convolution group within the deformable group
 #pragma unroll
         for (int o = 0; o < OG; ++o)
-          acc[j * OG + o] = fmaf(ws[((gj * OG + o) * CG + cc) * g.kk + k], v, acc[j * OG + o]);
+          acc[j * OG + o] = fmaf(wk[(j * OG + o) * CG + cc], v, acc[j * OG + o]);
       }
     }
   }
@@ -158,13 +173,17 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
   constexpr int VW = CPL % 8 == 0 ? 8 : 4, NR = CPL / VW;  // channels per load, loads per corner
   static_assert(GPD % L == 0 && CPL % 4 == 0 && 32 % L == 0, "whole groups, 16-byte runs");
   static_assert(NVL <= PL, "one grad_weight value per pixel slot of the warp");
-  extern __shared__ float sm[];  // weights [OPD][CG][kk], then grad_weight sums, same layout
+  // weights tap-major [kk][OPD][CG] (a lane's weights of one tap: NVL
+  // consecutive floats), then the grad_weight sums in the weight's layout
+  // [OPD][CG][kk]
+  extern __shared__ float sm[];
   const int dgi = blockIdx.y;
   const int wcount = OPD * CG * g.kk;
   float* ws = sm;
   float* gws = sm + wcount;
   for (int i = threadIdx.x; i < wcount; i += DG_THREADS) {
-    ws[i] = w[(long long)dgi * wcount + i];
+    const int v = i / g.kk;
+    ws[(i - v * g.kk) * NV + v] = w[(long long)dgi * wcount + i];
     gws[i] = 0.f;
   }
   __syncthreads();
@@ -193,6 +212,15 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
       mscale = mask_grad_scale(g, cp.m);
       if (cp.s.valid) {
         const float m = cp.m;
+        float wk[NVL];  // this lane's weights of tap k: [group][out][channel]
+#pragma unroll
+        for (int i = 0; i < NVL; i += 4) {
+          const float4 t4 = *reinterpret_cast<const float4*>(ws + k * NV + l * NVL + i);
+          wk[i] = t4.x;
+          wk[i + 1] = t4.y;
+          wk[i + 2] = t4.z;
+          wk[i + 3] = t4.w;
+        }
 #pragma unroll
         for (int qd = 0; qd < NR; ++qd) {
           float a[VW], b[VW], c[VW], d[VW];
@@ -205,11 +233,9 @@ bwd_dgroup_kernel(Geom g, const float* __restrict__ go, const float* __restrict_
           for (int e = 0; e < VW; ++e) {
             const int cl = VW * qd + e;  // channel within this lane's part
             const int j = cl / CG, cc = cl - (cl / CG) * CG;
-            const int gj = l * GPL + j;
             float gc = 0.f;  // grad column (.mm:820-821)
 #pragma unroll
-            for (int o = 0; o < OG; ++o)
-              gc = fmaf(gov[j * OG + o], ws[((gj * OG + o) * CG + cc) * g.kk + k], gc);
+            for (int o = 0; o < OG; ++o) gc = fmaf(gov[j * OG + o], wk[(j * OG + o) * CG + cc], gc);
             const float A = a[e], B = b[e], Cv = c[e], D = d[e];
             s_h += m * coord_dh(cp.s, A, B, Cv, D) * gc;
             s_w += m * coord_dw(cp.s, A, B, Cv, D) * gc;
