@@ -8,9 +8,11 @@
   empty grad_bias.
 * Autograd formulas for ``deform_conv2d_forward`` and
   ``deform_conv2d_forward_rows``, so the operators are differentiable when
-  called directly (the public ``deform_conv2d`` goes
-  through ``ops._DeformConv2dFunction``, which mirrors the reference's
-  ``_DeformConv2dFunction``, src/deform_conv2d_mps/ops.py:68-115).
+  called directly.  The public ``deform_conv2d`` runs the ``deform_conv2d``
+  operator in eager mode (its autograd node is registered in C++,
+  csrc/torch_ops.cpp) and, while torch.compile traces, goes through
+  ``ops._DeformConv2dFunction``, which mirrors the reference's
+  ``_DeformConv2dFunction`` (src/deform_conv2d_mps/ops.py:68-115).
 
 The reference registers only a real-device implementation
 (src/deform_conv2d_mps/_C/deform_conv2d_mps.mm:918-925); these are additions.
@@ -116,6 +118,7 @@ def register() -> None:
     operator library has been loaded)."""
     q = NS + "::"
     torch.library.register_fake(q + "deform_conv2d_forward")(_forward_fake)
+    torch.library.register_fake(q + "deform_conv2d")(_forward_fake)
     torch.library.register_fake(q + "deform_conv2d_backward")(_backward_fake)
     torch.library.register_fake(q + "deformable_col2im")(_col2im_fake)
     torch.library.register_fake(q + "deformable_col2im_coord")(_col2im_coord_fake)

@@ -13,6 +13,7 @@
 #include <ATen/Context.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <torch/csrc/autograd/custom_function.h>
 #include <torch/library.h>
 
 #include "dcn_b200.h"
@@ -425,6 +426,88 @@ std::tuple<at::Tensor, at::Tensor> deformable_col2im_coord(
   return std::make_tuple(grad_offset, grad_mask);
 }
 
+// Differentiable deform_conv2d as one operator, its autograd node in C++: the
+// eager path of the public Python API, with no Python frame in the forward or
+// the backward.  The same computation as ops._DeformConv2dFunction
+// (src/deform_conv2d_mps/ops.py:68-115 in the reference): the forward and
+// backward operators above, gradients for input, weight, offset, mask (none
+// for an empty mask) and bias (none when absent).  Both operators are reached
+// through the dispatcher, so fake tensors take their fake kernels.
+class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
+ public:
+  static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& input,
+                            const at::Tensor& weight, const at::Tensor& offset,
+                            const at::Tensor& mask, const at::Tensor& bias, int64_t stride_h,
+                            int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                            int64_t dilation_w, int64_t groups, int64_t deformable_groups,
+                            int64_t math) {
+    static auto op = c10::Dispatcher::singleton()
+                         .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_forward", "")
+                         .typed<at::Tensor(const at::Tensor&, const at::Tensor&,
+                                           const at::Tensor&, const at::Tensor&,
+                                           const c10::optional<at::Tensor>&, int64_t, int64_t,
+                                           int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                           int64_t)>();
+    const bool has_bias = bias.defined() && bias.numel() > 0;
+    c10::optional<at::Tensor> b;
+    if (has_bias) b = bias;
+    at::Tensor out;
+    {
+      at::AutoDispatchBelowADInplaceOrView below;
+      out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                    dilation_w, groups, deformable_groups, math);
+    }
+    ctx->save_for_backward({input, weight, offset, mask, bias});
+    ctx->saved_data["ints"] = std::vector<int64_t>{stride_h,   stride_w, pad_h,
+                                                   pad_w,      dilation_h, dilation_w,
+                                                   groups,     deformable_groups, math};
+    ctx->saved_data["has_bias"] = has_bias;
+    return out;
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    static auto op = c10::Dispatcher::singleton()
+                         .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_backward", "")
+                         .typed<Grads(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                      const at::Tensor&, const at::Tensor&,
+                                      const c10::optional<at::Tensor>&, int64_t, int64_t,
+                                      int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                                      int64_t)>();
+    const auto saved = ctx->get_saved_variables();
+    const auto v = ctx->saved_data["ints"].toIntVector();
+    const bool has_bias = ctx->saved_data["has_bias"].toBool();
+    const at::Tensor& mask = saved[3];
+    c10::optional<at::Tensor> b;
+    if (has_bias) b = saved[4];
+    auto r = op.call(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0], v[1],
+                     v[2], v[3], v[4], v[5], v[6], v[7], v[8]);
+    const bool has_mask = mask.numel() > 0;
+    return {std::get<0>(r),
+            std::get<3>(r),
+            std::get<1>(r),
+            has_mask ? std::get<2>(r) : at::Tensor(),
+            has_bias ? std::get<4>(r) : at::Tensor(),
+            at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(),
+            at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor()};
+  }
+};
+
+at::Tensor deform_conv2d_autograd(const at::Tensor& input, const at::Tensor& weight,
+                                  const at::Tensor& offset, const at::Tensor& mask,
+                                  const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                  int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                  int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                  int64_t deformable_groups, int64_t math) {
+  // an absent bias travels as an empty tensor (the autograd node takes
+  // defined tensors only)
+  return DeformConv2dFn::apply(input, weight, offset, mask,
+                               bias.has_value() && bias->defined() ? *bias : input.new_empty({0}),
+                               stride_h, stride_w,
+                               pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups,
+                               math);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(deform_conv2d_b200, m) {
@@ -456,6 +539,15 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
       "Tensor offset, Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, "
       "int pad_w, int dilation_h, int dilation_w, int groups, int deformable_groups, "
       "int row_begin, int math=-1) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  // The differentiable operator (forward + the C++ autograd node above).
+  m.def(
+      "deform_conv2d(Tensor input, Tensor weight, Tensor offset, Tensor mask, Tensor? bias, "
+      "int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, int dilation_w, "
+      "int groups, int deformable_groups, int math=-1) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(deform_conv2d_b200, Autograd, m) {
+  m.impl("deform_conv2d", TORCH_FN(deform_conv2d_autograd));
 }
 
 TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
@@ -465,4 +557,5 @@ TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
   m.impl("deform_conv2d_backward", TORCH_FN(deform_conv2d_backward));
   m.impl("deform_conv2d_forward_rows", TORCH_FN(deform_conv2d_forward_rows));
   m.impl("deform_conv2d_backward_rows", TORCH_FN(deform_conv2d_backward_rows));
+  m.impl("deform_conv2d", TORCH_FN(deform_conv2d_forward));  // below autograd
 }

@@ -169,6 +169,13 @@ def deform_conv2d_ex(input, offset, weight, bias=None, stride=(1, 1),
         raise RuntimeError("weight must be 4-D (outC, C/groups, kh, kw) with C/groups > 0")
     groups = input.shape[1] // weight.shape[1]
     deformable_groups = offset.shape[1] // (2 * kh * kw)
+    if not torch.compiler.is_compiling():
+        # eager: the differentiable operator, whose autograd node is C++ (no
+        # Python frame in the forward or the backward)
+        return _ops().deform_conv2d(
+            input, weight, offset, mask if mask is not None else input.new_empty(0), bias,
+            stride[0], stride[1], padding[0], padding[1], dilation[0], dilation[1], groups,
+            deformable_groups, math=_flags(flags))
     return _DeformConv2dFunction.apply(
         input, weight, offset, mask, bias, stride, padding, dilation, groups,
         deformable_groups, _flags(flags))
