@@ -142,7 +142,9 @@ SideStreams* side_streams_locked() {
 
 class Fork {
  public:
-  explicit Fork(cudaStream_t main) : lk_(g_side_mu), ss_(side_streams_locked()), main_(main) {}
+  // `use` false: everything stays on the caller's stream
+  Fork(cudaStream_t main, bool use)
+      : lk_(g_side_mu), ss_(use ? side_streams_locked() : nullptr), main_(main) {}
   cudaStream_t side(int i) const { return ss_ ? ss_->s[i] : main_; }
   // side streams start after everything enqueued on the caller's stream so far
   cudaError_t fork() {
@@ -163,6 +165,13 @@ class Fork {
   SideStreams* ss_;
   cudaStream_t main_;
 };
+
+// The side streams pay when the helpers beside the input staging are large
+// enough to hide the cross-stream event waits: inputs of 16 MB and more (the
+// detection neck's 31 MB); below that the waits cost more than the overlap.
+bool side_streams_pay(const dcn::Geom& g) {
+  return (long long)g.N * g.C * g.HW * (long long)sizeof(float) >= (16LL << 20);
+}
 
 bool is_device_ptr(const void* p) {
   if (p == nullptr) return false;
@@ -427,7 +436,7 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     // the weight pack (side stream) runs beside the input transpose
     const bool split = split_math(flags);
     float* wt = ws.take(dcn::tc_fwd_weight_bytes(g, split) / sizeof(float));
-    Fork fk(stream);
+    Fork fk(stream, side_streams_pay(g));
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
                 "tc_pack_weight");
@@ -670,7 +679,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     // grad_out prep (side 0, after zeroing grad_bias, which it sums into) and
     // the weight pack + the zeroing of the other accumulators (side 1) run
     // beside the input transpose
-    Fork fk(stream);
+    Fork fk(stream, side_streams_pay(g));
     DCN_ORDER(fk.fork(), "fork");
     if (bias_in_prep) {
       dcn::ZeroList zb{};
