@@ -155,7 +155,11 @@ __device__ __forceinline__ unsigned short to_h16(float y) {
 
 // 704 threads: 22 warps, up to 6 on one SM sub-partition of 16K registers,
 // so at most 80 registers a thread (a few bytes spill).
-template <int MODE>
+// NH = 2: tiles of 2 x 256 out channels (out channels per group a multiple of
+// 512): the gathered A tile feeds both halves, so it is gathered once instead
+// of once per 256 out channels; the two accumulators fill tensor memory (no
+// double buffering) and 80 KB stages leave room for two.
+template <int MODE, int NH>
 __global__ void __launch_bounds__(THREADS, 1)
 fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __restrict__ xt_,
               int bn, int tcols, int mtiles, int ntiles_n, int ntiles,
@@ -164,12 +168,14 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   using Cfg = FwdCfg<MODE>;
   constexpr bool SPLIT = Cfg::SPLIT, H16 = Cfg::H16;
   constexpr int FMT = Cfg::FMT;
-  constexpr int STAGES = Cfg::STAGES, PARTS = Cfg::PARTS, KCH = Cfg::KCH;
+  constexpr int STAGES = NH == 2 ? 2 : Cfg::STAGES, PARTS = Cfg::PARTS, KCH = Cfg::KCH;
+  static_assert(NH == 1 || (NH == 2 && !SPLIT), "wide tiles for single-part operands");
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
   const uint32_t sA0 = tc::smem_u32(smem);
-  const uint32_t b_stage = (uint32_t)bn * 128;
+  const int tn = NH * bn;  // out channels of a tile
+  const uint32_t b_stage = (uint32_t)tn * 128;
   const uint32_t sB0 = sA0 + STAGES * PARTS * A_STAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * PARTS * (A_STAGE + b_stage));
   uint64_t* empty = full + STAGES;
@@ -215,7 +221,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     constexpr int ESZ = H16 ? 2 : 4;  // element bytes
     int gs = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const Tile T = tile_of(t, mtiles, ntiles_n, bn);
+      const Tile T = tile_of(t, mtiles, ntiles_n, tn);
       const int row = gw * 8 + sub;
       const long long q = T.q0 + row;
       const bool rvalid = q < g.NP;
@@ -332,7 +338,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     if (lane == 0) {
       int gs = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const Tile T = tile_of(t, mtiles, ntiles_n, bn);
+        const Tile T = tile_of(t, mtiles, ntiles_n, tn);
         const int row = T.gi * g.Og + T.o0;
         for (int s = 0; s < steps; ++s, ++gs) {
           const int st = gs % STAGES;
@@ -340,7 +346,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
           tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
           const uint32_t sB = sB0 + st * PARTS * b_stage;
-          tc::tma_load_2d(sB, &wmap, s * KCH, row, &full[st]);
+#pragma unroll
+          for (int h = 0; h < NH; ++h)  // 256-row boxes
+            tc::tma_load_2d(sB + h * bn * 128, &wmap, s * KCH, row + h * bn, &full[st]);
           if constexpr (SPLIT)  // low parts: rows outC .. 2*outC - 1 of the packed weight
             tc::tma_load_2d(sB + b_stage, &wmap, s * KCH, g.outC + row, &full[st]);
         }
@@ -355,15 +363,21 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
                                                : tc::idesc_tf32(BM, bn);
       int gs = 0, it = 0;
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-        const int acc = it & 1;
-        if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_fwd_status);
+        // one accumulator set per tile: two alternate (NH = 1), or one fills
+        // tensor memory (NH = 2)
+        const int acc = NH == 2 ? 0 : (it & 1);
+        const int use = NH == 2 ? it : (it >> 1);  // earlier tiles in this accumulator
+        if (use >= 1) tc::mbar_wait(&acc_empty[acc], (use - 1) & 1, &g_tc_fwd_status);
         tc::tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(acc * bn);
+        const uint32_t d0 = tmem + (uint32_t)(acc * tn);
         for (int s = 0; s < steps; ++s, ++gs) {
           const int st = gs % STAGES;
           tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_fwd_status);
           tc::tc_fence_after();
-          const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB = sB0 + st * PARTS * b_stage;
+          const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB0s = sB0 + st * PARTS * b_stage;
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+          const uint32_t d = d0 + (uint32_t)(h * bn), sB = sB0s + (uint32_t)(h * bn * 128);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {  // 32 bytes of K per UMMA: 8 tf32 or 16 bf16
             if constexpr (H16) {
@@ -381,6 +395,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
                             (s | j) != 0 ? 1u : 0u);
             }
           }
+          }
           tc::umma_commit(&empty[st]);
         }
         tc::umma_commit(&acc_full[acc]);
@@ -391,9 +406,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     // ------------------------------ epilogue ------------------------------
     int it = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const Tile T = tile_of(t, mtiles, ntiles_n, bn);
-      const int acc = it & 1;
-      tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_fwd_status);
+      const Tile T = tile_of(t, mtiles, ntiles_n, tn);
+      const int acc = NH == 2 ? 0 : (it & 1);
+      tc::mbar_wait(&acc_full[acc], (NH == 2 ? it : (it >> 1)) & 1, &g_tc_fwd_status);
       tc::tc_fence_after();
       const int r = warp * 32 + lane;
       const long long q = T.q0 + r;
@@ -402,8 +417,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       const int p = valid ? (int)(q - (long long)n * g.P) : 0;
       const long long obase = ((long long)n * g.outC + (long long)T.gi * g.Og + T.o0) * g.P + p;
       const int bbase = T.gi * g.Og + T.o0;
-      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
-      for (int cb = 0; cb < bn; cb += 8) {
+      const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * tn);
+      for (int cb = 0; cb < tn; cb += 8) {
         float vv[8];
         tc::tmem_ld8(ta + (uint32_t)cb, vv);
         tc::tmem_ld_wait();
@@ -472,20 +487,25 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
                             const void* off, const void* mask, const void* bias, void* out,
                             int num_sms, cudaStream_t stream) {
   const int bn = tc_bn(g);
-  const size_t smem = smem_bytes(bn, mode == kSplit);
-  auto kern = mode == kSplit ? fwd_tc_kernel<kSplit>
-               : mode == kBF16 ? fwd_tc_kernel<kBF16>
-               : mode == kF16  ? fwd_tc_kernel<kF16>
-                               : fwd_tc_kernel<kTF32>;
+  // 512 out channels a tile when the group has a multiple of 512 (not in
+  // 3xTF32, whose two operand parts would not fit two stages)
+  const bool wide = mode != kSplit && g.Og % 512 == 0;
+  const int tn = wide ? 2 * bn : bn;
+  const size_t smem = wide ? 2 * ((size_t)A_STAGE + (size_t)tn * 128) + 128 + 1024
+                           : smem_bytes(bn, mode == kSplit);
+  auto kern = mode == kSplit ? fwd_tc_kernel<kSplit, 1>
+              : mode == kBF16 ? (wide ? fwd_tc_kernel<kBF16, 2> : fwd_tc_kernel<kBF16, 1>)
+              : mode == kF16  ? (wide ? fwd_tc_kernel<kF16, 2> : fwd_tc_kernel<kF16, 1>)
+                              : (wide ? fwd_tc_kernel<kTF32, 2> : fwd_tc_kernel<kTF32, 1>);
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), (int)smem);
   if (e != cudaSuccess) return e;
   const int mtiles = (int)((g.NP + BM - 1) / BM);
-  const int ntiles_n = g.Og / bn;
+  const int ntiles_n = g.Og / tn;
   const long long ntiles = (long long)mtiles * ntiles_n * g.G;
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, tmem_cols_for(bn), mtiles, ntiles_n,
-                                         (int)ntiles, off, mask, bias, out);
+  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, wide ? 512 : tmem_cols_for(bn), mtiles,
+                                         ntiles_n, (int)ntiles, off, mask, bias, out);
   return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@ CASES = {  # name -> (case, bf16 tensor-core forward expected)
                                    use_bias=False, offset_scale=2.0), True),
     "c64-o48-asym-boundary": (dict(inC=64, outC=48, H=9, W=13, kh=3, kw=2, stride=(2, 1),
                                    pad=(1, 2), dil=(2, 1), offset_scale=8.0), True),
+    "c64-o512-wide": (dict(N=1, inC=64, outC=512, H=7, W=8, offset_scale=2.0), True),
     "c32-o32-upcast": (dict(inC=32, outC=32, H=9, W=10, offset_scale=2.0), False),
     "c6-o6-g3-upcast": (dict(inC=6, outC=6, groups=3, H=8, W=9), False),
 }

@@ -22,6 +22,10 @@ TC_CASES = {
     "c128-o16-asym": dict(inC=128, outC=16, H=8, W=11, kh=1, kw=3, stride=(2, 1),
                           pad=(0, 2), dil=(2, 1)),
     "c32-o512-ntiles": dict(N=1, inC=32, outC=512, H=7, W=9),
+    # 512 out channels a tile (two 256-column accumulators), two tiles per
+    # group, and two groups of 512
+    "c64-o1024-wide-ntiles": dict(N=1, inC=64, outC=1024, H=6, W=9),
+    "c128-o1024-g2-wide": dict(N=1, inC=128, outC=1024, groups=2, H=7, W=6, offset_scale=2.0),
     "c64-o256-boundary": dict(N=3, inC=64, outC=256, H=13, W=17, offset_scale=8.0),
     "c256-o256-neck-like": dict(N=1, inC=256, outC=256, H=20, W=30, offset_scale=4.0,
                                 mask_kind="sigmoid", weight_kind="kaiming"),
