@@ -116,7 +116,11 @@ DCN_API const char* dcn_last_error(void);
  * DCN_ERR_INVALID_ARGUMENT when it is non-positive. */
 DCN_API int dcn_output_size(const dcn_shape* shape, int64_t* out_h, int64_t* out_w);
 
-/* Bytes of workspace dcn_forward needs for `shape` and `flags`. */
+/* Bytes of workspace dcn_forward needs for `shape` and `flags`.  On the
+ * tensor-core path this includes a scratch (sized for the current device's SM
+ * count) with which the forward splits a short last round of tiles over all
+ * SMs; given a workspace without that scratch, dcn_forward runs whole tiles
+ * only -- the results differ only in the order of fp32 additions. */
 DCN_API size_t dcn_forward_workspace_size(const dcn_shape* shape, uint32_t flags);
 
 /* Row windows (no reference counterpart): output rows [row_begin,
@@ -233,8 +237,9 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
  * start-up).  Same arguments and results as dcn_forward without the workspace:
  * the scratch comes from a 16 MiB array compiled into the library, which every
  * GPU that loads the library holds until the process exits.  Shapes whose
- * dcn_forward_workspace_size exceeds 16 MiB are rejected with
- * DCN_ERR_WORKSPACE before anything is launched.  The first call on a device
+ * least workspace (dcn_forward_workspace_size without the optional
+ * split-round scratch) exceeds 16 MiB are rejected with DCN_ERR_WORKSPACE
+ * before anything is launched.  The first call on a device
  * looks up the array's device address there (cudaGetSymbolAddress); make that
  * first call before any stream capture.  All calls share the one array:
  * calls that can overlap on the GPU (different streams, or different host

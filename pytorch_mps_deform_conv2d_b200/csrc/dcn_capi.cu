@@ -272,7 +272,8 @@ FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
 // target of the tensor-core gathers' dropped corners.
 size_t xt_floats(const dcn::Geom& g) { return (size_t)g.N * g.HW * g.C + g.C; }
 
-size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
+// The least workspace the forward accepts.
+size_t fwd_ws_min(const dcn::Geom& g, uint32_t flags) {
   size_t b = align_up(xt_floats(g) * sizeof(float));  // xt + zero row
   switch (pick_fwd(g, flags)) {
     case FwdAlgo::kGemm:
@@ -287,6 +288,16 @@ size_t fwd_ws(const dcn::Geom& g, uint32_t flags) {
   }
   return b + kAlign;  // slack for aligning the caller's base pointer
 }
+
+// Scratch with which the tensor-core forward splits a short last round of
+// tiles over all SMs.  The size query includes it; a workspace of only the
+// minimum runs whole tiles (same results up to the order of fp32 sums).
+size_t fwd_tail_ws(const dcn::Geom& g, uint32_t flags) {
+  if (pick_fwd(g, flags) != FwdAlgo::kTc) return 0;
+  return align_up(dcn::tc_fwd_tail_bytes(g, split_math(flags), false, num_sms_current()));
+}
+
+size_t fwd_ws(const dcn::Geom& g, uint32_t flags) { return fwd_ws_min(g, flags) + fwd_tail_ws(g, flags); }
 
 // Tensor-core backward with the column buffer (weight gradient as a dense
 // GEMM over the columns the grad-column kernel writes); DCN_ALGO_TC_GATHER_WEIGHT
@@ -329,6 +340,13 @@ void* align_ptr(void* p) {
 namespace dcn {
 // Lets other translation units of the library report through dcn_last_error.
 void set_last_error(int code, const char* msg) { fail(code, "%s", msg); }
+// The least workspace dcn_forward accepts for this shape (0: invalid shape);
+// dcn_forward_workspace_size adds the optional tail scratch.
+size_t forward_min_workspace(const dcn_shape* s, uint32_t flags) {
+  Geom g;
+  if (make_geom(s, true, true, g, "dcn_forward_workspace_size") != DCN_OK) return 0;
+  return fwd_ws_min(g, flags);
+}
 }  // namespace dcn
 
 extern "C" {
@@ -419,11 +437,12 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     DCN_CUDA(dcn::launch_fill_bias(output, g.use_bias ? bias : nullptr, g, stream), "fill");
     return DCN_OK;
   }
-  const size_t need = fwd_ws(g, flags);
+  const size_t need = fwd_ws_min(g, flags);
   if (workspace_bytes < need || workspace == nullptr)
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
+  const size_t usable = workspace_bytes - (size_t)(ws.base - static_cast<char*>(workspace));
   float* xt = ws.take(xt_floats(g));
   const FwdAlgo algo = pick_fwd(g, flags);
   // xt (+ its zero row): a transpose of NCHW input, a copy of NHWC input
@@ -436,14 +455,17 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     // the weight pack (side stream) runs beside the input transpose
     const bool split = split_math(flags);
     float* wt = ws.take(dcn::tc_fwd_weight_bytes(g, split) / sizeof(float));
+    const int sms = num_sms_current();
+    const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, split, false, sms);
+    void* tail = tail_bytes > 0 && usable >= ws.used + tail_bytes ? ws.base + ws.used : nullptr;
     Fork fk(stream, side_streams_pay(g));
     DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, tail, fk.side(0)),
                 "tc_pack_weight");
     DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
-    DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, num_sms_current(),
-                                stream),
+    DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, tail,
+                                tail ? tail_bytes : 0, sms, stream),
              "fwd_tc");
     return DCN_OK;
   }
@@ -486,10 +508,18 @@ size_t bf16_upcast_bytes(const dcn::Geom& g) {
          align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + align_up((size_t)g.outC * 4) +
          align_up((size_t)g.N * g.outC * g.P * 4);
 }
-size_t fwd_bf16_ws(const dcn::Geom& g, uint32_t flags) {
+// The least workspace of the 16-bit forward, and with the tail scratch of the
+// tensor-core forward (the size query).
+size_t fwd_bf16_ws_min(const dcn::Geom& g, uint32_t flags) {
   if (use_bf16_tc(g, flags))
     return align_up(((size_t)g.N * g.HW * g.C + g.C) * 2) +
            align_up(dcn::tc_fwd_weight_bf16_bytes(g)) + kAlign;
+  return bf16_upcast_bytes(g) + kAlign + fwd_ws_min(g, flags);
+}
+size_t fwd_bf16_ws(const dcn::Geom& g, uint32_t flags) {
+  if (use_bf16_tc(g, flags))
+    return fwd_bf16_ws_min(g, flags) +
+           align_up(dcn::tc_fwd_tail_bytes(g, false, true, num_sms_current()));
   return bf16_upcast_bytes(g) + kAlign + fwd_ws(g, flags);
 }
 }  // namespace
@@ -517,7 +547,7 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
             "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
   DCN_CHECK(mask == nullptr || is_device_ptr(mask), "mask must be a %s CUDA tensor", tname);
   DCN_CHECK(bias == nullptr || is_device_ptr(bias), "bias must be a %s CUDA tensor", tname);
-  const size_t need = fwd_bf16_ws(g, flags);
+  const size_t need = fwd_bf16_ws_min(g, flags);
   if (workspace_bytes < need || workspace == nullptr)
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_forward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
@@ -525,6 +555,11 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
   if (use_bf16_tc(g, flags)) {
     void* xt = base;
     void* wt = base + align_up(((size_t)g.N * g.HW * g.C + g.C) * 2);
+    char* tail = static_cast<char*>(wt) + align_up(dcn::tc_fwd_weight_bf16_bytes(g));
+    const int sms = num_sms_current();
+    const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, false, true, sms);
+    const size_t usable = workspace_bytes - (size_t)(tail - static_cast<char*>(workspace));
+    if (tail_bytes == 0 || usable < tail_bytes) tail = nullptr;
     if (flags & DCN_INPUT_NHWC) {  // channels-last: a copy plus the zero row
       const size_t xb = (size_t)g.N * g.HW * g.C * 2;
       if (xb) DCN_CUDA(cudaMemcpyAsync(xt, input, xb, cudaMemcpyDeviceToDevice, stream), "copy");
@@ -535,9 +570,9 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
                                              stream),
                "nchw_to_nhwc");
     }
-    DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, stream), "tc_pack_weight");
-    DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, f16,
-                                     num_sms_current(), stream),
+    DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, tail, stream), "tc_pack_weight");
+    DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, f16, tail,
+                                     tail ? tail_bytes : 0, sms, stream),
              f16 ? "fwd_tc_f16" : "fwd_tc_bf16");
     return DCN_OK;
   }

@@ -55,6 +55,9 @@ constexpr int EPI_WARPS = 4;
 constexpr int MMA_WARP = 4, TMA_WARP = 5, GATHER_WARP0 = 6;
 constexpr int THREADS = (GATHER_WARP0 + GATHER_WARPS) * 32;  // 704
 constexpr int A_STAGE = BM * 128;                            // 16 KB
+// Counters of a split last round: at most kTailCounts split tiles, in the
+// first kTailCountBytes of the forward's tail scratch.
+constexpr int kTailCounts = (int)(kTailCountBytes / sizeof(int));
 
 int tc_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
 int tmem_cols_for(int bn) {
@@ -99,6 +102,52 @@ __device__ __forceinline__ Tile tile_of(int t, int mtiles, int ntiles_n, int bn)
   T.o0 = (r % ntiles_n) * bn;
   T.gi = r / ntiles_n;
   return T;
+}
+
+// Schedule of a launch.  Tiles [0, whole) go round-robin over the grid, one
+// CTA each.  When the tile count leaves the last round short (tiles % grid SMs
+// busy, most of them idle), the remaining tiles are split by K instead: their K
+// steps, laid end to end, are cut into `ctas` equal ranges, one per CTA, so
+// every CTA runs about the same number of K steps.  A range covers the end of
+// one tile and the start of the next at most; each piece of a tile leaves its
+// partial sum in a slot (2 per CTA, [tn][BM] floats) and counts itself in
+// `count[tile - whole]` (zero before the launch); the CTA whose count comes
+// last adds the pieces in CTA order -- a fixed order, so the output does not
+// depend on which piece finishes last -- and writes the tile.  No CTA waits
+// for another.
+struct TailPlan {
+  int whole;               // tiles handed out whole
+  int ctas;                // CTAs sharing the split tiles (0: no split)
+  long long tail_steps;    // K steps of the split tiles
+  float* part;             // partial slots
+  int* count;              // pieces finished per split tile
+};
+struct Work {
+  int t;       // tile
+  int s0, s1;  // its K steps [s0, s1)
+  int slot;    // partial slot, -1 for a whole tile
+};
+// Runs f(work) for this CTA's work in order: its whole tiles, then its pieces
+// of split tiles.  The two loops inline f separately, so the whole-tile loop
+// keeps no split state live.
+template <class F>
+__device__ __forceinline__ void for_each_work(const TailPlan& tp, int steps, F&& f) {
+  for (int t = blockIdx.x; t < tp.whole; t += gridDim.x) f(Work{t, 0, steps, -1});
+  if ((int)blockIdx.x >= tp.ctas) return;
+  // tail_steps < 2^30 (host), so the positions fit in int
+  int x = (int)((long long)blockIdx.x * tp.tail_steps / tp.ctas);
+  const int xend = (int)((long long)(blockIdx.x + 1) * tp.tail_steps / tp.ctas);
+  for (int seg = 0; x < xend; ++seg) {
+    const int j = x / steps;
+    const int s0 = x - j * steps;
+    const int s1 = xend - x < steps - s0 ? s0 + (xend - x) : steps;
+    f(Work{tp.whole + j, s0, s1, 2 * (int)blockIdx.x + seg});
+    x += s1 - s0;
+  }
+}
+// CTA whose K range holds split step x: the largest c with c*T/ctas <= x.
+__device__ __forceinline__ int tail_cta_of(const TailPlan& tp, long long x) {
+  return (int)(((x + 1) * tp.ctas - 1) / tp.tail_steps);
 }
 
 // Scalar loads of the small operands (offsets, mask, bias) as fp32.
@@ -162,7 +211,7 @@ __device__ __forceinline__ unsigned short to_h16(float y) {
 template <int MODE, int NH>
 __global__ void __launch_bounds__(THREADS, 1)
 fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __restrict__ xt_,
-              int bn, int tcols, int mtiles, int ntiles_n, int ntiles,
+              int bn, int tcols, int mtiles, int ntiles_n, TailPlan tp,
               const void* __restrict__ off, const void* __restrict__ mask,
               const void* __restrict__ bias, void* __restrict__ out) {
   using Cfg = FwdCfg<MODE>;
@@ -182,6 +231,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* last_piece = reinterpret_cast<int*>(tmem_slot + 1);  // epilogue broadcast
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nchunk = g.Cg / KCH;
@@ -220,8 +270,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     const char* xq = static_cast<const char*>(xt_) + q4 * 32;
     constexpr int ESZ = H16 ? 2 : 4;  // element bytes
     int gs = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const Tile T = tile_of(t, mtiles, ntiles_n, tn);
+    for_each_work(tp, steps, [&](const Work& w) {
+      const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
       const int row = gw * 8 + sub;
       const long long q = T.q0 + row;
       const bool rvalid = q < g.NP;
@@ -231,12 +281,14 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       const uint32_t soff0 = tc::sw128_offset(row, 2 * q4), soff1 = tc::sw128_offset(row, 2 * q4 + 1);
       int coff[4];  // element offsets of the corners' channel vectors
       float cw[4];
-      // incremental (tap, channel chunk, deformable group) counters
-      int k = 0, ki = 0, kj = 0, c0 = 0;
+      // incremental (tap, channel chunk, deformable group) counters, from
+      // K step s0 = k * nchunk + c0 / KCH
+      int k = w.s0 / nchunk, c0 = (w.s0 - k * nchunk) * KCH;
+      int ki = k / g.kw, kj = k - ki * g.kw;
       const int gbase = T.gi * g.Cg;
-      int dgi = gbase / g.cpg, cpos = gbase - dgi * g.cpg;
+      int dgi = (gbase + c0) / g.cpg, cpos = gbase + c0 - dgi * g.cpg;
       bool replan = true;
-      for (int s = 0; s < steps; ++s, ++gs) {
+      for (int s = w.s0; s < w.s1; ++s, ++gs) {
         const int st = gs % STAGES;
         const int u = gs / STAGES;
         if (replan) {
@@ -332,15 +384,15 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           replan = true;
         }
       }
-    }
+    });
   } else if (warp == TMA_WARP) {
     // ------------------------------ weights (TMA) ------------------------------
     if (lane == 0) {
       int gs = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const Tile T = tile_of(t, mtiles, ntiles_n, tn);
+      for_each_work(tp, steps, [&](const Work& w) {
+        const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
         const int row = T.gi * g.Og + T.o0;
-        for (int s = 0; s < steps; ++s, ++gs) {
+        for (int s = w.s0; s < w.s1; ++s, ++gs) {
           const int st = gs % STAGES;
           const int u = gs / STAGES;
           if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
@@ -352,7 +404,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           if constexpr (SPLIT)  // low parts: rows outC .. 2*outC - 1 of the packed weight
             tc::tma_load_2d(sB + b_stage, &wmap, s * KCH, g.outC + row, &full[st]);
         }
-      }
+      });
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
@@ -362,7 +414,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
                              : FMT == kFmtBF16 ? tc::idesc_bf16(BM, bn)
                                                : tc::idesc_tf32(BM, bn);
       int gs = 0, it = 0;
-      for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      for_each_work(tp, steps, [&](const Work& w) {
         // one accumulator set per tile: two alternate (NH = 1), or one fills
         // tensor memory (NH = 2)
         const int acc = NH == 2 ? 0 : (it & 1);
@@ -370,8 +422,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         if (use >= 1) tc::mbar_wait(&acc_empty[acc], (use - 1) & 1, &g_tc_fwd_status);
         tc::tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(acc * tn);
-        for (int s = 0; s < steps; ++s, ++gs) {
+        for (int s = w.s0; s < w.s1; ++s, ++gs) {
           const int st = gs % STAGES;
+          const uint32_t accum = s != w.s0 ? 1u : 0u;  // the first K step overwrites
           tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_fwd_status);
           tc::tc_fence_after();
           const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB0s = sB0 + st * PARTS * b_stage;
@@ -382,35 +435,37 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           for (int j = 0; j < 4; ++j) {  // 32 bytes of K per UMMA: 8 tf32 or 16 bf16
             if constexpr (H16) {
               tc::umma_bf16(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
-                            (s | j) != 0 ? 1u : 0u);
+                            accum | (j != 0 ? 1u : 0u));
             } else if constexpr (SPLIT) {  // lo x hi + hi x lo + hi x hi
               tc::umma_tf32(d, tc::sdesc_sw128(sA + A_STAGE + j * 32),
-                            tc::sdesc_sw128(sB + j * 32), idesc, (s | j) != 0 ? 1u : 0u);
+                            tc::sdesc_sw128(sB + j * 32), idesc, accum | (j != 0 ? 1u : 0u));
               tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32),
                             tc::sdesc_sw128(sB + b_stage + j * 32), idesc, 1u);
               tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
                             1u);
             } else {
               tc::umma_tf32(d, tc::sdesc_sw128(sA + j * 32), tc::sdesc_sw128(sB + j * 32), idesc,
-                            (s | j) != 0 ? 1u : 0u);
+                            accum | (j != 0 ? 1u : 0u));
             }
           }
           }
           tc::umma_commit(&empty[st]);
         }
         tc::umma_commit(&acc_full[acc]);
-      }
+        ++it;
+      });
     }
     __syncwarp();
   } else {
     // ------------------------------ epilogue ------------------------------
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
-      const Tile T = tile_of(t, mtiles, ntiles_n, tn);
-      const int acc = NH == 2 ? 0 : (it & 1);
-      tc::mbar_wait(&acc_full[acc], (NH == 2 ? it : (it >> 1)) & 1, &g_tc_fwd_status);
+    const int r = warp * 32 + lane;
+    for_each_work(tp, steps, [&](const Work& w) {
+      const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
+      const int i = it++;
+      const int acc = NH == 2 ? 0 : (i & 1);
+      tc::mbar_wait(&acc_full[acc], (NH == 2 ? i : (i >> 1)) & 1, &g_tc_fwd_status);
       tc::tc_fence_after();
-      const int r = warp * 32 + lane;
       const long long q = T.q0 + r;
       const bool valid = q < g.NP;
       const int n = valid ? (int)(q / g.P) : 0;
@@ -418,26 +473,73 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       const long long obase = ((long long)n * g.outC + (long long)T.gi * g.Og + T.o0) * g.P + p;
       const int bbase = T.gi * g.Og + T.o0;
       const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * tn);
+      auto store = [&](int o, float v) {  // + bias, into the output
+        const float y = v + (g.use_bias ? ld_io<FMT>(bias, bbase + o) : 0.f);
+        const long long at = obase + (long long)o * g.P;
+        if constexpr (H16)
+          static_cast<unsigned short*>(out)[at] = to_h16<FMT>(y);
+        else
+          static_cast<float*>(out)[at] = y;
+      };
+      if (w.slot < 0) {  // whole tile
+        for (int cb = 0; cb < tn; cb += 8) {
+          float vv[8];
+          tc::tmem_ld8(ta + (uint32_t)cb, vv);
+          tc::tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) store(cb + j, vv[j]);
+          }
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+        return;
+      }
+      // a piece of a split tile: its partial into the slot (out channel
+      // major, so a warp's 32 rows are one 128-byte line) ...
+      float* mine = tp.part + (size_t)w.slot * tn * BM;
       for (int cb = 0; cb < tn; cb += 8) {
         float vv[8];
         tc::tmem_ld8(ta + (uint32_t)cb, vv);
         tc::tmem_ld_wait();
-        if (valid) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float y = vv[j] + (g.use_bias ? ld_io<FMT>(bias, bbase + cb + j) : 0.f);
-            const long long at = obase + (long long)(cb + j) * g.P;
-            if constexpr (H16)
-              static_cast<unsigned short*>(out)[at] = to_h16<FMT>(y);
-            else
-              static_cast<float*>(out)[at] = y;
-          }
-        }
+        for (int j = 0; j < 8; ++j) mine[(cb + j) * BM + r] = vv[j];
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
-    }
+      // ... made visible, then counted; the last piece to count sums them all
+      const int j = w.t - tp.whole;
+      const long long x0 = (long long)j * steps;
+      const int cfirst = tail_cta_of(tp, x0), clast = tail_cta_of(tp, x0 + steps - 1);
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      if (r == 0) *last_piece = atomicAdd(&tp.count[j], 1) == clast - cfirst;
+      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      if (*last_piece) {
+        __threadfence();
+        // CTAs after the first start their range inside this tile (their
+        // slot 0); the first one's range starts here or in an earlier tile
+        const bool first_starts_here =
+            (long long)cfirst * tp.tail_steps / tp.ctas == x0;
+        const float* p0 = tp.part + (size_t)(2 * cfirst + (first_starts_here ? 0 : 1)) * tn * BM;
+        if (valid) {
+          for (int cb = 0; cb < tn; cb += 8) {
+            float v[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) v[jj] = __ldcg(p0 + (size_t)(cb + jj) * BM + r);
+            for (int c = cfirst + 1; c <= clast; ++c) {
+              const float* pc = tp.part + (size_t)(2 * c) * tn * BM;
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) v[jj] += __ldcg(pc + (size_t)(cb + jj) * BM + r);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) store(cb + jj, v[jj]);
+          }
+        }
+      }
+    });
   }
 
   tc::tc_fence_before();
@@ -454,7 +556,9 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
 // tap-major with coalesced stores.
 __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __restrict__ w,
                                                              float* __restrict__ wt, Geom g,
-                                                             int split) {
+                                                             int split, int* __restrict__ zero) {
+  if (zero != nullptr && blockIdx.x == 0)  // the forward's split-tile counters
+    for (int i = threadIdx.x; i < kTailCounts; i += blockDim.x) zero[i] = 0;
   const int Kpad = g.kk * g.Cg;
   const long long oc = blockIdx.x;
   const float* src = w + oc * Kpad;
@@ -472,7 +576,10 @@ __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __rest
 // 16-bit packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = W[g*Og+o][c][k]
 // (bf16 or fp16 words moved as they are, no rounding).
 __global__ void __launch_bounds__(256) tc_pack_weight_bf16_kernel(
-    const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g) {
+    const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g,
+    int* __restrict__ zero) {
+  if (zero != nullptr && blockIdx.x == 0)  // the forward's split-tile counters
+    for (int i = threadIdx.x; i < kTailCounts; i += blockDim.x) zero[i] = 0;
   const int Kpad = g.kk * g.Cg;
   const long long oc = blockIdx.x;
   const unsigned short* src = w + oc * Kpad;
@@ -483,14 +590,57 @@ __global__ void __launch_bounds__(256) tc_pack_weight_bf16_kernel(
   }
 }
 
+// 512 out channels a tile when the group has a multiple of 512 (not in
+// 3xTF32, whose two operand parts would not fit two stages)
+bool wide_tiles(int mode, const Geom& g) { return mode != kSplit && g.Og % 512 == 0; }
+int tile_cols(int mode, const Geom& g) { return (wide_tiles(mode, g) ? 2 : 1) * tc_bn(g); }
+long long tile_count(int mode, const Geom& g) {
+  return (g.NP + BM - 1) / BM * (g.Og / tile_cols(mode, g)) * g.G;
+}
+int kstep_count(int mode, const Geom& g) {
+  return g.kk * g.Cg / (mode == kBF16 || mode == kF16 ? 64 : 32);
+}
+
+// The schedule (TailPlan) of `ntiles` tiles of `steps` K steps on `num_sms`
+// SMs: the last round is split when at least half the SMs would sit idle in
+// it, the tiles have enough K steps to share (8 or more) and the cut leaves
+// every CTA a quarter of a tile or more.  (The gather is bound by L2 -> SM
+// throughput more than by each SM's latency: a last round on part of the SMs
+// runs faster per tile than a full one, and the pieces' partial sums cost L2
+// traffic, so a split pays only when most of the SMs would idle -- measured:
+// 48 of 148 busy, forward -6%; 90 of 148, +3%; 108 of 148, +8%.)
+struct TailShape {
+  int grid = 0, whole = 0, ctas = 0;
+  long long tail_steps = 0;
+  size_t bytes = 0;  // scratch: counters + 2 slots a CTA
+};
+TailShape plan_tail(long long ntiles, int steps, int tn, int num_sms) {
+  TailShape p;
+  p.grid = (int)(ntiles < num_sms ? ntiles : num_sms);
+  p.whole = (int)ntiles;
+  if (steps < 8 || num_sms <= 0 || ntiles <= 0) return p;
+  const long long whole = ntiles / num_sms * num_sms, tail = ntiles - whole;
+  if (tail == 0 || tail > num_sms / 2 || tail > kTailCounts) return p;
+  const long long T = tail * steps;
+  if (T >= (1LL << 30)) return p;
+  const long long min_seg = steps / 4 > 2 ? steps / 4 : 2;
+  long long ctas = T / min_seg < num_sms ? T / min_seg : num_sms;
+  if (ctas <= tail) return p;                  // no more CTAs than tiles: nothing gained
+  if ((T + ctas - 1) / ctas > steps) return p;  // ranges of at most one tile
+  p.whole = (int)whole;
+  p.ctas = (int)ctas;
+  p.tail_steps = T;
+  p.grid = whole > 0 ? num_sms : (int)ctas;
+  p.bytes = kTailCountBytes + (size_t)2 * ctas * tn * BM * sizeof(float);
+  return p;
+}
+
 cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUtensorMap& wmap,
                             const void* off, const void* mask, const void* bias, void* out,
-                            int num_sms, cudaStream_t stream) {
+                            void* tail, size_t tail_bytes, int num_sms, cudaStream_t stream) {
   const int bn = tc_bn(g);
-  // 512 out channels a tile when the group has a multiple of 512 (not in
-  // 3xTF32, whose two operand parts would not fit two stages)
-  const bool wide = mode != kSplit && g.Og % 512 == 0;
-  const int tn = wide ? 2 * bn : bn;
+  const bool wide = wide_tiles(mode, g);
+  const int tn = tile_cols(mode, g);
   const size_t smem = wide ? 2 * ((size_t)A_STAGE + (size_t)tn * 128) + 128 + 1024
                            : smem_bytes(bn, mode == kSplit);
   auto kern = mode == kSplit ? fwd_tc_kernel<kSplit, 1>
@@ -501,11 +651,20 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
   if (e != cudaSuccess) return e;
   const int mtiles = (int)((g.NP + BM - 1) / BM);
   const int ntiles_n = g.Og / tn;
-  const long long ntiles = (long long)mtiles * ntiles_n * g.G;
+  const long long ntiles = tile_count(mode, g);
   if (ntiles > (1LL << 30)) return cudaErrorInvalidValue;
-  const int grid = (int)(ntiles < num_sms ? ntiles : num_sms);
-  kern<<<grid, THREADS, smem, stream>>>(g, wmap, xt, bn, wide ? 512 : tmem_cols_for(bn), mtiles,
-                                         ntiles_n, (int)ntiles, off, mask, bias, out);
+  TailShape ts = plan_tail(ntiles, kstep_count(mode, g), tn, num_sms);
+  if (ts.ctas > 0 && (tail == nullptr || tail_bytes < ts.bytes))  // no scratch: whole tiles
+    ts = plan_tail(ntiles, 0, tn, num_sms);
+  TailPlan tp;
+  tp.whole = ts.whole;
+  tp.ctas = ts.ctas;
+  tp.tail_steps = ts.tail_steps;
+  tp.count = static_cast<int*>(tail);
+  tp.part = ts.ctas > 0 ? reinterpret_cast<float*>(static_cast<char*>(tail) + kTailCountBytes)
+                        : nullptr;
+  kern<<<ts.grid, THREADS, smem, stream>>>(g, wmap, xt, bn, wide ? 512 : tmem_cols_for(bn),
+                                            mtiles, ntiles_n, tp, off, mask, bias, out);
   return cudaGetLastError();
 }
 
@@ -521,16 +680,23 @@ size_t tc_fwd_weight_bytes(const Geom& g, bool split) {
   return (size_t)(split ? 2 : 1) * g.outC * g.kk * g.Cg * sizeof(float);
 }
 
+size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms) {
+  if (g.NP <= 0 || g.G <= 0) return 0;
+  const int mode = split ? kSplit : (h16 ? kBF16 : kTF32);
+  return plan_tail(tile_count(mode, g), kstep_count(mode, g), tile_cols(mode, g), num_sms).bytes;
+}
+
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
-                                  cudaStream_t stream) {
+                                  void* tail, cudaStream_t stream) {
   if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
-  tc_pack_weight_kernel<<<g.outC, 256, 0, stream>>>(w, wt, g, split ? 1 : 0);
+  tc_pack_weight_kernel<<<g.outC, 256, 0, stream>>>(w, wt, g, split ? 1 : 0,
+                                                    static_cast<int*>(tail));
   return cudaGetLastError();
 }
 
 cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt, const float* off,
                           const float* mask, const float* bias, float* out, bool split,
-                          int num_sms, cudaStream_t stream) {
+                          void* tail, size_t tail_bytes, int num_sms, cudaStream_t stream) {
   if (!tc_fwd_supported(g)) return cudaErrorInvalidValue;
   const int Kpad = g.kk * g.Cg;
   CUtensorMap wmap;
@@ -538,7 +704,8 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt, const
                                    (uint64_t)g.outC * (split ? 2 : 1), (uint64_t)Kpad,
                                    (uint32_t)tc_bn(g));
   if (e != cudaSuccess) return e;
-  return launch_fwd_mode(split ? kSplit : kTF32, g, xt, wmap, off, mask, bias, out, num_sms,
+  return launch_fwd_mode(split ? kSplit : kTF32, g, xt, wmap, off, mask, bias, out, tail,
+                         tail_bytes, num_sms,
                          stream);
 }
 
@@ -550,24 +717,27 @@ bool tc_fwd_bf16_supported(const Geom& g) {
 
 size_t tc_fwd_weight_bf16_bytes(const Geom& g) { return (size_t)g.outC * g.kk * g.Cg * 2; }
 
-cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
+cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g, void* tail,
                                        cudaStream_t stream) {
   if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
   tc_pack_weight_bf16_kernel<<<g.outC, 256, 0, stream>>>(
-      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wt), g);
+      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wt), g,
+      static_cast<int*>(tail));
   return cudaGetLastError();
 }
 
 cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
                                const void* mask, const void* bias, void* out, bool f16,
-                               int num_sms, cudaStream_t stream) {
+                               void* tail, size_t tail_bytes, int num_sms,
+                               cudaStream_t stream) {
   if (!tc_fwd_bf16_supported(g)) return cudaErrorInvalidValue;
   const int Kpad = g.kk * g.Cg;
   CUtensorMap wmap;
   cudaError_t e = make_tmap_2d_bf16(&wmap, wt, (uint64_t)Kpad, (uint64_t)g.outC,
                                     (uint64_t)Kpad, (uint32_t)tc_bn(g), f16);
   if (e != cudaSuccess) return e;
-  return launch_fwd_mode(f16 ? kF16 : kBF16, g, xt, wmap, off, mask, bias, out, num_sms, stream);
+  return launch_fwd_mode(f16 ? kF16 : kBF16, g, xt, wmap, off, mask, bias, out, tail, tail_bytes,
+                         num_sms, stream);
 }
 
 }  // namespace dcn

@@ -23,13 +23,16 @@
 #include "dcn_b200.h"
 
 namespace dcn {
-void set_last_error(int code, const char* msg);  // dcn_capi.cu
+void set_last_error(int code, const char* msg);                    // dcn_capi.cu
+size_t forward_min_workspace(const dcn_shape* s, uint32_t flags);  // dcn_capi.cu
 }
 
 namespace {
 
-// Upper bound of the scratch one call may use (dcn_forward_workspace_size of
-// the call's shape must not exceed it): 16 MiB, e.g. a 2x64x128x128 input.
+// Upper bound of the scratch one call may use (the least workspace
+// dcn_forward accepts for the call's shape must not exceed it): 16 MiB, e.g. a
+// 2x64x128x128 input.  Whatever is left over serves as the optional scratch of
+// the tensor-core forward's split last round where it fits.
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -82,7 +85,7 @@ extern "C" DCN_API int dcn_forward_noalloc(const dcn_shape* shape, const float* 
   int64_t ho = 0, wo = 0;
   int rc = dcn_output_size(shape, &ho, &wo);  // validates the geometry, sets the message
   if (rc != DCN_OK) return rc;
-  const size_t need = dcn_forward_workspace_size(shape, flags);
+  const size_t need = dcn::forward_min_workspace(shape, flags);
   if (need > kNoAllocScratchBytes) {
     char msg[256];
     std::snprintf(msg, sizeof(msg),

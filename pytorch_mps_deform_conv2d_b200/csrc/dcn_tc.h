@@ -13,15 +13,25 @@ bool tc_fwd_supported(const Geom& g);
 // Bytes of the packed weight operand of the tensor-core forward (`split`:
 // high and low TF32 parts, for 3xTF32).
 size_t tc_fwd_weight_bytes(const Geom& g, bool split);
-// weight (outC, Cg, kh, kw) -> packed tensor-core B operand.
+// Scratch ("tail") with which the tensor-core forward splits a short last
+// round of tiles over all SMs (0 when this shape has none on `num_sms` SMs;
+// `h16`: the 16-bit forward).  Its first kTailCountBytes must be zero when
+// the forward starts: the weight pack kernels below clear them when given the
+// same pointer.  Without the scratch the forward runs whole tiles only.
+constexpr size_t kTailCountBytes = 4096;
+size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms);
+// weight (outC, Cg, kh, kw) -> packed tensor-core B operand; `tail` (NULL or
+// the forward's tail scratch) has its counters cleared on the way.
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
-                                  cudaStream_t stream);
+                                  void* tail, cudaStream_t stream);
 // Forward on tcgen05: implicit GEMM whose A tiles are gathered (bilinear
 // deformable sampling) by producer warps straight into swizzled shared memory.
-// `split`: 3xTF32 (fp32-level accuracy).
+// `split`: 3xTF32 (fp32-level accuracy).  `tail` / `tail_bytes`: the scratch
+// of tc_fwd_tail_bytes (NULL: whole tiles only).
 cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
                           const float* off, const float* mask, const float* bias,
-                          float* out, bool split, int num_sms, cudaStream_t stream);
+                          float* out, bool split, void* tail, size_t tail_bytes, int num_sms,
+                          cudaStream_t stream);
 
 // 16-bit forward (all tensors bf16, or all fp16 with `f16`; kind::f16 UMMAs,
 // fp32 accumulation): 64 channels of a tap per K step, so channels per group
@@ -30,11 +40,12 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
 // (tc_fwd_weight_bf16_bytes).
 bool tc_fwd_bf16_supported(const Geom& g);
 size_t tc_fwd_weight_bf16_bytes(const Geom& g);
-cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
+cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g, void* tail,
                                        cudaStream_t stream);
 cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
                                const void* mask, const void* bias, void* out, bool f16,
-                               int num_sms, cudaStream_t stream);
+                               void* tail, size_t tail_bytes, int num_sms,
+                               cudaStream_t stream);
 
 // Whether the tensor-core backward covers this geometry (grad-column kernel
 // and the column-buffer weight gradient), and whether the gather-based

@@ -69,7 +69,7 @@ def test_tf32_repeatable(cuda_device):
     case = make_case(inC=64, outC=64, H=16, W=16, offset_scale=2.0)
     a, _ = run_ours(case, flags=MATH_TF32, backward=False)
     b, _ = run_ours(case, flags=MATH_TF32, backward=False)
-    assert np.array_equal(a, b)  # the forward has no atomics: bitwise repeatable
+    assert np.array_equal(a, b)  # split tiles are summed in a fixed order: bitwise repeatable
 
 
 GRAD_TOL = 1e-3  # norm-wise relative error of every gradient in TF32 mode
