@@ -1,6 +1,6 @@
 /*
  * dcn_oracle.c -- CPU restatement of the reference deformable-convolution
- * algorithm.  TEST INFRASTRUCTURE ONLY: this file is the checker that the
+ * algorithm.  TEST INFRASTRUCTURE ONLY: this file is the oracle that the
  * CUDA kernels are compared against.  It is never linked into, loaded by or
  * called from the product library; only tests/, the smoke entry and the
  * bench's CPU-baseline leg load it.

@@ -2,8 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY.  The oracle restates the reference algorithm of
 ilirium/pytorch_mps_deform_conv2d on the CPU (``dcn_oracle.c`` names the
-reference file:line of every function).  It is the checker: ``tests/``, the
-smoke entry and the bench's CPU-baseline leg may call it; the product
+reference file:line of every function).  Results are checked against it:
+``tests/``, the smoke entry and the bench's CPU-baseline leg may call it; the product
 package never imports it.
 
 All arrays are float32 numpy arrays in the reference's layouts.  ``mask`` and
