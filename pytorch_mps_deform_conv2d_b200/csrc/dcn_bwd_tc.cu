@@ -916,7 +916,11 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
 // further in 3xTF32):  gW'[c, o] += sum_q col[k][q][c] go[q, o]  (.mm:842-880)
 // as a dense tcgen05 GEMM with both operands brought in by TMA.  Tiles as in
 // bwd_weight_tc: (tap k, 128 channels, bn out channels, group, pixel range).
-//   warps 0-3  epilogue: accumulator -> fp32 reductions into grad_weight
+//   warps 0-3  epilogue: accumulator -> fp32 reductions into grad_weight, or
+//              into a tap-major copy gwt[o][k][c] that the caller transposes
+//              into place (a warp's 32 rows of one tap and out channel are
+//              then one 128-byte line; in grad_weight's own [o][c][k] order
+//              they are kh*kw floats apart)
 //   warp  4    MMA issue
 //   warp  5    TMA producer: per 32-pixel K step, four 32-channel blocks of
 //              col (MN-major operand, 128-byte swizzle with 32-byte atoms)
@@ -951,8 +955,8 @@ template <bool SPLIT>
 __global__ void __launch_bounds__(WC_THREADS, 1)
 bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
                       const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
-                      float* __restrict__ gw, int nslots, int ntn, int splits, int per,
-                      int ntiles) {
+                      float* __restrict__ gw, int sk, int sc, int nslots, int ntn, int splits,
+                      int per, int ntiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
@@ -1081,8 +1085,10 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
       const int row = T.slot * 128 + warp * 32 + lane;  // (tap, channel) row of the group
       const int k = row / g.Cg, c = row - k * g.Cg;
       const bool live = k < g.kk;
-      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + k;
+      // element (o, k, c) at o * Cg*kk + k * sk + c * sc
       const long long ostride = (long long)g.Cg * g.kk;
+      float* dst = gw + (long long)(T.gi * g.Og + T.o0) * ostride + (long long)k * sk +
+                   (long long)c * sc;
       const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
       for (int cb = 0; cb < bn; cb += 8) {
         float vv[8];
@@ -1295,6 +1301,30 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   return cudaGetLastError();
 }
 
+// gwt[o][k][c] -> gw[o][c][k]: one thread per (o, c); a warp reads 32
+// consecutive channels of each tap (coalesced) and writes 32 x kk consecutive
+// floats.
+__global__ void __launch_bounds__(256) weight_from_tap_major_kernel(
+    const float* __restrict__ gwt, float* __restrict__ gw, int Cg, int kk, long long total) {
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const long long o = i / Cg;
+    const int c = (int)(i - o * Cg);
+    const float* src = gwt + o * Cg * kk + c;
+    float* dst = gw + i * kk;
+    for (int k = 0; k < kk; ++k) dst[k] = __ldg(src + (long long)k * Cg);
+  }
+}
+
+cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
+                                         cudaStream_t stream) {
+  const long long total = (long long)g.outC * g.Cg;
+  if (total == 0 || g.kk == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  weight_from_tap_major_kernel<<<(int)blocks, 256, 0, stream>>>(gwt, gw, g.Cg, g.kk, total);
+  return cudaGetLastError();
+}
+
 bool tc_wcol_supported(const Geom& g, bool split) {
   return tc_bwd_supported(g) && (long long)g.kk * g.NP * (split ? 2 : 1) < (1LL << 31);
 }
@@ -1304,7 +1334,7 @@ size_t tc_col_bytes(const Geom& g, bool split) {
 }
 
 cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* go_r, float* gw,
-                                  bool split, int num_sms, cudaStream_t stream) {
+                                  bool tap_major, bool split, int num_sms, cudaStream_t stream) {
   if (!tc_wcol_supported(g, split)) return cudaErrorInvalidValue;
   const int bn = weight_bn(g);
   const int Ppad = (g.P + 3) & ~3;
@@ -1324,6 +1354,7 @@ cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* 
   if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(w.ntiles < num_sms ? w.ntiles : num_sms);
   kern<<<grid, WC_THREADS, smem, stream>>>(g, colmap, gomap, bn, pow2_cols(2 * bn), gw,
+                                            tap_major ? g.Cg : 1, tap_major ? 1 : g.kk,
                                             weight_slots(g), w.ntn, w.splits, w.per,
                                             (int)w.ntiles);
   return cudaGetLastError();

@@ -321,7 +321,8 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     b += align_up(parts * g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));   // go_r
     b += align_up(parts * g.outC * g.Cg * g.kk * sizeof(float));               // packed weight
     if (use_col_path(g, flags))
-      b += align_up(dcn::tc_col_bytes(g, split_math(flags)));                  // column buffer
+      b += align_up(dcn::tc_col_bytes(g, split_math(flags))) +                 // column buffer
+           align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));             // tap-major grad_weight
     else
       b += align_up(dcn::tc_plan_bytes(g));                                    // sampling plans
   } else {
@@ -676,9 +677,11 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   dcn::ZeroList z{};
   z.add(grad_offset, (long long)(off_bytes / sizeof(float)));
   z.add(grad_mask, (long long)(msk_bytes / sizeof(float)));
-  z.add(grad_weight, (long long)(w_bytes / sizeof(float)));
-  if (no_pixels) z.add(grad_bias, g.outC);
   const bool zero_on_side = tc_bwd && !skip;
+  // (the tensor-core path adds grad_weight, or its tap-major workspace copy,
+  // below)
+  if (!zero_on_side) z.add(grad_weight, (long long)(w_bytes / sizeof(float)));
+  if (no_pixels) z.add(grad_bias, g.outC);
   if (!zero_on_side) DCN_CUDA(dcn::launch_zero(z, stream), "zero");
   if (grad_bias != nullptr && !bias_in_prep && !no_pixels)
     DCN_CUDA(dcn::launch_grad_bias(grad_output, grad_bias, g, stream), "grad_bias");
@@ -711,6 +714,10 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     const bool colp = use_col_path(g, flags);
     float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
+    // the column-buffer weight gradient sums into a tap-major copy
+    // (coalesced reductions), then puts it in grad_weight's layout
+    float* gwt = colp ? ws.take(w_bytes / sizeof(float)) : nullptr;
+    z.add(gwt ? gwt : grad_weight, (long long)(w_bytes / sizeof(float)));
     // grad_out prep (side 0, after zeroing grad_bias, which it sums into) and
     // the weight pack + the zeroing of the other accumulators (side 1) run
     // beside the input transpose
@@ -736,9 +743,12 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
              "bwd_data_tc");
     if (nhwc) {  // grad_input is complete: nothing to transpose
       if (colp) {
-        DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, grad_weight, split, num_sms_current(),
-                                            stream),
+        DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt ? gwt : grad_weight, gwt != nullptr,
+                                            split, num_sms_current(), stream),
                  "bwd_weight_col");
+        if (gwt)
+          DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+                   "grad_weight_layout");
       } else {
         void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
         DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
@@ -753,9 +763,12 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_CUDA_ON(fk.side(0), dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
                 "nhwc_to_nchw");
     if (colp) {
-      DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, grad_weight, split, num_sms_current(),
-                                          stream),
+      DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt ? gwt : grad_weight, gwt != nullptr,
+                                          split, num_sms_current(), stream),
                "bwd_weight_col");
+      if (gwt)
+        DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+                 "grad_weight_layout");
       DCN_ORDER(fk.join(0), "join");
     } else {
       void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));

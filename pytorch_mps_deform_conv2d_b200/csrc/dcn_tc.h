@@ -68,11 +68,17 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, const float* wbt,
                                const float* xt, const float* off, const float* mask, float* gxt,
                                float* goff, float* gmask, float* col, cudaStream_t stream);
-// Weight gradient as a dense TMA-fed GEMM over the column buffer.
+// Weight gradient as a dense TMA-fed GEMM over the column buffer, summed into
+// `gw` (pre-zeroed): grad_weight itself ([outC][Cg][kh*kw]), or with
+// `tap_major` a [outC][kh*kw][Cg] copy, whose reductions coalesce, for the
+// caller to transpose into place.
 bool tc_wcol_supported(const Geom& g, bool split);
 size_t tc_col_bytes(const Geom& g, bool split);
 cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* go_r, float* gw,
-                                  bool split, int num_sms, cudaStream_t stream);
+                                  bool tap_major, bool split, int num_sms, cudaStream_t stream);
+// [outC][kh*kw][Cg] -> grad_weight's [outC][Cg][kh*kw].
+cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
+                                         cudaStream_t stream);
 // Sampling plans of every (n, deformable group, tap, pixel): 32 bytes each
 // (corner element offsets into the NHWC copy, weights times mask).
 inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }
