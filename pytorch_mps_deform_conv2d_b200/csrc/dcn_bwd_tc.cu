@@ -692,8 +692,8 @@ template <bool SPLIT>
 __global__ void __launch_bounds__(W2_THREADS, 1)
 bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, int tcols,
                      const float* __restrict__ xt, const int4* __restrict__ plans,
-                     float* __restrict__ gw, int mtiles, int ntn, int splits, int per,
-                     int ntiles) {
+                     float* __restrict__ gw, int sk, int sc, int mtiles, int ntn, int splits,
+                     int per, int ntiles) {
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
@@ -885,8 +885,11 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
       tc::tc_fence_after();
       const int c = T.cm0 + warp * 32 + lane;  // channel within the group
-      float* dst = gw + ((long long)(T.gi * g.Og + T.o0) * g.Cg + c) * g.kk + T.k;
+      // element (o, k, c) at o * Cg*kk + k * sk + c * sc (grad_weight, or its
+      // tap-major copy)
       const long long ostride = (long long)g.Cg * g.kk;
+      float* dst = gw + (long long)(T.gi * g.Og + T.o0) * ostride + (long long)T.k * sk +
+                   (long long)c * sc;
       const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * bn);
       for (int cb = 0; cb < bn; cb += 8) {
         float vv[8];
@@ -1277,8 +1280,8 @@ cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, 
 }
 
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const void* plans, float* gw, bool split, int num_sms,
-                                 cudaStream_t stream) {
+                                 const void* plans, float* gw, bool tap_major, bool split,
+                                 int num_sms, cudaStream_t stream) {
   if (!tc_wgather_supported(g)) return cudaErrorInvalidValue;
   const int bn = weight_bn(g);
   const int Ppad = (g.P + 3) & ~3;
@@ -1296,8 +1299,9 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
   if (w.ntiles > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(w.ntiles < num_sms ? w.ntiles : num_sms);
   kern<<<grid, W2_THREADS, smem, stream>>>(g, gomap, bn, pow2_cols(2 * bn), xt,
-                                            static_cast<const int4*>(plans), gw, w.mtiles, w.ntn,
-                                            w.splits, w.per, (int)w.ntiles);
+                                            static_cast<const int4*>(plans), gw,
+                                            tap_major ? g.Cg : 1, tap_major ? 1 : g.kk, w.mtiles,
+                                            w.ntn, w.splits, w.per, (int)w.ntiles);
   return cudaGetLastError();
 }
 

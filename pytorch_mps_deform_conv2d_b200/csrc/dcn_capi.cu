@@ -320,9 +320,9 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     const size_t parts = split_math(flags) ? 2 : 1;                   // high (+ low) TF32 parts
     b += align_up(parts * g.N * g.outC * ((g.P + 3) & ~3) * sizeof(float));   // go_r
     b += align_up(parts * g.outC * g.Cg * g.kk * sizeof(float));               // packed weight
+    b += align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));               // tap-major grad_weight
     if (use_col_path(g, flags))
-      b += align_up(dcn::tc_col_bytes(g, split_math(flags))) +                 // column buffer
-           align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));             // tap-major grad_weight
+      b += align_up(dcn::tc_col_bytes(g, split_math(flags)));                  // column buffer
     else
       b += align_up(dcn::tc_plan_bytes(g));                                    // sampling plans
   } else {
@@ -714,10 +714,10 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     float* wbt = ws.take(parts * g.outC * g.Cg * g.kk);
     const bool colp = use_col_path(g, flags);
     float* col = colp ? ws.take(dcn::tc_col_bytes(g, split) / sizeof(float)) : nullptr;
-    // the column-buffer weight gradient sums into a tap-major copy
-    // (coalesced reductions), then puts it in grad_weight's layout
-    float* gwt = colp ? ws.take(w_bytes / sizeof(float)) : nullptr;
-    z.add(gwt ? gwt : grad_weight, (long long)(w_bytes / sizeof(float)));
+    // the weight gradient sums into a tap-major copy (coalesced reductions),
+    // then puts it in grad_weight's layout
+    float* gwt = ws.take(w_bytes / sizeof(float));
+    z.add(gwt, (long long)(w_bytes / sizeof(float)));
     // grad_out prep (side 0, after zeroing grad_bias, which it sums into) and
     // the weight pack + the zeroing of the other accumulators (side 1) run
     // beside the input transpose
@@ -743,19 +743,18 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
              "bwd_data_tc");
     if (nhwc) {  // grad_input is complete: nothing to transpose
       if (colp) {
-        DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt ? gwt : grad_weight, gwt != nullptr,
-                                            split, num_sms_current(), stream),
+        DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt, true, split, num_sms_current(),
+                                            stream),
                  "bwd_weight_col");
-        if (gwt)
-          DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
-                   "grad_weight_layout");
       } else {
         void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
         DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
-        DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split,
+        DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, gwt, true, split,
                                            num_sms_current(), stream),
                  "bwd_weight_tc");
       }
+      DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+               "grad_weight_layout");
       return DCN_OK;
     }
     // grad_input back to NCHW (side 0) beside the weight gradient
@@ -763,21 +762,19 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_CUDA_ON(fk.side(0), dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
                 "nhwc_to_nchw");
     if (colp) {
-      DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt ? gwt : grad_weight, gwt != nullptr,
-                                          split, num_sms_current(), stream),
+      DCN_CUDA(dcn::launch_bwd_weight_col(g, col, go_r, gwt, true, split, num_sms_current(),
+                                          stream),
                "bwd_weight_col");
-      if (gwt)
-        DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
-                 "grad_weight_layout");
-      DCN_ORDER(fk.join(0), "join");
     } else {
       void* plans = ws.take(dcn::tc_plan_bytes(g) / sizeof(float));
       DCN_CUDA(dcn::launch_tc_plans(g, offset, mask, plans, stream), "tc_plans");
-      DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, grad_weight, split,
+      DCN_CUDA(dcn::launch_bwd_weight_tc(g, go_r, xt, plans, gwt, true, split,
                                          num_sms_current(), stream),
                "bwd_weight_tc");
-      DCN_ORDER(fk.join(0), "join");
     }
+    DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+             "grad_weight_layout");
+    DCN_ORDER(fk.join(0), "join");
     return DCN_OK;
   }
   DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");

@@ -84,9 +84,10 @@ cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom
 inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }
 cudaError_t launch_tc_plans(const Geom& g, const float* off, const float* mask, void* plans,
                             cudaStream_t stream);
-// grad_weight (pre-zeroed) += col^T go on the tensor core, split over pixels.
+// grad_weight (pre-zeroed) += col^T go on the tensor core, split over pixels;
+// `tap_major`: into a [outC][kh*kw][Cg] copy as launch_bwd_weight_col.
 cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* xt,
-                                 const void* plans, float* gw, bool split, int num_sms,
-                                 cudaStream_t stream);
+                                 const void* plans, float* gw, bool tap_major, bool split,
+                                 int num_sms, cudaStream_t stream);
 
 }  // namespace dcn
