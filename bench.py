@@ -19,11 +19,14 @@ the timed events.
 
 The printed JSON line carries the roofline of the dominant kernel (timed live
 with the library's CUDA-event profiler), the CPU baseline (the reference
-package's own CPU route -- torchvision's kernel -- on a bounded sample of the
-same workload) and an end-to-end number through the public module API with
-host<->device copies inside the timed region.
+package's own CPU route -- torchvision's kernel -- on the whole workload: two
+timed steps, all host threads), end-to-end numbers through the public module
+API with host<->device copies inside the timed region (parameter gradients
+read back, and the output with all five gradients read back), and the step
+time of the other math modes.
 
-`--impl reference` times the reference's CPU implementation alone (rank 0).
+`--impl reference` times the reference's CPU implementation alone on the
+whole workload (rank 0): W untimed steps, then K timed ones.
 """
 from __future__ import annotations
 
@@ -94,6 +97,15 @@ def make_inputs(wl, seed=0, n=None, c_in=None):
         assert g == 1
         x, w = x[:, :c_in].contiguous(), w[:, :c_in].contiguous()
     return x, w, b, off, m, go
+
+
+def bench_config(wl, args=None):
+    """The workload the metric is quoted on, the same for both arms: one
+    iteration is forward + backward of this batch (how a run spreads its
+    iterations over devices is under the line's "run" key)."""
+    return {"workload": wl["desc"], "global_batch": wl["N"],
+            "io_dtype": getattr(args, "dtype", "fp32"),
+            "input_layout": getattr(args, "layout", "nchw")}
 
 
 def algorithmic_work(wl):
@@ -244,9 +256,9 @@ def reference_cpu_op():
 
 
 def cpu_sample_plan(wl):
-    """A sample of the workload: one image and a slice of the input channels.
-    Every term of the op's cost is linear in images x input channels, so the
-    per-iteration time is the sample time times `scale`."""
+    """A cut of the workload: one image and a slice of the input channels,
+    1/scale of its work (every cost term of the op is linear in images x
+    input channels).  Used only for the `sampled` cross-check figure."""
     n = 1
     c_in = wl["C"]
     if wl["groups"] == 1:
@@ -256,11 +268,15 @@ def cpu_sample_plan(wl):
     return n, c_in, scale
 
 
-def cpu_reference_step_fn(wl, threads):
+def cpu_reference_step_fn(wl, threads, sampled=False):
+    """One fwd+bwd step of the reference's CPU route on the whole workload
+    (or, with `sampled`, on the cut of cpu_sample_plan); returns the step,
+    the factor from its time to a whole-workload time (1 unless sampled) and
+    a description."""
     import torch
     torch.set_num_threads(threads)
     op, label = reference_cpu_op()
-    n, c_in, scale = cpu_sample_plan(wl)
+    n, c_in, scale = cpu_sample_plan(wl) if sampled else (None, None, 1.0)
     x, w, b, off, m, go = make_inputs(wl, n=n, c_in=c_in if c_in != wl["C"] else None)
     leaves = [t.clone().requires_grad_(True) if t is not None else None for t in (x, w, b, off, m)]
 
@@ -273,26 +289,41 @@ def cpu_reference_step_fn(wl, threads):
                  dilation=wl["dil"], mask=mm)
         out.backward(go)
 
-    sample = (f"{n} of {wl['N']} images x {c_in} of {wl['C']} input channels of the workload "
-              f"(1/{scale:g} of its work; every cost term is linear in images x input channels), "
-              f"fwd+bwd through {label}; value = sample time x {scale:g}")
-    return step, scale, sample
+    if sampled:
+        desc = (f"{n} of {wl['N']} images x {c_in} of {wl['C']} input channels of the workload "
+                f"(1/{scale:g} of its work), fwd+bwd through {label}; x {scale:g}")
+    else:
+        desc = (f"the whole workload ({wl['N']} images, all five inputs requiring grad, a "
+                f"fixed upstream gradient), fwd+bwd through {label}")
+    return step, scale, desc
 
 
-def cpu_baseline(wl, min_seconds=10.0):
+def time_cpu_steps(step, steps, warmup):
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    return (time.perf_counter() - t0) / steps
+
+
+def cpu_baseline(wl):
+    """The reference's CPU route timed on the whole workload on this host:
+    one untimed step, then two timed ones (about 25 s for the detection
+    neck on 16 cores).  `sampled`: the same route on a 1/16 cut of the
+    workload scaled back up, and its ratio to the measured figure (a check of
+    the linear scaling older bench lines relied on)."""
     import torch
     threads = os.cpu_count() or 1
-    step, scale, sample = cpu_reference_step_fn(wl, threads)
-    step()  # warm-up
-    times = []
-    t_end = time.perf_counter() + min_seconds
-    while len(times) < 2 or time.perf_counter() < t_end:
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    ms = statistics.mean(times) * 1e3 * scale
-    return {"value": round(ms, 3), "unit": "ms/iter", "cores": torch.get_num_threads(),
-            "kind": "reference", "sample": sample + f"; {len(times)} timed sample steps"}
+    step, _, desc = cpu_reference_step_fn(wl, threads)
+    full_ms = time_cpu_steps(step, steps=2, warmup=1) * 1e3
+    del step
+    sstep, scale, sdesc = cpu_reference_step_fn(wl, threads, sampled=True)
+    sample_ms = time_cpu_steps(sstep, steps=3, warmup=1) * 1e3 * scale
+    return {"value": round(full_ms, 3), "unit": "ms/iter", "cores": torch.get_num_threads(),
+            "kind": "reference", "sample": desc + "; 2 timed steps after 1 untimed, unscaled",
+            "sampled": {"value": round(sample_ms, 3), "ratio_to_measured":
+                        round(sample_ms / full_ms, 3), "sample": sdesc}}
 
 
 # ---------------------------------------------------------------------------
@@ -364,18 +395,21 @@ def run_ours(args, wl):
 
     from pytorch_mps_deform_conv2d_b200.distributed import deform_conv2d_row_sharded
 
-    def step():
+    def step_with_flags(fl):
         for t in leaves:
             t.grad = None
         if slabs > 1:  # this rank's output rows; grad_input summed over the image's ranks
             out = deform_conv2d_row_sharded(xd, offd, wd, bd, wl["stride"], wl["pad"],
                                             wl["dil"], md, row_begin=row0, group=group,
-                                            flags=flags)
+                                            flags=fl)
         else:
             out = deform_conv2d_ex(xd, offd, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
-                                   flags=flags)
+                                   flags=fl)
         out.backward(god)
         allreduce(params)
+
+    def step():
+        step_with_flags(flags)
 
     for _ in range(args.warmup):
         step()
@@ -490,23 +524,27 @@ def run_ours(args, wl):
         "dtype": ((f"{args.dtype} I/O, " if args.dtype in HALF else "") +
                   (args.math if any(k in TC_KERNELS for k in kernels) else "f32")),
         "data": "synthetic",
-        "config": {"workload": wl["desc"],
-                   "global_batch": wl["N"] if strong else wl["N"] * world,
-                   "per_gpu_batch": xd.shape[0],
-                   "parallelism": (f"dp{world // slabs}x{slabs} row slabs" if strong
-                                   else f"dp{world}"),
-                   "math": args.math, "input_layout": args.layout, "l2": "flushed between timed iterations (256 MiB write, "
-                                             "outside the timed events)",
-                   "wall_s": round(wall, 3),
-                   "kernel_table": ("a second pass of the same steps with a CUDA event pair "
-                                    "around every library launch (gpu_launches, kernels, "
-                                    "roofline.achieved); its ms/step: %.4f" %
-                                    (prof_ms / args.steps))},
+        "config": bench_config(wl, args),
+        "run": {"per_step_batch": wl["N"] if strong else wl["N"] * world,
+                "per_gpu_batch": xd.shape[0],
+                "parallelism": (f"dp{world // slabs}x{slabs} row slabs" if strong
+                                else f"dp{world}"),
+                "math": args.math,
+                "l2": "flushed between timed iterations (256 MiB write, outside the timed "
+                      "events)",
+                "wall_s": round(wall, 3),
+                "kernel_table": ("a second pass of the same steps with a CUDA event pair "
+                                 "around every library launch (gpu_launches, kernels, "
+                                 "roofline.achieved); its ms/step: %.4f" %
+                                 (prof_ms / args.steps))},
         "roofline": roof, "e2e": e2e, "gpu_launches": launches,
         "kernels": kernel_table,
     }
     if world == 1 and not args.profile:
         line["cuda_graph"] = graph_step_ms(step, leaves, flush, args.steps)
+        line["math_modes"] = other_math_modes(args, step_with_flags, flush)
+        line["e2e_full_readback"] = run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags,
+                                            allreduce, flush, full=True)
     if world == 1 and not (args.no_cpu_baseline or args.profile):
         line["cpu_baseline"] = cpu_baseline(wl)
     clk = clocks.summary()
@@ -551,16 +589,46 @@ def graph_step_ms(step, leaves, flush, steps):
     return {"ms_per_step": round(total / steps, 4), "mode": "whole fwd+bwd step replayed"}
 
 
-def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
+def other_math_modes(args, step_with_flags, flush):
+    """ms per step of the same step in the other math modes (3xTF32: fp32
+    accuracy on the tensor cores; fp32: FFMA on the CUDA cores, the strict
+    parity mode), timed like the headline: 2 untimed steps, then K steps with
+    CUDA events around each, L2 flushed before each."""
+    import torch
+    from pytorch_mps_deform_conv2d_b200.ops import _MODES
+    res = {}
+    for mode in ("3xtf32", "fp32"):
+        if mode == args.math:
+            continue
+        fl = _MODES[mode]
+        for _ in range(2):
+            step_with_flags(fl)
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step_with_flags(fl)
+            e1.record()
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        res[mode] = {"ms_per_step": round(total / args.steps, 4)}
+    return res
+
+
+def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush, full=False):
     """Same step through the public module API with the batch coming from
-    pinned host memory and the parameter gradients read back each step.
+    pinned host memory and the parameter gradients read back each step (with
+    `full`: the output and every gradient -- input, offset, mask, weight,
+    bias -- read back, the op's whole result).
 
     Two measurements: `serial` -- each step copies its inputs, computes and
     reads back, alone, L2 flushed before it; `pipelined` (the reported value)
     -- the steps run back to back the way a data loader feeds training: step
     i+1's host-to-device copies run on a copy stream into a second set of
     buffers while step i computes.  Every step still moves all of its inputs
-    over PCIe and reads its gradients back inside the timed region."""
+    over PCIe and reads its results back inside the timed region."""
     import torch
     import pytorch_mps_deform_conv2d_b200 as dcn
     mod = dcn.DeformConv2d(wl["C"], wl["outC"], wl["k"], stride=wl["stride"], padding=wl["pad"],
@@ -574,9 +642,15 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
     dcn.set_math_mode(args.math)
     host = [t.pin_memory() if t is not None else None for t in (x, off, m, go)]
     params = [p for p in mod.parameters()]
-    outs = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
+    pdt = params[0].dtype
+    # read back: the parameter gradients, and with `full` also the output and
+    # the input, offset and mask gradients (shapes of x, off, m, go)
+    back_shapes = [p.shape for p in params]
+    if full:
+        back_shapes += [t.shape for t in (go, x, off, m) if t is not None]
+    outs = [torch.empty(s, dtype=pdt, pin_memory=True) for s in back_shapes]
     h2d = sum(t.numel() * t.element_size() for t in host if t is not None)
-    d2h = sum(p.numel() * p.element_size() for p in params)
+    d2h = sum(o.numel() * o.element_size() for o in outs)
     compute = torch.cuda.current_stream(dev)
     copier = torch.cuda.Stream(dev)
     slots = [[torch.empty_like(t, device=dev) if t is not None else None for t in host]
@@ -602,8 +676,11 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
         out = mod(xd, od, md)
         out.backward(gd)
         allreduce(params)
-        for p, o in zip(params, outs):
-            o.copy_(p.grad, non_blocking=True)
+        results = [p.grad for p in params]
+        if full:
+            results += [out.detach()] + [t.grad for t in (xd, od, md) if t is not None]
+        for r, o in zip(results, outs):
+            o.copy_(r, non_blocking=True)
         used[slot].record(compute)
 
     try:
@@ -647,35 +724,41 @@ def run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags, allreduce, flush):
         serial, piped = float(t[0].item()), float(t[1].item())
     return {"value": round(piped / args.steps / world, 4), "unit": "ms/iter",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "mode": "pipelined",
-            "serial_value": round(serial / args.steps / world, 4)}
+            "serial_value": round(serial / args.steps / world, 4),
+            "read_back": ("output and all five gradients" if full
+                          else "grad_weight and grad_bias")}
 
 
 # ---------------------------------------------------------------------------
 # reference arm
 # ---------------------------------------------------------------------------
 def run_reference(args, wl):
+    """The reference's own CPU implementation of the path (its public
+    deform_conv2d on CPU tensors, which routes to torchvision's kernel) on the
+    whole workload, all host threads, rank 0 only: `warmup` untimed steps,
+    then `steps` timed ones (about 8.5 s a step for the detection neck on 16
+    cores)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    step, scale, sample = cpu_reference_step_fn(wl, threads)
+    step, _, desc = cpu_reference_step_fn(wl, threads)
     import torch
-    for _ in range(args.warmup):
-        step()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    sec = time.perf_counter() - t0
-    value = sec / args.steps * 1e3 * scale
+    value = time_cpu_steps(step, args.steps, args.warmup) * 1e3
+    wall = time.perf_counter() - t0
     line = {
         "metric": METRIC, "impl": "reference", "value": round(value, 3), "unit": "ms/iter",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(value, 3), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl["desc"], "global_batch": wl["N"], "parallelism": "host CPU"},
+        "config": bench_config(wl),
+        "run": {"where": "host CPU, one process", "threads": torch.get_num_threads(),
+                "wall_s": round(wall, 3)},
         "cpu_baseline": {"value": round(value, 3), "unit": "ms/iter",
                          "cores": torch.get_num_threads(), "kind": "reference",
-                         "sample": sample},
+                         "sample": desc + f"; {args.steps} timed steps after {args.warmup} "
+                                          "untimed, unscaled"},
         "e2e": {"value": round(value, 3), "unit": "ms/iter", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -94,6 +94,22 @@ extern "C" {
  *                    tensors (no reference counterpart: the reference makes
  *                    every operand contiguous NCHW). */
 #define DCN_INPUT_NHWC 0x20000
+/* Fourth byte: test switches (no reference counterpart).
+ *   DCN_TEST_WAIT_TIMEOUT  the tensor-core kernels' TMA producers issue no
+ *                    copies and every mbarrier wait gives up after about a
+ *                    millisecond, so the waits run out: the kernels raise
+ *                    their error word and return without results.  For
+ *                    testing dcn_device_status only; never in production. */
+#define DCN_TEST_WAIT_TIMEOUT 0x1000000
+
+/* Bits of the error word dcn_device_status reports: a bounded wait of that
+ * tensor-core kernel family ran out (no reference counterpart: the reference
+ * has no device-side waits).  The kernel then stops where it is -- its
+ * results are incomplete -- drains the copies and tensor-core operations it
+ * issued, frees its tensor memory and returns; it never traps or hangs. */
+#define DCN_STATUS_FWD_WAIT_TIMEOUT 0x1 /* forward (fwd_tc)                */
+#define DCN_STATUS_BWD_DATA_TIMEOUT 0x2 /* grad-column kernel (bwd_data_tc) */
+#define DCN_STATUS_BWD_WEIGHT_TIMEOUT 0x4 /* weight-gradient kernels        */
 
 /* Geometry of one deformable convolution: the shapes of the reference op's
  * tensors plus its integer arguments. */
@@ -239,9 +255,11 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
  * GPU that loads the library holds until the process exits.  Shapes whose
  * least workspace (dcn_forward_workspace_size without the optional
  * split-round scratch) exceeds 16 MiB are rejected with DCN_ERR_WORKSPACE
- * before anything is launched.  The first call on a device
- * looks up the array's device address there (cudaGetSymbolAddress); make that
- * first call before any stream capture.  All calls share the one array:
+ * before anything is launched.  The first call on a device (and in each
+ * further CUDA context on it: a context of the caller's own, or the primary
+ * context created again after cudaDeviceReset) looks up the array's device
+ * address there (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  All calls share the one array:
  * calls that can overlap on the GPU (different streams, or different host
  * threads on the same device) race on it and must be serialised by the
  * caller.  Nothing in the array needs to start at zero: each call overwrites
@@ -249,6 +267,15 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
 DCN_API int dcn_forward_noalloc(const dcn_shape* shape, const float* input,
                                 const float* weight, const float* offset, const float* mask,
                                 const float* bias, float* output, uint32_t flags, void* stream);
+
+/* Device error word of the current device (DCN_STATUS_* bits; 0 when every
+ * wait of the tensor-core kernels completed in time).  No reference
+ * counterpart.  The word is sticky: a bit stays raised, across calls, until a
+ * call with `clear` non-zero reads it, so a check after a batch of calls sees
+ * a failure of any of them.  The read is ordered after the work already
+ * enqueued on `stream` and the host waits for it (call it outside stream
+ * capture). */
+DCN_API int dcn_device_status(void* stream, int clear, int* status);
 
 /* Kernel profiler (no reference counterpart: the reference times its ops
  * with wall clocks around torch.mps.synchronize(), benchmarks/bench.py:39-49).

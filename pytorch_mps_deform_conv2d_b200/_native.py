@@ -103,6 +103,8 @@ def load_capi():
         lib.dcn_col2im.restype = ctypes.c_int
         lib.dcn_col2im_coord.argtypes = [vp] * 6 + [i64] * 12 + [vp]
         lib.dcn_col2im_coord.restype = ctypes.c_int
+        lib.dcn_device_status.argtypes = [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        lib.dcn_device_status.restype = ctypes.c_int
         lib.dcn_profiler_enable.argtypes = [ctypes.c_int]
         lib.dcn_profiler_enable.restype = ctypes.c_int
         lib.dcn_profiler_read.argtypes = [ctypes.POINTER(KernelStat), ctypes.c_int,

@@ -26,7 +26,10 @@
 
 namespace dcn {
 
-__device__ int g_tc_bwd_status;  // set to 1 by a wait that ran out
+// Error word of the tensor-core backward: kStatusBwdData / kStatusBwdWeight
+// raised by a wait of that kernel that ran out (read and cleared by
+// read_bwd_status).
+__device__ int g_tc_bwd_status;
 
 namespace {
 
@@ -427,7 +430,10 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   uint64_t* empty = full + D_STAGES;
   uint64_t* acc_full = empty + D_STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const tc::Watch watch{abort_flag, &g_tc_bwd_status, kStatusBwdData, g.wait_limit};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 32-out-channel K steps; a partial last one reads zero weights past Og
@@ -443,6 +449,8 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
       tc::mbar_init(&acc_full[a], 1);
       tc::mbar_init(&acc_empty[a], D_EPI_WARPS);
     }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
     tc::fence_mbar_init();
   }
   if (warp == D_MMA_WARP) {
@@ -455,8 +463,9 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   const uint32_t tmem = *tmem_slot;
 
   if (warp == D_TMA_WARP) {
-    if (lane == 0) {
-      int gs = 0;
+    if (lane == 0 && !g.no_async) {
+      int gs = 0;  // stages filled so far
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const DTile T = dtile_of(t, mtiles, nslots, ksplits);
         // per block: go_r row of out channel 0 of its image, first pixel; a
@@ -474,7 +483,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
           for (int s = 0; s < ochunks; ++s, ++gs) {
             const int st = gs % D_STAGES;
             const int u = gs / D_STAGES;
-            if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+            if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return;
             tc::mbar_arrive_expect_tx(&full[st], SSTAGE);
             const uint32_t sA = s0 + st * SSTAGE;
             // pixels past the image's last one are outside the map: zero fill
@@ -493,22 +502,27 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
           }
         }
       }
+      }();
+      if (tc::aborted(watch))  // the copies of the last stages land before exit
+        for (int i = gs > D_STAGES ? gs - D_STAGES : 0; i < gs; ++i)
+          tc::drain_wait(&full[i % D_STAGES], (i / D_STAGES) & 1, g.wait_limit);
     }
     __syncwarp();
   } else if (warp == D_MMA_WARP) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32_amn(D_BM, D_BN);
       int gs = 0, gt = 0;
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const DTile T = dtile_of(t, mtiles, nslots, ksplits);
         for (int sl = T.s0; sl < T.s1; ++sl, ++gt) {
           const int acc = gt & 1;
-          if (gt >= 2) tc::mbar_wait(&acc_empty[acc], ((gt >> 1) - 1) & 1, &g_tc_bwd_status);
+          if (gt >= 2 && !tc::wait(watch, &acc_empty[acc], ((gt >> 1) - 1) & 1)) return;
           tc::tc_fence_after();
           const uint32_t d = tmem + (uint32_t)(acc * D_BN);
           for (int s = 0; s < ochunks; ++s, ++gs) {
             const int st = gs % D_STAGES;
-            tc::mbar_wait(&full[st], (gs / D_STAGES) & 1, &g_tc_bwd_status);
+            if (!tc::wait(watch, &full[st], (gs / D_STAGES) & 1)) return;
             tc::tc_fence_after();
             const uint32_t sA = s0 + st * SSTAGE, sB = sA + D_BM * 128;
 #pragma unroll
@@ -531,6 +545,11 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
           tc::umma_commit(&acc_full[acc]);
         }
       }
+      }();
+      if (tc::aborted(watch)) {  // every UMMA issued so far completes before exit
+        tc::umma_commit(drain);
+        tc::drain_wait(drain, 0, g.wait_limit);
+      }
     }
     __syncwarp();
   } else {
@@ -539,6 +558,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     constexpr int CPW = 16 / D_EPI_WARPS;  // 32-channel chunks per warp
     unsigned char* scratch = epi + e * EPI_WARP_BYTES;
     int gt = 0;
+    [&]() {
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const DTile T = dtile_of(t, mtiles, nslots, ksplits);
       // this lane quarter's block: pixels qbase .. qbase + 31 of the flat
@@ -553,7 +573,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
       int plan_key = -1;
       for (int sl = T.s0; sl < T.s1; ++sl, ++gt) {
         const int acc = gt & 1;
-        tc::mbar_wait(&acc_full[acc], (gt >> 1) & 1, &g_tc_bwd_status);
+        if (!tc::wait(watch, &acc_full[acc], (gt >> 1) & 1)) return;
         tc::tc_fence_after();
 #pragma unroll 1
         for (int cc = 0; cc < CPW; ++cc) {
@@ -585,6 +605,7 @@ bwd_data_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
         }
       }
     }
+    }();
   }
 
   tc::tc_fence_before();
@@ -664,7 +685,7 @@ constexpr int W2_A_STAGE = 16384;
 // 3xTF32 carries high and low parts: 2 stages of twice the size.
 size_t weight_smem_bytes(int bn, bool split) {
   const int stages = split ? 2 : 4, parts = split ? 2 : 1;
-  return (size_t)stages * parts * (W2_A_STAGE + (size_t)bn * 128) + 128 + 1024;
+  return (size_t)stages * parts * (W2_A_STAGE + (size_t)bn * 128) + 256 + 1024;
 }
 
 struct WTile {
@@ -704,10 +725,14 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
   const uint32_t sB0 = sA0 + W2_STAGES * PARTS * W2_A_STAGE;
   uint64_t* full =
       reinterpret_cast<uint64_t*>(smem + W2_STAGES * PARTS * (W2_A_STAGE + b_stage));
-  uint64_t* empty = full + W2_STAGES;
+  uint64_t* tfull = full + W2_STAGES;  // the go_r rows' TMA bytes
+  uint64_t* empty = tfull + W2_STAGES;
   uint64_t* acc_full = empty + W2_STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const tc::Watch watch{abort_flag, &g_tc_bwd_status, kStatusBwdWeight, g.wait_limit};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pchunks = (g.P + 31) >> 5;
@@ -715,13 +740,16 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
 
   if (tid == 0) {
     for (int s = 0; s < W2_STAGES; ++s) {
-      tc::mbar_init(&full[s], W2_GATHER_WARPS + 1);
+      tc::mbar_init(&full[s], W2_GATHER_WARPS);
+      tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&acc_full[a], 1);
       tc::mbar_init(&acc_empty[a], 4);
     }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
     tc::fence_mbar_init();
   }
   if (warp == W2_MMA_WARP) {
@@ -740,6 +768,7 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
     const int quad = lane & 7, sub = lane >> 3;
     const int zoff = g.N * g.HW * g.C;
     int gs = 0;
+    [&]() {
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
       if (T.t_begin >= T.t_end) continue;
@@ -792,7 +821,7 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
           for (int c = 0; c < 4; ++c)
             v[i][c] = ldg4(xq + (unsigned)coff[i][c]);  // dropped corners: zero row
         if (tt + 1 < T.t_end) fetch(n, p0);
-        if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+        if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return;
         const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -814,10 +843,12 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
         if (lane == 0) tc::mbar_arrive(&full[st]);
       }
     }
+    }();
   } else if (warp == W2_TMA_WARP) {
     // ------------------------------ go_r rows (TMA) ------------------------------
-    if (lane == 0) {
-      int gs = 0;
+    if (lane == 0 && !g.no_async) {
+      int gs = 0;  // stages filled so far
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
@@ -825,15 +856,19 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
           const int u = gs / W2_STAGES;
           const int n = tt / pchunks;
           const int p0 = (tt - n * pchunks) << 5;
-          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
-          tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
+          if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return;
+          tc::mbar_arrive_expect_tx(&tfull[st], PARTS * b_stage);
           const int row = n * g.outC + T.gi * g.Og + T.o0;
           const uint32_t sB = sB0 + st * PARTS * b_stage;
-          tc::tma_load_2d(sB, &gomap, p0, row, &full[st]);
+          tc::tma_load_2d(sB, &gomap, p0, row, &tfull[st]);
           if constexpr (SPLIT)  // low parts: rows N*outC .. of go_r
-            tc::tma_load_2d(sB + b_stage, &gomap, p0, g.N * g.outC + row, &full[st]);
+            tc::tma_load_2d(sB + b_stage, &gomap, p0, g.N * g.outC + row, &tfull[st]);
         }
       }
+      }();
+      if (tc::aborted(watch))  // the copies of the last stages land before exit
+        for (int i = gs > W2_STAGES ? gs - W2_STAGES : 0; i < gs; ++i)
+          tc::drain_wait(&tfull[i % W2_STAGES], (i / W2_STAGES) & 1, g.wait_limit);
     }
     __syncwarp();
   } else if (warp == W2_MMA_WARP) {
@@ -841,17 +876,20 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
       int gs = 0, it = 0;
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
         if (T.t_begin >= T.t_end) continue;
         const int acc = it & 1;
-        if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_bwd_status);
+        if (it >= 2 && !tc::wait(watch, &acc_empty[acc], ((it >> 1) - 1) & 1)) return;
         tc::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * bn);
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
           const int st = gs % W2_STAGES;
           const int s = tt - T.t_begin;
-          tc::mbar_wait(&full[st], (gs / W2_STAGES) & 1, &g_tc_bwd_status);
+          if (!tc::wait(watch, &full[st], (gs / W2_STAGES) & 1) ||
+              !tc::wait(watch, &tfull[st], (gs / W2_STAGES) & 1))
+            return;
           tc::tc_fence_after();
           const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
@@ -873,6 +911,11 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
         tc::umma_commit(&acc_full[acc]);
         ++it;
       }
+      }();
+      if (tc::aborted(watch)) {  // every UMMA issued so far completes before exit
+        tc::umma_commit(drain);
+        tc::drain_wait(drain, 0, g.wait_limit);
+      }
     }
     __syncwarp();
   } else {
@@ -882,7 +925,7 @@ bwd_weight_tc_kernel(Geom g, const __grid_constant__ CUtensorMap gomap, int bn, 
       const WTile T = wtile_of(g, t, mtiles, ntn, splits, per, total_chunks, bn);
       if (T.t_begin >= T.t_end) continue;
       const int acc = it & 1;
-      tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
+      if (!tc::wait(watch, &acc_full[acc], (it >> 1) & 1)) break;
       tc::tc_fence_after();
       const int c = T.cm0 + warp * 32 + lane;  // channel within the group
       // element (o, k, c) at o * Cg*kk + k * sk + c * sc (grad_weight, or its
@@ -972,7 +1015,10 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const tc::Watch watch{abort_flag, &g_tc_bwd_status, kStatusBwdWeight, g.wait_limit};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pchunks = (g.P + 31) >> 5;
@@ -987,6 +1033,8 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
       tc::mbar_init(&acc_full[a], 1);
       tc::mbar_init(&acc_empty[a], 4);
     }
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
     tc::fence_mbar_init();
   }
   if (warp == WC_MMA_WARP) {
@@ -999,9 +1047,10 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
   const uint32_t tmem = *tmem_slot;
 
   if (warp == WC_TMA_WARP) {
-    if (lane == 0) {
+    if (lane == 0 && !g.no_async) {
       const int lo_rows = g.kk * (int)g.NP;  // row offset of the low parts
-      int gs = 0;
+      int gs = 0;  // stages filled so far
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
         // the four 32-row blocks of the slot: (tap, channel) of each
@@ -1017,7 +1066,7 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
           const int u = gs / STAGES;
           const int n = tt / pchunks;
           const int p0 = (tt - n * pchunks) << 5;
-          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_bwd_status);
+          if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return;
           tc::mbar_arrive_expect_tx(&full[st], PARTS * (W2_A_STAGE + b_stage));
           const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE;
 #pragma unroll
@@ -1037,23 +1086,28 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
             tc::tma_load_2d(sB + b_stage, &gomap, p0, g.N * g.outC + row, &full[st]);
         }
       }
+      }();
+      if (tc::aborted(watch))  // the copies of the last stages land before exit
+        for (int i = gs > STAGES ? gs - STAGES : 0; i < gs; ++i)
+          tc::drain_wait(&full[i % STAGES], (i / STAGES) & 1, g.wait_limit);
     }
     __syncwarp();
   } else if (warp == WC_MMA_WARP) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32_amn(W_BM, bn);
       int gs = 0, it = 0;
+      [&]() {
       for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
         if (T.t_begin >= T.t_end) continue;
         const int acc = it & 1;
-        if (it >= 2) tc::mbar_wait(&acc_empty[acc], ((it >> 1) - 1) & 1, &g_tc_bwd_status);
+        if (it >= 2 && !tc::wait(watch, &acc_empty[acc], ((it >> 1) - 1) & 1)) return;
         tc::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * bn);
         for (int tt = T.t_begin; tt < T.t_end; ++tt, ++gs) {
           const int st = gs % STAGES;
           const int s = tt - T.t_begin;
-          tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_bwd_status);
+          if (!tc::wait(watch, &full[st], (gs / STAGES) & 1)) return;
           tc::tc_fence_after();
           const uint32_t sA = sA0 + st * PARTS * W2_A_STAGE, sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
@@ -1075,6 +1129,11 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
         tc::umma_commit(&acc_full[acc]);
         ++it;
       }
+      }();
+      if (tc::aborted(watch)) {  // every UMMA issued so far completes before exit
+        tc::umma_commit(drain);
+        tc::drain_wait(drain, 0, g.wait_limit);
+      }
     }
     __syncwarp();
   } else {
@@ -1083,7 +1142,7 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
       const WCTile T = wctile_of(t, nslots, ntn, splits, per, total_chunks, bn);
       if (T.t_begin >= T.t_end) continue;
       const int acc = it & 1;
-      tc::mbar_wait(&acc_full[acc], (it >> 1) & 1, &g_tc_bwd_status);
+      if (!tc::wait(watch, &acc_full[acc], (it >> 1) & 1)) break;
       tc::tc_fence_after();
       const int row = T.slot * 128 + warp * 32 + lane;  // (tap, channel) row of the group
       const int k = row / g.Cg, c = row - k * g.Cg;
@@ -1187,6 +1246,21 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
 }
 
 }  // namespace
+
+cudaError_t read_bwd_status(int* status, bool clear, cudaStream_t stream) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_tc_bwd_status, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess && clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_tc_bwd_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice,
+                                stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  }
+  *status = v;
+  return e;
+}
 
 bool tc_bwd_supported(const Geom& g) {
   // channels per group: any multiple of 32 (a 128-row slot of the group's

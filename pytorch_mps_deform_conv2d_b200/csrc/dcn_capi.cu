@@ -200,6 +200,15 @@ struct Carver {
   }
 };
 
+// DCN_TEST_WAIT_TIMEOUT: the tensor-core kernels' TMA producers issue
+// nothing and every wait gives up after a short budget.
+void apply_test_flags(dcn::Geom& g, uint32_t flags) {
+  if (flags & DCN_TEST_WAIT_TIMEOUT) {
+    g.no_async = 1;
+    g.wait_limit = dcn::kTestWaitLimit;
+  }
+}
+
 // Validation shared by forward and backward (.mm:202-267, :693-760).
 int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
               const char* op) {
@@ -242,6 +251,8 @@ int make_geom(const dcn_shape* s, bool use_mask, bool use_bias, dcn::Geom& g,
   g.use_mask = use_mask ? 1 : 0; g.use_bias = use_bias ? 1 : 0;
   g.mask_logits = 0;
   g.oy0 = 0;
+  g.wait_limit = dcn::kWaitLimit;
+  g.no_async = 0;
   g.Cg = g.C / g.G; g.Og = g.outC / g.G; g.cpg = g.dg ? g.C / g.dg : 0;
   g.kk = g.kh * g.kw; g.P = g.Ho * g.Wo; g.HW = g.H * g.W;
   g.NP = (long long)g.N * g.P;
@@ -423,6 +434,7 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
   rc = apply_rows(g, row0, rows, "deform_conv2d_forward");
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
+  apply_test_flags(g, flags);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;  // .mm:273: nothing to dispatch
@@ -536,6 +548,7 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
   int rc = make_geom(s, mask != nullptr, bias != nullptr, g, "deform_conv2d_forward");
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
+  apply_test_flags(g, flags);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;
@@ -647,6 +660,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   rc = apply_rows(g, row0, rows, "deform_conv2d_backward");
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
+  apply_test_flags(g, flags);
   DCN_CHECK(mask != nullptr || grad_mask == nullptr,
             "deform_conv2d_backward: grad_mask must be NULL when mask is NULL");
   DCN_CHECK(mask == nullptr || grad_mask != nullptr,
@@ -997,6 +1011,18 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input, const flo
   DCN_CUDA(dcn::launch_col2im_coord_single(g, columns, input, offset, mask, grad_offset, grad_mask,
                                            stream),
            "col2im_coord");
+  return DCN_OK;
+}
+
+DCN_API int dcn_device_status(void* stream_, int clear, int* status) {
+  g_last_error.clear();
+  DCN_CHECK(status != nullptr, "dcn_device_status: status must not be NULL");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int f = 0, b = 0;
+  cudaError_t e = dcn::read_fwd_status(&f, clear != 0, stream);
+  if (e == cudaSuccess) e = dcn::read_bwd_status(&b, clear != 0, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "dcn_device_status");
+  *status = f | b;
   return DCN_OK;
 }
 

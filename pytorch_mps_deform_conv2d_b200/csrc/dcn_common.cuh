@@ -31,6 +31,11 @@ struct Geom {
   int P;               // Ho * Wo
   int HW;              // H * W
   long long NP;        // N * P
+  // tensor-core kernels: SM clock cycles one mbarrier wait may take before
+  // the CTA gives up (raises its error word and leaves), and a test switch
+  // under which their TMA producers issue nothing, so that the waits run out
+  long long wait_limit;
+  int no_async;
 };
 
 // Bilinear sampling plan of one (pixel, tap, deformable group): the four

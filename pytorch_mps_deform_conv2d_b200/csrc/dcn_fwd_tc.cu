@@ -19,10 +19,12 @@
 //               per K step issues its 8 corner loads (16 B, NHWC input),
 //               combines, rounds to TF32 and stores into the swizzled stage
 // A 4-stage shared-memory ring (A 16 KB + B up to 32 KB per stage) is guarded
-// by mbarriers: full[s] = 16 gather-warp arrivals + the TMA transaction bytes;
-// empty[s] = tcgen05.commit of the MMAs that read it.  Two accumulators of BN
-// columns in tensor memory (acc_full / acc_empty barriers) let the epilogue of
-// tile i run while tile i+1 is being accumulated.  Every wait is bounded.
+// by mbarriers: full[s] = 16 gather-warp arrivals, tfull[s] = the weight
+// tile's TMA transaction bytes; empty[s] = tcgen05.commit of the MMAs that
+// read it.  Two accumulators of BN columns in tensor memory (acc_full /
+// acc_empty barriers) let the epilogue of tile i run while tile i+1 is being
+// accumulated.  Every wait is bounded (tc::Watch): the first one that runs
+// out raises bit 1 of g_tc_fwd_status and makes every role of the CTA leave.
 //
 // 3xTF32 (SPLIT): each operand is carried as a high TF32 part and a low TF32
 // part (x - hi); every K step issues lo.hi + hi.lo + hi.hi, which recovers
@@ -45,7 +47,9 @@
 
 namespace dcn {
 
-__device__ int g_tc_fwd_status;  // set to 1 by a wait that ran out
+// Error word of the tensor-core forward: bit 1 is raised by a wait that ran
+// out (read and cleared by read_fwd_status).
+__device__ int g_tc_fwd_status;
 
 namespace {
 
@@ -85,9 +89,13 @@ struct FwdCfg {
   static constexpr int PARTS = SPLIT ? 2 : 1;
   static constexpr int KCH = H16 ? 64 : 32;  // channels of one tap per K step
 };
+// Barriers and flags after the stage ring: full, tfull, empty (one per stage),
+// acc_full, acc_empty (two), drain, epi_bar, then the tensor-memory address,
+// the epilogue's last-piece broadcast and the abort flag.
+constexpr int kBarrierBytes = 256;
 size_t smem_bytes(int bn, bool split) {
   const int parts = split ? 2 : 1, stages = split ? 2 : 4;
-  return (size_t)stages * parts * (A_STAGE + (size_t)bn * 128) + 128 + 1024;
+  return (size_t)stages * parts * (A_STAGE + (size_t)bn * 128) + kBarrierBytes + 1024;
 }
 
 struct Tile {
@@ -128,11 +136,12 @@ struct Work {
   int slot;    // partial slot, -1 for a whole tile
 };
 // Runs f(work) for this CTA's work in order: its whole tiles, then its pieces
-// of split tiles.  The two loops inline f separately, so the whole-tile loop
-// keeps no split state live.
+// of split tiles, until f returns false (a wait of the CTA gave up).  The two
+// loops inline f separately, so the whole-tile loop keeps no split state live.
 template <class F>
 __device__ __forceinline__ void for_each_work(const TailPlan& tp, int steps, F&& f) {
-  for (int t = blockIdx.x; t < tp.whole; t += gridDim.x) f(Work{t, 0, steps, -1});
+  for (int t = blockIdx.x; t < tp.whole; t += gridDim.x)
+    if (!f(Work{t, 0, steps, -1})) return;
   if ((int)blockIdx.x >= tp.ctas) return;
   // tail_steps < 2^30 (host), so the positions fit in int
   int x = (int)((long long)blockIdx.x * tp.tail_steps / tp.ctas);
@@ -141,7 +150,7 @@ __device__ __forceinline__ void for_each_work(const TailPlan& tp, int steps, F&&
     const int j = x / steps;
     const int s0 = x - j * steps;
     const int s1 = xend - x < steps - s0 ? s0 + (xend - x) : steps;
-    f(Work{tp.whole + j, s0, s1, 2 * (int)blockIdx.x + seg});
+    if (!f(Work{tp.whole + j, s0, s1, 2 * (int)blockIdx.x + seg})) return;
     x += s1 - s0;
   }
 }
@@ -226,12 +235,19 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   const int tn = NH * bn;  // out channels of a tile
   const uint32_t b_stage = (uint32_t)tn * 128;
   const uint32_t sB0 = sA0 + STAGES * PARTS * A_STAGE;
+  // full[s]: the 16 gather warps' A rows; tfull[s]: the weight tile's TMA
+  // bytes (a barrier of its own, so the TMA warp can drain its copies alone)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * PARTS * (A_STAGE + b_stage));
-  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = full + STAGES;
+  uint64_t* empty = tfull + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* epi_bar = drain + 1;  // the epilogue warps' meeting point (split tiles)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
   int* last_piece = reinterpret_cast<int*>(tmem_slot + 1);  // epilogue broadcast
+  int* abort_flag = last_piece + 1;
+  const tc::Watch watch{abort_flag, &g_tc_fwd_status, kStatusFwd, g.wait_limit};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nchunk = g.Cg / KCH;
@@ -239,13 +255,17 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      tc::mbar_init(&full[s], GATHER_WARPS + 1);
+      tc::mbar_init(&full[s], GATHER_WARPS);
+      tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&acc_full[a], 1);
       tc::mbar_init(&acc_empty[a], EPI_WARPS);
     }
+    tc::mbar_init(drain, 1);
+    tc::mbar_init(epi_bar, EPI_WARPS);
+    *abort_flag = 0;
     tc::fence_mbar_init();
   }
   if (warp == MMA_WARP) {
@@ -324,7 +344,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           ldg_v8(xq + (size_t)(unsigned)(coff[c] + gch0) * ESZ, v[c]);
-        if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
+        if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return false;
         const float a = cw[0], b = cw[1], c = cw[2], d = cw[3];
         if constexpr (H16) {
           uint32_t r[8];
@@ -384,27 +404,32 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           replan = true;
         }
       }
+      return true;
     });
   } else if (warp == TMA_WARP) {
     // ------------------------------ weights (TMA) ------------------------------
-    if (lane == 0) {
-      int gs = 0;
+    if (lane == 0 && !g.no_async) {
+      int gs = 0;  // stages filled so far
       for_each_work(tp, steps, [&](const Work& w) {
         const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
         const int row = T.gi * g.Og + T.o0;
         for (int s = w.s0; s < w.s1; ++s, ++gs) {
           const int st = gs % STAGES;
           const int u = gs / STAGES;
-          if (u > 0) tc::mbar_wait(&empty[st], (u - 1) & 1, &g_tc_fwd_status);
-          tc::mbar_arrive_expect_tx(&full[st], PARTS * b_stage);
+          if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return false;
+          tc::mbar_arrive_expect_tx(&tfull[st], PARTS * b_stage);
           const uint32_t sB = sB0 + st * PARTS * b_stage;
 #pragma unroll
           for (int h = 0; h < NH; ++h)  // 256-row boxes
-            tc::tma_load_2d(sB + h * bn * 128, &wmap, s * KCH, row + h * bn, &full[st]);
+            tc::tma_load_2d(sB + h * bn * 128, &wmap, s * KCH, row + h * bn, &tfull[st]);
           if constexpr (SPLIT)  // low parts: rows outC .. 2*outC - 1 of the packed weight
-            tc::tma_load_2d(sB + b_stage, &wmap, s * KCH, g.outC + row, &full[st]);
+            tc::tma_load_2d(sB + b_stage, &wmap, s * KCH, g.outC + row, &tfull[st]);
         }
+        return true;
       });
+      if (tc::aborted(watch))  // the copies of the last STAGES fills land before exit
+        for (int i = gs > STAGES ? gs - STAGES : 0; i < gs; ++i)
+          tc::drain_wait(&tfull[i % STAGES], (i / STAGES) & 1, g.wait_limit);
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
@@ -419,13 +444,15 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         // tensor memory (NH = 2)
         const int acc = NH == 2 ? 0 : (it & 1);
         const int use = NH == 2 ? it : (it >> 1);  // earlier tiles in this accumulator
-        if (use >= 1) tc::mbar_wait(&acc_empty[acc], (use - 1) & 1, &g_tc_fwd_status);
+        if (use >= 1 && !tc::wait(watch, &acc_empty[acc], (use - 1) & 1)) return false;
         tc::tc_fence_after();
         const uint32_t d0 = tmem + (uint32_t)(acc * tn);
         for (int s = w.s0; s < w.s1; ++s, ++gs) {
           const int st = gs % STAGES;
           const uint32_t accum = s != w.s0 ? 1u : 0u;  // the first K step overwrites
-          tc::mbar_wait(&full[st], (gs / STAGES) & 1, &g_tc_fwd_status);
+          if (!tc::wait(watch, &full[st], (gs / STAGES) & 1) ||
+              !tc::wait(watch, &tfull[st], (gs / STAGES) & 1))
+            return false;
           tc::tc_fence_after();
           const uint32_t sA = sA0 + st * PARTS * A_STAGE, sB0s = sB0 + st * PARTS * b_stage;
 #pragma unroll
@@ -453,18 +480,29 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         }
         tc::umma_commit(&acc_full[acc]);
         ++it;
+        return true;
       });
+      if (tc::aborted(watch)) {  // every UMMA issued so far completes before exit
+        tc::umma_commit(drain);
+        tc::drain_wait(drain, 0, g.wait_limit);
+      }
     }
     __syncwarp();
   } else {
     // ------------------------------ epilogue ------------------------------
     int it = 0;
     const int r = warp * 32 + lane;
+    int nsync = 0;  // epi_bar phases passed
+    auto epi_sync = [&]() {
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(epi_bar);
+      return tc::wait(watch, epi_bar, (uint32_t)(nsync++ & 1));
+    };
     for_each_work(tp, steps, [&](const Work& w) {
       const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
       const int i = it++;
       const int acc = NH == 2 ? 0 : (i & 1);
-      tc::mbar_wait(&acc_full[acc], (NH == 2 ? i : (i >> 1)) & 1, &g_tc_fwd_status);
+      if (!tc::wait(watch, &acc_full[acc], (NH == 2 ? i : (i >> 1)) & 1)) return false;
       tc::tc_fence_after();
       const long long q = T.q0 + r;
       const bool valid = q < g.NP;
@@ -494,7 +532,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
-        return;
+        return true;
       }
       // a piece of a split tile: its partial into the slot (out channel
       // major, so a warp's 32 rows are one 128-byte line) ...
@@ -514,9 +552,11 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       const long long x0 = (long long)j * steps;
       const int cfirst = tail_cta_of(tp, x0), clast = tail_cta_of(tp, x0 + steps - 1);
       __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      // the four epilogue warps meet on an mbarrier (a bounded wait: a warp
+      // that gave up earlier does not leave the others stuck)
+      if (!epi_sync()) return false;
       if (r == 0) *last_piece = atomicAdd(&tp.count[j], 1) == clast - cfirst;
-      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      if (!epi_sync()) return false;
       if (*last_piece) {
         __threadfence();
         // CTAs after the first start their range inside this tile (their
@@ -539,6 +579,7 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
           }
         }
       }
+      return true;
     });
   }
 
@@ -641,7 +682,7 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
   const int bn = tc_bn(g);
   const bool wide = wide_tiles(mode, g);
   const int tn = tile_cols(mode, g);
-  const size_t smem = wide ? 2 * ((size_t)A_STAGE + (size_t)tn * 128) + 128 + 1024
+  const size_t smem = wide ? 2 * ((size_t)A_STAGE + (size_t)tn * 128) + kBarrierBytes + 1024
                            : smem_bytes(bn, mode == kSplit);
   auto kern = mode == kSplit ? fwd_tc_kernel<kSplit, 1>
               : mode == kBF16 ? (wide ? fwd_tc_kernel<kBF16, 2> : fwd_tc_kernel<kBF16, 1>)
@@ -678,6 +719,21 @@ bool tc_fwd_supported(const Geom& g) {
 
 size_t tc_fwd_weight_bytes(const Geom& g, bool split) {
   return (size_t)(split ? 2 : 1) * g.outC * g.kk * g.Cg * sizeof(float);
+}
+
+cudaError_t read_fwd_status(int* status, bool clear, cudaStream_t stream) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_tc_fwd_status, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess && clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_tc_fwd_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice,
+                                stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  }
+  *status = v;
+  return e;
 }
 
 size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms) {

@@ -13,10 +13,14 @@
 // with this module's code on every GPU that loads the library and stays there
 // until the process exits.  In host code its name is only a stand-in for the
 // symbol, not a device address: its address on the current device is looked
-// up with cudaGetSymbolAddress (once per device, on the first call there) and
-// that address is what the kernels get.
+// up with cudaGetSymbolAddress (once per device and CUDA context, on the first
+// call there) and that address is what the kernels get.
 #include <cuda_runtime.h>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -38,41 +42,83 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device; the first call
-// per device resolves it (with that device current, which it is here).
+// The array's address belongs to the CUDA context it was resolved in: the
+// device's primary context normally, but a caller may run in a context of its
+// own, and cudaDeviceReset replaces the primary context.  So each device's
+// cached address is tagged with the unique ID of the context it was resolved
+// in (cuCtxGetId, never reused within a process), and a call from any other
+// context resolves it again.  Reading a cached address takes no lock.
+struct ScratchSlot {
+  std::atomic<unsigned long long> ctx_id{0};  // 0: nothing resolved yet
+  std::atomic<void*> addr{nullptr};
+};
+ScratchSlot g_slots[kMaxDevices];
+std::mutex g_setup_mu;
+
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+void resolve_ctx_queries() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  cudaGetLastError();
+}
+
+// Unique ID of the context current on this thread (0: none yet, or the
+// driver cannot say -- then every call takes the resolving path).
+unsigned long long current_ctx_id() {
+  std::call_once(g_ctx_once, resolve_ctx_queries);
+  if (g_ctx_current == nullptr || g_ctx_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+int cuda_error(const char* what, int dev, cudaError_t e) {
+  char msg[200];
+  std::snprintf(msg, sizeof(msg), "dcn_forward_noalloc: %s failed on device %d: %s", what, dev,
+                cudaGetErrorString(e));
+  dcn::set_last_error(DCN_ERR_CUDA, msg);
+  return DCN_ERR_CUDA;
+}
+
+// Device address of the scratch array in the current device's current
+// context.  The first call per device (and per context) resolves it with
+// cudaGetSymbolAddress, with that device current, which it is here.
 int scratch_address(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    char msg[160];
-    std::snprintf(msg, sizeof(msg), "dcn_forward_noalloc: cudaGetDevice failed: %s",
-                  cudaGetErrorString(e));
-    dcn::set_last_error(DCN_ERR_CUDA, msg);
-    return DCN_ERR_CUDA;
-  }
+  if (e != cudaSuccess) return cuda_error("cudaGetDevice", dev, e);
   if (dev < 0 || dev >= kMaxDevices) {
     dcn::set_last_error(DCN_ERR_UNSUPPORTED, "dcn_forward_noalloc: device index beyond 63");
     return DCN_ERR_UNSUPPORTED;
   }
-  std::lock_guard<std::mutex> lk(g_setup_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      char msg[200];
-      std::snprintf(msg, sizeof(msg),
-                    "dcn_forward_noalloc: cudaGetSymbolAddress of the scratch array failed on "
-                    "device %d: %s",
-                    dev, cudaGetErrorString(e));
-      dcn::set_last_error(DCN_ERR_CUDA, msg);
-      return DCN_ERR_CUDA;
-    }
-    g_scratch_addr[dev] = p;
+  ScratchSlot& slot = g_slots[dev];
+  unsigned long long id = current_ctx_id();
+  if (id != 0 && slot.ctx_id.load(std::memory_order_acquire) == id) {
+    *out = slot.addr.load(std::memory_order_relaxed);
+    return DCN_OK;
   }
-  *out = g_scratch_addr[dev];
+  std::lock_guard<std::mutex> lk(g_setup_mu);
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // makes a context current if none was
+  if (e != cudaSuccess || p == nullptr)
+    return cuda_error("cudaGetSymbolAddress of the scratch array", dev, e);
+  if (id == 0) id = current_ctx_id();
+  slot.addr.store(p, std::memory_order_relaxed);
+  slot.ctx_id.store(id, std::memory_order_release);
+  *out = p;
   return DCN_OK;
 }
 

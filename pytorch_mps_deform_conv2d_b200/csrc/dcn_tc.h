@@ -8,6 +8,18 @@
 
 namespace dcn {
 
+// Error words of the tensor-core kernels (a bit per kernel family whose
+// bounded mbarrier wait ran out: kStatusFwd, kStatusBwdData,
+// kStatusBwdWeight), read after the work already on `stream` (the host
+// waits for it) and cleared when `clear` is set.
+constexpr int kStatusFwd = 0x1, kStatusBwdData = 0x2, kStatusBwdWeight = 0x4;
+cudaError_t read_fwd_status(int* status, bool clear, cudaStream_t stream);
+cudaError_t read_bwd_status(int* status, bool clear, cudaStream_t stream);
+// Cycles a wait of the tensor-core kernels may take before it gives up
+// (~2 s at 1.9 GHz), and the short budget of the timeout test switch.
+constexpr long long kWaitLimit = 4000000000LL;
+constexpr long long kTestWaitLimit = 2000000LL;
+
 // Whether the tensor-core forward covers this geometry.
 bool tc_fwd_supported(const Geom& g);
 // Bytes of the packed weight operand of the tensor-core forward (`split`:

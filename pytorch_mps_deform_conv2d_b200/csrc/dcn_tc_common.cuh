@@ -72,6 +72,47 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return true;
 }
 
+// ---- bounded waits with a CTA-wide give-up ----
+// Every wait of the warp-specialised kernels goes through a Watch.  The first
+// wait of a CTA that runs out of its cycle budget raises bit `code` of the
+// global error word `status` and the CTA's abort flag (shared memory); from
+// then on every wait of the CTA gives up at once, so each role leaves its
+// loop, drains what it issued (drain_wait) and reaches the kernel's final
+// barrier, where tensor memory is freed.  No wait spins unbounded, none traps.
+struct Watch {
+  int* abort;       // shared memory, 0 until a wait of this CTA gives up
+  int* status;      // global error word
+  int code;         // bit raised in *status
+  long long limit;  // SM clock cycles a wait may take
+};
+__device__ __forceinline__ bool aborted(const Watch& w) {
+  return *reinterpret_cast<volatile int*>(w.abort) != 0;
+}
+__device__ __forceinline__ bool wait(const Watch& w, uint64_t* bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (aborted(w)) return false;
+    if (mbar_try(bar, parity)) return true;
+    if (clock64() - t0 > w.limit) {
+      *reinterpret_cast<volatile int*>(w.abort) = 1;
+      atomicOr(w.status, w.code);
+      return false;
+    }
+  }
+}
+// After an abort: waits (bounded, ignoring the abort flag) for a phase that
+// only this thread's own asynchronous work completes -- its TMA copies or
+// its tcgen05.commit -- so nothing is in flight when the CTA frees its
+// shared and tensor memory.
+__device__ __forceinline__ bool drain_wait(uint64_t* bar, uint32_t parity, long long limit) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity))
+    if (clock64() - t0 > limit) return false;
+  return true;
+}
+
 // ---- tensor memory ----
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

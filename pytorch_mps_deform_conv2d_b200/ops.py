@@ -25,6 +25,42 @@ ALGO_SIMT_GEMM = 0x100
 ALGO_SIMT_DIRECT = 0x200
 ALGO_TC_GATHER_WEIGHT = 0x400
 MASK_LOGITS = 0x10000
+# test switch: the tensor-core kernels' waits run out (checks the error word)
+TEST_WAIT_TIMEOUT = 0x1000000
+# bits of the device error word (dcn_device_status)
+STATUS_FWD_WAIT_TIMEOUT = 0x1
+STATUS_BWD_DATA_TIMEOUT = 0x2
+STATUS_BWD_WEIGHT_TIMEOUT = 0x4
+_STATUS_NAMES = {STATUS_FWD_WAIT_TIMEOUT: "forward (fwd_tc)",
+                 STATUS_BWD_DATA_TIMEOUT: "grad-column kernel (bwd_data_tc)",
+                 STATUS_BWD_WEIGHT_TIMEOUT: "weight-gradient kernel"}
+
+
+def device_status(clear: bool = True) -> int:
+    """Error word of the tensor-core kernels on the current CUDA device:
+    a bit per kernel family one of whose bounded waits ran out since the last
+    clearing read (0: none).  Waits for the work already on the current
+    stream; ``clear`` resets the word."""
+    import ctypes
+    stream = torch.cuda.current_stream()
+    status = ctypes.c_int(0)
+    lib = _native.load_capi()
+    rc = lib.dcn_device_status(ctypes.c_void_p(stream.cuda_stream), 1 if clear else 0,
+                               ctypes.byref(status))
+    if rc != 0:
+        raise RuntimeError(_native.capi_error())
+    return int(status.value)
+
+
+def check_device_status() -> None:
+    """Raises RuntimeError when a wait of a tensor-core kernel gave up since
+    the last check (the results of that call are incomplete); clears the
+    error word."""
+    word = device_status(clear=True)
+    if word:
+        names = [n for bit, n in _STATUS_NAMES.items() if word & bit]
+        raise RuntimeError("deform_conv2d: a device wait ran out in the " + ", ".join(names) +
+                           "; the results of that call are incomplete")
 
 _MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32, "3xtf32": MATH_3XTF32}
 _NAMES = {v: k for k, v in _MODES.items()}

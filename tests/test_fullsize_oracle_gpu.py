@@ -1,0 +1,119 @@
+"""The benchmarked workloads at their real sizes against the CPU oracle.
+
+Every configuration the bench measures -- the 8x64x64x64 training step, the
+grouped (groups 32, deformable groups 4) layer, the 2x256x100x152 detection
+neck and the 64x512x28x28 DCNv1 sweep -- runs forward + backward with the
+bench's own seeded inputs (random offsets: N(0, 2^2) .. N(0, 4^2), so many
+taps fall outside the image) through the public API in each math mode, and
+the output and all five gradients are compared with the oracle
+(oracle/dcn_oracle.c, pinned to the reference by tests/golden):
+
+  * fp32 (CUDA cores) and 3xTF32: the reference's per-gradient tolerances
+    (tests/test_backward.py:41-47 of the reference: grad_input 2e-3, the
+    rest 1e-4), applied as max |ours - oracle| <= tol * max(1, max |oracle|)
+    -- relative to the tensor's scale: at these sizes grad_weight sums
+    30400 .. 25088 pixels and reaches magnitudes of several hundred -- and
+    norm-wise;
+  * TF32: outputs within 5e-3 (norm-wise, and every element within
+    5e-3 * max |oracle|); every gradient within 1e-3 norm-wise, and every
+    element within TF32_ELEM[grad] * max |oracle| (the figures measured on a
+    B200, with margin, are in TF32_ELEM).
+"""
+import functools
+
+import numpy as np
+import pytest
+import torch
+
+import bench
+from _util import np_, rel_norm_err
+from pytorch_mps_deform_conv2d_b200 import _native
+from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32, MATH_FP32, MATH_TF32, deform_conv2d_ex
+
+pytestmark = pytest.mark.gpu
+
+NAMES = ("out", "input", "offset", "mask", "weight", "bias")
+FP32_TOL = dict(out=1e-4, input=2e-3, offset=1e-4, mask=1e-4, weight=1e-4, bias=1e-4)
+TF32_OUT = 5e-3
+TF32_GRAD = 1e-3
+# max |ours - oracle| / max |oracle| per gradient in TF32 mode
+TF32_ELEM = dict(input=1e-2, offset=1e-2, mask=1e-2, weight=1e-2, bias=1e-2)
+
+# tensor-core kernels each workload must run in the tensor-core modes (the
+# grouped layer has 2 channels per group: the CUDA-core kernels in every mode)
+TC_KERNELS = {"train": ("fwd_tc", "bwd_data_tc"), "neck": ("fwd_tc", "bwd_data_tc"),
+              "dcnv1": ("fwd_tc", "bwd_data_tc"), "grouped": ()}
+
+
+@functools.lru_cache(maxsize=None)
+def _inputs(name):
+    return bench.make_inputs(bench.WORKLOADS[name])
+
+
+@functools.lru_cache(maxsize=None)
+def _oracle(name):
+    from oracle import oracle
+    wl = bench.WORKLOADS[name]
+    x, w, b, off, m, go = (np_(t) for t in _inputs(name))
+    args = (wl["stride"], wl["pad"], wl["dil"])
+    out = oracle.forward(x, off, w, b, *args, mask=m)
+    gx, goff, gm, gw, gb = oracle.backward(go, x, off, w, b, *args, mask=m)
+    return dict(out=out, input=gx, offset=goff, mask=gm, weight=gw, bias=gb)
+
+
+def _ours(name, flags):
+    wl = bench.WORKLOADS[name]
+    x, w, b, off, m, go = _inputs(name)
+    leaves = [None if t is None else t.cuda().requires_grad_(True) for t in (x, w, b, off, m)]
+    xd, wd, bd, od, md = leaves
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out = deform_conv2d_ex(xd, od, wd, bd, wl["stride"], wl["pad"], wl["dil"], md,
+                               flags=flags)
+        out.backward(go.cuda())
+        torch.cuda.synchronize()
+    finally:
+        _native.profiler_enable(False)
+    kernels = _native.profiler_read()
+    got = dict(out=np_(out), input=np_(xd.grad), offset=np_(od.grad), weight=np_(wd.grad),
+               mask=np_(md.grad) if md is not None else None,
+               bias=np_(bd.grad) if bd is not None else None)
+    return got, kernels
+
+
+def _errors(got, ref):
+    """name -> (norm-wise rel err, max err / max(1, max|ref|), max err / max|ref|)."""
+    res = {}
+    for k in NAMES:
+        if ref[k] is None:
+            assert got[k] is None, k
+            continue
+        g, r = got[k].astype(np.float64), ref[k].astype(np.float64)
+        assert g.shape == r.shape, (k, g.shape, r.shape)
+        d = np.abs(g - r).max()
+        amax = np.abs(r).max()
+        res[k] = (rel_norm_err(g, r), d / max(1.0, amax), d / max(1e-30, amax))
+    return res
+
+
+@pytest.mark.parametrize("mode", ["fp32", "3xtf32", "tf32"])
+@pytest.mark.parametrize("name", ["train", "grouped", "neck", "dcnv1"])
+def test_workload_matches_oracle(cuda_device, name, mode):
+    flags = {"fp32": MATH_FP32, "3xtf32": MATH_3XTF32, "tf32": MATH_TF32}[mode]
+    got, kernels = _ours(name, flags)
+    errs = _errors(got, _oracle(name))
+    print(f"\nPARITY {name} {mode} " + " ".join(
+        f"{k}:norm={e[0]:.2e},scaled={e[1]:.2e},elem={e[2]:.2e}" for k, e in errs.items()))
+    if mode != "fp32":
+        for kern in TC_KERNELS[name]:
+            assert kern in kernels, f"{kern} did not run: {sorted(kernels)}"
+    for k, (norm, scaled, elem) in errs.items():
+        if mode == "tf32":
+            if k == "out":
+                assert norm <= TF32_OUT and elem <= TF32_OUT, (k, errs[k])
+            else:
+                assert norm <= TF32_GRAD, (k, errs[k])
+                assert elem <= TF32_ELEM[k], (k, errs[k])
+        else:
+            assert scaled <= FP32_TOL[k] and norm <= FP32_TOL[k], (k, errs[k])

@@ -45,7 +45,7 @@ def _shape(case):
         groups=x.shape[1] // w.shape[1], deformable_groups=case["off"].shape[1] // (2 * k))
 
 
-def _both(lib, case, dev, flags=0):
+def _both(lib, case, dev, flags=0, calls=1):
     d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
     s = _shape(case)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -55,12 +55,17 @@ def _both(lib, case, dev, flags=0):
     rc = lib.dcn_forward(ctypes.byref(s), _p(d["x"]), _p(d["w"]), _p(d["off"]), _p(d["m"]),
                          _p(d["b"]), _p(want), flags, _p(ws), nbytes, stream)
     assert rc == 0, _native.capi_error()
-    got = torch.full(case["go"].shape, float("nan"), device=dev)
-    rc = lib.dcn_forward_noalloc(ctypes.byref(s), _p(d["x"]), _p(d["w"]), _p(d["off"]),
-                                 _p(d["m"]), _p(d["b"]), _p(got), flags, stream)
-    assert rc == 0, _native.capi_error()
+    gots = []
+    for _ in range(calls):
+        got = torch.full(case["go"].shape, float("nan"), device=dev)
+        rc = lib.dcn_forward_noalloc(ctypes.byref(s), _p(d["x"]), _p(d["w"]), _p(d["off"]),
+                                     _p(d["m"]), _p(d["b"]), _p(got), flags, stream)
+        assert rc == 0, _native.capi_error()
+        gots.append(got)
     torch.cuda.synchronize()
-    return got.cpu().numpy(), want.cpu().numpy()
+    if calls == 1:
+        return gots[0].cpu().numpy(), want.cpu().numpy()
+    return [g.cpu().numpy() for g in gots], want.cpu().numpy()
 
 
 def test_noalloc_matches_forward_two_calls_in_a_row(cuda_device):
@@ -71,6 +76,32 @@ def test_noalloc_matches_forward_two_calls_in_a_row(cuda_device):
     for case in cases:
         got, want = _both(lib, case, cuda_device)
         scale = max(1.0, float(np.abs(want).max()))
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * scale)
+
+
+# Tensor-core forward through the built-in array: its TMA tensor map is built
+# over the array (the packed weight lives there, high and low TF32 parts in
+# 3xTF32), and 168 tiles of 128 pixels on 148 SMs leave a last round of 20
+# tiles, which the forward splits over the SMs with counters and partial sums
+# kept in the rest of the array.  Two calls in a row: the second one shows
+# that the counters start from zero again.
+@pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
+def test_noalloc_tensor_core_split_round_two_calls(cuda_device, mode):
+    from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32, MATH_TF32
+    flags = MATH_TF32 if mode == "tf32" else MATH_3XTF32
+    lib = _lib()
+    case = make_case(N=1, inC=32, outC=32, H=128, W=168, offset_scale=2.0,
+                     mask_kind="sigmoid", seed=4)
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        gots, want = _both(lib, case, cuda_device, flags=flags, calls=2)
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    assert stats.get("fwd_tc", (0, 0.0))[0] == 3, sorted(stats)  # dcn_forward + two calls
+    scale = max(1.0, float(np.abs(want).max()))
+    for got in gots:
         np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * scale)
 
 
