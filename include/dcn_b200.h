@@ -68,16 +68,25 @@ extern "C" {
  *                  close to fp32 accuracy at tensor-core speed.
  * The second byte can pin a kernel family (0 = automatic):
  *   DCN_ALGO_SIMT_GEMM / DCN_ALGO_SIMT_DIRECT  fp32 CUDA-core kernels (tests);
- *   DCN_ALGO_TC_GATHER_WEIGHT  tensor-core backward without the column buffer:
- *                  the weight gradient re-gathers its columns, so the backward
- *                  workspace drops kernel_h*kernel_w*N*Ho*Wo*C floats (x2 in
- *                  3xTF32) at some speed. */
+ *   DCN_ALGO_TC_GATHER_WEIGHT  tensor-core backward without the column buffer
+ *                  where the fused kernel does not run (3xTF32, more than 256
+ *                  out channels a group): the weight gradient re-gathers its
+ *                  columns, so the backward workspace drops
+ *                  kernel_h*kernel_w*N*Ho*Wo*C floats (x2 in 3xTF32) at some
+ *                  speed. */
 #define DCN_MATH_FP32 0x0
 #define DCN_MATH_TF32 0x1
 #define DCN_MATH_3XTF32 0x2
 #define DCN_ALGO_SIMT_GEMM 0x100
 #define DCN_ALGO_SIMT_DIRECT 0x200
 #define DCN_ALGO_TC_GATHER_WEIGHT 0x400
+/*   DCN_ALGO_TC_COLUMN_BUFFER  TF32 backward through the column buffer (the
+ *                  grad-column kernel writes the sampled columns, a dense GEMM
+ *                  reads them for the weight gradient) instead of the fused
+ *                  kernel that keeps them on chip; for comparisons.  (3xTF32,
+ *                  and groups with more than 256 out channels, always take
+ *                  the column buffer.) */
+#define DCN_ALGO_TC_COLUMN_BUFFER 0x800
 /* Third byte: operand conventions.
  *   DCN_MASK_LOGITS  `mask` holds logits: the kernels use sigmoid(mask) and
  *                    dcn_backward's grad_mask is the gradient with respect to

@@ -1245,6 +1245,501 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
   return w;
 }
 
+// ---------------------------------------------------------------------------
+// bwd_fused_tc: the whole TF32 tensor-core backward of one (pixel tile,
+// slot) in one persistent kernel, for out channels per group <= 256:
+//   GEMM1  gcol[q, r] = sum_o go[q, o] W[o, r]                      (.mm:820-821)
+//          q = 128 pixels (four 32-pixel blocks, one per tensor-memory lane
+//          quarter), r = a 128-row slot of the group's (tap, channel) rows,
+//          as in bwd_data_tc;
+//   epilogue (16 warps, one per (32-pixel block, 32-channel chunk) of the
+//          tile): as epilogue_chunk -- col2im with 16-byte vector reductions
+//          (deform_conv2d.metal:141-204), the coordinate / mask gradients
+//          from four per-corner sums (deform_conv2d.metal:225-295) -- except
+//          that the sampled column values mask * bilinear(x) (TF32) go to a
+//          shared-memory column tile, laid out as the MN-major operand of
+//   GEMM2  gW[r, o] += sum_q col[q, r] go[q, o]                      (.mm:842-880)
+//          A = the column tile, B = go_r rows (K-major), accumulated in
+//          tensor memory over all of the CTA's tiles of the slot and reduced
+//          into the tap-major grad_weight copy once per slot.
+// The columns never leave the SM, and there is no column buffer in HBM.  A
+// warp's 4 KB block of the column tile (32 pixel rows x 32 channels in the
+// 32-byte-atom swizzle) also serves as its transpose buffer: the grad-column
+// rows are written there, read by the gather and the scatter, and then
+// overwritten by the column values of the same pixels.
+// Work items are (slot, pixel tile) in slot-major order, cut into one
+// contiguous range per CTA, so a CTA's items share one or two slots and the
+// weight-gradient accumulator is drained once or twice.
+//   warp 0      TMA producer: per item, the GEMM1 stages of bwd_data_tc and,
+//               one item behind, 4 GEMM2 stages (Og rows x 32 pixels of go_r)
+//   warp 1      MMA issue: GEMM1 of item i, then GEMM2 of item i - 1
+//   warps 2-17  epilogue
+// Shared memory: 3 ring stages of 32 KB (both GEMMs), the 64 KB column tile,
+// the sampling plans (2 KB a warp), barriers.  Tensor memory: two 128-column
+// GEMM1 accumulators and the GEMM2 accumulator (Og <= 256 columns).
+// ---------------------------------------------------------------------------
+constexpr int F_TMA_WARP = 0, F_MMA_WARP = 1, F_EPI_WARP0 = 2, F_EPI_WARPS = 16;
+constexpr int F_THREADS = (F_EPI_WARP0 + F_EPI_WARPS) * 32;  // 576
+constexpr int F_STAGES = 3;
+constexpr int F_STAGE = 32768;        // GEMM1: go 16 KB + W 16 KB; GEMM2: go Og x 128 B
+constexpr int F_COL = 4 * 16384;      // the column tile
+constexpr int F_PLANS = F_EPI_WARPS * 32 * (int)sizeof(PixPlan);
+constexpr int F_BAR_BYTES = 256;
+
+size_t fused_smem_bytes() { return (size_t)F_STAGES * F_STAGE + F_COL + F_PLANS + F_BAR_BYTES + 1024; }
+
+struct FItem {
+  int gi, sl, mt;
+};
+__device__ __forceinline__ FItem fitem(long long u, int mtiles, int nslots) {
+  FItem it;
+  it.mt = (int)(u % mtiles);
+  const long long r = u / mtiles;
+  it.sl = (int)(r % nslots);
+  it.gi = (int)(r / nslots);
+  return it;
+}
+
+// Image, go_r row and first-pixel coordinate of each 32-pixel block of a
+// tile (a block past the last image reads past the row end: zero fill).
+__device__ __forceinline__ void fblocks(const Geom& g, const FItem& it, int bpi, int nblocks,
+                                        int (&arow)[4], int (&ax)[4]) {
+#pragma unroll
+  for (int mb = 0; mb < 4; ++mb) {
+    const int b = it.mt * 4 + mb;
+    const int n = b < nblocks ? b / bpi : 0;
+    arow[mb] = n * g.outC + it.gi * g.Og;
+    ax[mb] = b < nblocks ? (b - n * bpi) * 32 : bpi * 32;
+  }
+}
+
+// Byte offset of channels 8 * gran .. 8 * gran + 7 (the 32-byte granule
+// `gran`, + 16 for its upper half) of pixel row `px` in a warp's 4 KB block:
+// the MN-major, 32-byte-atom swizzled layout of a tcgen05 TF32 operand (K
+// row px of 128 bytes, granule position gran ^ (px % 4), rows grouped by 4
+// at W_SBO).
+__device__ __forceinline__ uint32_t cblk(int px, int gran) {
+  return (uint32_t)((px >> 2) * W_SBO + (px & 3) * 128 + (((gran ^ px) & 3) << 5));
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// One epilogue warp, one item: 32 pixel rows (tensor-memory lane quarter) x
+// 32 channels of tap k.  As epilogue_chunk, with the warp's column block `tb`
+// as the transpose buffer and the column values stored there at the end of
+// each group of 8 pixels, once the gather and the scatter of those pixels
+// have read their grad-column rows.
+__device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const float (&vals)[32],
+                                            int gch0, long long row_q, long long qend, int lane,
+                                            uint32_t tb, PixPlan* plan,
+                                            const float* __restrict__ xt,
+                                            const float* __restrict__ off,
+                                            const float* __restrict__ mask,
+                                            float* __restrict__ gxt, float* __restrict__ goff,
+                                            float* __restrict__ gmask) {
+  const int quad = lane & 3, sub = lane >> 2;
+  const int zoff = g.N * g.HW * g.C;
+  {  // this lane's pixel row into the block, 16 bytes at a time
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      tc::st_shared_v4(tb + cblk(lane, j >> 1) + ((j & 1) << 4), vals[4 * j], vals[4 * j + 1],
+                       vals[4 * j + 2], vals[4 * j + 3]);
+  }
+  __syncwarp();
+  const float* xq = xt + gch0 + quad * 8;  // corner loads: channels 8 quad .. 8 quad + 7
+#pragma unroll 2
+  for (int i = 0; i < 4; ++i) {
+    const int px = i * 8 + sub;
+    const PixPlan pl = plan[px];
+    const bool live = pl.idx.x >= 0;
+    const float m = pl.geo.z;
+    const float mw[4] = {m * pl.w.x, m * pl.w.y, m * pl.w.z, m * pl.w.w};
+    float d1 = 0.f, d2 = 0.f, d3 = 0.f, d4 = 0.f;
+    float cv[8];  // column values (mask * bilinear)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cv[e] = 0.f;
+    if (live) {
+      const float4 ga = ld_shared_f4(tb + cblk(px, quad));
+      const float4 gb = ld_shared_f4(tb + cblk(px, quad) + 16);
+      const float gc[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      float a[8], b[8], c[8], d[8];
+      ldg_f8(xq + (unsigned)pl.cidx.x, a);  // dropped corners: zero row
+      ldg_f8(xq + (unsigned)pl.cidx.y, b);
+      ldg_f8(xq + (unsigned)pl.cidx.z, c);
+      ldg_f8(xq + (unsigned)pl.cidx.w, d);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        d1 = fmaf(gc[e], a[e], d1);
+        d2 = fmaf(gc[e], b[e], d2);
+        d3 = fmaf(gc[e], c[e], d3);
+        d4 = fmaf(gc[e], d[e], d4);
+        cv[e] = mw[0] * a[e] + mw[1] * b[e] + mw[2] * c[e] + mw[3] * d[e];
+      }
+    }
+    // the four sums over the pixel's 4 lanes; lanes 0, 1, 2 of the pixel
+    // reduce d/dh, d/dw, d/dm into memory
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+    d2 += __shfl_xor_sync(0xffffffffu, d2, 1);
+    d3 += __shfl_xor_sync(0xffffffffu, d3, 1);
+    d4 += __shfl_xor_sync(0xffffffffu, d4, 1);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+    d2 += __shfl_xor_sync(0xffffffffu, d2, 2);
+    d3 += __shfl_xor_sync(0xffffffffu, d3, 2);
+    d4 += __shfl_xor_sync(0xffffffffu, d4, 2);
+    {
+      const float dh = m * ((1.f - pl.geo.y) * (d3 - d1) + pl.geo.y * (d4 - d2));
+      const float dw = m * ((1.f - pl.geo.x) * (d2 - d1) + pl.geo.x * (d4 - d3));
+      const float dm = (pl.w.x * d1 + pl.w.y * d2 + pl.w.z * d3 + pl.w.w * d4) *
+                       mask_grad_scale(g, m);
+      const float v = quad == 0 ? dh : (quad == 1 ? dw : dm);
+      float* dst = quad == 2 ? gmask + (live ? pl.idx.y : 0)
+                             : goff + (live ? pl.idx.x : 0) + (quad == 1 ? g.P : 0);
+      red_add_f32_if(live && quad < (g.use_mask ? 3 : 2), dst, v);
+    }
+    // col2im: 8 lanes per pixel, 4 channels each (each quarter warp's 16-byte
+    // reductions fill one pixel's 128-byte line); lanes L and L ^ 4 hold the
+    // plans of the pixel pair (i * 8 + 2 (sub / 2), + 1) that lanes
+    // L & ~7 .. L | 7 reduce
+    const int oc[4] = {__shfl_xor_sync(0xffffffffu, pl.cidx.x, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.y, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.z, 4),
+                       __shfl_xor_sync(0xffffffffu, pl.cidx.w, 4)};
+    const float omw[4] = {__shfl_xor_sync(0xffffffffu, mw[0], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[1], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[2], 4),
+                          __shfl_xor_sync(0xffffffffu, mw[3], 4)};
+    const bool olive = __shfl_xor_sync(0xffffffffu, (int)live, 4) != 0;
+    const int j = lane & 7;
+    float* gq = gxt + gch0 + j * 4;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const bool own = h == (sub & 1);
+      const bool hl = own ? live : olive;
+      const int rp = i * 8 + (sub & ~1) + h;
+      const float4 g4 = ld_shared_f4(tb + cblk(rp, j >> 1) + ((j & 1) << 4));
+      const int cis[4] = {own ? pl.cidx.x : oc[0], own ? pl.cidx.y : oc[1],
+                          own ? pl.cidx.z : oc[2], own ? pl.cidx.w : oc[3]};
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        // dropped corners (the zero row) and void samples are not reduced
+        const bool on = hl && cis[cc] != zoff;
+        const float wc = own ? mw[cc] : omw[cc];
+        red_add_v4_if(on, gq + (unsigned)(on ? cis[cc] : 0), wc * g4.x, wc * g4.y, wc * g4.z,
+                      wc * g4.w);
+      }
+    }
+    // the grad-column rows of these 8 pixels are read: their column values
+    // take their place (TF32-rounded; 0 for void samples and past the image)
+    __syncwarp();
+    tc::st_shared_v4(tb + cblk(px, quad), tc::to_tf32(cv[0]), tc::to_tf32(cv[1]),
+                     tc::to_tf32(cv[2]), tc::to_tf32(cv[3]));
+    tc::st_shared_v4(tb + cblk(px, quad) + 16, tc::to_tf32(cv[4]), tc::to_tf32(cv[5]),
+                     tc::to_tf32(cv[6]), tc::to_tf32(cv[7]));
+  }
+  (void)row_q;
+  (void)qend;
+  (void)k;
+  (void)dgi;
+  (void)off;
+  (void)mask;
+}
+
+__global__ void __launch_bounds__(F_THREADS, 1)
+bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
+                    const __grid_constant__ CUtensorMap bmap,
+                    const __grid_constant__ CUtensorMap g2map, int bpi, int nblocks, int mtiles,
+                    int nslots, long long nitems, const float* __restrict__ xt,
+                    const float* __restrict__ off, const float* __restrict__ mask,
+                    float* __restrict__ gxt, float* __restrict__ goff,
+                    float* __restrict__ gmask, float* __restrict__ gwt) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw_u32 = tc::smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
+  const uint32_t ring = tc::smem_u32(smem);
+  const uint32_t colt = ring + F_STAGES * F_STAGE;
+  PixPlan* plans = reinterpret_cast<PixPlan*>(smem + F_STAGES * F_STAGE + F_COL);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + F_STAGES * F_STAGE + F_COL + F_PLANS);
+  uint64_t* empty = full + F_STAGES;
+  uint64_t* acc_full = empty + F_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* col_full = acc_empty + 2;   // per 32-pixel K block: its 4 epilogue warps wrote it
+  uint64_t* col_empty = col_full + 4;   // per K block: GEMM2 has read it
+  uint64_t* acc2_full = col_empty + 4;
+  uint64_t* acc2_empty = acc2_full + 1;
+  uint64_t* drain = acc2_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const tc::Watch watch{abort_flag, &g_tc_bwd_status, kStatusBwdData | kStatusBwdWeight,
+                        g.wait_limit};
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // 32-out-channel K steps of GEMM1; a partial last one reads zero weights
+  // past Og (the weight map ends there), so the go_r rows it loads add nothing
+  const int ochunks = (g.Og + 31) >> 5;
+  // this CTA's items [u0, u0 + n) in slot-major order
+  const long long u0 = (long long)blockIdx.x * nitems / gridDim.x;
+  const int n = (int)((long long)(blockIdx.x + 1) * nitems / gridDim.x - u0);
+  auto seg_of = [&](int i) { return (u0 + i) / mtiles; };  // (group, slot) of item i
+
+  if (tid == 0) {
+    for (int s = 0; s < F_STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&acc_full[a], 1);
+      tc::mbar_init(&acc_empty[a], F_EPI_WARPS);
+    }
+    for (int q = 0; q < 4; ++q) {
+      tc::mbar_init(&col_full[q], 4);
+      tc::mbar_init(&col_empty[q], 1);
+    }
+    tc::mbar_init(acc2_full, 1);
+    tc::mbar_init(acc2_empty, F_EPI_WARPS);
+    tc::mbar_init(drain, 1);
+    *abort_flag = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == F_MMA_WARP) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == F_TMA_WARP) {
+    if (lane == 0 && !g.no_async) {
+      int gs = 0;  // stages filled so far
+      [&]() {
+        auto acquire = [&]() -> int {  // next ring stage, once the GEMMs have read it
+          const int st = gs % F_STAGES, u = gs / F_STAGES;
+          if (u > 0 && !tc::wait(watch, &empty[st], (u - 1) & 1)) return -1;
+          return st;
+        };
+        int arow[4], ax[4];
+        for (int i = 0; i <= n; ++i) {
+          if (i < n) {  // GEMM1 of item i: go_r blocks (MN-major) and W slot rows
+            const FItem it = fitem(u0 + i, mtiles, nslots);
+            fblocks(g, it, bpi, nblocks, arow, ax);
+            const int brow = it.gi * g.kk * g.Cg + it.sl * 128;
+            for (int s = 0; s < ochunks; ++s, ++gs) {
+              const int st = acquire();
+              if (st < 0) return;
+              const uint32_t sA = ring + st * F_STAGE;
+              tc::mbar_arrive_expect_tx(&full[st], F_STAGE);
+#pragma unroll
+              for (int mb = 0; mb < 4; ++mb)
+                tc::tma_load_2d(sA + mb * W_LBO, &amap, ax[mb], arow[mb] + s * 32, &full[st]);
+              tc::tma_load_2d(sA + 16384, &bmap, s * 32, brow, &full[st]);
+            }
+          }
+          if (i >= 1) {  // GEMM2 of item i - 1: go_r rows of each 32-pixel block
+            const FItem it = fitem(u0 + i - 1, mtiles, nslots);
+            fblocks(g, it, bpi, nblocks, arow, ax);
+            for (int pq = 0; pq < 4; ++pq, ++gs) {
+              const int st = acquire();
+              if (st < 0) return;
+              tc::mbar_arrive_expect_tx(&full[st], (uint32_t)g.Og * 128);
+              tc::tma_load_2d(ring + st * F_STAGE, &g2map, ax[pq], arow[pq], &full[st]);
+            }
+          }
+        }
+      }();
+      if (tc::aborted(watch))  // the copies of the last stages land before exit
+        for (int i = gs > F_STAGES ? gs - F_STAGES : 0; i < gs; ++i)
+          tc::drain_wait(&full[i % F_STAGES], (i / F_STAGES) & 1, g.wait_limit);
+    }
+    __syncwarp();
+  } else if (warp == F_MMA_WARP) {
+    if (lane == 0) {
+      // GEMM1: A = go_r pixels (MN-major), B = W slot rows (K-major)
+      const uint32_t idesc1 = idesc_tf32_amn(128, 128);
+      // GEMM2: A = column tile (MN-major: channels contiguous), B = go_r rows (K-major)
+      const uint32_t idesc2 = idesc_tf32_amn(128, g.Og);
+      int gs = 0, segs = 0;
+      [&]() {
+        for (int i = 0; i <= n; ++i) {
+          if (i < n) {
+            const int acc = i & 1;
+            if (i >= 2 && !tc::wait(watch, &acc_empty[acc], ((i >> 1) - 1) & 1)) return;
+            tc::tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(acc * 128);
+            for (int s = 0; s < ochunks; ++s, ++gs) {
+              const int st = gs % F_STAGES;
+              if (!tc::wait(watch, &full[st], (gs / F_STAGES) & 1)) return;
+              tc::tc_fence_after();
+              const uint32_t sA = ring + st * F_STAGE, sB = sA + 16384;
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
+                              idesc1, (s | j) != 0 ? 1u : 0u);
+              tc::umma_commit(&empty[st]);
+            }
+            tc::umma_commit(&acc_full[acc]);
+          }
+          if (i >= 1) {
+            const int p = i - 1;
+            const bool first = p == 0 || seg_of(p) != seg_of(p - 1);
+            const bool last = p == n - 1 || seg_of(p + 1) != seg_of(p);
+            // the previous slot's accumulator has been drained
+            if (first && segs > 0 && !tc::wait(watch, acc2_empty, (segs - 1) & 1)) return;
+            tc::tc_fence_after();
+            const uint32_t d2 = tmem + 256u;
+            for (int pq = 0; pq < 4; ++pq, ++gs) {
+              const int st = gs % F_STAGES;
+              if (!tc::wait(watch, &col_full[pq], p & 1) ||
+                  !tc::wait(watch, &full[st], (gs / F_STAGES) & 1))
+                return;
+              tc::tc_fence_after();
+              const uint32_t sB = ring + st * F_STAGE, sA = colt + pq * 16384;
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                tc::umma_tf32(d2, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
+                              idesc2, (first && pq == 0 && j == 0) ? 0u : 1u);
+              tc::umma_commit(&empty[st]);
+              tc::umma_commit(&col_empty[pq]);
+            }
+            if (last) {
+              tc::umma_commit(acc2_full);
+              ++segs;
+            }
+          }
+        }
+      }();
+      if (tc::aborted(watch)) {  // every UMMA issued so far completes before exit
+        tc::umma_commit(drain);
+        tc::drain_wait(drain, 0, g.wait_limit);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    const int e = warp - F_EPI_WARP0;
+    const int lq = warp & 3;     // tensor-memory lane quarter: 32-pixel block of the tile
+    const int chunk = e >> 2;    // 32-channel chunk of the slot
+    PixPlan* plan = plans + e * 32;
+    const uint32_t tb = colt + lq * 16384 + chunk * W_LBO;  // this warp's 4 KB block
+    const int zoff = g.N * g.HW * g.C;
+    int segs = 0;
+    [&]() {
+      for (int i = 0; i < n; ++i) {
+        const FItem it = fitem(u0 + i, mtiles, nslots);
+        const int acc = i & 1;
+        const int b = it.mt * 4 + lq;
+        const int bimg = b < nblocks ? b / bpi : 0;
+        const long long qbase = b < nblocks ? (long long)bimg * g.P + (long long)(b - bimg * bpi) * 32 : 0;
+        const long long qend = b < nblocks ? (long long)bimg * g.P + g.P : 0;
+        const long long row_q = qbase + lane;
+        const int row = it.sl * 128 + chunk * 32;  // (tap, channel) row within the group
+        const int k = row / g.Cg;
+        const bool rows_ok = k < g.kk;
+        const int gch0 = it.gi * g.Cg + (row - k * g.Cg);
+        const int dgi = gch0 / g.cpg;
+        if (!tc::wait(watch, &acc_full[acc], (i >> 1) & 1)) return;
+        tc::tc_fence_after();
+        float vals[32];
+        {
+          const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(acc * 128 + chunk * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float tv[8];
+            tc::tmem_ld8(ta + 8 * j, tv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) vals[8 * j + q] = tv[q];
+          }
+          tc::tmem_ld_wait();
+        }
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);  // the accumulator is free for item i + 2
+        {  // sampling plan of this lane's pixel for (tap k, deformable group dgi)
+          PixPlan pl;
+          pl.cidx = make_int4(zoff, zoff, zoff, zoff);
+          pl.w = make_float4(0.f, 0.f, 0.f, 0.f);
+          pl.geo = make_float4(0.f, 0.f, 0.f, 0.f);
+          pl.idx = make_int4(-1, 0, 0, 0);
+          if (rows_ok && row_q < qend) {
+            const int ni = (int)(row_q / g.P);
+            const int p = (int)(row_q - (long long)ni * g.P);
+            const int oy = p / g.Wo, ox = p - oy * g.Wo;
+            const int ki = k / g.kw, kj = k - ki * g.kw;
+            const long long oi = off_h_index(g, ni, dgi, k, p);
+            float h, w;
+            sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+            const Sample sp = make_sample(h, w, g.H, g.W);
+            if (sp.valid) {
+              const int nb = ni * g.HW;
+              pl.cidx.x = (sp.live & 1u) ? (nb + sp.i1) * g.C : zoff;
+              pl.cidx.y = (sp.live & 2u) ? (nb + sp.i2) * g.C : zoff;
+              pl.cidx.z = (sp.live & 4u) ? (nb + sp.i3) * g.C : zoff;
+              pl.cidx.w = (sp.live & 8u) ? (nb + sp.i4) * g.C : zoff;
+              pl.w = make_float4(sp.w1, sp.w2, sp.w3, sp.w4);
+              const long long mi = mask_index(g, ni, dgi, k, p);
+              pl.geo = make_float4(sp.lh, sp.lw, mask_of(g, mask, mi), 0.f);
+              pl.idx = make_int4((int)oi, (int)mi, 0, 0);
+            }
+          }
+          plan[lane] = pl;
+        }
+        // GEMM2 of the previous item has read this block of the column tile
+        if (i >= 1 && !tc::wait(watch, &col_empty[lq], (i - 1) & 1)) return;
+        if (rows_ok) {
+          fused_chunk(g, k, dgi, vals, gch0, row_q, qend, lane, tb, plan, xt, off, mask, gxt,
+                      goff, gmask);
+        } else {  // rows past the group's last tap: zero columns
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            tc::st_shared_v4(tb + cblk(lane, j >> 1) + ((j & 1) << 4), 0.f, 0.f, 0.f, 0.f);
+        }
+        // the column block is complete: visible to the tensor core
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&col_full[lq]);
+        if (i == n - 1 || seg_of(i + 1) != seg_of(i)) {
+          // the slot's weight gradient: tensor-memory lanes are its rows,
+          // columns its out channels; this warp drains 64 of them into the
+          // tap-major copy [o][k][c] (a warp's 32 rows: one 128-byte line)
+          if (!tc::wait(watch, acc2_full, segs & 1)) return;
+          tc::tc_fence_after();
+          const int r = it.sl * 128 + lq * 32 + lane;
+          const int kr = r / g.Cg, cr = r - kr * g.Cg;
+          float* dst = gwt + (long long)(it.gi * g.Og) * g.kk * g.Cg + (long long)kr * g.Cg + cr;
+          const long long ostride = (long long)g.kk * g.Cg;
+          const uint32_t t2 = tmem + ((uint32_t)(lq * 32) << 16) + 256u;
+          for (int cb = chunk * 64; cb < chunk * 64 + 64 && cb < g.Og; cb += 8) {
+            float vv[8];
+            tc::tmem_ld8(t2 + (uint32_t)cb, vv);
+            tc::tmem_ld_wait();
+            if (kr < g.kk) {
+#pragma unroll
+              for (int x = 0; x < 8; ++x) red_add_f32(dst + (long long)(cb + x) * ostride, vv[x]);
+            }
+          }
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(acc2_empty);
+          ++segs;
+        }
+      }
+    }();
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == F_MMA_WARP) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace
 
 cudaError_t read_bwd_status(int* status, bool clear, cudaStream_t stream) {
@@ -1400,6 +1895,47 @@ cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 16) blocks = 148LL * 16;
   weight_from_tap_major_kernel<<<(int)blocks, 256, 0, stream>>>(gwt, gw, g.Cg, g.kk, total);
+  return cudaGetLastError();
+}
+
+bool tc_fused_supported(const Geom& g) {
+  return tc_bwd_supported(g) && g.Og <= 256 && (long long)g.G * weight_slots(g) *
+                                                  (((long long)g.N * ((g.P + 31) / 32) + 3) / 4) <
+                                                  (1LL << 40);
+}
+
+cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* wbt,
+                                const float* xt, const float* off, const float* mask, float* gxt,
+                                float* goff, float* gmask, float* gwt, int num_sms,
+                                cudaStream_t stream) {
+  if (!tc_fused_supported(g)) return cudaErrorInvalidValue;
+  const int Ppad = (g.P + 3) & ~3;
+  CUtensorMap amap, bmap, g2map;
+  // go_r rows of P pixels: 32-pixel x 32-row boxes (GEMM1's A, MN-major) and
+  // 32-pixel x Og-row boxes (GEMM2's B, K-major); pixels past P read as zero
+  cudaError_t e = make_tmap_2d_f32(&amap, go_r, (uint64_t)g.P, (uint64_t)g.N * g.outC,
+                                   (uint64_t)Ppad, 32u, /*atom32=*/true);
+  if (e != cudaSuccess) return e;
+  // packed W: rows of (tap, channel), Og out channels each; 128-row boxes
+  e = make_tmap_2d_f32(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg, (uint64_t)g.Og,
+                       128u);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_2d_f32(&g2map, go_r, (uint64_t)g.P, (uint64_t)g.N * g.outC, (uint64_t)Ppad,
+                       (uint32_t)g.Og);
+  if (e != cudaSuccess) return e;
+  const size_t smem = fused_smem_bytes();
+  e = ensure_dynamic_smem(reinterpret_cast<const void*>(bwd_fused_tc_kernel), (int)smem);
+  if (e != cudaSuccess) return e;
+  const int bpi = (g.P + 31) / 32;  // 32-pixel blocks per image
+  if ((long long)g.N * bpi > (1LL << 30)) return cudaErrorInvalidValue;
+  const int nblocks = g.N * bpi;
+  const int mtiles = (nblocks + 3) / 4;
+  const int nslots = weight_slots(g);
+  const long long nitems = (long long)g.G * nslots * mtiles;
+  const int grid = (int)(nitems < num_sms ? nitems : num_sms);
+  bwd_fused_tc_kernel<<<grid, F_THREADS, smem, stream>>>(g, amap, bmap, g2map, bpi, nblocks,
+                                                         mtiles, nslots, nitems, xt, off, mask,
+                                                         gxt, goff, gmask, gwt);
   return cudaGetLastError();
 }
 

@@ -310,17 +310,28 @@ size_t fwd_tail_ws(const dcn::Geom& g, uint32_t flags) {
 
 size_t fwd_ws(const dcn::Geom& g, uint32_t flags) { return fwd_ws_min(g, flags) + fwd_tail_ws(g, flags); }
 
+// The fused tensor-core backward (grad columns, col2im, col2im_coord and the
+// weight gradient in one kernel, no column buffer): TF32 with out channels
+// per group <= 256, unless a weight-gradient route is pinned.
+bool use_fused_bwd(const dcn::Geom& g, uint32_t flags) {
+  return (flags & 0xff) == DCN_MATH_TF32 &&
+         !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT | DCN_ALGO_TC_GATHER_WEIGHT |
+                    DCN_ALGO_TC_COLUMN_BUFFER)) &&
+         dcn::tc_fused_supported(g);
+}
+
 // Tensor-core backward with the column buffer (weight gradient as a dense
 // GEMM over the columns the grad-column kernel writes); DCN_ALGO_TC_GATHER_WEIGHT
 // asks for the gather-based weight gradient where that kernel covers the shape.
 bool use_col_path(const dcn::Geom& g, uint32_t flags) {
-  return dcn::tc_wcol_supported(g, split_math(flags)) &&
+  return !use_fused_bwd(g, flags) && dcn::tc_wcol_supported(g, split_math(flags)) &&
          (!(flags & DCN_ALGO_TC_GATHER_WEIGHT) || !dcn::tc_wgather_supported(g));
 }
 
 bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
   return tc_math(flags) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT)) &&
-         dcn::tc_bwd_supported(g) && (use_col_path(g, flags) || dcn::tc_wgather_supported(g));
+         dcn::tc_bwd_supported(g) &&
+         (use_fused_bwd(g, flags) || use_col_path(g, flags) || dcn::tc_wgather_supported(g));
 }
 
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
@@ -334,7 +345,7 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
     b += align_up((size_t)g.outC * g.Cg * g.kk * sizeof(float));               // tap-major grad_weight
     if (use_col_path(g, flags))
       b += align_up(dcn::tc_col_bytes(g, split_math(flags)));                  // column buffer
-    else
+    else if (!use_fused_bwd(g, flags))
       b += align_up(dcn::tc_plan_bytes(g));                                    // sampling plans
   } else {
     b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
@@ -752,6 +763,25 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
+    if (use_fused_bwd(g, flags)) {
+      DCN_CUDA(dcn::launch_bwd_fused_tc(g, go_r, wbt, xt, offset, mask, gxt, grad_offset,
+                                        grad_mask, gwt, num_sms_current(), stream),
+               "bwd_fused_tc");
+      if (nhwc) {
+        DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+                 "grad_weight_layout");
+        return DCN_OK;
+      }
+      // grad_input back to NCHW (side 0) beside the grad_weight layout
+      DCN_ORDER(fk.fork(), "fork");
+      DCN_CUDA_ON(fk.side(0),
+                  dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
+                  "nhwc_to_nchw");
+      DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
+               "grad_weight_layout");
+      DCN_ORDER(fk.join(0), "join");
+      return DCN_OK;
+    }
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_r, split, wbt, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, col, stream),
              "bwd_data_tc");

@@ -80,6 +80,16 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, const float* wbt,
                                const float* xt, const float* off, const float* mask, float* gxt,
                                float* goff, float* gmask, float* col, cudaStream_t stream);
+// The fused TF32 backward (out channels per group <= 256): the grad-column
+// GEMM with the col2im scatter into gxt and the coordinate / mask reductions
+// into goff / gmask (as launch_bwd_data_tc), and the weight gradient from the
+// column tiles it samples on chip, summed into `gwt`, the tap-major
+// [outC][kh*kw][Cg] copy of grad_weight (pre-zeroed).  No column buffer.
+bool tc_fused_supported(const Geom& g);
+cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* wbt,
+                                const float* xt, const float* off, const float* mask, float* gxt,
+                                float* goff, float* gmask, float* gwt, int num_sms,
+                                cudaStream_t stream);
 // Weight gradient as a dense TMA-fed GEMM over the column buffer, summed into
 // `gw` (pre-zeroed): grad_weight itself ([outC][Cg][kh*kw]), or with
 // `tap_major` a [outC][kh*kw][Cg] copy, whose reductions coalesce, for the

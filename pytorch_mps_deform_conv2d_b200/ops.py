@@ -24,6 +24,7 @@ MATH_3XTF32 = 0x2
 ALGO_SIMT_GEMM = 0x100
 ALGO_SIMT_DIRECT = 0x200
 ALGO_TC_GATHER_WEIGHT = 0x400
+ALGO_TC_COLUMN_BUFFER = 0x800
 MASK_LOGITS = 0x10000
 # test switch: the tensor-core kernels' waits run out (checks the error word)
 TEST_WAIT_TIMEOUT = 0x1000000

@@ -9,7 +9,7 @@ import torch
 from _util import make_case
 from pytorch_mps_deform_conv2d_b200 import _native
 from pytorch_mps_deform_conv2d_b200.ops import (ALGO_SIMT_DIRECT, ALGO_SIMT_GEMM,
-                                                ALGO_TC_GATHER_WEIGHT, MATH_3XTF32, MATH_FP32,
+                                                ALGO_TC_COLUMN_BUFFER, ALGO_TC_GATHER_WEIGHT, MATH_3XTF32, MATH_FP32,
                                                 MATH_TF32, deform_conv2d_ex, deform_conv2d_rows)
 
 pytestmark = pytest.mark.gpu
@@ -19,7 +19,10 @@ CL = torch.channels_last
 # name -> (case, flags, kernels that must run)
 CASES = {
     "tc-tf32": (dict(inC=128, outC=64, H=10, W=9, offset_scale=2.0), MATH_TF32,
-                ("fwd_tc", "bwd_data_tc", "bwd_weight_col")),
+                ("fwd_tc", "bwd_fused_tc")),
+    "tc-tf32-column-buffer": (dict(inC=128, outC=64, H=10, W=9, offset_scale=2.0),
+                              MATH_TF32 | ALGO_TC_COLUMN_BUFFER,
+                              ("fwd_tc", "bwd_data_tc", "bwd_weight_col")),
     "tc-tf32-gather-weight": (dict(inC=128, outC=64, H=10, W=9, offset_scale=2.0),
                               MATH_TF32 | ALGO_TC_GATHER_WEIGHT, ("bwd_weight_tc",)),
     "tc-3xtf32-cg32-dg2": (dict(inC=64, outC=32, H=9, W=11, dg=2, offset_scale=2.0),

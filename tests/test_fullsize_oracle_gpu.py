@@ -36,13 +36,21 @@ NAMES = ("out", "input", "offset", "mask", "weight", "bias")
 FP32_TOL = dict(out=1e-4, input=2e-3, offset=1e-4, mask=1e-4, weight=1e-4, bias=1e-4)
 TF32_OUT = 5e-3
 TF32_GRAD = 1e-3
-# max |ours - oracle| / max |oracle| per gradient in TF32 mode
-TF32_ELEM = dict(input=1e-2, offset=1e-2, mask=1e-2, weight=1e-2, bias=1e-2)
+# max |ours - oracle| / max |oracle| per gradient in TF32 mode: measured on a
+# B200 at most 3.5e-4 over the four workloads (neck: input 2.8e-4, offset
+# 2.9e-4, mask 3.5e-4, weight 2.9e-4), gated at the north star's 1e-3
+TF32_ELEM = dict(input=1e-3, offset=1e-3, mask=1e-3, weight=1e-3, bias=1e-3)
 
-# tensor-core kernels each workload must run in the tensor-core modes (the
-# grouped layer has 2 channels per group: the CUDA-core kernels in every mode)
-TC_KERNELS = {"train": ("fwd_tc", "bwd_data_tc"), "neck": ("fwd_tc", "bwd_data_tc"),
-              "dcnv1": ("fwd_tc", "bwd_data_tc"), "grouped": ()}
+# tensor-core kernels each workload must run in the tensor-core modes: the
+# fused backward in TF32 up to 256 out channels a group, the grad-column
+# kernel (+ column buffer) otherwise; the grouped layer has 2 channels per
+# group: the CUDA-core kernels in every mode
+TC_KERNELS = {("train", "tf32"): ("fwd_tc", "bwd_fused_tc"),
+              ("neck", "tf32"): ("fwd_tc", "bwd_fused_tc"),
+              ("dcnv1", "tf32"): ("fwd_tc", "bwd_data_tc", "bwd_weight_col"),
+              ("train", "3xtf32"): ("fwd_tc", "bwd_data_tc", "bwd_weight_col"),
+              ("neck", "3xtf32"): ("fwd_tc", "bwd_data_tc", "bwd_weight_col"),
+              ("dcnv1", "3xtf32"): ("fwd_tc", "bwd_data_tc", "bwd_weight_col")}
 
 
 @functools.lru_cache(maxsize=None)
@@ -105,9 +113,8 @@ def test_workload_matches_oracle(cuda_device, name, mode):
     errs = _errors(got, _oracle(name))
     print(f"\nPARITY {name} {mode} " + " ".join(
         f"{k}:norm={e[0]:.2e},scaled={e[1]:.2e},elem={e[2]:.2e}" for k, e in errs.items()))
-    if mode != "fp32":
-        for kern in TC_KERNELS[name]:
-            assert kern in kernels, f"{kern} did not run: {sorted(kernels)}"
+    for kern in TC_KERNELS.get((name, mode), ()):
+        assert kern in kernels, f"{kern} did not run: {sorted(kernels)}"
     for k, (norm, scaled, elem) in errs.items():
         if mode == "tf32":
             if k == "out":

@@ -8,7 +8,7 @@ import torch
 
 from _util import make_case, rel_norm_err, run_oracle, run_ours
 from pytorch_mps_deform_conv2d_b200 import _native
-from pytorch_mps_deform_conv2d_b200.ops import ALGO_TC_GATHER_WEIGHT, MATH_TF32
+from pytorch_mps_deform_conv2d_b200.ops import ALGO_TC_COLUMN_BUFFER, ALGO_TC_GATHER_WEIGHT, MATH_TF32
 
 pytestmark = pytest.mark.gpu
 
@@ -107,18 +107,29 @@ TC_BWD_CASES = {
 }
 
 
-def _weight_kernel(case, path):
-    """Kernel name the weight path runs; the gather kernel covers only
-    128-channel multiples per group, other shapes keep the column buffer."""
-    algo, kernel = WEIGHT_PATHS[path]
-    cg = case["inC"] // case.get("groups", 1)
-    return algo, (kernel if cg % 128 == 0 else "bwd_weight_col")
+def _kernels(case, path):
+    """(flags, kernels that must run) of a backward route: the fused kernel
+    covers up to 256 out channels per group (others keep the column buffer);
+    the gather kernel covers only 128-channel multiples per group (others
+    keep the column buffer)."""
+    algo, kernels = WEIGHT_PATHS[path]
+    g = case.get("groups", 1)
+    cg, og = case["inC"] // g, case["outC"] // g
+    col = ("bwd_data_tc", "bwd_weight_col")
+    if path == "fused" and og > 256:
+        return algo, col
+    if path == "gather" and cg % 128 != 0:
+        return algo, col
+    return algo, kernels
 
 
-# The two tensor-core weight-gradient kernels: the dense GEMM over the column
-# buffer written by the grad-column kernel (default), and the one that
-# gathers its own columns (no column buffer).
-WEIGHT_PATHS = {"col": (0, "bwd_weight_col"), "gather": (ALGO_TC_GATHER_WEIGHT, "bwd_weight_tc")}
+# The tensor-core backward routes: the fused kernel (default in TF32: the
+# columns stay on chip), the grad-column kernel with the dense weight GEMM
+# over the column buffer, and the grad-column kernel with the weight kernel
+# that gathers its own columns (no column buffer).
+WEIGHT_PATHS = {"fused": (0, ("bwd_fused_tc",)),
+                "col": (ALGO_TC_COLUMN_BUFFER, ("bwd_data_tc", "bwd_weight_col")),
+                "gather": (ALGO_TC_GATHER_WEIGHT, ("bwd_data_tc", "bwd_weight_tc"))}
 
 
 def _grad_errors(case, flags=MATH_TF32):
@@ -139,10 +150,10 @@ def _grad_errors(case, flags=MATH_TF32):
 @pytest.mark.parametrize("path", sorted(WEIGHT_PATHS))
 @pytest.mark.parametrize("name", sorted(TC_BWD_CASES))
 def test_backward_tf32(cuda_device, name, path):
-    algo, kernel = _weight_kernel(TC_BWD_CASES[name], path)
+    algo, kernels = _kernels(TC_BWD_CASES[name], path)
     stats, out_err, errs, elem = _grad_errors(make_case(upstream="randn", **TC_BWD_CASES[name]),
                                               flags=MATH_TF32 | algo)
-    assert "bwd_data_tc" in stats and kernel in stats, sorted(stats)
+    assert all(k in stats for k in kernels), (kernels, sorted(stats))
     assert out_err <= OUT_TOL
     for k, e in errs.items():
         assert e <= GRAD_TOL, f"grad_{k}: norm-wise rel err {e:.2e} (all: {errs}, elem: {elem})"
@@ -154,6 +165,7 @@ def test_backward_tf32_uncovered_shape_uses_fp32_kernels(cuda_device):
     # kernels run and meet the fp32 tolerances.
     case = make_case(inC=48, outC=64, H=9, W=9, upstream="randn")
     stats, out_err, errs, elem = _grad_errors(case)
-    assert "bwd_data_tc" not in stats and "bwd_data_simt" in stats
+    assert "bwd_data_tc" not in stats and "bwd_fused_tc" not in stats
+    assert "bwd_data_simt" in stats
     for k, e in errs.items():
         assert e <= 1e-4, f"grad_{k}: {e:.2e}"
