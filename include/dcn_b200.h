@@ -103,6 +103,15 @@ extern "C" {
  *                    tensors (no reference counterpart: the reference makes
  *                    every operand contiguous NCHW). */
 #define DCN_INPUT_NHWC 0x20000
+/*   DCN_INPUT_STAGED `input` of dcn_forward / dcn_backward is not the input
+ *                    tensor but its staging copy as dcn_stage_input wrote it
+ *                    (NHWC plus one zero pixel row, dcn_staged_input_size
+ *                    bytes): the call skips its own staging, and the
+ *                    workspace queries drop the copy.  A training step stages
+ *                    once and passes the copy to both passes instead of
+ *                    transposing the input twice (no reference counterpart;
+ *                    with DCN_INPUT_NHWC, grad_input is still channels-last). */
+#define DCN_INPUT_STAGED 0x40000
 /* Fourth byte: test switches (no reference counterpart).
  *   DCN_TEST_WAIT_TIMEOUT  the tensor-core kernels' TMA producers issue no
  *                    copies and every mbarrier wait gives up after about a
@@ -276,6 +285,15 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input,
 DCN_API int dcn_forward_noalloc(const dcn_shape* shape, const float* input,
                                 const float* weight, const float* offset, const float* mask,
                                 const float* bias, float* output, uint32_t flags, void* stream);
+
+/* Staging copy of an input for DCN_INPUT_STAGED (no reference counterpart):
+ * `staged` (dcn_staged_input_size bytes of device memory) receives the input
+ * in NHWC followed by one zero pixel row, the layout the kernels gather
+ * from.  `input` is NCHW, or channels-last with DCN_INPUT_NHWC in `flags`.
+ * Enqueued on `stream`; the copy stays valid while `input` is unchanged. */
+DCN_API size_t dcn_staged_input_size(const dcn_shape* shape);
+DCN_API int dcn_stage_input(const dcn_shape* shape, const float* input, float* staged,
+                            uint32_t flags, void* stream);
 
 /* Device error word of the current device (DCN_STATUS_* bits; 0 when every
  * wait of the tensor-core kernels completed in time).  No reference

@@ -29,7 +29,7 @@ def _out_size(size, k, s, p, d):
 
 
 def _forward_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
-                  dilation_h, dilation_w, groups, deformable_groups, math=-1):
+                  dilation_h, dilation_w, groups, deformable_groups, math=-1, staged=None):
     ho = _out_size(input.shape[2], weight.shape[2], stride_h, pad_h, dilation_h)
     wo = _out_size(input.shape[3], weight.shape[3], stride_w, pad_w, dilation_w)
     return input.new_empty((input.shape[0], weight.shape[0], ho, wo))
@@ -45,7 +45,8 @@ def _input_format(input):
 
 
 def _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
-                   pad_w, dilation_h, dilation_w, groups, deformable_groups, math=-1):
+                   pad_w, dilation_h, dilation_w, groups, deformable_groups, math=-1,
+                   staged=None):
     grad_mask = mask.new_empty(mask.shape) if mask.numel() > 0 else input.new_empty((0,))
     use_bias = bias is not None and bias.numel() > 0
     grad_bias = input.new_empty((weight.shape[0],)) if use_bias else input.new_empty((0,))
@@ -53,6 +54,11 @@ def _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, str
                              memory_format=_input_format(input))
     return (grad_input, offset.new_empty(offset.shape), grad_mask,
             weight.new_empty(weight.shape), grad_bias)
+
+
+def _stage_input_fake(input):
+    n, c, h, w = input.shape
+    return input.new_empty((n * h * w * c + c,))
 
 
 def _forward_rows_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
@@ -85,12 +91,21 @@ _INT_ARGS = ("stride_h", "stride_w", "pad_h", "pad_w", "dilation_h", "dilation_w
              "deformable_groups", "math")
 
 
-def _setup_context(ctx, inputs, output):
+def _setup(ctx, inputs, nints):
     input, weight, offset, mask, bias = inputs[:5]
-    ctx.ints = tuple(inputs[5:])
+    ctx.ints = tuple(inputs[5:5 + nints])   # the integer arguments
+    ctx.n_rest = len(inputs) - 5           # + the staging copy, if the schema has one
     ctx.has_mask = mask.numel() > 0
     ctx.has_bias = bias is not None and bias.numel() > 0
     ctx.save_for_backward(input, weight, offset, mask, bias if ctx.has_bias else None)
+
+
+def _setup_context(ctx, inputs, output):
+    _setup(ctx, inputs, len(_INT_ARGS))  # deform_conv2d_forward: ints, then `staged`
+
+
+def _setup_rows_context(ctx, inputs, output):
+    _setup(ctx, inputs, len(_INT_ARGS) + 1)  # deform_conv2d_forward_rows: + row_begin
 
 
 def _forward_backward(ctx, grad_output):
@@ -100,7 +115,7 @@ def _forward_backward(ctx, grad_output):
     grad_input, grad_offset, grad_mask, grad_weight, grad_bias = grads
     return ((grad_input, grad_weight, grad_offset,
              grad_mask if ctx.has_mask else None,
-             grad_bias if ctx.has_bias else None) + (None,) * len(ctx.ints))
+             grad_bias if ctx.has_bias else None) + (None,) * ctx.n_rest)
 
 
 def _forward_rows_backward(ctx, grad_output):
@@ -110,7 +125,7 @@ def _forward_rows_backward(ctx, grad_output):
     grad_input, grad_offset, grad_mask, grad_weight, grad_bias = grads
     return ((grad_input, grad_weight, grad_offset,
              grad_mask if ctx.has_mask else None,
-             grad_bias if ctx.has_bias else None) + (None,) * len(ctx.ints))
+             grad_bias if ctx.has_bias else None) + (None,) * ctx.n_rest)
 
 
 def register() -> None:
@@ -120,6 +135,7 @@ def register() -> None:
     torch.library.register_fake(q + "deform_conv2d_forward")(_forward_fake)
     torch.library.register_fake(q + "deform_conv2d")(_forward_fake)
     torch.library.register_fake(q + "deform_conv2d_backward")(_backward_fake)
+    torch.library.register_fake(q + "deform_conv2d_stage_input")(_stage_input_fake)
     torch.library.register_fake(q + "deformable_col2im")(_col2im_fake)
     torch.library.register_fake(q + "deformable_col2im_coord")(_col2im_coord_fake)
     torch.library.register_autograd(q + "deform_conv2d_forward", _forward_backward,
@@ -127,4 +143,4 @@ def register() -> None:
     torch.library.register_fake(q + "deform_conv2d_forward_rows")(_forward_rows_fake)
     torch.library.register_fake(q + "deform_conv2d_backward_rows")(_backward_rows_fake)
     torch.library.register_autograd(q + "deform_conv2d_forward_rows", _forward_rows_backward,
-                                    setup_context=_setup_context)
+                                    setup_context=_setup_rows_context)

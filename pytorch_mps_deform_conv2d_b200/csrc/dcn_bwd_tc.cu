@@ -1267,20 +1267,24 @@ WSplit weight_split(const Geom& g, int bn, int num_sms, int tile_cost) {
 // 32-byte-atom swizzle) also serves as its transpose buffer: the grad-column
 // rows are written there, read by the gather and the scatter, and then
 // overwritten by the column values of the same pixels.
-// Work items are (slot, pixel tile) in slot-major order, cut into one
-// contiguous range per CTA, so a CTA's items share one or two slots and the
-// weight-gradient accumulator is drained once or twice.
+// Work items are (slot, pixel tile) in slot-major order.  When the slots fit
+// the grid, every slot gets the same `ranges` contiguous pixel-tile ranges,
+// one CTA each (CTA c: slot c % slots, range c / slots), so at any moment the
+// CTAs of all slots work on the same few pixel tiles and their inputs,
+// grad_out rows and grad-input lines are shared in L2; the weight-gradient
+// accumulator is drained once, at the end.  Otherwise (`ranges` 0) the items
+// are cut into one contiguous range per CTA, which touches one or two slots.
 //   warp 0      TMA producer: per item, the GEMM1 stages of bwd_data_tc and,
 //               one item behind, 4 GEMM2 stages (Og rows x 32 pixels of go_r)
 //   warp 1      MMA issue: GEMM1 of item i, then GEMM2 of item i - 1
 //   warps 2-17  epilogue
-// Shared memory: 3 ring stages of 32 KB (both GEMMs), the 64 KB column tile,
+// Shared memory: 4 ring stages of 32 KB (both GEMMs), the 64 KB column tile,
 // the sampling plans (2 KB a warp), barriers.  Tensor memory: two 128-column
 // GEMM1 accumulators and the GEMM2 accumulator (Og <= 256 columns).
 // ---------------------------------------------------------------------------
 constexpr int F_TMA_WARP = 0, F_MMA_WARP = 1, F_EPI_WARP0 = 2, F_EPI_WARPS = 16;
 constexpr int F_THREADS = (F_EPI_WARP0 + F_EPI_WARPS) * 32;  // 576
-constexpr int F_STAGES = 3;
+constexpr int F_STAGES = 4;  // 4 x 32 KB: GEMM2 of an item can have all four go_r blocks in flight
 constexpr int F_STAGE = 32768;        // GEMM1: go 16 KB + W 16 KB; GEMM2: go Og x 128 B
 constexpr int F_COL = 4 * 16384;      // the column tile
 constexpr int F_PLANS = F_EPI_WARPS * 32 * (int)sizeof(PixPlan);
@@ -1454,7 +1458,7 @@ __global__ void __launch_bounds__(F_THREADS, 1)
 bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
                     const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap g2map, int bpi, int nblocks, int mtiles,
-                    int nslots, long long nitems, const float* __restrict__ xt,
+                    int nslots, long long nitems, int ranges, const float* __restrict__ xt,
                     const float* __restrict__ off, const float* __restrict__ mask,
                     float* __restrict__ gxt, float* __restrict__ goff,
                     float* __restrict__ gmask, float* __restrict__ gwt) {
@@ -1483,8 +1487,18 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   // past Og (the weight map ends there), so the go_r rows it loads add nothing
   const int ochunks = (g.Og + 31) >> 5;
   // this CTA's items [u0, u0 + n) in slot-major order
-  const long long u0 = (long long)blockIdx.x * nitems / gridDim.x;
-  const int n = (int)((long long)(blockIdx.x + 1) * nitems / gridDim.x - u0);
+  long long u0;
+  int n;
+  if (ranges > 0) {  // one pixel-tile range of one slot
+    const int slots = (int)(nitems / mtiles);
+    const int s = (int)blockIdx.x % slots, rg = (int)blockIdx.x / slots;
+    const int mt0 = (int)((long long)rg * mtiles / ranges);
+    u0 = (long long)s * mtiles + mt0;
+    n = (int)((long long)(rg + 1) * mtiles / ranges) - mt0;
+  } else {
+    u0 = (long long)blockIdx.x * nitems / gridDim.x;
+    n = (int)((long long)(blockIdx.x + 1) * nitems / gridDim.x - u0);
+  }
   auto seg_of = [&](int i) { return (u0 + i) / mtiles; };  // (group, slot) of item i
 
   if (tid == 0) {
@@ -1931,11 +1945,17 @@ cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* w
   const int nblocks = g.N * bpi;
   const int mtiles = (nblocks + 3) / 4;
   const int nslots = weight_slots(g);
-  const long long nitems = (long long)g.G * nslots * mtiles;
-  const int grid = (int)(nitems < num_sms ? nitems : num_sms);
+  const long long slots = (long long)g.G * nslots;
+  const long long nitems = slots * mtiles;
+  // aligned pixel ranges per slot when the slots fit the SMs (at most one
+  // range per tile); else contiguous cuts of the slot-major item list
+  int ranges = slots <= num_sms ? (int)(num_sms / slots) : 0;
+  if (ranges > mtiles) ranges = mtiles;
+  const int grid = ranges > 0 ? (int)(ranges * slots)
+                              : (int)(nitems < num_sms ? nitems : num_sms);
   bwd_fused_tc_kernel<<<grid, F_THREADS, smem, stream>>>(g, amap, bmap, g2map, bpi, nblocks,
-                                                         mtiles, nslots, nitems, xt, off, mask,
-                                                         gxt, goff, gmask, gwt);
+                                                         mtiles, nslots, nitems, ranges, xt, off,
+                                                         mask, gxt, goff, gmask, gwt);
   return cudaGetLastError();
 }
 

@@ -283,9 +283,10 @@ FwdAlgo pick_fwd(const dcn::Geom& g, uint32_t flags) {
 // target of the tensor-core gathers' dropped corners.
 size_t xt_floats(const dcn::Geom& g) { return (size_t)g.N * g.HW * g.C + g.C; }
 
-// The least workspace the forward accepts.
+// The least workspace the forward accepts (no staging copy of the input when
+// the caller passes one, DCN_INPUT_STAGED).
 size_t fwd_ws_min(const dcn::Geom& g, uint32_t flags) {
-  size_t b = align_up(xt_floats(g) * sizeof(float));  // xt + zero row
+  size_t b = (flags & DCN_INPUT_STAGED) ? 0 : align_up(xt_floats(g) * sizeof(float));  // xt + zero row
   switch (pick_fwd(g, flags)) {
     case FwdAlgo::kGemm:
       b += align_up((size_t)g.G * g.kk * fwd_cpad(g) * g.Og * sizeof(float));
@@ -335,7 +336,7 @@ bool use_tc_bwd(const dcn::Geom& g, uint32_t flags) {
 }
 
 size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
-  size_t b = align_up(xt_floats(g) * sizeof(float));                   // xt + zero row
+  size_t b = (flags & DCN_INPUT_STAGED) ? 0 : align_up(xt_floats(g) * sizeof(float));  // xt + zero row
   if (!(flags & DCN_INPUT_NHWC))
     b += align_up((size_t)g.N * g.HW * g.C * sizeof(float));           // grad x (NHWC)
   if (use_tc_bwd(g, flags)) {
@@ -467,11 +468,14 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
   const size_t usable = workspace_bytes - (size_t)(ws.base - static_cast<char*>(workspace));
-  float* xt = ws.take(xt_floats(g));
+  // xt (+ its zero row): a transpose of NCHW input, a copy of NHWC input, or
+  // the caller's staging copy (DCN_INPUT_STAGED: nothing to do)
+  const bool staged = flags & DCN_INPUT_STAGED;
+  float* xt = staged ? const_cast<float*>(input) : ws.take(xt_floats(g));
   const FwdAlgo algo = pick_fwd(g, flags);
-  // xt (+ its zero row): a transpose of NCHW input, a copy of NHWC input
   const bool nhwc = flags & DCN_INPUT_NHWC;
   auto stage_input = [&]() {
+    if (staged) return cudaSuccess;
     return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, nullptr, stream)
                 : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, nullptr, stream);
   };
@@ -482,18 +486,18 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     const int sms = num_sms_current();
     const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, split, false, sms);
     void* tail = tail_bytes > 0 && usable >= ws.used + tail_bytes ? ws.base + ws.used : nullptr;
-    Fork fk(stream, side_streams_pay(g));
+    Fork fk(stream, side_streams_pay(g) && !staged);
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, tail, fk.side(0)),
                 "tc_pack_weight");
-    DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
+    if (!staged) DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
     DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, tail,
                                 tail ? tail_bytes : 0, sms, stream),
              "fwd_tc");
     return DCN_OK;
   }
-  DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
+  if (!staged) DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
   switch (algo) {
     case FwdAlgo::kDirect:
       DCN_CUDA(dcn::launch_fwd_simt_direct(g, xt, weight, offset, mask, bias, output, stream),
@@ -719,7 +723,9 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
                 need, workspace_bytes);
   Carver ws(align_ptr(workspace));
-  float* xt = ws.take(xt_floats(g));
+  // the caller's staging copy of the input (DCN_INPUT_STAGED), or our own
+  const bool staged = flags & DCN_INPUT_STAGED;
+  float* xt = staged ? const_cast<float*>(input) : ws.take(xt_floats(g));
   // the kernels accumulate grad_input in NHWC: into the caller's buffer when
   // it is channels-last, else into a workspace copy transposed at the end
   const bool nhwc = flags & DCN_INPUT_NHWC;
@@ -727,11 +733,14 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   DCN_CHECK(!nhwc || (reinterpret_cast<uintptr_t>(grad_input) & 15u) == 0,
             "deform_conv2d_backward: grad_input must be 16-byte aligned with DCN_INPUT_NHWC");
   float* gxt = nhwc ? grad_input : ws.take((size_t)g.N * g.HW * g.C);
-  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass
+  // xt (+ its zero row) and the zeroed grad-input accumulator in one pass;
+  // with a staged input only the accumulator is zeroed
   auto stage_input = [&]() {
+    if (staged) return cudaMemsetAsync(gxt, 0, x_bytes, stream);
     return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream)
                 : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream);
   };
+  const char* stage_name = staged ? "memset" : (nhwc ? "copy_nhwc" : "nchw_to_nhwc");
   if (tc_bwd) {
     const bool split = split_math(flags);
     const size_t parts = split ? 2 : 1;
@@ -760,7 +769,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_CUDA_ON(fk.side(1), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(1)),
                 "tc_pack_weight_bwd");
     DCN_CUDA_ON(fk.side(1), dcn::launch_zero(z, fk.side(1)), "zero");
-    DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
+    DCN_CUDA(stage_input(), stage_name);
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
     if (use_fused_bwd(g, flags)) {
@@ -821,7 +830,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_ORDER(fk.join(0), "join");
     return DCN_OK;
   }
-  DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
+  DCN_CUDA(stage_input(), stage_name);
   if (dcn::dgroup_supported(g) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT))) {
     DCN_CUDA(dcn::launch_bwd_dgroup(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
                                     grad_mask, grad_weight, stream),
@@ -1041,6 +1050,31 @@ DCN_API int dcn_col2im_coord(const float* columns, const float* input, const flo
   DCN_CUDA(dcn::launch_col2im_coord_single(g, columns, input, offset, mask, grad_offset, grad_mask,
                                            stream),
            "col2im_coord");
+  return DCN_OK;
+}
+
+DCN_API size_t dcn_staged_input_size(const dcn_shape* s) {
+  dcn::Geom g;
+  if (make_geom(s, false, false, g, "dcn_staged_input_size") != DCN_OK) return 0;
+  return xt_floats(g) * sizeof(float);
+}
+
+DCN_API int dcn_stage_input(const dcn_shape* s, const float* input, float* staged,
+                            uint32_t flags, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, false, false, g, "dcn_stage_input");
+  if (rc != DCN_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DCN_CHECK(is_device_ptr(staged), "dcn_stage_input: staged must be a CUDA device buffer");
+  DCN_CHECK((long long)g.N * g.C * g.HW == 0 || is_device_ptr(input),
+            "dcn_stage_input: input must be a CUDA tensor");
+  if (flags & DCN_INPUT_NHWC)
+    DCN_CUDA(dcn::launch_copy_nhwc(input, staged, g.N, g.C, g.HW, true, nullptr, stream),
+             "copy_nhwc");
+  else
+    DCN_CUDA(dcn::launch_nchw_to_nhwc(input, staged, g.N, g.C, g.HW, true, nullptr, stream),
+             "nchw_to_nhwc");
   return DCN_OK;
 }
 

@@ -8,7 +8,10 @@
 // allocator, and calls the C ABI (include/dcn_b200.h) on the current CUDA
 // stream.  Every schema has one extra trailing argument, `int math=-1`: -1
 // follows torch.backends.cuda.matmul.allow_tf32, otherwise it is the
-// DCN_MATH_* / DCN_ALGO_* flag word of the C ABI.
+// DCN_MATH_* / DCN_ALGO_* flag word of the C ABI.  The forward and backward
+// operators take one more, `Tensor? staged=None`: the input's NHWC staging
+// copy (deform_conv2d_stage_input), which the differentiable operator makes
+// once per step for both passes.
 #include <ATen/ATen.h>
 #include <ATen/Context.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -113,12 +116,27 @@ bool channels_last(const at::Tensor& t) {
          t.is_contiguous(at::MemoryFormat::ChannelsLast);
 }
 
+// The staging copy of `x` for DCN_INPUT_STAGED, when the caller passed one
+// (a float32 tensor of dcn_staged_input_size bytes on x's device); NULL
+// otherwise.
+const float* staged_ptr(const c10::optional<at::Tensor>& staged, const at::Tensor& x,
+                        const dcn_shape& s) {
+  if (!staged.has_value() || !staged->defined() || staged->numel() == 0) return nullptr;
+  TORCH_CHECK(staged->device() == x.device() && staged->scalar_type() == at::kFloat &&
+                  staged->is_contiguous() &&
+                  (size_t)staged->numel() * sizeof(float) == dcn_staged_input_size(&s),
+              "staged must be the float32 staging copy of the input "
+              "(deform_conv2d_stage_input)");
+  return staged->data_ptr<float>();
+}
+
 at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                         const at::Tensor& offset, const at::Tensor& mask,
                         const c10::optional<at::Tensor>& bias, int64_t stride_h,
                         int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
                         int64_t dilation_w, int64_t groups, int64_t deformable_groups,
-                        int64_t row_begin, int64_t math) {
+                        int64_t row_begin, int64_t math,
+                        const c10::optional<at::Tensor>& staged = c10::nullopt) {
   TORCH_CHECK(input.device().is_cuda() && weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
   // float32 (the reference's only dtype, .mm:206-209) or, as an addition,
@@ -185,11 +203,13 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                               ws.data_ptr(), wsr, stream.stream()));
     return out;
   }
-  const size_t ws_bytes = dcn_forward_workspace_size(&s, flags);
+  const float* xs = staged_ptr(staged, x, s);
+  const uint32_t fflags = flags | (xs ? DCN_INPUT_STAGED : 0u);
+  const size_t ws_bytes = dcn_forward_workspace_size(&s, fflags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
-  check_rc(dcn_forward(&s, x.data_ptr<float>(), w.data_ptr<float>(), off.data_ptr<float>(), mp,
-                       bp, out.data_ptr<float>(), flags, ws.data_ptr(), ws_bytes,
-                       stream.stream()));
+  check_rc(dcn_forward(&s, xs ? xs : x.data_ptr<float>(), w.data_ptr<float>(),
+                       off.data_ptr<float>(), mp, bp, out.data_ptr<float>(), fflags,
+                       ws.data_ptr(), ws_bytes, stream.stream()));
   return out;
 }
 
@@ -198,9 +218,51 @@ at::Tensor deform_conv2d_forward(const at::Tensor& input, const at::Tensor& weig
                                  const c10::optional<at::Tensor>& bias, int64_t stride_h,
                                  int64_t stride_w, int64_t pad_h, int64_t pad_w,
                                  int64_t dilation_h, int64_t dilation_w, int64_t groups,
-                                 int64_t deformable_groups, int64_t math) {
+                                 int64_t deformable_groups, int64_t math,
+                                 const c10::optional<at::Tensor>& staged) {
+  return forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, groups, deformable_groups, -1, math, staged);
+}
+
+// The differentiable operator's kernel below autograd: the forward without a
+// staging copy (its schema has none).
+at::Tensor deform_conv2d_plain(const at::Tensor& input, const at::Tensor& weight,
+                               const at::Tensor& offset, const at::Tensor& mask,
+                               const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                               int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                               int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                               int64_t deformable_groups, int64_t math) {
   return forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
                       dilation_h, dilation_w, groups, deformable_groups, -1, math);
+}
+
+// NHWC staging copy of a float32 input (its zero pixel row included), for
+// the `staged` argument of the forward and backward operators: a training
+// step stages its input once for both.
+at::Tensor deform_conv2d_stage_input(const at::Tensor& input) {
+  TORCH_CHECK(input.device().is_cuda() && input.scalar_type() == at::kFloat && input.dim() == 4,
+              "deform_conv2d_stage_input: input must be a 4-D float32 CUDA tensor");
+  c10::cuda::CUDAGuard guard(input.device());
+  const bool nhwc = channels_last(input);
+  auto x = nhwc ? input : input.contiguous();
+  dcn_shape s{};
+  s.batch = x.size(0);
+  s.in_channels = x.size(1);
+  s.height = x.size(2);
+  s.width = x.size(3);
+  s.out_channels = 1;
+  s.kernel_h = s.kernel_w = 1;
+  s.stride_h = s.stride_w = 1;
+  s.dilation_h = s.dilation_w = 1;
+  s.groups = 1;
+  s.deformable_groups = 1;
+  const size_t bytes = dcn_staged_input_size(&s);
+  TORCH_CHECK(bytes > 0, dcn_last_error());
+  auto staged = at::empty({(int64_t)(bytes / sizeof(float))}, x.options());
+  check_rc(dcn_stage_input(&s, x.data_ptr<float>(), staged.data_ptr<float>(),
+                           nhwc ? DCN_INPUT_NHWC : 0u,
+                           at::cuda::getCurrentCUDAStream().stream()));
+  return staged;
 }
 
 at::Tensor deform_conv2d_forward_rows(const at::Tensor& input, const at::Tensor& weight,
@@ -221,7 +283,8 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
                     const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
                     const c10::optional<at::Tensor>& bias, int64_t stride_h, int64_t stride_w,
                     int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
-                    int64_t groups, int64_t deformable_groups, int64_t row_begin, int64_t math) {
+                    int64_t groups, int64_t deformable_groups, int64_t row_begin, int64_t math,
+                    const c10::optional<at::Tensor>& staged = c10::nullopt) {
   TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
                   weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
@@ -271,7 +334,9 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
-  const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
+  const float* xs = row_begin >= 0 ? nullptr : staged_ptr(staged, x, s);
+  const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u) |
+                         (xs ? DCN_INPUT_STAGED : 0u);
   const size_t ws_bytes = row_begin >= 0 ? dcn_backward_rows_workspace_size(&s, out_h, flags)
                                          : dcn_backward_workspace_size(&s, flags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
@@ -288,7 +353,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
                                ptr(grad_input), ptr(grad_offset), gm, ptr(grad_weight), gb, flags,
                                ws.data_ptr(), ws_bytes, stream.stream()));
   else
-    check_rc(dcn_backward(&s, cptr(go), cptr(x), cptr(w), cptr(off), mp, ptr(grad_input),
+    check_rc(dcn_backward(&s, cptr(go), xs ? xs : cptr(x), cptr(w), cptr(off), mp, ptr(grad_input),
                           ptr(grad_offset), gm, ptr(grad_weight), gb, flags, ws.data_ptr(),
                           ws_bytes, stream.stream()));
   return std::make_tuple(grad_input, grad_offset, grad_mask, grad_weight, grad_bias);
@@ -299,9 +364,10 @@ Grads deform_conv2d_backward(const at::Tensor& grad_output, const at::Tensor& in
                              const at::Tensor& mask, const c10::optional<at::Tensor>& bias,
                              int64_t stride_h, int64_t stride_w, int64_t pad_h, int64_t pad_w,
                              int64_t dilation_h, int64_t dilation_w, int64_t groups,
-                             int64_t deformable_groups, int64_t math) {
+                             int64_t deformable_groups, int64_t math,
+                             const c10::optional<at::Tensor>& staged) {
   return backward_impl(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
-                       pad_w, dilation_h, dilation_w, groups, deformable_groups, -1, math);
+                       pad_w, dilation_h, dilation_w, groups, deformable_groups, -1, math, staged);
 }
 
 Grads deform_conv2d_backward_rows(const at::Tensor& grad_output, const at::Tensor& input,
@@ -447,17 +513,27 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
                                            const at::Tensor&, const at::Tensor&,
                                            const c10::optional<at::Tensor>&, int64_t, int64_t,
                                            int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                           int64_t)>();
+                                           int64_t, const c10::optional<at::Tensor>&)>();
+    static auto stage = c10::Dispatcher::singleton()
+                            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_stage_input", "")
+                            .typed<at::Tensor(const at::Tensor&)>();
     const bool has_bias = bias.defined() && bias.numel() > 0;
     c10::optional<at::Tensor> b;
     if (has_bias) b = bias;
-    at::Tensor out;
+    at::Tensor out, staged;
     {
       at::AutoDispatchBelowADInplaceOrView below;
+      // a float32 input is staged (NHWC) once, for the forward and the
+      // backward, instead of once in each
+      if (input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0)
+        staged = stage.call(input);
+      c10::optional<at::Tensor> st;
+      if (staged.defined()) st = staged;
       out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w, dilation_h,
-                    dilation_w, groups, deformable_groups, math);
+                    dilation_w, groups, deformable_groups, math, st);
     }
     ctx->save_for_backward({input, weight, offset, mask, bias});
+    if (staged.defined()) ctx->saved_data["staged"] = staged;
     ctx->saved_data["ints"] = std::vector<int64_t>{stride_h,   stride_w, pad_h,
                                                    pad_w,      dilation_h, dilation_w,
                                                    groups,     deformable_groups, math};
@@ -473,15 +549,17 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
                                       const at::Tensor&, const at::Tensor&,
                                       const c10::optional<at::Tensor>&, int64_t, int64_t,
                                       int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                      int64_t)>();
+                                      int64_t, const c10::optional<at::Tensor>&)>();
     const auto saved = ctx->get_saved_variables();
     const auto v = ctx->saved_data["ints"].toIntVector();
     const bool has_bias = ctx->saved_data["has_bias"].toBool();
     const at::Tensor& mask = saved[3];
     c10::optional<at::Tensor> b;
     if (has_bias) b = saved[4];
+    c10::optional<at::Tensor> st;
+    if (ctx->saved_data.count("staged")) st = ctx->saved_data["staged"].toTensor();
     auto r = op.call(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0], v[1],
-                     v[2], v[3], v[4], v[5], v[6], v[7], v[8]);
+                     v[2], v[3], v[4], v[5], v[6], v[7], v[8], st);
     const bool has_mask = mask.numel() > 0;
     return {std::get<0>(r),
             std::get<3>(r),
@@ -522,12 +600,16 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
   m.def(
       "deform_conv2d_forward(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
       "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
-      "int dilation_w, int groups, int deformable_groups, int math=-1) -> Tensor");
+      "int dilation_w, int groups, int deformable_groups, int math=-1, Tensor? staged=None) "
+      "-> Tensor");
   m.def(
       "deform_conv2d_backward(Tensor grad_output, Tensor input, Tensor weight, Tensor offset, "
       "Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, "
-      "int dilation_h, int dilation_w, int groups, int deformable_groups, int math=-1) "
-      "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+      "int dilation_h, int dilation_w, int groups, int deformable_groups, int math=-1, "
+      "Tensor? staged=None) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+  // NHWC staging copy of a float32 input for the `staged` argument above (no
+  // reference counterpart): a training step stages its input once.
+  m.def("deform_conv2d_stage_input(Tensor input) -> Tensor");
   // Row windows (no reference counterpart): offset / mask / output /
   // grad_output hold output rows [row_begin, row_begin + offset.size(2)).
   m.def(
@@ -557,5 +639,6 @@ TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
   m.impl("deform_conv2d_backward", TORCH_FN(deform_conv2d_backward));
   m.impl("deform_conv2d_forward_rows", TORCH_FN(deform_conv2d_forward_rows));
   m.impl("deform_conv2d_backward_rows", TORCH_FN(deform_conv2d_backward_rows));
-  m.impl("deform_conv2d", TORCH_FN(deform_conv2d_forward));  // below autograd
+  m.impl("deform_conv2d_stage_input", TORCH_FN(deform_conv2d_stage_input));
+  m.impl("deform_conv2d", TORCH_FN(deform_conv2d_plain));  // below autograd
 }

@@ -1,0 +1,76 @@
+"""Staged input (DCN_INPUT_STAGED): the NHWC staging copy that
+deform_conv2d_stage_input makes once per step feeds both the forward and the
+backward operator.  Results equal those of the unstaged calls (the forward
+bitwise, the gradients within the grad_input reductions' run-to-run noise),
+in every math mode and for NCHW and channels-last input, and the
+differentiable operator stages its input once per training step."""
+import numpy as np
+import pytest
+import torch
+
+from _util import make_case
+from pytorch_mps_deform_conv2d_b200 import _native
+from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32, MATH_FP32, MATH_TF32, deform_conv2d_ex
+
+pytestmark = pytest.mark.gpu
+
+MODES = {"fp32": MATH_FP32, "tf32": MATH_TF32, "3xtf32": MATH_3XTF32}
+
+
+def _ops():
+    _native.load_ops()
+    return torch.ops.deform_conv2d_b200
+
+
+@pytest.mark.parametrize("layout", ["nchw", "channels_last"])
+@pytest.mark.parametrize("mode", sorted(MODES))
+def test_staged_equals_unstaged(cuda_device, mode, layout):
+    flags = MODES[mode]
+    case = make_case(N=2, inC=64, outC=64, H=12, W=14, offset_scale=2.0, mask_kind="sigmoid")
+    d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    x = d["x"]
+    if layout == "channels_last":
+        x = x.contiguous(memory_format=torch.channels_last)
+    ops = _ops()
+    args = (1, 1, 1, 1, 1, 1, 1, 1)  # stride, pad, dilation, groups, deformable groups
+    staged = ops.deform_conv2d_stage_input(x)
+    assert staged.numel() == 2 * 12 * 14 * 64 + 64
+    out_a = ops.deform_conv2d_forward(x, d["w"], d["off"], d["m"], d["b"], *args, flags)
+    out_b = ops.deform_conv2d_forward(x, d["w"], d["off"], d["m"], d["b"], *args, flags, staged)
+    assert torch.equal(out_a, out_b)
+    ga = ops.deform_conv2d_backward(d["go"], x, d["w"], d["off"], d["m"], d["b"], *args, flags)
+    gb = ops.deform_conv2d_backward(d["go"], x, d["w"], d["off"], d["m"], d["b"], *args, flags,
+                                    staged)
+    torch.cuda.synchronize()
+    assert gb[0].is_contiguous(memory_format=torch.channels_last) == (layout == "channels_last")
+    for a, b in zip(ga, gb):
+        a, b = a.cpu().numpy(), b.cpu().numpy()
+        scale = max(1.0, float(np.abs(a).max()))
+        np.testing.assert_allclose(b, a, rtol=1e-5, atol=1e-5 * scale)
+
+
+def test_staged_size_is_checked(cuda_device):
+    case = make_case(N=1, inC=32, outC=32, H=8, W=9)
+    d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    bad = torch.zeros(17, device="cuda")
+    with pytest.raises(RuntimeError, match="staging copy"):
+        _ops().deform_conv2d_forward(d["x"], d["w"], d["off"], d["m"], d["b"],
+                                     1, 1, 1, 1, 1, 1, 1, 1, MATH_TF32, bad)
+
+
+@pytest.mark.parametrize("mode", ["fp32", "tf32"])
+def test_training_step_stages_its_input_once(cuda_device, mode):
+    case = make_case(N=2, inC=64, outC=64, H=12, W=14, offset_scale=2.0)
+    leaves = {k: case[k].cuda().requires_grad_(True) for k in ("x", "w", "b", "off", "m")}
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out = deform_conv2d_ex(leaves["x"], leaves["off"], leaves["w"], leaves["b"],
+                               case["stride"], case["padding"], case["dilation"], leaves["m"],
+                               flags=MODES[mode])
+        out.backward(case["go"].cuda())
+        torch.cuda.synchronize()
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    assert stats["nchw_to_nhwc"][0] == 1, stats  # staged once, for both passes
