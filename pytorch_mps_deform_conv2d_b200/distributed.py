@@ -34,16 +34,42 @@ def shard_batch(tensors: Sequence[Optional[torch.Tensor]], rank: int,
     return [t[sl] if t is not None else None for t in tensors]
 
 
+def _adjacent_view(grads: Sequence[Optional[torch.Tensor]]) -> Optional[torch.Tensor]:
+    """One 1-D view covering `grads` when they are contiguous, in order and
+    back to back in one storage (the backward operator allocates grad_weight
+    and grad_bias that way); None otherwise."""
+    if not grads or any(g is None or not g.is_contiguous() for g in grads):
+        return None
+    first = grads[0]
+    storage = first.untyped_storage()
+    end = first.data_ptr()
+    for g in grads:
+        if (g.dtype != first.dtype or g.device != first.device
+                or g.untyped_storage().data_ptr() != storage.data_ptr() or g.data_ptr() != end):
+            return None
+        end += g.numel() * g.element_size()
+    total = sum(g.numel() for g in grads)
+    return first.new_empty(0).set_(storage, first.storage_offset(), (total,), (1,))
+
+
 def allreduce_grads(params: Iterable[torch.nn.Parameter], group=None,
                     average: bool = False) -> None:
     """Sum (or average) the gradients of `params` across the process group
-    with one flat all-reduce.  Parameters without a gradient contribute
+    with one all-reduce: in place when the gradients lie back to back in one
+    buffer (as the backward operator writes grad_weight and grad_bias),
+    else through a packed copy.  Parameters without a gradient contribute
     zeros, so every rank issues the same collective."""
     params = list(params)
     if not params:
         return
     world = dist.get_world_size(group)
     if world == 1:
+        return
+    flat = _adjacent_view([p.grad for p in params])
+    if flat is not None:
+        dist.all_reduce(flat, group=group)
+        if average:
+            flat /= world
         return
     ref = params[0]
     flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1)

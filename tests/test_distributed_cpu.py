@@ -35,7 +35,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, case, result_q, fail_rank):
+def _worker(rank, world, port, case, result_q, fail_rank, adjacent=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=10))
@@ -48,8 +48,15 @@ def _worker(rank, world, port, case, result_q, fail_rank):
                                           case["b"].numpy(), 1, 1, 1, m.numpy())
         w = torch.nn.Parameter(case["w"].clone())
         b = torch.nn.Parameter(case["b"].clone())
-        w.grad, b.grad = torch.from_numpy(gw), torch.from_numpy(gb)
-        allreduce_grads([w, b])
+        if adjacent:  # grad_weight and grad_bias back to back in one buffer
+            flat = torch.cat([torch.from_numpy(gw).reshape(-1), torch.from_numpy(gb)])
+            w.grad = flat[:gw.size].view(gw.shape)
+            b.grad = flat[gw.size:]
+            allreduce_grads([w, b])
+            assert w.grad.data_ptr() == flat.data_ptr()  # reduced in place
+        else:
+            w.grad, b.grad = torch.from_numpy(gw), torch.from_numpy(gb)
+            allreduce_grads([w, b])
         result_q.put((rank, "ok", w.grad.numpy(), b.grad.numpy()))
     except Exception as e:  # report, then leave the group
         result_q.put((rank, "error", repr(e), None))
@@ -67,12 +74,12 @@ def _case():
                 off=torch.randn(N, 18, H, W), m=torch.rand(N, 9, H, W), go=torch.randn(N, O, H, W))
 
 
-def _run(world, fail_rank=-1):
+def _run(world, fail_rank=-1, adjacent=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     case = _case()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, fail_rank))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, fail_rank, adjacent))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -84,9 +91,10 @@ def _run(world, fail_rank=-1):
     return case, sorted(out, key=lambda r: r[0])
 
 
-def test_sharded_grads_equal_full_batch():
+@pytest.mark.parametrize("adjacent", [False, True], ids=["packed", "in-place"])
+def test_sharded_grads_equal_full_batch(adjacent):
     from oracle import oracle
-    case, out = _run(2)
+    case, out = _run(2, adjacent=adjacent)
     _, _, _, gw, gb = oracle.backward(case["go"].numpy(), case["x"].numpy(), case["off"].numpy(),
                                       case["w"].numpy(), case["b"].numpy(), 1, 1, 1,
                                       case["m"].numpy())
