@@ -1349,11 +1349,20 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
                                             float* __restrict__ gmask) {
   const int quad = lane & 3, sub = lane >> 2;
   const int zoff = g.N * g.HW * g.C;
+  // Bank spreading: in the swizzled block, rows r and r + 4 (the transpose
+  // writes, a lane a row) and rows 8i + 2s, 8i + 2s + 1 (the gather's and
+  // the column values' lanes) put the same 16-byte half of a granule on the
+  // same banks; lanes with bit 2 set take the two halves in the other order,
+  // so every 16-byte access of a quarter warp hits a different bank group.
+  const int hs = (lane >> 2) & 1;
   {  // this lane's pixel row into the block, 16 bytes at a time
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      tc::st_shared_v4(tb + cblk(lane, j >> 1) + ((j & 1) << 4), vals[4 * j], vals[4 * j + 1],
-                       vals[4 * j + 2], vals[4 * j + 3]);
+    for (int j = 0; j < 8; ++j) {
+      const int a = 4 * j, b = 4 * (j ^ 1);  // pieces j and j ^ 1 of the row
+      tc::st_shared_v4(tb + cblk(lane, j >> 1) + (((j & 1) ^ hs) << 4),
+                       hs ? vals[b] : vals[a], hs ? vals[b + 1] : vals[a + 1],
+                       hs ? vals[b + 2] : vals[a + 2], hs ? vals[b + 3] : vals[a + 3]);
+    }
   }
   __syncwarp();
   const float* xq = xt + gch0 + quad * 8;  // corner loads: channels 8 quad .. 8 quad + 7
@@ -1369,8 +1378,9 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
 #pragma unroll
     for (int e = 0; e < 8; ++e) cv[e] = 0.f;
     if (live) {
-      const float4 ga = ld_shared_f4(tb + cblk(px, quad));
-      const float4 gb = ld_shared_f4(tb + cblk(px, quad) + 16);
+      const float4 l0 = ld_shared_f4(tb + cblk(px, quad) + (hs << 4));
+      const float4 l1 = ld_shared_f4(tb + cblk(px, quad) + ((hs ^ 1) << 4));
+      const float4 ga = hs ? l1 : l0, gb = hs ? l0 : l1;
       const float gc[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
       float a[8], b[8], c[8], d[8];
       ldg_f8(xq + (unsigned)pl.cidx.x, a);  // dropped corners: zero row
@@ -1441,10 +1451,11 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
     // the grad-column rows of these 8 pixels are read: their column values
     // take their place (TF32-rounded; 0 for void samples and past the image)
     __syncwarp();
-    tc::st_shared_v4(tb + cblk(px, quad), tc::to_tf32(cv[0]), tc::to_tf32(cv[1]),
-                     tc::to_tf32(cv[2]), tc::to_tf32(cv[3]));
-    tc::st_shared_v4(tb + cblk(px, quad) + 16, tc::to_tf32(cv[4]), tc::to_tf32(cv[5]),
-                     tc::to_tf32(cv[6]), tc::to_tf32(cv[7]));
+    float hv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) hv[e] = tc::to_tf32(hs ? cv[e ^ 4] : cv[e]);
+    tc::st_shared_v4(tb + cblk(px, quad) + (hs << 4), hv[0], hv[1], hv[2], hv[3]);
+    tc::st_shared_v4(tb + cblk(px, quad) + ((hs ^ 1) << 4), hv[4], hv[5], hv[6], hv[7]);
   }
   (void)row_q;
   (void)qend;

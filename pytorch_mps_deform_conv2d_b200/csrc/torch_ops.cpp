@@ -330,18 +330,8 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   auto grad_input = at::empty_like(x);
   auto grad_offset = at::empty_like(off);
   auto grad_mask = use_mask ? at::empty_like(msk) : at::empty({0}, x.options());
-  // grad_weight and grad_bias are adjacent views of one buffer, so a data-
-  // parallel step can sum both with one all-reduce of that buffer, without
-  // packing them (distributed.allreduce_grads)
-  at::Tensor grad_weight, grad_bias;
-  if (use_bias) {
-    auto flat = at::empty({w.numel() + w.size(0)}, x.options());
-    grad_weight = flat.narrow(0, 0, w.numel()).view(w.sizes());
-    grad_bias = flat.narrow(0, w.numel(), w.size(0));
-  } else {
-    grad_weight = at::empty_like(w);
-    grad_bias = at::empty({0}, x.options());
-  }
+  auto grad_weight = at::empty_like(w);
+  auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
   const float* xs = row_begin >= 0 ? nullptr : staged_ptr(staged, x, s);

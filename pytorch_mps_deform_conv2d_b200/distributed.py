@@ -54,38 +54,36 @@ def _adjacent_view(grads: Sequence[Optional[torch.Tensor]]) -> Optional[torch.Te
 
 def allreduce_grads(params: Iterable[torch.nn.Parameter], group=None,
                     average: bool = False) -> None:
-    """Sum (or average) the gradients of `params` across the process group
-    with one all-reduce: in place when the gradients lie back to back in one
-    buffer (as the backward operator writes grad_weight and grad_bias),
-    else through a packed copy.  Parameters without a gradient contribute
-    zeros, so every rank issues the same collective."""
+    """Sum (or average) the gradients of `params` across the process group.
+
+    The gradients are reduced where they lie, without packing copies: in one
+    all-reduce when they sit back to back in one buffer, else as one
+    all-reduce per gradient issued together in a single collective group
+    (NCCL runs them as one launch; other backends back to back).  Parameters without a gradient get a zero
+    gradient first, so every rank issues the same collectives."""
     params = list(params)
     if not params:
         return
     world = dist.get_world_size(group)
     if world == 1:
         return
-    flat = _adjacent_view([p.grad for p in params])
+    for p in params:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+    grads = [p.grad for p in params]
+    flat = _adjacent_view(grads)
     if flat is not None:
         dist.all_reduce(flat, group=group)
-        if average:
-            flat /= world
-        return
-    ref = params[0]
-    flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1)
-                      for p in params]).to(ref.device)
-    dist.all_reduce(flat, group=group)
+    elif dist.get_backend(group) == "nccl":
+        with dist._coalescing_manager(group=group, device=grads[0].device):
+            for g in grads:
+                dist.all_reduce(g, group=group)
+    else:  # backends without coalescing (gloo): the collectives back to back
+        for work in [dist.all_reduce(g, group=group, async_op=True) for g in grads]:
+            work.wait()
     if average:
-        flat /= world
-    off = 0
-    for p in params:
-        n = p.numel()
-        g = flat[off:off + n].view_as(p)
-        if p.grad is None:
-            p.grad = g.clone()
-        else:
-            p.grad.copy_(g)
-        off += n
+        for g in grads:
+            g /= world
 
 
 # ---------------------------------------------------------------------------

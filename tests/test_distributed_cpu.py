@@ -91,7 +91,7 @@ def _run(world, fail_rank=-1, adjacent=False):
     return case, sorted(out, key=lambda r: r[0])
 
 
-@pytest.mark.parametrize("adjacent", [False, True], ids=["packed", "in-place"])
+@pytest.mark.parametrize("adjacent", [False, True], ids=["separate", "in-place"])
 def test_sharded_grads_equal_full_batch(adjacent):
     from oracle import oracle
     case, out = _run(2, adjacent=adjacent)
