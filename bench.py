@@ -127,9 +127,9 @@ def algorithmic_work(wl):
 
 # tcgen05 kernels (TF32 operands; 3xTF32 issues three products per multiply-add)
 TC_KERNELS = ("fwd_tc", "bwd_fused_tc", "bwd_data_tc", "bwd_weight_tc", "bwd_weight_col",
-              "fwd_tc_bf16",
-              "fwd_tc_f16")
-BF16_KERNELS = ("fwd_tc_bf16", "fwd_tc_f16")  # kind::f16 with 16-bit operands
+              "fwd_tc_bf16", "fwd_tc_f16", "bwd_fused_tc_bf16", "bwd_fused_tc_f16")
+# kind::f16 with 16-bit operands
+BF16_KERNELS = ("fwd_tc_bf16", "fwd_tc_f16", "bwd_fused_tc_bf16", "bwd_fused_tc_f16")
 HALF = {"bf16": "bfloat16", "fp16": "float16"}
 
 
@@ -137,7 +137,7 @@ def kernel_work(name, wl):
     """(amount, unit, bound) of one launch of a library kernel."""
     w = algorithmic_work(wl)
     N, C = wl["N"], wl["C"]
-    if name == "bwd_fused_tc":  # both backward GEMMs
+    if name.startswith("bwd_fused_tc"):  # both backward GEMMs
         return 2.0 * w["gemm_flops"], "flop", "tensor"
     if name.startswith(("fwd_", "bwd_data", "bwd_weight")):
         return w["gemm_flops"], "flop", "tensor"

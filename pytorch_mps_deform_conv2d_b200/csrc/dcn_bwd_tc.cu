@@ -19,6 +19,9 @@
 //                is gathered (bilinear sampling, as in the forward) straight
 //                into an MN-major operand (32-byte-atom swizzle); go_r rows arrive by
 //                cp.async.  Partial tiles are reduced into grad_weight.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include "dcn_launch.h"
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
@@ -1325,6 +1328,79 @@ __device__ __forceinline__ void fblocks(const Geom& g, const FItem& it, int bpi,
 __device__ __forceinline__ uint32_t cblk(int px, int gran) {
   return (uint32_t)((px >> 2) * W_SBO + (px & 3) * 128 + (((gran ^ px) & 3) << 5));
 }
+// ---- storage formats of the fused backward ----
+// kF32: fp32 tensors, TF32 operands (kind::tf32); kBF16s / kF16s: bf16 / fp16
+// tensors, 16-bit operands (kind::f16) -- the gathers read 16-bit corner
+// values, the column tile holds 16-bit values -- with fp32 accumulation in
+// tensor memory and fp32 grad-input, offset, mask and weight reductions.
+enum : int { kF32 = 0, kBF16s = 1, kF16s = 2 };
+
+// Offset / mask element i as fp32.
+template <int FMT>
+__device__ __forceinline__ float fld(const void* p, long long i) {
+  if constexpr (FMT == kBF16s) {
+    return __uint_as_float((uint32_t)__ldg(static_cast<const unsigned short*>(p) + i) << 16);
+  } else if constexpr (FMT == kF16s) {
+    return __half2float(__ushort_as_half(__ldg(static_cast<const unsigned short*>(p) + i)));
+  } else {
+    return __ldg(static_cast<const float*>(p) + i);
+  }
+}
+// The two 16-bit values of a 32-bit word (low half first) as fp32, and back
+// (round to nearest).
+template <int FMT>
+__device__ __forceinline__ float h_lo(uint32_t w) {
+  if constexpr (FMT == kF16s) return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+  else return __uint_as_float(w << 16);
+}
+template <int FMT>
+__device__ __forceinline__ float h_hi(uint32_t w) {
+  if constexpr (FMT == kF16s) return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+  else return __uint_as_float(w & 0xffff0000u);
+}
+template <int FMT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (FMT == kF16s) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+}
+// Byte offset of 16-byte chunk q (channels 8q .. 8q + 7) of pixel row px in
+// a warp's 16-bit column block: the MN-major operand of a kind::f16 GEMM with
+// the 64-byte swizzle -- K rows of 64 bytes (32 channels), chunk position
+// q ^ ((px / 2) % 4), rows grouped by 8 at W_SBO.
+__device__ __forceinline__ uint32_t cblk16(int px, int q) {
+  return (uint32_t)(px * 64 + (((q ^ (px >> 1)) & 3) << 4));
+}
+// Shared-memory descriptors of 64-byte-swizzled operands (sm100 version 1):
+// MN-major (32-element blocks W_LBO apart, 8-row K groups W_SBO apart) and
+// K-major (8-row groups of 64-byte rows, W_SBO apart).
+__device__ __forceinline__ uint64_t sdesc_sw64_mn(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(W_LBO >> 4) << 16) |
+         ((uint64_t)(W_SBO >> 4) << 32) | (1ull << 46) | (4ull << 61);
+}
+__device__ __forceinline__ uint64_t sdesc_sw64_k(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(W_SBO >> 4) << 32) |
+         (1ull << 46) | (4ull << 61);
+}
+// 16-byte read-only global load (8 16-bit values).
+__device__ __forceinline__ uint4 ldg_u4(const void* p) {
+  uint4 r;
+  asm("ld.global.nc.v4.b32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
 __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -1338,13 +1414,15 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 // 32 channels of tap k.  As epilogue_chunk, with the warp's column block `tb`
 // as the transpose buffer and the column values stored there at the end of
 // each group of 8 pixels, once the gather and the scatter of those pixels
-// have read their grad-column rows.
-__device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const float (&vals)[32],
-                                            int gch0, long long row_q, long long qend, int lane,
-                                            uint32_t tb, PixPlan* plan,
-                                            const float* __restrict__ xt,
-                                            const float* __restrict__ off,
-                                            const float* __restrict__ mask,
+// have read their grad-column rows.  16-bit formats: the corner values come
+// from the 16-bit NHWC copy (16 bytes a lane and corner), the column values
+// are rounded to the tensors' 16-bit type into the first 2 KB of the block
+// (K group i of 512 bytes lies over grad-column rows 4i .. 4i + 3, read in
+// pass i / 2 <= i).
+template <int FMT>
+__device__ __forceinline__ void fused_chunk(const Geom& g, const float (&vals)[32], int gch0,
+                                            int lane, uint32_t tb, PixPlan* plan,
+                                            const void* __restrict__ xt,
                                             float* __restrict__ gxt, float* __restrict__ goff,
                                             float* __restrict__ gmask) {
   const int quad = lane & 3, sub = lane >> 2;
@@ -1365,7 +1443,9 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
     }
   }
   __syncwarp();
-  const float* xq = xt + gch0 + quad * 8;  // corner loads: channels 8 quad .. 8 quad + 7
+  // corner loads: channels 8 quad .. 8 quad + 7
+  const float* xq = static_cast<const float*>(xt) + gch0 + quad * 8;
+  const unsigned short* xq16 = static_cast<const unsigned short*>(xt) + gch0 + quad * 8;
 #pragma unroll 2
   for (int i = 0; i < 4; ++i) {
     const int px = i * 8 + sub;
@@ -1383,10 +1463,24 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
       const float4 ga = hs ? l1 : l0, gb = hs ? l0 : l1;
       const float gc[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
       float a[8], b[8], c[8], d[8];
-      ldg_f8(xq + (unsigned)pl.cidx.x, a);  // dropped corners: zero row
-      ldg_f8(xq + (unsigned)pl.cidx.y, b);
-      ldg_f8(xq + (unsigned)pl.cidx.z, c);
-      ldg_f8(xq + (unsigned)pl.cidx.w, d);
+      if constexpr (FMT == kF32) {
+        ldg_f8(xq + (unsigned)pl.cidx.x, a);  // dropped corners: zero row
+        ldg_f8(xq + (unsigned)pl.cidx.y, b);
+        ldg_f8(xq + (unsigned)pl.cidx.z, c);
+        ldg_f8(xq + (unsigned)pl.cidx.w, d);
+      } else {
+        const uint4 ua = ldg_u4(xq16 + (unsigned)pl.cidx.x), ub = ldg_u4(xq16 + (unsigned)pl.cidx.y);
+        const uint4 uc = ldg_u4(xq16 + (unsigned)pl.cidx.z), ud = ldg_u4(xq16 + (unsigned)pl.cidx.w);
+        const uint32_t wa[4] = {ua.x, ua.y, ua.z, ua.w}, wb[4] = {ub.x, ub.y, ub.z, ub.w};
+        const uint32_t wc[4] = {uc.x, uc.y, uc.z, uc.w}, wd[4] = {ud.x, ud.y, ud.z, ud.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a[2 * e] = h_lo<FMT>(wa[e]); a[2 * e + 1] = h_hi<FMT>(wa[e]);
+          b[2 * e] = h_lo<FMT>(wb[e]); b[2 * e + 1] = h_hi<FMT>(wb[e]);
+          c[2 * e] = h_lo<FMT>(wc[e]); c[2 * e + 1] = h_hi<FMT>(wc[e]);
+          d[2 * e] = h_lo<FMT>(wd[e]); d[2 * e + 1] = h_hi<FMT>(wd[e]);
+        }
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         d1 = fmaf(gc[e], a[e], d1);
@@ -1451,28 +1545,35 @@ __device__ __forceinline__ void fused_chunk(const Geom& g, int k, int dgi, const
     // the grad-column rows of these 8 pixels are read: their column values
     // take their place (TF32-rounded; 0 for void samples and past the image)
     __syncwarp();
-    float hv[8];
+    if constexpr (FMT == kF32) {
+      float hv[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) hv[e] = tc::to_tf32(hs ? cv[e ^ 4] : cv[e]);
-    tc::st_shared_v4(tb + cblk(px, quad) + (hs << 4), hv[0], hv[1], hv[2], hv[3]);
-    tc::st_shared_v4(tb + cblk(px, quad) + ((hs ^ 1) << 4), hv[4], hv[5], hv[6], hv[7]);
+      for (int e = 0; e < 8; ++e) hv[e] = tc::to_tf32(hs ? cv[e ^ 4] : cv[e]);
+      tc::st_shared_v4(tb + cblk(px, quad) + (hs << 4), hv[0], hv[1], hv[2], hv[3]);
+      tc::st_shared_v4(tb + cblk(px, quad) + ((hs ^ 1) << 4), hv[4], hv[5], hv[6], hv[7]);
+    } else {
+      st_shared_u4(tb + cblk16(px, quad), pack2<FMT>(cv[0], cv[1]), pack2<FMT>(cv[2], cv[3]),
+                   pack2<FMT>(cv[4], cv[5]), pack2<FMT>(cv[6], cv[7]));
+    }
   }
-  (void)row_q;
-  (void)qend;
-  (void)k;
-  (void)dgi;
-  (void)off;
-  (void)mask;
 }
 
+// FMT kF32: TF32 operands, K steps of 32 out channels (GEMM1) and 8 pixels
+// (GEMM2, 4 UMMAs a 32-pixel block), 128-byte swizzles.  kBF16s / kF16s:
+// 16-bit operands (kind::f16), K steps of 64 out channels and 16 pixels (2
+// UMMAs a block); go_r blocks and GEMM2's B in the 64-byte swizzle (32 pixels
+// x 2 bytes a row), the same stage bytes and descriptor strides.
+template <int FMT>
 __global__ void __launch_bounds__(F_THREADS, 1)
 bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
                     const __grid_constant__ CUtensorMap bmap,
                     const __grid_constant__ CUtensorMap g2map, int bpi, int nblocks, int mtiles,
-                    int nslots, long long nitems, int ranges, const float* __restrict__ xt,
-                    const float* __restrict__ off, const float* __restrict__ mask,
+                    int nslots, long long nitems, int ranges, const void* __restrict__ xt,
+                    const void* __restrict__ off, const void* __restrict__ mask,
                     float* __restrict__ gxt, float* __restrict__ goff,
                     float* __restrict__ gmask, float* __restrict__ gwt) {
+  constexpr bool H16 = FMT != kF32;
+  constexpr int KO = H16 ? 64 : 32;  // out channels of a GEMM1 K step
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw_u32 = tc::smem_u32(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw_u32 & 1023u)) & 1023u);
@@ -1496,7 +1597,7 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 32-out-channel K steps of GEMM1; a partial last one reads zero weights
   // past Og (the weight map ends there), so the go_r rows it loads add nothing
-  const int ochunks = (g.Og + 31) >> 5;
+  const int ochunks = (g.Og + KO - 1) / KO;
   // this CTA's items [u0, u0 + n) in slot-major order
   long long u0;
   int n;
@@ -1562,8 +1663,8 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
               tc::mbar_arrive_expect_tx(&full[st], F_STAGE);
 #pragma unroll
               for (int mb = 0; mb < 4; ++mb)
-                tc::tma_load_2d(sA + mb * W_LBO, &amap, ax[mb], arow[mb] + s * 32, &full[st]);
-              tc::tma_load_2d(sA + 16384, &bmap, s * 32, brow, &full[st]);
+                tc::tma_load_2d(sA + mb * W_LBO, &amap, ax[mb], arow[mb] + s * KO, &full[st]);
+              tc::tma_load_2d(sA + 16384, &bmap, s * KO, brow, &full[st]);
             }
           }
           if (i >= 1) {  // GEMM2 of item i - 1: go_r rows of each 32-pixel block
@@ -1572,7 +1673,7 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             for (int pq = 0; pq < 4; ++pq, ++gs) {
               const int st = acquire();
               if (st < 0) return;
-              tc::mbar_arrive_expect_tx(&full[st], (uint32_t)g.Og * 128);
+              tc::mbar_arrive_expect_tx(&full[st], (uint32_t)g.Og * (H16 ? 64 : 128));
               tc::tma_load_2d(ring + st * F_STAGE, &g2map, ax[pq], arow[pq], &full[st]);
             }
           }
@@ -1585,10 +1686,15 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
     __syncwarp();
   } else if (warp == F_MMA_WARP) {
     if (lane == 0) {
-      // GEMM1: A = go_r pixels (MN-major), B = W slot rows (K-major)
-      const uint32_t idesc1 = idesc_tf32_amn(128, 128);
+      // GEMM1: A = go_r pixels (MN-major), B = W slot rows (K-major);
       // GEMM2: A = column tile (MN-major: channels contiguous), B = go_r rows (K-major)
-      const uint32_t idesc2 = idesc_tf32_amn(128, g.Og);
+      const uint32_t amn = 1u << 15;
+      const uint32_t idesc1 = FMT == kF16s    ? tc::idesc_f16(128, 128) | amn
+                              : FMT == kBF16s ? tc::idesc_bf16(128, 128) | amn
+                                              : idesc_tf32_amn(128, 128);
+      const uint32_t idesc2 = FMT == kF16s    ? tc::idesc_f16(128, g.Og) | amn
+                              : FMT == kBF16s ? tc::idesc_bf16(128, g.Og) | amn
+                                              : idesc_tf32_amn(128, g.Og);
       int gs = 0, segs = 0;
       [&]() {
         for (int i = 0; i <= n; ++i) {
@@ -1603,9 +1709,14 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
               tc::tc_fence_after();
               const uint32_t sA = ring + st * F_STAGE, sB = sA + 16384;
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
-                              idesc1, (s | j) != 0 ? 1u : 0u);
+              for (int j = 0; j < 4; ++j) {  // 8 (TF32) or 16 (16-bit) out channels each
+                if constexpr (H16)
+                  tc::umma_bf16(d, sdesc_sw64_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
+                                idesc1, (s | j) != 0 ? 1u : 0u);
+                else
+                  tc::umma_tf32(d, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                                tc::sdesc_sw128(sB + j * 32), idesc1, (s | j) != 0 ? 1u : 0u);
+              }
               tc::umma_commit(&empty[st]);
             }
             tc::umma_commit(&acc_full[acc]);
@@ -1626,9 +1737,15 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
               tc::tc_fence_after();
               const uint32_t sB = ring + st * F_STAGE, sA = colt + pq * 16384;
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tc::umma_tf32(d2, sdesc_sw128b32_mn(sA + j * 2 * W_SBO), tc::sdesc_sw128(sB + j * 32),
-                              idesc2, (first && pq == 0 && j == 0) ? 0u : 1u);
+              for (int j = 0; j < (H16 ? 2 : 4); ++j) {  // 8 (TF32) or 16 (16-bit) pixels each
+                if constexpr (H16)
+                  tc::umma_bf16(d2, sdesc_sw64_mn(sA + j * 2 * W_SBO), sdesc_sw64_k(sB + j * 32),
+                                idesc2, (first && pq == 0 && j == 0) ? 0u : 1u);
+                else
+                  tc::umma_tf32(d2, sdesc_sw128b32_mn(sA + j * 2 * W_SBO),
+                                tc::sdesc_sw128(sB + j * 32), idesc2,
+                                (first && pq == 0 && j == 0) ? 0u : 1u);
+              }
               tc::umma_commit(&empty[st]);
               tc::umma_commit(&col_empty[pq]);
             }
@@ -1698,7 +1815,7 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
             const int ki = k / g.kw, kj = k - ki * g.kw;
             const long long oi = off_h_index(g, ni, dgi, k, p);
             float h, w;
-            sample_pos(g, oy, ox, ki, kj, __ldg(off + oi), __ldg(off + oi + g.P), h, w);
+            sample_pos(g, oy, ox, ki, kj, fld<FMT>(off, oi), fld<FMT>(off, oi + g.P), h, w);
             const Sample sp = make_sample(h, w, g.H, g.W);
             if (sp.valid) {
               const int nb = ni * g.HW;
@@ -1708,7 +1825,12 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
               pl.cidx.w = (sp.live & 8u) ? (nb + sp.i4) * g.C : zoff;
               pl.w = make_float4(sp.w1, sp.w2, sp.w3, sp.w4);
               const long long mi = mask_index(g, ni, dgi, k, p);
-              pl.geo = make_float4(sp.lh, sp.lw, mask_of(g, mask, mi), 0.f);
+              float m = 1.f;
+              if (g.use_mask) {
+                const float raw = fld<FMT>(mask, mi);
+                m = g.mask_logits ? 1.f / (1.f + expf(-raw)) : raw;
+              }
+              pl.geo = make_float4(sp.lh, sp.lw, m, 0.f);
               pl.idx = make_int4((int)oi, (int)mi, 0, 0);
             }
           }
@@ -1717,8 +1839,7 @@ bwd_fused_tc_kernel(Geom g, const __grid_constant__ CUtensorMap amap,
         // GEMM2 of the previous item has read this block of the column tile
         if (i >= 1 && !tc::wait(watch, &col_empty[lq], (i - 1) & 1)) return;
         if (rows_ok) {
-          fused_chunk(g, k, dgi, vals, gch0, row_q, qend, lane, tb, plan, xt, off, mask, gxt,
-                      goff, gmask);
+          fused_chunk<FMT>(g, vals, gch0, lane, tb, plan, xt, gxt, goff, gmask);
         } else {  // rows past the group's last tap: zero columns
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -1929,6 +2050,37 @@ bool tc_fused_supported(const Geom& g) {
                                                   (1LL << 40);
 }
 
+namespace {
+// Grid and schedule of the fused backward, and the launch.
+template <int FMT>
+cudaError_t launch_fused(const Geom& g, const CUtensorMap& amap, const CUtensorMap& bmap,
+                         const CUtensorMap& g2map, const void* xt, const void* off,
+                         const void* mask, float* gxt, float* goff, float* gmask, float* gwt,
+                         int num_sms, cudaStream_t stream) {
+  const size_t smem = fused_smem_bytes();
+  cudaError_t e =
+      ensure_dynamic_smem(reinterpret_cast<const void*>(bwd_fused_tc_kernel<FMT>), (int)smem);
+  if (e != cudaSuccess) return e;
+  const int bpi = (g.P + 31) / 32;  // 32-pixel blocks per image
+  if ((long long)g.N * bpi > (1LL << 30)) return cudaErrorInvalidValue;
+  const int nblocks = g.N * bpi;
+  const int mtiles = (nblocks + 3) / 4;
+  const int nslots = weight_slots(g);
+  const long long slots = (long long)g.G * nslots;
+  const long long nitems = slots * mtiles;
+  // aligned pixel ranges per slot when the slots fit the SMs (at most one
+  // range per tile); else contiguous cuts of the slot-major item list
+  int ranges = slots <= num_sms ? (int)(num_sms / slots) : 0;
+  if (ranges > mtiles) ranges = mtiles;
+  const int grid = ranges > 0 ? (int)(ranges * slots)
+                              : (int)(nitems < num_sms ? nitems : num_sms);
+  bwd_fused_tc_kernel<FMT><<<grid, F_THREADS, smem, stream>>>(
+      g, amap, bmap, g2map, bpi, nblocks, mtiles, nslots, nitems, ranges, xt, off, mask, gxt,
+      goff, gmask, gwt);
+  return cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* wbt,
                                 const float* xt, const float* off, const float* mask, float* gxt,
                                 float* goff, float* gmask, float* gwt, int num_sms,
@@ -1948,26 +2100,151 @@ cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* w
   e = make_tmap_2d_f32(&g2map, go_r, (uint64_t)g.P, (uint64_t)g.N * g.outC, (uint64_t)Ppad,
                        (uint32_t)g.Og);
   if (e != cudaSuccess) return e;
-  const size_t smem = fused_smem_bytes();
-  e = ensure_dynamic_smem(reinterpret_cast<const void*>(bwd_fused_tc_kernel), (int)smem);
-  if (e != cudaSuccess) return e;
-  const int bpi = (g.P + 31) / 32;  // 32-pixel blocks per image
-  if ((long long)g.N * bpi > (1LL << 30)) return cudaErrorInvalidValue;
-  const int nblocks = g.N * bpi;
-  const int mtiles = (nblocks + 3) / 4;
-  const int nslots = weight_slots(g);
-  const long long slots = (long long)g.G * nslots;
-  const long long nitems = slots * mtiles;
-  // aligned pixel ranges per slot when the slots fit the SMs (at most one
-  // range per tile); else contiguous cuts of the slot-major item list
-  int ranges = slots <= num_sms ? (int)(num_sms / slots) : 0;
-  if (ranges > mtiles) ranges = mtiles;
-  const int grid = ranges > 0 ? (int)(ranges * slots)
-                              : (int)(nitems < num_sms ? nitems : num_sms);
-  bwd_fused_tc_kernel<<<grid, F_THREADS, smem, stream>>>(g, amap, bmap, g2map, bpi, nblocks,
-                                                         mtiles, nslots, nitems, ranges, xt, off,
-                                                         mask, gxt, goff, gmask, gwt);
+  return launch_fused<kF32>(g, amap, bmap, g2map, xt, off, mask, gxt, goff, gmask, gwt, num_sms,
+                            stream);
+}
+
+namespace {
+// 16-bit grad_out (N*outC rows of P) -> go_r rows padded to Ppad (a multiple
+// of 8: 16-byte pitch; the padding zero), its values unchanged; with `gb`
+// (fp32, pre-zeroed) the bias gradient summed on the way in fp32.
+template <int FMT>
+__global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __restrict__ go,
+                                                        unsigned short* __restrict__ go_r,
+                                                        float* __restrict__ gb, int outC, int P,
+                                                        int Ppad, int pspans) {
+  __shared__ float part[8];
+  const long long row = blockIdx.x / pspans;  // n * outC + o
+  const int pbeg = (int)(blockIdx.x - row * pspans) * PG_SPAN;
+  const int pend = min(Ppad, pbeg + PG_SPAN);
+  const unsigned short* src = go + row * P;
+  unsigned short* dst = go_r + row * Ppad;
+  float sum = 0.f;
+  for (int p = pbeg + threadIdx.x; p < pend; p += blockDim.x) {
+    const unsigned short v = p < P ? __ldg(src + p) : (unsigned short)0;
+    dst[p] = v;
+    if constexpr (FMT == kF16s) sum += __half2float(__ushort_as_half(v));
+    else sum += __uint_as_float((uint32_t)v << 16);
+  }
+  if (gb == nullptr) return;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(gb + row % outC, t);
+  }
+}
+
+// 16-bit weight (outC, Cg, kh, kw) -> wbt[(g*kk + k)*Cg + c][o] (16-bit, as
+// the fp32 pack of the grad-column operand), one thread per element.
+__global__ void __launch_bounds__(256) pack_weight_bwd16_kernel(
+    const unsigned short* __restrict__ w, unsigned short* __restrict__ wb, Geom g,
+    long long total) {
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    // i enumerates the output: ((gi*kk + k)*Cg + c)*Og + o
+    const int o = (int)(i % g.Og);
+    long long r = i / g.Og;
+    const int c = (int)(r % g.Cg);
+    r /= g.Cg;
+    const int k = (int)(r % g.kk);
+    const int gi = (int)(r / g.kk);
+    wb[i] = __ldg(w + ((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k);
+  }
+}
+
+// fp32 NHWC (N, HW, C) -> 16-bit NCHW (N, C, HW), rounded to nearest; 32x32
+// tiles.
+template <int FMT>
+__global__ void __launch_bounds__(256) nhwc_to_nchw16_kernel(const float* __restrict__ in,
+                                                             unsigned short* __restrict__ out,
+                                                             int HW, int C) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int p0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const float* src = in + (long long)n * HW * C;
+  unsigned short* dst = out + (long long)n * HW * C;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int p = p0 + ty + i, c = c0 + tx;
+    if (p < HW && c < C) tile[ty + i][tx] = src[(long long)p * C + c];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int c = c0 + ty + i, p = p0 + tx;
+    if (p < HW && c < C) {
+      const float v = tile[tx][ty + i];
+      if constexpr (FMT == kF16s) dst[(long long)c * HW + p] = __half_as_ushort(__float2half_rn(v));
+      else dst[(long long)c * HW + p] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
+  }
+}
+}  // namespace
+
+cudaError_t launch_prep_go16(const Geom& g, const void* go, void* go_r, float* gb, bool f16,
+                             cudaStream_t stream) {
+  if ((long long)g.N * g.outC * g.P == 0) return cudaSuccess;
+  const int Ppad = (g.P + 7) & ~7;
+  const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
+  const long long blocks = (long long)g.N * g.outC * pspans;
+  if (blocks > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  auto kern = f16 ? prep_go16_kernel<kF16s> : prep_go16_kernel<kBF16s>;
+  kern<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const unsigned short*>(go),
+                                              static_cast<unsigned short*>(go_r), gb, g.outC,
+                                              g.P, Ppad, pspans);
   return cudaGetLastError();
+}
+
+cudaError_t launch_pack_weight_bwd16(const void* w, void* wbt, const Geom& g,
+                                     cudaStream_t stream) {
+  const long long total = (long long)g.G * g.kk * g.Cg * g.Og;
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  pack_weight_bwd16_kernel<<<(int)blocks, 256, 0, stream>>>(
+      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wbt), g, total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_nhwc_to_nchw16(const float* gxt, void* gx, int N, int C, int HW, bool f16,
+                                  cudaStream_t stream) {
+  if ((long long)N * C * HW == 0) return cudaSuccess;
+  if (N > 65535 || (HW + 31) / 32 > 65535) return cudaErrorInvalidValue;
+  dim3 grid((C + 31) / 32, (HW + 31) / 32, N);
+  auto kern = f16 ? nhwc_to_nchw16_kernel<kF16s> : nhwc_to_nchw16_kernel<kBF16s>;
+  kern<<<grid, 256, 0, stream>>>(gxt, static_cast<unsigned short*>(gx), HW, C);
+  return cudaGetLastError();
+}
+
+bool tc_fused16_supported(const Geom& g) { return tc_fused_supported(g) && g.C % 8 == 0; }
+
+cudaError_t launch_bwd_fused_tc_h16(const Geom& g, const void* go_r, const void* wbt,
+                                    const void* xt, const void* off, const void* mask,
+                                    float* gxt, float* goff, float* gmask, float* gwt, bool f16,
+                                    int num_sms, cudaStream_t stream) {
+  if (!tc_fused16_supported(g)) return cudaErrorInvalidValue;
+  const int Ppad = (g.P + 7) & ~7;  // 16-byte row pitch
+  CUtensorMap amap, bmap, g2map;
+  // go_r rows: 32-pixel x 64-row boxes, 64-byte swizzle (GEMM1's A, MN-major)
+  // and 32-pixel x Og-row boxes, 64-byte swizzle (GEMM2's B, K-major)
+  cudaError_t e = make_tmap_2d_h16_box(&amap, go_r, (uint64_t)g.P, (uint64_t)g.N * g.outC,
+                                       (uint64_t)Ppad, 32u, 64u, f16);
+  if (e != cudaSuccess) return e;
+  // packed W: 64-out-channel x 128-row boxes, 128-byte swizzle (K-major)
+  e = make_tmap_2d_h16_box(&bmap, wbt, (uint64_t)g.Og, (uint64_t)g.G * g.kk * g.Cg,
+                           (uint64_t)g.Og, 64u, 128u, f16);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_2d_h16_box(&g2map, go_r, (uint64_t)g.P, (uint64_t)g.N * g.outC, (uint64_t)Ppad,
+                           32u, (uint32_t)g.Og, f16);
+  if (e != cudaSuccess) return e;
+  return f16 ? launch_fused<kF16s>(g, amap, bmap, g2map, xt, off, mask, gxt, goff, gmask, gwt,
+                                   num_sms, stream)
+             : launch_fused<kBF16s>(g, amap, bmap, g2map, xt, off, mask, gxt, goff, gmask, gwt,
+                                    num_sms, stream);
 }
 
 bool tc_wcol_supported(const Geom& g, bool split) {

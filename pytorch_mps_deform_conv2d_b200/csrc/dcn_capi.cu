@@ -911,10 +911,35 @@ static size_t bwd_bf16_copy_bytes(const dcn::Geom& g) {
   return go + 2 * (x + w + off + m) + b;
 }
 
+// The fused 16-bit tensor-core backward (kind::f16 operands of the tensors'
+// type) where it covers the shape and no other kernel family is pinned.
+static bool use_fused16(const dcn::Geom& g, uint32_t flags) {
+  return !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT | DCN_ALGO_TC_GATHER_WEIGHT |
+                    DCN_ALGO_TC_COLUMN_BUFFER)) &&
+         g.N > 0 && g.C > 0 && g.outC > 0 && g.P > 0 && dcn::tc_fused16_supported(g);
+}
+
+// Its workspace: the 16-bit staging copy, grad_out rows and packed weight;
+// fp32 accumulators of grad_input (NHWC), grad_offset, grad_mask, the
+// tap-major grad_weight and grad_bias; the fp32 grad_weight in place.
+static size_t bwd_fused16_bytes(const dcn::Geom& g) {
+  const size_t w = (size_t)g.outC * g.Cg * g.kk;
+  return align_up(((size_t)g.N * g.HW * g.C + g.C) * 2) +
+         align_up((size_t)g.N * g.outC * ((g.P + 7) & ~7) * 2) + align_up(w * 2) +
+         align_up((size_t)g.N * g.HW * g.C * 4) + align_up((size_t)g.N * 2 * g.dg * g.kk * g.P * 4) +
+         align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + 2 * align_up(w * 4) +
+         align_up((size_t)g.outC * 4) + kAlign;
+}
+
+static size_t bwd_h16_ws(const dcn::Geom& g, uint32_t flags) {
+  return use_fused16(g, flags) ? bwd_fused16_bytes(g)
+                               : bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+}
+
 DCN_API size_t dcn_backward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_backward_bf16_workspace_size") != DCN_OK) return 0;
-  return bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+  return bwd_h16_ws(g, flags & ~(uint32_t)DCN_INPUT_STAGED);
 }
 
 // The 16-bit backward (bf16, or fp16 with `f16`): the fp32 backward on upcast
@@ -929,6 +954,83 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
   int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
   if (rc != DCN_OK) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  flags &= ~(uint32_t)DCN_INPUT_STAGED;  // the staging copy is an fp32 layout
+  if (use_fused16(g, flags)) {
+    DCN_CHECK(mask != nullptr || grad_mask == nullptr,
+              "deform_conv2d_backward: grad_mask must be NULL when mask is NULL");
+    DCN_CHECK(mask == nullptr || grad_mask != nullptr,
+              "deform_conv2d_backward: grad_mask is required when mask is given");
+    g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
+    apply_test_flags(g, flags);
+    DCN_CHECK(is_device_ptr(grad_output) && is_device_ptr(input) && is_device_ptr(weight) &&
+                  is_device_ptr(offset) && (mask == nullptr || is_device_ptr(mask)),
+              "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
+    DCN_CHECK(is_device_ptr(grad_input) && is_device_ptr(grad_offset) &&
+                  is_device_ptr(grad_weight) && (grad_mask == nullptr || is_device_ptr(grad_mask)) &&
+                  (grad_bias == nullptr || is_device_ptr(grad_bias)),
+              "deform_conv2d_backward: gradient outputs must be CUDA device buffers");
+    const size_t need16 = bwd_fused16_bytes(g);
+    if (workspace_bytes < need16 || workspace == nullptr)
+      return fail(DCN_ERR_WORKSPACE,
+                  "deform_conv2d_backward: workspace of %zu bytes needed, %zu given", need16,
+                  workspace_bytes);
+    char* p = static_cast<char*>(align_ptr(workspace));
+    auto take = [&p](size_t bytes) {
+      char* q = p;
+      p += align_up(bytes);
+      return q;
+    };
+    const long long nx = (long long)g.N * g.HW * g.C, nw = (long long)g.outC * g.Cg * g.kk;
+    const long long noff = (long long)g.N * 2 * g.dg * g.kk * g.P;
+    const long long nm = (long long)g.N * g.dg * g.kk * g.P;
+    void* xt = take(((size_t)nx + g.C) * 2);
+    void* go_r = take((size_t)g.N * g.outC * ((g.P + 7) & ~7) * 2);
+    void* wbt = take((size_t)nw * 2);
+    float* gxt = reinterpret_cast<float*>(take((size_t)nx * 4));
+    float* goff = reinterpret_cast<float*>(take((size_t)noff * 4));
+    float* gm = reinterpret_cast<float*>(take((size_t)nm * 4));
+    float* gwt = reinterpret_cast<float*>(take((size_t)nw * 4));
+    float* gw = reinterpret_cast<float*>(take((size_t)nw * 4));
+    float* gb = reinterpret_cast<float*>(take((size_t)g.outC * 4));
+    const bool nhwc = flags & DCN_INPUT_NHWC;
+    dcn::ZeroList z{};
+    z.add(goff, noff);
+    if (mask) z.add(gm, nm);
+    z.add(gwt, nw);
+    if (grad_bias) z.add(gb, g.outC);
+    DCN_CUDA(dcn::launch_zero(z, stream), "zero");
+    DCN_CUDA(cudaMemsetAsync(gxt, 0, (size_t)nx * 4, stream), "memset");
+    if (nhwc) {  // channels-last: a copy plus the zero row
+      DCN_CUDA(cudaMemcpyAsync(xt, input, (size_t)nx * 2, cudaMemcpyDeviceToDevice, stream),
+               "copy");
+      DCN_CUDA(cudaMemsetAsync(static_cast<char*>(xt) + (size_t)nx * 2, 0, (size_t)g.C * 2,
+                               stream),
+               "memset");
+    } else {
+      DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
+                                             stream),
+               "nchw_to_nhwc");
+    }
+    DCN_CUDA(dcn::launch_prep_go16(g, grad_output, go_r, grad_bias ? gb : nullptr, f16, stream),
+             "tc_prep_go");
+    DCN_CUDA(dcn::launch_pack_weight_bwd16(weight, wbt, g, stream), "tc_pack_weight_bwd");
+    DCN_CUDA(dcn::launch_bwd_fused_tc_h16(g, go_r, wbt, xt, offset, mask, gxt, goff,
+                                          mask ? gm : nullptr, gwt, f16, num_sms_current(),
+                                          stream),
+             f16 ? "bwd_fused_tc_f16" : "bwd_fused_tc_bf16");
+    const char* down = f16 ? "f32_to_f16" : "f32_to_bf16";
+    if (nhwc)
+      DCN_CUDA(dcn::launch_f32_to_h16(gxt, grad_input, nx, f16, stream), down);
+    else
+      DCN_CUDA(dcn::launch_nhwc_to_nchw16(gxt, grad_input, g.N, g.C, g.HW, f16, stream),
+               "nhwc_to_nchw");
+    DCN_CUDA(dcn::launch_f32_to_h16(goff, grad_offset, noff, f16, stream), down);
+    if (mask) DCN_CUDA(dcn::launch_f32_to_h16(gm, grad_mask, nm, f16, stream), down);
+    DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, gw, g, stream), "grad_weight_layout");
+    DCN_CUDA(dcn::launch_f32_to_h16(gw, grad_weight, nw, f16, stream), down);
+    if (grad_bias) DCN_CUDA(dcn::launch_f32_to_h16(gb, grad_bias, g.outC, f16, stream), down);
+    return DCN_OK;
+  }
   const size_t need = bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
   if (workspace_bytes < need || workspace == nullptr)
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
@@ -982,7 +1084,7 @@ DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const
 DCN_API size_t dcn_backward_f16_workspace_size(const dcn_shape* s, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_backward_f16_workspace_size") != DCN_OK) return 0;
-  return bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+  return bwd_h16_ws(g, flags & ~(uint32_t)DCN_INPUT_STAGED);
 }
 
 DCN_API int dcn_backward_f16(const dcn_shape* s, const void* grad_output, const void* input,

@@ -90,6 +90,24 @@ cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* w
                                 const float* xt, const float* off, const float* mask, float* gxt,
                                 float* goff, float* gmask, float* gwt, int num_sms,
                                 cudaStream_t stream);
+// The fused backward for bf16 / fp16 tensors (`f16`): kind::f16 UMMAs with
+// the tensors' 16-bit type, 16-bit gathers and column values, fp32
+// accumulation and fp32 reductions into gxt, goff, gmask, gwt (pre-zeroed,
+// fp32).  `xt`: the 16-bit NHWC copy with its zero row; `go_r`: the 16-bit
+// grad_out rows padded to a multiple of 8 pixels (launch_prep_go16); `wbt`:
+// the 16-bit packed weight (launch_pack_weight_bwd16).  Needs C % 8 == 0.
+bool tc_fused16_supported(const Geom& g);
+cudaError_t launch_bwd_fused_tc_h16(const Geom& g, const void* go_r, const void* wbt,
+                                    const void* xt, const void* off, const void* mask,
+                                    float* gxt, float* goff, float* gmask, float* gwt, bool f16,
+                                    int num_sms, cudaStream_t stream);
+cudaError_t launch_prep_go16(const Geom& g, const void* go, void* go_r, float* gb, bool f16,
+                             cudaStream_t stream);
+cudaError_t launch_pack_weight_bwd16(const void* w, void* wbt, const Geom& g,
+                                     cudaStream_t stream);
+// fp32 NHWC grad-input accumulator -> 16-bit NCHW grad_input.
+cudaError_t launch_nhwc_to_nchw16(const float* gxt, void* gx, int N, int C, int HW, bool f16,
+                                  cudaStream_t stream);
 // Weight gradient as a dense TMA-fed GEMM over the column buffer, summed into
 // `gw` (pre-zeroed): grad_weight itself ([outC][Cg][kh*kw]), or with
 // `tap_major` a [outC][kh*kw][Cg] copy, whose reductions coalesce, for the

@@ -22,4 +22,11 @@ cudaError_t make_tmap_2d_f32(CUtensorMap* map, const float* base, uint64_t inner
 cudaError_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
                               uint64_t pitch_elems, uint32_t box_rows, bool f16 = false);
 
+// 16-bit tensor map with a box of `box_inner` elements (32: 64-byte rows and
+// the 64-byte swizzle; 64: 128-byte rows and the 128-byte swizzle) x
+// `box_rows` rows.
+cudaError_t make_tmap_2d_h16_box(CUtensorMap* map, const void* base, uint64_t inner,
+                                 uint64_t rows, uint64_t pitch_elems, uint32_t box_inner,
+                                 uint32_t box_rows, bool f16);
+
 }  // namespace dcn

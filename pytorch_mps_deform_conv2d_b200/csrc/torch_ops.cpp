@@ -290,22 +290,55 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
   const auto dt = input.scalar_type();
   if (dt == at::kBFloat16 || dt == at::kHalf) {
-    // 16-bit tensors: the gradients are computed by the float32 backward
-    // from upcast copies and returned in the input's dtype
+    // 16-bit tensors: the library's 16-bit backward (the fused tensor-core
+    // kernel with 16-bit operands where it covers the shape, else the fp32
+    // route on upcast copies); gradients in the input's dtype
+    const bool f16 = dt == at::kHalf;
     TORCH_CHECK(grad_output.scalar_type() == dt && weight.scalar_type() == dt &&
                     offset.scalar_type() == dt,
                 "deform_conv2d_backward: grad_output, input, weight and offset must all be "
                 "float32, all bfloat16 or all float16");
-    auto up = [](const at::Tensor& t) { return t.defined() ? t.to(at::kFloat) : t; };
-    c10::optional<at::Tensor> b32;
-    if (bias.has_value() && bias->defined()) b32 = bias->to(at::kFloat);
     TORCH_CHECK(row_begin < 0, "deform_conv2d_backward_rows: float32 tensors only");
-    auto r = backward_impl(up(grad_output), up(input), up(weight), up(offset), up(mask), b32,
-                           stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w, groups,
-                           deformable_groups, -1, math);
-    auto down = [dt](const at::Tensor& t) { return t.to(dt); };
-    return std::make_tuple(down(std::get<0>(r)), down(std::get<1>(r)), down(std::get<2>(r)),
-                           down(std::get<3>(r)), down(std::get<4>(r)));
+    TORCH_CHECK(grad_output.dim() == 4, "grad_output must be 4-D, got ", grad_output.dim());
+    const bool use_mask = mask.defined() && mask.numel() > 0;
+    int64_t out_h = 0, out_w = 0;
+    check_shapes(input, weight, offset, mask, use_mask, stride_h, stride_w, pad_h, pad_w,
+                 dilation_h, dilation_w, groups, deformable_groups, out_h, out_w);
+    TORCH_CHECK(grad_output.size(0) == input.size(0) && grad_output.size(1) == weight.size(0) &&
+                    grad_output.size(2) == out_h && grad_output.size(3) == out_w,
+                "grad_output shape mismatch: expected (", input.size(0), ", ", weight.size(0),
+                ", ", out_h, ", ", out_w, "), got ", grad_output.sizes());
+    const bool use_bias = bias.has_value() && bias->defined() && bias->numel() > 0;
+    c10::cuda::CUDAGuard guard(input.device());
+    auto go = grad_output.contiguous();
+    const bool nhwc = channels_last(input);
+    auto x = nhwc ? input : input.contiguous();
+    auto w = weight.contiguous();
+    auto off = offset.contiguous();
+    auto msk = use_mask ? mask.contiguous() : at::Tensor();
+    auto grad_input = at::empty_like(x);
+    auto grad_offset = at::empty_like(off);
+    auto grad_mask = use_mask ? at::empty_like(msk) : at::empty({0}, x.options());
+    auto grad_weight = at::empty_like(w);
+    auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
+    if (x.numel() == 0 && off.numel() == 0) {
+      grad_weight.zero_();
+      if (use_bias) grad_bias.zero_();
+      return std::make_tuple(grad_input, grad_offset, grad_mask, grad_weight, grad_bias);
+    }
+    const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                                   dilation_w, groups, deformable_groups);
+    const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
+    const size_t ws_bytes = f16 ? dcn_backward_f16_workspace_size(&s, flags)
+                                : dcn_backward_bf16_workspace_size(&s, flags);
+    auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
+    auto vp = [](const at::Tensor& t) -> void* { return t.numel() ? t.data_ptr() : nullptr; };
+    auto bwd16 = f16 ? dcn_backward_f16 : dcn_backward_bf16;
+    check_rc(bwd16(&s, vp(go), vp(x), vp(w), vp(off), use_mask ? vp(msk) : nullptr,
+                   vp(grad_input), vp(grad_offset), use_mask ? vp(grad_mask) : nullptr,
+                   vp(grad_weight), use_bias ? vp(grad_bias) : nullptr, flags, ws.data_ptr(),
+                   ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
+    return std::make_tuple(grad_input, grad_offset, grad_mask, grad_weight, grad_bias);
   }
   TORCH_CHECK(grad_output.scalar_type() == at::kFloat && input.scalar_type() == at::kFloat &&
                   weight.scalar_type() == at::kFloat && offset.scalar_type() == at::kFloat,

@@ -1,8 +1,11 @@
 """16-bit I/O: every tensor bf16, or every tensor fp16.  Forward on tcgen05
 with 16-bit operands of the same type when channels per group and per
-deformable group are multiples of 64, else the fp32 kernels on upcast copies;
-backward through the fp32 kernels on upcast copies, gradients returned in the
-input's dtype.  Parity against the oracle run on the same rounded inputs:
+deformable group are multiples of 64, else the fp32 kernels on upcast copies.
+Backward on the fused tensor-core kernel with 16-bit operands of the same type
+(kind::f16: 16-bit corner gathers and column values, fp32 accumulation and
+fp32 reductions) when channels per group and per deformable group are
+multiples of 32 and a group has at most 256 out channels, else the fp32 route
+on upcast copies; gradients returned in the input's dtype.  Parity against the oracle run on the same rounded inputs:
 norm-wise relative error <= 1e-2 for outputs and gradients (bf16 keeps 8
 mantissa bits, fp16 11: one rounding of the column values and one of the
 result are ~2e-3 each in bf16)."""
@@ -81,17 +84,29 @@ def test_half_forward(cuda_device, name, dtype):
     np.testing.assert_allclose(got, ref, rtol=0, atol=2 * TOL * float(np.abs(ref).max()))
 
 
+def _fused16(spec):
+    """Whether the fused 16-bit tensor-core backward covers the case."""
+    g = spec.get("groups", 1)
+    cg, og = spec["inC"] // g, spec["outC"] // g
+    cpg = spec["inC"] // spec.get("dg", 1)
+    return cg % 32 == 0 and cpg % 32 == 0 and og % 16 == 0 and og <= 256 and spec["inC"] % 8 == 0
+
+
 @pytest.mark.parametrize("dtype", sorted(DTYPES))
-@pytest.mark.parametrize("name", ["c64-o64", "c128-o64-g2-v1-nobias", "c6-o6-g3-upcast"])
+@pytest.mark.parametrize("name", sorted(CASES))
 def test_half_backward(cuda_device, name, dtype):
-    dt, _ = DTYPES[dtype]
+    dt, tag = DTYPES[dtype]
     spec, _ = CASES[name]
     case, c16, c32 = _bf16_case(spec, dt)
-    dcn.set_math_mode("fp32")
+    _native.profiler_read()
+    _native.profiler_enable(True)
     try:
         out, grads = _run(case, c16, backward=True)
     finally:
-        dcn.set_math_mode(None)
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    fused = f"bwd_fused_tc_{tag}"
+    assert (fused in stats) == _fused16(spec), sorted(stats)
     ref, rgrads = run_oracle(c32)
     assert rel_norm_err(out.detach().float().cpu().numpy(), ref) <= TOL
     assert set(grads) == set(rgrads)
