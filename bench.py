@@ -184,6 +184,69 @@ def measure_matmul_tflops(dtype_mode, n=8192, reps=5):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
+def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
+    """L2 <-> SM bandwidth of this GPU, best of `reps`: the library's probe
+    (dcn_l2_probe) sweeping an L2-resident buffer with 16-byte loads cached
+    in L2 only (kind 0, the corner gathers), with 16-byte fp32 reductions
+    (kind 1, the col2im scatter), and with both in one loop, 5 loads to 2
+    reductions (kind 2).  Returns {"l2_to_sm", "sm_to_l2_red", "mixed_5to2"}
+    in GB/s (kind 2: bytes read plus bytes reduced)."""
+    import ctypes
+
+    import torch
+    from pytorch_mps_deform_conv2d_b200 import _native
+    lib = _native.load_capi()
+    buf = torch.zeros(bytes_ // 4, device="cuda")
+    stream = torch.cuda.current_stream()
+    out = {}
+    for kind, name in ((0, "l2_to_sm"), (1, "sm_to_l2_red"), (2, "mixed_5to2")):
+        def launch():
+            rc = lib.dcn_l2_probe(kind, ctypes.c_void_p(buf.data_ptr()), bytes_, passes,
+                                  ctypes.c_void_p(stream.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"dcn_l2_probe({kind}) failed: {rc}")
+        for _ in range(2):
+            launch()
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            launch()
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        moved = bytes_ if kind < 2 else (bytes_ // 3584) * 3584
+        out[name] = round(moved * passes / (best * 1e-3) / 1e9, 1)
+    del buf
+    return out
+
+
+def binding_roofline(traffic, avg_ms, l2_peaks):
+    """The dominant kernel against the L2 <-> SM crossbar.  Bytes it moved
+    each way in one launch (ncu: l1tex__m_xbar2l1tex_read_bytes.sum and
+    l1tex__m_l1tex2xbar_write_bytes.sum, from the committed profile of the
+    same workload and mode) over its live launch time.  `frac` sets the
+    launch time against the time the mixed probe (5 bytes loaded to 2 bytes
+    reduced, about the fused backward's ratio) takes for the same bytes;
+    `frac_load` / `frac_red` are each direction against its own probe."""
+    if not traffic or "l2_to_sm_bytes" not in traffic or not l2_peaks:
+        return None
+    rd, wr = float(traffic["l2_to_sm_bytes"]), float(traffic.get("sm_to_l2_bytes", 0.0))
+    t = avg_ms * 1e-3
+    a_rd, a_wr = rd / t / 1e9, wr / t / 1e9
+    t_mixed = (rd + wr) / (l2_peaks["mixed_5to2"] * 1e9)
+    return {"resource": "L2 <-> SM crossbar (loads + fp32 reductions)", "unit": "GB/s",
+            "l2_to_sm_bytes": rd, "sm_to_l2_bytes": wr,
+            "achieved": round(a_rd + a_wr, 1), "peak": l2_peaks["mixed_5to2"],
+            "frac": round(t_mixed / t, 3),
+            "achieved_l2_to_sm": round(a_rd, 1), "peak_l2_to_sm": l2_peaks["l2_to_sm"],
+            "frac_load": round(a_rd / l2_peaks["l2_to_sm"], 3),
+            "achieved_sm_to_l2": round(a_wr, 1), "peak_sm_to_l2_red": l2_peaks["sm_to_l2_red"],
+            "frac_red": round(a_wr / l2_peaks["sm_to_l2_red"], 3),
+            "peak_source": "dcn_l2_probe in this run (64 MiB L2-resident buffer, all SMs)",
+            "bytes_source": traffic.get("source")}
+
+
 # ---------------------------------------------------------------------------
 # clocks
 # ---------------------------------------------------------------------------
@@ -476,9 +539,11 @@ def run_ours(args, wl):
     if args.profile:
         peak_tf32 = 0.5 * peaks.get("bf16_tflops", 1590.0)
         peak_fp32 = peak_tf32 / 8.0
+        l2_peaks = None
     else:
         peak_tf32 = measure_matmul_tflops("tf32")
         peak_fp32 = measure_matmul_tflops("fp32")
+        l2_peaks = measure_l2_gbs()
     # TF32 denominator: the larger of this run's cuBLAS TF32 GEMM and half the
     # measured bf16 peak (TF32 runs at half the bf16 rate on these tensor cores)
     half_bf16 = 0.5 * float(peaks.get("bf16_tflops", 1590.0))
@@ -508,6 +573,8 @@ def run_ours(args, wl):
                     bytes_per_launch=amount)
     traffic = load_traffic().get(f"{args.workload}:{args.math}:{dom}")
     roof["traffic"] = traffic["bytes_per_launch"] if traffic else None
+    roof["binding"] = binding_roofline(traffic, avg_ms, l2_peaks)
+    roof["l2_peaks_gbs"] = l2_peaks
     work = algorithmic_work(wl)
     step_roof_ms = work["flops"] / ((peak_tf32_used if args.math != "fp32" else peak_fp32) * 1e12) * 1e3
     roof["step_roofline_ms"] = round(max(step_roof_ms, work["bytes"] / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3), 4)
@@ -524,7 +591,8 @@ def run_ours(args, wl):
         "metric": METRIC, "value": round(value, 4), "unit": "ms/iter", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": False, "scaling": args.scaling, "vs_baseline": None,
-        "dtype": ((f"{args.dtype} I/O, " if args.dtype in HALF else "") +
+        "dtype": (args.dtype if any(k in BF16_KERNELS for k in kernels) else
+                  (f"{args.dtype} I/O, " if args.dtype in HALF else "") +
                   (args.math if any(k in TC_KERNELS for k in kernels) else "f32")),
         "data": "synthetic",
         "config": bench_config(wl, args),

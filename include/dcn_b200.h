@@ -304,6 +304,20 @@ DCN_API int dcn_stage_input(const dcn_shape* shape, const float* input, float* s
  * capture). */
 DCN_API int dcn_device_status(void* stream, int clear, int* status);
 
+/* L2 <-> SM bandwidth probe (a diagnostic; no reference counterpart).
+ * Enqueues on `stream` one kernel over all SMs that sweeps `passes` times over
+ * `bytes` (rounded down to 16) of the device buffer `buf` (16-byte aligned):
+ * kind 0 reads 16-byte vectors cached in L2 only, as the corner gathers do;
+ * kind 1 adds 1.0f to every fp32 with 16-byte reductions, as the col2im
+ * scatter does (kind 1 modifies the buffer); kind 2 does both in one loop,
+ * five 16-byte loads to two 16-byte reductions: of the bytes swept (rounded
+ * down to a multiple of 3584) the first 5/7 are read, 1.0f is added to every
+ * fp32 of the last 2/7.  With `bytes` well under the L2 size, bytes x passes
+ * over the kernel's device time is the L2 -> SM (kind 0), SM -> L2 reduction
+ * (kind 1) or mixed (kind 2) bandwidth the hot kernels are set against.
+ * The caller times it (CUDA events on `stream`). */
+DCN_API int dcn_l2_probe(int kind, void* buf, size_t bytes, int passes, void* stream);
+
 /* Kernel profiler (no reference counterpart: the reference times its ops
  * with wall clocks around torch.mps.synchronize(), benchmarks/bench.py:39-49).
  * When enabled, every kernel launch and scratch memset of the entry points

@@ -105,6 +105,8 @@ def load_capi():
         lib.dcn_col2im_coord.restype = ctypes.c_int
         lib.dcn_device_status.argtypes = [vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         lib.dcn_device_status.restype = ctypes.c_int
+        lib.dcn_l2_probe.argtypes = [ctypes.c_int, vp, ctypes.c_size_t, ctypes.c_int, vp]
+        lib.dcn_l2_probe.restype = ctypes.c_int
         lib.dcn_profiler_enable.argtypes = [ctypes.c_int]
         lib.dcn_profiler_enable.restype = ctypes.c_int
         lib.dcn_profiler_read.argtypes = [ctypes.POINTER(KernelStat), ctypes.c_int,

@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "dcn_kernels.h"
 #include "dcn_launch.h"
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
@@ -49,33 +50,45 @@ int pow2_cols(int n) {
 // ---------------------------------------------------------------------------
 // With `split` (3xTF32) the low TF32 parts fill rows N*outC .. 2*N*outC-1.
 // Pixels P .. Ppad-1 of a row are zero.  A block covers PG_SPAN pixels of one
-// (image, out channel) row -- 16-byte accesses when P % 4 == 0 -- and, with
-// `gb` (pre-zeroed grad_bias), adds its row's sum with one atomic.
-constexpr int PG_SPAN = 2048;
-__global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
-                                                      float* __restrict__ go_r,
-                                                      float* __restrict__ gb, int N, int outC,
-                                                      int P, int Ppad, int pspans, int split,
-                                                      int vec) {
+// (image, out channel) row -- 16-byte accesses when P % 4 == 0, all four of a
+// thread's loads issued before their stores -- and, with `gb` (pre-zeroed
+// grad_bias), adds its row's sum with one atomic, or with `gpart` writes it
+// to gpart[bid] (no atomics; bias_from_parts sums them).  `bid`: the block's
+// index among the prep blocks (256 threads).
+constexpr int PG_SPAN = 4096;
+constexpr int PG_UNROLL = PG_SPAN / (4 * 256);  // float4 loads in flight a thread
+__device__ __forceinline__ void prep_go_block(long long bid, const float* __restrict__ go,
+                                              float* __restrict__ go_r, float* __restrict__ gb,
+                                              float* __restrict__ gpart, int N, int outC, int P,
+                                              int Ppad, int pspans, int split, int vec) {
   __shared__ float part[8];
-  const long long row = blockIdx.x / pspans;  // n * outC + o
-  const int pbeg = (int)(blockIdx.x - row * pspans) * PG_SPAN;
+  const long long row = bid / pspans;  // n * outC + o
+  const int pbeg = (int)(bid - row * pspans) * PG_SPAN;
   const int pend = min(Ppad, pbeg + PG_SPAN);
   const float* src = go + row * P;
   float* hi = go_r + row * Ppad;
   float* lo = go_r + ((long long)N * outC + row) * Ppad;
   float sum = 0.f;
   if (vec) {  // P % 4 == 0: Ppad == P, 16-byte aligned rows
-    for (int p = pbeg + 4 * threadIdx.x; p < pend; p += 4 * blockDim.x) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(src + p));
-      const float4 h = make_float4(tc::to_tf32(v.x), tc::to_tf32(v.y), tc::to_tf32(v.z),
-                                   tc::to_tf32(v.w));
+    float4 v[PG_UNROLL];
+#pragma unroll
+    for (int u = 0; u < PG_UNROLL; ++u) {
+      const int p = pbeg + 4 * (threadIdx.x + u * 256);
+      v[u] = p < pend ? __ldg(reinterpret_cast<const float4*>(src + p))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < PG_UNROLL; ++u) {
+      const int p = pbeg + 4 * (threadIdx.x + u * 256);
+      if (p >= pend) continue;
+      const float4 h = make_float4(tc::to_tf32(v[u].x), tc::to_tf32(v[u].y),
+                                   tc::to_tf32(v[u].z), tc::to_tf32(v[u].w));
       *reinterpret_cast<float4*>(hi + p) = h;
       if (split)
         *reinterpret_cast<float4*>(lo + p) =
-            make_float4(tc::to_tf32(v.x - h.x), tc::to_tf32(v.y - h.y), tc::to_tf32(v.z - h.z),
-                        tc::to_tf32(v.w - h.w));
-      sum += (v.x + v.y) + (v.z + v.w);
+            make_float4(tc::to_tf32(v[u].x - h.x), tc::to_tf32(v[u].y - h.y),
+                        tc::to_tf32(v[u].z - h.z), tc::to_tf32(v[u].w - h.w));
+      sum += (v[u].x + v[u].y) + (v[u].z + v[u].w);
     }
   } else {
     for (int p = pbeg + threadIdx.x; p < pend; p += blockDim.x) {
@@ -86,7 +99,7 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
       sum += v;
     }
   }
-  if (gb == nullptr) return;
+  if (gb == nullptr && gpart == nullptr) return;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
@@ -94,8 +107,16 @@ __global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ 
   if (threadIdx.x == 0) {
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
-    atomicAdd(gb + row % outC, t);
+    if (gpart != nullptr) gpart[bid] = t;
+    else atomicAdd(gb + row % outC, t);
   }
+}
+__global__ void __launch_bounds__(256) prep_go_kernel(const float* __restrict__ go,
+                                                      float* __restrict__ go_r,
+                                                      float* __restrict__ gb, int N, int outC,
+                                                      int P, int Ppad, int pspans, int split,
+                                                      int vec) {
+  prep_go_block(blockIdx.x, go, go_r, gb, nullptr, N, outC, P, Ppad, pspans, split, vec);
 }
 
 // MN-major A operands (M contiguous: the channels of the weight gradient's
@@ -1182,13 +1203,13 @@ bwd_weight_col_kernel(Geom g, const __grid_constant__ CUtensorMap colmap,
 // wb_t[(g*kk + k)*Cg + c][o] = tf32(W[g*Og + o][c][k])  (B of bwd_data: rows = channels);
 // with `split`, the low parts follow in rows G*kk*Cg ..  Per group a 32 x 32
 // tile transpose of W viewed as [o][c*kk + k]: coalesced on both sides.
-__global__ void __launch_bounds__(256) tc_pack_weight_bwd_kernel(const float* __restrict__ w,
-                                                                 float* __restrict__ wb, Geom g,
-                                                                 int split) {
+__device__ __forceinline__ void pack_weight_bwd_tile(int bx, int by, int gi,
+                                                     const float* __restrict__ w,
+                                                     float* __restrict__ wb, const Geom& g,
+                                                     int split) {
   __shared__ float tile[32][33];
-  const int gi = blockIdx.z;
   const int CK = g.Cg * g.kk;
-  const int o0 = blockIdx.y * 32, ck0 = blockIdx.x * 32;
+  const int o0 = by * 32, ck0 = bx * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const float* src = w + (long long)gi * g.Og * CK;
 #pragma unroll
@@ -1210,6 +1231,11 @@ __global__ void __launch_bounds__(256) tc_pack_weight_bwd_kernel(const float* __
       if (split) wb[lo + idx] = tc::to_tf32(v - hi);
     }
   }
+}
+__global__ void __launch_bounds__(256) tc_pack_weight_bwd_kernel(const float* __restrict__ w,
+                                                                 float* __restrict__ wb, Geom g,
+                                                                 int split) {
+  pack_weight_bwd_tile(blockIdx.x, blockIdx.y, blockIdx.z, w, wb, g, split);
 }
 
 int weight_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
@@ -1938,6 +1964,87 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
   return cudaGetLastError();
 }
 
+namespace {
+// The fused backward's helpers in one launch (staged input, TF32): blocks
+// [0, nb_prep) prepare grad_out rows (grad_bias as per-block partial sums),
+// the next nb_pack blocks pack the weight (one 32 x 32 tile each), the last
+// nb_zero blocks zero the accumulators, grid-stride.  Blocks are independent.
+struct Prologue {
+  const float* go;
+  float* go_r;
+  float* gpart;
+  const float* w;
+  float* wbt;
+  float* zp[4];
+  long long zn[4];
+  int zcount;
+  int Ppad, pspans, vec;
+  int nb_prep, pack_x, pack_y, nb_pack, nb_zero;
+};
+__global__ void __launch_bounds__(256) bwd_prologue_kernel(Prologue a, Geom g) {
+  int b = blockIdx.x;
+  if (b < a.nb_prep) {
+    prep_go_block(b, a.go, a.go_r, nullptr, a.gpart, g.N, g.outC, g.P, a.Ppad, a.pspans, 0,
+                  a.vec);
+    return;
+  }
+  b -= a.nb_prep;
+  if (b < a.nb_pack) {
+    const int per_g = a.pack_x * a.pack_y;
+    const int gi = b / per_g, r = b - gi * per_g;
+    pack_weight_bwd_tile(r % a.pack_x, r / a.pack_x, gi, a.w, a.wbt, g, 0);
+    return;
+  }
+  b -= a.nb_pack;
+  const long long stride = (long long)a.nb_zero * blockDim.x;
+  const long long t0 = (long long)b * blockDim.x + threadIdx.x;
+  for (int l = 0; l < a.zcount; ++l) {
+    float* p = a.zp[l];
+    const long long n = a.zn[l];
+    const long long n4 = (reinterpret_cast<uintptr_t>(p) & 15u) == 0 ? n >> 2 : 0;
+    float4* p4 = reinterpret_cast<float4*>(p);
+    for (long long i = t0; i < n4; i += stride) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long long i = (n4 << 2) + t0; i < n; i += stride) p[i] = 0.f;
+  }
+}
+}  // namespace
+
+size_t tc_bias_part_floats(const Geom& g) {
+  const int Ppad = (g.P + 3) & ~3;
+  return (size_t)g.N * g.outC * ((Ppad + PG_SPAN - 1) / PG_SPAN);
+}
+
+cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, float* gpart,
+                                const float* w, float* wbt, const ZeroList& z,
+                                cudaStream_t stream) {
+  Prologue a{};
+  a.go = go;
+  a.go_r = go_r;
+  a.gpart = gpart;
+  a.w = w;
+  a.wbt = wbt;
+  a.zcount = z.count;
+  for (int l = 0; l < z.count; ++l) {
+    a.zp[l] = z.ptr[l];
+    a.zn[l] = z.n[l];
+  }
+  a.Ppad = (g.P + 3) & ~3;
+  a.pspans = (a.Ppad + PG_SPAN - 1) / PG_SPAN;
+  a.vec = g.P % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
+          (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0;
+  const long long prep = (long long)g.N * g.outC * a.pspans;
+  a.pack_x = (g.Cg * g.kk + 31) / 32;
+  a.pack_y = (g.Og + 31) / 32;
+  const long long pack = (long long)a.pack_x * a.pack_y * g.G;
+  a.nb_zero = device_sm_count() * 4;
+  const long long blocks = prep + pack + a.nb_zero;
+  if (blocks > (1LL << 31) - 1 || g.P == 0) return cudaErrorInvalidValue;
+  a.nb_prep = (int)prep;
+  a.nb_pack = (int)pack;
+  bwd_prologue_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a, g);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_bwd_data_tc(const Geom& g, const float* go_r, bool split, const float* wbt,
                                const float* xt, const float* off, const float* mask, float* gxt,
                                float* goff, float* gmask, float* col, cudaStream_t stream) {
@@ -2023,24 +2130,40 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
 // gwt[o][k][c] -> gw[o][c][k]: one thread per (o, c); a warp reads 32
 // consecutive channels of each tap (coalesced) and writes 32 x kk consecutive
 // floats.
+// With `gpart`: also grad_bias[o] = the sum of the prologue's partial sums
+// of out channel o, in a fixed order.
 __global__ void __launch_bounds__(256) weight_from_tap_major_kernel(
-    const float* __restrict__ gwt, float* __restrict__ gw, int Cg, int kk, long long total) {
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const float* __restrict__ gwt, float* __restrict__ gw, int Cg, int kk, long long total,
+    const float* __restrict__ gpart, float* __restrict__ gb, int N, int outC, int pspans) {
+  const long long stride = (long long)gridDim.x * 256;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += stride) {
     const long long o = i / Cg;
     const int c = (int)(i - o * Cg);
     const float* src = gwt + o * Cg * kk + c;
     float* dst = gw + i * kk;
     for (int k = 0; k < kk; ++k) dst[k] = __ldg(src + (long long)k * Cg);
   }
+  if (gpart == nullptr) return;
+  for (long long o = blockIdx.x * 256LL + threadIdx.x; o < outC; o += stride) {
+    float t = 0.f;
+    for (int n = 0; n < N; ++n) {
+      const float* q = gpart + ((long long)n * outC + o) * pspans;
+      for (int sp = 0; sp < pspans; ++sp) t += __ldg(q + sp);
+    }
+    gb[o] = t;
+  }
 }
 
 cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
-                                         cudaStream_t stream) {
+                                         cudaStream_t stream, const float* gpart, float* gb) {
   const long long total = (long long)g.outC * g.Cg;
   if (total == 0 || g.kk == 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 16) blocks = 148LL * 16;
-  weight_from_tap_major_kernel<<<(int)blocks, 256, 0, stream>>>(gwt, gw, g.Cg, g.kk, total);
+  const int Ppad = (g.P + 3) & ~3;
+  const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
+  weight_from_tap_major_kernel<<<(int)blocks, 256, 0, stream>>>(
+      gwt, gw, g.Cg, g.kk, total, gb != nullptr ? gpart : nullptr, gb, g.N, g.outC, pspans);
   return cudaGetLastError();
 }
 
@@ -2112,7 +2235,7 @@ template <int FMT>
 __global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __restrict__ go,
                                                         unsigned short* __restrict__ go_r,
                                                         float* __restrict__ gb, int outC, int P,
-                                                        int Ppad, int pspans) {
+                                                        int Ppad, int pspans, int vec) {
   __shared__ float part[8];
   const long long row = blockIdx.x / pspans;  // n * outC + o
   const int pbeg = (int)(blockIdx.x - row * pspans) * PG_SPAN;
@@ -2120,11 +2243,21 @@ __global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __
   const unsigned short* src = go + row * P;
   unsigned short* dst = go_r + row * Ppad;
   float sum = 0.f;
-  for (int p = pbeg + threadIdx.x; p < pend; p += blockDim.x) {
-    const unsigned short v = p < P ? __ldg(src + p) : (unsigned short)0;
-    dst[p] = v;
-    if constexpr (FMT == kF16s) sum += __half2float(__ushort_as_half(v));
-    else sum += __uint_as_float((uint32_t)v << 16);
+  if (vec) {  // P % 8 == 0: Ppad == P, 16-byte aligned rows, 8 values a load
+    for (int p = pbeg + 8 * threadIdx.x; p < pend; p += 8 * blockDim.x) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + p));
+      *reinterpret_cast<uint4*>(dst + p) = v;
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sum += h_lo<FMT>(w[e]) + h_hi<FMT>(w[e]);
+    }
+  } else {
+    for (int p = pbeg + threadIdx.x; p < pend; p += blockDim.x) {
+      const unsigned short v = p < P ? __ldg(src + p) : (unsigned short)0;
+      dst[p] = v;
+      if constexpr (FMT == kF16s) sum += __half2float(__ushort_as_half(v));
+      else sum += __uint_as_float((uint32_t)v << 16);
+    }
   }
   if (gb == nullptr) return;
 #pragma unroll
@@ -2183,7 +2316,52 @@ __global__ void __launch_bounds__(256) nhwc_to_nchw16_kernel(const float* __rest
     }
   }
 }
+
+// The 16-bit backward's gradients in one launch: the tap-major fp32 weight
+// gradient gwt[o][k][c] to grad_weight[o][c][k], then up to three fp32
+// arrays element-wise (grad_offset, grad_mask, grad_bias), all rounded to 16
+// bits (to nearest even).  One index space over all of them, grid-stride.
+template <int FMT>
+__global__ void __launch_bounds__(256) grads_to_h16_kernel(const float* __restrict__ gwt,
+                                                           unsigned short* __restrict__ gw,
+                                                           int Cg, int kk, long long nw,
+                                                           H16List rest) {
+  const long long total = nw + rest.n[0] + rest.n[1] + rest.n[2];
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    float v;
+    unsigned short* dst;
+    if (i < nw) {  // i = (o*Cg + c)*kk + k
+      const long long ock = (long long)Cg * kk;
+      const long long o = i / ock;
+      const int r = (int)(i - o * ock);
+      const int c = r / kk, k = r - c * kk;
+      v = __ldg(gwt + o * ock + (long long)k * Cg + c);
+      dst = gw + i;
+    } else {
+      long long j = i - nw;
+      int a = 0;
+      while (a < 2 && j >= rest.n[a]) j -= rest.n[a++];
+      v = __ldg(rest.src[a] + j);
+      dst = rest.dst[a] + j;
+    }
+    if constexpr (FMT == kF16s) *dst = __half_as_ushort(__float2half_rn(v));
+    else *dst = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+}
 }  // namespace
+
+cudaError_t launch_grads_to_h16(const float* gwt, void* gw, const Geom& g, const H16List& rest,
+                                bool f16, cudaStream_t stream) {
+  const long long nw = (long long)g.outC * g.Cg * g.kk;
+  const long long total = nw + rest.n[0] + rest.n[1] + rest.n[2];
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 8) blocks = 148LL * 8;
+  auto kern = f16 ? grads_to_h16_kernel<kF16s> : grads_to_h16_kernel<kBF16s>;
+  kern<<<(int)blocks, 256, 0, stream>>>(gwt, static_cast<unsigned short*>(gw), g.Cg, g.kk, nw,
+                                        rest);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_prep_go16(const Geom& g, const void* go, void* go_r, float* gb, bool f16,
                              cudaStream_t stream) {
@@ -2192,10 +2370,12 @@ cudaError_t launch_prep_go16(const Geom& g, const void* go, void* go_r, float* g
   const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
   const long long blocks = (long long)g.N * g.outC * pspans;
   if (blocks > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  const int vec = g.P % 8 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0;
   auto kern = f16 ? prep_go16_kernel<kF16s> : prep_go16_kernel<kBF16s>;
   kern<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const unsigned short*>(go),
                                               static_cast<unsigned short*>(go_r), gb, g.outC,
-                                              g.P, Ppad, pspans);
+                                              g.P, Ppad, pspans, vec);
   return cudaGetLastError();
 }
 

@@ -348,6 +348,8 @@ size_t bwd_ws(const dcn::Geom& g, uint32_t flags) {
       b += align_up(dcn::tc_col_bytes(g, split_math(flags)));                  // column buffer
     else if (!use_fused_bwd(g, flags))
       b += align_up(dcn::tc_plan_bytes(g));                                    // sampling plans
+    else
+      b += align_up(dcn::tc_bias_part_floats(g) * sizeof(float));              // bias partial sums
   } else {
     b += align_up((size_t)g.G * g.kk * g.Og * g.Cg * sizeof(float));   // packed weight
   }
@@ -589,6 +591,11 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
     const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, false, true, sms);
     const size_t usable = workspace_bytes - (size_t)(tail - static_cast<char*>(workspace));
     if (tail_bytes == 0 || usable < tail_bytes) tail = nullptr;
+    // the weight pack (side stream) runs beside the input staging
+    Fork fk(stream, side_streams_pay(g));
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bf16(weight, wt, g, tail, fk.side(0)),
+                "tc_pack_weight");
     if (flags & DCN_INPUT_NHWC) {  // channels-last: a copy plus the zero row
       const size_t xb = (size_t)g.N * g.HW * g.C * 2;
       if (xb) DCN_CUDA(cudaMemcpyAsync(xt, input, xb, cudaMemcpyDeviceToDevice, stream), "copy");
@@ -599,7 +606,7 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
                                              stream),
                "nchw_to_nhwc");
     }
-    DCN_CUDA(dcn::launch_tc_pack_weight_bf16(weight, wt, g, tail, stream), "tc_pack_weight");
+    DCN_ORDER(fk.join(0), "join");
     DCN_CUDA(dcn::launch_fwd_tc_bf16(g, xt, wt, offset, mask, bias, output, f16, tail,
                                      tail ? tail_bytes : 0, sms, stream),
              f16 ? "fwd_tc_f16" : "fwd_tc_bf16");
@@ -752,24 +759,57 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     // then puts it in grad_weight's layout
     float* gwt = ws.take(w_bytes / sizeof(float));
     z.add(gwt, (long long)(w_bytes / sizeof(float)));
-    // grad_out prep (side 0, after zeroing grad_bias, which it sums into) and
-    // the weight pack + the zeroing of the other accumulators (side 1) run
-    // beside the input transpose
+    if (staged && use_fused_bwd(g, flags)) {
+      // the helpers in one launch on the caller's stream (no cross-stream
+      // waits): grad_out rows with grad_bias partial sums, the packed weight,
+      // the zeroed accumulators; then the fused kernel; then grad_input back
+      // to NCHW beside the grad_weight layout, which also sums grad_bias
+      float* gpart = ws.take(dcn::tc_bias_part_floats(g));
+      z.add(gxt, (long long)(x_bytes / sizeof(float)));
+      DCN_CUDA(dcn::launch_bwd_prologue(g, grad_output, go_r, bias_in_prep ? gpart : nullptr,
+                                        weight, wbt, z, stream),
+               "bwd_prologue");
+      DCN_CUDA(dcn::launch_bwd_fused_tc(g, go_r, wbt, xt, offset, mask, gxt, grad_offset,
+                                        grad_mask, gwt, num_sms_current(), stream),
+               "bwd_fused_tc");
+      float* gb_out = bias_in_prep ? grad_bias : nullptr;
+      if (nhwc) {
+        DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream, gpart, gb_out),
+                 "grad_weight_layout");
+        return DCN_OK;
+      }
+      Fork fk(stream, side_streams_pay(g));
+      DCN_ORDER(fk.fork(), "fork");
+      DCN_CUDA_ON(fk.side(0),
+                  dcn::launch_weight_from_tap_major(gwt, grad_weight, g, fk.side(0), gpart,
+                                                    gb_out),
+                  "grad_weight_layout");
+      DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
+      DCN_ORDER(fk.join(0), "join");
+      return DCN_OK;
+    }
+    // The grad_out prep (after zeroing grad_bias, which it sums into) stays
+    // on the caller's stream, where it starts at once: it is the longest
+    // helper.  The weight pack + the zeroing of the other accumulators (side
+    // 0) and the input staging or the grad-input zeroing (side 1) run beside
+    // it, behind the cross-stream wait.
     Fork fk(stream, side_streams_pay(g));
     DCN_ORDER(fk.fork(), "fork");
-    if (bias_in_prep) {
-      dcn::ZeroList zb{};
-      zb.add(grad_bias, g.outC);
-      DCN_CUDA_ON(fk.side(0), dcn::launch_zero(zb, fk.side(0)), "zero");
-    }
-    DCN_CUDA_ON(fk.side(0),
-                dcn::launch_tc_prep_go(g, grad_output, go_r, bias_in_prep ? grad_bias : nullptr,
-                                       split, fk.side(0)),
-                "tc_prep_go");
-    DCN_CUDA_ON(fk.side(1), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(1)),
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(0)),
                 "tc_pack_weight_bwd");
-    DCN_CUDA_ON(fk.side(1), dcn::launch_zero(z, fk.side(1)), "zero");
-    DCN_CUDA(stage_input(), stage_name);
+    DCN_CUDA_ON(fk.side(0), dcn::launch_zero(z, fk.side(0)), "zero");
+    const cudaStream_t stage_stream = fk.side(1);
+    DCN_CUDA_ON(stage_stream,
+                staged ? cudaMemsetAsync(gxt, 0, x_bytes, stage_stream)
+                : nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stage_stream)
+                       : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt,
+                                                  stage_stream),
+                stage_name);
+    if (bias_in_prep)
+      DCN_CUDA(cudaMemsetAsync(grad_bias, 0, (size_t)g.outC * sizeof(float), stream), "memset");
+    DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_r, bias_in_prep ? grad_bias : nullptr,
+                                    split, stream),
+             "tc_prep_go");
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
     if (use_fused_bwd(g, flags)) {
@@ -781,13 +821,11 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
                  "grad_weight_layout");
         return DCN_OK;
       }
-      // grad_input back to NCHW (side 0) beside the grad_weight layout
+      // grad_input back to NCHW, and the grad_weight layout beside it (side 0)
       DCN_ORDER(fk.fork(), "fork");
-      DCN_CUDA_ON(fk.side(0),
-                  dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, fk.side(0)),
-                  "nhwc_to_nchw");
-      DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
-               "grad_weight_layout");
+      DCN_CUDA_ON(fk.side(0), dcn::launch_weight_from_tap_major(gwt, grad_weight, g, fk.side(0)),
+                  "grad_weight_layout");
+      DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
       DCN_ORDER(fk.join(0), "join");
       return DCN_OK;
     }
@@ -921,13 +959,13 @@ static bool use_fused16(const dcn::Geom& g, uint32_t flags) {
 
 // Its workspace: the 16-bit staging copy, grad_out rows and packed weight;
 // fp32 accumulators of grad_input (NHWC), grad_offset, grad_mask, the
-// tap-major grad_weight and grad_bias; the fp32 grad_weight in place.
+// tap-major grad_weight and grad_bias.
 static size_t bwd_fused16_bytes(const dcn::Geom& g) {
   const size_t w = (size_t)g.outC * g.Cg * g.kk;
   return align_up(((size_t)g.N * g.HW * g.C + g.C) * 2) +
          align_up((size_t)g.N * g.outC * ((g.P + 7) & ~7) * 2) + align_up(w * 2) +
          align_up((size_t)g.N * g.HW * g.C * 4) + align_up((size_t)g.N * 2 * g.dg * g.kk * g.P * 4) +
-         align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + 2 * align_up(w * 4) +
+         align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + align_up(w * 4) +
          align_up((size_t)g.outC * 4) + kAlign;
 }
 
@@ -990,45 +1028,60 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
     float* goff = reinterpret_cast<float*>(take((size_t)noff * 4));
     float* gm = reinterpret_cast<float*>(take((size_t)nm * 4));
     float* gwt = reinterpret_cast<float*>(take((size_t)nw * 4));
-    float* gw = reinterpret_cast<float*>(take((size_t)nw * 4));
     float* gb = reinterpret_cast<float*>(take((size_t)g.outC * 4));
     const bool nhwc = flags & DCN_INPUT_NHWC;
     dcn::ZeroList z{};
     z.add(goff, noff);
     if (mask) z.add(gm, nm);
     z.add(gwt, nw);
-    if (grad_bias) z.add(gb, g.outC);
-    DCN_CUDA(dcn::launch_zero(z, stream), "zero");
-    DCN_CUDA(cudaMemsetAsync(gxt, 0, (size_t)nx * 4, stream), "memset");
+    // as the fp32 route: the grad_out prep on the caller's stream; the weight
+    // pack + zeroing (side 0) and the input staging + grad-input zeroing
+    // (side 1) beside it
+    Fork fk(stream, side_streams_pay(g));
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_pack_weight_bwd16(weight, wbt, g, fk.side(0)),
+                "tc_pack_weight_bwd");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_zero(z, fk.side(0)), "zero");
+    const cudaStream_t s1 = fk.side(1);
+    DCN_CUDA_ON(s1, cudaMemsetAsync(gxt, 0, (size_t)nx * 4, s1), "memset");
     if (nhwc) {  // channels-last: a copy plus the zero row
-      DCN_CUDA(cudaMemcpyAsync(xt, input, (size_t)nx * 2, cudaMemcpyDeviceToDevice, stream),
-               "copy");
-      DCN_CUDA(cudaMemsetAsync(static_cast<char*>(xt) + (size_t)nx * 2, 0, (size_t)g.C * 2,
-                               stream),
-               "memset");
+      DCN_CUDA_ON(s1, cudaMemcpyAsync(xt, input, (size_t)nx * 2, cudaMemcpyDeviceToDevice, s1),
+                  "copy");
+      DCN_CUDA_ON(s1,
+                  cudaMemsetAsync(static_cast<char*>(xt) + (size_t)nx * 2, 0,
+                                  (size_t)g.C * 2, s1),
+                  "memset");
     } else {
-      DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
-                                             stream),
-               "nchw_to_nhwc");
+      DCN_CUDA_ON(s1,
+                  dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
+                                                s1),
+                  "nchw_to_nhwc");
     }
+    if (grad_bias) DCN_CUDA(cudaMemsetAsync(gb, 0, (size_t)g.outC * 4, stream), "memset");
     DCN_CUDA(dcn::launch_prep_go16(g, grad_output, go_r, grad_bias ? gb : nullptr, f16, stream),
              "tc_prep_go");
-    DCN_CUDA(dcn::launch_pack_weight_bwd16(weight, wbt, g, stream), "tc_pack_weight_bwd");
+    DCN_ORDER(fk.join(0), "join");
+    DCN_ORDER(fk.join(1), "join");
     DCN_CUDA(dcn::launch_bwd_fused_tc_h16(g, go_r, wbt, xt, offset, mask, gxt, goff,
                                           mask ? gm : nullptr, gwt, f16, num_sms_current(),
                                           stream),
              f16 ? "bwd_fused_tc_f16" : "bwd_fused_tc_bf16");
-    const char* down = f16 ? "f32_to_f16" : "f32_to_bf16";
+    // grad_input back to the tensors' layout and type, the other gradients
+    // rounded beside it (side 0)
+    dcn::H16List rest{};
+    rest.add(goff, grad_offset, noff);
+    if (mask) rest.add(gm, grad_mask, nm);
+    if (grad_bias) rest.add(gb, grad_bias, g.outC);
+    DCN_ORDER(fk.fork(), "fork");
+    DCN_CUDA_ON(fk.side(0), dcn::launch_grads_to_h16(gwt, grad_weight, g, rest, f16, fk.side(0)),
+                "grads_to_h16");
     if (nhwc)
-      DCN_CUDA(dcn::launch_f32_to_h16(gxt, grad_input, nx, f16, stream), down);
+      DCN_CUDA(dcn::launch_f32_to_h16(gxt, grad_input, nx, f16, stream),
+               f16 ? "f32_to_f16" : "f32_to_bf16");
     else
       DCN_CUDA(dcn::launch_nhwc_to_nchw16(gxt, grad_input, g.N, g.C, g.HW, f16, stream),
                "nhwc_to_nchw");
-    DCN_CUDA(dcn::launch_f32_to_h16(goff, grad_offset, noff, f16, stream), down);
-    if (mask) DCN_CUDA(dcn::launch_f32_to_h16(gm, grad_mask, nm, f16, stream), down);
-    DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, gw, g, stream), "grad_weight_layout");
-    DCN_CUDA(dcn::launch_f32_to_h16(gw, grad_weight, nw, f16, stream), down);
-    if (grad_bias) DCN_CUDA(dcn::launch_f32_to_h16(gb, grad_bias, g.outC, f16, stream), down);
+    DCN_ORDER(fk.join(0), "join");
     return DCN_OK;
   }
   const size_t need = bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);

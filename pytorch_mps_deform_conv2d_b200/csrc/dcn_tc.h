@@ -108,6 +108,25 @@ cudaError_t launch_pack_weight_bwd16(const void* w, void* wbt, const Geom& g,
 // fp32 NHWC grad-input accumulator -> 16-bit NCHW grad_input.
 cudaError_t launch_nhwc_to_nchw16(const float* gxt, void* gx, int N, int C, int HW, bool f16,
                                   cudaStream_t stream);
+// fp32 gradients to their 16-bit outputs in one launch: the tap-major weight
+// gradient `gwt` ([outC][kk][Cg]) to `gw` ([outC][Cg][kk]) and the `count`
+// arrays of `H16List` element-wise (rounded to nearest even).
+struct H16List {
+  const float* src[3];
+  unsigned short* dst[3];
+  long long n[3];
+  int count;
+  void add(const float* s, void* d, long long count_) {
+    if (s != nullptr && d != nullptr && count_ > 0) {
+      src[count] = s;
+      dst[count] = static_cast<unsigned short*>(d);
+      n[count] = count_;
+      ++count;
+    }
+  }
+};
+cudaError_t launch_grads_to_h16(const float* gwt, void* gw, const Geom& g, const H16List& rest,
+                                bool f16, cudaStream_t stream);
 // Weight gradient as a dense TMA-fed GEMM over the column buffer, summed into
 // `gw` (pre-zeroed): grad_weight itself ([outC][Cg][kh*kw]), or with
 // `tap_major` a [outC][kh*kw][Cg] copy, whose reductions coalesce, for the
@@ -116,9 +135,21 @@ bool tc_wcol_supported(const Geom& g, bool split);
 size_t tc_col_bytes(const Geom& g, bool split);
 cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* go_r, float* gw,
                                   bool tap_major, bool split, int num_sms, cudaStream_t stream);
-// [outC][kh*kw][Cg] -> grad_weight's [outC][Cg][kh*kw].
+// [outC][kh*kw][Cg] -> grad_weight's [outC][Cg][kh*kw]; with `gpart` and
+// `gb`, grad_bias from launch_bwd_prologue's partial sums as well.
 cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
-                                         cudaStream_t stream);
+                                         cudaStream_t stream, const float* gpart = nullptr,
+                                         float* gb = nullptr);
+struct ZeroList;  // dcn_kernels.h
+// The fused TF32 backward's helpers for a staged input, in one launch:
+// launch_tc_prep_go's work with grad_bias as per-block partial sums into
+// `gpart` (tc_bias_part_floats of them; NULL: no bias), the packed weight of
+// launch_tc_pack_weight_bwd (TF32, no split), and the zeroing of the
+// accumulators in `z`.  No block depends on another.
+size_t tc_bias_part_floats(const Geom& g);
+cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, float* gpart,
+                                const float* w, float* wbt, const ZeroList& z,
+                                cudaStream_t stream);
 // Sampling plans of every (n, deformable group, tap, pixel): 32 bytes each
 // (corner element offsets into the NHWC copy, weights times mask).
 inline size_t tc_plan_bytes(const Geom& g) { return (size_t)g.N * g.dg * g.kk * g.P * 32; }
