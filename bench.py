@@ -189,8 +189,10 @@ def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
     (dcn_l2_probe) sweeping an L2-resident buffer with 16-byte loads cached
     in L2 only (kind 0, the corner gathers), with 16-byte fp32 reductions
     (kind 1, the col2im scatter), and with both in one loop, 5 loads to 2
-    reductions (kind 2).  Returns {"l2_to_sm", "sm_to_l2_red", "mixed_5to2"}
-    in GB/s (kind 2: bytes read plus bytes reduced)."""
+    reductions (kind 2), and with 16-byte loads from random 128-byte lines
+    (kind 3, the corner gathers' pattern).  Returns {"l2_to_sm",
+    "sm_to_l2_red", "mixed_5to2", "gather"} in GB/s (kind 2: bytes read plus
+    bytes reduced)."""
     import ctypes
 
     import torch
@@ -199,7 +201,9 @@ def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
     buf = torch.zeros(bytes_ // 4, device="cuda")
     stream = torch.cuda.current_stream()
     out = {}
-    for kind, name in ((0, "l2_to_sm"), (1, "sm_to_l2_red"), (2, "mixed_5to2")):
+    warps = torch.cuda.get_device_properties(buf.device).multi_processor_count * 64
+    for kind, name in ((0, "l2_to_sm"), (1, "sm_to_l2_red"), (2, "mixed_5to2"),
+                       (3, "gather")):
         def launch():
             rc = lib.dcn_l2_probe(kind, ctypes.c_void_p(buf.data_ptr()), bytes_, passes,
                                   ctypes.c_void_p(stream.cuda_stream))
@@ -215,34 +219,55 @@ def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
             e1.record()
             torch.cuda.synchronize()
             best = min(best, e0.elapsed_time(e1))
-        moved = bytes_ if kind < 2 else (bytes_ // 3584) * 3584
+        moved = (bytes_ if kind < 2 else (bytes_ // 3584) * 3584 if kind == 2
+                 else 512 * (bytes_ // 512 // warps // 4 * 4) * warps)
         out[name] = round(moved * passes / (best * 1e-3) / 1e9, 1)
     del buf
     return out
 
 
-def binding_roofline(traffic, avg_ms, l2_peaks):
+def gather_bytes(name, wl):
+    """Corner-gather bytes of one launch of a tensor-core kernel that gathers
+    (every sample reads 4 corner vectors of all its channels; dropped
+    corners read the zero row): 4 x C x element size x taps x N x P."""
+    if not name.startswith(("fwd_tc", "bwd_fused_tc")):
+        return 0.0
+    esize = 2 if name.endswith(("_bf16", "_f16")) else 4
+    return 4.0 * wl["C"] * esize * wl["k"] ** 2 * wl["N"] * algorithmic_work(wl)["P"]
+
+
+def binding_roofline(traffic, avg_ms, l2_peaks, gathered=0.0):
     """The dominant kernel against the L2 <-> SM crossbar.  Bytes it moved
     each way in one launch (ncu: l1tex__m_xbar2l1tex_read_bytes.sum and
     l1tex__m_l1tex2xbar_write_bytes.sum, from the committed profile of the
-    same workload and mode) over its live launch time.  `frac` sets the
-    launch time against the time the mixed probe (5 bytes loaded to 2 bytes
-    reduced, about the fused backward's ratio) takes for the same bytes;
-    `frac_load` / `frac_red` are each direction against its own probe."""
+    same workload and mode), split into corner gathers (`gathered`, random
+    128-byte lines) and streaming loads (the rest: TMA tiles, offsets).
+    Floor model from the probes of this run: loads take gathers / gather
+    rate + the rest / load rate, reductions take their bytes / reduction
+    rate; the two directions overlap by the fraction `overlap` that the mixed
+    probe (5:2 loads to reductions) shows between running them one after the
+    other and fully side by side.  `frac` = floor / launch time."""
     if not traffic or "l2_to_sm_bytes" not in traffic or not l2_peaks:
         return None
     rd, wr = float(traffic["l2_to_sm_bytes"]), float(traffic.get("sm_to_l2_bytes", 0.0))
+    gat = min(gathered, rd)
     t = avg_ms * 1e-3
-    a_rd, a_wr = rd / t / 1e9, wr / t / 1e9
-    t_mixed = (rd + wr) / (l2_peaks["mixed_5to2"] * 1e9)
-    return {"resource": "L2 <-> SM crossbar (loads + fp32 reductions)", "unit": "GB/s",
-            "l2_to_sm_bytes": rd, "sm_to_l2_bytes": wr,
-            "achieved": round(a_rd + a_wr, 1), "peak": l2_peaks["mixed_5to2"],
-            "frac": round(t_mixed / t, 3),
-            "achieved_l2_to_sm": round(a_rd, 1), "peak_l2_to_sm": l2_peaks["l2_to_sm"],
-            "frac_load": round(a_rd / l2_peaks["l2_to_sm"], 3),
-            "achieved_sm_to_l2": round(a_wr, 1), "peak_sm_to_l2_red": l2_peaks["sm_to_l2_red"],
-            "frac_red": round(a_wr / l2_peaks["sm_to_l2_red"], 3),
+    P_ld, P_red = l2_peaks["l2_to_sm"] * 1e9, l2_peaks["sm_to_l2_red"] * 1e9
+    P_gat, P_mix = l2_peaks["gather"] * 1e9, l2_peaks["mixed_5to2"] * 1e9
+    # overlap of the probe's own mix: 5 bytes loaded, 2 reduced
+    ser, par, mix = 5 / P_ld + 2 / P_red, max(5 / P_ld, 2 / P_red), 7 / P_mix
+    overlap = min(1.0, max(0.0, (ser - mix) / (ser - par)))
+    t_ld = gat / P_gat + (rd - gat) / P_ld
+    t_red = wr / P_red
+    floor = t_ld + t_red - overlap * min(t_ld, t_red)
+    return {"resource": "L2 <-> SM crossbar (gathers, tiles, fp32 reductions)",
+            "unit": "GB/s", "l2_to_sm_bytes": rd, "gather_bytes": gat, "sm_to_l2_bytes": wr,
+            "achieved": round((rd + wr) / t / 1e9, 1),
+            "floor_ms": round(floor * 1e3, 4), "loads_ms": round(t_ld * 1e3, 4),
+            "reductions_ms": round(t_red * 1e3, 4), "overlap": round(overlap, 3),
+            "frac": round(floor / t, 3),
+            "peaks_gbs": {k: l2_peaks[k] for k in ("l2_to_sm", "gather", "sm_to_l2_red",
+                                                    "mixed_5to2")},
             "peak_source": "dcn_l2_probe in this run (64 MiB L2-resident buffer, all SMs)",
             "bytes_source": traffic.get("source")}
 
@@ -573,7 +598,7 @@ def run_ours(args, wl):
                     bytes_per_launch=amount)
     traffic = load_traffic().get(f"{args.workload}:{args.math}:{dom}")
     roof["traffic"] = traffic["bytes_per_launch"] if traffic else None
-    roof["binding"] = binding_roofline(traffic, avg_ms, l2_peaks)
+    roof["binding"] = binding_roofline(traffic, avg_ms, l2_peaks, gather_bytes(dom, wl))
     roof["l2_peaks_gbs"] = l2_peaks
     work = algorithmic_work(wl)
     step_roof_ms = work["flops"] / ((peak_tf32_used if args.math != "fp32" else peak_fp32) * 1e12) * 1e3

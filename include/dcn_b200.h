@@ -312,9 +312,13 @@ DCN_API int dcn_device_status(void* stream, int clear, int* status);
  * scatter does (kind 1 modifies the buffer); kind 2 does both in one loop,
  * five 16-byte loads to two 16-byte reductions: of the bytes swept (rounded
  * down to a multiple of 3584) the first 5/7 are read, 1.0f is added to every
- * fp32 of the last 2/7.  With `bytes` well under the L2 size, bytes x passes
- * over the kernel's device time is the L2 -> SM (kind 0), SM -> L2 reduction
- * (kind 1) or mixed (kind 2) bandwidth the hot kernels are set against.
+ * fp32 of the last 2/7; kind 3 reads 16-byte vectors (L2 only) from random
+ * 128-byte lines of the buffer, 8 lanes to a line, as the corner gathers do
+ * (needs bytes / 512 >= 4 x the probe's 2048 threads an SM x SMs / 32).  With
+ * `bytes` well under the L2 size, bytes x passes over the kernel's device
+ * time is the L2 -> SM (kind 0), SM -> L2 reduction (kind 1), mixed (kind 2)
+ * or gather (kind 3; the whole-warp share of the bytes) bandwidth the hot
+ * kernels are set against.
  * The caller times it (CUDA events on `stream`). */
 DCN_API int dcn_l2_probe(int kind, void* buf, size_t bytes, int passes, void* stream);
 

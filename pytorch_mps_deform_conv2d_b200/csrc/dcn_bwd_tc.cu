@@ -22,6 +22,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 #include "dcn_kernels.h"
 #include "dcn_launch.h"
 #include "dcn_tc.h"
@@ -50,12 +52,12 @@ int pow2_cols(int n) {
 // ---------------------------------------------------------------------------
 // With `split` (3xTF32) the low TF32 parts fill rows N*outC .. 2*N*outC-1.
 // Pixels P .. Ppad-1 of a row are zero.  A block covers PG_SPAN pixels of one
-// (image, out channel) row -- 16-byte accesses when P % 4 == 0, all four of a
+// (image, out channel) row -- 16-byte accesses when P % 4 == 0, all eight of a
 // thread's loads issued before their stores -- and, with `gb` (pre-zeroed
 // grad_bias), adds its row's sum with one atomic, or with `gpart` writes it
-// to gpart[bid] (no atomics; bias_from_parts sums them).  `bid`: the block's
+// to gpart[bid] (no atomics; weight_from_tap_major_kernel sums them).  `bid`: the block's
 // index among the prep blocks (256 threads).
-constexpr int PG_SPAN = 4096;
+constexpr int PG_SPAN = 8192;
 constexpr int PG_UNROLL = PG_SPAN / (4 * 256);  // float4 loads in flight a thread
 __device__ __forceinline__ void prep_go_block(long long bid, const float* __restrict__ go,
                                               float* __restrict__ go_r, float* __restrict__ gb,
@@ -1965,10 +1967,13 @@ cudaError_t launch_tc_pack_weight_bwd(const float* w, float* wbt, const Geom& g,
 }
 
 namespace {
-// The fused backward's helpers in one launch (staged input, TF32): blocks
-// [0, nb_prep) prepare grad_out rows (grad_bias as per-block partial sums),
-// the next nb_pack blocks pack the weight (one 32 x 32 tile each), the last
-// nb_zero blocks zero the accumulators, grid-stride.  Blocks are independent.
+// The fused backward's helpers in one launch (staged input, TF32), as work
+// items: [0, nb_prep) prepare a PG_SPAN of a grad_out row each (grad_bias as
+// per-item partial sums), the next nb_pack pack a 32 x 32 weight tile each,
+// the rest zero 16 KB of an accumulator each (zc[l] items for array l; the
+// first item of an array also takes its scalar tail).  A block takes items
+// blockIdx.x, + gridDim.x, ...: every block gets a mix of the three kinds.
+constexpr int ZERO_ITEM = 4096;  // floats an item zeroes (256 threads x 4 float4)
 struct Prologue {
   const float* go;
   float* go_r;
@@ -1976,35 +1981,45 @@ struct Prologue {
   const float* w;
   float* wbt;
   float* zp[4];
-  long long zn[4];
+  long long zn[4];   // floats of array l
+  long long zv[4];   // float4 vectors zeroed as vectors (0: misaligned, all scalar)
+  int zitems[4];     // items of array l
   int zcount;
   int Ppad, pspans, vec;
-  int nb_prep, pack_x, pack_y, nb_pack, nb_zero;
+  int nb_prep, pack_x, pack_y, nb_pack, total;
 };
 __global__ void __launch_bounds__(256) bwd_prologue_kernel(Prologue a, Geom g) {
-  int b = blockIdx.x;
-  if (b < a.nb_prep) {
-    prep_go_block(b, a.go, a.go_r, nullptr, a.gpart, g.N, g.outC, g.P, a.Ppad, a.pspans, 0,
-                  a.vec);
-    return;
-  }
-  b -= a.nb_prep;
-  if (b < a.nb_pack) {
-    const int per_g = a.pack_x * a.pack_y;
-    const int gi = b / per_g, r = b - gi * per_g;
-    pack_weight_bwd_tile(r % a.pack_x, r / a.pack_x, gi, a.w, a.wbt, g, 0);
-    return;
-  }
-  b -= a.nb_pack;
-  const long long stride = (long long)a.nb_zero * blockDim.x;
-  const long long t0 = (long long)b * blockDim.x + threadIdx.x;
-  for (int l = 0; l < a.zcount; ++l) {
-    float* p = a.zp[l];
-    const long long n = a.zn[l];
-    const long long n4 = (reinterpret_cast<uintptr_t>(p) & 15u) == 0 ? n >> 2 : 0;
-    float4* p4 = reinterpret_cast<float4*>(p);
-    for (long long i = t0; i < n4; i += stride) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (long long i = (n4 << 2) + t0; i < n; i += stride) p[i] = 0.f;
+  for (int it = blockIdx.x; it < a.total; it += gridDim.x) {
+    int b = it;
+    if (b < a.nb_prep) {
+      prep_go_block(b, a.go, a.go_r, nullptr, a.gpart, g.N, g.outC, g.P, a.Ppad, a.pspans, 0,
+                    a.vec);
+    } else if ((b -= a.nb_prep) < a.nb_pack) {
+      const int per_g = a.pack_x * a.pack_y;
+      const int gi = b / per_g, r = b - gi * per_g;
+      pack_weight_bwd_tile(r % a.pack_x, r / a.pack_x, gi, a.w, a.wbt, g, 0);
+    } else {
+      b -= a.nb_pack;
+      int l = 0;
+      while (l < a.zcount - 1 && b >= a.zitems[l]) b -= a.zitems[l++];
+      float* p = a.zp[l];
+      const long long n = a.zn[l], nv = a.zv[l];
+      if (nv > 0) {
+        float4* p4 = reinterpret_cast<float4*>(p);
+        const long long v0 = (long long)b * (ZERO_ITEM / 4);
+#pragma unroll
+        for (int u = 0; u < ZERO_ITEM / 1024; ++u) {
+          const long long v = v0 + u * 256 + threadIdx.x;
+          if (v < nv) p4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (b == 0)
+          for (long long i = (nv << 2) + threadIdx.x; i < n; i += 256) p[i] = 0.f;
+      } else {
+        const long long e0 = (long long)b * ZERO_ITEM;
+        for (long long i = e0 + threadIdx.x; i < e0 + ZERO_ITEM && i < n; i += 256) p[i] = 0.f;
+      }
+    }
+    __syncthreads();  // the shared staging of one item is free before the next
   }
 }
 }  // namespace
@@ -2017,6 +2032,7 @@ size_t tc_bias_part_floats(const Geom& g) {
 cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, float* gpart,
                                 const float* w, float* wbt, const ZeroList& z,
                                 cudaStream_t stream) {
+  if (g.P == 0 || z.count > 4) return cudaErrorInvalidValue;
   Prologue a{};
   a.go = go;
   a.go_r = go_r;
@@ -2024,9 +2040,15 @@ cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, flo
   a.w = w;
   a.wbt = wbt;
   a.zcount = z.count;
+  long long zitems = 0;
   for (int l = 0; l < z.count; ++l) {
     a.zp[l] = z.ptr[l];
     a.zn[l] = z.n[l];
+    a.zv[l] = (reinterpret_cast<uintptr_t>(z.ptr[l]) & 15u) == 0 ? z.n[l] >> 2 : 0;
+    const long long items = (z.n[l] + ZERO_ITEM - 1) / ZERO_ITEM;
+    if (items > (1LL << 30)) return cudaErrorInvalidValue;
+    a.zitems[l] = (int)items;
+    zitems += items;
   }
   a.Ppad = (g.P + 3) & ~3;
   a.pspans = (a.Ppad + PG_SPAN - 1) / PG_SPAN;
@@ -2036,12 +2058,13 @@ cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, flo
   a.pack_x = (g.Cg * g.kk + 31) / 32;
   a.pack_y = (g.Og + 31) / 32;
   const long long pack = (long long)a.pack_x * a.pack_y * g.G;
-  a.nb_zero = device_sm_count() * 4;
-  const long long blocks = prep + pack + a.nb_zero;
-  if (blocks > (1LL << 31) - 1 || g.P == 0) return cudaErrorInvalidValue;
+  const long long total = prep + pack + zitems;
+  if (total > (1LL << 31) - 1) return cudaErrorInvalidValue;
   a.nb_prep = (int)prep;
   a.nb_pack = (int)pack;
-  bwd_prologue_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a, g);
+  a.total = (int)total;
+  const long long grid = std::min<long long>(total, (long long)device_sm_count() * 8);
+  bwd_prologue_kernel<<<(unsigned)grid, 256, 0, stream>>>(a, g);
   return cudaGetLastError();
 }
 

@@ -53,7 +53,8 @@ def test_load_probe_leaves_the_buffer(cuda_device):
 
 def test_bad_arguments_are_refused(cuda_device):
     buf = torch.zeros(1024, device="cuda")
-    assert _probe(3, buf, 4096, 1) == 1
+    assert _probe(4, buf, 4096, 1) == 1
+    assert _probe(3, buf, 4096, 1) == 1  # too small for one gather round
     assert _probe(2, buf, 3568, 1) == 1  # under one mixed block
     assert _probe(0, buf, 4096, 0) == 1
     assert _probe(0, buf, 8, 1) == 1
@@ -63,8 +64,9 @@ def test_bad_arguments_are_refused(cuda_device):
 
 def test_bandwidths_are_plausible(cuda_device):
     import bench
-    peaks = bench.measure_l2_gbs(bytes_=16 << 20, passes=16, reps=3)
+    peaks = bench.measure_l2_gbs(bytes_=32 << 20, passes=8, reps=3)
     # above HBM-class copy rates, below anything the crossbar could carry
     assert 2000.0 < peaks["l2_to_sm"] < 200000.0, peaks
     assert 500.0 < peaks["sm_to_l2_red"] < 200000.0, peaks
     assert 500.0 < peaks["mixed_5to2"] < 200000.0, peaks
+    assert 500.0 < peaks["gather"] < 200000.0, peaks
