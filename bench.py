@@ -143,6 +143,12 @@ def kernel_work(name, wl):
         return w["gemm_flops"], "flop", "tensor"
     if name in ("nchw_to_nhwc", "nhwc_to_nchw", "copy_nhwc"):
         return 2.0 * 4 * N * C * wl["H"] * wl["W"], "byte", "hbm"
+    if name == "bwd_prologue":  # grad_out in + rows out, zeroed accumulators, packed weight
+        ho, wo = out_hw(wl)
+        O, k2, dg = wl["outC"], wl["k"] ** 2, wl["dg"]
+        wts = O * (C // wl["groups"]) * k2
+        zeroed = N * C * wl["H"] * wl["W"] + N * 3 * dg * k2 * ho * wo + wts
+        return 4.0 * (2 * N * O * ho * wo + zeroed + 2 * wts), "byte", "hbm"
     if name == "grad_bias":
         return 4.0 * N * wl["outC"] * w["P"], "byte", "hbm"
     return None, None, None
@@ -190,9 +196,10 @@ def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
     in L2 only (kind 0, the corner gathers), with 16-byte fp32 reductions
     (kind 1, the col2im scatter), and with both in one loop, 5 loads to 2
     reductions (kind 2), and with 16-byte loads from random 128-byte lines
-    (kind 3, the corner gathers' pattern).  Returns {"l2_to_sm",
-    "sm_to_l2_red", "mixed_5to2", "gather"} in GB/s (kind 2: bytes read plus
-    bytes reduced)."""
+    (kind 3, the corner gathers' pattern) and 16-byte reductions into random
+    lines (kind 4, the col2im scatter's pattern).  Returns {"l2_to_sm",
+    "sm_to_l2_red", "mixed_5to2", "gather", "scatter_red"} in GB/s (kind 2:
+    bytes read plus bytes reduced)."""
     import ctypes
 
     import torch
@@ -203,7 +210,7 @@ def measure_l2_gbs(bytes_=64 << 20, passes=16, reps=5):
     out = {}
     warps = torch.cuda.get_device_properties(buf.device).multi_processor_count * 64
     for kind, name in ((0, "l2_to_sm"), (1, "sm_to_l2_red"), (2, "mixed_5to2"),
-                       (3, "gather")):
+                       (3, "gather"), (4, "scatter_red")):
         def launch():
             rc = lib.dcn_l2_probe(kind, ctypes.c_void_p(buf.data_ptr()), bytes_, passes,
                                   ctypes.c_void_p(stream.cuda_stream))
@@ -243,8 +250,8 @@ def binding_roofline(traffic, avg_ms, l2_peaks, gathered=0.0):
     same workload and mode), split into corner gathers (`gathered`, random
     128-byte lines) and streaming loads (the rest: TMA tiles, offsets).
     Floor model from the probes of this run: loads take gathers / gather
-    rate + the rest / load rate, reductions take their bytes / reduction
-    rate; the two directions overlap by the fraction `overlap` that the mixed
+    rate + the rest / load rate, reductions take their bytes / scatter rate
+    (16-byte reductions into random lines); the two directions overlap by the fraction `overlap` that the mixed
     probe (5:2 loads to reductions) shows between running them one after the
     other and fully side by side.  `frac` = floor / launch time."""
     if not traffic or "l2_to_sm_bytes" not in traffic or not l2_peaks:
@@ -254,11 +261,13 @@ def binding_roofline(traffic, avg_ms, l2_peaks, gathered=0.0):
     t = avg_ms * 1e-3
     P_ld, P_red = l2_peaks["l2_to_sm"] * 1e9, l2_peaks["sm_to_l2_red"] * 1e9
     P_gat, P_mix = l2_peaks["gather"] * 1e9, l2_peaks["mixed_5to2"] * 1e9
+    P_sct = l2_peaks.get("scatter_red", l2_peaks["sm_to_l2_red"]) * 1e9
     # overlap of the probe's own mix: 5 bytes loaded, 2 reduced
     ser, par, mix = 5 / P_ld + 2 / P_red, max(5 / P_ld, 2 / P_red), 7 / P_mix
     overlap = min(1.0, max(0.0, (ser - mix) / (ser - par)))
     t_ld = gat / P_gat + (rd - gat) / P_ld
-    t_red = wr / P_red
+    # the kernels' reductions land on lines that follow the sampling offsets
+    t_red = wr / P_sct
     floor = t_ld + t_red - overlap * min(t_ld, t_red)
     return {"resource": "L2 <-> SM crossbar (gathers, tiles, fp32 reductions)",
             "unit": "GB/s", "l2_to_sm_bytes": rd, "gather_bytes": gat, "sm_to_l2_bytes": wr,
@@ -266,8 +275,8 @@ def binding_roofline(traffic, avg_ms, l2_peaks, gathered=0.0):
             "floor_ms": round(floor * 1e3, 4), "loads_ms": round(t_ld * 1e3, 4),
             "reductions_ms": round(t_red * 1e3, 4), "overlap": round(overlap, 3),
             "frac": round(floor / t, 3),
-            "peaks_gbs": {k: l2_peaks[k] for k in ("l2_to_sm", "gather", "sm_to_l2_red",
-                                                    "mixed_5to2")},
+            "peaks_gbs": {k: l2_peaks.get(k) for k in ("l2_to_sm", "gather", "sm_to_l2_red",
+                                                        "scatter_red", "mixed_5to2")},
             "peak_source": "dcn_l2_probe in this run (64 MiB L2-resident buffer, all SMs)",
             "bytes_source": traffic.get("source")}
 
@@ -605,6 +614,25 @@ def run_ours(args, wl):
     roof["step_roofline_ms"] = round(max(step_roof_ms, work["bytes"] / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3), 4)
     roof["step_frac"] = round(roof["step_roofline_ms"] / ms_per_step, 3)
     roof["peaks_measured_tflops"] = {"tf32": round(peak_tf32, 1), "fp32": round(peak_fp32, 1)}
+    # the step against its binding resources: each kernel's crossbar floor
+    # (committed profile + this run's probes) or, for the HBM-bound helpers,
+    # its algorithmic bytes at the HBM peak; kernels without a model add 0
+    if l2_peaks and world == 1:
+        tr_all = load_traffic()
+        floor_ms, parts = 0.0, {}
+        for name, (n_launch, tot_ms) in kernels.items():
+            tr = tr_all.get(f"{args.workload}:{args.math}:{name}")
+            if tr is not None and "l2_to_sm_bytes" in tr:
+                bnd = binding_roofline(tr, tot_ms / n_launch, l2_peaks, gather_bytes(name, wl))
+                f = bnd["floor_ms"]
+            else:
+                amount, unit, _ = kernel_work(name, wl)
+                f = amount / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3 if unit == "byte" else 0.0
+            parts[name] = round(f * n_launch / args.steps, 4)
+            floor_ms += f * n_launch / args.steps
+        roof["step_floor_ms"] = round(floor_ms, 4)
+        roof["step_floor_frac"] = round(floor_ms / ms_per_step, 3)
+        roof["step_floor_parts_ms"] = parts
 
     # ---- end to end through the public module API, host buffers ----
     e2e = None if (args.profile or strong) else run_e2e(args, wl, x, w, b, off, m, go, dev, world, flags,

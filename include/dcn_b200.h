@@ -313,12 +313,15 @@ DCN_API int dcn_device_status(void* stream, int clear, int* status);
  * five 16-byte loads to two 16-byte reductions: of the bytes swept (rounded
  * down to a multiple of 3584) the first 5/7 are read, 1.0f is added to every
  * fp32 of the last 2/7; kind 3 reads 16-byte vectors (L2 only) from random
- * 128-byte lines of the buffer, 8 lanes to a line, as the corner gathers do
- * (needs bytes / 512 >= 4 x the probe's 2048 threads an SM x SMs / 32).  With
+ * 128-byte lines of the buffer, 8 lanes to a line, as the corner gathers do;
+ * kind 4 adds 1.0f with 16-byte reductions in the same random pattern, as the
+ * col2im scatter does (kinds 3 and 4 need bytes / 512 >= 4 x the probe's 2048
+ * threads an SM x SMs / 32).  With
  * `bytes` well under the L2 size, bytes x passes over the kernel's device
- * time is the L2 -> SM (kind 0), SM -> L2 reduction (kind 1), mixed (kind 2)
- * or gather (kind 3; the whole-warp share of the bytes) bandwidth the hot
- * kernels are set against.
+ * time is the L2 -> SM (kind 0), SM -> L2 reduction (kind 1), mixed (kind 2),
+ * gather (kind 3) or scatter (kind 4) bandwidth the hot kernels are set
+ * against (kinds 3 and 4 move 512 x floor(bytes / 512 / W / 4) x 4 x W bytes
+ * a pass, W = 64 warps a SM x SMs).
  * The caller times it (CUDA events on `stream`). */
 DCN_API int dcn_l2_probe(int kind, void* buf, size_t bytes, int passes, void* stream);
 

@@ -14,7 +14,9 @@
 //           two directions overlap or share one budget;
 //   kind 3: 16-byte loads cached in L2 only from random 128-byte lines, 8
 //           lanes to a line (4 lines a warp instruction): the access pattern
-//           of the corner gathers, whose lines follow the sampling offsets.
+//           of the corner gathers, whose lines follow the sampling offsets;
+//   kind 4: 16-byte fp32 reductions into random 128-byte lines, 8 lanes to a
+//           line: the col2im scatter's pattern.
 // No reference counterpart: the reference has no device kernels of this kind.
 #include <cuda_runtime.h>
 
@@ -104,6 +106,15 @@ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
   x ^= x >> 16;
   return x;
 }
+// Line of load / reduction j of warp w in pass `it` (lanes 8i .. 8i + 7
+// share line i of the four).
+__device__ __forceinline__ long long probe_line(long long w, long long j, int lane, int it,
+                                                long long nlines) {
+  const uint32_t h = mix32((uint32_t)(w * 0x9e3779b1u) ^
+                           mix32((uint32_t)j * 4u + (uint32_t)(lane >> 3) +
+                                 (uint32_t)it * 0x85ebca6bu));
+  return (long long)(h % (uint32_t)nlines);
+}
 __global__ void __launch_bounds__(kProbeThreads)
     l2_gather_probe_kernel(const int4* __restrict__ buf, long long n16, int passes, int* sink) {
   const long long nlines = n16 / 8;
@@ -117,13 +128,8 @@ __global__ void __launch_bounds__(kProbeThreads)
     for (long long j = 0; j + kUnroll <= per_warp; j += kUnroll) {
       int4 v[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const uint32_t h = mix32((uint32_t)(w * 0x9e3779b1u) ^ mix32((uint32_t)(j + u) * 4u +
-                                                                      (uint32_t)(lane >> 3) +
-                                                                      (uint32_t)it * 0x85ebca6bu));
-        const long long line = (long long)(h % (uint32_t)nlines);
-        v[u] = __ldcg(buf + line * 8 + (lane & 7));
-      }
+      for (int u = 0; u < kUnroll; ++u)
+        v[u] = __ldcg(buf + probe_line(w, j + u, lane, it, nlines) * 8 + (lane & 7));
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) acc ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
     }
@@ -131,11 +137,29 @@ __global__ void __launch_bounds__(kProbeThreads)
   if (acc == 0x13579bdf) sink[0] = acc;
 }
 
+// Kind 4: as kind 3 with 16-byte reductions (adding 1.0f) instead of loads.
+__global__ void __launch_bounds__(kProbeThreads)
+    l2_scatter_probe_kernel(float* __restrict__ buf, long long n16, int passes) {
+  const long long nlines = n16 / 8;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const long long per_warp = n16 / 32 / warps;
+  for (int it = 0; it < passes; ++it)
+    for (long long j = 0; j + kUnroll <= per_warp; j += kUnroll)
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        float* dst = buf + (probe_line(w, j + u, lane, it, nlines) * 8 + (lane & 7)) * 4;
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %1, %1, %1};" ::"l"(dst), "f"(1.0f)
+                     : "memory");
+      }
+}
+
 }  // namespace
 
 extern "C" DCN_API int dcn_l2_probe(int kind, void* buf, size_t bytes, int passes,
                                     void* stream) {
-  if (kind < 0 || kind > 3 || buf == nullptr || passes < 1 || bytes < 16 ||
+  if (kind < 0 || kind > 4 || buf == nullptr || passes < 1 || bytes < 16 ||
       (reinterpret_cast<uintptr_t>(buf) & 15) != 0)
     return DCN_ERR_INVALID_ARGUMENT;
   int dev = 0, sms = 0;
@@ -152,11 +176,15 @@ extern "C" DCN_API int dcn_l2_probe(int kind, void* buf, size_t bytes, int passe
                                                        passes, static_cast<int*>(buf));
   } else if (kind == 1) {
     l2_red_probe_kernel<<<grid, kProbeThreads, 0, s>>>(static_cast<float*>(buf), n16, passes);
-  } else if (kind == 3) {
+  } else if (kind >= 3) {
     if (n16 / 8 > 0xffffffffLL || n16 / 32 < (long long)grid * (kProbeThreads / 32) * kUnroll)
       return DCN_ERR_INVALID_ARGUMENT;
-    l2_gather_probe_kernel<<<grid, kProbeThreads, 0, s>>>(static_cast<const int4*>(buf), n16,
-                                                         passes, static_cast<int*>(buf));
+    if (kind == 3)
+      l2_gather_probe_kernel<<<grid, kProbeThreads, 0, s>>>(static_cast<const int4*>(buf), n16,
+                                                           passes, static_cast<int*>(buf));
+    else
+      l2_scatter_probe_kernel<<<grid, kProbeThreads, 0, s>>>(static_cast<float*>(buf), n16,
+                                                            passes);
   } else {
     if (n16 < 224) return DCN_ERR_INVALID_ARGUMENT;
     l2_mixed_probe_kernel<<<grid, kProbeThreads, 0, s>>>(static_cast<int4*>(buf), n16 / 224,

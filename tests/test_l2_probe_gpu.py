@@ -43,6 +43,17 @@ def test_mixed_probe_adds_to_its_last_two_sevenths(cuda_device):
     assert torch.all(buf[nr + nw:] == 0.0)
 
 
+def test_scatter_probe_adds_four_per_reduction(cuda_device):
+    buf = torch.zeros(8 << 20, device="cuda")  # 32 MiB
+    assert _probe(4, buf, buf.numel() * 4, 2) == 0
+    torch.cuda.synchronize()
+    warps = torch.cuda.get_device_properties(0).multi_processor_count * 64
+    per_warp = buf.numel() * 4 // 16 // 32 // warps // 4 * 4
+    expected = 2 * warps * per_warp * 32 * 4  # passes x reductions x 4 floats
+    assert float(buf.double().sum()) == expected
+    assert float(buf.max()) <= 2 * 32 * 4 * per_warp  # nothing outside the lines' floats
+
+
 def test_load_probe_leaves_the_buffer(cuda_device):
     buf = torch.arange(1 << 18, device="cuda", dtype=torch.float32)
     ref = buf.clone()
@@ -53,7 +64,8 @@ def test_load_probe_leaves_the_buffer(cuda_device):
 
 def test_bad_arguments_are_refused(cuda_device):
     buf = torch.zeros(1024, device="cuda")
-    assert _probe(4, buf, 4096, 1) == 1
+    assert _probe(5, buf, 4096, 1) == 1
+    assert _probe(4, buf, 4096, 1) == 1  # too small for one scatter round
     assert _probe(3, buf, 4096, 1) == 1  # too small for one gather round
     assert _probe(2, buf, 3568, 1) == 1  # under one mixed block
     assert _probe(0, buf, 4096, 0) == 1
@@ -70,3 +82,4 @@ def test_bandwidths_are_plausible(cuda_device):
     assert 500.0 < peaks["sm_to_l2_red"] < 200000.0, peaks
     assert 500.0 < peaks["mixed_5to2"] < 200000.0, peaks
     assert 500.0 < peaks["gather"] < 200000.0, peaks
+    assert 200.0 < peaks["scatter_red"] < 200000.0, peaks
