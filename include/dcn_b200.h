@@ -112,6 +112,16 @@ extern "C" {
  *                    transposing the input twice (no reference counterpart;
  *                    with DCN_INPUT_NHWC, grad_input is still channels-last). */
 #define DCN_INPUT_STAGED 0x40000
+/*   DCN_KEEP_STAGED  dcn_forward stages the input as usual and leaves the
+ *                    staging copy (the layout dcn_stage_input writes) in the
+ *                    first dcn_staged_input_size bytes of the workspace,
+ *                    counted from the workspace pointer rounded up to 256
+ *                    bytes, for a later call with DCN_INPUT_STAGED: a
+ *                    training step stages inside its forward, where the
+ *                    weight pack runs beside the staging, instead of in a
+ *                    call of its own.  Not with DCN_INPUT_STAGED; dcn_forward
+ *                    only (no reference counterpart). */
+#define DCN_KEEP_STAGED 0x80000
 /* Fourth byte: test switches (no reference counterpart).
  *   DCN_TEST_WAIT_TIMEOUT  the tensor-core kernels' TMA producers issue no
  *                    copies and every mbarrier wait gives up after about a

@@ -61,6 +61,13 @@ def _stage_input_fake(input):
     return input.new_empty((n * h * w * c + c,))
 
 
+def _forward_staging_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                          dilation_h, dilation_w, groups, deformable_groups, math=-1):
+    out = _forward_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                        dilation_h, dilation_w, groups, deformable_groups, math)
+    return out, _stage_input_fake(input)
+
+
 def _forward_rows_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
                        dilation_h, dilation_w, groups, deformable_groups, row_begin, math=-1):
     wo = _out_size(input.shape[3], weight.shape[3], stride_w, pad_w, dilation_w)
@@ -136,6 +143,7 @@ def register() -> None:
     torch.library.register_fake(q + "deform_conv2d")(_forward_fake)
     torch.library.register_fake(q + "deform_conv2d_backward")(_backward_fake)
     torch.library.register_fake(q + "deform_conv2d_stage_input")(_stage_input_fake)
+    torch.library.register_fake(q + "deform_conv2d_forward_staging")(_forward_staging_fake)
     torch.library.register_fake(q + "deformable_col2im")(_col2im_fake)
     torch.library.register_fake(q + "deformable_col2im_coord")(_col2im_coord_fake)
     torch.library.register_autograd(q + "deform_conv2d_forward", _forward_backward,

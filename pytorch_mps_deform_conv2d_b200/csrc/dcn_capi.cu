@@ -471,8 +471,11 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
   Carver ws(align_ptr(workspace));
   const size_t usable = workspace_bytes - (size_t)(ws.base - static_cast<char*>(workspace));
   // xt (+ its zero row): a transpose of NCHW input, a copy of NHWC input, or
-  // the caller's staging copy (DCN_INPUT_STAGED: nothing to do)
+  // the caller's staging copy (DCN_INPUT_STAGED: nothing to do).  It is the
+  // workspace's first carve, where DCN_KEEP_STAGED leaves it for the caller.
   const bool staged = flags & DCN_INPUT_STAGED;
+  DCN_CHECK(!(staged && (flags & DCN_KEEP_STAGED)),
+            "deform_conv2d_forward: DCN_KEEP_STAGED needs an input to stage, not a staging copy");
   float* xt = staged ? const_cast<float*>(input) : ws.take(xt_floats(g));
   const FwdAlgo algo = pick_fwd(g, flags);
   const bool nhwc = flags & DCN_INPUT_NHWC;
@@ -566,6 +569,8 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   apply_test_flags(g, flags);
+  DCN_CHECK(!(flags & (DCN_KEEP_STAGED | DCN_INPUT_STAGED)),
+            "deform_conv2d_forward: the 16-bit forward stages its input itself");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;

@@ -136,7 +136,8 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                         int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
                         int64_t dilation_w, int64_t groups, int64_t deformable_groups,
                         int64_t row_begin, int64_t math,
-                        const c10::optional<at::Tensor>& staged = c10::nullopt) {
+                        const c10::optional<at::Tensor>& staged = c10::nullopt,
+                        at::Tensor* keep_staged = nullptr) {
   TORCH_CHECK(input.device().is_cuda() && weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_forward: input, weight and offset must be CUDA tensors");
   // float32 (the reference's only dtype, .mm:206-209) or, as an addition,
@@ -204,12 +205,21 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
     return out;
   }
   const float* xs = staged_ptr(staged, x, s);
-  const uint32_t fflags = flags | (xs ? DCN_INPUT_STAGED : 0u);
+  const uint32_t fflags =
+      flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);
   const size_t ws_bytes = dcn_forward_workspace_size(&s, fflags);
   auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
   check_rc(dcn_forward(&s, xs ? xs : x.data_ptr<float>(), w.data_ptr<float>(),
                        off.data_ptr<float>(), mp, bp, out.data_ptr<float>(), fflags,
                        ws.data_ptr(), ws_bytes, stream.stream()));
+  if (keep_staged != nullptr) {
+    // the staging copy the forward left at the workspace's 256-byte aligned start
+    const uintptr_t base = reinterpret_cast<uintptr_t>(ws.data_ptr());
+    const int64_t lead = (int64_t)(((base + 255) & ~(uintptr_t)255) - base);
+    const int64_t bytes = (int64_t)dcn_staged_input_size(&s);
+    TORCH_CHECK(bytes > 0 && lead + bytes <= ws.numel(), "deform_conv2d_forward: no staging copy");
+    *keep_staged = ws.narrow(0, lead, bytes).view(at::kFloat);
+  }
   return out;
 }
 
@@ -263,6 +273,24 @@ at::Tensor deform_conv2d_stage_input(const at::Tensor& input) {
                            nhwc ? DCN_INPUT_NHWC : 0u,
                            at::cuda::getCurrentCUDAStream().stream()));
   return staged;
+}
+
+// The forward that also returns its NHWC staging copy of the (float32)
+// input, for the `staged` argument of the backward: a training step stages
+// inside the forward, where the weight pack runs beside the staging.
+std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_staging(
+    const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset,
+    const at::Tensor& mask, const c10::optional<at::Tensor>& bias, int64_t stride_h,
+    int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
+    int64_t groups, int64_t deformable_groups, int64_t math) {
+  TORCH_CHECK(input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0,
+              "deform_conv2d_forward_staging: input must be a non-empty 4-D float32 tensor");
+  at::Tensor staged;
+  auto out = forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                          dilation_h, dilation_w, groups, deformable_groups, -1, math,
+                          c10::nullopt, &staged);
+  if (!staged.defined()) staged = deform_conv2d_stage_input(input);  // no output pixels
+  return std::make_tuple(out, staged);
 }
 
 at::Tensor deform_conv2d_forward_rows(const at::Tensor& input, const at::Tensor& weight,
@@ -547,23 +575,29 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
                                            const c10::optional<at::Tensor>&, int64_t, int64_t,
                                            int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
                                            int64_t, const c10::optional<at::Tensor>&)>();
-    static auto stage = c10::Dispatcher::singleton()
-                            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_stage_input", "")
-                            .typed<at::Tensor(const at::Tensor&)>();
+    static auto fwd_staging =
+        c10::Dispatcher::singleton()
+            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_forward_staging", "")
+            .typed<std::tuple<at::Tensor, at::Tensor>(
+                const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                const c10::optional<at::Tensor>&, int64_t, int64_t, int64_t, int64_t, int64_t,
+                int64_t, int64_t, int64_t, int64_t)>();
     const bool has_bias = bias.defined() && bias.numel() > 0;
     c10::optional<at::Tensor> b;
     if (has_bias) b = bias;
     at::Tensor out, staged;
     {
       at::AutoDispatchBelowADInplaceOrView below;
-      // a float32 input is staged (NHWC) once, for the forward and the
-      // backward, instead of once in each
-      if (input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0)
-        staged = stage.call(input);
-      c10::optional<at::Tensor> st;
-      if (staged.defined()) st = staged;
-      out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w, dilation_h,
-                    dilation_w, groups, deformable_groups, math, st);
+      // a float32 input is staged (NHWC) once, inside the forward, and the
+      // staging copy kept for the backward
+      if (input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0) {
+        std::tie(out, staged) =
+            fwd_staging.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
+                             dilation_h, dilation_w, groups, deformable_groups, math);
+      } else {
+        out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, groups, deformable_groups, math, c10::nullopt);
+      }
     }
     ctx->save_for_backward({input, weight, offset, mask, bias});
     if (staged.defined()) ctx->saved_data["staged"] = staged;
@@ -643,6 +677,12 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
   // NHWC staging copy of a float32 input for the `staged` argument above (no
   // reference counterpart): a training step stages its input once.
   m.def("deform_conv2d_stage_input(Tensor input) -> Tensor");
+  // The forward that also returns its staging copy of a float32 input (no
+  // reference counterpart): what the differentiable operator runs.
+  m.def(
+      "deform_conv2d_forward_staging(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
+      "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
+      "int dilation_w, int groups, int deformable_groups, int math=-1) -> (Tensor, Tensor)");
   // Row windows (no reference counterpart): offset / mask / output /
   // grad_output hold output rows [row_begin, row_begin + offset.size(2)).
   m.def(
@@ -673,5 +713,6 @@ TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
   m.impl("deform_conv2d_forward_rows", TORCH_FN(deform_conv2d_forward_rows));
   m.impl("deform_conv2d_backward_rows", TORCH_FN(deform_conv2d_backward_rows));
   m.impl("deform_conv2d_stage_input", TORCH_FN(deform_conv2d_stage_input));
+  m.impl("deform_conv2d_forward_staging", TORCH_FN(deform_conv2d_forward_staging));
   m.impl("deform_conv2d", TORCH_FN(deform_conv2d_plain));  // below autograd
 }

@@ -30,6 +30,13 @@ def test_opcheck_forward(cuda_device, use_mask, use_bias):
                           (x, w, off, m, b, 1, 1, 1, 1, 1, 1, 1, 1, MATH_FP32))
 
 
+def test_opcheck_forward_staging(cuda_device):
+    ops = _native.load_ops()
+    x, w, off, m, b = _inputs(requires_grad=False)
+    torch.library.opcheck(ops.deform_conv2d_forward_staging,
+                          (x, w, off, m, b, 1, 1, 1, 1, 1, 1, 1, 1, MATH_FP32))
+
+
 def test_opcheck_backward(cuda_device):
     ops = _native.load_ops()
     x, w, off, m, b = _inputs(requires_grad=False)

@@ -49,6 +49,45 @@ def test_staged_equals_unstaged(cuda_device, mode, layout):
         np.testing.assert_allclose(b, a, rtol=1e-5, atol=1e-5 * scale)
 
 
+@pytest.mark.parametrize("layout", ["nchw", "channels_last"])
+@pytest.mark.parametrize("mode", sorted(MODES))
+def test_forward_staging_keeps_the_staging_copy(cuda_device, mode, layout):
+    """deform_conv2d_forward_staging (DCN_KEEP_STAGED): the output of the
+    plain forward and the copy deform_conv2d_stage_input makes, bit for bit."""
+    flags = MODES[mode]
+    case = make_case(N=2, inC=64, outC=64, H=12, W=14, offset_scale=2.0, mask_kind="sigmoid")
+    d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    x = d["x"]
+    if layout == "channels_last":
+        x = x.contiguous(memory_format=torch.channels_last)
+    ops = _ops()
+    args = (1, 1, 1, 1, 1, 1, 1, 1)
+    out, staged = ops.deform_conv2d_forward_staging(x, d["w"], d["off"], d["m"], d["b"], *args,
+                                                    flags)
+    ref = ops.deform_conv2d_forward(x, d["w"], d["off"], d["m"], d["b"], *args, flags)
+    assert torch.equal(out, ref)
+    assert staged.dtype == torch.float32 and staged.numel() == 2 * 12 * 14 * 64 + 64
+    assert torch.equal(staged, ops.deform_conv2d_stage_input(x))
+
+
+def test_keep_staged_refuses_a_staged_input(cuda_device):
+    import ctypes
+    lib = _native.load_capi()
+    case = make_case(N=1, inC=32, outC=32, H=8, W=9)
+    d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    shape = _native.DcnShape(batch=1, in_channels=32, height=8, width=9, out_channels=32,
+                             kernel_h=3, kernel_w=3, stride_h=1, stride_w=1, pad_h=1, pad_w=1,
+                             dilation_h=1, dilation_w=1, groups=1, deformable_groups=1)
+    out = torch.empty(1, 32, 8, 9, device="cuda")
+    ws = torch.empty(1 << 24, dtype=torch.uint8, device="cuda")
+    vp = ctypes.c_void_p
+    rc = lib.dcn_forward(ctypes.byref(shape), vp(d["x"].data_ptr()), vp(d["w"].data_ptr()),
+                         vp(d["off"].data_ptr()), vp(d["m"].data_ptr()), vp(d["b"].data_ptr()),
+                         vp(out.data_ptr()), 0x40000 | 0x80000, vp(ws.data_ptr()), ws.numel(),
+                         vp(torch.cuda.current_stream().cuda_stream))
+    assert rc == 1 and b"KEEP_STAGED" in lib.dcn_last_error()
+
+
 def test_staged_size_is_checked(cuda_device):
     case = make_case(N=1, inC=32, outC=32, H=8, W=9)
     d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
