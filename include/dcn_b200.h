@@ -304,6 +304,18 @@ DCN_API int dcn_forward_noalloc(const dcn_shape* shape, const float* input,
 DCN_API size_t dcn_staged_input_size(const dcn_shape* shape);
 DCN_API int dcn_stage_input(const dcn_shape* shape, const float* input, float* staged,
                             uint32_t flags, void* stream);
+/* The same for bf16 or fp16 tensors (16-bit values moved as they are):
+ * dcn_staged_input_size_h16 bytes, for the 16-bit entry points with
+ * DCN_INPUT_STAGED.  Those take a staging copy (DCN_INPUT_STAGED) or keep
+ * theirs (dcn_forward_bf16 / _f16 with DCN_KEEP_STAGED, at the workspace
+ * start as dcn_forward) only on their tensor-core routes:
+ * dcn_h16_staging(shape, flags) is 1 when both the 16-bit forward and
+ * backward take them for this shape and flags, 0 otherwise (then the calls
+ * refuse both flags).  No reference counterpart. */
+DCN_API size_t dcn_staged_input_size_h16(const dcn_shape* shape);
+DCN_API int dcn_stage_input_h16(const dcn_shape* shape, const void* input, void* staged,
+                                uint32_t flags, void* stream);
+DCN_API int dcn_h16_staging(const dcn_shape* shape, uint32_t flags);
 
 /* Device error word of the current device (DCN_STATUS_* bits; 0 when every
  * wait of the tensor-core kernels completed in time).  No reference

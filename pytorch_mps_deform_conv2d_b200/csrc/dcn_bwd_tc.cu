@@ -1974,17 +1974,60 @@ namespace {
 // first item of an array also takes its scalar tail).  A block takes items
 // blockIdx.x, + gridDim.x, ...: every block gets a mix of the three kinds.
 constexpr int ZERO_ITEM = 4096;  // floats an item zeroes (256 threads x 4 float4)
+struct ZeroItems {
+  float* zp[4];
+  long long zn[4];   // floats of array l
+  long long zv[4];   // float4 vectors zeroed as vectors (0: misaligned, all scalar)
+  int zitems[4];     // items of array l
+  int zcount;
+  int total;         // items of all arrays
+};
+// Zero item b of `z` (256 threads).
+__device__ __forceinline__ void zero_item(const ZeroItems& z, int b) {
+  int l = 0;
+  while (l < z.zcount - 1 && b >= z.zitems[l]) b -= z.zitems[l++];
+  float* p = z.zp[l];
+  const long long n = z.zn[l], nv = z.zv[l];
+  if (nv > 0) {
+    float4* p4 = reinterpret_cast<float4*>(p);
+    const long long v0 = (long long)b * (ZERO_ITEM / 4);
+#pragma unroll
+    for (int u = 0; u < ZERO_ITEM / 1024; ++u) {
+      const long long v = v0 + u * 256 + threadIdx.x;
+      if (v < nv) p4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (b == 0)
+      for (long long i = (nv << 2) + threadIdx.x; i < n; i += 256) p[i] = 0.f;
+  } else {
+    const long long e0 = (long long)b * ZERO_ITEM;
+    for (long long i = e0 + threadIdx.x; i < e0 + ZERO_ITEM && i < n; i += 256) p[i] = 0.f;
+  }
+}
+// The items of a ZeroList (host).
+bool zero_items(const ZeroList& zl, ZeroItems& z) {
+  z = ZeroItems{};
+  z.zcount = zl.count;
+  long long total = 0;
+  for (int l = 0; l < zl.count; ++l) {
+    z.zp[l] = zl.ptr[l];
+    z.zn[l] = zl.n[l];
+    z.zv[l] = (reinterpret_cast<uintptr_t>(zl.ptr[l]) & 15u) == 0 ? zl.n[l] >> 2 : 0;
+    const long long items = (zl.n[l] + ZERO_ITEM - 1) / ZERO_ITEM;
+    if (items > (1LL << 30)) return false;
+    z.zitems[l] = (int)items;
+    total += items;
+  }
+  if (total > (1LL << 30)) return false;
+  z.total = (int)total;
+  return true;
+}
 struct Prologue {
   const float* go;
   float* go_r;
   float* gpart;
   const float* w;
   float* wbt;
-  float* zp[4];
-  long long zn[4];   // floats of array l
-  long long zv[4];   // float4 vectors zeroed as vectors (0: misaligned, all scalar)
-  int zitems[4];     // items of array l
-  int zcount;
+  ZeroItems z;
   int Ppad, pspans, vec;
   int nb_prep, pack_x, pack_y, nb_pack, total;
 };
@@ -1999,25 +2042,7 @@ __global__ void __launch_bounds__(256) bwd_prologue_kernel(Prologue a, Geom g) {
       const int gi = b / per_g, r = b - gi * per_g;
       pack_weight_bwd_tile(r % a.pack_x, r / a.pack_x, gi, a.w, a.wbt, g, 0);
     } else {
-      b -= a.nb_pack;
-      int l = 0;
-      while (l < a.zcount - 1 && b >= a.zitems[l]) b -= a.zitems[l++];
-      float* p = a.zp[l];
-      const long long n = a.zn[l], nv = a.zv[l];
-      if (nv > 0) {
-        float4* p4 = reinterpret_cast<float4*>(p);
-        const long long v0 = (long long)b * (ZERO_ITEM / 4);
-#pragma unroll
-        for (int u = 0; u < ZERO_ITEM / 1024; ++u) {
-          const long long v = v0 + u * 256 + threadIdx.x;
-          if (v < nv) p4[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (b == 0)
-          for (long long i = (nv << 2) + threadIdx.x; i < n; i += 256) p[i] = 0.f;
-      } else {
-        const long long e0 = (long long)b * ZERO_ITEM;
-        for (long long i = e0 + threadIdx.x; i < e0 + ZERO_ITEM && i < n; i += 256) p[i] = 0.f;
-      }
+      zero_item(a.z, b - a.nb_pack);
     }
     __syncthreads();  // the shared staging of one item is free before the next
   }
@@ -2039,17 +2064,8 @@ cudaError_t launch_bwd_prologue(const Geom& g, const float* go, float* go_r, flo
   a.gpart = gpart;
   a.w = w;
   a.wbt = wbt;
-  a.zcount = z.count;
-  long long zitems = 0;
-  for (int l = 0; l < z.count; ++l) {
-    a.zp[l] = z.ptr[l];
-    a.zn[l] = z.n[l];
-    a.zv[l] = (reinterpret_cast<uintptr_t>(z.ptr[l]) & 15u) == 0 ? z.n[l] >> 2 : 0;
-    const long long items = (z.n[l] + ZERO_ITEM - 1) / ZERO_ITEM;
-    if (items > (1LL << 30)) return cudaErrorInvalidValue;
-    a.zitems[l] = (int)items;
-    zitems += items;
-  }
+  if (!zero_items(z, a.z)) return cudaErrorInvalidValue;
+  const long long zitems = a.z.total;
   a.Ppad = (g.P + 3) & ~3;
   a.pspans = (a.Ppad + PG_SPAN - 1) / PG_SPAN;
   a.vec = g.P % 4 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
@@ -2253,15 +2269,17 @@ cudaError_t launch_bwd_fused_tc(const Geom& g, const float* go_r, const float* w
 namespace {
 // 16-bit grad_out (N*outC rows of P) -> go_r rows padded to Ppad (a multiple
 // of 8: 16-byte pitch; the padding zero), its values unchanged; with `gb`
-// (fp32, pre-zeroed) the bias gradient summed on the way in fp32.
+// (fp32, pre-zeroed) the bias gradient summed on the way in fp32, or with
+// `gpart` the span's sum written to gpart[bid] (as prep_go_block).
 template <int FMT>
-__global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __restrict__ go,
-                                                        unsigned short* __restrict__ go_r,
-                                                        float* __restrict__ gb, int outC, int P,
-                                                        int Ppad, int pspans, int vec) {
+__device__ __forceinline__ void prep_go16_block(long long bid,
+                                                const unsigned short* __restrict__ go,
+                                                unsigned short* __restrict__ go_r,
+                                                float* __restrict__ gb, float* __restrict__ gpart,
+                                                int outC, int P, int Ppad, int pspans, int vec) {
   __shared__ float part[8];
-  const long long row = blockIdx.x / pspans;  // n * outC + o
-  const int pbeg = (int)(blockIdx.x - row * pspans) * PG_SPAN;
+  const long long row = bid / pspans;  // n * outC + o
+  const int pbeg = (int)(bid - row * pspans) * PG_SPAN;
   const int pend = min(Ppad, pbeg + PG_SPAN);
   const unsigned short* src = go + row * P;
   unsigned short* dst = go_r + row * Ppad;
@@ -2282,7 +2300,7 @@ __global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __
       else sum += __uint_as_float((uint32_t)v << 16);
     }
   }
-  if (gb == nullptr) return;
+  if (gb == nullptr && gpart == nullptr) return;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sum;
@@ -2290,16 +2308,25 @@ __global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __
   if (threadIdx.x == 0) {
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
-    atomicAdd(gb + row % outC, t);
+    if (gpart != nullptr) gpart[bid] = t;
+    else atomicAdd(gb + row % outC, t);
   }
+}
+template <int FMT>
+__global__ void __launch_bounds__(256) prep_go16_kernel(const unsigned short* __restrict__ go,
+                                                        unsigned short* __restrict__ go_r,
+                                                        float* __restrict__ gb, int outC, int P,
+                                                        int Ppad, int pspans, int vec) {
+  prep_go16_block<FMT>(blockIdx.x, go, go_r, gb, nullptr, outC, P, Ppad, pspans, vec);
 }
 
 // 16-bit weight (outC, Cg, kh, kw) -> wbt[(g*kk + k)*Cg + c][o] (16-bit, as
-// the fp32 pack of the grad-column operand), one thread per element.
-__global__ void __launch_bounds__(256) pack_weight_bwd16_kernel(
-    const unsigned short* __restrict__ w, unsigned short* __restrict__ wb, Geom g,
-    long long total) {
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+// the fp32 pack of the grad-column operand): elements [i0, i1), thread t of
+// 256 takes i0 + t, i0 + t + stride, ...
+__device__ __forceinline__ void pack16_range(long long i0, long long i1, long long stride,
+                                             const unsigned short* __restrict__ w,
+                                             unsigned short* __restrict__ wb, const Geom& g) {
+  for (long long i = i0 + threadIdx.x; i < i1; i += stride) {
     // i enumerates the output: ((gi*kk + k)*Cg + c)*Og + o
     const int o = (int)(i % g.Og);
     long long r = i / g.Og;
@@ -2308,6 +2335,44 @@ __global__ void __launch_bounds__(256) pack_weight_bwd16_kernel(
     const int k = (int)(r % g.kk);
     const int gi = (int)(r / g.kk);
     wb[i] = __ldg(w + ((long long)(gi * g.Og + o) * g.Cg + c) * g.kk + k);
+  }
+}
+__global__ void __launch_bounds__(256) pack_weight_bwd16_kernel(
+    const unsigned short* __restrict__ w, unsigned short* __restrict__ wb, Geom g,
+    long long total) {
+  pack16_range(blockIdx.x * 256LL, total, (long long)gridDim.x * 256, w, wb, g);
+}
+
+// The 16-bit fused backward's helpers in one launch, as bwd_prologue_kernel:
+// items [0, nb_prep) prepare a grad_out span each (grad_bias partial sums),
+// the next nb_pack pack PACK16_ITEM weight elements each, the rest zero the
+// accumulators.
+constexpr int PACK16_ITEM = 2048;
+struct Prologue16 {
+  const unsigned short* go;
+  unsigned short* go_r;
+  float* gpart;
+  const unsigned short* w;
+  unsigned short* wbt;
+  long long wtotal;
+  ZeroItems z;
+  int Ppad, pspans, vec;
+  int nb_prep, nb_pack, total;
+};
+template <int FMT>
+__global__ void __launch_bounds__(256) bwd_prologue16_kernel(Prologue16 a, Geom g) {
+  for (int it = blockIdx.x; it < a.total; it += gridDim.x) {
+    int b = it;
+    if (b < a.nb_prep) {
+      prep_go16_block<FMT>(b, a.go, a.go_r, nullptr, a.gpart, g.outC, g.P, a.Ppad, a.pspans,
+                           a.vec);
+    } else if ((b -= a.nb_prep) < a.nb_pack) {
+      const long long i0 = (long long)b * PACK16_ITEM;
+      pack16_range(i0, std::min<long long>(i0 + PACK16_ITEM, a.wtotal), 256, a.w, a.wbt, g);
+    } else {
+      zero_item(a.z, b - a.nb_pack);
+    }
+    __syncthreads();  // the shared staging of one item is free before the next
   }
 }
 
@@ -2348,7 +2413,19 @@ template <int FMT>
 __global__ void __launch_bounds__(256) grads_to_h16_kernel(const float* __restrict__ gwt,
                                                            unsigned short* __restrict__ gw,
                                                            int Cg, int kk, long long nw,
-                                                           H16List rest) {
+                                                           H16List rest,
+                                                           const float* __restrict__ gpart,
+                                                           unsigned short* __restrict__ gb16,
+                                                           int N, int outC, int pspans) {
+  if (gpart != nullptr)  // grad_bias from the prologue's partial sums, in a fixed order
+    for (long long o = blockIdx.x * 256LL + threadIdx.x; o < outC; o += gridDim.x * 256LL) {
+      float t = 0.f;
+      for (int n = 0; n < N; ++n)
+        for (int sp = 0; sp < pspans; ++sp)
+          t += __ldg(gpart + ((long long)n * outC + o) * pspans + sp);
+      if constexpr (FMT == kF16s) gb16[o] = __half_as_ushort(__float2half_rn(t));
+      else gb16[o] = __bfloat16_as_ushort(__float2bfloat16_rn(t));
+    }
   const long long total = nw + rest.n[0] + rest.n[1] + rest.n[2];
   for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
     float v;
@@ -2374,15 +2451,18 @@ __global__ void __launch_bounds__(256) grads_to_h16_kernel(const float* __restri
 }  // namespace
 
 cudaError_t launch_grads_to_h16(const float* gwt, void* gw, const Geom& g, const H16List& rest,
-                                bool f16, cudaStream_t stream) {
+                                bool f16, cudaStream_t stream, const float* gpart, void* gb) {
   const long long nw = (long long)g.outC * g.Cg * g.kk;
-  const long long total = nw + rest.n[0] + rest.n[1] + rest.n[2];
+  const long long total = nw + rest.n[0] + rest.n[1] + rest.n[2] + (gpart ? g.outC : 0);
   if (total == 0) return cudaSuccess;
   long long blocks = (total + 255) / 256;
   if (blocks > 148LL * 8) blocks = 148LL * 8;
+  const int Ppad = (g.P + 7) & ~7;
   auto kern = f16 ? grads_to_h16_kernel<kF16s> : grads_to_h16_kernel<kBF16s>;
   kern<<<(int)blocks, 256, 0, stream>>>(gwt, static_cast<unsigned short*>(gw), g.Cg, g.kk, nw,
-                                        rest);
+                                        rest, gb != nullptr ? gpart : nullptr,
+                                        static_cast<unsigned short*>(gb), g.N, g.outC,
+                                        (Ppad + PG_SPAN - 1) / PG_SPAN);
   return cudaGetLastError();
 }
 
@@ -2411,6 +2491,40 @@ cudaError_t launch_pack_weight_bwd16(const void* w, void* wbt, const Geom& g,
   pack_weight_bwd16_kernel<<<(int)blocks, 256, 0, stream>>>(
       static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wbt), g, total);
   return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_prologue16(const Geom& g, const void* go, void* go_r, float* gpart,
+                                  const void* w, void* wbt, const ZeroList& z, bool f16,
+                                  cudaStream_t stream) {
+  if (g.P == 0 || z.count > 4) return cudaErrorInvalidValue;
+  Prologue16 a{};
+  a.go = static_cast<const unsigned short*>(go);
+  a.go_r = static_cast<unsigned short*>(go_r);
+  a.gpart = gpart;
+  a.w = static_cast<const unsigned short*>(w);
+  a.wbt = static_cast<unsigned short*>(wbt);
+  a.wtotal = (long long)g.G * g.kk * g.Cg * g.Og;
+  if (!zero_items(z, a.z)) return cudaErrorInvalidValue;
+  a.Ppad = (g.P + 7) & ~7;
+  a.pspans = (a.Ppad + PG_SPAN - 1) / PG_SPAN;
+  a.vec = g.P % 8 == 0 && (reinterpret_cast<uintptr_t>(go) & 15u) == 0 &&
+          (reinterpret_cast<uintptr_t>(go_r) & 15u) == 0;
+  const long long prep = (long long)g.N * g.outC * a.pspans;
+  const long long pack = (a.wtotal + PACK16_ITEM - 1) / PACK16_ITEM;
+  const long long total = prep + pack + a.z.total;
+  if (total > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  a.nb_prep = (int)prep;
+  a.nb_pack = (int)pack;
+  a.total = (int)total;
+  const long long grid = std::min<long long>(total, (long long)device_sm_count() * 8);
+  auto kern = f16 ? bwd_prologue16_kernel<kF16s> : bwd_prologue16_kernel<kBF16s>;
+  kern<<<(unsigned)grid, 256, 0, stream>>>(a, g);
+  return cudaGetLastError();
+}
+
+size_t tc_bias_part_floats16(const Geom& g) {
+  const int Ppad = (g.P + 7) & ~7;
+  return (size_t)g.N * g.outC * ((Ppad + PG_SPAN - 1) / PG_SPAN);
 }
 
 cudaError_t launch_nhwc_to_nchw16(const float* gxt, void* gx, int N, int C, int HW, bool f16,

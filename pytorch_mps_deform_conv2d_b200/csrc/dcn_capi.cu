@@ -569,8 +569,12 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
   if (rc != DCN_OK) return rc;
   g.mask_logits = (flags & DCN_MASK_LOGITS) && mask != nullptr ? 1 : 0;
   apply_test_flags(g, flags);
-  DCN_CHECK(!(flags & (DCN_KEEP_STAGED | DCN_INPUT_STAGED)),
-            "deform_conv2d_forward: the 16-bit forward stages its input itself");
+  const bool staged = flags & DCN_INPUT_STAGED, keep = flags & DCN_KEEP_STAGED;
+  DCN_CHECK(!(staged && keep),
+            "deform_conv2d_forward: DCN_KEEP_STAGED needs an input to stage, not a staging copy");
+  DCN_CHECK(!(staged || keep) || use_bf16_tc(g, flags),
+            "deform_conv2d_forward: a 16-bit staging copy needs the tensor-core forward, which "
+            "does not cover this shape");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const long long out_numel = (long long)g.N * g.outC * g.P;
   if (out_numel == 0) return DCN_OK;
@@ -589,19 +593,23 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
                 need, workspace_bytes);
   char* base = static_cast<char*>(align_ptr(workspace));
   if (use_bf16_tc(g, flags)) {
-    void* xt = base;
-    void* wt = base + align_up(((size_t)g.N * g.HW * g.C + g.C) * 2);
+    // the 16-bit staging copy: the caller's (DCN_INPUT_STAGED) or the
+    // workspace's first carve, where DCN_KEEP_STAGED leaves it
+    void* xt = staged ? const_cast<void*>(input) : base;
+    void* wt = base + (staged ? 0 : align_up(((size_t)g.N * g.HW * g.C + g.C) * 2));
     char* tail = static_cast<char*>(wt) + align_up(dcn::tc_fwd_weight_bf16_bytes(g));
     const int sms = num_sms_current();
     const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, false, true, sms);
     const size_t usable = workspace_bytes - (size_t)(tail - static_cast<char*>(workspace));
     if (tail_bytes == 0 || usable < tail_bytes) tail = nullptr;
     // the weight pack (side stream) runs beside the input staging
-    Fork fk(stream, side_streams_pay(g));
+    Fork fk(stream, side_streams_pay(g) && !staged);
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bf16(weight, wt, g, tail, fk.side(0)),
                 "tc_pack_weight");
-    if (flags & DCN_INPUT_NHWC) {  // channels-last: a copy plus the zero row
+    if (staged) {
+      // nothing to stage
+    } else if (flags & DCN_INPUT_NHWC) {  // channels-last: a copy plus the zero row
       const size_t xb = (size_t)g.N * g.HW * g.C * 2;
       if (xb) DCN_CUDA(cudaMemcpyAsync(xt, input, xb, cudaMemcpyDeviceToDevice, stream), "copy");
       DCN_CUDA(cudaMemsetAsync(static_cast<char*>(xt) + xb, 0, (size_t)g.C * 2, stream),
@@ -965,24 +973,25 @@ static bool use_fused16(const dcn::Geom& g, uint32_t flags) {
 // Its workspace: the 16-bit staging copy, grad_out rows and packed weight;
 // fp32 accumulators of grad_input (NHWC), grad_offset, grad_mask, the
 // tap-major grad_weight and grad_bias.
-static size_t bwd_fused16_bytes(const dcn::Geom& g) {
+static size_t bwd_fused16_bytes(const dcn::Geom& g, bool staged) {
   const size_t w = (size_t)g.outC * g.Cg * g.kk;
-  return align_up(((size_t)g.N * g.HW * g.C + g.C) * 2) +
+  return (staged ? 0 : align_up(((size_t)g.N * g.HW * g.C + g.C) * 2)) +
          align_up((size_t)g.N * g.outC * ((g.P + 7) & ~7) * 2) + align_up(w * 2) +
          align_up((size_t)g.N * g.HW * g.C * 4) + align_up((size_t)g.N * 2 * g.dg * g.kk * g.P * 4) +
          align_up((size_t)g.N * g.dg * g.kk * g.P * 4) + align_up(w * 4) +
-         align_up((size_t)g.outC * 4) + kAlign;
+         align_up(dcn::tc_bias_part_floats16(g) * 4) + kAlign;
 }
 
 static size_t bwd_h16_ws(const dcn::Geom& g, uint32_t flags) {
-  return use_fused16(g, flags) ? bwd_fused16_bytes(g)
-                               : bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
+  return use_fused16(g, flags)
+             ? bwd_fused16_bytes(g, flags & DCN_INPUT_STAGED)
+             : bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags & ~(uint32_t)DCN_INPUT_STAGED);
 }
 
 DCN_API size_t dcn_backward_bf16_workspace_size(const dcn_shape* s, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_backward_bf16_workspace_size") != DCN_OK) return 0;
-  return bwd_h16_ws(g, flags & ~(uint32_t)DCN_INPUT_STAGED);
+  return bwd_h16_ws(g, flags);
 }
 
 // The 16-bit backward (bf16, or fp16 with `f16`): the fp32 backward on upcast
@@ -997,7 +1006,7 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
   int rc = make_geom(s, mask != nullptr, grad_bias != nullptr, g, "deform_conv2d_backward");
   if (rc != DCN_OK) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  flags &= ~(uint32_t)DCN_INPUT_STAGED;  // the staging copy is an fp32 layout
+  const bool staged = flags & DCN_INPUT_STAGED;
   if (use_fused16(g, flags)) {
     DCN_CHECK(mask != nullptr || grad_mask == nullptr,
               "deform_conv2d_backward: grad_mask must be NULL when mask is NULL");
@@ -1012,7 +1021,7 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
                   is_device_ptr(grad_weight) && (grad_mask == nullptr || is_device_ptr(grad_mask)) &&
                   (grad_bias == nullptr || is_device_ptr(grad_bias)),
               "deform_conv2d_backward: gradient outputs must be CUDA device buffers");
-    const size_t need16 = bwd_fused16_bytes(g);
+    const size_t need16 = bwd_fused16_bytes(g, staged);
     if (workspace_bytes < need16 || workspace == nullptr)
       return fail(DCN_ERR_WORKSPACE,
                   "deform_conv2d_backward: workspace of %zu bytes needed, %zu given", need16,
@@ -1026,59 +1035,60 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
     const long long nx = (long long)g.N * g.HW * g.C, nw = (long long)g.outC * g.Cg * g.kk;
     const long long noff = (long long)g.N * 2 * g.dg * g.kk * g.P;
     const long long nm = (long long)g.N * g.dg * g.kk * g.P;
-    void* xt = take(((size_t)nx + g.C) * 2);
+    // the caller's 16-bit staging copy (DCN_INPUT_STAGED), or our own
+    void* xt = staged ? const_cast<void*>(input) : take(((size_t)nx + g.C) * 2);
     void* go_r = take((size_t)g.N * g.outC * ((g.P + 7) & ~7) * 2);
     void* wbt = take((size_t)nw * 2);
     float* gxt = reinterpret_cast<float*>(take((size_t)nx * 4));
     float* goff = reinterpret_cast<float*>(take((size_t)noff * 4));
     float* gm = reinterpret_cast<float*>(take((size_t)nm * 4));
     float* gwt = reinterpret_cast<float*>(take((size_t)nw * 4));
-    float* gb = reinterpret_cast<float*>(take((size_t)g.outC * 4));
+    float* gpart = reinterpret_cast<float*>(take(dcn::tc_bias_part_floats16(g) * 4));
     const bool nhwc = flags & DCN_INPUT_NHWC;
     dcn::ZeroList z{};
     z.add(goff, noff);
     if (mask) z.add(gm, nm);
     z.add(gwt, nw);
-    // as the fp32 route: the grad_out prep on the caller's stream; the weight
-    // pack + zeroing (side 0) and the input staging + grad-input zeroing
-    // (side 1) beside it
-    Fork fk(stream, side_streams_pay(g));
-    DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_pack_weight_bwd16(weight, wbt, g, fk.side(0)),
-                "tc_pack_weight_bwd");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_zero(z, fk.side(0)), "zero");
-    const cudaStream_t s1 = fk.side(1);
-    DCN_CUDA_ON(s1, cudaMemsetAsync(gxt, 0, (size_t)nx * 4, s1), "memset");
-    if (nhwc) {  // channels-last: a copy plus the zero row
-      DCN_CUDA_ON(s1, cudaMemcpyAsync(xt, input, (size_t)nx * 2, cudaMemcpyDeviceToDevice, s1),
-                  "copy");
-      DCN_CUDA_ON(s1,
-                  cudaMemsetAsync(static_cast<char*>(xt) + (size_t)nx * 2, 0,
-                                  (size_t)g.C * 2, s1),
-                  "memset");
-    } else {
-      DCN_CUDA_ON(s1,
-                  dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
-                                                s1),
-                  "nchw_to_nhwc");
+    z.add(gxt, nx);
+    // the input staging (unless staged) on a side stream beside the helpers'
+    // one launch: grad_out rows with grad_bias partial sums, the packed
+    // weight, the zeroed accumulators
+    Fork fk(stream, side_streams_pay(g));  // one per call: it holds the side streams' lock
+    if (!staged) {
+      DCN_ORDER(fk.fork(), "fork");
+      const cudaStream_t s1 = fk.side(1);
+      if (nhwc) {  // channels-last: a copy plus the zero row
+        DCN_CUDA_ON(s1,
+                    cudaMemcpyAsync(xt, input, (size_t)nx * 2, cudaMemcpyDeviceToDevice, s1),
+                    "copy");
+        DCN_CUDA_ON(s1,
+                    cudaMemsetAsync(static_cast<char*>(xt) + (size_t)nx * 2, 0,
+                                    (size_t)g.C * 2, s1),
+                    "memset");
+      } else {
+        DCN_CUDA_ON(s1,
+                    dcn::launch_nchw_to_nhwc_bf16(input, xt, g.N, g.C, g.HW, /*zero_row=*/true,
+                                                  s1),
+                    "nchw_to_nhwc");
+      }
     }
-    if (grad_bias) DCN_CUDA(cudaMemsetAsync(gb, 0, (size_t)g.outC * 4, stream), "memset");
-    DCN_CUDA(dcn::launch_prep_go16(g, grad_output, go_r, grad_bias ? gb : nullptr, f16, stream),
-             "tc_prep_go");
-    DCN_ORDER(fk.join(0), "join");
-    DCN_ORDER(fk.join(1), "join");
+    DCN_CUDA(dcn::launch_bwd_prologue16(g, grad_output, go_r, grad_bias ? gpart : nullptr,
+                                        weight, wbt, z, f16, stream),
+             "bwd_prologue");
+    if (!staged) DCN_ORDER(fk.join(1), "join");
     DCN_CUDA(dcn::launch_bwd_fused_tc_h16(g, go_r, wbt, xt, offset, mask, gxt, goff,
                                           mask ? gm : nullptr, gwt, f16, num_sms_current(),
                                           stream),
              f16 ? "bwd_fused_tc_f16" : "bwd_fused_tc_bf16");
     // grad_input back to the tensors' layout and type, the other gradients
-    // rounded beside it (side 0)
+    // rounded (grad_bias summed from its parts) beside it (side 0)
     dcn::H16List rest{};
     rest.add(goff, grad_offset, noff);
     if (mask) rest.add(gm, grad_mask, nm);
-    if (grad_bias) rest.add(gb, grad_bias, g.outC);
     DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_grads_to_h16(gwt, grad_weight, g, rest, f16, fk.side(0)),
+    DCN_CUDA_ON(fk.side(0),
+                dcn::launch_grads_to_h16(gwt, grad_weight, g, rest, f16, fk.side(0), gpart,
+                                         grad_bias),
                 "grads_to_h16");
     if (nhwc)
       DCN_CUDA(dcn::launch_f32_to_h16(gxt, grad_input, nx, f16, stream),
@@ -1089,6 +1099,8 @@ static int backward_h16(bool f16, const dcn_shape* s, const void* grad_output, c
     DCN_ORDER(fk.join(0), "join");
     return DCN_OK;
   }
+  DCN_CHECK(!staged, "deform_conv2d_backward: a 16-bit staging copy needs the tensor-core "
+                     "backward, which does not cover this shape");
   const size_t need = bwd_bf16_copy_bytes(g) + kAlign + bwd_ws(g, flags);
   if (workspace_bytes < need || workspace == nullptr)
     return fail(DCN_ERR_WORKSPACE, "deform_conv2d_backward: workspace of %zu bytes needed, %zu given",
@@ -1142,7 +1154,7 @@ DCN_API int dcn_backward_bf16(const dcn_shape* s, const void* grad_output, const
 DCN_API size_t dcn_backward_f16_workspace_size(const dcn_shape* s, uint32_t flags) {
   dcn::Geom g;
   if (make_geom(s, true, true, g, "dcn_backward_f16_workspace_size") != DCN_OK) return 0;
-  return bwd_h16_ws(g, flags & ~(uint32_t)DCN_INPUT_STAGED);
+  return bwd_h16_ws(g, flags);
 }
 
 DCN_API int dcn_backward_f16(const dcn_shape* s, const void* grad_output, const void* input,
@@ -1236,6 +1248,40 @@ DCN_API int dcn_stage_input(const dcn_shape* s, const float* input, float* stage
     DCN_CUDA(dcn::launch_nchw_to_nhwc(input, staged, g.N, g.C, g.HW, true, nullptr, stream),
              "nchw_to_nhwc");
   return DCN_OK;
+}
+
+DCN_API size_t dcn_staged_input_size_h16(const dcn_shape* s) {
+  dcn::Geom g;
+  if (make_geom(s, false, false, g, "dcn_staged_input_size_h16") != DCN_OK) return 0;
+  return ((size_t)g.N * g.HW * g.C + g.C) * 2;
+}
+
+DCN_API int dcn_stage_input_h16(const dcn_shape* s, const void* input, void* staged,
+                                uint32_t flags, void* stream_) {
+  g_last_error.clear();
+  dcn::Geom g;
+  int rc = make_geom(s, false, false, g, "dcn_stage_input_h16");
+  if (rc != DCN_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const size_t nx = (size_t)g.N * g.HW * g.C;
+  DCN_CHECK(is_device_ptr(staged), "dcn_stage_input_h16: staged must be a CUDA device buffer");
+  DCN_CHECK(nx == 0 || is_device_ptr(input), "dcn_stage_input_h16: input must be a CUDA tensor");
+  if (flags & DCN_INPUT_NHWC) {  // a copy plus the zero row
+    if (nx) DCN_CUDA(cudaMemcpyAsync(staged, input, nx * 2, cudaMemcpyDeviceToDevice, stream), "copy");
+    DCN_CUDA(cudaMemsetAsync(static_cast<char*>(staged) + nx * 2, 0, (size_t)g.C * 2, stream),
+             "memset");
+  } else {
+    DCN_CUDA(dcn::launch_nchw_to_nhwc_bf16(input, staged, g.N, g.C, g.HW, /*zero_row=*/true,
+                                           stream),
+             "nchw_to_nhwc");
+  }
+  return DCN_OK;
+}
+
+DCN_API int dcn_h16_staging(const dcn_shape* s, uint32_t flags) {
+  dcn::Geom g;
+  if (make_geom(s, true, true, g, "dcn_h16_staging") != DCN_OK) return 0;
+  return use_bf16_tc(g, flags) && use_fused16(g, flags) ? 1 : 0;
 }
 
 DCN_API int dcn_device_status(void* stream_, int clear, int* status) {

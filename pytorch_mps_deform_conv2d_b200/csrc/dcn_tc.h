@@ -7,6 +7,7 @@
 #include "dcn_common.cuh"
 
 namespace dcn {
+struct ZeroList;  // dcn_kernels.h
 
 // Error words of the tensor-core kernels (a bit per kernel family whose
 // bounded mbarrier wait ran out: kStatusFwd, kStatusBwdData,
@@ -125,8 +126,19 @@ struct H16List {
     }
   }
 };
+// With `gpart` and `gb`: also the 16-bit grad_bias from launch_bwd_prologue16's
+// partial sums.
 cudaError_t launch_grads_to_h16(const float* gwt, void* gw, const Geom& g, const H16List& rest,
-                                bool f16, cudaStream_t stream);
+                                bool f16, cudaStream_t stream, const float* gpart = nullptr,
+                                void* gb = nullptr);
+// The 16-bit fused backward's helpers in one launch (as launch_bwd_prologue):
+// 16-bit grad_out rows with fp32 grad_bias partial sums into `gpart`
+// (tc_bias_part_floats16 of them; NULL: no bias), the 16-bit packed weight,
+// the zeroing of `z`.
+size_t tc_bias_part_floats16(const Geom& g);
+cudaError_t launch_bwd_prologue16(const Geom& g, const void* go, void* go_r, float* gpart,
+                                  const void* w, void* wbt, const ZeroList& z, bool f16,
+                                  cudaStream_t stream);
 // Weight gradient as a dense TMA-fed GEMM over the column buffer, summed into
 // `gw` (pre-zeroed): grad_weight itself ([outC][Cg][kh*kw]), or with
 // `tap_major` a [outC][kh*kw][Cg] copy, whose reductions coalesce, for the
@@ -140,7 +152,6 @@ cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* 
 cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
                                          cudaStream_t stream, const float* gpart = nullptr,
                                          float* gb = nullptr);
-struct ZeroList;  // dcn_kernels.h
 // The fused TF32 backward's helpers for a staged input, in one launch:
 // launch_tc_prep_go's work with grad_bias as per-block partial sums into
 // `gpart` (tc_bias_part_floats of them; NULL: no bias), the packed weight of

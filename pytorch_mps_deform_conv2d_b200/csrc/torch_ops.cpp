@@ -130,6 +130,41 @@ const float* staged_ptr(const c10::optional<at::Tensor>& staged, const at::Tenso
   return staged->data_ptr<float>();
 }
 
+// The 16-bit staging copy of `x` (a tensor of x's dtype, dcn_staged_input_size_h16
+// bytes) when the caller passed one; NULL otherwise.
+const void* staged_ptr16(const c10::optional<at::Tensor>& staged, const at::Tensor& x,
+                         const dcn_shape& s) {
+  if (!staged.has_value() || !staged->defined() || staged->numel() == 0) return nullptr;
+  TORCH_CHECK(staged->device() == x.device() && staged->scalar_type() == x.scalar_type() &&
+                  staged->is_contiguous() &&
+                  (size_t)staged->numel() * 2 == dcn_staged_input_size_h16(&s),
+              "staged must be the 16-bit staging copy of the input "
+              "(deform_conv2d_stage_input)");
+  return staged->data_ptr();
+}
+
+// Whether the 16-bit forward and backward of this call take a staging copy
+// (dcn_h16_staging: both on their tensor-core routes).
+bool h16_staging(const at::Tensor& input, const at::Tensor& weight, int64_t stride_h,
+                 int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                 int64_t dilation_w, int64_t groups, int64_t deformable_groups, int64_t math) {
+  if (input.dim() != 4 || weight.dim() != 4) return false;
+  const dcn_shape s = make_shape(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                                 dilation_w, groups, deformable_groups);
+  const uint32_t flags = resolve_flags(math) | (channels_last(input) ? DCN_INPUT_NHWC : 0u);
+  return dcn_h16_staging(&s, flags) == 1;
+}
+
+// The staging copy a forward with DCN_KEEP_STAGED left at the 256-byte
+// aligned start of its workspace `ws`: `bytes` bytes viewed as `dt`.
+at::Tensor kept_staging(const at::Tensor& ws, size_t bytes, at::ScalarType dt) {
+  const uintptr_t base = reinterpret_cast<uintptr_t>(ws.data_ptr());
+  const int64_t lead = (int64_t)(((base + 255) & ~(uintptr_t)255) - base);
+  TORCH_CHECK(bytes > 0 && lead + (int64_t)bytes <= ws.numel(),
+              "deform_conv2d_forward: no staging copy");
+  return ws.narrow(0, lead, (int64_t)bytes).view(dt);
+}
+
 at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
                         const at::Tensor& offset, const at::Tensor& mask,
                         const c10::optional<at::Tensor>& bias, int64_t stride_h,
@@ -185,13 +220,18 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (h16) {
-    const size_t ws16 = f16 ? dcn_forward_f16_workspace_size(&s, flags)
-                            : dcn_forward_bf16_workspace_size(&s, flags);
+    const void* xs = staged_ptr16(staged, x, s);
+    const uint32_t flags16 =
+        flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);
+    const size_t ws16 = f16 ? dcn_forward_f16_workspace_size(&s, flags16)
+                            : dcn_forward_bf16_workspace_size(&s, flags16);
     auto ws = at::empty({(int64_t)std::max<size_t>(ws16, 1)}, x.options().dtype(at::kByte));
     auto fwd16 = f16 ? dcn_forward_f16 : dcn_forward_bf16;
-    check_rc(fwd16(&s, x.data_ptr(), w.data_ptr(), off.data_ptr(),
+    check_rc(fwd16(&s, xs ? xs : x.data_ptr(), w.data_ptr(), off.data_ptr(),
                    use_mask ? msk.data_ptr() : nullptr, b.defined() ? b.data_ptr() : nullptr,
-                   out.data_ptr(), flags, ws.data_ptr(), ws16, stream.stream()));
+                   out.data_ptr(), flags16, ws.data_ptr(), ws16, stream.stream()));
+    if (keep_staged != nullptr)
+      *keep_staged = kept_staging(ws, dcn_staged_input_size_h16(&s), x.scalar_type());
     return out;
   }
   const float* mp = use_mask ? msk.data_ptr<float>() : nullptr;
@@ -212,14 +252,8 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   check_rc(dcn_forward(&s, xs ? xs : x.data_ptr<float>(), w.data_ptr<float>(),
                        off.data_ptr<float>(), mp, bp, out.data_ptr<float>(), fflags,
                        ws.data_ptr(), ws_bytes, stream.stream()));
-  if (keep_staged != nullptr) {
-    // the staging copy the forward left at the workspace's 256-byte aligned start
-    const uintptr_t base = reinterpret_cast<uintptr_t>(ws.data_ptr());
-    const int64_t lead = (int64_t)(((base + 255) & ~(uintptr_t)255) - base);
-    const int64_t bytes = (int64_t)dcn_staged_input_size(&s);
-    TORCH_CHECK(bytes > 0 && lead + bytes <= ws.numel(), "deform_conv2d_forward: no staging copy");
-    *keep_staged = ws.narrow(0, lead, bytes).view(at::kFloat);
-  }
+  if (keep_staged != nullptr)
+    *keep_staged = kept_staging(ws, dcn_staged_input_size(&s), at::kFloat);
   return out;
 }
 
@@ -250,8 +284,11 @@ at::Tensor deform_conv2d_plain(const at::Tensor& input, const at::Tensor& weight
 // the `staged` argument of the forward and backward operators: a training
 // step stages its input once for both.
 at::Tensor deform_conv2d_stage_input(const at::Tensor& input) {
-  TORCH_CHECK(input.device().is_cuda() && input.scalar_type() == at::kFloat && input.dim() == 4,
-              "deform_conv2d_stage_input: input must be a 4-D float32 CUDA tensor");
+  const auto dt = input.scalar_type();
+  const bool h16 = dt == at::kBFloat16 || dt == at::kHalf;
+  TORCH_CHECK(input.device().is_cuda() && (dt == at::kFloat || h16) && input.dim() == 4,
+              "deform_conv2d_stage_input: input must be a 4-D float32, bfloat16 or float16 "
+              "CUDA tensor");
   c10::cuda::CUDAGuard guard(input.device());
   const bool nhwc = channels_last(input);
   auto x = nhwc ? input : input.contiguous();
@@ -266,6 +303,14 @@ at::Tensor deform_conv2d_stage_input(const at::Tensor& input) {
   s.dilation_h = s.dilation_w = 1;
   s.groups = 1;
   s.deformable_groups = 1;
+  if (h16) {  // the same layout in the input's 16-bit type
+    const size_t bytes = dcn_staged_input_size_h16(&s);
+    TORCH_CHECK(bytes > 0, dcn_last_error());
+    auto staged = at::empty({(int64_t)(bytes / 2)}, x.options());
+    check_rc(dcn_stage_input_h16(&s, x.data_ptr(), staged.data_ptr(), nhwc ? DCN_INPUT_NHWC : 0u,
+                                 at::cuda::getCurrentCUDAStream().stream()));
+    return staged;
+  }
   const size_t bytes = dcn_staged_input_size(&s);
   TORCH_CHECK(bytes > 0, dcn_last_error());
   auto staged = at::empty({(int64_t)(bytes / sizeof(float))}, x.options());
@@ -283,8 +328,22 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_staging(
     const at::Tensor& mask, const c10::optional<at::Tensor>& bias, int64_t stride_h,
     int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
     int64_t groups, int64_t deformable_groups, int64_t math) {
-  TORCH_CHECK(input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0,
-              "deform_conv2d_forward_staging: input must be a non-empty 4-D float32 tensor");
+  TORCH_CHECK(input.dim() == 4 && input.numel() > 0,
+              "deform_conv2d_forward_staging: input must be a non-empty 4-D tensor");
+  const auto dt = input.scalar_type();
+  if (dt == at::kBFloat16 || dt == at::kHalf) {
+    // the 16-bit forward keeps its staging copy on its tensor-core route;
+    // elsewhere the copy is made on its own (and the backward's upcast route
+    // does not take it)
+    at::Tensor staged;
+    const bool keep = h16_staging(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                                  dilation_w, groups, deformable_groups, math);
+    auto out = forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                            dilation_h, dilation_w, groups, deformable_groups, -1, math,
+                            c10::nullopt, keep ? &staged : nullptr);
+    if (!staged.defined()) staged = deform_conv2d_stage_input(input);
+    return std::make_tuple(out, staged);
+  }
   at::Tensor staged;
   auto out = forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
                           dilation_h, dilation_w, groups, deformable_groups, -1, math,
@@ -356,13 +415,16 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
     }
     const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h,
                                    dilation_w, groups, deformable_groups);
-    const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u);
+    const void* xs = staged_ptr16(staged, x, s);
+    const uint32_t flags =
+        resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u) | (xs ? DCN_INPUT_STAGED : 0u);
     const size_t ws_bytes = f16 ? dcn_backward_f16_workspace_size(&s, flags)
                                 : dcn_backward_bf16_workspace_size(&s, flags);
     auto ws = at::empty({(int64_t)std::max<size_t>(ws_bytes, 1)}, x.options().dtype(at::kByte));
     auto vp = [](const at::Tensor& t) -> void* { return t.numel() ? t.data_ptr() : nullptr; };
     auto bwd16 = f16 ? dcn_backward_f16 : dcn_backward_bf16;
-    check_rc(bwd16(&s, vp(go), vp(x), vp(w), vp(off), use_mask ? vp(msk) : nullptr,
+    check_rc(bwd16(&s, vp(go), xs ? const_cast<void*>(xs) : vp(x), vp(w), vp(off),
+                   use_mask ? vp(msk) : nullptr,
                    vp(grad_input), vp(grad_offset), use_mask ? vp(grad_mask) : nullptr,
                    vp(grad_weight), use_bias ? vp(grad_bias) : nullptr, flags, ws.data_ptr(),
                    ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
@@ -588,9 +650,17 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
     at::Tensor out, staged;
     {
       at::AutoDispatchBelowADInplaceOrView below;
-      // a float32 input is staged (NHWC) once, inside the forward, and the
-      // staging copy kept for the backward
-      if (input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0) {
+      // a float32 input, or a 16-bit one whose passes both run on the tensor
+      // cores, is staged (NHWC) once, inside the forward, and the staging
+      // copy kept for the backward
+      const auto dt = input.scalar_type();
+      const bool stage_once =
+          input.dim() == 4 && input.numel() > 0 &&
+          (dt == at::kFloat ||
+           ((dt == at::kBFloat16 || dt == at::kHalf) &&
+            h16_staging(input, weight, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
+                        groups, deformable_groups, math)));
+      if (stage_once) {
         std::tie(out, staged) =
             fwd_staging.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
                              dilation_h, dilation_w, groups, deformable_groups, math);

@@ -113,3 +113,82 @@ def test_training_step_stages_its_input_once(cuda_device, mode):
         _native.profiler_enable(False)
     stats = _native.profiler_read()
     assert stats["nchw_to_nhwc"][0] == 1, stats  # staged once, for both passes
+
+
+H16 = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+
+@pytest.mark.parametrize("layout", ["nchw", "channels_last"])
+@pytest.mark.parametrize("dt", sorted(H16))
+def test_forward_staging_h16_keeps_the_staging_copy(cuda_device, dt, layout):
+    """16-bit tensors on the tensor-core route: the forward keeps its 16-bit
+    staging copy (DCN_KEEP_STAGED), the same bits deform_conv2d_stage_input
+    makes, and its output equals the plain forward's."""
+    case = make_case(N=2, inC=64, outC=64, H=12, W=14, offset_scale=2.0, mask_kind="sigmoid")
+    d = {k: (v.cuda().to(H16[dt]) if isinstance(v, torch.Tensor) else v)
+         for k, v in case.items()}
+    x = d["x"]
+    if layout == "channels_last":
+        x = x.contiguous(memory_format=torch.channels_last)
+    ops = _ops()
+    args = (1, 1, 1, 1, 1, 1, 1, 1)
+    out, staged = ops.deform_conv2d_forward_staging(x, d["w"], d["off"], d["m"], d["b"], *args,
+                                                    MATH_TF32)
+    ref = ops.deform_conv2d_forward(x, d["w"], d["off"], d["m"], d["b"], *args, MATH_TF32)
+    assert torch.equal(out, ref)
+    assert staged.dtype == H16[dt] and staged.numel() == 2 * 12 * 14 * 64 + 64
+    assert torch.equal(staged, ops.deform_conv2d_stage_input(x))
+    # the backward on the staging copy gives the unstaged gradients (up to
+    # the order of the fp32 reductions, then one 16-bit rounding)
+    ga = ops.deform_conv2d_backward(d["go"], x, d["w"], d["off"], d["m"], d["b"], *args,
+                                    MATH_TF32)
+    gb = ops.deform_conv2d_backward(d["go"], x, d["w"], d["off"], d["m"], d["b"], *args,
+                                    MATH_TF32, staged)
+    torch.cuda.synchronize()
+    for a, b in zip(ga, gb):
+        a, b = a.float().cpu().numpy(), b.float().cpu().numpy()
+        scale = max(1.0, float(np.abs(a).max()))
+        np.testing.assert_allclose(b, a, rtol=2e-2, atol=1e-2 * scale)
+
+
+@pytest.mark.parametrize("dt", sorted(H16))
+def test_h16_training_step_stages_its_input_once(cuda_device, dt):
+    case = make_case(N=2, inC=64, outC=64, H=12, W=14, offset_scale=2.0)
+    leaves = {k: case[k].cuda().to(H16[dt]).requires_grad_(True)
+              for k in ("x", "w", "b", "off", "m")}
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out = deform_conv2d_ex(leaves["x"], leaves["off"], leaves["w"], leaves["b"],
+                               case["stride"], case["padding"], case["dilation"], leaves["m"],
+                               flags=MATH_TF32)
+        out.backward(case["go"].cuda().to(H16[dt]))
+        torch.cuda.synchronize()
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    tag = "bf16" if dt == "bf16" else "f16"
+    assert f"fwd_tc_{tag}" in stats and f"bwd_fused_tc_{tag}" in stats, sorted(stats)
+    assert stats["nchw_to_nhwc"][0] == 1, stats  # staged once, for both passes
+    assert all(leaves[k].grad is not None and leaves[k].grad.dtype == H16[dt] for k in leaves)
+
+
+def test_h16_uncovered_shape_is_not_staged(cuda_device):
+    # 48 channels: not a multiple of 64, so the 16-bit calls take the upcast
+    # route, which takes no staging copy; the training step still runs
+    case = make_case(N=1, inC=48, outC=32, H=8, W=9, offset_scale=2.0)
+    leaves = {k: case[k].cuda().to(torch.bfloat16).requires_grad_(True)
+              for k in ("x", "w", "b", "off", "m")}
+    out = deform_conv2d_ex(leaves["x"], leaves["off"], leaves["w"], leaves["b"],
+                           case["stride"], case["padding"], case["dilation"], leaves["m"],
+                           flags=MATH_TF32)
+    out.backward(case["go"].cuda().to(torch.bfloat16))
+    torch.cuda.synchronize()
+    assert all(leaves[k].grad is not None for k in leaves)
+    ops = _ops()
+    args = (1, 1, 1, 1, 1, 1, 1, 1)
+    d = {k: leaves[k].detach() for k in leaves}
+    staged = ops.deform_conv2d_stage_input(d["x"])
+    with pytest.raises(RuntimeError, match="staging copy"):
+        ops.deform_conv2d_forward(d["x"], d["w"], d["off"], d["m"], d["b"], *args, MATH_TF32,
+                                  staged)
