@@ -608,7 +608,6 @@ def run_ours(args, wl):
     traffic = load_traffic().get(f"{args.workload}:{args.math}:{dom}")
     roof["traffic"] = traffic["bytes_per_launch"] if traffic else None
     roof["binding"] = binding_roofline(traffic, avg_ms, l2_peaks, gather_bytes(dom, wl))
-    roof["l2_peaks_gbs"] = l2_peaks
     work = algorithmic_work(wl)
     step_roof_ms = work["flops"] / ((peak_tf32_used if args.math != "fp32" else peak_fp32) * 1e12) * 1e3
     roof["step_roofline_ms"] = round(max(step_roof_ms, work["bytes"] / (peaks.get("hbm_gbs", 6650.0) * 1e9) * 1e3), 4)
