@@ -86,6 +86,73 @@ def allreduce_grads(params: Iterable[torch.nn.Parameter], group=None,
             g /= world
 
 
+class GradAllReduce:
+    """Sums `params`' gradients across the group as soon as the backward has
+    produced them, the way a data-parallel wrapper does: a hook on each
+    parameter (``register_post_accumulate_grad_hook``) counts the gradients
+    accumulated in this backward, and when the last of them is in, one
+    asynchronous collective (one coalesced NCCL group; gloo: back-to-back
+    async all-reduces) starts on them while autograd goes on with the layers
+    before this one.  ``wait()`` -- before the optimizer step -- blocks until
+    it is done (with ``average``, divides by the world size) and re-arms the
+    hooks for the next step.  Every rank must run the same backward, so the
+    collectives match; a parameter that got no gradient in a step has none
+    reduced (call ``wait()`` on every rank all the same).
+
+        sync = GradAllReduce(module.parameters())
+        loss.backward()
+        sync.wait()
+        opt.step()
+    """
+
+    def __init__(self, params: Iterable[torch.nn.Parameter], group=None,
+                 average: bool = False):
+        self.params = [p for p in params if p.requires_grad]
+        self.group = group
+        self.average = average
+        self._ready: List[torch.nn.Parameter] = []
+        self._works = []
+        self._handles = [p.register_post_accumulate_grad_hook(self._on_grad)
+                         for p in self.params]
+
+    def _on_grad(self, p: torch.nn.Parameter) -> None:
+        self._ready.append(p)
+        if len(self._ready) == len(self.params):
+            self._launch()
+
+    def _launch(self) -> None:
+        grads = [p.grad for p in self._ready]
+        if dist.get_world_size(self.group) == 1:
+            return
+        if dist.get_backend(self.group) == "nccl":
+            with dist._coalescing_manager(group=self.group, device=grads[0].device,
+                                          async_ops=True) as cm:
+                for g in grads:
+                    dist.all_reduce(g, group=self.group)
+            self._works = [cm]
+        else:
+            self._works = [dist.all_reduce(g, group=self.group, async_op=True) for g in grads]
+
+    def wait(self) -> None:
+        """Waits for this step's collective (launching it for the gradients
+        that did arrive, if not all parameters got one) and re-arms."""
+        if self._ready and not self._works and len(self._ready) < len(self.params):
+            self._launch()
+        for w in self._works:
+            w.wait()
+        if self.average and self._ready:
+            world = dist.get_world_size(self.group)
+            for p in self._ready:
+                p.grad /= world
+        self._ready, self._works = [], []
+
+    def remove(self) -> None:
+        """Detaches the hooks."""
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+
+
 # ---------------------------------------------------------------------------
 # Row slabs: more ranks than images
 # ---------------------------------------------------------------------------

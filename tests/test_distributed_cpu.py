@@ -108,3 +108,52 @@ def test_failed_rank_surfaces_as_error_not_hang():
     _, out = _run(2, fail_rank=1)
     assert out[1][1] == "error" and "injected" in out[1][2]
     assert out[0][1] == "error"  # the survivor's collective fails on the timeout
+
+
+def _hook_worker(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        from pytorch_mps_deform_conv2d_b200.distributed import GradAllReduce
+        w = torch.nn.Parameter(torch.zeros(4, 3))
+        b = torch.nn.Parameter(torch.zeros(4))
+        sync = GradAllReduce([w, b], average=False)
+        got = []
+        for step in range(2):  # the hooks re-arm after wait()
+            w.grad = b.grad = None
+            xs = torch.full((4, 3), float(rank + 1 + 10 * step))
+            ys = torch.full((4,), float(2 * (rank + 1) + 10 * step))
+            ((w * xs).sum() + (b * ys).sum()).backward()
+            sync.wait()
+            got.append((w.grad.clone().numpy(), b.grad.clone().numpy()))
+        sync.remove()
+        result_q.put((rank, "ok", got))
+    except Exception as e:
+        result_q.put((rank, "error", repr(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_grad_allreduce_hooks_sum_after_backward():
+    """GradAllReduce: the collective starts from the parameters' hooks once
+    both gradients are accumulated, and wait() leaves the summed gradients."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hook_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=120) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank, status, got in out:
+        assert status == "ok", got
+        for step, (gw, gb) in enumerate(got):
+            np.testing.assert_array_equal(gw, np.full((4, 3), 1 + 2 + 20 * step, np.float32))
+            np.testing.assert_array_equal(gb, np.full((4,), 2 + 4 + 20 * step, np.float32))
