@@ -62,9 +62,15 @@ def _stage_input_fake(input):
 
 
 def _forward_staging_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
-                          dilation_h, dilation_w, groups, deformable_groups, math=-1):
-    out = _forward_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
-                        dilation_h, dilation_w, groups, deformable_groups, math)
+                          dilation_h, dilation_w, groups, deformable_groups, math=-1,
+                          row_begin=-1):
+    if row_begin >= 0:  # a row window: offset holds its rows
+        out = _forward_rows_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
+                                 pad_w, dilation_h, dilation_w, groups, deformable_groups,
+                                 row_begin, math)
+    else:
+        out = _forward_fake(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
+                            dilation_h, dilation_w, groups, deformable_groups, math)
     return out, _stage_input_fake(input)
 
 
@@ -76,7 +82,7 @@ def _forward_rows_fake(input, weight, offset, mask, bias, stride_h, stride_w, pa
 
 def _backward_rows_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w,
                         pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups,
-                        row_begin, math=-1):
+                        row_begin, math=-1, staged=None):
     return _backward_fake(grad_output, input, weight, offset, mask, bias, stride_h, stride_w,
                           pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups, math)
 
@@ -149,6 +155,7 @@ def register() -> None:
     torch.library.register_autograd(q + "deform_conv2d_forward", _forward_backward,
                                     setup_context=_setup_context)
     torch.library.register_fake(q + "deform_conv2d_forward_rows")(_forward_rows_fake)
+    torch.library.register_fake(q + "deform_conv2d_rows")(_forward_rows_fake)
     torch.library.register_fake(q + "deform_conv2d_backward_rows")(_backward_rows_fake)
     torch.library.register_autograd(q + "deform_conv2d_forward_rows", _forward_rows_backward,
                                     setup_context=_setup_rows_context)

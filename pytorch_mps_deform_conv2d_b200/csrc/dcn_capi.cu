@@ -493,7 +493,7 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     void* tail = tail_bytes > 0 && usable >= ws.used + tail_bytes ? ws.base + ws.used : nullptr;
     Fork fk(stream, side_streams_pay(g) && !staged);
     DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, tail, fk.side(0)),
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
                 "tc_pack_weight");
     if (!staged) DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
     DCN_ORDER(fk.join(0), "join");
@@ -605,7 +605,7 @@ static int forward_h16(bool f16, const dcn_shape* s, const void* input, const vo
     // the weight pack (side stream) runs beside the input staging
     Fork fk(stream, side_streams_pay(g) && !staged);
     DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bf16(weight, wt, g, tail, fk.side(0)),
+    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bf16(weight, wt, g, fk.side(0)),
                 "tc_pack_weight");
     if (staged) {
       // nothing to stage

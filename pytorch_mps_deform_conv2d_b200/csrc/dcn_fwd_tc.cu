@@ -59,9 +59,6 @@ constexpr int EPI_WARPS = 4;
 constexpr int MMA_WARP = 4, TMA_WARP = 5, GATHER_WARP0 = 6;
 constexpr int THREADS = (GATHER_WARP0 + GATHER_WARPS) * 32;  // 704
 constexpr int A_STAGE = BM * 128;                            // 16 KB
-// Counters of a split last round: at most kTailCounts split tiles, in the
-// first kTailCountBytes of the forward's tail scratch.
-constexpr int kTailCounts = (int)(kTailCountBytes / sizeof(int));
 
 int tc_bn(const Geom& g) { return g.Og <= 256 ? g.Og : 256; }
 int tmem_cols_for(int bn) {
@@ -90,8 +87,8 @@ struct FwdCfg {
   static constexpr int KCH = H16 ? 64 : 32;  // channels of one tap per K step
 };
 // Barriers and flags after the stage ring: full, tfull, empty (one per stage),
-// acc_full, acc_empty (two), drain, epi_bar, then the tensor-memory address,
-// the epilogue's last-piece broadcast and the abort flag.
+// acc_full, acc_empty (two), drain, then the tensor-memory address and the
+// abort flag.
 constexpr int kBarrierBytes = 256;
 size_t smem_bytes(int bn, bool split) {
   const int parts = split ? 2 : 1, stages = split ? 2 : 4;
@@ -118,17 +115,15 @@ __device__ __forceinline__ Tile tile_of(int t, int mtiles, int ntiles_n, int bn)
 // steps, laid end to end, are cut into `ctas` equal ranges, one per CTA, so
 // every CTA runs about the same number of K steps.  A range covers the end of
 // one tile and the start of the next at most; each piece of a tile leaves its
-// partial sum in a slot (2 per CTA, [tn][BM] floats) and counts itself in
-// `count[tile - whole]` (zero before the launch); the CTA whose count comes
-// last adds the pieces in CTA order -- a fixed order, so the output does not
-// depend on which piece finishes last -- and writes the tile.  No CTA waits
-// for another.
+// partial sum in a slot (2 per CTA, [tn][BM] floats), and fwd_tail_sum_kernel,
+// launched after the forward, adds every split tile's pieces in CTA order --
+// a fixed order, so the output does not depend on which piece finishes first
+// -- with all of the GPU's threads on it.  No CTA waits for another.
 struct TailPlan {
   int whole;               // tiles handed out whole
   int ctas;                // CTAs sharing the split tiles (0: no split)
   long long tail_steps;    // K steps of the split tiles
   float* part;             // partial slots
-  int* count;              // pieces finished per split tile
 };
 struct Work {
   int t;       // tile
@@ -243,10 +238,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint64_t* epi_bar = drain + 1;  // the epilogue warps' meeting point (split tiles)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
-  int* last_piece = reinterpret_cast<int*>(tmem_slot + 1);  // epilogue broadcast
-  int* abort_flag = last_piece + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   const tc::Watch watch{abort_flag, &g_tc_fwd_status, kStatusFwd, g.wait_limit};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -264,7 +257,6 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       tc::mbar_init(&acc_empty[a], EPI_WARPS);
     }
     tc::mbar_init(drain, 1);
-    tc::mbar_init(epi_bar, EPI_WARPS);
     *abort_flag = 0;
     tc::fence_mbar_init();
   }
@@ -492,12 +484,6 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
     // ------------------------------ epilogue ------------------------------
     int it = 0;
     const int r = warp * 32 + lane;
-    int nsync = 0;  // epi_bar phases passed
-    auto epi_sync = [&]() {
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(epi_bar);
-      return tc::wait(watch, epi_bar, (uint32_t)(nsync++ & 1));
-    };
     for_each_work(tp, steps, [&](const Work& w) {
       const Tile T = tile_of(w.t, mtiles, ntiles_n, tn);
       const int i = it++;
@@ -535,7 +521,8 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
         return true;
       }
       // a piece of a split tile: its partial into the slot (out channel
-      // major, so a warp's 32 rows are one 128-byte line) ...
+      // major, so a warp's 32 rows are one 128-byte line); fwd_tail_sum_kernel
+      // adds the pieces after the launch
       float* mine = tp.part + (size_t)w.slot * tn * BM;
       for (int cb = 0; cb < tn; cb += 8) {
         float vv[8];
@@ -547,38 +534,6 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
-      // ... made visible, then counted; the last piece to count sums them all
-      const int j = w.t - tp.whole;
-      const long long x0 = (long long)j * steps;
-      const int cfirst = tail_cta_of(tp, x0), clast = tail_cta_of(tp, x0 + steps - 1);
-      __threadfence();
-      // the four epilogue warps meet on an mbarrier (a bounded wait: a warp
-      // that gave up earlier does not leave the others stuck)
-      if (!epi_sync()) return false;
-      if (r == 0) *last_piece = atomicAdd(&tp.count[j], 1) == clast - cfirst;
-      if (!epi_sync()) return false;
-      if (*last_piece) {
-        __threadfence();
-        // CTAs after the first start their range inside this tile (their
-        // slot 0); the first one's range starts here or in an earlier tile
-        const bool first_starts_here =
-            (long long)cfirst * tp.tail_steps / tp.ctas == x0;
-        const float* p0 = tp.part + (size_t)(2 * cfirst + (first_starts_here ? 0 : 1)) * tn * BM;
-        if (valid) {
-          for (int cb = 0; cb < tn; cb += 8) {
-            float v[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) v[jj] = __ldcg(p0 + (size_t)(cb + jj) * BM + r);
-            for (int c = cfirst + 1; c <= clast; ++c) {
-              const float* pc = tp.part + (size_t)(2 * c) * tn * BM;
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) v[jj] += __ldcg(pc + (size_t)(cb + jj) * BM + r);
-            }
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) store(cb + jj, v[jj]);
-          }
-        }
-      }
       return true;
     });
   }
@@ -591,15 +546,44 @@ fwd_tc_kernel(Geom g, const __grid_constant__ CUtensorMap wmap, const void* __re
   }
 }
 
+// The split tiles' sums: element e of tail tile j (e = o * BM + r: out
+// channel o of the tile, pixel row r) is the sum of the tile's pieces' slots
+// in CTA order -- the first CTA's slot 0 when its range starts in this tile,
+// else its slot 1, then slot 0 of each later CTA -- plus the bias.
+template <int FMT>
+__global__ void __launch_bounds__(256) fwd_tail_sum_kernel(Geom g, TailPlan tp, int steps,
+                                                           int mtiles, int ntiles_n, int tn,
+                                                           const void* __restrict__ bias,
+                                                           void* __restrict__ out) {
+  const long long e = blockIdx.x * 256LL + threadIdx.x;
+  const long long per_tile = (long long)tn * BM;
+  const int j = (int)(e / per_tile);
+  const int rem = (int)(e - (long long)j * per_tile);
+  const int o = rem / BM, r = rem - o * BM;
+  const Tile T = tile_of(tp.whole + j, mtiles, ntiles_n, tn);
+  const long long q = T.q0 + r;
+  if (j >= (int)(tp.tail_steps / steps) || q >= g.NP) return;
+  const long long x0 = (long long)j * steps;
+  const int cfirst = tail_cta_of(tp, x0), clast = tail_cta_of(tp, x0 + steps - 1);
+  const bool first_starts_here = (long long)cfirst * tp.tail_steps / tp.ctas == x0;
+  float v = __ldcg(tp.part + (size_t)(2 * cfirst + (first_starts_here ? 0 : 1)) * per_tile + rem);
+  for (int c = cfirst + 1; c <= clast; ++c) v += __ldcg(tp.part + (size_t)(2 * c) * per_tile + rem);
+  const int n = (int)(q / g.P);
+  const int p = (int)(q - (long long)n * g.P);
+  const int oc = T.gi * g.Og + T.o0 + o;
+  const long long at = ((long long)n * g.outC + oc) * g.P + p;
+  const float y = v + (g.use_bias ? ld_io<FMT>(bias, oc) : 0.f);
+  if constexpr (FMT == kFmtF32) static_cast<float*>(out)[at] = y;
+  else static_cast<unsigned short*>(out)[at] = to_h16<FMT>(y);
+}
+
 // Packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = tf32(W[g*Og+o][c][k]);
 // with `split`, rows outC .. 2*outC-1 hold the low parts tf32(W - hi).  One
 // block per out channel: the (Cg x kk) row is read through L1 and written
 // tap-major with coalesced stores.
 __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __restrict__ w,
                                                              float* __restrict__ wt, Geom g,
-                                                             int split, int* __restrict__ zero) {
-  if (zero != nullptr && blockIdx.x == 0)  // the forward's split-tile counters
-    for (int i = threadIdx.x; i < kTailCounts; i += blockDim.x) zero[i] = 0;
+                                                             int split) {
   const int Kpad = g.kk * g.Cg;
   const long long oc = blockIdx.x;
   const float* src = w + oc * Kpad;
@@ -617,10 +601,7 @@ __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __rest
 // 16-bit packed B operand: wt[(g*Og + o) * Kpad + k*Cg + c] = W[g*Og+o][c][k]
 // (bf16 or fp16 words moved as they are, no rounding).
 __global__ void __launch_bounds__(256) tc_pack_weight_bf16_kernel(
-    const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g,
-    int* __restrict__ zero) {
-  if (zero != nullptr && blockIdx.x == 0)  // the forward's split-tile counters
-    for (int i = threadIdx.x; i < kTailCounts; i += blockDim.x) zero[i] = 0;
+    const unsigned short* __restrict__ w, unsigned short* __restrict__ wt, Geom g) {
   const int Kpad = g.kk * g.Cg;
   const long long oc = blockIdx.x;
   const unsigned short* src = w + oc * Kpad;
@@ -653,7 +634,7 @@ int kstep_count(int mode, const Geom& g) {
 struct TailShape {
   int grid = 0, whole = 0, ctas = 0;
   long long tail_steps = 0;
-  size_t bytes = 0;  // scratch: counters + 2 slots a CTA
+  size_t bytes = 0;  // scratch: 2 partial-sum slots a CTA
 };
 TailShape plan_tail(long long ntiles, int steps, int tn, int num_sms) {
   TailShape p;
@@ -661,7 +642,7 @@ TailShape plan_tail(long long ntiles, int steps, int tn, int num_sms) {
   p.whole = (int)ntiles;
   if (steps < 8 || num_sms <= 0 || ntiles <= 0) return p;
   const long long whole = ntiles / num_sms * num_sms, tail = ntiles - whole;
-  if (tail == 0 || tail > num_sms / 2 || tail > kTailCounts) return p;
+  if (tail == 0 || tail > num_sms / 2) return p;
   const long long T = tail * steps;
   if (T >= (1LL << 30)) return p;
   const long long min_seg = steps / 4 > 2 ? steps / 4 : 2;
@@ -672,7 +653,7 @@ TailShape plan_tail(long long ntiles, int steps, int tn, int num_sms) {
   p.ctas = (int)ctas;
   p.tail_steps = T;
   p.grid = whole > 0 ? num_sms : (int)ctas;
-  p.bytes = kTailCountBytes + (size_t)2 * ctas * tn * BM * sizeof(float);
+  p.bytes = (size_t)2 * ctas * tn * BM * sizeof(float);
   return p;
 }
 
@@ -701,11 +682,20 @@ cudaError_t launch_fwd_mode(int mode, const Geom& g, const void* xt, const CUten
   tp.whole = ts.whole;
   tp.ctas = ts.ctas;
   tp.tail_steps = ts.tail_steps;
-  tp.count = static_cast<int*>(tail);
-  tp.part = ts.ctas > 0 ? reinterpret_cast<float*>(static_cast<char*>(tail) + kTailCountBytes)
-                        : nullptr;
+  tp.part = ts.ctas > 0 ? static_cast<float*>(tail) : nullptr;
   kern<<<ts.grid, THREADS, smem, stream>>>(g, wmap, xt, bn, wide ? 512 : tmem_cols_for(bn),
                                             mtiles, ntiles_n, tp, off, mask, bias, out);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || ts.ctas == 0) return e;
+  // the split tiles' pieces, added in CTA order, + bias, into the output
+  const long long elems = (ntiles - ts.whole) * (long long)tn * BM;
+  const long long blocks = (elems + 255) / 256;
+  if (blocks > (1LL << 31) - 1) return cudaErrorInvalidValue;
+  const int steps = kstep_count(mode, g);
+  auto sum = mode == kBF16 ? fwd_tail_sum_kernel<kFmtBF16>
+             : mode == kF16 ? fwd_tail_sum_kernel<kFmtF16>
+                            : fwd_tail_sum_kernel<kFmtF32>;
+  sum<<<(unsigned)blocks, 256, 0, stream>>>(g, tp, steps, mtiles, ntiles_n, tn, bias, out);
   return cudaGetLastError();
 }
 
@@ -743,10 +733,9 @@ size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms) {
 }
 
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
-                                  void* tail, cudaStream_t stream) {
+                                  cudaStream_t stream) {
   if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
-  tc_pack_weight_kernel<<<g.outC, 256, 0, stream>>>(w, wt, g, split ? 1 : 0,
-                                                    static_cast<int*>(tail));
+  tc_pack_weight_kernel<<<g.outC, 256, 0, stream>>>(w, wt, g, split ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -773,12 +762,11 @@ bool tc_fwd_bf16_supported(const Geom& g) {
 
 size_t tc_fwd_weight_bf16_bytes(const Geom& g) { return (size_t)g.outC * g.kk * g.Cg * 2; }
 
-cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g, void* tail,
+cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
                                        cudaStream_t stream) {
   if ((long long)g.outC * g.kk * g.Cg == 0) return cudaSuccess;
   tc_pack_weight_bf16_kernel<<<g.outC, 256, 0, stream>>>(
-      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wt), g,
-      static_cast<int*>(tail));
+      static_cast<const unsigned short*>(w), static_cast<unsigned short*>(wt), g);
   return cudaGetLastError();
 }
 

@@ -28,15 +28,12 @@ bool tc_fwd_supported(const Geom& g);
 size_t tc_fwd_weight_bytes(const Geom& g, bool split);
 // Scratch ("tail") with which the tensor-core forward splits a short last
 // round of tiles over all SMs (0 when this shape has none on `num_sms` SMs;
-// `h16`: the 16-bit forward).  Its first kTailCountBytes must be zero when
-// the forward starts: the weight pack kernels below clear them when given the
-// same pointer.  Without the scratch the forward runs whole tiles only.
-constexpr size_t kTailCountBytes = 4096;
+// `h16`: the 16-bit forward): the pieces' partial sums, which a second
+// launch adds.  Without the scratch the forward runs whole tiles only.
 size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms);
-// weight (outC, Cg, kh, kw) -> packed tensor-core B operand; `tail` (NULL or
-// the forward's tail scratch) has its counters cleared on the way.
+// weight (outC, Cg, kh, kw) -> packed tensor-core B operand.
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
-                                  void* tail, cudaStream_t stream);
+                                  cudaStream_t stream);
 // Forward on tcgen05: implicit GEMM whose A tiles are gathered (bilinear
 // deformable sampling) by producer warps straight into swizzled shared memory.
 // `split`: 3xTF32 (fp32-level accuracy).  `tail` / `tail_bytes`: the scratch
@@ -53,7 +50,7 @@ cudaError_t launch_fwd_tc(const Geom& g, const float* xt, const float* wt,
 // (tc_fwd_weight_bf16_bytes).
 bool tc_fwd_bf16_supported(const Geom& g);
 size_t tc_fwd_weight_bf16_bytes(const Geom& g);
-cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g, void* tail,
+cudaError_t launch_tc_pack_weight_bf16(const void* w, void* wt, const Geom& g,
                                        cudaStream_t stream);
 cudaError_t launch_fwd_tc_bf16(const Geom& g, const void* xt, const void* wt, const void* off,
                                const void* mask, const void* bias, void* out, bool f16,

@@ -236,15 +236,19 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   }
   const float* mp = use_mask ? msk.data_ptr<float>() : nullptr;
   const float* bp = b.defined() ? b.data_ptr<float>() : nullptr;
+  const float* xs = staged_ptr(staged, x, s);
   if (row_begin >= 0) {
-    const size_t wsr = dcn_forward_rows_workspace_size(&s, out_h, flags);
+    const uint32_t rflags =
+        flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);
+    const size_t wsr = dcn_forward_rows_workspace_size(&s, out_h, rflags);
     auto ws = at::empty({(int64_t)std::max<size_t>(wsr, 1)}, x.options().dtype(at::kByte));
-    check_rc(dcn_forward_rows(&s, row_begin, out_h, x.data_ptr<float>(), w.data_ptr<float>(),
-                              off.data_ptr<float>(), mp, bp, out.data_ptr<float>(), flags,
-                              ws.data_ptr(), wsr, stream.stream()));
+    check_rc(dcn_forward_rows(&s, row_begin, out_h, xs ? xs : x.data_ptr<float>(),
+                              w.data_ptr<float>(), off.data_ptr<float>(), mp, bp,
+                              out.data_ptr<float>(), rflags, ws.data_ptr(), wsr, stream.stream()));
+    if (keep_staged != nullptr)
+      *keep_staged = kept_staging(ws, dcn_staged_input_size(&s), at::kFloat);
     return out;
   }
-  const float* xs = staged_ptr(staged, x, s);
   const uint32_t fflags =
       flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);
   const size_t ws_bytes = dcn_forward_workspace_size(&s, fflags);
@@ -327,11 +331,12 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_staging(
     const at::Tensor& input, const at::Tensor& weight, const at::Tensor& offset,
     const at::Tensor& mask, const c10::optional<at::Tensor>& bias, int64_t stride_h,
     int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
-    int64_t groups, int64_t deformable_groups, int64_t math) {
+    int64_t groups, int64_t deformable_groups, int64_t math, int64_t row_begin) {
   TORCH_CHECK(input.dim() == 4 && input.numel() > 0,
               "deform_conv2d_forward_staging: input must be a non-empty 4-D tensor");
   const auto dt = input.scalar_type();
   if (dt == at::kBFloat16 || dt == at::kHalf) {
+    TORCH_CHECK(row_begin < 0, "deform_conv2d_forward_staging: row windows take float32 tensors");
     // the 16-bit forward keeps its staging copy on its tensor-core route;
     // elsewhere the copy is made on its own (and the backward's upcast route
     // does not take it)
@@ -346,8 +351,8 @@ std::tuple<at::Tensor, at::Tensor> deform_conv2d_forward_staging(
   }
   at::Tensor staged;
   auto out = forward_impl(input, weight, offset, mask, bias, stride_h, stride_w, pad_h, pad_w,
-                          dilation_h, dilation_w, groups, deformable_groups, -1, math,
-                          c10::nullopt, &staged);
+                          dilation_h, dilation_w, groups, deformable_groups,
+                          row_begin >= 0 ? row_begin : -1, math, c10::nullopt, &staged);
   if (!staged.defined()) staged = deform_conv2d_stage_input(input);  // no output pixels
   return std::make_tuple(out, staged);
 }
@@ -457,7 +462,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
-  const float* xs = row_begin >= 0 ? nullptr : staged_ptr(staged, x, s);
+  const float* xs = staged_ptr(staged, x, s);
   const uint32_t flags = resolve_flags(math) | (nhwc ? DCN_INPUT_NHWC : 0u) |
                          (xs ? DCN_INPUT_STAGED : 0u);
   const size_t ws_bytes = row_begin >= 0 ? dcn_backward_rows_workspace_size(&s, out_h, flags)
@@ -472,7 +477,8 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   float* gb = use_bias ? ptr(grad_bias) : nullptr;
   const float* mp = use_mask ? cptr(msk) : nullptr;
   if (row_begin >= 0)
-    check_rc(dcn_backward_rows(&s, row_begin, out_h, cptr(go), cptr(x), cptr(w), cptr(off), mp,
+    check_rc(dcn_backward_rows(&s, row_begin, out_h, cptr(go), xs ? xs : cptr(x), cptr(w),
+                               cptr(off), mp,
                                ptr(grad_input), ptr(grad_offset), gm, ptr(grad_weight), gb, flags,
                                ws.data_ptr(), ws_bytes, stream.stream()));
   else
@@ -499,10 +505,11 @@ Grads deform_conv2d_backward_rows(const at::Tensor& grad_output, const at::Tenso
                                   int64_t stride_h, int64_t stride_w, int64_t pad_h,
                                   int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
                                   int64_t groups, int64_t deformable_groups, int64_t row_begin,
-                                  int64_t math) {
+                                  int64_t math, const c10::optional<at::Tensor>& staged) {
   TORCH_CHECK(row_begin >= 0, "deform_conv2d_backward_rows: row_begin must be >= 0");
   return backward_impl(grad_output, input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
-                       pad_w, dilation_h, dilation_w, groups, deformable_groups, row_begin, math);
+                       pad_w, dilation_h, dilation_w, groups, deformable_groups, row_begin, math,
+                       staged);
 }
 
 at::Tensor deformable_col2im(const at::Tensor& columns, const at::Tensor& offset,
@@ -643,7 +650,7 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
             .typed<std::tuple<at::Tensor, at::Tensor>(
                 const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                 const c10::optional<at::Tensor>&, int64_t, int64_t, int64_t, int64_t, int64_t,
-                int64_t, int64_t, int64_t, int64_t)>();
+                int64_t, int64_t, int64_t, int64_t, int64_t)>();
     const bool has_bias = bias.defined() && bias.numel() > 0;
     c10::optional<at::Tensor> b;
     if (has_bias) b = bias;
@@ -663,7 +670,7 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
       if (stage_once) {
         std::tie(out, staged) =
             fwd_staging.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
-                             dilation_h, dilation_w, groups, deformable_groups, math);
+                             dilation_h, dilation_w, groups, deformable_groups, math, -1);
       } else {
         out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
                       dilation_h, dilation_w, groups, deformable_groups, math, c10::nullopt);
@@ -707,6 +714,111 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
             at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor()};
   }
 };
+
+// The row-window operator's C++ autograd node: output rows [row_begin,
+// row_begin + offset.size(2)) of a replicated input, their gradients by the
+// row-window backward (no Python frame in either pass).
+class DeformConv2dRowsFn : public torch::autograd::Function<DeformConv2dRowsFn> {
+ public:
+  static at::Tensor forward(torch::autograd::AutogradContext* ctx, const at::Tensor& input,
+                            const at::Tensor& weight, const at::Tensor& offset,
+                            const at::Tensor& mask, const at::Tensor& bias, int64_t stride_h,
+                            int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t dilation_h,
+                            int64_t dilation_w, int64_t groups, int64_t deformable_groups,
+                            int64_t row_begin, int64_t math) {
+    static auto op =
+        c10::Dispatcher::singleton()
+            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_forward_rows", "")
+            .typed<at::Tensor(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                              const at::Tensor&, const c10::optional<at::Tensor>&, int64_t,
+                              int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                              int64_t, int64_t)>();
+    static auto fwd_staging =
+        c10::Dispatcher::singleton()
+            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_forward_staging", "")
+            .typed<std::tuple<at::Tensor, at::Tensor>(
+                const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                const c10::optional<at::Tensor>&, int64_t, int64_t, int64_t, int64_t, int64_t,
+                int64_t, int64_t, int64_t, int64_t, int64_t)>();
+    const bool has_bias = bias.defined() && bias.numel() > 0;
+    c10::optional<at::Tensor> b;
+    if (has_bias) b = bias;
+    at::Tensor out, staged;
+    {
+      at::AutoDispatchBelowADInplaceOrView below;
+      // a float32 input is staged inside the forward and kept for the backward
+      if (input.scalar_type() == at::kFloat && input.dim() == 4 && input.numel() > 0)
+        std::tie(out, staged) =
+            fwd_staging.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
+                             dilation_h, dilation_w, groups, deformable_groups, math, row_begin);
+      else
+        out = op.call(input, weight, offset, mask, b, stride_h, stride_w, pad_h, pad_w,
+                      dilation_h, dilation_w, groups, deformable_groups, row_begin, math);
+    }
+    if (staged.defined()) ctx->saved_data["staged"] = staged;
+    ctx->save_for_backward({input, weight, offset, mask, bias});
+    ctx->saved_data["ints"] = std::vector<int64_t>{stride_h,   stride_w,   pad_h,
+                                                   pad_w,      dilation_h, dilation_w,
+                                                   groups,     deformable_groups, row_begin,
+                                                   math};
+    ctx->saved_data["has_bias"] = has_bias;
+    return out;
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    static auto op =
+        c10::Dispatcher::singleton()
+            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_backward_rows", "")
+            .typed<Grads(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                         const at::Tensor&, const at::Tensor&, const c10::optional<at::Tensor>&,
+                         int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                         int64_t, int64_t, const c10::optional<at::Tensor>&)>();
+    const auto saved = ctx->get_saved_variables();
+    const auto v = ctx->saved_data["ints"].toIntVector();
+    const bool has_bias = ctx->saved_data["has_bias"].toBool();
+    const at::Tensor& mask = saved[3];
+    c10::optional<at::Tensor> b;
+    if (has_bias) b = saved[4];
+    c10::optional<at::Tensor> st;
+    if (ctx->saved_data.count("staged")) st = ctx->saved_data["staged"].toTensor();
+    auto r = op.call(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0], v[1],
+                     v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], st);
+    const bool has_mask = mask.numel() > 0;
+    return {std::get<0>(r),
+            std::get<3>(r),
+            std::get<1>(r),
+            has_mask ? std::get<2>(r) : at::Tensor(),
+            has_bias ? std::get<4>(r) : at::Tensor(),
+            at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(),
+            at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor()};
+  }
+};
+
+at::Tensor deform_conv2d_rows_autograd(const at::Tensor& input, const at::Tensor& weight,
+                                       const at::Tensor& offset, const at::Tensor& mask,
+                                       const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                       int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                       int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                       int64_t deformable_groups, int64_t row_begin,
+                                       int64_t math) {
+  return DeformConv2dRowsFn::apply(
+      input, weight, offset, mask,
+      bias.has_value() && bias->defined() ? *bias : input.new_empty({0}), stride_h, stride_w,
+      pad_h, pad_w, dilation_h, dilation_w, groups, deformable_groups, row_begin, math);
+}
+
+// The row-window operator below autograd.
+at::Tensor deform_conv2d_rows_plain(const at::Tensor& input, const at::Tensor& weight,
+                                    const at::Tensor& offset, const at::Tensor& mask,
+                                    const c10::optional<at::Tensor>& bias, int64_t stride_h,
+                                    int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                    int64_t dilation_h, int64_t dilation_w, int64_t groups,
+                                    int64_t deformable_groups, int64_t row_begin, int64_t math) {
+  return deform_conv2d_forward_rows(input, weight, offset, mask, bias, stride_h, stride_w, pad_h,
+                                    pad_w, dilation_h, dilation_w, groups, deformable_groups,
+                                    row_begin, math);
+}
 
 at::Tensor deform_conv2d_autograd(const at::Tensor& input, const at::Tensor& weight,
                                   const at::Tensor& offset, const at::Tensor& mask,
@@ -752,7 +864,8 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
   m.def(
       "deform_conv2d_forward_staging(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
       "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
-      "int dilation_w, int groups, int deformable_groups, int math=-1) -> (Tensor, Tensor)");
+      "int dilation_w, int groups, int deformable_groups, int math=-1, int row_begin=-1) "
+      "-> (Tensor, Tensor)");
   // Row windows (no reference counterpart): offset / mask / output /
   // grad_output hold output rows [row_begin, row_begin + offset.size(2)).
   m.def(
@@ -763,16 +876,23 @@ TORCH_LIBRARY(deform_conv2d_b200, m) {
       "deform_conv2d_backward_rows(Tensor grad_output, Tensor input, Tensor weight, "
       "Tensor offset, Tensor mask, Tensor? bias, int stride_h, int stride_w, int pad_h, "
       "int pad_w, int dilation_h, int dilation_w, int groups, int deformable_groups, "
-      "int row_begin, int math=-1) -> (Tensor, Tensor, Tensor, Tensor, Tensor)");
+      "int row_begin, int math=-1, Tensor? staged=None) "
+      "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
   // The differentiable operator (forward + the C++ autograd node above).
   m.def(
       "deform_conv2d(Tensor input, Tensor weight, Tensor offset, Tensor mask, Tensor? bias, "
       "int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, int dilation_w, "
       "int groups, int deformable_groups, int math=-1) -> Tensor");
+  // Its row-window form (no reference counterpart).
+  m.def(
+      "deform_conv2d_rows(Tensor input, Tensor weight, Tensor offset, Tensor mask, "
+      "Tensor? bias, int stride_h, int stride_w, int pad_h, int pad_w, int dilation_h, "
+      "int dilation_w, int groups, int deformable_groups, int row_begin, int math=-1) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(deform_conv2d_b200, Autograd, m) {
   m.impl("deform_conv2d", TORCH_FN(deform_conv2d_autograd));
+  m.impl("deform_conv2d_rows", TORCH_FN(deform_conv2d_rows_autograd));
 }
 
 TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
@@ -785,4 +905,5 @@ TORCH_LIBRARY_IMPL(deform_conv2d_b200, CUDA, m) {
   m.impl("deform_conv2d_stage_input", TORCH_FN(deform_conv2d_stage_input));
   m.impl("deform_conv2d_forward_staging", TORCH_FN(deform_conv2d_forward_staging));
   m.impl("deform_conv2d", TORCH_FN(deform_conv2d_plain));  // below autograd
+  m.impl("deform_conv2d_rows", TORCH_FN(deform_conv2d_rows_plain));
 }

@@ -241,6 +241,9 @@ def deform_conv2d_rows(input, offset, weight, bias=None, stride=(1, 1), padding=
     groups = input.shape[1] // weight.shape[1]
     deformable_groups = offset.shape[1] // (2 * kh * kw)
     m = mask if mask is not None else input.new_empty(0)
-    return _ops().deform_conv2d_forward_rows(
-        input, weight, offset, m, bias, stride[0], stride[1], padding[0], padding[1],
-        dilation[0], dilation[1], groups, deformable_groups, int(row_begin), _flags(flags))
+    # eager: the row operator whose autograd node is C++; traced: the
+    # operator with the registered autograd formula
+    op = (_ops().deform_conv2d_rows if not torch.compiler.is_compiling()
+          else _ops().deform_conv2d_forward_rows)
+    return op(input, weight, offset, m, bias, stride[0], stride[1], padding[0], padding[1],
+              dilation[0], dilation[1], groups, deformable_groups, int(row_begin), _flags(flags))

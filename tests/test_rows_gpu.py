@@ -85,3 +85,36 @@ def test_row_window_out_of_range_raises(cuda_device):
     off = case["off"].cuda()[:, :, 2:].contiguous()  # rows 2..5 of 6
     with pytest.raises(RuntimeError, match="outside the 6 output rows"):
         deform_conv2d_rows(x, off, w, None, 1, 1, 1, None, row_begin=3)
+
+
+def test_row_window_step_stages_its_input_once(cuda_device):
+    """The row operator's C++ autograd node stages the replicated input once,
+    inside its forward, and hands the copy to the row backward (the fused
+    tensor-core backward with its one-launch prologue), with the gradients
+    of the unstaged row operators."""
+    case = make_case(N=1, inC=64, outC=64, H=14, W=12, offset_scale=2.0, upstream="randn")
+    args = (case["stride"], case["padding"], case["dilation"])
+    rows = slice(4, 11)
+    off_r = case["off"][:, :, rows].contiguous()
+    m_r = case["m"][:, :, rows].contiguous()
+    go_r = case["go"][:, :, rows].contiguous().cuda()
+    x, w, b, off, m = (_leaf(t) for t in (case["x"], case["w"], case["b"], off_r, m_r))
+    _native.profiler_read()
+    _native.profiler_enable(True)
+    try:
+        out = deform_conv2d_rows(x, off, w, b, *args, m, row_begin=rows.start, flags=MATH_TF32)
+        out.backward(go_r)
+        torch.cuda.synchronize()
+    finally:
+        _native.profiler_enable(False)
+    stats = _native.profiler_read()
+    assert stats["nchw_to_nhwc"][0] == 1, stats
+    assert "bwd_prologue" in stats and "bwd_fused_tc" in stats, sorted(stats)
+    ops = _native.load_ops()
+    ints = (1, 1, 1, 1, 1, 1, 1, 1, rows.start, MATH_TF32)
+    ref = ops.deform_conv2d_backward_rows(go_r, x.detach(), w.detach(), off.detach(),
+                                          m.detach(), b.detach(), *ints)
+    got = (x.grad, off.grad, m.grad, w.grad, b.grad)
+    for a, r in zip(got, ref):
+        scale = max(1.0, float(r.abs().max()))
+        torch.testing.assert_close(a, r, rtol=1e-4, atol=1e-4 * scale)

@@ -82,9 +82,9 @@ def test_noalloc_matches_forward_two_calls_in_a_row(cuda_device):
 # Tensor-core forward through the built-in array: its TMA tensor map is built
 # over the array (the packed weight lives there, high and low TF32 parts in
 # 3xTF32), and 168 tiles of 128 pixels on 148 SMs leave a last round of 20
-# tiles, which the forward splits over the SMs with counters and partial sums
-# kept in the rest of the array.  Two calls in a row: the second one shows
-# that the counters start from zero again.
+# tiles, which the forward splits over the SMs with partial sums kept in the
+# rest of the array (a second launch adds them).  Two calls in a row: the
+# second one reuses the array's slots and gives the same bits.
 @pytest.mark.parametrize("mode", ["tf32", "3xtf32"])
 def test_noalloc_tensor_core_split_round_two_calls(cuda_device, mode):
     from pytorch_mps_deform_conv2d_b200.ops import MATH_3XTF32, MATH_TF32
