@@ -97,7 +97,10 @@ class GradAllReduce:
     it is done (with ``average``, divides by the world size) and re-arms the
     hooks for the next step.  Every rank must run the same backward, so the
     collectives match; a parameter that got no gradient in a step has none
-    reduced (call ``wait()`` on every rank all the same).
+    reduced (call ``wait()`` on every rank all the same).  One backward per
+    step: with gradients accumulated over several backward passes, the
+    collective would start after the first of them -- reduce with
+    :func:`allreduce_grads` after the last one instead.
 
         sync = GradAllReduce(module.parameters())
         loss.backward()
