@@ -155,6 +155,16 @@ bool h16_staging(const at::Tensor& input, const at::Tensor& weight, int64_t stri
   return dcn_h16_staging(&s, flags) == 1;
 }
 
+at::Tensor deform_conv2d_stage_input(const at::Tensor& input);
+
+// Whether a forward whose workspace is `ws_bytes` should keep its staging
+// copy (`staged_bytes`) in that workspace: the kept copy pins the whole
+// workspace until the backward, so not when the rest of it (packed weight,
+// a split round's partial sums) would hold much more than the copy itself.
+bool keep_in_workspace(size_t ws_bytes, size_t staged_bytes) {
+  return ws_bytes <= staged_bytes + staged_bytes / 8 + (size_t(1) << 20);
+}
+
 // The staging copy a forward with DCN_KEEP_STAGED left at the 256-byte
 // aligned start of its workspace `ws`: `bytes` bytes viewed as `dt`.
 at::Tensor kept_staging(const at::Tensor& ws, size_t bytes, at::ScalarType dt) {
@@ -221,6 +231,15 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   auto stream = at::cuda::getCurrentCUDAStream();
   if (h16) {
     const void* xs = staged_ptr16(staged, x, s);
+    if (keep_staged != nullptr) {
+      const size_t wsk = f16 ? dcn_forward_f16_workspace_size(&s, flags | DCN_KEEP_STAGED)
+                             : dcn_forward_bf16_workspace_size(&s, flags | DCN_KEEP_STAGED);
+      if (!keep_in_workspace(wsk, dcn_staged_input_size_h16(&s))) {
+        *keep_staged = deform_conv2d_stage_input(x);
+        xs = keep_staged->data_ptr();
+        keep_staged = nullptr;
+      }
+    }
     const uint32_t flags16 =
         flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);
     const size_t ws16 = f16 ? dcn_forward_f16_workspace_size(&s, flags16)
@@ -237,6 +256,18 @@ at::Tensor forward_impl(const at::Tensor& input, const at::Tensor& weight,
   const float* mp = use_mask ? msk.data_ptr<float>() : nullptr;
   const float* bp = b.defined() ? b.data_ptr<float>() : nullptr;
   const float* xs = staged_ptr(staged, x, s);
+  if (keep_staged != nullptr) {
+    // stage on its own (then run staged) when the workspace would pin more
+    // than the copy
+    const size_t wsk = row_begin >= 0
+                           ? dcn_forward_rows_workspace_size(&s, out_h, flags | DCN_KEEP_STAGED)
+                           : dcn_forward_workspace_size(&s, flags | DCN_KEEP_STAGED);
+    if (!keep_in_workspace(wsk, dcn_staged_input_size(&s))) {
+      *keep_staged = deform_conv2d_stage_input(x);
+      xs = keep_staged->data_ptr<float>();
+      keep_staged = nullptr;
+    }
+  }
   if (row_begin >= 0) {
     const uint32_t rflags =
         flags | (xs ? DCN_INPUT_STAGED : 0u) | (keep_staged != nullptr ? DCN_KEEP_STAGED : 0u);

@@ -192,3 +192,25 @@ def test_h16_uncovered_shape_is_not_staged(cuda_device):
     with pytest.raises(RuntimeError, match="staging copy"):
         ops.deform_conv2d_forward(d["x"], d["w"], d["off"], d["m"], d["b"], *args, MATH_TF32,
                                   staged)
+
+
+@pytest.mark.parametrize("H,W,kept", [(119, 256, True), (60, 128, False)])
+def test_staging_copy_does_not_pin_a_large_workspace(cuda_device, H, W, kept):
+    """The forward keeps its staging copy in its workspace only when the rest
+    of that workspace is small: 238 tiles of 128 pixels (no split round) keep
+    it there; 60 tiles (a split round whose partial sums would be pinned with
+    it) stage into a buffer of their own.  Either way the copy is the one
+    deform_conv2d_stage_input makes."""
+    case = make_case(N=1, inC=32, outC=32, H=H, W=W, offset_scale=2.0, mask_kind="sigmoid")
+    d = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in case.items()}
+    ops = _ops()
+    args = (1, 1, 1, 1, 1, 1, 1, 1)
+    out, staged = ops.deform_conv2d_forward_staging(d["x"], d["w"], d["off"], d["m"], d["b"],
+                                                    *args, MATH_TF32)
+    nbytes = staged.numel() * 4
+    pinned = staged.untyped_storage().nbytes()
+    assert (pinned > nbytes) == kept, (pinned, nbytes)
+    assert pinned <= nbytes + nbytes // 8 + (1 << 20) + 512
+    assert torch.equal(staged, ops.deform_conv2d_stage_input(d["x"]))
+    ref = ops.deform_conv2d_forward(d["x"], d["w"], d["off"], d["m"], d["b"], *args, MATH_TF32)
+    assert torch.equal(out, ref)
