@@ -110,18 +110,22 @@ def test_failed_rank_surfaces_as_error_not_hang():
     assert out[0][1] == "error"  # the survivor's collective fails on the timeout
 
 
-def _hook_worker(rank, world, port, result_q):
+def _hook_worker(rank, world, port, result_q, bucketed=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=10))
     try:
-        from pytorch_mps_deform_conv2d_b200.distributed import GradAllReduce
+        from pytorch_mps_deform_conv2d_b200.distributed import GradAllReduce, GradBucket
         w = torch.nn.Parameter(torch.zeros(4, 3))
         b = torch.nn.Parameter(torch.zeros(4))
+        bucket = GradBucket([w, b]) if bucketed else None  # one flat collective
         sync = GradAllReduce([w, b], average=False)
         got = []
         for step in range(2):  # the hooks re-arm after wait()
-            w.grad = b.grad = None
+            if bucket is not None:
+                bucket.zero_()
+            else:
+                w.grad = b.grad = None
             xs = torch.full((4, 3), float(rank + 1 + 10 * step))
             ys = torch.full((4,), float(2 * (rank + 1) + 10 * step))
             ((w * xs).sum() + (b * ys).sum()).backward()
@@ -138,13 +142,16 @@ def _hook_worker(rank, world, port, result_q):
             pass
 
 
-def test_grad_allreduce_hooks_sum_after_backward():
+@pytest.mark.parametrize("bucketed", [False, True], ids=["separate", "bucket"])
+def test_grad_allreduce_hooks_sum_after_backward(bucketed):
     """GradAllReduce: the collective starts from the parameters' hooks once
-    both gradients are accumulated, and wait() leaves the summed gradients."""
+    both gradients are accumulated, and wait() leaves the summed gradients
+    (separate gradients, or a GradBucket's views reduced as one buffer)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_hook_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_hook_worker, args=(r, 2, port, q, bucketed))
+             for r in range(2)]
     for p in procs:
         p.start()
     out = sorted([q.get(timeout=120) for _ in procs], key=lambda r: r[0])
@@ -157,3 +164,50 @@ def test_grad_allreduce_hooks_sum_after_backward():
         for step, (gw, gb) in enumerate(got):
             np.testing.assert_array_equal(gw, np.full((4, 3), 1 + 2 + 20 * step, np.float32))
             np.testing.assert_array_equal(gb, np.full((4,), 2 + 4 + 20 * step, np.float32))
+
+
+def _bucket_worker(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        from pytorch_mps_deform_conv2d_b200.distributed import GradBucket
+        w = torch.nn.Parameter(torch.zeros(4, 3))
+        b = torch.nn.Parameter(torch.zeros(4))
+        bucket = GradBucket([w, b])
+        got = []
+        for step in range(2):
+            bucket.zero_()
+            xs = torch.full((4, 3), float(rank + 1 + 10 * step))
+            ((w * xs).sum() + (b * (rank + 2)).sum()).backward()
+            # accumulated in place into the bucket's views
+            assert w.grad.data_ptr() == bucket.flat.data_ptr()
+            allreduce_grads([w, b])
+            got.append((w.grad.clone().numpy(), b.grad.clone().numpy()))
+        result_q.put((rank, "ok", got))
+    except Exception as e:
+        result_q.put((rank, "error", repr(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_grad_bucket_accumulates_in_place_and_reduces_once():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted([q.get(timeout=120) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    for rank, status, got in out:
+        assert status == "ok", got
+        for step, (gw, gb) in enumerate(got):
+            np.testing.assert_array_equal(gw, np.full((4, 3), 1 + 2 + 20 * step, np.float32))
+            np.testing.assert_array_equal(gb, np.full((4,), 2 + 3, np.float32))
