@@ -755,10 +755,10 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
   float* gxt = nhwc ? grad_input : ws.take((size_t)g.N * g.HW * g.C);
   // xt (+ its zero row) and the zeroed grad-input accumulator in one pass;
   // with a staged input only the accumulator is zeroed
-  auto stage_input = [&]() {
-    if (staged) return cudaMemsetAsync(gxt, 0, x_bytes, stream);
-    return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream)
-                : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stream);
+  auto stage_input = [&](cudaStream_t st) {
+    if (staged) return cudaMemsetAsync(gxt, 0, x_bytes, st);
+    return nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, st)
+                : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, st);
   };
   const char* stage_name = staged ? "memset" : (nhwc ? "copy_nhwc" : "nchw_to_nhwc");
   if (tc_bwd) {
@@ -772,26 +772,18 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     // then puts it in grad_weight's layout
     float* gwt = ws.take(w_bytes / sizeof(float));
     z.add(gwt, (long long)(w_bytes / sizeof(float)));
-    if (staged && use_fused_bwd(g, flags)) {
-      // the helpers in one launch on the caller's stream (no cross-stream
-      // waits): grad_out rows with grad_bias partial sums, the packed weight,
-      // the zeroed accumulators; then the fused kernel; then grad_input back
-      // to NCHW beside the grad_weight layout, which also sums grad_bias
-      float* gpart = ws.take(dcn::tc_bias_part_floats(g));
-      z.add(gxt, (long long)(x_bytes / sizeof(float)));
-      DCN_CUDA(dcn::launch_bwd_prologue(g, grad_output, go_r, bias_in_prep ? gpart : nullptr,
-                                        weight, wbt, z, stream),
-               "bwd_prologue");
+    Fork fk(stream, side_streams_pay(g));  // one per call: it holds the side streams' lock
+    // the fused kernel, then grad_input back to NCHW beside the grad_weight
+    // layout (which sums grad_bias from the prologue's partial sums, if any)
+    auto fused_rest = [&](const float* gpart, float* gb_out) -> int {
       DCN_CUDA(dcn::launch_bwd_fused_tc(g, go_r, wbt, xt, offset, mask, gxt, grad_offset,
                                         grad_mask, gwt, num_sms_current(), stream),
                "bwd_fused_tc");
-      float* gb_out = bias_in_prep ? grad_bias : nullptr;
-      if (nhwc) {
+      if (nhwc) {  // grad_input is complete: nothing to transpose
         DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream, gpart, gb_out),
                  "grad_weight_layout");
         return DCN_OK;
       }
-      Fork fk(stream, side_streams_pay(g));
       DCN_ORDER(fk.fork(), "fork");
       DCN_CUDA_ON(fk.side(0),
                   dcn::launch_weight_from_tap_major(gwt, grad_weight, g, fk.side(0), gpart,
@@ -800,24 +792,28 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
       DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
       DCN_ORDER(fk.join(0), "join");
       return DCN_OK;
+    };
+    if (staged && use_fused_bwd(g, flags)) {
+      // the helpers in one launch on the caller's stream (no cross-stream
+      // waits): grad_out rows with grad_bias partial sums, the packed weight,
+      // the zeroed accumulators
+      float* gpart = ws.take(dcn::tc_bias_part_floats(g));
+      z.add(gxt, (long long)(x_bytes / sizeof(float)));
+      DCN_CUDA(dcn::launch_bwd_prologue(g, grad_output, go_r, bias_in_prep ? gpart : nullptr,
+                                        weight, wbt, z, stream),
+               "bwd_prologue");
+      return fused_rest(gpart, bias_in_prep ? grad_bias : nullptr);
     }
     // The grad_out prep (after zeroing grad_bias, which it sums into) stays
     // on the caller's stream, where it starts at once: it is the longest
     // helper.  The weight pack + the zeroing of the other accumulators (side
     // 0) and the input staging or the grad-input zeroing (side 1) run beside
     // it, behind the cross-stream wait.
-    Fork fk(stream, side_streams_pay(g));
     DCN_ORDER(fk.fork(), "fork");
     DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight_bwd(weight, wbt, g, split, fk.side(0)),
                 "tc_pack_weight_bwd");
     DCN_CUDA_ON(fk.side(0), dcn::launch_zero(z, fk.side(0)), "zero");
-    const cudaStream_t stage_stream = fk.side(1);
-    DCN_CUDA_ON(stage_stream,
-                staged ? cudaMemsetAsync(gxt, 0, x_bytes, stage_stream)
-                : nhwc ? dcn::launch_copy_nhwc(input, xt, g.N, g.C, g.HW, true, gxt, stage_stream)
-                       : dcn::launch_nchw_to_nhwc(input, xt, g.N, g.C, g.HW, true, gxt,
-                                                  stage_stream),
-                stage_name);
+    DCN_CUDA_ON(fk.side(1), stage_input(fk.side(1)), stage_name);
     if (bias_in_prep)
       DCN_CUDA(cudaMemsetAsync(grad_bias, 0, (size_t)g.outC * sizeof(float), stream), "memset");
     DCN_CUDA(dcn::launch_tc_prep_go(g, grad_output, go_r, bias_in_prep ? grad_bias : nullptr,
@@ -825,23 +821,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
              "tc_prep_go");
     DCN_ORDER(fk.join(0), "join");
     DCN_ORDER(fk.join(1), "join");
-    if (use_fused_bwd(g, flags)) {
-      DCN_CUDA(dcn::launch_bwd_fused_tc(g, go_r, wbt, xt, offset, mask, gxt, grad_offset,
-                                        grad_mask, gwt, num_sms_current(), stream),
-               "bwd_fused_tc");
-      if (nhwc) {
-        DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream),
-                 "grad_weight_layout");
-        return DCN_OK;
-      }
-      // grad_input back to NCHW, and the grad_weight layout beside it (side 0)
-      DCN_ORDER(fk.fork(), "fork");
-      DCN_CUDA_ON(fk.side(0), dcn::launch_weight_from_tap_major(gwt, grad_weight, g, fk.side(0)),
-                  "grad_weight_layout");
-      DCN_CUDA(dcn::launch_nhwc_to_nchw(gxt, grad_input, g.N, g.C, g.HW, stream), "nhwc_to_nchw");
-      DCN_ORDER(fk.join(0), "join");
-      return DCN_OK;
-    }
+    if (use_fused_bwd(g, flags)) return fused_rest(nullptr, nullptr);
     DCN_CUDA(dcn::launch_bwd_data_tc(g, go_r, split, wbt, xt, offset, mask, gxt, grad_offset,
                                      grad_mask, col, stream),
              "bwd_data_tc");
@@ -881,7 +861,7 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
     DCN_ORDER(fk.join(0), "join");
     return DCN_OK;
   }
-  DCN_CUDA(stage_input(), stage_name);
+  DCN_CUDA(stage_input(stream), stage_name);
   if (dcn::dgroup_supported(g) && !(flags & (DCN_ALGO_SIMT_GEMM | DCN_ALGO_SIMT_DIRECT))) {
     DCN_CUDA(dcn::launch_bwd_dgroup(g, grad_output, weight, xt, offset, mask, gxt, grad_offset,
                                     grad_mask, grad_weight, stream),
