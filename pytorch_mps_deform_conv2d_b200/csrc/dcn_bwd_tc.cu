@@ -28,6 +28,7 @@
 #include "dcn_launch.h"
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
+#include "dcn_transpose.cuh"
 #include "dcn_tma.h"
 
 namespace dcn {
@@ -2171,11 +2172,14 @@ cudaError_t launch_bwd_weight_tc(const Geom& g, const float* go_r, const float* 
 // floats.
 // With `gpart`: also grad_bias[o] = the sum of the prologue's partial sums
 // of out channel o, in a fixed order.
-__global__ void __launch_bounds__(256) weight_from_tap_major_kernel(
-    const float* __restrict__ gwt, float* __restrict__ gw, int Cg, int kk, long long total,
-    const float* __restrict__ gpart, float* __restrict__ gb, int N, int outC, int pspans) {
-  const long long stride = (long long)gridDim.x * 256;
-  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += stride) {
+// Block `bb` of `nb` blocks of 256 threads: its share of the (o, c) rows of
+// the layout change and of the grad_bias sums.
+__device__ __forceinline__ void weight_from_tap_major_blocks(
+    long long bb, long long nb, const float* __restrict__ gwt, float* __restrict__ gw, int Cg,
+    int kk, long long total, const float* __restrict__ gpart, float* __restrict__ gb, int N,
+    int outC, int pspans) {
+  const long long stride = nb * 256;
+  for (long long i = bb * 256 + threadIdx.x; i < total; i += stride) {
     const long long o = i / Cg;
     const int c = (int)(i - o * Cg);
     const float* src = gwt + o * Cg * kk + c;
@@ -2183,13 +2187,41 @@ __global__ void __launch_bounds__(256) weight_from_tap_major_kernel(
     for (int k = 0; k < kk; ++k) dst[k] = __ldg(src + (long long)k * Cg);
   }
   if (gpart == nullptr) return;
-  for (long long o = blockIdx.x * 256LL + threadIdx.x; o < outC; o += stride) {
+  for (long long o = bb * 256 + threadIdx.x; o < outC; o += stride) {
     float t = 0.f;
     for (int n = 0; n < N; ++n) {
       const float* q = gpart + ((long long)n * outC + o) * pspans;
       for (int sp = 0; sp < pspans; ++sp) t += __ldg(q + sp);
     }
     gb[o] = t;
+  }
+}
+__global__ void __launch_bounds__(256) weight_from_tap_major_kernel(
+    const float* __restrict__ gwt, float* __restrict__ gw, int Cg, int kk, long long total,
+    const float* __restrict__ gpart, float* __restrict__ gb, int N, int outC, int pspans) {
+  weight_from_tap_major_blocks(blockIdx.x, gridDim.x, gwt, gw, Cg, kk, total, gpart, gb, N,
+                               outC, pspans);
+}
+
+// The fused backward's last two jobs in one launch on the caller's stream:
+// blocks [0, tiles) transpose the NHWC grad-input accumulator gxt into
+// grad_input (NCHW, 64 x 64 tiles), the blocks after them lay out
+// grad_weight from its tap-major copy and sum grad_bias
+// (weight_from_tap_major_kernel's work).  One launch instead of a transpose
+// beside a side-stream layout kernel saves the fork, the join and a launch.
+__global__ void __launch_bounds__(256) bwd_finish_kernel(
+    const float* __restrict__ gxt, float* __restrict__ gx, int C, int HW, int tiles_x,
+    int per_img, int tiles, const float* __restrict__ gwt, float* __restrict__ gw, int Cg,
+    int kk, long long total, const float* __restrict__ gpart, float* __restrict__ gb, int N,
+    int outC, int pspans) {
+  __shared__ float tile[64][65];
+  const int b = blockIdx.x;
+  if (b < tiles) {
+    const int n = b / per_img, r = b - n * per_img;
+    transpose4_tile(gxt, gx, HW, C, n, r % tiles_x, r / tiles_x, tile, nullptr);
+  } else {
+    weight_from_tap_major_blocks(b - tiles, (long long)gridDim.x - tiles, gwt, gw, Cg, kk, total,
+                                 gpart, gb, N, outC, pspans);
   }
 }
 
@@ -2203,6 +2235,30 @@ cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom
   const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
   weight_from_tap_major_kernel<<<(int)blocks, 256, 0, stream>>>(
       gwt, gw, g.Cg, g.kk, total, gb != nullptr ? gpart : nullptr, gb, g.N, g.outC, pspans);
+  return cudaGetLastError();
+}
+
+bool bwd_finish_fits(const float* gxt, const float* gx, const Geom& g) {
+  return transpose4_fits(gxt, gx, g.HW, g.C) &&
+         transpose4_tiles(g.N, g.HW, g.C) + 148LL * 16 <= (1LL << 31) - 1;
+}
+
+cudaError_t launch_bwd_finish(const float* gxt, float* gx, const float* gwt, float* gw,
+                              const Geom& g, const float* gpart, float* gb, cudaStream_t stream) {
+  if (!bwd_finish_fits(gxt, gx, g)) return cudaErrorInvalidValue;
+  // gxt (N, HW, C) -> grad_input (N, C, HW): rows HW, columns C
+  const long long tiles = transpose4_tiles(g.N, g.HW, g.C);
+  const long long total = g.kk > 0 ? (long long)g.outC * g.Cg : 0;
+  long long wblocks = (std::max(total, gb != nullptr ? (long long)g.outC : 0LL) + 255) / 256;
+  if (wblocks > 148LL * 16) wblocks = 148LL * 16;
+  if (tiles + wblocks == 0) return cudaSuccess;
+  const int tiles_x = transpose4_tiles_x(g.C);
+  const int per_img = tiles_x * ((g.HW + 63) / 64);
+  const int Ppad = (g.P + 3) & ~3;
+  const int pspans = (Ppad + PG_SPAN - 1) / PG_SPAN;
+  bwd_finish_kernel<<<(unsigned)(tiles + wblocks), 256, 0, stream>>>(
+      gxt, gx, g.C, g.HW, tiles_x, per_img, (int)tiles, gwt, gw, g.Cg, g.kk, total,
+      gb != nullptr ? gpart : nullptr, gb, g.N, g.outC, pspans);
   return cudaGetLastError();
 }
 

@@ -491,12 +491,17 @@ static int forward_core(const dcn_shape* s, int64_t row0, int64_t rows, const fl
     const int sms = num_sms_current();
     const size_t tail_bytes = dcn::tc_fwd_tail_bytes(g, split, false, sms);
     void* tail = tail_bytes > 0 && usable >= ws.used + tail_bytes ? ws.base + ws.used : nullptr;
-    Fork fk(stream, side_streams_pay(g) && !staged);
-    DCN_ORDER(fk.fork(), "fork");
-    DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
-                "tc_pack_weight");
-    if (!staged) DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
-    DCN_ORDER(fk.join(0), "join");
+    if (!staged && !nhwc && dcn::fwd_prologue_fits(input, xt, g)) {
+      // the staging transpose and the weight pack in one launch
+      DCN_CUDA(dcn::launch_fwd_prologue(input, xt, weight, wt, g, split, stream), "fwd_prologue");
+    } else {
+      Fork fk(stream, side_streams_pay(g) && !staged);
+      DCN_ORDER(fk.fork(), "fork");
+      DCN_CUDA_ON(fk.side(0), dcn::launch_tc_pack_weight(weight, wt, g, split, fk.side(0)),
+                  "tc_pack_weight");
+      if (!staged) DCN_CUDA(stage_input(), nhwc ? "copy_nhwc" : "nchw_to_nhwc");
+      DCN_ORDER(fk.join(0), "join");
+    }
     DCN_CUDA(dcn::launch_fwd_tc(g, xt, wt, offset, mask, bias, output, split, tail,
                                 tail ? tail_bytes : 0, sms, stream),
              "fwd_tc");
@@ -782,6 +787,12 @@ static int backward_core(const dcn_shape* s, int64_t row0, int64_t rows,
       if (nhwc) {  // grad_input is complete: nothing to transpose
         DCN_CUDA(dcn::launch_weight_from_tap_major(gwt, grad_weight, g, stream, gpart, gb_out),
                  "grad_weight_layout");
+        return DCN_OK;
+      }
+      if (dcn::bwd_finish_fits(gxt, grad_input, g)) {  // both in one launch
+        DCN_CUDA(dcn::launch_bwd_finish(gxt, grad_input, gwt, grad_weight, g, gpart, gb_out,
+                                        stream),
+                 "bwd_finish");
         return DCN_OK;
       }
       DCN_ORDER(fk.fork(), "fork");

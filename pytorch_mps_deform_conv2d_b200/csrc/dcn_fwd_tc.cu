@@ -44,6 +44,7 @@
 #include "dcn_tc.h"
 #include "dcn_tc_common.cuh"
 #include "dcn_tma.h"
+#include "dcn_transpose.cuh"
 
 namespace dcn {
 
@@ -581,11 +582,10 @@ __global__ void __launch_bounds__(256) fwd_tail_sum_kernel(Geom g, TailPlan tp, 
 // with `split`, rows outC .. 2*outC-1 hold the low parts tf32(W - hi).  One
 // block per out channel: the (Cg x kk) row is read through L1 and written
 // tap-major with coalesced stores.
-__global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __restrict__ w,
-                                                             float* __restrict__ wt, Geom g,
-                                                             int split) {
+__device__ __forceinline__ void pack_weight_row(long long oc, const float* __restrict__ w,
+                                                float* __restrict__ wt, const Geom& g,
+                                                int split) {
   const int Kpad = g.kk * g.Cg;
-  const long long oc = blockIdx.x;
   const float* src = w + oc * Kpad;
   float* dst = wt + oc * Kpad;
   const long long lo = (long long)g.outC * Kpad;
@@ -595,6 +595,38 @@ __global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __rest
     const float hi = tc::to_tf32(v);
     dst[j] = hi;
     if (split) dst[lo + j] = tc::to_tf32(v - hi);
+  }
+}
+__global__ void __launch_bounds__(256) tc_pack_weight_kernel(const float* __restrict__ w,
+                                                             float* __restrict__ wt, Geom g,
+                                                             int split) {
+  pack_weight_row(blockIdx.x, w, wt, g, split);
+}
+
+// The tensor-core forward's two helpers in one launch on the caller's
+// stream: blocks [0, tiles) stage the NCHW input as its NHWC copy xt (64 x 64
+// tiles; block 0 also zeroes the pixel row after it, the sampling plans'
+// stand-in for out-of-image corners), the outC blocks after them pack the
+// weight (tc_pack_weight_kernel's rows).  One launch instead of a transpose
+// beside a side-stream pack saves the fork, the join and a launch gap in
+// front of the forward kernel.
+__global__ void __launch_bounds__(256) fwd_prologue_kernel(const float* __restrict__ x,
+                                                           float* __restrict__ xt, int tiles_x,
+                                                           int per_img, int tiles,
+                                                           const float* __restrict__ w,
+                                                           float* __restrict__ wt, Geom g,
+                                                           int split) {
+  __shared__ float tile[64][65];
+  const int b = blockIdx.x;
+  if (b < tiles) {
+    const int n = b / per_img, r = b - n * per_img;
+    transpose4_tile(x, xt, g.C, g.HW, n, r % tiles_x, r / tiles_x, tile, nullptr);
+    if (b == 0) {
+      float* zrow = xt + (long long)g.N * g.HW * g.C;
+      for (int i = threadIdx.x; i < g.C; i += blockDim.x) zrow[i] = 0.f;
+    }
+  } else {
+    pack_weight_row(b - tiles, w, wt, g, split);
   }
 }
 
@@ -730,6 +762,34 @@ size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms) {
   if (g.NP <= 0 || g.G <= 0) return 0;
   const int mode = split ? kSplit : (h16 ? kBF16 : kTF32);
   return plan_tail(tile_count(mode, g), kstep_count(mode, g), tile_cols(mode, g), num_sms).bytes;
+}
+
+bool fwd_prologue_fits(const float* x, const float* xt, const Geom& g) {
+  return transpose4_fits(x, xt, g.C, g.HW) &&
+         transpose4_tiles(g.N, g.C, g.HW) + g.outC <= (1LL << 31) - 1;
+}
+
+cudaError_t launch_fwd_prologue(const float* x, float* xt, const float* w, float* wt,
+                                const Geom& g, bool split, cudaStream_t stream) {
+  if (!fwd_prologue_fits(x, xt, g)) return cudaErrorInvalidValue;
+  // x (N, C, HW) -> xt (N, HW, C): rows C, columns HW
+  const int tiles_x = transpose4_tiles_x(g.HW);
+  const int per_img = tiles_x * ((g.C + 63) / 64);
+  const long long tiles = transpose4_tiles(g.N, g.C, g.HW);
+  const long long blocks = tiles + ((long long)g.outC * g.kk * g.Cg > 0 ? g.outC : 0);
+  if (blocks == 0) {  // nothing to stage or pack: the zero row alone
+    return g.C > 0 ? cudaMemsetAsync(xt + (long long)g.N * g.HW * g.C, 0,
+                                     (size_t)g.C * sizeof(float), stream)
+                   : cudaSuccess;
+  }
+  if (tiles == 0) {  // an empty input: the zero row, then the pack
+    cudaError_t e = g.C > 0 ? cudaMemsetAsync(xt, 0, (size_t)g.C * sizeof(float), stream)
+                            : cudaSuccess;
+    if (e != cudaSuccess) return e;
+  }
+  fwd_prologue_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, xt, tiles_x, per_img, (int)tiles,
+                                                           w, wt, g, split ? 1 : 0);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 
 #include "dcn_kernels.h"
+#include "dcn_transpose.cuh"
 
 namespace dcn {
 
@@ -63,38 +64,7 @@ __global__ void __launch_bounds__(256) transpose4_kernel(const float* __restrict
                                                          TransposeExtras ex) {
   __shared__ float tile[64][65];
   zero_tail(ex);
-  const int n = blockIdx.z;
-  const int r0 = blockIdx.y * 64, s0 = blockIdx.x * 64;
-  const float* src = in + (long long)n * R * S;
-  float* dst = out + (long long)n * R * S;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = r0 + ty + 16 * i, s = s0 + tx * 4;
-    if (r < R && s < S) {
-      const float4 v = *reinterpret_cast<const float4*>(src + (long long)r * S + s);
-      tile[ty + 16 * i][tx * 4 + 0] = v.x;
-      tile[ty + 16 * i][tx * 4 + 1] = v.y;
-      tile[ty + 16 * i][tx * 4 + 2] = v.z;
-      tile[ty + 16 * i][tx * 4 + 3] = v.w;
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int s = s0 + ty + 16 * i, r = r0 + tx * 4;
-    if (s < S && r < R) {
-      float4 v;
-      v.x = tile[tx * 4 + 0][ty + 16 * i];
-      v.y = tile[tx * 4 + 1][ty + 16 * i];
-      v.z = tile[tx * 4 + 2][ty + 16 * i];
-      v.w = tile[tx * 4 + 3][ty + 16 * i];
-      *reinterpret_cast<float4*>(dst + (long long)s * R + r) = v;
-      if (ex.zout)
-        *reinterpret_cast<float4*>(ex.zout + (long long)n * R * S + (long long)s * R + r) =
-            make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  }
+  transpose4_tile(in, out, R, S, blockIdx.z, blockIdx.x, blockIdx.y, tile, ex.zout);
 }
 
 cudaError_t launch_transpose(const float* in, float* out, int N, int R, int S,

@@ -34,6 +34,13 @@ size_t tc_fwd_tail_bytes(const Geom& g, bool split, bool h16, int num_sms);
 // weight (outC, Cg, kh, kw) -> packed tensor-core B operand.
 cudaError_t launch_tc_pack_weight(const float* w, float* wt, const Geom& g, bool split,
                                   cudaStream_t stream);
+// The NCHW input's NHWC staging copy (with its zero pixel row) and the
+// packed weight of launch_tc_pack_weight in one launch.  Needs C and HW
+// multiples of 4 and 16-byte aligned x / xt (fwd_prologue_fits); else
+// cudaErrorInvalidValue, and the two separate launches apply.
+bool fwd_prologue_fits(const float* x, const float* xt, const Geom& g);
+cudaError_t launch_fwd_prologue(const float* x, float* xt, const float* w, float* wt,
+                                const Geom& g, bool split, cudaStream_t stream);
 // Forward on tcgen05: implicit GEMM whose A tiles are gathered (bilinear
 // deformable sampling) by producer warps straight into swizzled shared memory.
 // `split`: 3xTF32 (fp32-level accuracy).  `tail` / `tail_bytes`: the scratch
@@ -149,6 +156,13 @@ cudaError_t launch_bwd_weight_col(const Geom& g, const float* col, const float* 
 cudaError_t launch_weight_from_tap_major(const float* gwt, float* gw, const Geom& g,
                                          cudaStream_t stream, const float* gpart = nullptr,
                                          float* gb = nullptr);
+// launch_nhwc_to_nchw(gxt -> gx) and launch_weight_from_tap_major in one
+// launch.  Needs C and HW multiples of 4 and 16-byte aligned gxt / gx
+// (bwd_finish_fits); else cudaErrorInvalidValue, and the two separate
+// launches apply.
+bool bwd_finish_fits(const float* gxt, const float* gx, const Geom& g);
+cudaError_t launch_bwd_finish(const float* gxt, float* gx, const float* gwt, float* gw,
+                              const Geom& g, const float* gpart, float* gb, cudaStream_t stream);
 // The fused TF32 backward's helpers for a staged input, in one launch:
 // launch_tc_prep_go's work with grad_bias as per-block partial sums into
 // `gpart` (tc_bias_part_floats of them; NULL: no bias), the packed weight of

@@ -101,3 +101,10 @@ def run_oracle(case, backward=True):
         if gb is not None:
             grads["b"] = gb
     return out, grads
+
+
+def staging_launches(stats):
+    """Launches that staged an input as its NHWC copy, by the library's
+    profiler: the plain transpose / copy, or the tensor-core forward's
+    prologue that stages and packs the weight in one launch."""
+    return sum(stats[k][0] for k in ("nchw_to_nhwc", "copy_nhwc", "fwd_prologue") if k in stats)
