@@ -137,15 +137,16 @@ def kernel_work(name, wl):
     """(amount, unit, bound) of one launch of a library kernel."""
     w = algorithmic_work(wl)
     N, C = wl["N"], wl["C"]
+    # (the helpers first: "fwd_prologue" shares the tensor-core kernels' prefix)
+    if name in ("fwd_prologue", "bwd_finish"):  # a transpose + the weight read and rewritten
+        wts = wl["outC"] * (C // wl["groups"]) * wl["k"] ** 2
+        return 2.0 * 4 * (N * C * wl["H"] * wl["W"] + wts), "byte", "hbm"
     if name.startswith("bwd_fused_tc"):  # both backward GEMMs
         return 2.0 * w["gemm_flops"], "flop", "tensor"
     if name.startswith(("fwd_", "bwd_data", "bwd_weight")):
         return w["gemm_flops"], "flop", "tensor"
     if name in ("nchw_to_nhwc", "nhwc_to_nchw", "copy_nhwc"):
         return 2.0 * 4 * N * C * wl["H"] * wl["W"], "byte", "hbm"
-    if name in ("fwd_prologue", "bwd_finish"):  # a transpose + the weight read and rewritten
-        wts = wl["outC"] * (C // wl["groups"]) * wl["k"] ** 2
-        return 2.0 * 4 * (N * C * wl["H"] * wl["W"] + wts), "byte", "hbm"
     if name == "bwd_prologue":  # grad_out in + rows out, zeroed accumulators, packed weight
         ho, wo = out_hw(wl)
         O, k2, dg = wl["outC"], wl["k"] ** 2, wl["dg"]
