@@ -402,12 +402,29 @@ at::Tensor deform_conv2d_forward_rows(const at::Tensor& input, const at::Tensor&
 
 using Grads = std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor>;
 
+// grad_weight and grad_bias.  `adjacent` (with a bias): two views of one
+// buffer, the bias right after the weight, so that a data-parallel step sums
+// both with a single all-reduce of that buffer (distributed.allreduce_grads
+// and GradAllReduce find them adjacent); autograd hands such views on as the
+// parameters' .grad when nothing else holds them.  Only the autograd nodes
+// ask for it: a registered operator's outputs must not alias one another.
+std::pair<at::Tensor, at::Tensor> param_grads(const at::Tensor& w, bool use_bias,
+                                              bool adjacent) {
+  if (adjacent && use_bias) {
+    auto flat = at::empty({w.numel() + w.size(0)}, w.options());
+    return {flat.narrow(0, 0, w.numel()).view(w.sizes()), flat.narrow(0, w.numel(), w.size(0))};
+  }
+  return {at::empty_like(w), use_bias ? at::empty({w.size(0)}, w.options())
+                                      : at::empty({0}, w.options())};
+}
+
 Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
                     const at::Tensor& weight, const at::Tensor& offset, const at::Tensor& mask,
                     const c10::optional<at::Tensor>& bias, int64_t stride_h, int64_t stride_w,
                     int64_t pad_h, int64_t pad_w, int64_t dilation_h, int64_t dilation_w,
                     int64_t groups, int64_t deformable_groups, int64_t row_begin, int64_t math,
-                    const c10::optional<at::Tensor>& staged = c10::nullopt) {
+                    const c10::optional<at::Tensor>& staged = c10::nullopt,
+                    bool adjacent_param_grads = false) {
   TORCH_CHECK(grad_output.device().is_cuda() && input.device().is_cuda() &&
                   weight.device().is_cuda() && offset.device().is_cuda(),
               "deform_conv2d_backward: grad_output, input, weight and offset must be CUDA tensors");
@@ -442,8 +459,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
     auto grad_input = at::empty_like(x);
     auto grad_offset = at::empty_like(off);
     auto grad_mask = use_mask ? at::empty_like(msk) : at::empty({0}, x.options());
-    auto grad_weight = at::empty_like(w);
-    auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
+    auto [grad_weight, grad_bias] = param_grads(w, use_bias, adjacent_param_grads);
     if (x.numel() == 0 && off.numel() == 0) {
       grad_weight.zero_();
       if (use_bias) grad_bias.zero_();
@@ -489,8 +505,7 @@ Grads backward_impl(const at::Tensor& grad_output, const at::Tensor& input,
   auto grad_input = at::empty_like(x);
   auto grad_offset = at::empty_like(off);
   auto grad_mask = use_mask ? at::empty_like(msk) : at::empty({0}, x.options());
-  auto grad_weight = at::empty_like(w);
-  auto grad_bias = use_bias ? at::empty({w.size(0)}, x.options()) : at::empty({0}, x.options());
+  auto [grad_weight, grad_bias] = param_grads(w, use_bias, adjacent_param_grads);
   const dcn_shape s = make_shape(x, w, stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w,
                                  groups, deformable_groups);
   const float* xs = staged_ptr(staged, x, s);
@@ -718,13 +733,6 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
 
   static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
                                                  torch::autograd::variable_list grads) {
-    static auto op = c10::Dispatcher::singleton()
-                         .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_backward", "")
-                         .typed<Grads(const at::Tensor&, const at::Tensor&, const at::Tensor&,
-                                      const at::Tensor&, const at::Tensor&,
-                                      const c10::optional<at::Tensor>&, int64_t, int64_t,
-                                      int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                                      int64_t, const c10::optional<at::Tensor>&)>();
     const auto saved = ctx->get_saved_variables();
     const auto v = ctx->saved_data["ints"].toIntVector();
     const bool has_bias = ctx->saved_data["has_bias"].toBool();
@@ -733,8 +741,9 @@ class DeformConv2dFn : public torch::autograd::Function<DeformConv2dFn> {
     if (has_bias) b = saved[4];
     c10::optional<at::Tensor> st;
     if (ctx->saved_data.count("staged")) st = ctx->saved_data["staged"].toTensor();
-    auto r = op.call(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0], v[1],
-                     v[2], v[3], v[4], v[5], v[6], v[7], v[8], st);
+    // the backward operator's work, with grad_weight / grad_bias side by side
+    auto r = backward_impl(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0],
+                           v[1], v[2], v[3], v[4], v[5], v[6], v[7], -1, v[8], st, true);
     const bool has_mask = mask.numel() > 0;
     return {std::get<0>(r),
             std::get<3>(r),
@@ -798,13 +807,6 @@ class DeformConv2dRowsFn : public torch::autograd::Function<DeformConv2dRowsFn> 
 
   static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
                                                  torch::autograd::variable_list grads) {
-    static auto op =
-        c10::Dispatcher::singleton()
-            .findSchemaOrThrow("deform_conv2d_b200::deform_conv2d_backward_rows", "")
-            .typed<Grads(const at::Tensor&, const at::Tensor&, const at::Tensor&,
-                         const at::Tensor&, const at::Tensor&, const c10::optional<at::Tensor>&,
-                         int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                         int64_t, int64_t, const c10::optional<at::Tensor>&)>();
     const auto saved = ctx->get_saved_variables();
     const auto v = ctx->saved_data["ints"].toIntVector();
     const bool has_bias = ctx->saved_data["has_bias"].toBool();
@@ -813,8 +815,9 @@ class DeformConv2dRowsFn : public torch::autograd::Function<DeformConv2dRowsFn> 
     if (has_bias) b = saved[4];
     c10::optional<at::Tensor> st;
     if (ctx->saved_data.count("staged")) st = ctx->saved_data["staged"].toTensor();
-    auto r = op.call(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0], v[1],
-                     v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], st);
+    TORCH_CHECK(v[8] >= 0, "deform_conv2d_backward_rows: row_begin must be >= 0");
+    auto r = backward_impl(grads[0].contiguous(), saved[0], saved[1], saved[2], mask, b, v[0],
+                           v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], st, true);
     const bool has_mask = mask.numel() > 0;
     return {std::get<0>(r),
             std::get<3>(r),

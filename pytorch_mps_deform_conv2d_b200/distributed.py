@@ -35,11 +35,13 @@ def shard_batch(tensors: Sequence[Optional[torch.Tensor]], rank: int,
 
 
 def _adjacent_view(grads: Sequence[Optional[torch.Tensor]]) -> Optional[torch.Tensor]:
-    """One 1-D view covering `grads` when they are contiguous, in order and
-    back to back in one storage (a GradBucket lays them out that way); None
-    otherwise."""
+    """One 1-D view covering `grads` when they are contiguous and lie back to
+    back in one storage, in any order of the list (a GradBucket lays them out
+    that way, and so does the operator's autograd node for grad_weight and
+    grad_bias); None otherwise."""
     if not grads or any(g is None or not g.is_contiguous() for g in grads):
         return None
+    grads = sorted(grads, key=lambda g: g.data_ptr())
     first = grads[0]
     storage = first.untyped_storage()
     end = first.data_ptr()

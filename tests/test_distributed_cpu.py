@@ -211,3 +211,15 @@ def test_grad_bucket_accumulates_in_place_and_reduces_once():
         for step, (gw, gb) in enumerate(got):
             np.testing.assert_array_equal(gw, np.full((4, 3), 1 + 2 + 20 * step, np.float32))
             np.testing.assert_array_equal(gb, np.full((4,), 2 + 3, np.float32))
+
+
+def test_adjacent_view_takes_the_gradients_in_any_order():
+    from pytorch_mps_deform_conv2d_b200.distributed import _adjacent_view
+    flat = torch.arange(15, dtype=torch.float32)
+    gw, gb = flat[:12].view(4, 3), flat[12:]
+    for grads in ([gw, gb], [gb, gw]):  # hooks may deliver either first
+        view = _adjacent_view(grads)
+        assert view is not None and view.data_ptr() == flat.data_ptr()
+        assert torch.equal(view, flat)
+    assert _adjacent_view([gw, flat[13:]]) is None  # a gap
+    assert _adjacent_view([gw, torch.zeros(3)]) is None  # another storage
